@@ -1,0 +1,301 @@
+"""CPU oracle for the mps_pointops hot path -- TEST INFRASTRUCTURE ONLY.
+
+Thin numpy/ctypes front end over ``oracle/pointops_oracle.c`` (built by
+``oracle/Makefile`` into ``oracle/_build/liboracle.so``).  Each function
+restates one CPU algorithm of the reference package gamzerA/mps-pointops
+v1.0.0; the C source cites the reference file:line it follows.
+
+Only the test suite, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
+``bench.py`` may import this module.  The product package never does: a
+CUDA call that silently landed here would void every parity claim.
+
+Work is split over independent clouds / query ranges on host threads
+(ctypes drops the GIL during a foreign call).  The split never changes the
+order of a floating-point accumulation that tests compare bit-for-bit.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+_LIB_PATH = _HERE / "_build" / "liboracle.so"
+_lib = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i64p = ctypes.POINTER(ctypes.c_int64)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_i64 = ctypes.c_int64
+
+
+def build() -> Path:
+    """Compile the C oracle in place (idempotent)."""
+    src = _HERE / "pointops_oracle.c"
+    if not _LIB_PATH.exists() or _LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        subprocess.run(["make", "-s", "-C", str(_HERE)], check=True)
+    return _LIB_PATH
+
+
+def _load():
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            build()
+        lib = ctypes.CDLL(str(_LIB_PATH))
+        lib.oracle_fps.argtypes = [_f32p, _i64, _i64, _i64, _i64, ctypes.c_int, _i64p]
+        lib.oracle_knn.argtypes = [_f32p, _f32p, _i64, _i64, _i64, _i64, _i64, _f32p, _i64p]
+        lib.oracle_knn_sqdist.argtypes = [_f32p, _f32p, _i64, _i64, _i64, _i64, _i64, _i64p, _f32p]
+        lib.oracle_ball_query.argtypes = [_f32p, _f32p, _i64p, _i64p, _i64, _i64, _i64, _i64,
+                                          ctypes.c_float, _f32p, _i64p]
+        lib.oracle_three_nn.argtypes = [_f32p, _f32p, _i64, _i64, _i64, _f32p, _i32p]
+        lib.oracle_three_interpolate.argtypes = [_f32p, _i64p, _f32p, _i64, _i64, _i64, _i64, _f32p]
+        lib.oracle_three_interpolate_backward.argtypes = [_f32p, _i64p, _f32p, _i64, _i64, _i64,
+                                                          _i64, _f32p]
+        lib.oracle_chamfer_nearest.argtypes = [_f32p, _f32p, _i64p, _i64p, _i64, _i64, _i64, _i64,
+                                               _f32p, _i64p]
+        lib.oracle_chamfer_mean_loss_and_grad.argtypes = [
+            _f32p, _f32p, _i64p, _i64p, _i64, _i64, _i64, _i64, _i64p, _i64p, _f32p, _f32p,
+            _f32p, _f32p]
+        lib.oracle_chamfer_mean_loss_and_grad.restype = ctypes.c_double
+        _lib = lib
+    return _lib
+
+
+def _ptr(a: np.ndarray | None, kind):
+    if a is None:
+        return ctypes.cast(None, kind)
+    return a.ctypes.data_as(kind)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+def _i64a(a) -> np.ndarray | None:
+    return None if a is None else np.ascontiguousarray(np.asarray(a, dtype=np.int64))
+
+
+def threads() -> int:
+    env = os.environ.get("MPO_ORACLE_THREADS")
+    return max(1, int(env)) if env else max(1, os.cpu_count() or 1)
+
+
+def _parallel(jobs):
+    jobs = list(jobs)
+    n = min(threads(), len(jobs))
+    if n <= 1:
+        for j in jobs:
+            j()
+        return
+    with ThreadPoolExecutor(n) as pool:
+        for f in [pool.submit(j) for j in jobs]:
+            f.result()
+
+
+def _ranges(total: int, parts: int):
+    parts = max(1, min(parts, total))
+    step = -(-total // parts) if total else 0
+    return [(lo, min(total, lo + step)) for lo in range(0, total, step)] if total else []
+
+
+# ---------------------------------------------------------------- FPS
+def furthest_point_sample(xyz, npoint: int, start_idx: int = 0,
+                          skip_near_origin: bool = False) -> np.ndarray:
+    """mps_pointops/reference.py:27-58.  (B,N,3) -> (B,npoint) int64."""
+    lib = _load()
+    xyz = _f32(xyz)
+    B, N, _ = xyz.shape
+    out = np.empty((B, npoint), dtype=np.int64)
+    if B == 0 or npoint == 0:
+        return out
+
+    def job(b):
+        return lambda: lib.oracle_fps(_ptr(xyz[b], _f32p), 1, N, npoint, start_idx,
+                                      int(skip_near_origin), _ptr(out[b], _i64p))
+    _parallel(job(b) for b in range(B))
+    return out
+
+
+# ---------------------------------------------------------------- kNN
+def knn(query, ref, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """Exact (SD, index) kNN: tests/test_knn.py:15-23, tests/test_feature_knn.py:16-35.
+
+    Returns Euclidean distances (B,M,k) float32 and indices (B,M,k) int64.
+    """
+    lib = _load()
+    query, ref = _f32(query), _f32(ref)
+    B, M, D = query.shape
+    N = ref.shape[1]
+    dist = np.empty((B, M, k), dtype=np.float32)
+    idx = np.empty((B, M, k), dtype=np.int64)
+    if B == 0 or M == 0 or k == 0:
+        return dist, idx
+    jobs = []
+    parts = max(1, threads() * 4 // max(1, B))
+    for b in range(B):
+        for lo, hi in _ranges(M, parts):
+            def job(b=b, lo=lo, hi=hi):
+                lib.oracle_knn(_ptr(query[b, lo:hi], _f32p), _ptr(ref[b], _f32p), 1, hi - lo, N,
+                               D, k, _ptr(dist[b, lo:hi], _f32p), _ptr(idx[b, lo:hi], _i64p))
+            jobs.append(job)
+    _parallel(jobs)
+    return dist, idx
+
+
+def knn_sqdist(query, ref, idx) -> np.ndarray:
+    """Squared distances of selected neighbours (inf for index -1)."""
+    lib = _load()
+    query, ref, idx = _f32(query), _f32(ref), _i64a(idx)
+    B, M, D = query.shape
+    out = np.empty(idx.shape, dtype=np.float32)
+    lib.oracle_knn_sqdist(_ptr(query, _f32p), _ptr(ref, _f32p), B, M, ref.shape[1], D,
+                          idx.shape[-1], _ptr(idx, _i64p), _ptr(out, _f32p))
+    return out
+
+
+# ---------------------------------------------------------------- ball query
+def radius_squared(radius: float) -> float:
+    """fl32(fl32(r) * fl32(r)) (mps_pointops/_ball_query_mps.py:104-119)."""
+    r32 = np.float32(radius)
+    with np.errstate(over="ignore"):
+        return float(np.float32(r32 * r32))
+
+
+def ball_query(query, ref, radius: float, K: int, query_lengths=None,
+               point_lengths=None) -> tuple[np.ndarray, np.ndarray]:
+    """mps_pointops/reference.py:83-121 (+ lengths, _ball_query_mps.py:73-84)."""
+    lib = _load()
+    query, ref = _f32(query), _f32(ref)
+    ql, pl = _i64a(query_lengths), _i64a(point_lengths)
+    B, M, _ = query.shape
+    N = ref.shape[1]
+    r2 = radius_squared(radius)
+    dist2 = np.zeros((B, M, K), dtype=np.float32)
+    idx = np.full((B, M, K), -1, dtype=np.int64)
+    if B == 0 or M == 0 or K == 0:
+        return dist2, idx
+    jobs = []
+    parts = max(1, threads() * 4 // max(1, B))
+    for b in range(B):
+        for lo, hi in _ranges(M, parts):
+            def job(b=b, lo=lo, hi=hi):
+                qlb = None if ql is None else np.array([max(0, min(hi, ql[b]) - lo)], np.int64)
+                plb = None if pl is None else pl[b:b + 1].copy()
+                lib.oracle_ball_query(_ptr(query[b, lo:hi], _f32p), _ptr(ref[b], _f32p),
+                                      _ptr(qlb, _i64p), _ptr(plb, _i64p), 1, hi - lo, N, K,
+                                      ctypes.c_float(r2), _ptr(dist2[b, lo:hi], _f32p),
+                                      _ptr(idx[b, lo:hi], _i64p))
+            jobs.append(job)
+    _parallel(jobs)
+    return dist2, idx
+
+
+def ball_query_pointnet2(radius: float, nsample: int, xyz, new_xyz) -> np.ndarray:
+    """mps_pointops/compat.py:76-85: misses repeat the first hit (0 if none), int32."""
+    _, idx = ball_query(new_xyz, xyz, radius, nsample)
+    first = np.maximum(idx[..., :1], 0)
+    return np.where(idx >= 0, idx, first).astype(np.int32)
+
+
+# ---------------------------------------------------------------- three_nn / interpolate
+def three_nn(unknown, known) -> tuple[np.ndarray, np.ndarray]:
+    """mps_pointops/pointnet2.py:54-72.  Euclidean distances, int32 indices."""
+    lib = _load()
+    unknown, known = _f32(unknown), _f32(known)
+    B, N, _ = unknown.shape
+    M = known.shape[1]
+    dist = np.empty((B, N, 3), dtype=np.float32)
+    idx = np.empty((B, N, 3), dtype=np.int32)
+    if B == 0 or N == 0:
+        return dist, idx
+    jobs = []
+    parts = max(1, threads() * 4 // max(1, B))
+    for b in range(B):
+        for lo, hi in _ranges(N, parts):
+            def job(b=b, lo=lo, hi=hi):
+                lib.oracle_three_nn(_ptr(unknown[b, lo:hi], _f32p), _ptr(known[b], _f32p), 1,
+                                    hi - lo, M, _ptr(dist[b, lo:hi], _f32p),
+                                    _ptr(idx[b, lo:hi], _i32p))
+            jobs.append(job)
+    _parallel(jobs)
+    return dist, idx
+
+
+def three_interpolate(features, indices, weights) -> np.ndarray:
+    """mps_pointops/pointnet2.py:135-147."""
+    lib = _load()
+    features, weights = _f32(features), _f32(weights)
+    indices = _i64a(indices)
+    B, C, M = features.shape
+    N = indices.shape[1]
+    out = np.empty((B, C, N), dtype=np.float32)
+    lib.oracle_three_interpolate(_ptr(features, _f32p), _ptr(indices, _i64p),
+                                 _ptr(weights, _f32p), B, C, M, N, _ptr(out, _f32p))
+    return out
+
+
+def three_interpolate_backward(grad_out, indices, weights, M: int) -> np.ndarray:
+    """mps_pointops/pointnet2.py:168-188 (feature gradient; weight grad is zero)."""
+    lib = _load()
+    grad_out, weights = _f32(grad_out), _f32(weights)
+    indices = _i64a(indices)
+    B, C, N = grad_out.shape
+    out = np.empty((B, C, M), dtype=np.float32)
+    lib.oracle_three_interpolate_backward(_ptr(grad_out, _f32p), _ptr(indices, _i64p),
+                                          _ptr(weights, _f32p), B, C, M, N, _ptr(out, _f32p))
+    return out
+
+
+# ---------------------------------------------------------------- Chamfer
+def chamfer_nearest(query, ref, query_lengths=None, ref_lengths=None):
+    """mps_pointops/chamfer.py:161-212 + 297-308: first-minimum index and its SD."""
+    lib = _load()
+    query, ref = _f32(query), _f32(ref)
+    ql, rl = _i64a(query_lengths), _i64a(ref_lengths)
+    B, P, D = query.shape
+    Q = ref.shape[1]
+    dist = np.empty((B, P), dtype=np.float32)
+    idx = np.empty((B, P), dtype=np.int64)
+    if B == 0 or P == 0:
+        return dist, idx
+    jobs = []
+    parts = max(1, threads() * 4 // max(1, B))
+    for b in range(B):
+        for lo, hi in _ranges(P, parts):
+            def job(b=b, lo=lo, hi=hi):
+                qlb = None if ql is None else np.array([max(0, min(hi, ql[b]) - lo)], np.int64)
+                rlb = None if rl is None else rl[b:b + 1].copy()
+                lib.oracle_chamfer_nearest(_ptr(query[b, lo:hi], _f32p), _ptr(ref[b], _f32p),
+                                           _ptr(qlb, _i64p), _ptr(rlb, _i64p), 1, hi - lo, Q, D,
+                                           _ptr(dist[b, lo:hi], _f32p), _ptr(idx[b, lo:hi], _i64p))
+            jobs.append(job)
+    _parallel(jobs)
+    return dist, idx
+
+
+def chamfer_mean_loss_and_grad(x, y, x_lengths=None, y_lengths=None):
+    """Squared-L2 Chamfer, mean/mean reductions, loss and both gradients (float64 sums).
+
+    mps_pointops/chamfer.py:342-488 (forward) and :215-251 (backward).
+    Returns (loss, grad_x, grad_y, (dist_x, idx_x), (dist_y, idx_y)).
+    """
+    lib = _load()
+    x, y = _f32(x), _f32(y)
+    lx, ly = _i64a(x_lengths), _i64a(y_lengths)
+    dx, ix = chamfer_nearest(x, y, lx, ly)
+    dy, iy = chamfer_nearest(y, x, ly, lx)
+    B, P, D = x.shape
+    Q = y.shape[1]
+    gx = np.empty_like(x)
+    gy = np.empty_like(y)
+    loss = lib.oracle_chamfer_mean_loss_and_grad(
+        _ptr(x, _f32p), _ptr(y, _f32p), _ptr(lx, _i64p), _ptr(ly, _i64p), B, P, Q, D,
+        _ptr(ix, _i64p), _ptr(iy, _i64p), _ptr(dx, _f32p), _ptr(dy, _f32p),
+        _ptr(gx, _f32p), _ptr(gy, _f32p))
+    return loss, gx, gy, (dx, ix), (dy, iy)

@@ -1,0 +1,327 @@
+"""Generate the golden fixtures in tests/golden/ from the reference package.
+
+Run once, in a container that has the reference checkout (default
+``/root/reference``, override with ``MPO_REFERENCE_PATH``)::
+
+    python tests/golden/make_golden.py
+
+Every output is produced by the reference's OWN code: its CPU path
+(``mps_pointops.reference``, ``pointnet2._three_nn_reference``,
+``chamfer.chamfer_distance`` ...), the exact kNN oracles in its test files
+(``tests/test_knn.py:15-23``, ``tests/test_feature_knn.py:16-35``), its parity
+input generators (``tools/pointnet2parity.py:125-170``) and the parity records
+it ships (``docs/parity/pointnet2-cuda.json``: the original PointNet++ CUDA
+extension; ``docs/parity/pointnet2-segmentation-*.npz``).  The inputs are
+stored next to the outputs, so the tests need neither the reference nor a
+torch RNG of the same version at run time.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REF = Path(os.environ.get("MPO_REFERENCE_PATH", "/root/reference"))
+OUT = Path(__file__).resolve().parent
+sys.path.insert(0, str(REF))
+sys.path.insert(0, str(REF / "tests"))
+sys.path.insert(0, str(REF / "tools"))
+
+from mps_pointops import compat, reference  # noqa: E402  (the reference package)
+from mps_pointops import chamfer as ref_chamfer  # noqa: E402
+from mps_pointops import pointnet2 as ref_pointnet2  # noqa: E402
+import test_feature_knn  # noqa: E402  (reference tests: scalar fp32 oracle)
+import test_knn  # noqa: E402  (reference tests: exact lexsort oracle)
+import pointnet2parity  # noqa: E402  (reference tools: parity inputs)
+
+
+def cloud(b, n, seed=0):
+    """tests/test_fps.py:9-11, tests/test_knn.py:10-12."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(b, n, 3, generator=g)
+
+
+def save(name: str, **arrays) -> None:
+    arrays = {k: (v.detach().cpu().numpy() if isinstance(v, torch.Tensor) else np.asarray(v))
+              for k, v in arrays.items()}
+    np.savez_compressed(OUT / f"{name}.npz", **arrays)
+
+
+# ------------------------------------------------------------------ FPS
+def fps_cases():
+    cases = {}
+    for n in [1, 2, 31, 32, 33, 1023, 1024, 1025, 5000]:          # tests/test_fps.py:22-25
+        cases[f"n{n}"] = (cloud(1, n), min(n, 256), 0, False)
+    cases["batch5"] = (cloud(5, 3000), 128, 0, False)                # :28-31
+    cases["start777"] = (cloud(2, 1000), 64, 777, False)            # :34-36
+    cases["oversample"] = (cloud(1, 10), 25, 0, False)               # :39-42
+    cases["duplicates"] = (torch.tensor([[[0.0, 0, 0], [1, 0, 0], [1, 0, 0], [-1, 0, 0],
+                                          [0, 1, 0], [0, 1, 0]]]), 6, 0, False)  # :45-48
+    xyz = cloud(1, 2000)                                             # tests/test_compat.py:95-111
+    inside = np.float32(np.sqrt(np.float32(1e-3))) * np.float32(0.999)
+    outside = np.float32(np.sqrt(np.float32(1e-3))) * np.float32(1.001)
+    xyz[0, 1:40] = torch.tensor([inside, 0.0, 0.0]) * torch.rand(
+        39, 1, generator=torch.Generator().manual_seed(5))
+    xyz[0, 40] = torch.tensor([float(inside), 0.0, 0.0])
+    xyz[0, 41] = torch.tensor([float(outside), 0.0, 0.0])
+    cases["skip_near_origin"] = (xyz, 2000, 0, True)
+    cases["all_near_origin"] = (torch.zeros(1, 50, 3), 5, 0, True)  # tests/test_compat.py:114-118
+    pattern = torch.zeros((1, 129, 3))                               # tests/test_fps.py:103-118
+    pattern[0, 1::2, 0] = 1
+    pattern[0, 2::4, 1] = -1
+    for skip in (False, True):
+        cases[f"ties_skip{int(skip)}"] = (pattern.clone(), 150, 3, skip)
+    for n in [4095, 4096, 4097, 8193]:                               # tests/test_fps.py:88-100
+        cases[f"chunk{n}"] = (cloud(1, n, seed=27), min(n + 2, 20), n // 2, False)
+    g = torch.Generator().manual_seed(0)
+    cases["config1_compat"] = (torch.rand(8, 4096, 3, generator=g), 1024, 0, True)
+    out = {}
+    for name, (xyz, npoint, start, skip) in cases.items():
+        want = reference.furthest_point_sample(xyz, npoint, start, skip)
+        out[f"{name}/xyz"] = xyz
+        out[f"{name}/meta"] = np.array([npoint, start, int(skip)], dtype=np.int64)
+        out[f"{name}/idx"] = want
+    save("fps", **out)
+
+
+# ------------------------------------------------------------------ kNN
+def knn_cases():
+    out = {}
+    for n in [1, 31, 32, 33, 1000, 5000]:                            # tests/test_knn.py:35-42
+        for k in [1, 5, 32, 128]:
+            if k > n:
+                continue
+            ref = cloud(1, n)
+            out[f"n{n}_k{k}/query"] = ref[:, :50] + 0.01
+            out[f"n{n}_k{k}/ref"] = ref
+    for m in [1, 7, 8, 9, 100]:                                      # :45-48
+        out[f"m{m}/query"] = cloud(1, m, seed=1)
+        out[f"m{m}/ref"] = cloud(1, 2000)
+    ref = cloud(1, 256)                                              # :51-54 (k = N = 256)
+    out["kmax/query"], out["kmax/ref"] = ref[:, :20], ref
+    out["batch3/query"], out["batch3/ref"] = cloud(3, 40, seed=1), cloud(3, 3000)  # :57-59
+    for desc in (False, True):                                       # :62-67
+        ref = cloud(1, 20000)
+        ref = ref[:, ref[0, :, 0].argsort(descending=desc)]
+        out[f"sorted{int(desc)}/query"], out[f"sorted{int(desc)}/ref"] = cloud(1, 64, seed=1), ref
+    ref = torch.zeros(1, 300, 3)                                     # :70-74
+    ref[0, ::3] = 1.0
+    out["ties/query"], out["ties/ref"] = torch.zeros(1, 2, 3), ref
+    ks = {"kmax": 256, "batch3": 32, "sorted0": 128, "sorted1": 128, "ties": 150}
+    names = sorted({k.split("/")[0] for k in out})
+    for name in names:
+        if name.startswith("n"):
+            k = int(name.split("_k")[1])
+        elif name.startswith("m"):
+            k = 16
+        else:
+            k = ks[name]
+        q, r = out[f"{name}/query"], out[f"{name}/ref"]
+        d, i = test_knn.exact(q, r, k)                               # the reference's own oracle
+        out[f"{name}/k"] = np.array(k)
+        out[f"{name}/dist"] = d.astype(np.float32)
+        out[f"{name}/idx"] = i.astype(np.int64)
+    save("knn", **out)
+
+
+def feature_knn_cases():
+    out = {}
+    for dim in [1, 2, 4, 64, 128]:                                   # tests/test_feature_knn.py:38-58
+        for k in [1, 5, 33]:
+            gen = torch.Generator().manual_seed(107 + dim)
+            query = torch.randn((2, 9, dim), generator=gen)
+            ref = torch.randn((2, 97, dim), generator=gen)
+            ref[:, 20] = ref[:, 3]
+            query[:, 0] = ref[:, 3]
+            name = f"d{dim}_k{k}"
+            dists, idxs = zip(*(test_feature_knn._oracle(query[b], ref[b], k) for b in range(2)))
+            out[f"{name}/query"], out[f"{name}/ref"] = query, ref
+            out[f"{name}/k"] = np.array(k)
+            out[f"{name}/dist"] = np.stack(dists)
+            out[f"{name}/idx"] = np.stack(idxs)
+    gen = torch.Generator().manual_seed(2026)                        # :61-73
+    ref = torch.randn((1, 300, 64), generator=gen)
+    query = torch.randn((1, 4, 64), generator=gen)
+    ref[0, 1] = ref[0, 0]
+    query[0, 0] = ref[0, 0]
+    d, i = test_feature_knn._oracle(query[0], ref[0], 256)
+    out["k256/query"], out["k256/ref"], out["k256/k"] = query, ref, np.array(256)
+    out["k256/dist"], out["k256/idx"] = d[None], i[None]
+    save("feature_knn", **out)
+
+
+# ------------------------------------------------------------------ ball query
+def ball_query_cases():
+    out = {}
+
+    def add(name, q, r, radius, K):
+        d2, idx = reference.ball_query(q, r, radius, K)              # reference.py:83-121
+        out[f"{name}/query"], out[f"{name}/ref"] = q, r
+        out[f"{name}/radius"], out[f"{name}/K"] = np.array(radius, np.float64), np.array(K)
+        out[f"{name}/dist2"], out[f"{name}/idx"] = d2, idx
+
+    torch.manual_seed(9)
+    add("random", torch.randn(2, 7, 3), torch.randn(2, 19, 3), 2.0, 5)
+    add("first_k", torch.zeros((1, 1, 3)),                           # tests/test_ball_query_mps.py:76-87
+        torch.tensor([[[0.8, 0, 0], [0.1, 0, 0], [1.0, 0, 0], [0.2, 0, 0]]]), 1.0, 2)
+    positions = [0, 1, 31, 32, 64, 128, 224, 250, 256]              # :90-112
+    pts = torch.zeros((1, 257, 3))
+    pts[0, :, 0] = torch.arange(257, dtype=torch.float32)
+    for k in [1, 7, 31, 33, 65]:
+        add(f"sorted_k{k}", pts[:, positions].clone(), pts, 20.5, k)
+    one = torch.tensor(1.0)
+    add("boundary", torch.zeros((1, 1, 3)), torch.tensor(                # :216-229
+        [[[torch.nextafter(one, torch.tensor(0.0)).item(), 0, 0], [1.0, 0, 0],
+          [torch.nextafter(one, torch.tensor(float("inf"))).item(), 0, 0]]]), 1.0, 3)
+    add("r2_rounding", torch.zeros((1, 1, 3)),                       # :248-261
+        torch.tensor([[[0.09999999403953552, 3.112176273134537e-05, 0.0]]]), 0.1, 1)
+    nf = torch.full((1, 97, 3), 2.0)                                  # :200-213
+    nf[0, [0, 31, 32, 63, 64, 95, 96], :] = 0.0
+    nf[0, 31, 0], nf[0, 64, 0] = float("nan"), float("inf")
+    add("nonfinite_blocks", torch.zeros((1, 1, 3)), nf, 0.5, 7)
+    q = torch.tensor([[[0.0, 0, 0], [float("nan"), 0, 0], [float("inf"), 0, 0],
+                       [-float("inf"), 0, 0]]])                       # :465-490
+    p = torch.tensor([[[float("nan"), 0, 0], [float("inf"), 0, 0], [-float("inf"), 0, 0],
+                       [0.25, 0, 0], [0.5, 0, 0]]])
+    add("nonfinite_queries", q, p, 1.0, 3)
+    add("tiny_radius", torch.zeros((1, 1, 3)),                       # :385-409
+        torch.tensor([[[0.0, 0.0, 0.0], [1e-20, 0.0, 0.0]]]), 1e-30, 2)
+    add("huge_radius", torch.zeros((1, 1, 3)),
+        torch.tensor([[[1e19, 0.0, 0.0], [5e19, 0.0, 0.0], [2e20, 0.0, 0.0]]]), 1e20, 3)
+    add("zero_radius", torch.rand(1, 4, 3, generator=torch.Generator().manual_seed(3)),
+        torch.rand(1, 20, 3, generator=torch.Generator().manual_seed(4)), 0.0, 3)
+    g = torch.Generator().manual_seed(11)
+    add("dense", torch.rand(3, 300, 3, generator=g), torch.rand(3, 2000, 3, generator=g), 0.15, 64)
+    save("ball_query", **out)
+
+    # compat padding, BASELINE config 1 (xyz = rand(8,4096,3) seed 0, centres = FPS 1024)
+    g = torch.Generator().manual_seed(0)
+    xyz = torch.rand(8, 4096, 3, generator=g)
+    idx = compat.furthest_point_sample(xyz, 1024)
+    centres = compat.gather_operation(xyz.transpose(1, 2).contiguous(), idx).transpose(1, 2).contiguous()
+    grouped = compat.ball_query(0.2, 32, xyz, centres)
+    knn_d, knn_i = test_knn.exact(centres, xyz, 16)
+    tn_d, tn_i = ref_pointnet2._three_nn_reference(xyz, centres)
+    save("config1", xyz=xyz, fps_idx=idx, centres=centres, ball_query_idx=grouped,
+         knn_dist=knn_d.astype(np.float32), knn_idx=knn_i.astype(np.int64),
+         three_nn_dist=tn_d, three_nn_idx=tn_i)
+    pad = compat.ball_query(0.5, 4, torch.tensor([[[5.0, 0, 0], [0.1, 0, 0], [9, 9, 9], [0.2, 0, 0]]]),
+                            torch.tensor([[[0.0, 0, 0], [50.0, 50, 50]]]))  # tests/test_compat.py:140-145
+    save("compat_pad", idx=pad)
+
+
+# ------------------------------------------------------------------ PointNet++ propagation
+def pointnet2_cases():
+    out = {}
+    rng = np.random.default_rng(59)                                   # tests/test_pointnet2.py:42-58
+    unknown = torch.from_numpy(rng.normal(size=(2, 37, 6)).astype("float32"))[..., ::2].contiguous()
+    known = torch.from_numpy(rng.normal(size=(2, 113, 6)).astype("float32"))[..., ::2].contiguous()
+    d, i = ref_pointnet2._three_nn_reference(unknown, known)
+    out.update({"nn_random/unknown": unknown, "nn_random/known": known,
+                "nn_random/dist": d, "nn_random/idx": i})
+    u = torch.tensor([[[0., 0., 0.], [2., 0., 0.]]])                  # :24-39
+    k = torch.tensor([[[1., 0., 0.], [-1., 0., 0.], [0., 2., 0.], [1., 0., 0.]]])
+    d, i = ref_pointnet2._three_nn_reference(u, k)
+    out.update({"nn_ties/unknown": u, "nn_ties/known": k, "nn_ties/dist": d, "nn_ties/idx": i})
+    gen = torch.Generator().manual_seed(109)                          # :115-126
+    f = torch.randn(2, 4, 17, generator=gen)
+    ind = torch.randint(17, (2, 11, 3), generator=gen, dtype=torch.int32)
+    w = torch.randn(2, 11, 3, generator=gen)
+    up = torch.randn(2, 4, 11, generator=gen)
+    fr = f.clone().requires_grad_()
+    o = ref_pointnet2._three_interpolate_reference(fr, ind, w)
+    o.backward(up)
+    out.update({"interp_random/features": f, "interp_random/indices": ind,
+                "interp_random/weights": w, "interp_random/grad_out": up,
+                "interp_random/out": o.detach(), "interp_random/grad_features": fr.grad})
+    save("pointnet2", **out)
+
+    # Original PointNet++ CUDA extension outputs (docs/parity/pointnet2-cuda.json) with the
+    # inputs rebuilt by the reference's own generators (tools/pointnet2parity.py:125-170).
+    rec = json.loads((REF / "docs/parity/pointnet2-cuda.json").read_text())
+    cpu = torch.device("cpu")
+    up = {}
+    for name, make in (("ties-and-duplicates", pointnet2parity._small_inputs),
+                       ("seeded-stride", pointnet2parity._large_inputs)):
+        unknown, known, features, weights, gradient = make(cpu)
+        case = rec["cases"][name]
+        key = name.replace("-", "_")
+        up[f"{key}/unknown"], up[f"{key}/known"] = unknown.detach(), known.detach()
+        up[f"{key}/features"], up[f"{key}/weights"] = features.detach(), weights.detach()
+        up[f"{key}/gradient"] = gradient
+        for field, dtype in (("nearest_indices", np.int32), ("distances", np.float32),
+                             ("interpolate_indices", np.int32), ("interpolated", np.float32),
+                             ("feature_gradient", np.float32), ("weight_gradient", np.float32)):
+            up[f"{key}/{field}"] = np.asarray(case[field], dtype=dtype)
+    save("pointnet2_upstream_cuda", **up)
+
+    # PointNet++ SSG segmentation fixture: the xyz of docs/parity/pointnet2-segmentation-
+    # synthetic-fixture.npz and the 12 selection arrays the reference recorded on MPS
+    # (docs/parity/pointnet2-segmentation-mps-safe.npz); its CPU path reproduces all 12.
+    fx = np.load(REF / "docs/parity/pointnet2-segmentation-synthetic-fixture.npz")
+    mps = np.load(REF / "docs/parity/pointnet2-segmentation-mps-safe.npz")
+    sel = {k.replace("::", "_"): mps[k] for k in mps.files if k.startswith("selection::")}
+    save("pointnet2_segmentation", xyz=fx["points"][..., :3].copy(), **sel)
+
+
+# ------------------------------------------------------------------ Chamfer
+def chamfer_cases():
+    out = {}
+
+    def add(name, x, y, lx=None, ly=None):
+        B = x.shape[0]
+        flx = torch.full((B,), x.shape[1], dtype=torch.long) if lx is None else lx
+        fly = torch.full((B,), y.shape[1], dtype=torch.long) if ly is None else ly
+        ix = ref_chamfer._nearest_indices(x, y, flx, fly)           # chamfer.py:161-212
+        iy = ref_chamfer._nearest_indices(y, x, fly, flx)
+        dx = ref_chamfer._selected_squared_distance(x, y, ix, flx)  # chamfer.py:297-308
+        dy = ref_chamfer._selected_squared_distance(y, x, iy, fly)
+        xr, yr = x.clone().requires_grad_(), y.clone().requires_grad_()
+        loss, _ = ref_chamfer.chamfer_distance(xr, yr, lx, ly)
+        loss.backward()
+        out[f"{name}/x"], out[f"{name}/y"] = x, y
+        if lx is not None:
+            out[f"{name}/x_lengths"], out[f"{name}/y_lengths"] = lx, ly
+        out[f"{name}/idx_x"], out[f"{name}/idx_y"] = ix, iy
+        out[f"{name}/dist_x"], out[f"{name}/dist_y"] = dx, dy
+        out[f"{name}/loss"] = loss.detach()
+        out[f"{name}/grad_x"], out[f"{name}/grad_y"] = xr.grad, yr.grad
+
+    gen = torch.Generator().manual_seed(137)                          # tests/test_chamfer.py:480-511
+    add("lengths", torch.randn((3, 13, 3), generator=gen), torch.randn((3, 67, 3), generator=gen),
+        torch.tensor([13, 4, 9]), torch.tensor([67, 39, 3]))
+    gen = torch.Generator().manual_seed(2026)                         # :431-449
+    add("uneven", torch.randn((2, 7, 3), generator=gen), torch.randn((2, 5, 3), generator=gen),
+        torch.tensor([7, 3]), torch.tensor([5, 2]))
+    q = torch.zeros((2, 9, 3))                                         # :452-477 (finite rows)
+    r = torch.full((2, 37, 3), 9.0)
+    r[:, 0], r[:, 31], r[:, 36] = torch.tensor([1.0, 0, 0]), torch.tensor([-1.0, 0, 0]), \
+        torch.tensor([0.0, 1, 0])
+    add("ties", q, r, torch.tensor([8, 7]), torch.tensor([37, 32]))
+    add("tie_reverse", torch.tensor([[[0.0, 0, 0], [2.0, 0, 0]]]), torch.tensor([[[1.0, 0, 0]]]))
+    g2 = torch.Generator().manual_seed(2)                              # BASELINE config 2 shape, smaller
+    x = torch.randn(2, 2048, 3, generator=g2)
+    g3 = torch.Generator().manual_seed(3)
+    y = x + 0.05 * torch.randn(2, 2048, 3, generator=g3)
+    y = torch.stack([y[b, torch.randperm(2048, generator=g3)] for b in range(2)])
+    add("config2_small", x, y)
+    g4 = torch.Generator().manual_seed(4)
+    add("d8", torch.randn(2, 33, 8, generator=g4), torch.randn(2, 45, 8, generator=g4))
+    save("chamfer", **out)
+
+
+if __name__ == "__main__":
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    fps_cases()
+    knn_cases()
+    feature_knn_cases()
+    ball_query_cases()
+    pointnet2_cases()
+    chamfer_cases()
+    for f in sorted(OUT.glob("*.npz")):
+        print(f"{f.name}: {f.stat().st_size / 1024:.0f} KiB")
