@@ -1,0 +1,375 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 point-op hot path (one JSON line on rank 0).
+
+Workload (the metric's single-GPU configuration):
+squared-L2 Chamfer distance forward + backward on B = 32 pairs of clouds of
+N = M = 8192 fp32 points per GPU, x ~ N(0,1)^3 and y = x + N(0,0.05)^3 in a
+per-cloud random permutation, mean/mean reduction, gradients for both clouds.
+A step is one `chamfer_distance(x, y)` + `loss.backward()` through the public
+API.  Metric: Chamfer pairs/s = B * N * M per step / step time (whole job).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 runs one process per GPU under torchrun (NCCL over NVLink): each rank
+owns 32 clouds (weak scaling) and the only collective is the all-reduce of the
+Chamfer loss partials.  `--impl reference` times the reference's CPU algorithm
+(the C restatement in oracle/, all host threads) on the same workload; under
+torchrun only rank 0 runs it.
+
+Also reported: `e2e` (the same step with the inputs copied from pinned host
+memory and the loss read back every step), the live CUDA-event time of the
+dominant kernel against its roofline, the CPU baseline, SM clocks sampled
+during the timed region, the native kernel launch count, and a secondary
+line for BASELINE config 1 (FPS + ball query + kNN, clouds/s).
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "mps-pointops_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+B_PER_GPU, NPTS, D = 32, 8192, 3
+FLOPS_PER_PAIR = 8  # 3 sub + 3 mul + 2 add, each rounded (no FMA)
+METRIC = "Chamfer pairs/sec"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def chamfer_inputs(batch: int, seed: int):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(batch, NPTS, D, generator=g)
+    y = x + 0.05 * torch.randn(batch, NPTS, D, generator=g)
+    y = torch.stack([y[b, torch.randperm(NPTS, generator=g)] for b in range(batch)])
+    return x.contiguous(), y.contiguous()
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    QUERY = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def mark(self, begin: bool):
+        if begin:
+            self.t0 = time.monotonic()
+        else:
+            self.t1 = time.monotonic()
+
+    def stop(self, bus_ids: set[str]) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 10]
+        mine = [r for r in rows if r[1].strip().lower()[-12:] in bus_ids] or rows
+        sm = [float(r[2]) for r in mine if r[2].strip().replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in mine if r[3].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in mine for i in range(4) if "Active" in r[6 + i]})
+        if not sm:
+            return None
+        busy = [s for s in sm if s > 0.5 * max(sm)]
+        return {"sm_mhz": statistics.median(busy or sm), "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ distributed
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ B200 arm
+def chamfer_step(x, y, world, group_batch):
+    from mps_pointops.chamfer import chamfer_distance
+    from mps_pointops.dist import chamfer_distance_sharded
+    xr = x.detach().requires_grad_()
+    yr = y.detach().requires_grad_()
+    if world > 1:
+        loss = chamfer_distance_sharded(xr, yr, group_batch)
+    else:
+        loss, _ = chamfer_distance(xr, yr)
+    loss.backward()
+    return loss
+
+
+def timed_steps(fn, steps: int, flush: torch.Tensor | None) -> list[float]:
+    """Per-step CUDA-event times (ms); the L2 flush between steps is untimed."""
+    times = []
+    s = torch.cuda.current_stream()
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        fn()
+        b.record(s)
+        times.append((a, b))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in times]
+
+
+def ssg_secondary(steps: int, warmup: int, world: int, rank: int) -> dict:
+    """compat FPS 1024 -> gather -> ball query (0.2, 32) ->
+    kNN k=16 on 8 uniform clouds of 4096 points per GPU; clouds/s."""
+    from mps_pointops import compat, knn
+    g = torch.Generator().manual_seed(1000 * rank)
+    xyz = torch.rand(8, 4096, 3, generator=g).cuda()
+
+    def step():
+        idx = compat.furthest_point_sample(xyz, 1024)
+        centres = compat.gather_operation(xyz.transpose(1, 2).contiguous(), idx)
+        centres = centres.transpose(1, 2).contiguous()
+        compat.ball_query(0.2, 32, xyz, centres)
+        knn(centres, xyz, 16)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = statistics.mean(timed_steps(step, steps, None))
+    ms = max_over_ranks(ms, world)
+    return {"metric": "clouds/sec for FPS+ball_query+kNN (B=8,N=4096)",
+            "value": 8 * world / (ms / 1e3), "unit": "clouds/s", "ms_per_step": ms,
+            "config": {"workload": "ssg_config1", "global_batch": 8 * world, "points": 4096}}
+
+
+def cpu_baseline_sample(max_seconds: float = 15.0) -> dict:
+    """The oracle (C restatement of the reference's CPU Chamfer search,
+    mps_pointops/chamfer.py:161-251) on the bench inputs, forward + backward,
+    all host threads, over as many clouds as fit in ~max_seconds."""
+    from oracle import oracle as O
+    x, y = chamfer_inputs(B_PER_GPU, seed=2)
+    xn, yn = x.numpy(), y.numpy()
+    t0 = time.perf_counter()
+    done = 0
+    while done < B_PER_GPU:
+        O.chamfer_mean_loss_and_grad(xn[done:done + 1], yn[done:done + 1])
+        done += 1
+        if time.perf_counter() - t0 > max_seconds:
+            break
+    sec = time.perf_counter() - t0
+    return {"value": done * NPTS * NPTS / sec, "unit": "pairs/s", "cores": O.threads(),
+            "kind": "port",
+            "sample": f"{done} of {B_PER_GPU} cloud pairs (8192 x 8192), forward+backward, "
+                      f"{sec:.1f} s"}
+
+
+def run_b200(args, world, rank, local):
+    from mps_pointops import _native as N
+    from mps_pointops.chamfer import chamfer_distance  # noqa: F401  (import before timing)
+    dev = torch.device("cuda", local)
+    N.lib()
+    group_batch = B_PER_GPU * world
+    x_cpu, y_cpu = chamfer_inputs(B_PER_GPU, seed=2 + 1000 * rank)
+    x, y = x_cpu.to(dev), y_cpu.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    props = torch.cuda.get_device_properties(dev)
+    bus = {str(getattr(props, "pci_bus_id", "")).lower()[-12:]}
+
+    for _ in range(max(args.warmup, 3)):
+        chamfer_step(x, y, world, group_batch)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = ClockSampler()
+    clocks.start()
+    time.sleep(0.3)
+    launches0 = N.launch_count()
+    clocks.mark(True)
+    with N.KernelTimer("chamfer_nearest") as ktimer:
+        step_ms = timed_steps(lambda: chamfer_step(x, y, world, group_batch), args.steps, flush)
+    clocks.mark(False)
+    launches = N.launch_count() - launches0
+    barrier(world)
+    clock_info = clocks.stop(bus)
+    ms = max_over_ranks(statistics.mean(step_ms), world)
+    kernel_ms = max_over_ranks(ktimer.mean_ms(), world)
+    pairs_per_step = group_batch * NPTS * NPTS
+    value = pairs_per_step / (ms / 1e3)
+
+    # e2e: public API with pinned host inputs, H2D every step, loss read back.
+    xh, yh = x_cpu.pin_memory(), y_cpu.pin_memory()
+
+    def e2e_step():
+        xd = xh.to(dev, non_blocking=True)
+        yd = yh.to(dev, non_blocking=True)
+        return float(chamfer_step(xd, yd, world, group_batch).item())
+
+    for _ in range(2):
+        e2e_step()
+    barrier(world)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        e2e_step()
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
+
+    secondary = None if args.no_secondary else ssg_secondary(args.steps, args.warmup, world, rank)
+
+    # Roofline of the dominant kernel: the nearest search (8 rounded flops per
+    # unique pair) against the FP32 add/mul issue peak.
+    local_pairs = B_PER_GPU * NPTS * NPTS
+    achieved = local_pairs * FLOPS_PER_PAIR / (kernel_ms / 1e3) / 1e12
+    sm_max = (clock_info or {}).get("sm_max_mhz") or 1965.0
+    peak = 128 * props.multi_processor_count * sm_max * 1e6 / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "chamfer_nearest_config2.txt"
+    if tfile.exists():
+        for line in tfile.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                traffic = float(line.split(":", 1)[1])
+    out = {
+        "metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic, seeded: x ~ N(0,1)^3, y = x + N(0,0.05)^3, per-cloud permutation",
+        "config": {"workload": "chamfer_config2_fwd_bwd", "global_batch": group_batch,
+                   "points_per_cloud": NPTS, "dims": D, "reduction": "mean/mean",
+                   "parallelism": f"dp{world}",
+                   "l2": "flushed between timed steps (256 MiB write, untimed)"},
+        "e2e": {"value": pairs_per_step / (e2e_ms / 1e3), "unit": "pairs/s",
+                "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(x_cpu.numel() * 4 + y_cpu.numel() * 4),
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": int(max_over_ranks(float(launches), world)),
+        "roofline": {"kernel": "nearest3_kernel (both directions, mpo_chamfer_nearest)",
+                     "bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel_ms": kernel_ms,
+                     "work": f"{FLOPS_PER_PAIR} flop x {local_pairs} unique pairs per launch",
+                     "peak_source": "nominal FP32 add/mul issue rate: 128 lanes x "
+                                    f"{props.multi_processor_count} SMs x {sm_max:.0f} MHz "
+                                    "(MEASURED_PEAKS.json has no FP32 figure)"},
+        "clocks": clock_info,
+    }
+    if secondary:
+        out["secondary"] = secondary
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline_sample()
+    return out
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args) -> dict:
+    """The reference's CPU algorithm (oracle/ C restatement of
+    mps_pointops/chamfer.py:161-251 + the mean reductions) on the bench
+    workload, every host thread; each step is one cloud pair of the batch."""
+    from oracle import oracle as O
+    O.build()
+    x, y = chamfer_inputs(B_PER_GPU, seed=2)
+    xn, yn = x.numpy(), y.numpy()
+    for i in range(min(args.warmup, 1)):
+        O.chamfer_mean_loss_and_grad(xn[i:i + 1], yn[i:i + 1])
+    steps = max(1, min(args.steps, 8))
+    t0 = time.perf_counter()
+    for i in range(steps):
+        O.chamfer_mean_loss_and_grad(xn[i % B_PER_GPU:i % B_PER_GPU + 1],
+                                     yn[i % B_PER_GPU:i % B_PER_GPU + 1])
+    sec = (time.perf_counter() - t0) / steps
+    value = NPTS * NPTS / sec
+    return {"metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": sec * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic, seeded (same inputs as the b200 arm)", "impl": "reference",
+            "config": {"workload": "chamfer_config2_fwd_bwd", "global_batch": B_PER_GPU,
+                       "points_per_cloud": NPTS, "dims": D, "reduction": "mean/mean",
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": "pairs/s", "cores": O.threads(),
+                             "kind": "port",
+                             "sample": f"{steps} steps of 1 cloud pair (8192 x 8192), "
+                                       "forward+backward, C restatement of the reference's "
+                                       "CPU path"},
+            "e2e": {"value": value, "unit": "pairs/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        print(json.dumps(run_reference(args)), flush=True)
+        return
+    world, rank, local = init_dist()
+    try:
+        out = run_b200(args, world, rank, local)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

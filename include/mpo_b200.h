@@ -1,0 +1,196 @@
+/*
+ * mpo_b200.h -- C ABI of libmpo_b200.so, the sm_100a (B200) kernels behind
+ * the point-cloud hot path of gamzerA/mps-pointops v1.0.0.
+ *
+ * Conventions (every entry point):
+ *   - Pointers are CUDA device pointers to dense row-major arrays on the
+ *     current device; shapes are given by the int64 sizes.  float = IEEE
+ *     binary32.  Nullable pointers say so.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call
+ *     only enqueues work and returns; results are ready when the stream is.
+ *   - Outputs and workspaces are owned by the caller.  Every output slot is
+ *     written, padding included.  Nothing is allocated inside the library.
+ *   - The return value is 0 (MPO_OK) or an MPO_ERR_* code; mpo_last_error()
+ *     then holds a message (per calling thread).
+ *   - Squared distances are ((d0*d0 + d1*d1) + d2*d2) for D == 3 and the
+ *     sequential sum for D != 3, d = a - b, each operation rounded on its own
+ *     (no FMA), exactly as the reference's CPU code; ties go to the lowest
+ *     index.
+ *
+ * Each declaration cites the reference interface it replaces (paths relative
+ * to the reference project).  The reference dispatches to Metal through
+ * torch.mps.compile_shader (mps_pointops/ops.py:33-37); these entry points
+ * take the place of those `library.<kernel>(...)` calls.
+ */
+#ifndef MPO_B200_H_
+#define MPO_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MPO_API __attribute__((visibility("default")))
+#else
+#define MPO_API
+#endif
+
+#define MPO_ABI_VERSION 1
+
+#define MPO_OK 0
+#define MPO_ERR_INVALID_ARGUMENT 1
+#define MPO_ERR_CUDA 2
+#define MPO_ERR_UNSUPPORTED 3
+#define MPO_ERR_WORKSPACE_TOO_SMALL 4
+
+/* ABI version of the loaded library (MPO_ABI_VERSION). */
+MPO_API int32_t mpo_abi_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+MPO_API const char* mpo_last_error(void);
+
+/* Number of kernels this library has launched in the process (all devices,
+ * all threads).  No counterpart in the reference; used to count the native
+ * launches inside a timed region. */
+MPO_API uint64_t mpo_launch_count(void);
+
+/* MPO_OK if `device` is an sm_100 part this build runs on, else
+ * MPO_ERR_UNSUPPORTED.  Replaces the Metal runtime probes
+ * mps_pointops/_ball_query_mps.py:34-63 (_require_compile_shader,
+ * _check_simd_width). */
+MPO_API int mpo_device_supported(int device);
+
+/* ------------------------------------------------------------------ FPS
+ * Replaces the `furthest_point_sample` and `fps_update_partials` /
+ * `fps_reduce_partials` dispatches of mps_pointops/ops.py:53-141
+ * (kernels fps.metal:19-107, fps_multigroup.metal:10-133); contract of
+ * mps_pointops/reference.py:27-58.
+ *   xyz (B,N,3) -> out (B,npoint), int64 or, with out_int32 != 0, int32
+ *   (the pointnet2_ops form of mps_pointops/compat.py:53-59).
+ *   skip_near_origin: points with ((x*x+y*y)+z*z) < fl32(1e-3) are never
+ *   picked after the start.  Requires N >= 1 when npoint > 0 and
+ *   0 <= start_idx < N.  strategy mirrors the reference's `strategy=`
+ *   argument: MPO_FPS_AUTO picks by size, MPO_FPS_SINGLE runs one CTA per
+ *   cloud (N <= 8192), MPO_FPS_GROUP spreads each cloud over a cooperative
+ *   group of CTAs (the large-cloud path, selectable at any size).  The
+ *   workspace (mpo_fps_workspace_bytes) holds the cross-CTA step slots of the
+ *   group path; status_out (nullable, device int32) receives 0, or 1 if a
+ *   bounded cross-CTA wait gave up. */
+#define MPO_FPS_AUTO 0
+#define MPO_FPS_SINGLE 1
+#define MPO_FPS_GROUP 2
+MPO_API size_t mpo_fps_workspace_bytes(int64_t B, int64_t N, int64_t npoint, int strategy);
+MPO_API int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
+                    int skip_near_origin, int out_int32, int strategy, void* out,
+                    int32_t* status_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ kNN
+ * Replaces the `knn` (D == 3, kernels/knn.metal:32-140) and
+ * `feature_knn_dense` (D != 3, kernels/feature_knn.metal:51-164) dispatches
+ * of mps_pointops/ops.py:144-205.
+ *   query (B,M,D), ref (B,N,D) -> dist (B,M,k) Euclidean (sqrt after
+ *   selection), idx (B,M,k) int64, sorted by (squared distance, index).
+ *   sqdist (nullable, (B,M,k)) receives the squared distances before the
+ *   square root.  1 <= k <= min(N, 256).  D == 3 drops NaN candidates and
+ *   ranks +inf; D != 3 drops every non-finite candidate; unfilled slots are
+ *   (inf, -1). */
+MPO_API int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int64_t D,
+            int64_t k, float* dist, int64_t* idx, float* sqdist, void* stream);
+
+/* ------------------------------------------------------------------ ball query
+ * Replaces the `ball_query_f32` dispatch of mps_pointops/_ball_query_mps.py:
+ * 122-166 (kernels/ball_query.metal:30-124) behind ops.ball_query
+ * (mps_pointops/ops.py:208-227); contract of mps_pointops/reference.py:83-121.
+ *   query (B,M,3), ref (B,N,3), radius_sq = fl32(fl32(r)*fl32(r)) ->
+ *   dist2 (B,M,K) f32 and idx (B,M,K) int64: the first K reference points in
+ *   input order with squared distance < radius_sq; empty slots (-1, 0).
+ *   query_lengths / ref_lengths (nullable, (B,) int64): queries at or beyond
+ *   query_lengths[b] are all padding, references at or beyond ref_lengths[b]
+ *   never match (mps_pointops/_ball_query_mps.py:73-84). */
+MPO_API int mpo_ball_query(const float* query, const float* ref, const int64_t* query_lengths,
+                   const int64_t* ref_lengths, int64_t B, int64_t M, int64_t N, int64_t K,
+                   float radius_sq, float* dist2, int64_t* idx, void* stream);
+
+/* pointnet2_ops form (mps_pointops/compat.py:76-85): xyz (B,N,3), new_xyz
+ * (B,npoint,3) -> idx (B,npoint,nsample) int32 where an empty slot repeats
+ * the query's first hit, and a query without hits is all zeros. */
+MPO_API int mpo_ball_query_pointnet2(const float* xyz, const float* new_xyz, int64_t B, int64_t N,
+                             int64_t npoint, int64_t nsample, float radius_sq, int32_t* idx,
+                             void* stream);
+
+/* Backward of the squared distances (mps_pointops/_ball_query_mps.py:168-203):
+ * grad_query[b,m] = sum_s 2 g (q - x_idx), grad_ref[b,idx] -= 2 g (q - x_idx)
+ * over the slots with idx >= 0.  grad_query and grad_ref (nullable) are
+ * overwritten. */
+MPO_API int mpo_ball_query_backward(const float* grad_dist2, const float* query, const float* ref,
+                            const int64_t* idx, int64_t B, int64_t M, int64_t N, int64_t K,
+                            float* grad_query, float* grad_ref, void* stream);
+
+/* ------------------------------------------------------------------ PointNet++ propagation
+ * Replaces `three_nn_f32` (kernels/pointnet2.metal:8-50) behind
+ * mps_pointops/pointnet2.py:75-100; contract of pointnet2.py:54-72.
+ *   unknown (B,N,3), known (B,M,3), M >= 3 -> dist (B,N,3) Euclidean,
+ *   idx (B,N,3) int32, ordered by (squared distance, index) with NaN last. */
+MPO_API int mpo_three_nn(const float* unknown, const float* known, int64_t B, int64_t N, int64_t M,
+                 float* dist, int32_t* idx, void* stream);
+
+/* Replaces `three_interpolate_f32` (kernels/pointnet2.metal:52-71) behind
+ * mps_pointops/pointnet2.py:150-166; contract of pointnet2.py:135-147.
+ *   features (B,C,M), idx (B,N,3) int32 in [0,M), weights (B,N,3) ->
+ *   out (B,C,N) = ((f0*w0 + f1*w1) + f2*w2). */
+MPO_API int mpo_three_interpolate(const float* features, const int32_t* idx, const float* weights,
+                          int64_t B, int64_t C, int64_t M, int64_t N, float* out, void* stream);
+
+/* Replaces `three_interpolate_backward_f32` (kernels/pointnet2.metal:76-103)
+ * behind mps_pointops/pointnet2.py:168-188: grad_features (B,C,M) is
+ * overwritten with sum over (n,t) of grad_out[b,c,n] * weights[b,n,t] at
+ * idx[b,n,t]. */
+MPO_API int mpo_three_interpolate_backward(const float* grad_out, const int32_t* idx,
+                                   const float* weights, int64_t B, int64_t C, int64_t M,
+                                   int64_t N, float* grad_features, void* stream);
+
+/* ------------------------------------------------------------------ Chamfer
+ * Replaces `chamfer_nearest_f32` / `chamfer_nearest_nd_f32`
+ * (kernels/chamfer_nn.metal:13-82, 159-226) behind
+ * mps_pointops/chamfer.py:122-158; contract of chamfer.py:161-212 and
+ * 297-308 (squared L2).
+ *   x (B,P,D), y (B,Q,D), lengths (nullable, (B,) int64) ->
+ *   idx_x (B,P): the first y index with the smallest squared distance among
+ *   y[:y_lengths[b]] (the first valid y even if every distance overflows to
+ *   +inf), -1 for padded x rows or an empty y cloud; dist_x (B,P) its squared
+ *   distance, 0 where idx_x is -1.  With bidirectional != 0 the same is
+ *   computed for y against x into dist_y / idx_y from the same pair
+ *   evaluations.  The workspace (mpo_chamfer_workspace_bytes) holds the
+ *   partial column minima. */
+MPO_API size_t mpo_chamfer_workspace_bytes(int64_t B, int64_t P, int64_t Q, int64_t D,
+                                   int bidirectional);
+MPO_API int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths,
+                        const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q, int64_t D,
+                        int bidirectional, float* dist_x, int64_t* idx_x, float* dist_y,
+                        int64_t* idx_y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward of the selected squared distances (mps_pointops/chamfer.py:215-251)
+ * for one or both directions: for every x row with idx_x >= 0,
+ *   g = 2 * grad_dist_x * (x - y[idx_x]);  grad_x += g;  grad_y[idx_x] -= g
+ * and symmetrically for y rows when grad_dist_y is non-NULL.  grad_x and
+ * grad_y are overwritten. */
+MPO_API int mpo_chamfer_backward(const float* x, const float* y, int64_t B, int64_t P, int64_t Q,
+                         int64_t D, const int64_t* idx_x, const float* grad_dist_x,
+                         const int64_t* idx_y, const float* grad_dist_y, float* grad_x,
+                         float* grad_y, void* stream);
+
+/* Input checks of mps_pointops/chamfer.py:79-110 in one launch: flags
+ * (device int32[4]) receive {x has a non-finite valid coordinate, the same
+ * for y, x_lengths outside [0,P], y_lengths outside [0,Q]}, each 0 or 1. */
+MPO_API int mpo_chamfer_check_inputs(const float* x, const float* y, const int64_t* x_lengths,
+                                     const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q,
+                                     int64_t D, int32_t* flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MPO_B200_H_ */

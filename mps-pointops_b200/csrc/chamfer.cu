@@ -1,0 +1,370 @@
+// Squared-L2 Chamfer nearest-neighbour search, its backward and its input
+// check, on sm_100a.
+//
+// Contract: gamzerA/mps-pointops mps_pointops/chamfer.py:161-212 and 297-308
+// (norm = 2): for each query row i < query_lengths[b], the FIRST reference
+// index j < ref_lengths[b] with the smallest SD; if every SD overflows to
+// +inf the first valid reference (index 0) is still selected; dist = SD of the
+// selected pair.  Padded query rows and clouds without a valid reference give
+// (dist 0, index -1).  Backward: chamfer.py:227-251.
+//
+// Design (B200), per direction:
+//   * One thread owns one (query, split); a CTA of 256 threads covers 256/S
+//     queries of one cloud and S splits.  Reference tiles of 1024 points are
+//     staged as float4 in shared memory (double-buffered through registers)
+//     and read with warp-broadcast loads.
+//   * Hot loop: 4 distances, their minimum (3 min ops) and ONE compare with
+//     the running best; only when the block minimum improves does the thread
+//     locate the first position attaining it.  Within a thread indices grow,
+//     so strict < keeps the lowest index; splits merge with (SD, index) order.
+#include <string>
+
+#include "../../include/mpo_b200.h"
+#include "mpo_common.cuh"
+
+namespace mpo {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kTile = 1024;
+constexpr uint32_t kNone = 0xffffffffu;
+
+__global__ void __launch_bounds__(kThreads)
+nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
+                const int64_t* __restrict__ query_lengths, const int64_t* __restrict__ ref_lengths,
+                int64_t M, int64_t N, int S, float* __restrict__ out_dist,
+                int64_t* __restrict__ out_idx) {
+    extern __shared__ float4 tile[];  // [2][kTile]
+    __shared__ float m_d[kThreads];
+    __shared__ uint32_t m_i[kThreads];
+    const int b = blockIdx.y;
+    const int qpc = kThreads / S;
+    const int tid = threadIdx.x;
+    const int split = tid / qpc;
+    const int ql = tid % qpc;
+    const int64_t q = (int64_t)blockIdx.x * qpc + ql;
+    const int64_t qlen = query_lengths ? query_lengths[b] : M;
+    const int64_t nl = ref_lengths ? min64(ref_lengths[b], N) : N;
+    const bool active = q < M && q < qlen;
+    const float* __restrict__ r = ref + (size_t)b * (size_t)N * 3;
+
+    float qx = 0.f, qy = 0.f, qz = 0.f;
+    if (active) {
+        const float* qp = query + ((size_t)b * (size_t)M + (size_t)q) * 3;
+        qx = qp[0];
+        qy = qp[1];
+        qz = qp[2];
+    }
+    float bd = INFINITY;
+    uint32_t bj = kNone;
+
+    const int64_t ntiles = ceil_div(nl, kTile);
+    const int slice = kTile / S;
+    constexpr int kLoads = 3 * kTile / kThreads;
+    float pre[kLoads];
+#define MPO_LOAD_TILE(t)                                                   \
+    do {                                                                   \
+        const int64_t base_ = (t) * kTile * 3;                             \
+        _Pragma("unroll") for (int u = 0; u < kLoads; ++u) {               \
+            const int64_t e_ = base_ + tid + (int64_t)u * kThreads;        \
+            pre[u] = e_ < nl * 3 ? r[e_] : 0.f;                            \
+        }                                                                  \
+    } while (0)
+#define MPO_STORE_TILE(buf)                                                \
+    do {                                                                   \
+        float* t_ = reinterpret_cast<float*>(tile + (buf) * kTile);        \
+        _Pragma("unroll") for (int u = 0; u < kLoads; ++u) {               \
+            const int e_ = tid + u * kThreads;                             \
+            t_[(e_ / 3) * 4 + (e_ % 3)] = pre[u];                          \
+        }                                                                  \
+    } while (0)
+    if (ntiles > 0) {
+        MPO_LOAD_TILE(0);
+        MPO_STORE_TILE(0);
+    }
+    __syncthreads();
+    for (int64_t t = 0; t < ntiles; ++t) {
+        const int buf = (int)(t & 1);
+        if (t + 1 < ntiles) MPO_LOAD_TILE(t + 1);
+        if (active) {
+            const float4* tp = tile + buf * kTile + split * slice;
+            const int64_t j0 = t * kTile + (int64_t)split * slice;
+            const int cnt = (int)max64(0, min64(slice, nl - j0));
+            int e = 0;
+            for (; e + 4 <= cnt; e += 4) {
+                float dd[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float4 p = tp[e + u];
+                    dd[u] = sqd3(qx, qy, qz, p.x, p.y, p.z);
+                }
+                const float m = fminf(fminf(dd[0], dd[1]), fminf(dd[2], dd[3]));
+                if (m < bd) {
+                    const int u = dd[0] == m ? 0 : dd[1] == m ? 1 : dd[2] == m ? 2 : 3;
+                    bd = m;
+                    bj = (uint32_t)(j0 + e + u);
+                }
+            }
+            for (; e < cnt; ++e) {
+                const float4 p = tp[e];
+                const float d = sqd3(qx, qy, qz, p.x, p.y, p.z);
+                if (d < bd) {
+                    bd = d;
+                    bj = (uint32_t)(j0 + e);
+                }
+            }
+        }
+        if (t + 1 < ntiles) MPO_STORE_TILE(buf ^ 1);
+        __syncthreads();
+    }
+#undef MPO_LOAD_TILE
+#undef MPO_STORE_TILE
+    if (S > 1) {
+        m_d[tid] = bd;
+        m_i[tid] = bj;
+        __syncthreads();
+        if (split == 0) {
+            for (int o = 1; o < S; ++o) {
+                const float d = m_d[o * qpc + ql];
+                const uint32_t j = m_i[o * qpc + ql];
+                if (j != kNone && (bj == kNone || d < bd || (d == bd && j < bj))) {
+                    bd = d;
+                    bj = j;
+                }
+            }
+        }
+    }
+    if (split != 0 || q >= M) return;
+    const size_t o = (size_t)b * (size_t)M + (size_t)q;
+    if (!active || nl <= 0) {
+        out_dist[o] = 0.f;
+        out_idx[o] = -1;
+        return;
+    }
+    if (bj == kNone) {  // every SD overflowed: the first valid reference
+        bj = 0;
+        bd = sqd3(qx, qy, qz, r[0], r[1], r[2]);
+    }
+    out_dist[o] = bd;
+    out_idx[o] = (int64_t)bj;
+}
+
+// Generic D (feature-space Chamfer): query row and reference tile in shared
+// memory, SD accumulated in increasing dimension order.
+constexpr int kDThreads = 128;
+
+__global__ void __launch_bounds__(kDThreads)
+nearestd_kernel(const float* __restrict__ query, const float* __restrict__ ref,
+                const int64_t* __restrict__ query_lengths, const int64_t* __restrict__ ref_lengths,
+                int64_t M, int64_t N, int D, int tileN, float* __restrict__ out_dist,
+                int64_t* __restrict__ out_idx) {
+    extern __shared__ float smemf[];
+    const int tid = threadIdx.x;
+    const int b = blockIdx.y;
+    const int64_t q = (int64_t)blockIdx.x * kDThreads + tid;
+    const int64_t qlen = query_lengths ? query_lengths[b] : M;
+    const int64_t nl = ref_lengths ? min64(ref_lengths[b], N) : N;
+    const bool active = q < M && q < qlen;
+    const int qs = D + 1;
+    float* sq = smemf;
+    float* st = smemf + (size_t)kDThreads * qs;
+    for (int e = tid; e < kDThreads * D; e += kDThreads) {
+        const int qq = e / D, t = e % D;
+        const int64_t gq = (int64_t)blockIdx.x * kDThreads + qq;
+        sq[qq * qs + t] = gq < M ? query[((size_t)b * M + gq) * D + t] : 0.f;
+    }
+    const float* __restrict__ r = ref + (size_t)b * (size_t)N * D;
+    const float* myq = sq + tid * qs;
+    float bd = INFINITY;
+    uint32_t bj = kNone;
+    for (int64_t t0 = 0; t0 < nl; t0 += tileN) {
+        __syncthreads();
+        const int64_t lim = min64((int64_t)tileN * D, (nl - t0) * D);
+        for (int64_t e = tid; e < lim; e += kDThreads) st[e] = r[t0 * D + e];
+        __syncthreads();
+        if (!active) continue;
+        const int cnt = (int)min64(tileN, nl - t0);
+        for (int e = 0; e < cnt; ++e) {
+            const float* rp = st + (size_t)e * D;
+            float dd = __fsub_rn(myq[0], rp[0]);
+            float s = __fmul_rn(dd, dd);
+            for (int u = 1; u < D; ++u) {
+                dd = __fsub_rn(myq[u], rp[u]);
+                s = __fadd_rn(s, __fmul_rn(dd, dd));
+            }
+            if (s < bd) {
+                bd = s;
+                bj = (uint32_t)(t0 + e);
+            }
+        }
+    }
+    if (q >= M) return;
+    const size_t o = (size_t)b * (size_t)M + (size_t)q;
+    if (!active || nl <= 0) {
+        out_dist[o] = 0.f;
+        out_idx[o] = -1;
+        return;
+    }
+    if (bj == kNone) {
+        bj = 0;
+        bd = sqd_seq(query + o * D, r, D);
+    }
+    out_dist[o] = bd;
+    out_idx[o] = (int64_t)bj;
+}
+
+// Backward for one direction: rows with idx >= 0 add
+// g = 2 * gd * (q - r[idx]) to grad_q and -g to grad_r[idx].
+__global__ void chamfer_bwd_kernel(const float* __restrict__ qpts, const float* __restrict__ rpts,
+                                   int64_t B, int64_t M, int64_t N, int64_t D,
+                                   const int64_t* __restrict__ idx, const float* __restrict__ gd,
+                                   float* __restrict__ grad_q, float* __restrict__ grad_r) {
+    const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= B * M) return;
+    const int64_t j = idx[row];
+    if (j < 0) return;
+    const int64_t b = row / M;
+    const float c = 2.0f * gd[row];
+    const float* qp = qpts + row * D;
+    const float* rp = rpts + (b * N + j) * D;
+    float* gq = grad_q + row * D;
+    float* gr = grad_r + (b * N + j) * D;
+    for (int64_t t = 0; t < D; ++t) {
+        const float g = __fmul_rn(__fsub_rn(qp[t], rp[t]), c);
+        atomicAdd(gq + t, g);
+        atomicAdd(gr + t, -g);
+    }
+}
+
+__global__ void check_inputs_kernel(const float* __restrict__ pts,
+                                    const int64_t* __restrict__ lengths, int64_t B, int64_t M,
+                                    int64_t D, int32_t* __restrict__ bad_value,
+                                    int32_t* __restrict__ bad_length) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (lengths && e < B) {
+        const int64_t len = lengths[e];
+        if (len < 0 || len > M) *bad_length = 1;
+    }
+    if (e >= B * M * D) return;
+    const int64_t row = e / D;
+    const int64_t b = row / M;
+    const int64_t i = row % M;
+    const int64_t len = lengths ? lengths[b] : M;
+    if (i < len && !isfinite(pts[e])) *bad_value = 1;
+}
+
+}  // namespace
+}  // namespace mpo
+
+extern "C" {
+
+size_t mpo_chamfer_workspace_bytes(int64_t B, int64_t P, int64_t Q, int64_t D,
+                                   int bidirectional) {
+    (void)B;
+    (void)P;
+    (void)Q;
+    (void)D;
+    (void)bidirectional;
+    return 0;
+}
+
+static int nearest_dir(const float* q, const float* r, const int64_t* ql, const int64_t* rl,
+                       int64_t B, int64_t M, int64_t N, int64_t D, float* dist, int64_t* idx,
+                       cudaStream_t s) {
+    using namespace mpo;
+    if (B == 0 || M == 0) return kOk;
+    if (D == 3) {
+        int S = 1;
+        while (S < 8 && B * M * S < (int64_t)sm_count() * 1024) S *= 2;
+        const int qpc = kThreads / S;
+        const size_t smem = 2 * kTile * sizeof(float4);
+        if (cudaFuncSetAttribute(nearest3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem) != cudaSuccess)
+            return fail(kCudaError, "chamfer: cannot raise the shared-memory limit");
+        dim3 grid((unsigned)ceil_div(M, qpc), (unsigned)B);
+        nearest3_kernel<<<grid, kThreads, smem, s>>>(q, r, ql, rl, M, N, S, dist, idx);
+        return check_launch("nearest3_kernel");
+    }
+    int tileN = 256;
+    size_t smem = ((size_t)kDThreads * (D + 1) + (size_t)tileN * D) * sizeof(float);
+    while (smem > 200 * 1024 && tileN > 1) {
+        tileN /= 2;
+        smem = ((size_t)kDThreads * (D + 1) + (size_t)tileN * D) * sizeof(float);
+    }
+    if (smem > 200 * 1024) return fail(kUnsupported, "chamfer: coordinate dimension too large");
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(nearestd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return fail(kCudaError, "chamfer: cannot raise the shared-memory limit");
+    dim3 grid((unsigned)ceil_div(M, kDThreads), (unsigned)B);
+    nearestd_kernel<<<grid, kDThreads, smem, s>>>(q, r, ql, rl, M, N, (int)D, tileN, dist, idx);
+    return check_launch("nearestd_kernel");
+}
+
+int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths,
+                        const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q, int64_t D,
+                        int bidirectional, float* dist_x, int64_t* idx_x, float* dist_y,
+                        int64_t* idx_y, void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace mpo;
+    (void)workspace;
+    (void)workspace_bytes;
+    MPO_REQUIRE(B >= 0 && P >= 0 && Q >= 0 && D >= 1, "bad sizes");
+    MPO_REQUIRE(B <= 65535, "batch must be at most 65535");
+    MPO_REQUIRE(P < (int64_t)0x7fffffff && Q < (int64_t)0x7fffffff, "clouds must be below 2**31");
+    cudaStream_t s = (cudaStream_t)stream;
+    int st = nearest_dir(x, y, x_lengths, y_lengths, B, P, Q, D, dist_x, idx_x, s);
+    if (st || !bidirectional) return st;
+    return nearest_dir(y, x, y_lengths, x_lengths, B, Q, P, D, dist_y, idx_y, s);
+}
+
+int mpo_chamfer_backward(const float* x, const float* y, int64_t B, int64_t P, int64_t Q,
+                         int64_t D, const int64_t* idx_x, const float* grad_dist_x,
+                         const int64_t* idx_y, const float* grad_dist_y, float* grad_x,
+                         float* grad_y, void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(B >= 0 && P >= 0 && Q >= 0 && D >= 1, "bad sizes");
+    MPO_REQUIRE(grad_x && grad_y, "null gradient pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (B * P * D > 0 && cudaMemsetAsync(grad_x, 0, sizeof(float) * B * P * D, s) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_backward: memset failed");
+    if (B * Q * D > 0 && cudaMemsetAsync(grad_y, 0, sizeof(float) * B * Q * D, s) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_backward: memset failed");
+    if (grad_dist_x && B * P > 0) {
+        chamfer_bwd_kernel<<<(unsigned)ceil_div(B * P, 256), 256, 0, s>>>(
+            x, y, B, P, Q, D, idx_x, grad_dist_x, grad_x, grad_y);
+        int st = check_launch("chamfer_bwd_kernel");
+        if (st) return st;
+    }
+    if (grad_dist_y && B * Q > 0) {
+        chamfer_bwd_kernel<<<(unsigned)ceil_div(B * Q, 256), 256, 0, s>>>(
+            y, x, B, Q, P, D, idx_y, grad_dist_y, grad_y, grad_x);
+        return check_launch("chamfer_bwd_kernel");
+    }
+    return kOk;
+}
+
+int mpo_chamfer_check_inputs(const float* x, const float* y, const int64_t* x_lengths,
+                             const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q,
+                             int64_t D, int32_t* flags, void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(flags, "null flag pointer");
+    MPO_REQUIRE(B >= 0 && P >= 0 && Q >= 0 && D >= 1, "bad sizes");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(flags, 0, 4 * sizeof(int32_t), s) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_check_inputs: memset failed");
+    const int64_t nx = max64(B * P * D, B), ny = max64(B * Q * D, B);
+    if (nx > 0) {
+        check_inputs_kernel<<<(unsigned)ceil_div(nx, 256), 256, 0, s>>>(x, x_lengths, B, P, D,
+                                                                          flags + 0, flags + 2);
+        int st = check_launch("check_inputs_kernel");
+        if (st) return st;
+    }
+    if (ny > 0) {
+        check_inputs_kernel<<<(unsigned)ceil_div(ny, 256), 256, 0, s>>>(y, y_lengths, B, Q, D,
+                                                                          flags + 1, flags + 3);
+        return check_launch("check_inputs_kernel");
+    }
+    return kOk;
+}
+
+}  // extern "C"

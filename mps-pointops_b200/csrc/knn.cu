@@ -1,0 +1,546 @@
+// Brute-force k-nearest-neighbour search (xyz and feature space) and the
+// k = 3 PointNet++ specialisation, on sm_100a.
+//
+// Contracts (gamzerA/mps-pointops):
+//   knn       mps_pointops/ops.py:144-205; exact order of tests/test_knn.py:15-23
+//             and tests/test_feature_knn.py:16-35: ascending (SD, index),
+//             Euclidean distance = sqrt(SD) taken after selection.
+//   three_nn  mps_pointops/pointnet2.py:54-100: the same order with NaN after
+//             every number (torch's stable argsort), int32 indices.
+//
+// Design (B200):
+//   * One thread owns one (query, split).  A CTA of 256 threads covers
+//     256/S queries of one cloud and S splits; split s scans the s-th slice
+//     of every reference tile, so each warp (one split, 32 queries) reads the
+//     same shared-memory address -> broadcast, no bank conflicts.
+//   * Reference tiles (1024 points, stored as float4) are staged through
+//     shared memory, double-buffered: the next tile is loaded into registers
+//     with coalesced scalar loads while the current one is scanned.
+//   * The running top-k list (capacity K in {4, 8, 16, 32}) lives in
+//     registers, sorted by (SD, index).  The hot loop costs the 8 rounded
+//     float ops of the distance plus ONE compare against the current k-th
+//     distance (`!(d > kth)`); the register insertion runs only for the rare
+//     candidate that passes.  Within one thread the reference index grows
+//     monotonically, so a tie with the k-th entry never displaces it.
+//   * After the scan, splits 1..S-1 publish their lists to shared memory and
+//     split 0 merges them with the full (SD, index) order.
+//   * k in (32, 256] uses a warp-per-query kernel whose sorted list is spread
+//     over the 32 lanes (8 slots each) and updated with ballot/shuffle.
+#include <string>
+
+#include "../../include/mpo_b200.h"
+#include "mpo_common.cuh"
+
+namespace mpo {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kTile = 1024;  // reference points per shared-memory tile (D == 3)
+constexpr uint32_t kNoIndex = 0xffffffffu;
+
+// Candidate policies.
+enum Policy : int {
+    kDropNaN = 0,        // kNN, D == 3: NaN never enters, +inf is ranked
+    kDropNonFinite = 1,  // kNN, D != 3: every non-finite SD is dropped
+    kNaNLast = 2,        // three_nn: NaN ranks after every number
+};
+
+template <int POLICY>
+__device__ __forceinline__ bool admissible(float d) {
+    if (POLICY == kDropNaN) return !isnan(d);
+    if (POLICY == kDropNonFinite) return isfinite(d);
+    return true;
+}
+
+// Strict (SD, index) order; with kNaNLast a NaN sorts after every number and
+// NaNs sort by index.
+template <int POLICY>
+__device__ __forceinline__ bool before(float d, uint32_t i, float e, uint32_t j) {
+    if (POLICY == kNaNLast) {
+        const bool dn = isnan(d), en = isnan(e);
+        if (dn != en) return en;
+        if (dn) return i < j;
+    }
+    return d < e || (d == e && i < j);
+}
+
+// Register-resident sorted list of capacity K.  The logical list of runtime
+// length k (<= K) is right-aligned: physical slot s holds logical entry
+// s - (K - k); the K - k leading slots hold (-inf, 0) sentinels that precede
+// every candidate and never move.  The k-th entry is therefore always in the
+// static slot K - 1 and no register array is ever indexed dynamically.
+template <int K, int POLICY>
+struct TopK {
+    float d[K];
+    uint32_t i[K];
+    int cnt;   // filled logical entries
+    int base;  // K - k
+
+    __device__ __forceinline__ void init(int k) {
+        base = K - k;
+#pragma unroll
+        for (int s = 0; s < K; ++s) {
+            d[s] = s < base ? -INFINITY : INFINITY;
+            i[s] = s < base ? 0u : kNoIndex;
+        }
+        cnt = 0;
+    }
+
+    // Offer (dd, jj): the candidate bubbles down the sorted list, swapping
+    // with every entry it precedes (empty slots always yield).
+    __device__ __forceinline__ void offer(float dd, uint32_t jj) {
+        if (!admissible<POLICY>(dd)) return;
+        if (cnt >= K - base && !before<POLICY>(dd, jj, d[K - 1], i[K - 1])) return;
+        const int empty_from = base + cnt;
+#pragma unroll
+        for (int s = 0; s < K; ++s) {
+            const bool take = (s >= empty_from) || before<POLICY>(dd, jj, d[s], i[s]);
+            const float od = d[s];
+            const uint32_t oi = i[s];
+            d[s] = take ? dd : od;
+            i[s] = take ? jj : oi;
+            dd = take ? od : dd;
+            jj = take ? oi : jj;
+        }
+        cnt = min(cnt + 1, K - base);
+    }
+
+    // Threshold for the hot-loop filter: a candidate with d > kth can never
+    // enter (NaN and ties are decided in offer()).  Empty slots hold +inf.
+    __device__ __forceinline__ float kth() const { return d[K - 1]; }
+    __device__ __forceinline__ bool full() const { return cnt >= K - base; }
+};
+
+// --------------------------------------------------------------------------
+// D == 3 kernel.
+template <int K, int POLICY>
+__global__ void __launch_bounds__(kThreads)
+knn3_kernel(const float* __restrict__ query, const float* __restrict__ ref, int64_t M, int64_t N,
+            int k, int S, float* __restrict__ dist, int64_t* __restrict__ idx64,
+            int32_t* __restrict__ idx32, float* __restrict__ sqdist) {
+    extern __shared__ float4 smem4[];
+    float4* tile = smem4;  // [2][kTile]
+    const int b = blockIdx.y;
+    const int qpc = kThreads / S;
+    const int tid = threadIdx.x;
+    const int split = tid / qpc;
+    const int ql = tid % qpc;
+    const int64_t q = (int64_t)blockIdx.x * qpc + ql;
+    const bool active = q < M;
+    const float* __restrict__ r = ref + (size_t)b * (size_t)N * 3;
+
+    float qx = 0.f, qy = 0.f, qz = 0.f;
+    if (active) {
+        const float* qp = query + ((size_t)b * (size_t)M + (size_t)q) * 3;
+        qx = qp[0];
+        qy = qp[1];
+        qz = qp[2];
+    }
+    TopK<K, POLICY> top;
+    top.init(k);
+
+    const int64_t ntiles = ceil_div(N, kTile);
+    const int slice = kTile / S;
+    constexpr int kLoads = 3 * kTile / kThreads;  // 12 scalar loads per thread per tile
+    float pre[kLoads];
+
+#define MPO_LOAD_TILE(t)                                                   \
+    do {                                                                   \
+        const int64_t base_ = (t) * kTile * 3;                             \
+        _Pragma("unroll") for (int u = 0; u < kLoads; ++u) {               \
+            const int64_t e_ = base_ + tid + (int64_t)u * kThreads;        \
+            pre[u] = e_ < N * 3 ? r[e_] : 0.f;                             \
+        }                                                                  \
+    } while (0)
+#define MPO_STORE_TILE(buf)                                                \
+    do {                                                                   \
+        float* t_ = reinterpret_cast<float*>(tile + (buf) * kTile);        \
+        _Pragma("unroll") for (int u = 0; u < kLoads; ++u) {               \
+            const int e_ = tid + u * kThreads;                             \
+            t_[(e_ / 3) * 4 + (e_ % 3)] = pre[u];                          \
+        }                                                                  \
+    } while (0)
+
+    if (ntiles > 0) {
+        MPO_LOAD_TILE(0);
+        MPO_STORE_TILE(0);
+    }
+    __syncthreads();
+    for (int64_t t = 0; t < ntiles; ++t) {
+        const int buf = (int)(t & 1);
+        if (t + 1 < ntiles) MPO_LOAD_TILE(t + 1);
+        if (active) {
+            const float4* tp = tile + buf * kTile + split * slice;
+            const int64_t j0 = t * kTile + split * slice;
+            const int cnt = (int)max64(0, min64(slice, N - j0));
+            float thr = top.kth();
+            for (int e = 0; e < cnt; e += 4) {
+                float dd[4];
+                unsigned hit = 0;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float4 p = tp[e + u];
+                    dd[u] = sqd3(qx, qy, qz, p.x, p.y, p.z);
+                    hit |= (!(dd[u] > thr) && e + u < cnt) ? (1u << u) : 0u;
+                }
+                while (hit) {
+                    const int u = __ffs(hit) - 1;
+                    hit &= hit - 1;
+                    const float d = u == 0 ? dd[0] : u == 1 ? dd[1] : u == 2 ? dd[2] : dd[3];
+                    top.offer(d, (uint32_t)(j0 + e + u));
+                }
+                thr = top.kth();
+            }
+        }
+        if (t + 1 < ntiles) MPO_STORE_TILE(buf ^ 1);
+        __syncthreads();
+    }
+#undef MPO_LOAD_TILE
+#undef MPO_STORE_TILE
+
+    // Merge the S split lists into split 0 (full (SD, index) order).
+    if (S > 1) {
+        float* md = reinterpret_cast<float*>(smem4);
+        uint32_t* mi = reinterpret_cast<uint32_t*>(md + (size_t)kThreads * K);
+        if (split > 0) {
+#pragma unroll
+            for (int s = 0; s < K; ++s) {
+                md[(size_t)tid * K + s] = top.d[s];
+                mi[(size_t)tid * K + s] = top.i[s];
+            }
+        }
+        __syncthreads();
+        if (split == 0 && active) {
+            for (int o = 1; o < S; ++o) {
+                const int src = o * qpc + ql;
+                for (int s = K - k; s < K; ++s) {
+                    const uint32_t j = mi[(size_t)src * K + s];
+                    if (j == kNoIndex) break;
+                    const float d = md[(size_t)src * K + s];
+                    if (top.full() && !before<POLICY>(d, j, top.d[K - 1], top.i[K - 1])) break;
+                    top.offer(d, j);
+                }
+            }
+        }
+    }
+    if (split != 0 || !active) return;
+    const size_t row = ((size_t)b * (size_t)M + (size_t)q) * (size_t)k;
+#pragma unroll
+    for (int s = 0; s < K; ++s) {
+        const int l = s - top.base;
+        if (l >= 0) {
+            const bool filled = l < top.cnt;
+            const float d = filled ? top.d[s] : INFINITY;
+            dist[row + l] = sqrtf(d);
+            if (sqdist) sqdist[row + l] = d;
+            if (idx64) idx64[row + l] = filled ? (int64_t)top.i[s] : -1;
+            if (idx32) idx32[row + l] = filled ? (int32_t)top.i[s] : -1;
+        }
+    }
+}
+
+// --------------------------------------------------------------------------
+// Generic D kernel (feature space): the query row and the reference tile
+// both sit in shared memory; SD accumulates in increasing dimension order.
+constexpr int kFeatThreads = 128;
+
+template <int K, int POLICY>
+__global__ void __launch_bounds__(kFeatThreads)
+knnd_kernel(const float* __restrict__ query, const float* __restrict__ ref, int64_t M, int64_t N,
+            int D, int k, int S, int tileN, float* __restrict__ dist, int64_t* __restrict__ idx64,
+            float* __restrict__ sqdist) {
+    extern __shared__ float smemf[];
+    const int qpc = kFeatThreads / S;
+    const int tid = threadIdx.x;
+    const int split = tid / qpc;
+    const int ql = tid % qpc;
+    const int b = blockIdx.y;
+    const int64_t q = (int64_t)blockIdx.x * qpc + ql;
+    const bool active = q < M;
+    const int qstride = D + 1;  // odd stride: conflict-free per-thread rows
+    float* sq = smemf;                          // [qpc][D+1]
+    float* st = smemf + (size_t)qpc * qstride;  // [tileN][D]
+    for (int e = tid; e < qpc * D; e += kFeatThreads) {
+        const int qq = e / D, t = e % D;
+        const int64_t gq = (int64_t)blockIdx.x * qpc + qq;
+        sq[qq * qstride + t] = gq < M ? query[((size_t)b * M + gq) * D + t] : 0.f;
+    }
+    TopK<K, POLICY> top;
+    top.init(k);
+    const float* __restrict__ r = ref + (size_t)b * (size_t)N * D;
+    const float* myq = sq + ql * qstride;
+    const int slice = tileN / S;
+    for (int64_t t0 = 0; t0 < N; t0 += tileN) {
+        __syncthreads();
+        const int64_t lim = min64((int64_t)tileN * D, (N - t0) * D);
+        for (int64_t e = tid; e < lim; e += kFeatThreads) st[e] = r[t0 * D + e];
+        __syncthreads();
+        if (!active) continue;
+        const int64_t j0 = t0 + (int64_t)split * slice;
+        const int cnt = (int)max64(0, min64(slice, N - j0));
+        const float* tp = st + (size_t)split * slice * D;
+        float thr = top.kth();
+        for (int e = 0; e < cnt; ++e) {
+            const float* rp = tp + (size_t)e * D;
+            float dd = __fsub_rn(myq[0], rp[0]);
+            float s = __fmul_rn(dd, dd);
+            for (int u = 1; u < D; ++u) {
+                dd = __fsub_rn(myq[u], rp[u]);
+                s = __fadd_rn(s, __fmul_rn(dd, dd));
+            }
+            if (!(s > thr)) {
+                top.offer(s, (uint32_t)(j0 + e));
+                thr = top.kth();
+            }
+        }
+    }
+    if (S > 1) {
+        __syncthreads();
+        float* md = smemf;
+        uint32_t* mi = reinterpret_cast<uint32_t*>(md + (size_t)kFeatThreads * K);
+        if (split > 0) {
+#pragma unroll
+            for (int s = 0; s < K; ++s) {
+                md[(size_t)tid * K + s] = top.d[s];
+                mi[(size_t)tid * K + s] = top.i[s];
+            }
+        }
+        __syncthreads();
+        if (split == 0 && active) {
+            for (int o = 1; o < S; ++o) {
+                const int src = o * qpc + ql;
+                for (int s = K - k; s < K; ++s) {
+                    const uint32_t j = mi[(size_t)src * K + s];
+                    if (j == kNoIndex) break;
+                    const float d = md[(size_t)src * K + s];
+                    if (top.full() && !before<POLICY>(d, j, top.d[K - 1], top.i[K - 1])) break;
+                    top.offer(d, j);
+                }
+            }
+        }
+    }
+    if (split != 0 || !active) return;
+    const size_t row = ((size_t)b * (size_t)M + (size_t)q) * (size_t)k;
+#pragma unroll
+    for (int s = 0; s < K; ++s) {
+        const int l = s - top.base;
+        if (l >= 0) {
+            const bool filled = l < top.cnt;
+            const float d = filled ? top.d[s] : INFINITY;
+            dist[row + l] = sqrtf(d);
+            if (sqdist) sqdist[row + l] = d;
+            idx64[row + l] = filled ? (int64_t)top.i[s] : -1;
+        }
+    }
+}
+
+// --------------------------------------------------------------------------
+// Large k (32 < k <= 256): one warp per query, sorted list spread over the
+// lanes, slot s held by lane s % 32 in register s / 32.
+constexpr int kWarpSlots = 8;  // 8 * 32 = 256
+
+template <int POLICY>
+__global__ void __launch_bounds__(256)
+knn_warp_kernel(const float* __restrict__ query, const float* __restrict__ ref, int64_t M,
+                int64_t N, int D, int k, float* __restrict__ dist, int64_t* __restrict__ idx64,
+                float* __restrict__ sqdist) {
+    const int lane = threadIdx.x & 31;
+    const int64_t q = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int b = blockIdx.y;
+    if (q >= M) return;
+    const float* __restrict__ qp = query + ((size_t)b * M + q) * D;
+    const float* __restrict__ r = ref + (size_t)b * N * D;
+    float ld[kWarpSlots];
+    uint32_t li[kWarpSlots];
+#pragma unroll
+    for (int t = 0; t < kWarpSlots; ++t) {
+        ld[t] = INFINITY;
+        li[t] = kNoIndex;
+    }
+    int cnt = 0;  // warp-uniform
+    auto kth_pair = [&](float& kd, uint32_t& ki) {
+        const int tk = (k - 1) / 32;
+        float v = ld[0];
+        uint32_t w = li[0];
+#pragma unroll
+        for (int t = 1; t < kWarpSlots; ++t) {
+            v = (t == tk) ? ld[t] : v;
+            w = (t == tk) ? li[t] : w;
+        }
+        kd = __shfl_sync(FULL_MASK, v, (k - 1) % 32);
+        ki = __shfl_sync(FULL_MASK, w, (k - 1) % 32);
+    };
+    for (int64_t j0 = 0; j0 < N; j0 += 32) {
+        const int64_t j = j0 + lane;
+        float d = INFINITY;
+        if (j < N) d = (D == 3) ? sqd3(qp[0], qp[1], qp[2], r[3 * j], r[3 * j + 1], r[3 * j + 2])
+                                : sqd_seq(qp, r + (size_t)j * D, D);
+        // k-th entry (slot k-1) lives in lane (k-1)%32, register (k-1)/32.
+        float kd;
+        uint32_t ki;
+        kth_pair(kd, ki);
+        const bool cand = j < N && admissible<POLICY>(d) &&
+                          (cnt < k || before<POLICY>(d, (uint32_t)j, kd, ki));
+        unsigned pending = __ballot_sync(FULL_MASK, cand);
+        while (pending) {
+            const int src = __ffs(pending) - 1;
+            pending &= pending - 1;
+            const float cd = __shfl_sync(FULL_MASK, d, src);
+            const uint32_t ci = (uint32_t)(j0 + src);
+            // re-check against the (possibly updated) k-th entry
+            if (cnt >= k) {
+                float kd2;
+                uint32_t ki2;
+                kth_pair(kd2, ki2);
+                if (!before<POLICY>(cd, ci, kd2, ki2)) continue;
+            }
+            // position = number of filled entries ordered before the candidate
+            int below = 0;
+#pragma unroll
+            for (int t = 0; t < kWarpSlots; ++t) {
+                const int s = t * 32 + lane;
+                below += (s < cnt && before<POLICY>(ld[t], li[t], cd, ci)) ? 1 : 0;
+            }
+            const int pos = __reduce_add_sync(FULL_MASK, below);
+            // shift slots [pos, k-1) right by one
+            float prev_d_last = 0.f;
+            uint32_t prev_i_last = 0;
+#pragma unroll
+            for (int t = 0; t < kWarpSlots; ++t) {
+                float up_d = __shfl_up_sync(FULL_MASK, ld[t], 1);
+                uint32_t up_i = __shfl_up_sync(FULL_MASK, li[t], 1);
+                const float last_d = __shfl_sync(FULL_MASK, ld[t], 31);
+                const uint32_t last_i = __shfl_sync(FULL_MASK, li[t], 31);
+                if (lane == 0) {
+                    up_d = prev_d_last;
+                    up_i = prev_i_last;
+                }
+                prev_d_last = last_d;
+                prev_i_last = last_i;
+                const int s = t * 32 + lane;
+                if (s < k) {
+                    if (s > pos) {
+                        ld[t] = up_d;
+                        li[t] = up_i;
+                    } else if (s == pos) {
+                        ld[t] = cd;
+                        li[t] = ci;
+                    }
+                }
+            }
+            cnt = min(cnt + 1, k);
+        }
+    }
+    const size_t row = ((size_t)b * M + q) * (size_t)k;
+#pragma unroll
+    for (int t = 0; t < kWarpSlots; ++t) {
+        const int s = t * 32 + lane;
+        if (s < k) {
+            const bool filled = s < cnt;
+            const float d = filled ? ld[t] : INFINITY;
+            dist[row + s] = sqrtf(d);
+            if (sqdist) sqdist[row + s] = d;
+            idx64[row + s] = filled ? (int64_t)li[t] : -1;
+        }
+    }
+}
+
+int choose_splits(int64_t B, int64_t M, int64_t N) {
+    const int64_t want = (int64_t)sm_count() * 1024;
+    int S = 1;
+    while (S < 8 && B * M * S < want && N / (kTile / (S * 2)) > 0 && kTile / (S * 2) >= 32) S *= 2;
+    return S;
+}
+
+template <int K, int POLICY>
+int launch_knn3(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int k,
+                float* dist, int64_t* idx64, int32_t* idx32, float* sqdist, cudaStream_t s) {
+    const int S = choose_splits(B, M, N);
+    const int qpc = kThreads / S;
+    size_t smem = 2 * kTile * sizeof(float4);
+    const size_t merge = (size_t)kThreads * K * 8;
+    if (merge > smem) smem = merge;
+    auto kern = knn3_kernel<K, POLICY>;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+        return fail(kCudaError, "knn: cannot raise the shared-memory limit");
+    dim3 grid((unsigned)ceil_div(M, qpc), (unsigned)B);
+    kern<<<grid, kThreads, smem, s>>>(query, ref, M, N, k, S, dist, idx64, idx32, sqdist);
+    return check_launch("knn3_kernel");
+}
+
+template <int K>
+int launch_knnd(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int D,
+                int k, float* dist, int64_t* idx64, float* sqdist, cudaStream_t s) {
+    int S = 1;
+    while (S < 4 && B * M * S < (int64_t)sm_count() * 512) S *= 2;
+    const int qpc = kFeatThreads / S;
+    int tileN = 64 * S;
+    size_t smem = ((size_t)qpc * (D + 1) + (size_t)tileN * D) * sizeof(float);
+    while (smem > 200 * 1024 && tileN > S) {
+        tileN /= 2;
+        smem = ((size_t)qpc * (D + 1) + (size_t)tileN * D) * sizeof(float);
+    }
+    if (smem > 200 * 1024) return fail(kUnsupported, "knn: feature dimension too large");
+    const size_t merge = (size_t)kFeatThreads * K * 8;
+    if (merge > smem) smem = merge;
+    auto kern = knnd_kernel<K, kDropNonFinite>;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+        return fail(kCudaError, "knn: cannot raise the shared-memory limit");
+    dim3 grid((unsigned)ceil_div(M, qpc), (unsigned)B);
+    kern<<<grid, kFeatThreads, smem, s>>>(query, ref, M, N, D, k, S, tileN, dist, idx64, sqdist);
+    return check_launch("knnd_kernel");
+}
+
+}  // namespace
+}  // namespace mpo
+
+extern "C" {
+
+int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int64_t D,
+            int64_t k, float* dist, int64_t* idx, float* sqdist, void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(B >= 0 && M >= 0 && N >= 0 && D >= 1, "bad sizes");
+    MPO_REQUIRE(k >= 0 && k <= N, "k must be in [0, N]");
+    MPO_REQUIRE(k <= 256, "k must be at most 256");
+    MPO_REQUIRE(N < (int64_t)0x7fffffff && M < (int64_t)0x7fffffff, "M and N must be below 2**31");
+    if (B == 0 || M == 0 || k == 0) return kOk;
+    MPO_REQUIRE(query && ref && dist && idx, "null pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    const int kk = (int)k;
+    if (D == 3) {
+        if (k <= 4) return launch_knn3<4, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
+        if (k <= 8) return launch_knn3<8, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
+        if (k <= 16) return launch_knn3<16, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
+        if (k <= 32) return launch_knn3<32, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
+    } else if (D <= 4096) {
+        if (k <= 4) return launch_knnd<4>(query, ref, B, M, N, (int)D, kk, dist, idx, sqdist, s);
+        if (k <= 8) return launch_knnd<8>(query, ref, B, M, N, (int)D, kk, dist, idx, sqdist, s);
+        if (k <= 16) return launch_knnd<16>(query, ref, B, M, N, (int)D, kk, dist, idx, sqdist, s);
+        if (k <= 32) return launch_knnd<32>(query, ref, B, M, N, (int)D, kk, dist, idx, sqdist, s);
+    }
+    // Large k (or very wide features): warp per query.
+    dim3 grid((unsigned)ceil_div(M, 8), (unsigned)B);
+    if (D == 3)
+        knn_warp_kernel<kDropNaN><<<grid, 256, 0, s>>>(query, ref, M, N, (int)D, kk, dist, idx, sqdist);
+    else
+        knn_warp_kernel<kDropNonFinite><<<grid, 256, 0, s>>>(query, ref, M, N, (int)D, kk, dist, idx, sqdist);
+    return check_launch("knn_warp_kernel");
+}
+
+int mpo_three_nn(const float* unknown, const float* known, int64_t B, int64_t N, int64_t M,
+                 float* dist, int32_t* idx, void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(B >= 0 && N >= 0 && M >= 0, "bad sizes");
+    if (B == 0 || N == 0) return kOk;
+    MPO_REQUIRE(M >= 3, "three_nn needs at least 3 known points");
+    MPO_REQUIRE(M < (int64_t)0x7fffffff, "M must be below 2**31");
+    MPO_REQUIRE(unknown && known && dist && idx, "null pointer");
+    return launch_knn3<4, kNaNLast>(unknown, known, B, N, M, 3, dist, nullptr, idx, nullptr,
+                                    (cudaStream_t)stream);
+}
+
+}  // extern "C"

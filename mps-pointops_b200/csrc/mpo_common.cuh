@@ -1,0 +1,104 @@
+// Shared device helpers and host error plumbing for libmpo_b200.
+//
+// Arithmetic contract: every squared distance is formed with explicitly
+// rounded single-precision intrinsics (__fsub_rn / __fmul_rn / __fadd_rn),
+// which nvcc never contracts into an FMA, in the reference's order:
+//   D == 3 : ((d0*d0 + d1*d1) + d2*d2),   d = a - b
+//   D != 3 : s = d0*d0; s = s + dt*dt for t = 1 .. D-1
+// (gamzerA/mps-pointops mps_pointops/reference.py:21-24, chamfer.py:199-201).
+// The library is also compiled with -fmad=false so no other float expression
+// is contracted either.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace mpo {
+
+constexpr unsigned FULL_MASK = 0xffffffffu;
+
+// ------------------------------------------------------------------ errors
+// Status codes returned by every C-ABI entry point (see include/mpo_b200.h).
+enum Status : int {
+    kOk = 0,
+    kInvalidArgument = 1,
+    kCudaError = 2,
+    kUnsupported = 3,
+    kWorkspaceTooSmall = 4,
+};
+
+void set_last_error(const std::string& msg);
+int fail(int status, const std::string& msg);
+int check_launch(const char* what);  // also counts one kernel launch
+void count_launches(uint64_t n);
+int sm_count(int device = -1);
+int current_device();
+
+#define MPO_REQUIRE(cond, msg)                                   \
+    do {                                                         \
+        if (!(cond)) return ::mpo::fail(::mpo::kInvalidArgument, \
+                                        std::string(__func__) + ": " + (msg)); \
+    } while (0)
+
+// ------------------------------------------------------------------ math
+__device__ __forceinline__ float sqd3(float ax, float ay, float az, float bx, float by,
+                                      float bz) {
+    const float dx = __fsub_rn(ax, bx);
+    const float dy = __fsub_rn(ay, by);
+    const float dz = __fsub_rn(az, bz);
+    return __fadd_rn(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)), __fmul_rn(dz, dz));
+}
+
+// Sequential D-dimensional squared distance, a and b in registers or memory.
+__device__ __forceinline__ float sqd_seq(const float* a, const float* b, int D) {
+    float d = __fsub_rn(a[0], b[0]);
+    float s = __fmul_rn(d, d);
+    for (int t = 1; t < D; ++t) {
+        d = __fsub_rn(a[t], b[t]);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+    }
+    return s;
+}
+
+// NaN-propagating minimum (torch.minimum semantics): PTX min.NaN.f32.
+__device__ __forceinline__ float fmin_nan(float a, float b) {
+    float r;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+// Monotone map of a float onto uint32 (larger float -> larger key) for
+// argmax reductions.  -inf maps near 0, +inf to 0xff800000; NaN is mapped by
+// callers that need it.
+__device__ __forceinline__ uint32_t ordered_key(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float ordered_key_inv(uint32_t k) {
+    const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+    return __uint_as_float(u);
+}
+
+// Acquire / relaxed global loads used by the bounded spin waits.
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__host__ __device__ __forceinline__ int64_t ceil_div(int64_t a, int64_t b) {
+    return (a + b - 1) / b;
+}
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+}  // namespace mpo

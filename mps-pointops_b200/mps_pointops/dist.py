@@ -1,0 +1,118 @@
+"""Multi-GPU partitioning of the point-cloud ops (one process per GPU).
+
+The reference is single-device; this module adds the data-parallel layout of
+the batched workloads.  Independent clouds (or, for one very large cloud,
+contiguous query ranges against a replicated reference cloud) are split
+contiguously over the ranks of a ``torch.distributed`` process group; every
+rank runs the single-GPU kernels on its shard.  The only cross-rank traffic is
+
+* ``all_gather_shards``: an ``all_gather_into_tensor`` of per-shard outputs
+  (indices, distances) when every rank needs the full result, and
+* ``chamfer_distance_sharded``: one ``all_reduce(SUM)`` of the Chamfer loss
+  partials -- the gradients of a cloud depend only on that cloud, so no
+  gradient exchange is needed.
+
+Both go through NCCL over NVLink on GPUs and work with ``gloo`` on the CPU.
+The functions take the local op as a parameter (``local_fn``) so the
+partitioning logic can be exercised without a GPU.
+"""
+
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous [lo, hi) slice of ``total`` items owned by ``rank``; the first
+    ``total % world`` ranks get one extra item."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} for world size {world}")
+    base, extra = divmod(total, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def _world(group) -> tuple[int, int]:
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def all_gather_shards(local: torch.Tensor, total: int, dim: int = 0, group=None) -> torch.Tensor:
+    """Concatenate every rank's shard of a tensor split along ``dim`` by
+    :func:`shard_range` into the full tensor on every rank."""
+    rank, world = _world(group)
+    sizes = [shard_range(total, r, world) for r in range(world)]
+    longest = max(hi - lo for lo, hi in sizes)
+    moved = local.movedim(dim, 0).contiguous()
+    pad = longest - moved.shape[0]
+    if pad:
+        moved = torch.cat([moved, moved.new_zeros((pad, *moved.shape[1:]))])
+    out = moved.new_empty((world * longest, *moved.shape[1:]))
+    dist.all_gather_into_tensor(out, moved, group=group)
+    parts = [out[r * longest: r * longest + (hi - lo)] for r, (lo, hi) in enumerate(sizes)]
+    return torch.cat(parts).movedim(0, dim)
+
+
+def chamfer_distance_sharded(x_local: torch.Tensor, y_local: torch.Tensor, batch_total: int,
+                             group=None, local_fn: Callable | None = None) -> torch.Tensor:
+    """Mean/mean squared-L2 Chamfer loss over a batch split across ranks.
+
+    ``x_local`` / ``y_local`` hold this rank's clouds (its :func:`shard_range`
+    slice of ``batch_total``).  Returns the global loss (identical on every
+    rank); its backward yields exactly this rank's slice of the single-GPU
+    gradient, because loss = (1/B) * sum over clouds of the per-cloud loss.
+    """
+    if local_fn is None:
+        from .chamfer import chamfer_distance as local_fn
+    partial, _ = local_fn(x_local, y_local, batch_reduction="sum")
+    total = partial.detach().clone()
+    dist.all_reduce(total, op=dist.ReduceOp.SUM, group=group)
+    scale = 1.0 / max(batch_total, 1)
+    return partial * scale + (total - partial.detach()) * scale
+
+
+def knn_query_sharded(query: torch.Tensor, ref: torch.Tensor, k: int, group=None,
+                      gather: bool = True, local_fn: Callable | None = None):
+    """kNN of a large query set against a replicated reference cloud: rank r
+    searches its contiguous query slice; with ``gather`` the (dist, idx)
+    shards are all-gathered along the query axis."""
+    if local_fn is None:
+        from .ops import knn as local_fn
+    rank, world = _world(group)
+    lo, hi = shard_range(query.shape[1], rank, world)
+    d, i = local_fn(query[:, lo:hi], ref, k)
+    if not gather:
+        return d, i
+    return (all_gather_shards(d, query.shape[1], dim=1, group=group),
+            all_gather_shards(i, query.shape[1], dim=1, group=group))
+
+
+def ball_query_sharded(query: torch.Tensor, ref: torch.Tensor, radius: float, K: int, group=None,
+                       gather: bool = True, local_fn: Callable | None = None):
+    """Ball query of a large query set against a replicated reference cloud,
+    partitioned like :func:`knn_query_sharded`."""
+    if local_fn is None:
+        from .ops import ball_query as local_fn
+    rank, world = _world(group)
+    lo, hi = shard_range(query.shape[1], rank, world)
+    d, i = local_fn(query[:, lo:hi], ref, radius, K)
+    if not gather:
+        return d, i
+    return (all_gather_shards(d, query.shape[1], dim=1, group=group),
+            all_gather_shards(i, query.shape[1], dim=1, group=group))
+
+
+def batch_sharded(fn: Callable, *tensors: torch.Tensor, batch_total: int, group=None,
+                  gather: bool = True, **kwargs):
+    """Run ``fn`` on this rank's slice of independent clouds (dim 0) and
+    optionally all-gather every tensor output along dim 0."""
+    rank, world = _world(group)
+    lo, hi = shard_range(batch_total, rank, world)
+    out = fn(*(t[lo:hi] for t in tensors), **kwargs)
+    if not gather:
+        return out
+    if isinstance(out, torch.Tensor):
+        return all_gather_shards(out, batch_total, 0, group)
+    return tuple(all_gather_shards(o, batch_total, 0, group) for o in out)

@@ -1,0 +1,55 @@
+"""The C-ABI library loads here (no GPU) and exports what include/mpo_b200.h declares."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+from mps_pointops import _native as N
+
+HEADER = ROOT / "include" / "mpo_b200.h"
+
+
+def declared() -> set[str]:
+    return set(re.findall(r"^MPO_API\s+[\w\s\*]+?\b(mpo_\w+)\(", HEADER.read_text(), flags=re.M))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = N.lib()
+    names = declared()
+    assert len(names) >= 16
+    for name in names:
+        assert hasattr(lib, name), name
+    assert names == set(N.SIGNATURES), "ctypes signatures must mirror the header"
+
+
+def test_abi_version_and_error_channel():
+    lib = N.lib()
+    assert lib.mpo_abi_version() == N.ABI_VERSION == 1
+    # Argument validation happens before any CUDA call, so it runs without a GPU.
+    st = lib.mpo_knn(None, None, 1, 1, 1000, 3, 300, None, None, None, None)
+    assert st == 1
+    assert "at most 256" in N.last_error()
+    st = lib.mpo_fps(None, 1, 10, 4, 12, 0, 0, 0, None, None, None, 0, None)
+    assert st == 1 and "start_idx" in N.last_error()
+    st = lib.mpo_fps(None, 1, 10, 4, 0, 0, 0, 7, None, None, None, 0, None)
+    assert st == 1 and "strategy" in N.last_error()
+
+
+def test_workspace_queries():
+    lib = N.lib()
+    assert lib.mpo_fps_workspace_bytes(8, 4096, 1024, 0) == 0
+    assert lib.mpo_fps_workspace_bytes(1, 1 << 20, 65536, 0) > 0
+    assert lib.mpo_fps_workspace_bytes(3, 100, 10, 2) >= 3 * 32
+
+
+def test_no_oracle_in_product_package():
+    pkg = ROOT / "mps-pointops_b200"
+    for path in pkg.rglob("*.py"):
+        text = path.read_text()
+        assert "oracle" not in text.replace("# ", ""), path
+    for path in (pkg / "csrc").glob("*"):
+        assert "oracle" not in path.read_text(), path

@@ -1,0 +1,115 @@
+"""FPS on B200 vs the reference's CPU path (golden fixtures) and the oracle.
+
+Indices must be bit-exact (mps_pointops/reference.py:27-58 contract); cases
+follow gamzerA/mps-pointops tests/test_fps.py and tests/test_compat.py.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import mps_pointops
+from conftest import golden
+from mps_pointops import compat
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def cloud(b, n, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(b, n, 3, generator=g)
+
+
+@pytest.mark.parametrize("strategy", ["auto", "multigroup"])
+def test_golden_cases(cuda_device, strategy):
+    for name, c in golden("fps").items():
+        npoint, start, skip = (int(v) for v in c["meta"])
+        xyz = torch.from_numpy(c["xyz"]).to(cuda_device)
+        if strategy == "multigroup" and xyz.shape[0] > 1:
+            continue
+        got = mps_pointops.furthest_point_sample(xyz, npoint, start, bool(skip), strategy=strategy)
+        assert got.dtype == torch.long
+        np.testing.assert_array_equal(got.cpu().numpy(), c["idx"], err_msg=f"{name}/{strategy}")
+
+
+def test_compat_int32_skip_near_origin(cuda_device):
+    c = golden("fps")["skip_near_origin"]
+    got = compat.furthest_point_sample(torch.from_numpy(c["xyz"]).to(cuda_device), 2000)
+    assert got.dtype == torch.int32
+    np.testing.assert_array_equal(got.cpu().numpy(), c["idx"].astype(np.int32))
+    picked = set(got[0].tolist())
+    assert picked.isdisjoint(range(1, 41)) and 41 in picked
+    zeros = compat.furthest_point_sample(torch.zeros(1, 50, 3, device=cuda_device), 5)
+    assert zeros.tolist() == [[0, 0, 0, 0, 0]]
+
+
+@pytest.mark.parametrize("n", [1, 2, 31, 32, 33, 1023, 1024, 1025, 2049, 4096, 5000, 8192, 8193,
+                               20000])
+def test_sizes_match_oracle(cuda_device, n):
+    xyz = cloud(2, n, seed=n)
+    npoint = min(n, 300)
+    want = O.furthest_point_sample(xyz.numpy(), npoint, n // 3, False)
+    got = mps_pointops.furthest_point_sample(xyz.to(cuda_device), npoint, n // 3)
+    np.testing.assert_array_equal(got.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("n", [2, 33, 4097, 8193, 100_000])
+def test_group_path_matches_single(cuda_device, n):
+    xyz = cloud(1, n, seed=19).to(cuda_device)
+    auto = mps_pointops.furthest_point_sample(xyz, 128, start_idx=1, strategy="auto")
+    group = mps_pointops.furthest_point_sample(xyz, 128, start_idx=1, strategy="multigroup")
+    assert torch.equal(auto, group)
+    want = O.furthest_point_sample(xyz.cpu().numpy(), 128, 1, False)
+    np.testing.assert_array_equal(group.cpu().numpy(), want)
+
+
+def test_large_cloud_prefix_matches_oracle(cuda_device):
+    """BASELINE config 3 input (2^20 points on a jittered sphere), first 256 steps."""
+    g = torch.Generator().manual_seed(4)
+    p = torch.randn(1, 1 << 20, 3, generator=g)
+    p = p / p.norm(dim=-1, keepdim=True)
+    p = p * (1 + 0.01 * torch.randn(1, 1 << 20, 1, generator=g))
+    want = O.furthest_point_sample(p.numpy(), 256, 0, False)
+    got = mps_pointops.furthest_point_sample(p.to(cuda_device), 256)
+    np.testing.assert_array_equal(got.cpu().numpy(), want)
+
+
+def test_group_status_word_reports_success(cuda_device):
+    from mps_pointops import _native as N
+    xyz = cloud(1, 20000, seed=3).to(cuda_device)
+    out = torch.empty(1, 64, dtype=torch.long, device=cuda_device)
+    status = torch.full((1,), 7, dtype=torch.int32, device=cuda_device)
+    lib = N.lib()
+    ws = torch.empty(lib.mpo_fps_workspace_bytes(1, 20000, 64, 2), dtype=torch.uint8,
+                     device=cuda_device)
+    N.check(lib.mpo_fps(N.ptr(xyz), 1, 20000, 64, 0, 0, 0, 2, N.ptr(out), N.ptr(status),
+                        N.ptr(ws), ws.numel(), N.stream(cuda_device)), "fps")
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    np.testing.assert_array_equal(out.cpu().numpy(),
+                                  O.furthest_point_sample(xyz.cpu().numpy(), 64, 0, False))
+
+
+def test_noncontiguous_and_empty(cuda_device):
+    xyz = cloud(1, 4000)[:, ::2]
+    got = mps_pointops.furthest_point_sample(xyz.to(cuda_device), 100)
+    np.testing.assert_array_equal(got.cpu().numpy(),
+                                  O.furthest_point_sample(xyz.numpy(), 100, 0, False))
+    x = torch.randn(3, 50, 3, device=cuda_device)
+    assert mps_pointops.furthest_point_sample(x, 0).shape == (3, 0)
+    assert mps_pointops.furthest_point_sample(x[:0], 5).shape == (0, 5)
+    with pytest.raises(TypeError):
+        mps_pointops.furthest_point_sample(x.half(), 4)
+    with pytest.raises(ValueError, match="batch size 1"):
+        mps_pointops.furthest_point_sample(x, 8, strategy="multigroup")
+
+
+def test_nan_points_follow_torch_argmax(cuda_device):
+    xyz = cloud(1, 300, seed=5)
+    xyz[0, 17, 1] = float("nan")
+    want = O.furthest_point_sample(xyz.numpy(), 20, 0, False)
+    got = mps_pointops.furthest_point_sample(xyz.to(cuda_device), 20)
+    np.testing.assert_array_equal(got.cpu().numpy(), want)
