@@ -108,7 +108,8 @@ class ClockSampler:
         sm = [float(r[2]) for r in mine if r[2].strip().replace(".", "").isdigit()]
         mx = [float(r[3]) for r in mine if r[3].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in mine for i in range(4) if "Active" in r[6 + i]})
+        reasons = sorted({names[i] for r in mine for i in range(4)
+                          if r[6 + i].strip().lower() == "active"})
         if not sm:
             return None
         busy = [s for s in sm if s > 0.5 * max(sm)]
@@ -276,12 +277,13 @@ def run_b200(args, world, rank, local):
 
     secondary = None if args.no_secondary else ssg_secondary(args.steps, args.warmup, world, rank)
 
-    # Roofline of the dominant kernel: the nearest search (8 rounded flops per
-    # unique pair) against the FP32 add/mul issue peak.
+    # Roofline of the dominant kernel: the nearest search (8 separately rounded
+    # flops per unique pair) against the FP32 add/mul issue peak of packed
+    # f32x2 instructions, 2 x 128 lanes per SM per clock.
     local_pairs = B_PER_GPU * NPTS * NPTS
     achieved = local_pairs * FLOPS_PER_PAIR / (kernel_ms / 1e3) / 1e12
     sm_max = (clock_info or {}).get("sm_max_mhz") or 1965.0
-    peak = 128 * props.multi_processor_count * sm_max * 1e6 / 1e12
+    peak = 2 * 128 * props.multi_processor_count * sm_max * 1e6 / 1e12
     traffic = None
     tfile = ROOT / "profiles" / "chamfer_nearest_config2.txt"
     if tfile.exists():
@@ -302,14 +304,16 @@ def run_b200(args, world, rank, local):
                 "h2d_bytes_per_step": int(x_cpu.numel() * 4 + y_cpu.numel() * 4),
                 "d2h_bytes_per_step": 4},
         "gpu_launches": int(max_over_ranks(float(launches), world)),
-        "roofline": {"kernel": "nearest3_kernel (both directions, mpo_chamfer_nearest)",
+        "roofline": {"kernel": "chamfer_sym3_kernel + finalize (mpo_chamfer_nearest, both "
+                               "directions in one pass)",
                      "bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "kernel_ms": kernel_ms,
                      "work": f"{FLOPS_PER_PAIR} flop x {local_pairs} unique pairs per launch",
-                     "peak_source": "nominal FP32 add/mul issue rate: 128 lanes x "
+                     "peak_source": "nominal packed-f32x2 add/mul issue rate: 2 x 128 lanes x "
                                     f"{props.multi_processor_count} SMs x {sm_max:.0f} MHz "
-                                    "(MEASURED_PEAKS.json has no FP32 figure)"},
+                                    "(MEASURED_PEAKS.json has no FP32 figure; an fadd2+fmul2 "
+                                    "probe measured 71 TFLOP/s on this pool)"},
         "clocks": clock_info,
     }
     if secondary:

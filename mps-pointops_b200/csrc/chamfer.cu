@@ -149,6 +149,231 @@ nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
     out_idx[o] = (int64_t)bj;
 }
 
+// --------------------------------------------------------------------------
+// Symmetric D == 3 search: every (x_i, y_j) squared distance is evaluated
+// ONCE and feeds both the row minimum (x -> y) and the column minimum
+// (y -> x).
+//
+// Work item = (cloud, 1024 x-rows, 1024 y-columns); CTAs take items from an
+// atomic counter.  The y tile is staged in shared memory as duplicated pairs
+// ((y.x, y.x, y.y, y.y), (y.z, y.z, -, -)) so a warp-broadcast load yields
+// packed f32x2 operands.  Lane l of warp w owns x-rows
+// i0 + (32 w + l) * R .. + R - 1 (contiguous, so row order = (warp, lane, k)),
+// packed two per f32x2 register, and a warp walks the columns together:
+//   * rows: a running minimum over blocks of C columns (one min per pair),
+//     compared with the row's best once per block as raw bits (SD >= 0, so
+//     bit order == value order); the column inside the winning block is
+//     recovered at the end of the item by recomputing C distances;
+//   * columns: the lane's minimum over its R rows, then one redux.sync.min
+//     over the warp and one ballot of the lanes holding it -> one 64-bit
+//     (min bits, lane mask) record per (warp, column) in shared memory; at
+//     the end of the item a thread per column picks the first warp, the first
+//     lane and (recomputing R distances) the first row holding the minimum.
+// Both directions are committed as 64-bit keys (SD bits << 32 | index) with
+// atomicMin into global scratch, which yields the smallest SD and, among
+// equal SDs, the lowest index -- the reference's first-minimum rule.
+// Padding (index >= length) enters as +inf coordinates: it ties valid
+// entries only at +inf and then loses on index, and padding-vs-padding pairs
+// are NaN, which never wins a min.
+namespace sym {
+constexpr int kWarps = 4;
+constexpr int kR = 8;   // x-rows per lane (even: packed in pairs)
+constexpr int kC = 8;   // columns per row-minimum block
+constexpr int kThreads = kWarps * 32;
+constexpr int kBM = kWarps * 32 * kR;  // 1024 rows per item
+constexpr int kBN = 1024;              // columns per item
+constexpr size_t kSmem = (size_t)kBN * 2 * sizeof(float4) + (size_t)kWarps * kBN * 8;
+constexpr unsigned long long kMaxKey = ~0ull;
+
+__global__ void __launch_bounds__(kThreads, 3)
+chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
+                    const int64_t* __restrict__ x_lengths, const int64_t* __restrict__ y_lengths,
+                    int64_t B, int64_t P, int64_t Q, unsigned long long* __restrict__ keys_x,
+                    unsigned long long* __restrict__ keys_y, unsigned* __restrict__ counter) {
+    extern __shared__ float4 smem4[];
+    float4* s_col = smem4;                                                 // [kBN][2]
+    unsigned long long* s_part = reinterpret_cast<unsigned long long*>(smem4 + 2 * kBN);
+    __shared__ unsigned s_item;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t row_blocks = ceil_div(P, kBM), col_blocks = ceil_div(Q, kBN);
+    const int64_t per_cloud = row_blocks * col_blocks, total = B * per_cloud;
+
+    for (;;) {
+        if (tid == 0) s_item = atomicAdd(counter, 1u);
+        __syncthreads();
+        const int64_t item = s_item;
+        __syncthreads();
+        if (item >= total) break;
+        const int64_t b = item / per_cloud;
+        const int64_t rem = item % per_cloud;
+        const int64_t i0 = (rem / col_blocks) * kBM, j0 = (rem % col_blocks) * kBN;
+        const int64_t xlen = x_lengths ? min64(max64(x_lengths[b], 0), P) : P;
+        const int64_t ylen = y_lengths ? min64(max64(y_lengths[b], 0), Q) : Q;
+        if (i0 >= xlen || j0 >= ylen) continue;  // uniform: nothing valid here
+        const float* __restrict__ xb = x + (size_t)b * P * 3;
+        const float* __restrict__ yb = y + (size_t)b * Q * 3;
+
+        for (int e = tid; e < kBN; e += kThreads) {
+            const int64_t j = j0 + e;
+            float px = INFINITY, py = INFINITY, pz = INFINITY;
+            if (j < ylen) {
+                px = yb[3 * j];
+                py = yb[3 * j + 1];
+                pz = yb[3 * j + 2];
+            }
+            s_col[2 * e] = make_float4(px, px, py, py);
+            s_col[2 * e + 1] = make_float4(pz, pz, 0.f, 0.f);
+        }
+        const int64_t rbase = i0 + (int64_t)(warp * 32 + lane) * kR;
+        f32x2 X[kR / 2], Y[kR / 2], Z[kR / 2];
+#pragma unroll
+        for (int q = 0; q < kR / 2; ++q) {
+            float c[6];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int64_t r = rbase + 2 * q + h;
+                const bool ok = r < xlen;
+                c[3 * h + 0] = ok ? xb[3 * r + 0] : INFINITY;
+                c[3 * h + 1] = ok ? xb[3 * r + 1] : INFINITY;
+                c[3 * h + 2] = ok ? xb[3 * r + 2] : INFINITY;
+            }
+            X[q] = pack2(c[0], c[3]);
+            Y[q] = pack2(c[1], c[4]);
+            Z[q] = pack2(c[2], c[5]);
+        }
+        __syncthreads();
+
+        uint32_t best[kR];
+        int blk[kR];
+#pragma unroll
+        for (int k = 0; k < kR; ++k) {
+            best[k] = 0xffffffffu;
+            blk[k] = -1;
+        }
+        for (int jb = 0; jb < kBN; jb += kC) {
+            float m[kR];
+#pragma unroll
+            for (int c = 0; c < kC; ++c) {
+                const int j = jb + c;
+                const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(&s_col[2 * j]);
+                const f32x2 bz = *reinterpret_cast<const f32x2*>(&s_col[2 * j + 1]);
+                float d[kR];
+#pragma unroll
+                for (int q = 0; q < kR / 2; ++q) {
+                    const f32x2 dd = sqd3x2(X[q], Y[q], Z[q], a.x, a.y, bz);
+                    unpack2(dd, d[2 * q], d[2 * q + 1]);
+                }
+#pragma unroll
+                for (int k = 0; k < kR; ++k) m[k] = (c == 0) ? d[k] : fminf(m[k], d[k]);
+                float cm0 = fminf(d[0], d[1]), cm1 = fminf(d[2], d[3]);
+                float cm2 = fminf(d[4], d[5]), cm3 = fminf(d[6], d[7]);
+                const float cm = fminf(fminf(cm0, cm1), fminf(cm2, cm3));
+                const unsigned cb = __float_as_uint(cm);
+                const unsigned wmin = __reduce_min_sync(FULL_MASK, cb);
+                const unsigned mask = __ballot_sync(FULL_MASK, cb == wmin);
+                if (lane == 0) s_part[warp * kBN + j] = ((unsigned long long)wmin << 32) | mask;
+            }
+#pragma unroll
+            for (int k = 0; k < kR; ++k) {
+                const uint32_t mb = __float_as_uint(m[k]);
+                if (mb < best[k]) {
+                    best[k] = mb;
+                    blk[k] = jb;
+                }
+            }
+        }
+
+        // Rows: recover the first column of the winning block and commit.
+#pragma unroll
+        for (int k = 0; k < kR; ++k) {
+            const int64_t r = rbase + k;
+            if (r < xlen && blk[k] >= 0) {
+                float rx, ry, rz, t0, t1;
+                unpack2(X[k / 2], t0, t1);
+                rx = (k & 1) ? t1 : t0;
+                unpack2(Y[k / 2], t0, t1);
+                ry = (k & 1) ? t1 : t0;
+                unpack2(Z[k / 2], t0, t1);
+                rz = (k & 1) ? t1 : t0;
+                int col = blk[k];
+                for (int c = 0; c < kC; ++c) {
+                    const float4 pa = s_col[2 * (blk[k] + c)];
+                    const float4 pb = s_col[2 * (blk[k] + c) + 1];
+                    if (__float_as_uint(sqd3(rx, ry, rz, pa.x, pa.z, pb.x)) == best[k]) {
+                        col = blk[k] + c;
+                        break;
+                    }
+                }
+                atomicMin(&keys_x[(size_t)b * P + r],
+                          ((unsigned long long)best[k] << 32) | (unsigned long long)(j0 + col));
+            }
+        }
+        __syncthreads();
+        // Columns: first warp, first lane, first row holding the minimum.
+        for (int e = tid; e < kBN; e += kThreads) {
+            const int64_t j = j0 + e;
+            if (j >= ylen) continue;
+            unsigned bv = 0xffffffffu, bm = 0u;
+            int bw = 0;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const unsigned long long pv = s_part[w * kBN + e];
+                const unsigned v = (unsigned)(pv >> 32);
+                if (v < bv) {
+                    bv = v;
+                    bw = w;
+                    bm = (unsigned)pv;
+                }
+            }
+            const int l = __ffs(bm) - 1;
+            const int64_t r0 = i0 + (int64_t)(bw * 32 + l) * kR;
+            const float4 pa = s_col[2 * e];
+            const float4 pb = s_col[2 * e + 1];
+            int64_t row = r0;
+            for (int k = 0; k < kR; ++k) {
+                const int64_t r = r0 + k;
+                if (r >= xlen) break;
+                const float d = sqd3(xb[3 * r], xb[3 * r + 1], xb[3 * r + 2], pa.x, pa.z, pb.x);
+                if (__float_as_uint(d) == bv) {
+                    row = r;
+                    break;
+                }
+            }
+            atomicMin(&keys_y[(size_t)b * Q + j],
+                      ((unsigned long long)bv << 32) | (unsigned long long)row);
+        }
+        __syncthreads();
+    }
+}
+
+// Keys -> (squared distance, index) in the public layout; padded rows and
+// clouds whose other side is empty give (0, -1).
+__global__ void finalize_kernel(const unsigned long long* __restrict__ keys,
+                                const int64_t* __restrict__ self_lengths,
+                                const int64_t* __restrict__ other_lengths, int64_t B, int64_t M,
+                                int64_t N, float* __restrict__ dist, int64_t* __restrict__ idx) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= B * M) return;
+    const int64_t b = e / M, i = e % M;
+    const int64_t len = self_lengths ? self_lengths[b] : M;
+    const int64_t olen = other_lengths ? other_lengths[b] : N;
+    const unsigned long long key = keys[e];
+    if (i >= len || olen <= 0 || key == kMaxKey) {
+        dist[e] = 0.f;
+        idx[e] = -1;
+        return;
+    }
+    dist[e] = __uint_as_float((unsigned)(key >> 32));
+    idx[e] = (int64_t)(key & 0xffffffffull);
+}
+
+inline bool use_sym(int64_t P, int64_t Q, int64_t D) { return D == 3 && P >= 512 && Q >= 512; }
+
+inline size_t scratch_bytes(int64_t B, int64_t P, int64_t Q) {
+    return ((size_t)B * (P + Q)) * sizeof(unsigned long long) + 256;
+}
+}  // namespace sym
+
 // Generic D (feature-space Chamfer): query row and reference tile in shared
 // memory, SD accumulated in increasing dimension order.
 constexpr int kDThreads = 128;
@@ -260,12 +485,9 @@ extern "C" {
 
 size_t mpo_chamfer_workspace_bytes(int64_t B, int64_t P, int64_t Q, int64_t D,
                                    int bidirectional) {
-    (void)B;
-    (void)P;
-    (void)Q;
-    (void)D;
     (void)bidirectional;
-    return 0;
+    if (B <= 0 || !mpo::sym::use_sym(P, Q, D)) return 0;
+    return mpo::sym::scratch_bytes(B, P, Q);
 }
 
 static int nearest_dir(const float* q, const float* r, const int64_t* ql, const int64_t* rl,
@@ -292,8 +514,7 @@ static int nearest_dir(const float* q, const float* r, const int64_t* ql, const 
         smem = ((size_t)kDThreads * (D + 1) + (size_t)tileN * D) * sizeof(float);
     }
     if (smem > 200 * 1024) return fail(kUnsupported, "chamfer: coordinate dimension too large");
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(nearestd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(nearestd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
         return fail(kCudaError, "chamfer: cannot raise the shared-memory limit");
     dim3 grid((unsigned)ceil_div(M, kDThreads), (unsigned)B);
@@ -306,15 +527,45 @@ int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths
                         int bidirectional, float* dist_x, int64_t* idx_x, float* dist_y,
                         int64_t* idx_y, void* workspace, size_t workspace_bytes, void* stream) {
     using namespace mpo;
-    (void)workspace;
-    (void)workspace_bytes;
     MPO_REQUIRE(B >= 0 && P >= 0 && Q >= 0 && D >= 1, "bad sizes");
     MPO_REQUIRE(B <= 65535, "batch must be at most 65535");
     MPO_REQUIRE(P < (int64_t)0x7fffffff && Q < (int64_t)0x7fffffff, "clouds must be below 2**31");
     cudaStream_t s = (cudaStream_t)stream;
-    int st = nearest_dir(x, y, x_lengths, y_lengths, B, P, Q, D, dist_x, idx_x, s);
+    if (B == 0) return kOk;
+    if (!sym::use_sym(P, Q, D)) {
+        int st = nearest_dir(x, y, x_lengths, y_lengths, B, P, Q, D, dist_x, idx_x, s);
+        if (st || !bidirectional) return st;
+        return nearest_dir(y, x, y_lengths, x_lengths, B, Q, P, D, dist_y, idx_y, s);
+    }
+    const size_t need = sym::scratch_bytes(B, P, Q);
+    if (workspace == nullptr || workspace_bytes < need)
+        return fail(kWorkspaceTooSmall, "mpo_chamfer_nearest: workspace must hold " +
+                                            std::to_string(need) + " bytes");
+    unsigned long long* keys_x = reinterpret_cast<unsigned long long*>(workspace);
+    unsigned long long* keys_y = keys_x + (size_t)B * P;
+    unsigned* counter = reinterpret_cast<unsigned*>(keys_y + (size_t)B * Q);
+    if (cudaMemsetAsync(keys_x, 0xff, (size_t)B * (P + Q) * 8, s) != cudaSuccess ||
+        cudaMemsetAsync(counter, 0, sizeof(unsigned), s) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_nearest: scratch reset failed");
+    if (cudaFuncSetAttribute(sym::chamfer_sym3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sym::kSmem) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_nearest: shared-memory limit");
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sym::chamfer_sym3_kernel,
+                                                  sym::kThreads, sym::kSmem);
+    const int64_t items = B * ceil_div(P, sym::kBM) * ceil_div(Q, sym::kBN);
+    const int64_t grid = min64(items, (int64_t)sm_count() * max64(per_sm, 1));
+    sym::chamfer_sym3_kernel<<<(unsigned)grid, sym::kThreads, sym::kSmem, s>>>(
+        x, y, x_lengths, y_lengths, B, P, Q, keys_x, keys_y, counter);
+    int st = check_launch("chamfer_sym3_kernel");
+    if (st) return st;
+    sym::finalize_kernel<<<(unsigned)ceil_div(B * P, 256), 256, 0, s>>>(
+        keys_x, x_lengths, y_lengths, B, P, Q, dist_x, idx_x);
+    st = check_launch("chamfer finalize_kernel");
     if (st || !bidirectional) return st;
-    return nearest_dir(y, x, y_lengths, x_lengths, B, Q, P, D, dist_y, idx_y, s);
+    sym::finalize_kernel<<<(unsigned)ceil_div(B * Q, 256), 256, 0, s>>>(
+        keys_y, y_lengths, x_lengths, B, Q, P, dist_y, idx_y);
+    return check_launch("chamfer finalize_kernel");
 }
 
 int mpo_chamfer_backward(const float* x, const float* y, int64_t B, int64_t P, int64_t Q,
@@ -323,7 +574,7 @@ int mpo_chamfer_backward(const float* x, const float* y, int64_t B, int64_t P, i
                          float* grad_y, void* stream) {
     using namespace mpo;
     MPO_REQUIRE(B >= 0 && P >= 0 && Q >= 0 && D >= 1, "bad sizes");
-    MPO_REQUIRE(grad_x && grad_y, "null gradient pointer");
+    MPO_REQUIRE((grad_x || B * P * D == 0) && (grad_y || B * Q * D == 0), "null gradient pointer");
     cudaStream_t s = (cudaStream_t)stream;
     if (B * P * D > 0 && cudaMemsetAsync(grad_x, 0, sizeof(float) * B * P * D, s) != cudaSuccess)
         return fail(kCudaError, "mpo_chamfer_backward: memset failed");

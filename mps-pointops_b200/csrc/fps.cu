@@ -90,7 +90,11 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
         for (int64_t e = tid; e < 3 * N; e += nthr) s_xyz[e] = p[e];
     }
     if (tid == 0) s_abort = 0;
-    __syncthreads();
+    bool mine_nonfinite = false;
+#pragma unroll
+    for (int s = 0; s < P; ++s)
+        mine_nonfinite |= !(isfinite(px[s]) && isfinite(py[s]) && isfinite(pz[s]));
+    bool nan_mode = __syncthreads_or(mine_nonfinite) != 0;
 
     uint32_t far = (uint32_t)start_idx;
     float cx, cy, cz;
@@ -113,18 +117,38 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
         }
         if (i + 1 == npoint) break;
 
+        // NaN can only enter min_d2 through a non-finite coordinate of this
+        // CTA's points or of a centroid; from then on (sticky) the keys must
+        // rank NaN above every number, like torch.argmax.
+        nan_mode = nan_mode || !(isfinite(cx) && isfinite(cy) && isfinite(cz));
         uint32_t bkey = 0u, bidx = 0xffffffffu;
+        if (!nan_mode) {
 #pragma unroll
-        for (int s = 0; s < P; ++s) {
-            const int64_t j = lo + tid + (int64_t)s * nthr;
-            const bool valid = j < hi;
-            const float d = sqd3(px[s], py[s], pz[s], cx, cy, cz);
-            const float m = fmin_nan(md[s], d);
-            md[s] = valid ? m : md[s];
-            const uint32_t k = valid ? ordered_key(m) : 0u;
-            if (k > bkey) {
-                bkey = k;
-                bidx = (uint32_t)j;
+            for (int s = 0; s < P; ++s) {
+                const int64_t j = lo + tid + (int64_t)s * nthr;
+                const bool valid = j < hi;
+                const float d = sqd3(px[s], py[s], pz[s], cx, cy, cz);
+                const float m = fminf(md[s], d);
+                md[s] = valid ? m : md[s];
+                const uint32_t k = valid ? ordered_key(m) : 0u;
+                if (k > bkey) {
+                    bkey = k;
+                    bidx = (uint32_t)j;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int s = 0; s < P; ++s) {
+                const int64_t j = lo + tid + (int64_t)s * nthr;
+                const bool valid = j < hi;
+                const float d = sqd3(px[s], py[s], pz[s], cx, cy, cz);
+                const float m = fmin_nan(md[s], d);
+                md[s] = valid ? m : md[s];
+                const uint32_t k = !valid ? 0u : (isnan(m) ? 0xffffffffu : ordered_key(m));
+                if (k > bkey) {
+                    bkey = k;
+                    bidx = (uint32_t)j;
+                }
             }
         }
         const uint32_t wmax = __reduce_max_sync(FULL_MASK, bkey);
@@ -185,11 +209,9 @@ int launch_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t s
                GroupSync* sync, int32_t* status, cudaStream_t stream) {
     auto kern = fps_kernel<P, GROUP>;
     const size_t smem = GROUP ? 0 : (size_t)N * 3 * sizeof(float);
-    if (smem > 48 * 1024) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess) {
-            return fail(kCudaError, "mpo_fps: cannot raise the shared-memory limit");
-        }
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+        return fail(kCudaError, "mpo_fps: cannot set the shared-memory limit");
     }
     if (!GROUP) {
         kern<<<(unsigned)B, threads, smem, stream>>>(xyz, N, npoint, start_idx, skip, out_int32,

@@ -122,8 +122,7 @@ int mpo_three_interpolate_backward(const float* grad_out, const int32_t* idx,
     MPO_REQUIRE(grad_out && idx && weights, "null pointer");
     const size_t smem = (size_t)M * sizeof(float);
     if (smem <= 192 * 1024 && C <= 2147483647 && B <= 65535) {
-        if (smem > 48 * 1024 &&
-            cudaFuncSetAttribute(interp_bwd_smem_kernel,
+        if (cudaFuncSetAttribute(interp_bwd_smem_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem) != cudaSuccess)
             return fail(kCudaError, "three_interpolate_backward: shared-memory limit");

@@ -461,8 +461,7 @@ int launch_knn3(const float* query, const float* ref, int64_t B, int64_t M, int6
     const size_t merge = (size_t)kThreads * K * 8;
     if (merge > smem) smem = merge;
     auto kern = knn3_kernel<K, POLICY>;
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");
     dim3 grid((unsigned)ceil_div(M, qpc), (unsigned)B);
@@ -486,8 +485,7 @@ int launch_knnd(const float* query, const float* ref, int64_t B, int64_t M, int6
     const size_t merge = (size_t)kFeatThreads * K * 8;
     if (merge > smem) smem = merge;
     auto kern = knnd_kernel<K, kDropNonFinite>;
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");
     dim3 grid((unsigned)ceil_div(M, qpc), (unsigned)B);

@@ -62,6 +62,57 @@ __device__ __forceinline__ float sqd_seq(const float* a, const float* b, int D) 
     return s;
 }
 
+// Packed pairs of floats (PTX .f32x2, sm_100): two lanes of IEEE binary32
+// arithmetic per instruction, each rounded to nearest on its own -- the same
+// bits as two scalar __fsub_rn / __fmul_rn / __fadd_rn.  On B200 these issue
+// at twice the scalar FP32 rate.
+typedef unsigned long long f32x2;
+
+__device__ __forceinline__ f32x2 pack2(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2(f32x2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// Rounded square of both lanes, d*d.  ptxas contracts mul.rn.f32x2 followed
+// by add.rn.f32x2 into a fused f32x2 FMA even under -fmad=false, which would
+// change the low bit of about one squared distance in five.  The square is
+// therefore written as fma.rn(d, d, +0.0): for a square (never -0) this is
+// exactly the rounded product, and because fma(a, b, +0) differs from a*b
+// when a*b is -0, the optimizer cannot rewrite it into a multiply and then
+// contract it with the following add.
+__device__ __forceinline__ f32x2 sq2(f32x2 d) {
+    f32x2 r;
+    asm("fma.rn.f32x2 %0, %1, %1, %2;" : "=l"(r) : "l"(d), "l"(0ull));
+    return r;
+}
+// ((dx*dx + dy*dy) + dz*dz) for two (a, b) pairs at once; bit-identical to
+// two scalar sqd3() calls.
+__device__ __forceinline__ f32x2 sqd3x2(f32x2 ax, f32x2 ay, f32x2 az, f32x2 bx, f32x2 by,
+                                        f32x2 bz) {
+    const f32x2 dx = sub2(ax, bx);
+    const f32x2 dy = sub2(ay, by);
+    const f32x2 dz = sub2(az, bz);
+    return add2(add2(sq2(dx), sq2(dy)), sq2(dz));
+}
+
 // NaN-propagating minimum (torch.minimum semantics): PTX min.NaN.f32.
 __device__ __forceinline__ float fmin_nan(float a, float b) {
     float r;

@@ -117,6 +117,7 @@ class _NearestSquared(torch.autograd.Function):
         ctx.save_for_backward(xc, yc, idx_x, idx_y)
         ctx.bidirectional = bidirectional
         ctx.mark_non_differentiable(idx_x, idx_y)
+        ctx.set_materialize_grads(False)
         return dist_x, dist_y, idx_x, idx_y
 
     @staticmethod

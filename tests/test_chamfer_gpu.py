@@ -220,3 +220,71 @@ def test_first_index_tie_any_dimension(cuda_device, dimension):  # tests/test_ch
     assert torch.equal(x.grad[0, 0].cpu(), want)
     assert torch.equal(y.grad[0, 0].cpu(), -want)
     assert not y.grad[0, 1].any()
+
+
+# ---------------------------------------------------------------- symmetric D == 3 path
+# Clouds of >= 512 points on both sides take the one-pass symmetric kernel
+# (1024 x 1024 work items, 64-bit key atomics); these cases cross item edges.
+
+@pytest.mark.parametrize("shape", [(1, 512, 512), (2, 1500, 2100), (3, 3000, 700),
+                                   (1, 1025, 4097)])
+def test_symmetric_matches_oracle(cuda_device, shape):
+    B, P, Q = shape
+    g = torch.Generator().manual_seed(P * 7 + Q)
+    x, y = torch.randn(B, P, 3, generator=g), torch.randn(B, Q, 3, generator=g)
+    dx, ix, dy, iy = nearest(x.to(cuda_device), y.to(cuda_device))
+    wdx, wix = O.chamfer_nearest(x.numpy(), y.numpy())
+    wdy, wiy = O.chamfer_nearest(y.numpy(), x.numpy())
+    np.testing.assert_array_equal(ix.cpu().numpy(), wix)
+    np.testing.assert_array_equal(iy.cpu().numpy(), wiy)
+    np.testing.assert_array_equal(dx.cpu().numpy(), wdx)
+    np.testing.assert_array_equal(dy.cpu().numpy(), wdy)
+
+
+def test_symmetric_lengths_and_padding(cuda_device):
+    g = torch.Generator().manual_seed(11)
+    x, y = torch.randn(3, 2100, 3, generator=g), torch.randn(3, 1900, 3, generator=g)
+    x[:, 1500:] = float("nan")  # padding may hold anything
+    y[:, 1800:] = float("inf")
+    lx, ly = torch.tensor([1500, 0, 1025]), torch.tensor([1800, 700, 0])
+    dx, ix, dy, iy = nearest(x.to(cuda_device), y.to(cuda_device), lx.to(cuda_device),
+                             ly.to(cuda_device))
+    wdx, wix = O.chamfer_nearest(x.numpy(), y.numpy(), lx.numpy(), ly.numpy())
+    wdy, wiy = O.chamfer_nearest(y.numpy(), x.numpy(), ly.numpy(), lx.numpy())
+    np.testing.assert_array_equal(ix.cpu().numpy(), wix)
+    np.testing.assert_array_equal(iy.cpu().numpy(), wiy)
+    np.testing.assert_array_equal(dx.cpu().numpy(), wdx)
+    np.testing.assert_array_equal(dy.cpu().numpy(), wdy)
+
+
+def test_symmetric_ties_across_items(cuda_device):
+    """Exact ties spread over warps, lanes, blocks and 1024-point items: the
+    lowest index must win in both directions."""
+    x = torch.full((1, 3000, 3), 50.0)
+    y = torch.full((1, 2500, 3), -50.0)
+    for i in (7, 8, 255, 256, 1023, 1024, 2047, 2999):
+        x[0, i] = torch.tensor([1.0, 0.0, 0.0]) if i % 2 else torch.tensor([0.0, 0.0, -1.0])
+    for j in (3, 511, 512, 1023, 1024, 1031, 2499):
+        y[0, j] = torch.tensor([0.0, 1.0, 0.0]) if j % 2 else torch.tensor([-1.0, 0.0, 0.0])
+    x[0, 2000] = torch.tensor([0.0, 0.0, 0.0])
+    y[0, 2400] = torch.tensor([0.0, 0.0, 0.0])
+    dx, ix, dy, iy = nearest(x.to(cuda_device), y.to(cuda_device))
+    wdx, wix = O.chamfer_nearest(x.numpy(), y.numpy())
+    wdy, wiy = O.chamfer_nearest(y.numpy(), x.numpy())
+    np.testing.assert_array_equal(ix.cpu().numpy(), wix)
+    np.testing.assert_array_equal(iy.cpu().numpy(), wiy)
+    np.testing.assert_array_equal(dx.cpu().numpy(), wdx)
+    np.testing.assert_array_equal(dy.cpu().numpy(), wdy)
+
+
+def test_symmetric_overflow_rows(cuda_device):
+    g = torch.Generator().manual_seed(5)
+    x, y = torch.randn(1, 600, 3, generator=g), torch.randn(1, 1100, 3, generator=g)
+    x[0, 17] = torch.tensor([3e19, 0.0, 0.0])   # every SD of this row overflows
+    y[0, 1099] = torch.tensor([-3e19, 0.0, 0.0])
+    dx, ix, dy, iy = nearest(x.to(cuda_device), y.to(cuda_device))
+    wdx, wix = O.chamfer_nearest(x.numpy(), y.numpy())
+    wdy, wiy = O.chamfer_nearest(y.numpy(), x.numpy())
+    np.testing.assert_array_equal(ix.cpu().numpy(), wix)
+    np.testing.assert_array_equal(iy.cpu().numpy(), wiy)
+    assert ix[0, 17].item() == 0 and torch.isinf(dx[0, 17])
