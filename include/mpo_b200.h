@@ -87,6 +87,19 @@ MPO_API int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int6
                     int skip_near_origin, int out_int32, int strategy, void* out,
                     int32_t* status_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free FPS.  No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory (for example a plugin given only
+ * its input and output buffers), so it takes no workspace.  Same contract,
+ * arguments and results as mpo_fps; the CTA-group path keeps its step slots
+ * in a fixed 32 KiB array inside the library (per device), which limits that
+ * path to 1024 clouds per call (larger B is rejected with
+ * MPO_ERR_INVALID_ARGUMENT).  The first call on a device looks the array up
+ * (cudaGetSymbolAddress) and should come before any stream capture.  All
+ * calls share the array: calls whose GPU work overlaps race on it. */
+MPO_API int mpo_fps_noalloc(const float* xyz, int64_t B, int64_t N, int64_t npoint,
+                            int64_t start_idx, int skip_near_origin, int out_int32, int strategy,
+                            void* out, int32_t* status_out, void* stream);
+
 /* ------------------------------------------------------------------ kNN
  * Replaces the `knn` (D == 3, kernels/knn.metal:32-140) and
  * `feature_knn_dense` (D != 3, kernels/feature_knn.metal:51-164) dispatches

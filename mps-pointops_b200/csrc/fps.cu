@@ -26,6 +26,7 @@
 //     (kSpinLimit); on expiry the CTA records status 1 and returns.
 #include <cooperative_groups.h>
 
+#include <mutex>
 #include <string>
 
 #include "../../include/mpo_b200.h"
@@ -314,6 +315,116 @@ int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t star
     const int threads = (int)min64(kMaxThreads, ((ceil_div(per_cta, kMaxP) + 31) / 32) * 32);
     return launch_fps<8, true>(xyz, B, N, npoint, start_idx, skip, o32, out, (int)G, per_cta,
                                threads, reinterpret_cast<GroupSync*>(workspace), status_out, s);
+}
+
+}  // extern "C"
+
+// --------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory at all: a plugin that its host
+// application hands nothing but input and output buffers, or a loop whose
+// rules forbid any allocation once it is running.  mpo_fps_noalloc serves
+// them: the cross-CTA step slots of the CTA-group path live in the
+// file-scope array below instead of a caller workspace.
+//   * Capacity: kNoAllocMaxClouds clouds per call on the group path
+//     (32 bytes each, 32 KiB per device, held by every device that loads
+//     this library until the process exits).  The one-CTA-per-cloud path
+//     needs no scratch and has no such limit.
+//   * In host code the array's name is only a host-side stand-in; the
+//     device address is looked up once per device with cudaGetSymbolAddress
+//     (device current) on the first call that needs it, so that first call
+//     should happen before any stream capture begins.
+//   * Every call shares the array.  It is cleared on the caller's stream at
+//     the start of each call, so calls whose GPU work overlaps (different
+//     streams, or different host threads) race on it and must be serialised
+//     by the caller.
+namespace mpo {
+namespace {
+constexpr int64_t kNoAllocMaxClouds = 1024;
+static __device__ __align__(256) GroupSync g_fps_noalloc_scratch[kNoAllocMaxClouds];
+
+int noalloc_scratch(GroupSync** out) {
+    static std::mutex mu;
+    static GroupSync* addr[64] = {};
+    const int dev = current_device();
+    if (dev < 0 || dev >= 64) return fail(kUnsupported, "mpo_fps_noalloc: device index above 63");
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_fps_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            return fail(kCudaError, std::string("mpo_fps_noalloc: cudaGetSymbolAddress: ") +
+                                        cudaGetErrorString(e));
+        }
+        addr[dev] = reinterpret_cast<GroupSync*>(p);
+    }
+    *out = addr[dev];
+    return kOk;
+}
+}  // namespace
+}  // namespace mpo
+
+extern "C" {
+
+int mpo_fps_noalloc(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
+                    int skip_near_origin, int out_int32, int strategy, void* out,
+                    int32_t* status_out, void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(B >= 0 && N >= 0 && npoint >= 0, "negative size");
+    MPO_REQUIRE(strategy == MPO_FPS_AUTO || strategy == MPO_FPS_SINGLE ||
+                    strategy == MPO_FPS_GROUP,
+                "unknown strategy");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (status_out) {
+        if (cudaMemsetAsync(status_out, 0, sizeof(int32_t), s) != cudaSuccess)
+            return fail(kCudaError, "mpo_fps_noalloc: status reset failed");
+    }
+    if (B == 0 || npoint == 0) return kOk;
+    MPO_REQUIRE(N >= 1, "cannot sample from an empty point cloud");
+    MPO_REQUIRE(start_idx >= 0 && start_idx < N, "start_idx out of range");
+    MPO_REQUIRE(N < (int64_t)0x7fffffff, "N must be below 2**31");
+    MPO_REQUIRE(xyz != nullptr && out != nullptr, "null pointer");
+    const int skip = skip_near_origin ? 1 : 0;
+    const int o32 = out_int32 ? 1 : 0;
+    if (strategy != MPO_FPS_GROUP && N <= kPointsPerCta) {
+        const int P = pick_p(N);
+        const int threads = (int)min64(kMaxThreads, ((ceil_div(N, P) + 31) / 32) * 32);
+        switch (P) {
+            case 1: return launch_fps<1, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
+            case 2: return launch_fps<2, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
+            case 4: return launch_fps<4, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
+            default: return launch_fps<8, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
+        }
+    }
+    if (strategy == MPO_FPS_SINGLE) {
+        return fail(kUnsupported, "mpo_fps_noalloc: the single-CTA strategy holds at most " +
+                                      std::to_string((long long)kPointsPerCta) + " points");
+    }
+    if (B > kNoAllocMaxClouds) {
+        return fail(kInvalidArgument,
+                    "mpo_fps_noalloc: the CTA-group path holds at most " +
+                        std::to_string((long long)kNoAllocMaxClouds) +
+                        " clouds per call in its fixed scratch; got " +
+                        std::to_string((long long)B) + " (use mpo_fps with a workspace)");
+    }
+    const int sms = sm_count();
+    int64_t G = ceil_div(N, kPointsPerCta);
+    if (strategy == MPO_FPS_GROUP) G = min64(max64(G, 2), N);
+    if (G > sms) {
+        return fail(kUnsupported, "mpo_fps_noalloc: clouds above " +
+                                      std::to_string((long long)kPointsPerCta * sms) +
+                                      " points are not supported on this device");
+    }
+    GroupSync* scratch = nullptr;
+    int st = noalloc_scratch(&scratch);
+    if (st) return st;
+    if (cudaMemsetAsync(scratch, 0, (size_t)B * sizeof(GroupSync), s) != cudaSuccess)
+        return fail(kCudaError, "mpo_fps_noalloc: scratch reset failed");
+    const int64_t per_cta = ceil_div(N, G);
+    const int threads = (int)min64(kMaxThreads, ((ceil_div(per_cta, kMaxP) + 31) / 32) * 32);
+    return launch_fps<8, true>(xyz, B, N, npoint, start_idx, skip, o32, out, (int)G, per_cta,
+                               threads, scratch, status_out, s);
 }
 
 }  // extern "C"
