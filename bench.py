@@ -285,7 +285,7 @@ def run_b200(args, world, rank, local):
     sm_max = (clock_info or {}).get("sm_max_mhz") or 1965.0
     peak = 2 * 128 * props.multi_processor_count * sm_max * 1e6 / 1e12
     traffic = None
-    tfile = ROOT / "profiles" / "chamfer_nearest_config2.txt"
+    tfile = ROOT / "profiles" / "chamfer_sym3_config2.md"
     if tfile.exists():
         for line in tfile.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):

@@ -176,16 +176,20 @@ nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
 // entries only at +inf and then loses on index, and padding-vs-padding pairs
 // are NaN, which never wins a min.
 namespace sym {
-constexpr int kWarps = 4;
-constexpr int kR = 8;   // x-rows per lane (even: packed in pairs)
-constexpr int kC = 8;   // columns per row-minimum block
-constexpr int kThreads = kWarps * 32;
-constexpr int kBM = kWarps * 32 * kR;  // 1024 rows per item
-constexpr int kBN = 1024;              // columns per item
-constexpr size_t kSmem = (size_t)kBN * 2 * sizeof(float4) + (size_t)kWarps * kBN * 8;
 constexpr unsigned long long kMaxKey = ~0ull;
 
-__global__ void __launch_bounds__(kThreads, 3)
+// Tile shape: kWarps warps, kR x-rows per lane (even: packed in pairs), kC
+// columns per row-minimum block, kBN y-columns per item, kMinBlocks CTAs
+// per SM for the register budget.
+template <int kWarps, int kR, int kC, int kBN, int kMinBlocks>
+struct Shape {
+    static constexpr int kThreads = kWarps * 32;
+    static constexpr int kBM = kWarps * 32 * kR;
+    static constexpr size_t kSmem = (size_t)kBN * 2 * sizeof(float4) + (size_t)kWarps * kBN * 8;
+};
+
+template <int kWarps, int kR, int kC, int kBN, int kMinBlocks>
+__global__ void __launch_bounds__(kWarps * 32, kMinBlocks)
 chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
                     const int64_t* __restrict__ x_lengths, const int64_t* __restrict__ y_lengths,
                     int64_t B, int64_t P, int64_t Q, unsigned long long* __restrict__ keys_x,
@@ -194,6 +198,9 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
     float4* s_col = smem4;                                                 // [kBN][2]
     unsigned long long* s_part = reinterpret_cast<unsigned long long*>(smem4 + 2 * kBN);
     __shared__ unsigned s_item;
+    constexpr int kThreads = kWarps * 32;
+    constexpr int kBM = kWarps * 32 * kR;
+    static_assert(kR % 2 == 0 && kBN % kC == 0, "bad tile shape");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t row_blocks = ceil_div(P, kBM), col_blocks = ceil_div(Q, kBN);
     const int64_t per_cloud = row_blocks * col_blocks, total = B * per_cloud;
@@ -265,9 +272,15 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
                 }
 #pragma unroll
                 for (int k = 0; k < kR; ++k) m[k] = (c == 0) ? d[k] : fminf(m[k], d[k]);
-                float cm0 = fminf(d[0], d[1]), cm1 = fminf(d[2], d[3]);
-                float cm2 = fminf(d[4], d[5]), cm3 = fminf(d[6], d[7]);
-                const float cm = fminf(fminf(cm0, cm1), fminf(cm2, cm3));
+                float t[kR];
+#pragma unroll
+                for (int k = 0; k < kR; ++k) t[k] = d[k];
+#pragma unroll
+                for (int w2 = kR / 2; w2 >= 1; w2 /= 2) {
+#pragma unroll
+                    for (int k = 0; k < w2; ++k) t[k] = fminf(t[k], t[k + w2]);
+                }
+                const float cm = t[0];
                 const unsigned cb = __float_as_uint(cm);
                 const unsigned wmin = __reduce_min_sync(FULL_MASK, cb);
                 const unsigned mask = __ballot_sync(FULL_MASK, cb == wmin);
@@ -368,6 +381,10 @@ __global__ void finalize_kernel(const unsigned long long* __restrict__ keys,
 }
 
 inline bool use_sym(int64_t P, int64_t Q, int64_t D) { return D == 3 && P >= 512 && Q >= 512; }
+
+// The tile shape used by mpo_chamfer_nearest.
+#define MPO_SYM_DEFAULT 4, 8, 8, 1024, 3
+using Default = Shape<MPO_SYM_DEFAULT>;
 
 inline size_t scratch_bytes(int64_t B, int64_t P, int64_t Q) {
     return ((size_t)B * (P + Q)) * sizeof(unsigned long long) + 256;
@@ -547,16 +564,17 @@ int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths
     if (cudaMemsetAsync(keys_x, 0xff, (size_t)B * (P + Q) * 8, s) != cudaSuccess ||
         cudaMemsetAsync(counter, 0, sizeof(unsigned), s) != cudaSuccess)
         return fail(kCudaError, "mpo_chamfer_nearest: scratch reset failed");
-    if (cudaFuncSetAttribute(sym::chamfer_sym3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sym::kSmem) != cudaSuccess)
+    auto kern = sym::chamfer_sym3_kernel<MPO_SYM_DEFAULT>;
+    using Sh = sym::Default;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)Sh::kSmem) != cudaSuccess)
         return fail(kCudaError, "mpo_chamfer_nearest: shared-memory limit");
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sym::chamfer_sym3_kernel,
-                                                  sym::kThreads, sym::kSmem);
-    const int64_t items = B * ceil_div(P, sym::kBM) * ceil_div(Q, sym::kBN);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Sh::kThreads, Sh::kSmem);
+    const int64_t items = B * ceil_div(P, Sh::kBM) * ceil_div(Q, 1024);
     const int64_t grid = min64(items, (int64_t)sm_count() * max64(per_sm, 1));
-    sym::chamfer_sym3_kernel<<<(unsigned)grid, sym::kThreads, sym::kSmem, s>>>(
-        x, y, x_lengths, y_lengths, B, P, Q, keys_x, keys_y, counter);
+    kern<<<(unsigned)grid, Sh::kThreads, Sh::kSmem, s>>>(x, y, x_lengths, y_lengths, B, P, Q,
+                                                         keys_x, keys_y, counter);
     int st = check_launch("chamfer_sym3_kernel");
     if (st) return st;
     sym::finalize_kernel<<<(unsigned)ceil_div(B * P, 256), 256, 0, s>>>(
