@@ -91,11 +91,12 @@ MPO_API int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int6
  * callers that cannot allocate device memory (for example a plugin given only
  * its input and output buffers), so it takes no workspace.  Same contract,
  * arguments and results as mpo_fps; the CTA-group path keeps its step slots
- * in a fixed 32 KiB array inside the library (per device), which limits that
- * path to 1024 clouds per call (larger B is rejected with
- * MPO_ERR_INVALID_ARGUMENT).  The first call on a device looks the array up
- * (cudaGetSymbolAddress) and should come before any stream capture.  All
- * calls share the array: calls whose GPU work overlaps race on it. */
+ * in a fixed 8 KiB array inside the library (per device) -- enough for any
+ * batch on a 148-SM B200, since cooperative waves reuse the slots; a launch
+ * that would need more is rejected with MPO_ERR_INVALID_ARGUMENT.  The first
+ * call on a device looks the array up (cudaGetSymbolAddress) and should come
+ * before any stream capture.  All calls share the array: calls whose GPU
+ * work overlaps race on it. */
 MPO_API int mpo_fps_noalloc(const float* xyz, int64_t B, int64_t N, int64_t npoint,
                             int64_t start_idx, int skip_near_origin, int out_int32, int strategy,
                             void* out, int32_t* status_out, void* stream);

@@ -11,7 +11,8 @@
 // zeros without a hit) and writes int32.
 //
 // Design (B200): one warp per query scans the reference cloud in input order,
-// 32 points per step.  Each lane evaluates one point; __ballot_sync gives
+// 128 points per step (four independent 32-point chunks, so the loads of a
+// step overlap).  Each lane evaluates one point; __ballot_sync gives
 // the hit mask and __popc(mask & lanes_below) the rank of each hit, so the
 // hits land in their output slots in order with no serial scan.  The warp
 // stops as soon as K hits are found (on uniform clouds that is a small
@@ -48,24 +49,36 @@ ball_query_kernel(const float* __restrict__ query, const float* __restrict__ ref
         const float* qp = query + ((size_t)b * (size_t)M + (size_t)q) * 3;
         const float qx = qp[0], qy = qp[1], qz = qp[2];
         const float* __restrict__ r = ref + (size_t)b * (size_t)N * 3;
-        for (int64_t j0 = 0; j0 < nl && found < K; j0 += 32) {
-            const int64_t j = j0 + lane;
-            float d = INFINITY;
-            if (j < nl) d = sqd3(qx, qy, qz, r[3 * j], r[3 * j + 1], r[3 * j + 2]);
-            const bool hit = j < nl && d < r2;
-            const unsigned mask = __ballot_sync(FULL_MASK, hit);
-            if (mask == 0u) continue;
-            if (first < 0) first = j0 + (__ffs(mask) - 1);
-            const int64_t slot = found + __popc(mask & below);
-            if (hit && slot < K) {
-                if (POINTNET2) {
-                    idx32[row + slot] = (int32_t)j;
-                } else {
-                    idx64[row + slot] = j;
-                    dist2[row + slot] = d;
-                }
+        // Four 32-point chunks per iteration: their loads are independent,
+        // so a lane has 12 loads in flight; hits are still ranked in input
+        // order chunk by chunk.
+        constexpr int kU = 4;
+        for (int64_t j0 = 0; j0 < nl && found < K; j0 += 32 * kU) {
+            float d[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int64_t j = j0 + u * 32 + lane;
+                d[u] = INFINITY;
+                if (j < nl) d[u] = sqd3(qx, qy, qz, r[3 * j], r[3 * j + 1], r[3 * j + 2]);
             }
-            found += __popc(mask);
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int64_t j = j0 + u * 32 + lane;
+                const bool hit = j < nl && d[u] < r2;
+                const unsigned mask = __ballot_sync(FULL_MASK, hit);
+                if (mask == 0u) continue;
+                if (first < 0) first = j0 + u * 32 + (__ffs(mask) - 1);
+                const int64_t slot = found + __popc(mask & below);
+                if (hit && slot < K) {
+                    if (POINTNET2) {
+                        idx32[row + slot] = (int32_t)j;
+                    } else {
+                        idx64[row + slot] = j;
+                        dist2[row + slot] = d[u];
+                    }
+                }
+                found += __popc(mask);
+            }
         }
     }
     // Padding.

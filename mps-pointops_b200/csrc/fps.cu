@@ -8,22 +8,26 @@
 //   (reference.py:46-50).
 //
 // Design (B200): the whole npoint-step loop runs inside ONE launch.
-//   * A cloud is owned by a group of G CTAs of up to 1024 threads; each
-//     thread keeps P <= 8 points (x, y, z, min_d2) in registers for the whole
-//     run, so a step touches no memory except the argmax exchange.
-//   * Argmax per step: each thread scans its points, then a warp reduces
-//     (ordered key, index) pairs with two redux.sync instructions (max key,
-//     then min index among the lanes holding it), and every warp redundantly
-//     reduces the per-warp results from shared memory -- one __syncthreads()
-//     per step.
+//   * A cloud is owned by a group of G CTAs of up to 256 threads; each thread
+//     keeps P <= 32 points (x, y, z, min_d2) in registers for the whole run,
+//     so a step touches no memory except the argmax exchange.  Few warps with
+//     many points each keep the per-step reduction overhead small.
+//   * Argmax per step: each thread scans its points (float compare on the
+//     finite fast path), then a warp reduces (ordered key, index) pairs with
+//     two redux.sync instructions (max key, then min index among the lanes
+//     holding it), and every warp redundantly reduces the per-warp results
+//     from shared memory -- one __syncthreads() per step.
 //   * G == 1 (clouds up to 8192 points): the cloud's xyz is also staged in
 //     shared memory so the next centroid is a shared-memory load.
 //   * G > 1 (large clouds: 2^20 points on 128 SMs): a
-//     cooperative launch makes the group co-resident; each CTA publishes its
-//     best as a 64-bit key (ordered distance << 32 | ~index) with one
-//     atomicMax into a rotating slot and arrives on a counter; thread 0 then
-//     spins with ld.acquire on the counter.  The spin is bounded
-//     (kSpinLimit); on expiry the CTA records status 1 and returns.
+//     cooperative launch makes the group co-resident.  Each CTA publishes its
+//     best as one 64-bit word (ordered distance key << 32 | step sequence
+//     << 21 | index) into its slot of a double-buffered slot array (buffer =
+//     step parity), and one warp of every CTA polls the G slots with
+//     ld.relaxed.gpu until all carry the current step's sequence, then
+//     reduces them itself -- no atomics and one cross-SM round trip per step.
+//     The poll is bounded in time (kSpinLimitNs of %globaltimer); on expiry
+//     the CTA records status 1, raises the group's error word and returns.
 #include <cooperative_groups.h>
 
 #include <mutex>
@@ -35,31 +39,35 @@
 namespace mpo {
 namespace {
 
-constexpr int kMaxThreads = 1024;
-constexpr int kMaxP = 8;
+constexpr int kMaxThreads = 256;
+constexpr int kMaxP = 32;
 constexpr int64_t kPointsPerCta = (int64_t)kMaxThreads * kMaxP;  // 8192
-constexpr unsigned kSpinLimit = 1u << 26;
+constexpr unsigned long long kSpinLimitNs = 2000000000ull;  // 2 s per step
+constexpr int kIndexBits = 21;  // group path: N <= 8192 * 148 < 2^21
+constexpr unsigned long long kIndexMask = (1ull << kIndexBits) - 1;
 
-// Cross-CTA exchange state of one cloud (lives in the caller's workspace,
-// zeroed before each launch).
-struct GroupSync {
-    unsigned long long slot[3];
-    unsigned count;
-    unsigned error;
-};
+// Cross-CTA exchange state of the clouds of one cooperative wave, in the
+// caller's workspace (zeroed before each wave):
+//   slots[cloud_in_wave][parity][G]  u64
+//   error[cloud_in_wave]             u32
+inline size_t group_bytes(int64_t clouds, int64_t G) {
+    return (size_t)clouds * 2 * (size_t)G * 8 + (size_t)clouds * 8;
+}
 
 template <int P, bool GROUP>
 __global__ void __launch_bounds__(kMaxThreads, 1)
 fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t start_idx,
            int skip, int out_int32, void* __restrict__ out, int G, int64_t per_cta,
-           int cloud_offset, GroupSync* __restrict__ sync, int32_t* __restrict__ status) {
+           int cloud_offset, unsigned long long* __restrict__ slots,
+           unsigned* __restrict__ errors, int32_t* __restrict__ status) {
     extern __shared__ float s_xyz[];  // G == 1 only: the cloud, 3 floats per point
     __shared__ uint32_t s_key[2][32];
     __shared__ uint32_t s_idx[2][32];
     __shared__ uint32_t s_far;
     __shared__ int s_abort;
 
-    const int b = cloud_offset + blockIdx.x / G;
+    const int wave_cloud = blockIdx.x / G;
+    const int b = cloud_offset + wave_cloud;
     const int g = blockIdx.x % G;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -68,8 +76,9 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
     const int nthr = blockDim.x;
     const float* __restrict__ p = xyz + (size_t)b * (size_t)N * 3;
     const int64_t lo = (int64_t)g * per_cta;
-    const int64_t hi = min(N, lo + per_cta);
-    GroupSync* gs = GROUP ? sync + b : nullptr;
+    const int64_t hi = min64(N, lo + per_cta);
+    unsigned long long* my_slots = GROUP ? slots + (size_t)wave_cloud * 2 * G : nullptr;
+    unsigned* my_error = GROUP ? errors + wave_cloud : nullptr;
 
     float px[P], py[P], pz[P], md[P];
 #pragma unroll
@@ -124,19 +133,25 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
         nan_mode = nan_mode || !(isfinite(cx) && isfinite(cy) && isfinite(cz));
         uint32_t bkey = 0u, bidx = 0xffffffffu;
         if (!nan_mode) {
+            // Finite fast path: min_d2 is -inf (skipped or unused slot, kept
+            // there by min) or in [0, +inf]; a float compare finds the
+            // thread's first maximum and the ordered key is formed once.
+            float bv = -INFINITY;
+            uint32_t bj = 0xffffffffu;
 #pragma unroll
             for (int s = 0; s < P; ++s) {
-                const int64_t j = lo + tid + (int64_t)s * nthr;
-                const bool valid = j < hi;
                 const float d = sqd3(px[s], py[s], pz[s], cx, cy, cz);
-                const float m = fminf(md[s], d);
-                md[s] = valid ? m : md[s];
-                const uint32_t k = valid ? ordered_key(m) : 0u;
-                if (k > bkey) {
-                    bkey = k;
-                    bidx = (uint32_t)j;
+                md[s] = fminf(md[s], d);
+                if (md[s] > bv) {
+                    bv = md[s];
+                    bj = (uint32_t)(lo + tid + (int64_t)s * nthr);
                 }
             }
+            // A lane whose points are all -inf offers its first valid point
+            // (the lowest index among equal keys).
+            if (bj == 0xffffffffu && lo + tid < hi) bj = (uint32_t)(lo + tid);
+            bidx = bj;
+            bkey = bj == 0xffffffffu ? 0u : ordered_key(bv);
         } else {
 #pragma unroll
             for (int s = 0; s < P; ++s) {
@@ -171,28 +186,57 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
             cy = s_xyz[3 * far + 1];
             cz = s_xyz[3 * far + 2];
         } else {
-            if (tid == 0) {
-                const int slot = (int)(i % 3);
-                const unsigned long long packed =
-                    ((unsigned long long)cmax << 32) | (unsigned long long)(0xffffffffu - cidx);
-                atomicMax(&gs->slot[slot], packed);
-                __threadfence();
-                atomicAdd(&gs->count, 1u);
-                const unsigned target = (unsigned)(i + 1) * (unsigned)G;
-                unsigned spins = 0;
-                while (ld_acquire_u32(&gs->count) < target) {
-                    if (++spins > kSpinLimit || ld_acquire_u32(&gs->error) != 0u) {
-                        atomicExch(&gs->error, 1u);
-                        if (status) atomicExch(status, 1);
-                        s_abort = 1;
+            // Publish this CTA's best into slots[parity][g], then warp 0 waits
+            // for all G slots of this step and reduces them.  A CTA can be at
+            // most one step ahead of the slowest reader, so two buffers suffice.
+            unsigned long long* cur = my_slots + (size_t)buf * G;
+            const unsigned long long seq = (unsigned long long)((i + 1) & 0x7ff);
+            if (warp == 0) {
+                if (lane == 0) {
+                    const unsigned long long word = ((unsigned long long)cmax << 32) |
+                                                    (seq << kIndexBits) |
+                                                    ((unsigned long long)cidx & kIndexMask);
+                    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(cur + g), "l"(word)
+                                 : "memory");
+                }
+                uint32_t bk = 0u, bi = 0xffffffffu;
+                const unsigned long long t0 = globaltimer_ns();
+                bool abort = false;
+                for (;;) {
+                    bool ok = true;
+                    bk = 0u;
+                    bi = 0xffffffffu;
+                    for (int c = lane; c < G; c += 32) {
+                        const unsigned long long v = ld_relaxed_u64(cur + c);
+                        if (((v >> kIndexBits) & 0x7ffull) != seq) {
+                            ok = false;
+                        } else {
+                            const uint32_t kk = (uint32_t)(v >> 32);
+                            const uint32_t ii = (uint32_t)(v & kIndexMask);
+                            if (kk > bk || (kk == bk && ii < bi)) {
+                                bk = kk;
+                                bi = ii;
+                            }
+                        }
+                    }
+                    if (__all_sync(FULL_MASK, ok)) break;
+                    if (globaltimer_ns() - t0 > kSpinLimitNs || ld_acquire_u32(my_error) != 0u) {
+                        abort = true;
                         break;
                     }
                 }
-                const unsigned long long win = ld_relaxed_u64(&gs->slot[slot]);
-                s_far = 0xffffffffu - (uint32_t)(win & 0xffffffffull);
-                // Step i+2 reuses slot (i+2)%3 == (i-1)%3, which every CTA has
-                // finished reading once it arrived for step i.
-                if (g == 0) gs->slot[(i + 2) % 3] = 0ull;
+                abort = __any_sync(FULL_MASK, abort);
+                if (abort) {
+                    if (lane == 0) {
+                        atomicExch(my_error, 1u);
+                        if (status) atomicExch(status, 1);
+                        s_abort = 1;
+                    }
+                } else {
+                    const uint32_t gk = __reduce_max_sync(FULL_MASK, bk);
+                    const uint32_t gi = __reduce_min_sync(FULL_MASK, bk == gk ? bi : 0xffffffffu);
+                    if (lane == 0) s_far = gi;
+                }
             }
             __syncthreads();
             if (s_abort) return;
@@ -204,36 +248,94 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
     }
 }
 
-template <int P, bool GROUP>
-int launch_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
-               int skip, int out_int32, void* out, int G, int64_t per_cta, int threads,
-               GroupSync* sync, int32_t* status, cudaStream_t stream) {
-    auto kern = fps_kernel<P, GROUP>;
-    const size_t smem = GROUP ? 0 : (size_t)N * 3 * sizeof(float);
+// Points per thread for a CTA that owns `per_cta` points with <= 256 threads.
+int pick_p(int64_t per_cta) {
+    if (per_cta <= 256) return 1;
+    if (per_cta <= 512) return 2;
+    if (per_cta <= 1024) return 4;
+    if (per_cta <= 2048) return 8;
+    if (per_cta <= 4096) return 16;
+    return 32;
+}
+
+int threads_for(int64_t per_cta, int P) {
+    return (int)min64(kMaxThreads, ((ceil_div(per_cta, P) + 31) / 32) * 32);
+}
+
+template <int P>
+int launch_single(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
+                  int skip, int out_int32, void* out, int32_t* status, cudaStream_t stream) {
+    auto kern = fps_kernel<P, false>;
+    const size_t smem = (size_t)N * 3 * sizeof(float);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess) {
+        cudaSuccess)
         return fail(kCudaError, "mpo_fps: cannot set the shared-memory limit");
+    kern<<<(unsigned)B, threads_for(N, P), smem, stream>>>(xyz, N, npoint, start_idx, skip,
+                                                           out_int32, out, 1, N, 0, nullptr,
+                                                           nullptr, status);
+    return check_launch("mpo_fps");
+}
+
+int launch_single_any(const float* xyz, int64_t B, int64_t N, int64_t npoint,
+                      int64_t start_idx, int skip, int o32, void* out, int32_t* status,
+                      cudaStream_t s) {
+    switch (pick_p(N)) {
+        case 1: return launch_single<1>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
+        case 2: return launch_single<2>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
+        case 4: return launch_single<4>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
+        case 8: return launch_single<8>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
+        case 16: return launch_single<16>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
+        default: return launch_single<32>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
     }
-    if (!GROUP) {
-        kern<<<(unsigned)B, threads, smem, stream>>>(xyz, N, npoint, start_idx, skip, out_int32,
-                                                     out, 1, per_cta, 0, sync, status);
-        return check_launch("mpo_fps");
-    }
-    // Co-residency of each group is guaranteed by cooperative launch; clouds
-    // are processed in waves that fit on the device at one CTA per SM.
+}
+
+// Group plan for one call: CTAs per cloud and clouds per cooperative wave.
+struct GroupPlan {
+    int64_t G = 0, per_cta = 0, clouds_per_wave = 0;
+};
+
+int plan_group(int64_t B, int64_t N, int strategy, GroupPlan* plan, const char* who) {
     const int sms = sm_count();
-    const int clouds_per_wave = sms / G;
-    if (clouds_per_wave < 1) return fail(kUnsupported, "mpo_fps: cloud too large for one wave");
-    for (int64_t c0 = 0; c0 < B; c0 += clouds_per_wave) {
-        const int nc = (int)min64(clouds_per_wave, B - c0);
+    int64_t G = ceil_div(N, kPointsPerCta);
+    // A forced group on a small cloud still uses at least two CTAs (when the
+    // cloud has two points) so the cross-CTA exchange is exercised.
+    if (strategy == MPO_FPS_GROUP) G = min64(max64(G, 2), N);
+    if (G > sms) {
+        return fail(kUnsupported, std::string(who) + ": clouds above " +
+                                      std::to_string((long long)kPointsPerCta * sms) +
+                                      " points are not supported on this device");
+    }
+    plan->G = G;
+    plan->per_cta = ceil_div(N, G);
+    plan->clouds_per_wave = min64(B, sms / G);
+    return kOk;
+}
+
+// Runs the group path in cooperative waves; `scratch` holds group_bytes()
+// for one wave and is zeroed on the stream before each wave.
+int launch_group(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
+                 int skip, int out_int32, void* out, const GroupPlan& plan, void* scratch,
+                 int32_t* status, cudaStream_t stream, const char* who) {
+    auto kern = fps_kernel<kMaxP, true>;
+    int G = (int)plan.G;
+    int64_t per_cta = plan.per_cta;
+    const int threads = threads_for(per_cta, kMaxP);
+    unsigned long long* slots = reinterpret_cast<unsigned long long*>(scratch);
+    unsigned* errors = reinterpret_cast<unsigned*>(slots + (size_t)plan.clouds_per_wave * 2 * G);
+    const size_t bytes = group_bytes(plan.clouds_per_wave, G);
+    for (int64_t c0 = 0; c0 < B; c0 += plan.clouds_per_wave) {
+        const int nc = (int)min64(plan.clouds_per_wave, B - c0);
+        if (cudaMemsetAsync(scratch, 0, bytes, stream) != cudaSuccess)
+            return fail(kCudaError, std::string(who) + ": scratch reset failed");
         int cloud_offset = (int)c0;
-        void* args[] = {(void*)&xyz,  (void*)&N,      (void*)&npoint, (void*)&start_idx,
-                        (void*)&skip, (void*)&out_int32, (void*)&out,  (void*)&G,
-                        (void*)&per_cta, (void*)&cloud_offset, (void*)&sync, (void*)&status};
+        void* args[] = {(void*)&xyz,      (void*)&N,         (void*)&npoint, (void*)&start_idx,
+                        (void*)&skip,     (void*)&out_int32, (void*)&out,    (void*)&G,
+                        (void*)&per_cta,  (void*)&cloud_offset, (void*)&slots, (void*)&errors,
+                        (void*)&status};
         cudaError_t e = cudaLaunchCooperativeKernel((const void*)kern, dim3(nc * G),
                                                     dim3(threads), args, 0, stream);
         if (e != cudaSuccess) {
-            return fail(kCudaError, std::string("mpo_fps: cooperative launch: ") +
+            return fail(kCudaError, std::string(who) + ": cooperative launch: " +
                                         cudaGetErrorString(e));
         }
         count_launches(1);
@@ -241,11 +343,32 @@ int launch_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t s
     return kOk;
 }
 
-int pick_p(int64_t per_cta) {
-    if (per_cta <= 1024) return 1;
-    if (per_cta <= 2048) return 2;
-    if (per_cta <= 4096) return 4;
-    return 8;
+int check_fps_args(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
+                   int strategy, void* out, int32_t* status_out, cudaStream_t s,
+                   const char* who, bool* nothing_to_do) {
+    const std::string w(who);
+    *nothing_to_do = false;
+    if (!(B >= 0 && N >= 0 && npoint >= 0)) return fail(kInvalidArgument, w + ": negative size");
+    if (!(strategy == MPO_FPS_AUTO || strategy == MPO_FPS_SINGLE || strategy == MPO_FPS_GROUP))
+        return fail(kInvalidArgument, w + ": unknown strategy");
+    if (status_out) {
+        if (cudaMemsetAsync(status_out, 0, sizeof(int32_t), s) != cudaSuccess)
+            return fail(kCudaError, w + ": status reset failed");
+    }
+    if (B == 0 || npoint == 0) {
+        *nothing_to_do = true;
+        return kOk;
+    }
+    if (N < 1) return fail(kInvalidArgument, w + ": cannot sample from an empty point cloud");
+    if (!(start_idx >= 0 && start_idx < N))
+        return fail(kInvalidArgument, w + ": start_idx out of range");
+    if (N >= (int64_t)0x7fffffff) return fail(kInvalidArgument, w + ": N must be below 2**31");
+    if (xyz == nullptr || out == nullptr) return fail(kInvalidArgument, w + ": null pointer");
+    if (strategy == MPO_FPS_SINGLE && N > kPointsPerCta) {
+        return fail(kUnsupported, w + ": the single-CTA strategy holds at most " +
+                                      std::to_string((long long)kPointsPerCta) + " points");
+    }
+    return kOk;
 }
 
 }  // namespace
@@ -255,66 +378,35 @@ extern "C" {
 
 size_t mpo_fps_workspace_bytes(int64_t B, int64_t N, int64_t npoint, int strategy) {
     (void)npoint;
-    if (strategy != MPO_FPS_GROUP && N <= mpo::kPointsPerCta) return 0;
-    return (size_t)(B > 0 ? B : 1) * sizeof(mpo::GroupSync);
+    if (B <= 0 || N <= 0 || (strategy != MPO_FPS_GROUP && N <= mpo::kPointsPerCta)) return 0;
+    mpo::GroupPlan plan;
+    if (mpo::plan_group(B, N, strategy, &plan, "mpo_fps_workspace_bytes") != mpo::kOk) return 0;
+    return mpo::group_bytes(plan.clouds_per_wave, plan.G);
 }
 
 int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
             int skip_near_origin, int out_int32, int strategy, void* out, int32_t* status_out,
             void* workspace, size_t workspace_bytes, void* stream) {
     using namespace mpo;
-    MPO_REQUIRE(B >= 0 && N >= 0 && npoint >= 0, "negative size");
-    MPO_REQUIRE(strategy == MPO_FPS_AUTO || strategy == MPO_FPS_SINGLE ||
-                    strategy == MPO_FPS_GROUP,
-                "unknown strategy");
     cudaStream_t s = (cudaStream_t)stream;
-    if (status_out) {
-        if (cudaMemsetAsync(status_out, 0, sizeof(int32_t), s) != cudaSuccess)
-            return fail(kCudaError, "mpo_fps: status reset failed");
-    }
-    if (B == 0 || npoint == 0) return kOk;
-    MPO_REQUIRE(N >= 1, "cannot sample from an empty point cloud");
-    MPO_REQUIRE(start_idx >= 0 && start_idx < N, "start_idx out of range");
-    MPO_REQUIRE(N < (int64_t)0x7fffffff, "N must be below 2**31");
-    MPO_REQUIRE(xyz != nullptr && out != nullptr, "null pointer");
+    bool done = false;
+    int st = check_fps_args(xyz, B, N, npoint, start_idx, strategy, out, status_out, s, "mpo_fps",
+                            &done);
+    if (st || done) return st;
     const int skip = skip_near_origin ? 1 : 0;
     const int o32 = out_int32 ? 1 : 0;
-
-    if (strategy != MPO_FPS_GROUP && N <= kPointsPerCta) {
-        const int P = pick_p(N);
-        const int threads = (int)min64(kMaxThreads, ((ceil_div(N, P) + 31) / 32) * 32);
-        switch (P) {
-            case 1: return launch_fps<1, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
-            case 2: return launch_fps<2, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
-            case 4: return launch_fps<4, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
-            default: return launch_fps<8, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
-        }
-    }
-    if (strategy == MPO_FPS_SINGLE) {
-        return fail(kUnsupported, "mpo_fps: the single-CTA strategy holds at most " +
-                                      std::to_string((long long)kPointsPerCta) + " points");
-    }
-    const int sms = sm_count();
-    // Forced group on a small cloud still uses at least two CTAs (when the
-    // cloud has two points) so the cross-CTA exchange is exercised.
-    int64_t G = ceil_div(N, kPointsPerCta);
-    if (strategy == MPO_FPS_GROUP) G = min64(max64(G, 2), N);
-    if (G > sms) {
-        return fail(kUnsupported, "mpo_fps: clouds above " +
-                                      std::to_string((long long)kPointsPerCta * sms) +
-                                      " points are not supported on this device");
-    }
-    const size_t need = mpo_fps_workspace_bytes(B, N, npoint, strategy);
+    if (strategy != MPO_FPS_GROUP && N <= kPointsPerCta)
+        return launch_single_any(xyz, B, N, npoint, start_idx, skip, o32, out, status_out, s);
+    GroupPlan plan;
+    st = plan_group(B, N, strategy, &plan, "mpo_fps");
+    if (st) return st;
+    const size_t need = group_bytes(plan.clouds_per_wave, plan.G);
     if (workspace == nullptr || workspace_bytes < need) {
         return fail(kWorkspaceTooSmall, "mpo_fps: workspace must hold " + std::to_string(need) +
                                             " bytes");
     }
-    if (cudaMemsetAsync(workspace, 0, need, s) != cudaSuccess)
-        return fail(kCudaError, "mpo_fps: workspace reset failed");
-    const int64_t per_cta = ceil_div(N, G);
-    const int threads = (int)min64(kMaxThreads, ((ceil_div(per_cta, kMaxP) + 31) / 32) * 32);
-    return launch_fps<8, true>(xyz, B, N, npoint, start_idx, skip, o32, out, (int)G, per_cta,
-                               threads, reinterpret_cast<GroupSync*>(workspace), status_out, s);
+    return launch_group(xyz, B, N, npoint, start_idx, skip, o32, out, plan, workspace,
+                        status_out, s, "mpo_fps");
 }
 
 }  // extern "C"
@@ -327,26 +419,28 @@ int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t star
 // rules forbid any allocation once it is running.  mpo_fps_noalloc serves
 // them: the cross-CTA step slots of the CTA-group path live in the
 // file-scope array below instead of a caller workspace.
-//   * Capacity: kNoAllocMaxClouds clouds per call on the group path
-//     (32 bytes each, 32 KiB per device, held by every device that loads
-//     this library until the process exits).  The one-CTA-per-cloud path
-//     needs no scratch and has no such limit.
+//   * Capacity: kNoAllocScratchBytes (8 KiB per device, held by every device
+//     that loads this library until the process exits).  The group path
+//     needs 16 bytes per CTA of one cooperative wave plus 8 per cloud (under
+//     4 KiB on a 148-SM B200) whatever the batch size, because waves reuse
+//     the slots; a configuration needing more is rejected.  The
+//     one-CTA-per-cloud path needs no scratch.
 //   * In host code the array's name is only a host-side stand-in; the
 //     device address is looked up once per device with cudaGetSymbolAddress
 //     (device current) on the first call that needs it, so that first call
 //     should happen before any stream capture begins.
-//   * Every call shares the array.  It is cleared on the caller's stream at
-//     the start of each call, so calls whose GPU work overlaps (different
-//     streams, or different host threads) race on it and must be serialised
-//     by the caller.
+//   * Every call shares the array.  It is cleared on the caller's stream
+//     before each wave, so calls whose GPU work overlaps (different streams,
+//     or different host threads) race on it and must be serialised by the
+//     caller.
 namespace mpo {
 namespace {
-constexpr int64_t kNoAllocMaxClouds = 1024;
-static __device__ __align__(256) GroupSync g_fps_noalloc_scratch[kNoAllocMaxClouds];
+constexpr size_t kNoAllocScratchBytes = 8192;
+static __device__ __align__(256) unsigned char g_fps_noalloc_scratch[kNoAllocScratchBytes];
 
-int noalloc_scratch(GroupSync** out) {
+int noalloc_scratch(void** out) {
     static std::mutex mu;
-    static GroupSync* addr[64] = {};
+    static void* addr[64] = {};
     const int dev = current_device();
     if (dev < 0 || dev >= 64) return fail(kUnsupported, "mpo_fps_noalloc: device index above 63");
     std::lock_guard<std::mutex> lock(mu);
@@ -357,7 +451,7 @@ int noalloc_scratch(GroupSync** out) {
             return fail(kCudaError, std::string("mpo_fps_noalloc: cudaGetSymbolAddress: ") +
                                         cudaGetErrorString(e));
         }
-        addr[dev] = reinterpret_cast<GroupSync*>(p);
+        addr[dev] = p;
     }
     *out = addr[dev];
     return kOk;
@@ -371,60 +465,31 @@ int mpo_fps_noalloc(const float* xyz, int64_t B, int64_t N, int64_t npoint, int6
                     int skip_near_origin, int out_int32, int strategy, void* out,
                     int32_t* status_out, void* stream) {
     using namespace mpo;
-    MPO_REQUIRE(B >= 0 && N >= 0 && npoint >= 0, "negative size");
-    MPO_REQUIRE(strategy == MPO_FPS_AUTO || strategy == MPO_FPS_SINGLE ||
-                    strategy == MPO_FPS_GROUP,
-                "unknown strategy");
     cudaStream_t s = (cudaStream_t)stream;
-    if (status_out) {
-        if (cudaMemsetAsync(status_out, 0, sizeof(int32_t), s) != cudaSuccess)
-            return fail(kCudaError, "mpo_fps_noalloc: status reset failed");
-    }
-    if (B == 0 || npoint == 0) return kOk;
-    MPO_REQUIRE(N >= 1, "cannot sample from an empty point cloud");
-    MPO_REQUIRE(start_idx >= 0 && start_idx < N, "start_idx out of range");
-    MPO_REQUIRE(N < (int64_t)0x7fffffff, "N must be below 2**31");
-    MPO_REQUIRE(xyz != nullptr && out != nullptr, "null pointer");
+    bool done = false;
+    int st = check_fps_args(xyz, B, N, npoint, start_idx, strategy, out, status_out, s,
+                            "mpo_fps_noalloc", &done);
+    if (st || done) return st;
     const int skip = skip_near_origin ? 1 : 0;
     const int o32 = out_int32 ? 1 : 0;
-    if (strategy != MPO_FPS_GROUP && N <= kPointsPerCta) {
-        const int P = pick_p(N);
-        const int threads = (int)min64(kMaxThreads, ((ceil_div(N, P) + 31) / 32) * 32);
-        switch (P) {
-            case 1: return launch_fps<1, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
-            case 2: return launch_fps<2, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
-            case 4: return launch_fps<4, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
-            default: return launch_fps<8, false>(xyz, B, N, npoint, start_idx, skip, o32, out, 1, N, threads, nullptr, status_out, s);
-        }
-    }
-    if (strategy == MPO_FPS_SINGLE) {
-        return fail(kUnsupported, "mpo_fps_noalloc: the single-CTA strategy holds at most " +
-                                      std::to_string((long long)kPointsPerCta) + " points");
-    }
-    if (B > kNoAllocMaxClouds) {
-        return fail(kInvalidArgument,
-                    "mpo_fps_noalloc: the CTA-group path holds at most " +
-                        std::to_string((long long)kNoAllocMaxClouds) +
-                        " clouds per call in its fixed scratch; got " +
-                        std::to_string((long long)B) + " (use mpo_fps with a workspace)");
-    }
-    const int sms = sm_count();
-    int64_t G = ceil_div(N, kPointsPerCta);
-    if (strategy == MPO_FPS_GROUP) G = min64(max64(G, 2), N);
-    if (G > sms) {
-        return fail(kUnsupported, "mpo_fps_noalloc: clouds above " +
-                                      std::to_string((long long)kPointsPerCta * sms) +
-                                      " points are not supported on this device");
-    }
-    GroupSync* scratch = nullptr;
-    int st = noalloc_scratch(&scratch);
+    if (strategy != MPO_FPS_GROUP && N <= kPointsPerCta)
+        return launch_single_any(xyz, B, N, npoint, start_idx, skip, o32, out, status_out, s);
+    GroupPlan plan;
+    st = plan_group(B, N, strategy, &plan, "mpo_fps_noalloc");
     if (st) return st;
-    if (cudaMemsetAsync(scratch, 0, (size_t)B * sizeof(GroupSync), s) != cudaSuccess)
-        return fail(kCudaError, "mpo_fps_noalloc: scratch reset failed");
-    const int64_t per_cta = ceil_div(N, G);
-    const int threads = (int)min64(kMaxThreads, ((ceil_div(per_cta, kMaxP) + 31) / 32) * 32);
-    return launch_fps<8, true>(xyz, B, N, npoint, start_idx, skip, o32, out, (int)G, per_cta,
-                               threads, scratch, status_out, s);
+    const size_t need = group_bytes(plan.clouds_per_wave, plan.G);
+    if (need > kNoAllocScratchBytes) {
+        return fail(kInvalidArgument,
+                    "mpo_fps_noalloc: this launch needs " + std::to_string(need) +
+                        " bytes of exchange scratch, above the fixed " +
+                        std::to_string(kNoAllocScratchBytes) +
+                        " bytes (use mpo_fps with a workspace)");
+    }
+    void* scratch = nullptr;
+    st = noalloc_scratch(&scratch);
+    if (st) return st;
+    return launch_group(xyz, B, N, npoint, start_idx, skip, o32, out, plan, scratch, status_out,
+                        s, "mpo_fps_noalloc");
 }
 
 }  // extern "C"

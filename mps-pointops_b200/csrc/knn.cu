@@ -26,6 +26,10 @@
 //     split 0 merges them with the full (SD, index) order.
 //   * k in (32, 256] uses a warp-per-query kernel whose sorted list is spread
 //     over the 32 lanes (8 slots each) and updated with ballot/shuffle.
+//   * k <= 32 on clouds up to 2^18 points (and three_nn) uses a warp-per-query
+//     kernel with one list slot per lane (knn_wq3_kernel): a thread-owned list
+//     makes the whole warp replay the insertion whenever any lane inserts,
+//     which on moderate clouds happens on almost every step.
 #include <string>
 
 #include "../../include/mpo_b200.h"
@@ -36,6 +40,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kTile = 1024;  // reference points per shared-memory tile (D == 3)
+constexpr int kQueue = 16;   // per-lane candidate queue (D == 3 thread kernel)
 constexpr uint32_t kNoIndex = 0xffffffffu;
 
 // Candidate policies.
@@ -114,7 +119,7 @@ struct TopK {
 // --------------------------------------------------------------------------
 // D == 3 kernel.
 template <int K, int POLICY>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
 knn3_kernel(const float* __restrict__ query, const float* __restrict__ ref, int64_t M, int64_t N,
             int k, int S, float* __restrict__ dist, int64_t* __restrict__ idx64,
             int32_t* __restrict__ idx32, float* __restrict__ sqdist) {
@@ -161,11 +166,23 @@ knn3_kernel(const float* __restrict__ query, const float* __restrict__ ref, int6
         }                                                                  \
     } while (0)
 
+    // Candidates that pass the threshold are queued per lane in shared memory
+    // ([slot][thread], conflict-free) and inserted in bulk when some lane's
+    // queue is nearly full: the warp then replays ONE insertion round for all
+    // lanes instead of one per candidate of any lane.
+    uint32_t* qi = reinterpret_cast<uint32_t*>(tile + 2 * kTile);
+    float* qd = reinterpret_cast<float*>(qi + kQueue * kThreads);
+    int qn = 0;
+    auto flush = [&]() {
+        for (int e = 0; e < qn; ++e) top.offer(qd[e * kThreads + tid], qi[e * kThreads + tid]);
+        qn = 0;
+    };
     if (ntiles > 0) {
         MPO_LOAD_TILE(0);
         MPO_STORE_TILE(0);
     }
     __syncthreads();
+    float thr = top.kth();
     for (int64_t t = 0; t < ntiles; ++t) {
         const int buf = (int)(t & 1);
         if (t + 1 < ntiles) MPO_LOAD_TILE(t + 1);
@@ -173,28 +190,30 @@ knn3_kernel(const float* __restrict__ query, const float* __restrict__ ref, int6
             const float4* tp = tile + buf * kTile + split * slice;
             const int64_t j0 = t * kTile + split * slice;
             const int cnt = (int)max64(0, min64(slice, N - j0));
-            float thr = top.kth();
             for (int e = 0; e < cnt; e += 4) {
-                float dd[4];
-                unsigned hit = 0;
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const float4 p = tp[e + u];
-                    dd[u] = sqd3(qx, qy, qz, p.x, p.y, p.z);
-                    hit |= (!(dd[u] > thr) && e + u < cnt) ? (1u << u) : 0u;
+                    const float d = sqd3(qx, qy, qz, p.x, p.y, p.z);
+                    if (!(d > thr) && e + u < cnt) {
+                        qd[qn * kThreads + tid] = d;
+                        qi[qn * kThreads + tid] = (uint32_t)(j0 + e + u);
+                        ++qn;
+                    }
                 }
-                while (hit) {
-                    const int u = __ffs(hit) - 1;
-                    hit &= hit - 1;
-                    const float d = u == 0 ? dd[0] : u == 1 ? dd[1] : u == 2 ? dd[2] : dd[3];
-                    top.offer(d, (uint32_t)(j0 + e + u));
+                if (__any_sync(__activemask(), qn > kQueue - 4)) {
+                    flush();
+                    thr = top.kth();
                 }
-                thr = top.kth();
             }
         }
         if (t + 1 < ntiles) MPO_STORE_TILE(buf ^ 1);
         __syncthreads();
     }
+    if (active) flush();
+    // The merge below reuses the tile and queue memory: every warp must have
+    // drained its queue first.
+    __syncthreads();
 #undef MPO_LOAD_TILE
 #undef MPO_STORE_TILE
 
@@ -445,6 +464,103 @@ knn_warp_kernel(const float* __restrict__ query, const float* __restrict__ ref, 
     }
 }
 
+// --------------------------------------------------------------------------
+// Warp per query, k <= 32 (D == 3): lane s holds list slot s, so the k-th
+// entry -- the threshold every lane compares against -- is one shuffle away
+// and an insertion is a warp-wide shift (ballot + popc for the position,
+// shfl_up for the move): ~12 warp instructions however many lanes see
+// candidates, instead of a per-thread register insertion that diverges.
+// Eight queries of one cloud per CTA share a reference tile of kWqTile points
+// in shared memory; lane l evaluates reference j0 + l of each 32-point chunk.
+constexpr int kWqWarps = 8;
+constexpr int kWqTile = 2048;
+
+template <int POLICY>
+__global__ void __launch_bounds__(kWqWarps * 32)
+knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, int64_t M,
+               int64_t N, int k, float* __restrict__ dist, int64_t* __restrict__ idx64,
+               int32_t* __restrict__ idx32, float* __restrict__ sqdist) {
+    __shared__ float4 tile[kWqTile];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int b = blockIdx.y;
+    const int64_t q = (int64_t)blockIdx.x * kWqWarps + warp;
+    const bool active = q < M;
+    const float* __restrict__ r = ref + (size_t)b * (size_t)N * 3;
+    float qx = 0.f, qy = 0.f, qz = 0.f;
+    if (active) {
+        const float* qp = query + ((size_t)b * (size_t)M + (size_t)q) * 3;
+        qx = qp[0];
+        qy = qp[1];
+        qz = qp[2];
+    }
+    float ld = INFINITY;    // slot `lane`
+    uint32_t li = kNoIndex;
+    int cnt = 0;            // warp-uniform
+    float kd = INFINITY;    // k-th entry once the list is full
+    uint32_t ki = kNoIndex;
+    for (int64_t t0 = 0; t0 < N; t0 += kWqTile) {
+        const int tn = (int)min64(kWqTile, N - t0);
+        __syncthreads();
+        for (int e = threadIdx.x; e < 3 * tn; e += kWqWarps * 32)
+            reinterpret_cast<float*>(tile)[(e / 3) * 4 + (e % 3)] = r[t0 * 3 + e];
+        __syncthreads();
+        if (!active) continue;
+        for (int c0 = 0; c0 < tn; c0 += 32) {
+            const int e = c0 + lane;
+            float d = INFINITY;
+            if (e < tn) {
+                const float4 p = tile[e];
+                d = sqd3(qx, qy, qz, p.x, p.y, p.z);
+            }
+            const float thr = cnt < k ? INFINITY : kd;
+            unsigned pending = __ballot_sync(FULL_MASK, e < tn && !(d > thr));
+            while (pending) {
+                const int src = __ffs(pending) - 1;
+                pending &= pending - 1;
+                const float cd = __shfl_sync(FULL_MASK, d, src);
+                const uint32_t ci = (uint32_t)(t0 + c0 + src);
+                if (!admissible<POLICY>(cd)) continue;
+                if (cnt >= k && !before<POLICY>(cd, ci, kd, ki)) continue;
+                const int pos = __popc(__ballot_sync(
+                    FULL_MASK, lane < cnt && before<POLICY>(ld, li, cd, ci)));
+                const float ud = __shfl_up_sync(FULL_MASK, ld, 1);
+                const uint32_t ui = __shfl_up_sync(FULL_MASK, li, 1);
+                if (lane > pos) {
+                    ld = ud;
+                    li = ui;
+                } else if (lane == pos) {
+                    ld = cd;
+                    li = ci;
+                }
+                cnt = min(cnt + 1, k);
+                kd = __shfl_sync(FULL_MASK, ld, k - 1);
+                ki = __shfl_sync(FULL_MASK, li, k - 1);
+            }
+        }
+    }
+    if (!active || lane >= k) return;
+    const size_t row = ((size_t)b * (size_t)M + (size_t)q) * (size_t)k;
+    const bool filled = lane < cnt;
+    const float d = filled ? ld : INFINITY;
+    dist[row + lane] = sqrtf(d);
+    if (sqdist) sqdist[row + lane] = d;
+    if (idx64) idx64[row + lane] = filled ? (int64_t)li : -1;
+    if (idx32) idx32[row + lane] = filled ? (int32_t)li : -1;
+}
+
+template <int POLICY>
+int launch_wq3(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int k,
+               float* dist, int64_t* idx64, int32_t* idx32, float* sqdist, cudaStream_t s) {
+    dim3 grid((unsigned)ceil_div(M, kWqWarps), (unsigned)B);
+    knn_wq3_kernel<POLICY><<<grid, kWqWarps * 32, 0, s>>>(query, ref, M, N, k, dist, idx64,
+                                                          idx32, sqdist);
+    return check_launch("knn_wq3_kernel");
+}
+
+// Warp-per-query for moderate clouds; thread-per-query (rare, non-divergent
+// insertions relative to a long scan) for very large reference clouds.
+inline bool use_wq3(int64_t N) { return N <= (int64_t)1 << 18; }
+
 int choose_splits(int64_t B, int64_t M, int64_t N) {
     const int64_t want = (int64_t)sm_count() * 1024;
     int S = 1;
@@ -457,7 +573,7 @@ int launch_knn3(const float* query, const float* ref, int64_t B, int64_t M, int6
                 float* dist, int64_t* idx64, int32_t* idx32, float* sqdist, cudaStream_t s) {
     const int S = choose_splits(B, M, N);
     const int qpc = kThreads / S;
-    size_t smem = 2 * kTile * sizeof(float4);
+    size_t smem = 2 * kTile * sizeof(float4) + (size_t)kQueue * kThreads * 8;
     const size_t merge = (size_t)kThreads * K * 8;
     if (merge > smem) smem = merge;
     auto kern = knn3_kernel<K, POLICY>;
@@ -509,6 +625,9 @@ int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t 
     MPO_REQUIRE(query && ref && dist && idx, "null pointer");
     cudaStream_t s = (cudaStream_t)stream;
     const int kk = (int)k;
+    if (D == 3 && k <= 32 && use_wq3(N)) {
+        return launch_wq3<kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
+    }
     if (D == 3) {
         if (k <= 4) return launch_knn3<4, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
         if (k <= 8) return launch_knn3<8, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
@@ -537,6 +656,9 @@ int mpo_three_nn(const float* unknown, const float* known, int64_t B, int64_t N,
     MPO_REQUIRE(M >= 3, "three_nn needs at least 3 known points");
     MPO_REQUIRE(M < (int64_t)0x7fffffff, "M must be below 2**31");
     MPO_REQUIRE(unknown && known && dist && idx, "null pointer");
+    if (use_wq3(M))
+        return launch_wq3<kNaNLast>(unknown, known, B, N, M, 3, dist, nullptr, idx, nullptr,
+                                    (cudaStream_t)stream);
     return launch_knn3<4, kNaNLast>(unknown, known, B, N, M, 3, dist, nullptr, idx, nullptr,
                                     (cudaStream_t)stream);
 }

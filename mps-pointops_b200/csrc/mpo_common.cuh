@@ -146,6 +146,13 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
     return v;
 }
 
+// Nanosecond wall clock of the GPU, for bounding spin waits in real time.
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 __host__ __device__ __forceinline__ int64_t ceil_div(int64_t a, int64_t b) {
     return (a + b - 1) / b;
 }

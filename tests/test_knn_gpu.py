@@ -151,3 +151,20 @@ def test_knn_cuda_module_layouts(cuda_device, transpose_mode):  # tests/test_com
         d, i = module(ref.transpose(1, 2), query.transpose(1, 2))
         d, i = d.transpose(1, 2), i.transpose(1, 2)
     assert torch.equal(i, want_i) and torch.equal(d, want_d)
+
+
+@pytest.mark.parametrize("k", [1, 16, 32])
+def test_large_reference_thread_path(cuda_device, k):
+    """Reference clouds above 2^18 points take the thread-per-query kernel."""
+    ref = cloud(1, 300_000, seed=21)
+    check(cloud(1, 40, seed=22), ref, k, cuda_device)
+
+
+def test_three_nn_large_known_cloud(cuda_device):
+    from mps_pointops.pointnet2 import three_nn
+    known = cloud(1, 300_000, seed=23)
+    unknown = cloud(1, 50, seed=24)
+    want_d, want_i = O.three_nn(unknown.numpy(), known.numpy())
+    d, i = three_nn(unknown.to(cuda_device), known.to(cuda_device))
+    np.testing.assert_array_equal(i.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(d.cpu().numpy(), want_d)

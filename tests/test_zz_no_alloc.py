@@ -65,10 +65,11 @@ def test_no_alloc_fps_matches_workspace_entry_point_twice(cuda_device):
     assert status.item() == 0 and torch.equal(got, _with_workspace(big, 64, 0, 0))
 
 
-def test_no_alloc_fps_rejects_too_many_clouds(cuda_device):
-    lib = N.lib()
-    xyz = torch.zeros(1025, 4, 3, device=cuda_device)
-    out = torch.empty(1025, 2, dtype=torch.long, device=cuda_device)
-    st = lib.mpo_fps_noalloc(N.ptr(xyz), 1025, 4, 2, 0, 0, 0, GROUP, N.ptr(out), None,
-                             N.stream(cuda_device))
-    assert st == 1 and "1024 clouds" in N.last_error()
+def test_no_alloc_fps_large_batch_reuses_scratch(cuda_device):
+    """200 clouds of 20000 points: 3 CTAs per cloud, several cooperative waves
+    that reuse the same fixed scratch one after another."""
+    xyz = _cloud(200, 20000, seed=4).to(cuda_device)
+    want = _with_workspace(xyz, 16, 7, GROUP)
+    got, status = _no_alloc(xyz, 16, 7, GROUP)
+    torch.cuda.synchronize()
+    assert status.item() == 0 and torch.equal(got, want)
