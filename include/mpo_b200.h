@@ -91,7 +91,7 @@ MPO_API int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int6
  * callers that cannot allocate device memory (for example a plugin given only
  * its input and output buffers), so it takes no workspace.  Same contract,
  * arguments and results as mpo_fps; the CTA-group path keeps its step slots
- * in a fixed 8 KiB array inside the library (per device) -- enough for any
+ * in a fixed 40 KiB array inside the library (per device) -- enough for any
  * batch on a 148-SM B200, since cooperative waves reuse the slots; a launch
  * that would need more is rejected with MPO_ERR_INVALID_ARGUMENT.  The first
  * call on a device looks the array up (cudaGetSymbolAddress) and should come

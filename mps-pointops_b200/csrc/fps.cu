@@ -48,10 +48,12 @@ constexpr unsigned long long kIndexMask = (1ull << kIndexBits) - 1;
 
 // Cross-CTA exchange state of the clouds of one cooperative wave, in the
 // caller's workspace (zeroed before each wave):
-//   slots[cloud_in_wave][parity][G]  u64
+//   slots[cloud_in_wave][parity][G]  one u64 per 128-byte line, so the G
+//                                    readers of a step spread over G lines
 //   error[cloud_in_wave]             u32
+constexpr int kSlotStride = 16;  // u64 words per slot (128 bytes)
 inline size_t group_bytes(int64_t clouds, int64_t G) {
-    return (size_t)clouds * 2 * (size_t)G * 8 + (size_t)clouds * 8;
+    return (size_t)clouds * 2 * (size_t)G * 8 * kSlotStride + (size_t)clouds * 8;
 }
 
 template <int P, bool GROUP>
@@ -77,7 +79,8 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
     const float* __restrict__ p = xyz + (size_t)b * (size_t)N * 3;
     const int64_t lo = (int64_t)g * per_cta;
     const int64_t hi = min64(N, lo + per_cta);
-    unsigned long long* my_slots = GROUP ? slots + (size_t)wave_cloud * 2 * G : nullptr;
+    unsigned long long* my_slots =
+        GROUP ? slots + (size_t)wave_cloud * 2 * G * kSlotStride : nullptr;
     unsigned* my_error = GROUP ? errors + wave_cloud : nullptr;
 
     float px[P], py[P], pz[P], md[P];
@@ -189,25 +192,26 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
             // Publish this CTA's best into slots[parity][g], then warp 0 waits
             // for all G slots of this step and reduces them.  A CTA can be at
             // most one step ahead of the slowest reader, so two buffers suffice.
-            unsigned long long* cur = my_slots + (size_t)buf * G;
+            unsigned long long* cur = my_slots + (size_t)buf * G * kSlotStride;
             const unsigned long long seq = (unsigned long long)((i + 1) & 0x7ff);
             if (warp == 0) {
                 if (lane == 0) {
                     const unsigned long long word = ((unsigned long long)cmax << 32) |
                                                     (seq << kIndexBits) |
                                                     ((unsigned long long)cidx & kIndexMask);
-                    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(cur + g), "l"(word)
+                    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(cur + g * kSlotStride),
+                                 "l"(word)
                                  : "memory");
                 }
                 uint32_t bk = 0u, bi = 0xffffffffu;
                 const unsigned long long t0 = globaltimer_ns();
                 bool abort = false;
-                for (;;) {
+                for (unsigned round = 1;; ++round) {
                     bool ok = true;
                     bk = 0u;
                     bi = 0xffffffffu;
                     for (int c = lane; c < G; c += 32) {
-                        const unsigned long long v = ld_relaxed_u64(cur + c);
+                        const unsigned long long v = ld_relaxed_u64(cur + c * kSlotStride);
                         if (((v >> kIndexBits) & 0x7ffull) != seq) {
                             ok = false;
                         } else {
@@ -220,7 +224,8 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
                         }
                     }
                     if (__all_sync(FULL_MASK, ok)) break;
-                    if (globaltimer_ns() - t0 > kSpinLimitNs || ld_acquire_u32(my_error) != 0u) {
+                    if ((round & 63u) == 0u &&
+                        (globaltimer_ns() - t0 > kSpinLimitNs || ld_acquire_u32(my_error) != 0u)) {
                         abort = true;
                         break;
                     }
@@ -321,7 +326,8 @@ int launch_group(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t
     int64_t per_cta = plan.per_cta;
     const int threads = threads_for(per_cta, kMaxP);
     unsigned long long* slots = reinterpret_cast<unsigned long long*>(scratch);
-    unsigned* errors = reinterpret_cast<unsigned*>(slots + (size_t)plan.clouds_per_wave * 2 * G);
+    unsigned* errors =
+        reinterpret_cast<unsigned*>(slots + (size_t)plan.clouds_per_wave * 2 * G * kSlotStride);
     const size_t bytes = group_bytes(plan.clouds_per_wave, G);
     for (int64_t c0 = 0; c0 < B; c0 += plan.clouds_per_wave) {
         const int nc = (int)min64(plan.clouds_per_wave, B - c0);
@@ -419,10 +425,10 @@ int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t star
 // rules forbid any allocation once it is running.  mpo_fps_noalloc serves
 // them: the cross-CTA step slots of the CTA-group path live in the
 // file-scope array below instead of a caller workspace.
-//   * Capacity: kNoAllocScratchBytes (8 KiB per device, held by every device
+//   * Capacity: kNoAllocScratchBytes (40 KiB per device, held by every device
 //     that loads this library until the process exits).  The group path
-//     needs 16 bytes per CTA of one cooperative wave plus 8 per cloud (under
-//     4 KiB on a 148-SM B200) whatever the batch size, because waves reuse
+//     needs 256 bytes per CTA of one cooperative wave plus 8 per cloud (under
+//     38 KiB on a 148-SM B200) whatever the batch size, because waves reuse
 //     the slots; a configuration needing more is rejected.  The
 //     one-CTA-per-cloud path needs no scratch.
 //   * In host code the array's name is only a host-side stand-in; the
@@ -435,7 +441,7 @@ int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t star
 //     caller.
 namespace mpo {
 namespace {
-constexpr size_t kNoAllocScratchBytes = 8192;
+constexpr size_t kNoAllocScratchBytes = 40960;
 static __device__ __align__(256) unsigned char g_fps_noalloc_scratch[kNoAllocScratchBytes];
 
 int noalloc_scratch(void** out) {
