@@ -52,9 +52,33 @@ def _validate_normals(points: Tensor, normals: Tensor | None, name: str) -> None
         raise ValueError(f"{name} must match its points' device and dtype")
 
 
-def _validate_clouds(x, y, x_lengths, y_lengths):
+class _PendingCheck:
+    """Flags of mpo_chamfer_check_inputs copied to pinned host memory
+    asynchronously; ``raise_if_bad`` waits for that copy only, so the device
+    work queued after the check keeps running while the host reads them."""
+
+    def __init__(self, flags_host: Tensor, event: torch.cuda.Event, P: int, Q: int):
+        self.flags, self.event, self.P, self.Q = flags_host, event, P, Q
+
+    def raise_if_bad(self) -> None:
+        self.event.synchronize()
+        bad_x, bad_y, bad_lx, bad_ly = self.flags.tolist()
+        if bad_lx:
+            raise ValueError(f"x_lengths must lie in [0, {self.P}]")
+        if bad_ly:
+            raise ValueError(f"y_lengths must lie in [0, {self.Q}]")
+        if bad_x:
+            raise ValueError("valid x coordinates must be finite")
+        if bad_y:
+            raise ValueError("valid y coordinates must be finite")
+
+
+def _validate_clouds(x, y, x_lengths, y_lengths, defer: bool = False):
     """mps_pointops/chamfer.py:79-110: shapes, dtype, lengths in range and
-    finite valid coordinates -- here one native check and one host sync."""
+    finite valid coordinates -- here one native check.  With ``defer`` the
+    result is returned as a _PendingCheck to be raised after the search has
+    been queued (the kernels clamp lengths, so queuing them first is safe);
+    otherwise it is raised here."""
     if x.ndim != 3 or y.ndim != 3 or x.shape[-1] < 1 or y.shape[-1] != x.shape[-1]:
         raise ValueError("x and y must have shapes (B, P, D) and (B, Q, D) with D >= 1")
     if x.shape[0] != y.shape[0]:
@@ -80,16 +104,15 @@ def _validate_clouds(x, y, x_lengths, y_lengths):
         N.check(N.lib().mpo_chamfer_check_inputs(N.ptr(xc), N.ptr(yc), N.ptr(lx), N.ptr(ly), B, P,
                                                  Q, D, N.ptr(flags), N.stream(x.device)),
                 "chamfer input check")
-    bad_x, bad_y, bad_lx, bad_ly = flags.tolist()
-    if bad_lx:
-        raise ValueError(f"x_lengths must lie in [0, {P}]")
-    if bad_ly:
-        raise ValueError(f"y_lengths must lie in [0, {Q}]")
-    if bad_x:
-        raise ValueError("valid x coordinates must be finite")
-    if bad_y:
-        raise ValueError("valid y coordinates must be finite")
-    return lx, ly
+        host = torch.empty(4, dtype=torch.int32, pin_memory=True)
+        host.copy_(flags, non_blocking=True)
+        event = torch.cuda.Event()
+        event.record(torch.cuda.current_stream(x.device))
+    pending = _PendingCheck(host, event, P, Q)
+    if not defer:
+        pending.raise_if_bad()
+        pending = None
+    return lx, ly, pending
 
 
 class _NearestSquared(torch.autograd.Function):
@@ -214,7 +237,11 @@ def chamfer_distance(
         raise ValueError('Normals must be None if point_reduction is "max"')
     x, x_lengths, x_normals = _unpack_cloud(x, x_lengths, x_normals, "x")
     y, y_lengths, y_normals = _unpack_cloud(y, y_lengths, y_normals, "y")
-    lx, ly = _validate_clouds(x, y, x_lengths, y_lengths)
+    # When nothing else can raise between the input check and the search
+    # (no normals, no weights), the check's result is read after the search
+    # is queued, so the device never idles on this host round trip.
+    defer = x_normals is None and y_normals is None and weights is None and norm == 2
+    lx, ly, pending = _validate_clouds(x, y, x_lengths, y_lengths, defer=defer)
     if x.shape[-1] != 3 and (x_normals is not None or y_normals is not None):
         raise NotImplementedError("normal loss currently requires D == 3")
     _validate_normals(x, x_normals, "x_normals")
@@ -234,6 +261,8 @@ def chamfer_distance(
         raise NotImplementedError("norm=1 (L1) Chamfer is not implemented in the B200 build")
 
     dx, dy, ix, iy = _NearestSquared.apply(x, y, lx, ly, not single_directional)
+    if pending is not None:
+        pending.raise_if_bad()
     nx = ny = None
     if return_normals:
         flx, fly = _full_lengths(x, lx), _full_lengths(y, ly)
