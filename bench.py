@@ -278,12 +278,13 @@ def run_b200(args, world, rank, local):
     secondary = None if args.no_secondary else ssg_secondary(args.steps, args.warmup, world, rank)
 
     # Roofline of the dominant kernel: the nearest search (8 separately rounded
-    # flops per unique pair) against the FP32 add/mul issue peak of packed
-    # f32x2 instructions, 2 x 128 lanes per SM per clock.
+    # flops per unique pair) against the FP32 pipe: 128 rounded fp32 ops per
+    # SM per clock (a packed f32x2 op holds the pipe for two cycles, so
+    # packing saves issue slots but does not raise this bound).
     local_pairs = B_PER_GPU * NPTS * NPTS
     achieved = local_pairs * FLOPS_PER_PAIR / (kernel_ms / 1e3) / 1e12
     sm_max = (clock_info or {}).get("sm_max_mhz") or 1965.0
-    peak = 2 * 128 * props.multi_processor_count * sm_max * 1e6 / 1e12
+    peak = 128 * props.multi_processor_count * sm_max * 1e6 / 1e12
     traffic = None
     tfile = ROOT / "profiles" / "chamfer_sym3_config2.md"
     if tfile.exists():
@@ -310,10 +311,12 @@ def run_b200(args, world, rank, local):
                      "frac": achieved / peak, "traffic": traffic,
                      "kernel_ms": kernel_ms,
                      "work": f"{FLOPS_PER_PAIR} flop x {local_pairs} unique pairs per launch",
-                     "peak_source": "nominal packed-f32x2 add/mul issue rate: 2 x 128 lanes x "
-                                    f"{props.multi_processor_count} SMs x {sm_max:.0f} MHz "
-                                    "(MEASURED_PEAKS.json has no FP32 figure; an fadd2+fmul2 "
-                                    "probe measured 71 TFLOP/s on this pool)"},
+                     "peak_source": "nominal FP32 pipe rate for separately rounded add/sub/mul: "
+                                    f"128 lanes x {props.multi_processor_count} SMs x "
+                                    f"{sm_max:.0f} MHz (MEASURED_PEAKS.json has no FP32 figure; "
+                                    "a packed fma.rn.f32x2 probe on this pool sustained one "
+                                    "instruction per 2 cycles per SM sub-partition, i.e. the "
+                                    "same 128 lane-ops per SM per clock)"},
         "clocks": clock_info,
     }
     if secondary:

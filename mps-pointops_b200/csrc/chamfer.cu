@@ -155,9 +155,10 @@ nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
 // (y -> x).
 //
 // Work item = (cloud, 1024 x-rows, 1024 y-columns); CTAs take items from an
-// atomic counter.  The y tile is staged in shared memory as duplicated pairs
-// ((y.x, y.x, y.y, y.y), (y.z, y.z, -, -)) so a warp-broadcast load yields
-// packed f32x2 operands.  Lane l of warp w owns x-rows
+// atomic counter.  The y tile is staged in shared memory so that warp-
+// broadcast loads yield packed f32x2 operands: one float4 (y.x, y.x, y.y,
+// y.y) per column and one float4 (z_j, z_j, z_j+1, z_j+1) per column pair
+// (three 16-byte loads per two columns).  Lane l of warp w owns x-rows
 // i0 + (32 w + l) * R .. + R - 1 (contiguous, so row order = (warp, lane, k)),
 // packed two per f32x2 register, and a warp walks the columns together:
 //   * rows: a running minimum over blocks of C columns (one min per pair),
@@ -165,27 +166,36 @@ nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
 //     bit order == value order); the column inside the winning block is
 //     recovered at the end of the item by recomputing C distances;
 //   * columns: the lane's minimum over its R rows, then one redux.sync.min
-//     over the warp and one ballot of the lanes holding it -> one 64-bit
-//     (min bits, lane mask) record per (warp, column) in shared memory; at
-//     the end of the item a thread per column picks the first warp, the first
-//     lane and (recomputing R distances) the first row holding the minimum.
+//     over the warp and one ballot of the lanes holding it; the C records of
+//     a block are kept in registers and written once per block as 64-bit
+//     (min bits, lane mask) words (lane c stores column c).  At the end of
+//     the item a thread per column picks the first warp, the first lane and
+//     (recomputing R distances) the first row holding the minimum.
 // Both directions are committed as 64-bit keys (SD bits << 32 | index) with
 // atomicMin into global scratch, which yields the smallest SD and, among
 // equal SDs, the lowest index -- the reference's first-minimum rule.
 // Padding (index >= length) enters as +inf coordinates: it ties valid
 // entries only at +inf and then loses on index, and padding-vs-padding pairs
 // are NaN, which never wins a min.
+//
+// Cost model (B200, measured): a packed f32x2 op holds the FP32 pipe for two
+// cycles, i.e. the pipe does 128 rounded fp32 ops per SM per clock whether
+// packed or not; packing halves the issue slots the distance needs, so the
+// min/ballot bookkeeping (about 3 issue slots per pair-row) is what separates
+// the kernel from the FP32 bound of 8 ops per pair.
 namespace sym {
 constexpr unsigned long long kMaxKey = ~0ull;
 
 // Tile shape: kWarps warps, kR x-rows per lane (even: packed in pairs), kC
-// columns per row-minimum block, kBN y-columns per item, kMinBlocks CTAs
-// per SM for the register budget.
+// columns per row-minimum block (even), kBN y-columns per item, kMinBlocks
+// CTAs per SM for the register budget.
 template <int kWarps, int kR, int kC, int kBN, int kMinBlocks>
 struct Shape {
     static constexpr int kThreads = kWarps * 32;
     static constexpr int kBM = kWarps * 32 * kR;
-    static constexpr size_t kSmem = (size_t)kBN * 2 * sizeof(float4) + (size_t)kWarps * kBN * 8;
+    static constexpr int kCols = kBN;
+    static constexpr size_t kColBytes = (size_t)kBN * 16 + (size_t)kBN / 2 * 16;
+    static constexpr size_t kSmem = kColBytes + (size_t)kWarps * kBN * 8;
 };
 
 template <int kWarps, int kR, int kC, int kBN, int kMinBlocks>
@@ -194,16 +204,20 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
                     const int64_t* __restrict__ x_lengths, const int64_t* __restrict__ y_lengths,
                     int64_t B, int64_t P, int64_t Q, unsigned long long* __restrict__ keys_x,
                     unsigned long long* __restrict__ keys_y, unsigned* __restrict__ counter) {
+    using S = Shape<kWarps, kR, kC, kBN, kMinBlocks>;
     extern __shared__ float4 smem4[];
-    float4* s_col = smem4;                                                 // [kBN][2]
-    unsigned long long* s_part = reinterpret_cast<unsigned long long*>(smem4 + 2 * kBN);
+    float4* s_xy = smem4;        // [kBN]      (y.x, y.x, y.y, y.y)
+    float4* s_z = smem4 + kBN;   // [kBN / 2]  (z_2i, z_2i, z_2i+1, z_2i+1)
+    unsigned long long* s_part =
+        reinterpret_cast<unsigned long long*>(reinterpret_cast<unsigned char*>(smem4) + S::kColBytes);
     __shared__ unsigned s_item;
-    constexpr int kThreads = kWarps * 32;
-    constexpr int kBM = kWarps * 32 * kR;
-    static_assert(kR % 2 == 0 && kBN % kC == 0, "bad tile shape");
+    constexpr int kThreads = S::kThreads;
+    constexpr int kBM = S::kBM;
+    static_assert(kR % 2 == 0 && kC % 2 == 0 && kC <= 32 && kBN % kC == 0, "bad tile shape");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t row_blocks = ceil_div(P, kBM), col_blocks = ceil_div(Q, kBN);
     const int64_t per_cloud = row_blocks * col_blocks, total = B * per_cloud;
+    const float* s_zf = reinterpret_cast<const float*>(s_z);
 
     for (;;) {
         if (tid == 0) s_item = atomicAdd(counter, 1u);
@@ -220,6 +234,7 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
         const float* __restrict__ xb = x + (size_t)b * P * 3;
         const float* __restrict__ yb = y + (size_t)b * Q * 3;
 
+        float* s_zw = reinterpret_cast<float*>(s_z);
         for (int e = tid; e < kBN; e += kThreads) {
             const int64_t j = j0 + e;
             float px = INFINITY, py = INFINITY, pz = INFINITY;
@@ -228,8 +243,9 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
                 py = yb[3 * j + 1];
                 pz = yb[3 * j + 2];
             }
-            s_col[2 * e] = make_float4(px, px, py, py);
-            s_col[2 * e + 1] = make_float4(pz, pz, 0.f, 0.f);
+            s_xy[e] = make_float4(px, px, py, py);
+            s_zw[2 * e] = pz;
+            s_zw[2 * e + 1] = pz;
         }
         const int64_t rbase = i0 + (int64_t)(warp * 32 + lane) * kR;
         f32x2 X[kR / 2], Y[kR / 2], Z[kR / 2];
@@ -259,32 +275,48 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
         }
         for (int jb = 0; jb < kBN; jb += kC) {
             float m[kR];
+            unsigned pmin[kC], pmask[kC];
 #pragma unroll
-            for (int c = 0; c < kC; ++c) {
-                const int j = jb + c;
-                const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(&s_col[2 * j]);
-                const f32x2 bz = *reinterpret_cast<const f32x2*>(&s_col[2 * j + 1]);
-                float d[kR];
+            for (int c2 = 0; c2 < kC; c2 += 2) {
+                const ulonglong2 a0 = *reinterpret_cast<const ulonglong2*>(&s_xy[jb + c2]);
+                const ulonglong2 a1 = *reinterpret_cast<const ulonglong2*>(&s_xy[jb + c2 + 1]);
+                const ulonglong2 zz = *reinterpret_cast<const ulonglong2*>(&s_z[(jb + c2) >> 1]);
 #pragma unroll
-                for (int q = 0; q < kR / 2; ++q) {
-                    const f32x2 dd = sqd3x2(X[q], Y[q], Z[q], a.x, a.y, bz);
-                    unpack2(dd, d[2 * q], d[2 * q + 1]);
+                for (int h = 0; h < 2; ++h) {
+                    const int c = c2 + h;
+                    const ulonglong2 a = h ? a1 : a0;
+                    const f32x2 bz = h ? zz.y : zz.x;
+                    float d[kR];
+#pragma unroll
+                    for (int q = 0; q < kR / 2; ++q) {
+                        const f32x2 dd = sqd3x2(X[q], Y[q], Z[q], a.x, a.y, bz);
+                        unpack2(dd, d[2 * q], d[2 * q + 1]);
+                    }
+#pragma unroll
+                    for (int k = 0; k < kR; ++k) m[k] = (c == 0) ? d[k] : fminf(m[k], d[k]);
+                    float t[kR];
+#pragma unroll
+                    for (int k = 0; k < kR; ++k) t[k] = d[k];
+#pragma unroll
+                    for (int w2 = kR / 2; w2 >= 1; w2 /= 2) {
+#pragma unroll
+                        for (int k = 0; k < w2; ++k) t[k] = fminf(t[k], t[k + w2]);
+                    }
+                    const unsigned cb = __float_as_uint(t[0]);
+                    pmin[c] = __reduce_min_sync(FULL_MASK, cb);
+                    pmask[c] = __ballot_sync(FULL_MASK, cb == pmin[c]);
                 }
+            }
+            if (lane < kC) {
+                unsigned v = pmin[0], mk = pmask[0];
 #pragma unroll
-                for (int k = 0; k < kR; ++k) m[k] = (c == 0) ? d[k] : fminf(m[k], d[k]);
-                float t[kR];
-#pragma unroll
-                for (int k = 0; k < kR; ++k) t[k] = d[k];
-#pragma unroll
-                for (int w2 = kR / 2; w2 >= 1; w2 /= 2) {
-#pragma unroll
-                    for (int k = 0; k < w2; ++k) t[k] = fminf(t[k], t[k + w2]);
+                for (int c = 1; c < kC; ++c) {
+                    if (lane == c) {
+                        v = pmin[c];
+                        mk = pmask[c];
+                    }
                 }
-                const float cm = t[0];
-                const unsigned cb = __float_as_uint(cm);
-                const unsigned wmin = __reduce_min_sync(FULL_MASK, cb);
-                const unsigned mask = __ballot_sync(FULL_MASK, cb == wmin);
-                if (lane == 0) s_part[warp * kBN + j] = ((unsigned long long)wmin << 32) | mask;
+                s_part[warp * kBN + jb + lane] = ((unsigned long long)v << 32) | mk;
             }
 #pragma unroll
             for (int k = 0; k < kR; ++k) {
@@ -310,10 +342,10 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
                 rz = (k & 1) ? t1 : t0;
                 int col = blk[k];
                 for (int c = 0; c < kC; ++c) {
-                    const float4 pa = s_col[2 * (blk[k] + c)];
-                    const float4 pb = s_col[2 * (blk[k] + c) + 1];
-                    if (__float_as_uint(sqd3(rx, ry, rz, pa.x, pa.z, pb.x)) == best[k]) {
-                        col = blk[k] + c;
+                    const int j = blk[k] + c;
+                    const float4 pa = s_xy[j];
+                    if (__float_as_uint(sqd3(rx, ry, rz, pa.x, pa.z, s_zf[2 * j])) == best[k]) {
+                        col = j;
                         break;
                     }
                 }
@@ -340,13 +372,13 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
             }
             const int l = __ffs(bm) - 1;
             const int64_t r0 = i0 + (int64_t)(bw * 32 + l) * kR;
-            const float4 pa = s_col[2 * e];
-            const float4 pb = s_col[2 * e + 1];
+            const float4 pa = s_xy[e];
+            const float pz = s_zf[2 * e];
             int64_t row = r0;
             for (int k = 0; k < kR; ++k) {
                 const int64_t r = r0 + k;
                 if (r >= xlen) break;
-                const float d = sqd3(xb[3 * r], xb[3 * r + 1], xb[3 * r + 2], pa.x, pa.z, pb.x);
+                const float d = sqd3(xb[3 * r], xb[3 * r + 1], xb[3 * r + 2], pa.x, pa.z, pz);
                 if (__float_as_uint(d) == bv) {
                     row = r;
                     break;
@@ -571,7 +603,7 @@ int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths
         return fail(kCudaError, "mpo_chamfer_nearest: shared-memory limit");
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Sh::kThreads, Sh::kSmem);
-    const int64_t items = B * ceil_div(P, Sh::kBM) * ceil_div(Q, 1024);
+    const int64_t items = B * ceil_div(P, Sh::kBM) * ceil_div(Q, Sh::kCols);
     const int64_t grid = min64(items, (int64_t)sm_count() * max64(per_sm, 1));
     kern<<<(unsigned)grid, Sh::kThreads, Sh::kSmem, s>>>(x, y, x_lengths, y_lengths, B, P, Q,
                                                          keys_x, keys_y, counter);
