@@ -38,7 +38,7 @@ extern "C" {
 #define MPO_API
 #endif
 
-#define MPO_ABI_VERSION 1
+#define MPO_ABI_VERSION 2
 
 #define MPO_OK 0
 #define MPO_ERR_INVALID_ARGUMENT 1
@@ -110,9 +110,15 @@ MPO_API int mpo_fps_noalloc(const float* xyz, int64_t B, int64_t N, int64_t npoi
  *   sqdist (nullable, (B,M,k)) receives the squared distances before the
  *   square root.  1 <= k <= min(N, 256).  D == 3 drops NaN candidates and
  *   ranks +inf; D != 3 drops every non-finite candidate; unfilled slots are
- *   (inf, -1). */
+ *   (inf, -1).
+ *   workspace: mpo_knn_workspace_bytes(B, M, N, D, k) bytes of device memory
+ *   (0 when the call needs none: D == 3, small or narrow problems).  Feature
+ *   kNN with 16 <= D <= 1024, k <= 32 and N >= 2048 proposes candidates with
+ *   tensor-core (tcgen05) scores and ranks them by the exact fp32 SD. */
+MPO_API size_t mpo_knn_workspace_bytes(int64_t B, int64_t M, int64_t N, int64_t D, int64_t k);
 MPO_API int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int64_t D,
-            int64_t k, float* dist, int64_t* idx, float* sqdist, void* stream);
+            int64_t k, float* dist, int64_t* idx, float* sqdist, void* workspace,
+            size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------ ball query
  * Replaces the `ball_query_f32` dispatch of mps_pointops/_ball_query_mps.py:

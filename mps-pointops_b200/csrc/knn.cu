@@ -34,6 +34,7 @@
 
 #include "../../include/mpo_b200.h"
 #include "mpo_common.cuh"
+#include "knn_select.cuh"
 
 namespace mpo {
 namespace {
@@ -41,80 +42,6 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kTile = 1024;  // reference points per shared-memory tile (D == 3)
 constexpr int kQueue = 16;   // per-lane candidate queue (D == 3 thread kernel)
-constexpr uint32_t kNoIndex = 0xffffffffu;
-
-// Candidate policies.
-enum Policy : int {
-    kDropNaN = 0,        // kNN, D == 3: NaN never enters, +inf is ranked
-    kDropNonFinite = 1,  // kNN, D != 3: every non-finite SD is dropped
-    kNaNLast = 2,        // three_nn: NaN ranks after every number
-};
-
-template <int POLICY>
-__device__ __forceinline__ bool admissible(float d) {
-    if (POLICY == kDropNaN) return !isnan(d);
-    if (POLICY == kDropNonFinite) return isfinite(d);
-    return true;
-}
-
-// Strict (SD, index) order; with kNaNLast a NaN sorts after every number and
-// NaNs sort by index.
-template <int POLICY>
-__device__ __forceinline__ bool before(float d, uint32_t i, float e, uint32_t j) {
-    if (POLICY == kNaNLast) {
-        const bool dn = isnan(d), en = isnan(e);
-        if (dn != en) return en;
-        if (dn) return i < j;
-    }
-    return d < e || (d == e && i < j);
-}
-
-// Register-resident sorted list of capacity K.  The logical list of runtime
-// length k (<= K) is right-aligned: physical slot s holds logical entry
-// s - (K - k); the K - k leading slots hold (-inf, 0) sentinels that precede
-// every candidate and never move.  The k-th entry is therefore always in the
-// static slot K - 1 and no register array is ever indexed dynamically.
-template <int K, int POLICY>
-struct TopK {
-    float d[K];
-    uint32_t i[K];
-    int cnt;   // filled logical entries
-    int base;  // K - k
-
-    __device__ __forceinline__ void init(int k) {
-        base = K - k;
-#pragma unroll
-        for (int s = 0; s < K; ++s) {
-            d[s] = s < base ? -INFINITY : INFINITY;
-            i[s] = s < base ? 0u : kNoIndex;
-        }
-        cnt = 0;
-    }
-
-    // Offer (dd, jj): the candidate bubbles down the sorted list, swapping
-    // with every entry it precedes (empty slots always yield).
-    __device__ __forceinline__ void offer(float dd, uint32_t jj) {
-        if (!admissible<POLICY>(dd)) return;
-        if (cnt >= K - base && !before<POLICY>(dd, jj, d[K - 1], i[K - 1])) return;
-        const int empty_from = base + cnt;
-#pragma unroll
-        for (int s = 0; s < K; ++s) {
-            const bool take = (s >= empty_from) || before<POLICY>(dd, jj, d[s], i[s]);
-            const float od = d[s];
-            const uint32_t oi = i[s];
-            d[s] = take ? dd : od;
-            i[s] = take ? jj : oi;
-            dd = take ? od : dd;
-            jj = take ? oi : jj;
-        }
-        cnt = min(cnt + 1, K - base);
-    }
-
-    // Threshold for the hot-loop filter: a candidate with d > kth can never
-    // enter (NaN and ties are decided in offer()).  Empty slots hold +inf.
-    __device__ __forceinline__ float kth() const { return d[K - 1]; }
-    __device__ __forceinline__ bool full() const { return cnt >= K - base; }
-};
 
 // --------------------------------------------------------------------------
 // D == 3 kernel.
@@ -614,8 +541,14 @@ int launch_knnd(const float* query, const float* ref, int64_t B, int64_t M, int6
 
 extern "C" {
 
+size_t mpo_knn_workspace_bytes(int64_t B, int64_t M, int64_t N, int64_t D, int64_t k) {
+    if (B <= 0 || M <= 0 || !mpo::fknn_tc_eligible(M, N, D, k)) return 0;
+    return mpo::fknn_tc_workspace_bytes(B, M, N);
+}
+
 int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int64_t D,
-            int64_t k, float* dist, int64_t* idx, float* sqdist, void* stream) {
+            int64_t k, float* dist, int64_t* idx, float* sqdist, void* workspace,
+            size_t workspace_bytes, void* stream) {
     using namespace mpo;
     MPO_REQUIRE(B >= 0 && M >= 0 && N >= 0 && D >= 1, "bad sizes");
     MPO_REQUIRE(k >= 0 && k <= N, "k must be in [0, N]");
@@ -625,6 +558,9 @@ int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t 
     MPO_REQUIRE(query && ref && dist && idx, "null pointer");
     cudaStream_t s = (cudaStream_t)stream;
     const int kk = (int)k;
+    if (fknn_tc_eligible(M, N, D, k))
+        return fknn_tc_run(query, ref, B, M, N, D, k, dist, idx, sqdist, workspace,
+                           workspace_bytes, s);
     if (D == 3 && k <= 32 && use_wq3(N)) {
         return launch_wq3<kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
     }

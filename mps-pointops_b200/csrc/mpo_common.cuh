@@ -34,6 +34,13 @@ int fail(int status, const std::string& msg);
 int check_launch(const char* what);  // also counts one kernel launch
 void count_launches(uint64_t n);
 int sm_count(int device = -1);
+
+// Tensor-core feature kNN (feature_knn_tc.cu).
+bool fknn_tc_eligible(int64_t M, int64_t N, int64_t D, int64_t k);
+size_t fknn_tc_workspace_bytes(int64_t B, int64_t M, int64_t N);
+int fknn_tc_run(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int64_t D,
+                int64_t k, float* dist, int64_t* idx, float* sqdist, void* workspace,
+                size_t workspace_bytes, cudaStream_t s);
 int current_device();
 
 #define MPO_REQUIRE(cond, msg)                                   \

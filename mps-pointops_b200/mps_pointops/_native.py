@@ -20,7 +20,7 @@ from pathlib import Path
 import torch
 
 LIB_NAME = "libmpo_b200.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 _lib = None
 _lock = threading.Lock()
 _checked_devices: set[int] = set()
@@ -40,7 +40,8 @@ SIGNATURES = {
     "mpo_fps_workspace_bytes": (_sz, [_i64, _i64, _i64, _int]),
     "mpo_fps": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _sz, _vp]),
     "mpo_fps_noalloc": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp]),
-    "mpo_knn": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "mpo_knn_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "mpo_knn": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mpo_ball_query": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp]),
     "mpo_ball_query_pointnet2": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _f32, _vp, _vp]),
     "mpo_ball_query_backward": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp,

@@ -130,8 +130,11 @@ def knn(query: Tensor, ref: Tensor, k: int) -> tuple[Tensor, Tensor]:
         return dist, idx
     query, ref = query.contiguous(), ref.contiguous()
     with N.on_device(query.device):
-        N.check(N.lib().mpo_knn(N.ptr(query), N.ptr(ref), B, M, Nr, D, k, N.ptr(dist),
-                                N.ptr(idx), None, N.stream(query.device)), "knn")
+        lib = N.lib()
+        ws_bytes = int(lib.mpo_knn_workspace_bytes(B, M, Nr, D, k))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=query.device) if ws_bytes else None
+        N.check(lib.mpo_knn(N.ptr(query), N.ptr(ref), B, M, Nr, D, k, N.ptr(dist), N.ptr(idx),
+                            None, N.ptr(ws), ws_bytes, N.stream(query.device)), "knn")
     return dist, idx
 
 

@@ -28,11 +28,15 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_error_channel():
     lib = N.lib()
-    assert lib.mpo_abi_version() == N.ABI_VERSION == 1
+    assert lib.mpo_abi_version() == N.ABI_VERSION == 2
     # Argument validation happens before any CUDA call, so it runs without a GPU.
-    st = lib.mpo_knn(None, None, 1, 1, 1000, 3, 300, None, None, None, None)
+    st = lib.mpo_knn(None, None, 1, 1, 1000, 3, 300, None, None, None, None, 0, None)
     assert st == 1
     assert "at most 256" in N.last_error()
+    # The tensor-core feature path needs a workspace; D == 3 needs none.
+    assert lib.mpo_knn_workspace_bytes(2, 4096, 4096, 64, 20) > 2 * 4096 * 64 * 8
+    assert lib.mpo_knn_workspace_bytes(2, 4096, 4096, 3, 20) == 0
+    assert lib.mpo_knn_workspace_bytes(2, 4096, 1000, 64, 20) == 0
     st = lib.mpo_fps(None, 1, 10, 4, 12, 0, 0, 0, None, None, None, 0, None)
     assert st == 1 and "start_idx" in N.last_error()
     st = lib.mpo_fps(None, 1, 10, 4, 0, 0, 0, 7, None, None, None, 0, None)

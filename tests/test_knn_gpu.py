@@ -89,7 +89,7 @@ def test_sqdist_output_is_exact(cuda_device):
     sd = torch.empty(1, 300, 24, device=cuda_device)
     qc, rc = q.to(cuda_device), r.to(cuda_device)
     N.check(N.lib().mpo_knn(N.ptr(qc), N.ptr(rc), 1, 300, 5000, 3, 24, N.ptr(dist), N.ptr(idx),
-                            N.ptr(sd), N.stream(cuda_device)), "knn")
+                            N.ptr(sd), None, 0, N.stream(cuda_device)), "knn")
     want = O.knn_sqdist(q.numpy(), r.numpy(), idx.cpu().numpy())
     np.testing.assert_array_equal(sd.cpu().numpy(), want)
 
