@@ -11,27 +11,31 @@
 // The tensor cores only PROPOSE candidates; every reported distance and every
 // ranking decision comes from the exact fp32 SD.  Design:
 //
-//  1. Norms (fknn_norms_kernel): n(p) = sum of p_t^2 in fp32 for queries and
-//     references; per cloud the largest reference norm and a flag for
-//     non-finite or huge norms (such clouds skip the tensor path).
-//  2. Approximate scores on tcgen05 (fknn_tc_kernel): for a CTA's 128 queries
-//     and a 256-reference tile, dot(q, r) comes from kind::f16 MMAs with bf16
-//     operands split as p = hi + lo (hi = bf16(p), lo = bf16(p - hi)):
-//     dot ~= hi.hi' + hi.lo' + lo.hi' accumulated in fp32 in tensor memory
-//     (TMEM, 128 lanes x 256 columns).  The epilogue thread of a query row
-//     reads its accumulator row with tcgen05.ld and forms the score
-//     s_j = n(r_j) - 2 dot'_j, so SD'_j = n(q) + s_j approximates SD_j with
-//     |SD'_j - SD_j| <= eps(q) = C_K (n(q) + max_j n(r_j)) (bound below).
+//  1. Pack (fknn_pack_kernel, fknn_norms_kernel): queries and references are
+//     split as p = hi + lo (hi = bf16(p), lo = bf16(p - hi)) and written once
+//     in the operand layout of the MMA (per 128-row tile, K-major core
+//     matrices), so a tile reaches shared memory with one bulk copy; norms
+//     n(p) = sum of p_t^2 (fp32), padded with +inf per 128-reference tile;
+//     per cloud the largest reference norm and a flag for non-finite or huge
+//     norms (such clouds skip the tensor path).
+//  2. Approximate scores (fknn_tc_kernel): a CTA owns 128 queries; warp 0
+//     streams 128-reference tiles into a 2-stage shared-memory ring with
+//     cp.async.bulk, warp 1 issues tcgen05.mma kind::f16 (bf16 x bf16 -> fp32,
+//     M = 128, N = 128, K = 16): dot ~= hi.hi' + hi.lo' + lo.hi' into one of
+//     two TMEM accumulators (128 lanes x 128 columns each), and warps 2-5 (one
+//     per TMEM lane quarter, one thread per query) read the other accumulator
+//     with tcgen05.ld and form s_j = n(r_j) - 2 dot'_j, so SD'_j = n(q) + s_j
+//     approximates SD_j with |SD'_j - SD_j| <= eps(q) = C_K (n(q) + max n(r)).
 //       pass 1: the minimum of s over each group of 32 consecutive columns;
-//               the k-th smallest group minimum U is an upper bound on the
-//               k-th smallest s (k groups -> k distinct columns).
+//               the k-th smallest group minimum U bounds the k-th smallest s
+//               from above (k groups -> k distinct columns).
 //       pass 2: every column with s_j <= U + 2 eps(q) is appended to the
 //               query's candidate list (capacity kCap).
 //     The k nearest by exact SD are all candidates: F_k <= n(q) + U + eps
 //     (k columns have SD' <= n(q) + U), and a needed column has
 //     SD' <= F_k + eps.
 //  3. Exact re-rank (fknn_rerank_kernel): exact fp32 SD of every candidate,
-//     sorted by (SD, index).  A query whose list overflowed, or whose cloud
+//     ranked by (SD, index).  A query whose list overflowed, or whose cloud
 //     was flagged, is scanned exactly over all references instead.
 //
 // Error bound C_K (per unit of n(q) + n(r), K = D padded to 16): the dropped
@@ -40,48 +44,51 @@
 // reference's own rounding add the rest.  C_K = 2 * (2^-13 + 3K 2^-21 +
 // (3D + 16) 2^-24) is about twice the sum of those terms.
 //
-// Work per (query tile, reference tile): 3 * 2 * 128 * 256 * K flops on the
-// tensor pipe; the synchronous loop below (stage tile -> MMA -> epilogue)
-// relies on two resident CTAs per SM to overlap the phases.
+// Every wait on an mbarrier is bounded (kWaitNs of %globaltimer); on expiry
+// the CTA records status 1, the waiting role stops, the rows of the CTA are
+// sent to the exact path, and the TMEM is freed before the CTA exits.
 #include <cuda_bf16.h>
 
 #include <string>
 
 #include "../../include/mpo_b200.h"
-#include "mpo_common.cuh"
 #include "knn_select.cuh"
+#include "mpo_common.cuh"
 
 namespace mpo {
 namespace {
 
-constexpr int kTM = 128;          // queries per CTA (TMEM lanes)
-constexpr int kTN = 256;          // references per tile (TMEM columns)
-constexpr int kKC = 64;           // features per staged K chunk
-constexpr int kThreadsTC = 256;   // 8 warps: 2 per TMEM lane quarter
-constexpr int kCap = 64;          // candidates kept per query
-constexpr int kMaxK = 32;         // largest k served by this path
+constexpr int kTM = 128;         // queries per CTA (TMEM lanes)
+constexpr int kTN = 128;         // references per tile (accumulator columns)
+constexpr int kMaxD = 128;       // widest feature vector of the tensor path
+constexpr int kCap = 64;         // candidates kept per query
+constexpr int kMaxK = 32;        // largest k served by this path
+constexpr int kThreadsTC = 192;  // warp 0 producer, warp 1 MMA, warps 2-5 epilogue
 constexpr unsigned long long kWaitNs = 2000000000ull;
+constexpr float kHuge = 1.15292150e18f;  // 2^60: larger norms go to the exact path
 
-// Shared-memory layout (bytes), K-major core-matrix ("interleaved", no
-// swizzle) layout for both operands: element (row, t) of a 64-feature chunk
-// sits at (row / 8) * kSBO + (t / 8) * 128 + (row % 8) * 16 + (t % 8) * 2.
-constexpr int kSBO = (kKC / 8) * 128;                  // 1024 B per 8-row group
-constexpr int kABytes = kTM * kKC * 2;                 // 16 KB per bf16 part
-constexpr int kBBytes = kTN * kKC * 2;                 // 32 KB per bf16 part
-constexpr int kOffAhi = 0;
-constexpr int kOffAlo = kOffAhi + kABytes;
-constexpr int kOffBhi = kOffAlo + kABytes;
-constexpr int kOffBlo = kOffBhi + kBBytes;
-constexpr int kOffNy = kOffBlo + kBBytes;              // float[kTN]
-constexpr int kOffCount = kOffNy + kTN * 4;            // u32[kTM] (pass 2)
-// Pass 1 merges the two column halves' lists in the (then idle) B region.
-static_assert(2 * kTM * kMaxK * 4 <= 2 * kBBytes, "merge buffer must fit");
-constexpr int kOffMisc = kOffCount + kTM * 4;          // mbarrier (8) + tmem slot (4)
-constexpr int kSmemTC = kOffMisc + 64;
-// 2 CTAs per SM fit (TMEM: 2 x 256 columns = all 512).
-static_assert(2 * kSmemTC <= 227 * 1024, "two CTAs per SM must fit");
+// Operand layout of one 128-row tile and one bf16 part (hi or lo), K-major
+// core matrices without swizzle: element (row, t) sits at
+//   (row / 8) * SBO + (t / 8) * 128 + (row % 8) * 16 + (t % 8) * 2,
+// SBO = Kpad / 8 * 128.  A tile block holds the hi part, then the lo part.
+__host__ __device__ constexpr int kpad_of(int D) { return (D + 15) / 16 * 16; }
+__host__ __device__ constexpr int part_bytes(int Kpad) { return 128 * Kpad * 2; }
 
-// ---- PTX wrappers (tcgen05, mbarrier, proxies) ---------------------------
+// Shared memory: A (2 parts) | 2 stages x (B 2 parts + 128 norms) | barriers.
+struct TcSmem {
+    int part, a_off, b_off, stage_bytes, ny_off, bar_off, total;
+    __host__ __device__ TcSmem(int Kpad) {
+        part = part_bytes(Kpad);
+        a_off = 0;
+        b_off = 2 * part;
+        stage_bytes = 2 * part + kTN * 4;
+        ny_off = 2 * part;  // within a stage
+        bar_off = b_off + 2 * stage_bytes;
+        total = bar_off + 128;
+    }
+};
+
+// ---- PTX wrappers (tcgen05, mbarrier, bulk copies, proxies) -----------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -111,9 +118,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     }
     return true;
 }
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -136,7 +140,7 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
 // Instruction descriptor: kind::f16, A = B = bf16 (K-major), D = f32, M = 128,
-// N = 256.
+// N = kTN.
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTN >> 3) << 17) |
                             ((uint32_t)(kTM >> 4) << 24);
 __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
@@ -187,275 +191,457 @@ __device__ __forceinline__ void split8(const float (&x)[8], uint4& hi, uint4& lo
     lo = make_uint4(l[0] | (l[1] << 16), l[2] | (l[3] << 16), l[4] | (l[5] << 16), l[6] | (l[7] << 16));
 }
 
-// Stage rows [row0, row0 + rows) x features [t0, t0 + kKC) of a (n, D) fp32
-// matrix as hi/lo bf16 in the core-matrix layout; rows >= n and features
-// >= D are zero.
-__device__ __forceinline__ void stage_rows(const float* __restrict__ p, int64_t n, int D,
-                                           int64_t row0, int rows, int t0, unsigned char* hi_base,
-                                           unsigned char* lo_base, int tid, int nthreads) {
-    const int chunks = rows * (kKC / 8);
-    for (int c = tid; c < chunks; c += nthreads) {
-        const int row = c / (kKC / 8);
-        const int kc = c % (kKC / 8);
-        const int64_t gr = row0 + row;
-        float x[8];
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Arrive on bar and add tx bytes that the following bulk copies will complete.
+__device__ __forceinline__ void bulk_expect(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+// Plain (non-multicast) bulk copy global -> own shared memory; completion is
+// signalled as tx bytes on bar.  Addresses and size are multiples of 16.
+__device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+// ---- 1. pack and norms --------------------------------------------------------
+// Thread per (row, 8-feature chunk) of the padded tiles; rows past n and
+// features past D are zero.
+__global__ void fknn_pack_kernel(const float* __restrict__ p, int64_t B, int64_t n, int D, int Kpad,
+                                 int64_t tiles, unsigned char* __restrict__ out) {
+    const int chunks = Kpad / 8;
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t rows = B * tiles * 128;
+    if (e >= rows * chunks) return;
+    const int64_t prow = e / chunks;  // padded row: b * tiles * 128 + tile * 128 + rr
+    const int c = (int)(e % chunks);
+    const int64_t b = prow / (tiles * 128);
+    const int64_t i = prow % (tiles * 128);
+    const int64_t tile = i / 128;
+    const int rr = (int)(i % 128);
+    float x[8];
+    const bool live = i < n;
+    const float* src = p + (b * n + i) * D + c * 8;
+    if (live && (D & 3) == 0 && c * 8 + 8 <= D) {
+        const float4 u = reinterpret_cast<const float4*>(src)[0];
+        const float4 v = reinterpret_cast<const float4*>(src)[1];
+        x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
+        x[4] = v.x; x[5] = v.y; x[6] = v.z; x[7] = v.w;
+    } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int t = t0 + kc * 8 + i;
-            x[i] = (gr < n && t < D) ? p[gr * D + t] : 0.f;
+        for (int t = 0; t < 8; ++t) x[t] = (live && c * 8 + t < D) ? src[t] : 0.f;
+    }
+    uint4 hi, lo;
+    split8(x, hi, lo);
+    const int part = part_bytes(Kpad);
+    unsigned char* blk = out + (size_t)(b * tiles + tile) * 2 * part;
+    const int off = (rr >> 3) * (Kpad / 8 * 128) + c * 128 + (rr & 7) * 16;
+    *reinterpret_cast<uint4*>(blk + off) = hi;
+    *reinterpret_cast<uint4*>(blk + part + off) = lo;
+}
+
+// Thread per point: nq[b*M + i]; nr padded per cloud to tiles*128 entries
+// (+inf past N); nmax = largest finite reference norm per cloud (one atomic
+// per warp), bad = a norm that is not finite or above kHuge.
+__global__ void fknn_norms_kernel(const float* __restrict__ q, const float* __restrict__ r,
+                                  int64_t B, int64_t M, int64_t N, int64_t ntiles, int D,
+                                  float* __restrict__ nq, float* __restrict__ nr,
+                                  unsigned* __restrict__ nmax, int* __restrict__ bad) {
+    const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t npad = ntiles * 128;
+    const int64_t total = B * (M + npad);
+    const bool live = w < total;
+    const bool is_q = w < B * M;
+    const int64_t row = is_q ? w : w - B * M;
+    const int64_t b = live ? (is_q ? row / M : row / npad) : -1;
+    const int64_t i = is_q ? row % M : row % npad;
+    bool ref_ok = false;
+    float s = 0.f;
+    if (live) {
+        if (!is_q && i >= N) {
+            nr[row] = INFINITY;
+        } else {
+            const float* p = is_q ? q + row * D : r + (b * N + i) * D;
+            if ((D & 3) == 0) {
+                const float4* p4 = reinterpret_cast<const float4*>(p);
+                for (int t = 0; t < D / 4; ++t) {
+                    const float4 v = p4[t];
+                    s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+                    s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+                    s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+                    s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+                }
+            } else {
+                for (int t = 0; t < D; ++t) s = __fadd_rn(s, __fmul_rn(p[t], p[t]));
+            }
+            const bool ok = isfinite(s) && s <= kHuge;
+            if (!ok) bad[b] = 1;
+            if (is_q) {
+                nq[row] = s;
+            } else {
+                nr[row] = s;
+                ref_ok = ok;
+            }
         }
-        uint4 h, l;
-        split8(x, h, l);
-        const int off = (row >> 3) * kSBO + kc * 128 + (row & 7) * 16;
-        *reinterpret_cast<uint4*>(hi_base + off) = h;
-        *reinterpret_cast<uint4*>(lo_base + off) = l;
+    }
+    const unsigned bits = ref_ok ? __float_as_uint(s) : 0u;
+    const int64_t b0 = __shfl_sync(FULL_MASK, b, 0);
+    if (__all_sync(FULL_MASK, b == b0)) {
+        const unsigned mx = __reduce_max_sync(FULL_MASK, bits);
+        if ((threadIdx.x & 31) == 0 && mx) atomicMax(&nmax[b0], mx);
+    } else if (bits) {
+        atomicMax(&nmax[b], bits);
     }
 }
 
 __device__ __forceinline__ float eps_coef(int D) {
-    const int K = (D + 15) / 16 * 16;
+    const int K = kpad_of(D);
     return 2.f * (1.220703125e-4f /* 2^-13 */ + 3.f * (float)K * 4.76837158203125e-7f /* 2^-21 */ +
                   (3.f * (float)D + 16.f) * 5.9604644775390625e-8f /* 2^-24 */);
 }
 
-// ---- 1. norms ---------------------------------------------------------------
-// One warp per point; nmax = largest reference norm (bit order of non-negative
-// floats), bad = some norm is not finite or above 2^100 (scores could lose
-// all precision), which sends the cloud to the exact path.
-__global__ void fknn_norms_kernel(const float* __restrict__ q, const float* __restrict__ r,
-                                  int64_t B, int64_t M, int64_t N, int D, float* __restrict__ nq,
-                                  float* __restrict__ nr, unsigned* __restrict__ nmax,
-                                  int* __restrict__ bad) {
-    const int lane = threadIdx.x & 31;
-    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int64_t total = B * (M + N);
-    if (w >= total) return;
-    const bool is_q = w < B * M;
-    const int64_t row = is_q ? w : w - B * M;
-    const float* p = (is_q ? q : r) + row * D;
-    float s = 0.f;
-    for (int t = lane; t < D; t += 32) s = __fadd_rn(s, __fmul_rn(p[t], p[t]));
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(FULL_MASK, s, o));
-    if (lane != 0) return;
-    const int64_t b = is_q ? row / M : row / N;
-    const bool ok = isfinite(s) && s <= 1.2676506e30f;  // 2^100
-    if (!ok) bad[b] = 1;
-    if (is_q) {
-        nq[row] = s;
-    } else {
-        nr[row] = s;
-        if (ok) atomicMax(&nmax[b], __float_as_uint(s));
-    }
-}
-
 // ---- 2. approximate scores on the tensor cores ------------------------------
-// KCAP >= k: capacity of the pass-1 list of group minima, right-aligned so
-// that the k-th smallest sits in the static slot KCAP - 1 (leading slots hold
-// -inf sentinels).
+// Barriers: full[s] (producer expect_tx + bulk-copy bytes), empty[s] (MMA
+// commit: operands of stage s read, plus the 4 epilogue warps: norms of stage
+// s read), accf[a] (MMA commit: accumulator a written), acce[a] (4 epilogue
+// warps: accumulator a read).  Phase parity of round n = n & 1;
+// "free" barriers are waited with the opposite parity first.
 template <int PASS, int KCAP>
 __global__ void __launch_bounds__(kThreadsTC, 1)
-fknn_tc_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t M, int64_t N,
-               int D, int k, const float* __restrict__ nq, const float* __restrict__ nr,
+fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __restrict__ rpack,
+               int64_t M, int64_t N, int64_t mtiles, int64_t ntiles, int D, int k,
+               const float* __restrict__ nq, const float* __restrict__ nr,
                const unsigned* __restrict__ nmax, const int* __restrict__ bad,
                float* __restrict__ ubound, unsigned* __restrict__ counts, uint2* __restrict__ cand,
                int* __restrict__ status) {
-    extern __shared__ __align__(1024) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int b = blockIdx.y;
-    const int64_t m0 = (int64_t)blockIdx.x * kTM;
+    const int64_t mt = blockIdx.x;
     if (bad[b]) return;  // uniform: the cloud goes to the exact path
+    const int Kpad = kpad_of(D);
+    const TcSmem L(Kpad);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar = sbase + L.bar_off;
+    // barrier addresses: full 0,1 | empty 2,3 | accf 4,5 | acce 6,7 | afull 8
+    auto B_ = [&](int i) { return bar + 8u * (uint32_t)i; };
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.bar_off + 80);
+    int* s_abort = reinterpret_cast<int*>(smem + L.bar_off + 84);
 
-    float* s_ny = reinterpret_cast<float*>(smem + kOffNy);
-    float* s_list = reinterpret_cast<float*>(smem + kOffBhi);  // pass 1, after the loop
-    unsigned* s_count = reinterpret_cast<unsigned*>(smem + kOffCount);
-    const uint32_t bar = smem_u32(smem + kOffMisc);
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + kOffMisc + 8);
-    const float* qb = q + (int64_t)b * M * D;
-    const float* rb = r + (int64_t)b * N * D;
-
-    if (warp == 0) tmem_alloc(smem_u32(s_tmem), kTN);
+    if (warp == 0) tmem_alloc(smem_u32(s_tmem), 2 * kTN);
     if (tid == 0) {
-        mbar_init(bar, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(B_(0 + i), 1);
+            mbar_init(B_(2 + i), 5);
+            mbar_init(B_(4 + i), 1);
+            mbar_init(B_(6 + i), 4);
+        }
+        mbar_init(B_(8), 1);
+        *s_abort = 0;
         mbar_fence_init();
     }
-    if (PASS == 2 && tid < kTM) s_count[tid] = 0u;
-
-    // This thread's query row and column half.
-    const int quarter = warp & 3, half = warp >> 2;
-    const int row = quarter * 32 + lane;
-    const int64_t gq = m0 + row;
-    const bool qvalid = gq < M;
-    const float nqi = qvalid ? nq[(int64_t)b * M + gq] : 0.f;
-    const float eps = eps_coef(D) * (nqi + __uint_as_float(nmax[b]));
-    float thr = -INFINITY;  // pass 2: s_j <= thr makes j a candidate
-    if (PASS == 2 && qvalid) thr = ubound[(int64_t)b * M + gq] + 2.f * eps;
-    // Pass 1: the k smallest group minima of this thread's columns, sorted.
-    float lst[KCAP];
-#pragma unroll
-    for (int i = 0; i < KCAP; ++i) lst[i] = i < KCAP - k ? -INFINITY : INFINITY;
-
-    const int nkc = (D + kKC - 1) / kKC;
-    const bool a_resident = nkc == 1;
-    if (a_resident)
-        stage_rows(qb, M, D, m0, kTM, 0, smem + kOffAhi, smem + kOffAlo, tid, kThreadsTC);
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-    uint32_t phase = 0;
-    bool ok = true;
+    const uint32_t sbo = (uint32_t)(Kpad / 8 * 128);
+    const uint32_t a_bytes = (uint32_t)(2 * L.part);
 
-    for (int64_t n0 = 0; n0 < N && ok; n0 += kTN) {
-        for (int kc = 0; kc < nkc && ok; ++kc) {
-            if (!a_resident)
-                stage_rows(qb, M, D, m0, kTM, kc * kKC, smem + kOffAhi, smem + kOffAlo, tid,
-                           kThreadsTC);
-            stage_rows(rb, N, D, n0, kTN, kc * kKC, smem + kOffBhi, smem + kOffBlo, tid,
-                       kThreadsTC);
-            if (kc == 0) {
-                for (int j = tid; j < kTN; j += kThreadsTC)
-                    s_ny[j] = (n0 + j < N) ? nr[(int64_t)b * N + n0 + j] : INFINITY;
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const unsigned char* asrc = qpack + (size_t)(b * mtiles + mt) * a_bytes;
+            bulk_expect(B_(8), a_bytes);
+            bulk_copy(sbase + L.a_off, asrc, a_bytes, B_(8));
+            int64_t issued = 0;
+            for (int64_t t = 0; t < ntiles; ++t) {
+                const int st = (int)(t & 1);
+                const uint32_t n = (uint32_t)(t >> 1);
+                if (!mbar_wait(B_(2 + st), (n & 1) ^ 1) || *(volatile int*)s_abort) {
+                    atomicExch(status, 1);
+                    *(volatile int*)s_abort = 1;
+                    break;
+                }
+                const uint32_t dst = sbase + L.b_off + (uint32_t)(st * L.stage_bytes);
+                bulk_expect(B_(0 + st), a_bytes + kTN * 4);
+                bulk_copy(dst, rpack + (size_t)(b * ntiles + t) * a_bytes, a_bytes, B_(0 + st));
+                bulk_copy(dst + L.ny_off, nr + (size_t)(b * ntiles + t) * kTN, kTN * 4, B_(0 + st));
+                ++issued;
             }
-            fence_proxy_async_smem();
-            __syncthreads();
-            if (tid == 0) {
+            // Copies still in flight (only after an abort) land before exit.
+            mbar_wait(B_(8), 0);
+            for (int64_t t = max64(issued - 2, 0); t < issued; ++t)
+                mbar_wait(B_(0 + (int)(t & 1)), (uint32_t)((t >> 1) & 1));
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            bool ok = mbar_wait(B_(8), 0);
+            for (int64_t t = 0; t < ntiles && ok; ++t) {
+                const int st = (int)(t & 1), ac = (int)(t & 1);
+                const uint32_t n = (uint32_t)(t >> 1);
+                ok = mbar_wait(B_(0 + st), n & 1) && mbar_wait(B_(6 + ac), (n & 1) ^ 1) &&
+                     !*(volatile int*)s_abort;
+                if (!ok) break;
                 tc_fence_after();
-                const int ksteps = min(kKC, ((D - kc * kKC) + 15) / 16 * 16) / 16;
-                for (int s = 0; s < ksteps; ++s) {
-                    const uint32_t koff = (uint32_t)s * 256u;
-                    const uint64_t ahi = smem_desc(smem_u32(smem + kOffAhi) + koff, 128, kSBO);
-                    const uint64_t alo = smem_desc(smem_u32(smem + kOffAlo) + koff, 128, kSBO);
-                    const uint64_t bhi = smem_desc(smem_u32(smem + kOffBhi) + koff, 128, kSBO);
-                    const uint64_t blo = smem_desc(smem_u32(smem + kOffBlo) + koff, 128, kSBO);
-                    const uint32_t first = (kc == 0 && s == 0) ? 0u : 1u;
-                    mma_bf16(tmem, ahi, bhi, first);
-                    mma_bf16(tmem, ahi, blo, 1u);
-                    mma_bf16(tmem, alo, bhi, 1u);
+                const uint32_t d = tmem + (uint32_t)(ac * kTN);
+                const uint32_t a0 = sbase + L.a_off;
+                const uint32_t b0 = sbase + L.b_off + (uint32_t)(st * L.stage_bytes);
+                const uint32_t part = (uint32_t)L.part;
+                for (int s = 0; s < Kpad / 16; ++s) {
+                    const uint32_t ko = (uint32_t)s * 256u;
+                    const uint64_t ahi = smem_desc(a0 + ko, 128, sbo);
+                    const uint64_t alo = smem_desc(a0 + part + ko, 128, sbo);
+                    const uint64_t bhi = smem_desc(b0 + ko, 128, sbo);
+                    const uint64_t blo = smem_desc(b0 + part + ko, 128, sbo);
+                    mma_bf16(d, ahi, bhi, s == 0 ? 0u : 1u);
+                    mma_bf16(d, ahi, blo, 1u);
+                    mma_bf16(d, alo, bhi, 1u);
                 }
-                mma_commit(bar);
+                mma_commit(B_(2 + st));  // stage st may be refilled
+                mma_commit(B_(4 + ac));  // accumulator ac is ready
             }
-            const bool done = mbar_wait(bar, phase);
-            ok = __syncthreads_and(done) != 0;  // every thread takes the same path
-            if (!ok && tid == 0) atomicExch(status, 1);
-            phase ^= 1u;
-            tc_fence_after();
-        }
-        if (!ok) break;
-        // Epilogue: this thread's row, columns [half * 128, half * 128 + 128).
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-            const int col0 = half * 128 + c * 32;
-            float v[32];
-            tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0, v);
-            if (PASS == 1) {
-                float g = INFINITY;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) g = fminf(g, fmaf(-2.f, v[i], s_ny[col0 + i]));
-                if (g < lst[KCAP - 1]) {
-                    // Insert g, dropping the largest; sentinels never move.
-#pragma unroll
-                    for (int i = KCAP - 1; i >= 1; --i) {
-                        const float lo = lst[i - 1];
-                        lst[i] = (g < lo) ? lo : ((g < lst[i]) ? g : lst[i]);
-                    }
-                    lst[0] = fminf(lst[0], g);
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float sj = fmaf(-2.f, v[i], s_ny[col0 + i]);
-                    if (sj <= thr) {
-                        const unsigned slot = atomicAdd(&s_count[row], 1u);
-                        if (slot < (unsigned)kCap && qvalid)
-                            cand[((int64_t)b * M + gq) * kCap + slot] =
-                                make_uint2((unsigned)(n0 + col0 + i), __float_as_uint(sj));
-                    }
-                }
+            if (!ok) {
+                atomicExch(status, 1);
+                *(volatile int*)s_abort = 1;
             }
-        }
-        tc_fence_before();
-        __syncthreads();  // TMEM and the B tile are free again
-    }
-
-    if (PASS == 1) {
-        // k-th smallest group minimum over both halves of the row: each half
-        // writes its k entries, half 0 merges.
-        __syncthreads();  // the B region is idle now
-#pragma unroll
-        for (int i = 0; i < KCAP; ++i)
-            if (i >= KCAP - k) s_list[(half * kTM + row) * kMaxK + (i - (KCAP - k))] = lst[i];
-        __syncthreads();
-        if (half == 0 && qvalid) {
-            const float* la = s_list + row * kMaxK;
-            const float* lb = s_list + (kTM + row) * kMaxK;
-            int ia = 0, ib = 0;
-            float kth = INFINITY;
-            for (int t = 0; t < k; ++t) {
-                const float a = la[ia], bb = lb[ib];
-                if (a <= bb) {
-                    kth = a;
-                    ++ia;
-                } else {
-                    kth = bb;
-                    ++ib;
-                }
-            }
-            ubound[(int64_t)b * M + gq] = ok ? kth : INFINITY;
         }
     } else {
-        __syncthreads();
-        if (half == 0 && qvalid) counts[(int64_t)b * M + gq] = ok ? s_count[row] : 0xffffffffu;
+        // ---------------- epilogue: one thread per query ----------------
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const int64_t gq = mt * kTM + row;
+        const bool qvalid = gq < M;
+        const float nqi = qvalid ? nq[(int64_t)b * M + gq] : 0.f;
+        const float eps = eps_coef(D) * (nqi + __uint_as_float(nmax[b]));
+        float thr = -INFINITY;  // pass 2: s_j <= thr makes j a candidate
+        if (PASS == 2 && qvalid) thr = ubound[(int64_t)b * M + gq] + 2.f * eps;
+        float lst[KCAP];  // pass 1: k smallest group minima, right-aligned
+#pragma unroll
+        for (int i = 0; i < KCAP; ++i) lst[i] = i < KCAP - k ? -INFINITY : INFINITY;
+        unsigned found = 0;
+        bool ok = true;
+        for (int64_t t = 0; t < ntiles; ++t) {
+            const int st = (int)(t & 1), ac = (int)(t & 1);
+            const uint32_t n = (uint32_t)(t >> 1);
+            const bool got = mbar_wait(B_(4 + ac), n & 1);
+            ok = __all_sync(FULL_MASK, got) && !*(volatile int*)s_abort;
+            if (!ok) break;
+            tc_fence_after();
+            const float* s_ny = reinterpret_cast<const float*>(smem + L.b_off + st * L.stage_bytes +
+                                                               L.ny_off);
+            // The norms of stage st stay until this warp arrives on empty[st].
+#pragma unroll 1
+            for (int c = 0; c < kTN / 32; ++c) {
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(ac * kTN + c * 32),
+                          v);
+                const float4* ny4 = reinterpret_cast<const float4*>(s_ny + c * 32);
+                if (PASS == 1) {
+                    float g = INFINITY;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 y = ny4[i];
+                        g = fminf(g, fmaf(-2.f, v[4 * i + 0], y.x));
+                        g = fminf(g, fmaf(-2.f, v[4 * i + 1], y.y));
+                        g = fminf(g, fmaf(-2.f, v[4 * i + 2], y.z));
+                        g = fminf(g, fmaf(-2.f, v[4 * i + 3], y.w));
+                    }
+                    if (g < lst[KCAP - 1]) {
+#pragma unroll
+                        for (int i = KCAP - 1; i >= 1; --i) {
+                            const float lo = lst[i - 1];
+                            lst[i] = (g < lo) ? lo : ((g < lst[i]) ? g : lst[i]);
+                        }
+                        lst[0] = fminf(lst[0], g);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 y = ny4[i];
+                        const float sv[4] = {fmaf(-2.f, v[4 * i + 0], y.x),
+                                             fmaf(-2.f, v[4 * i + 1], y.y),
+                                             fmaf(-2.f, v[4 * i + 2], y.z),
+                                             fmaf(-2.f, v[4 * i + 3], y.w)};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            if (sv[u] <= thr) {
+                                if (found < (unsigned)kCap)
+                                    cand[((int64_t)b * M + gq) * kCap + found] = make_uint2(
+                                        (unsigned)(t * kTN + c * 32 + 4 * i + u), __float_as_uint(sv[u]));
+                                ++found;
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(B_(6 + ac));  // accumulator read
+                mbar_arrive(B_(2 + st));  // norms of the stage read
+            }
+        }
+        if (!ok) {
+            if (lane == 0) atomicExch(status, 1);
+            *(volatile int*)s_abort = 1;
+        }
+        if (qvalid) {
+            if (PASS == 1) ubound[(int64_t)b * M + gq] = ok ? lst[KCAP - 1] : INFINITY;
+            else counts[(int64_t)b * M + gq] = ok ? found : 0xffffffffu;
+        }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTN);
+        tmem_dealloc(tmem, 2 * kTN);
     }
 }
 
 // ---- 3. exact re-rank --------------------------------------------------------
-// Thread per query: the exact sequential-fp32 SD of every candidate (or of
-// every reference when the candidate list overflowed or the cloud was
-// flagged), selected in (SD, index) order with non-finite SD dropped.
+// Warp per query.  Normal case: lane l takes candidates l and l + 32, computes
+// their exact sequential-fp32 SD (non-finite SD are dropped), and the rank of
+// each candidate in (SD, index) order over the whole list decides its output
+// slot.  Overflowed lists and flagged clouds: the lanes scan every reference
+// (j = lane mod 32) into per-lane sorted lists, merged by k rounds of warp
+// minimum.
+// Exact sequential SD of query row qs (shared memory) and reference row rp,
+// reading the reference 32 features at a time (float4 when aligned) so that
+// each lane keeps eight loads in flight.
+__device__ __forceinline__ float sqd_staged(const float* __restrict__ qs,
+                                            const float* __restrict__ rp, int D) {
+    float s = 0.f;
+    if ((D & 3) == 0) {
+        const float4* r4 = reinterpret_cast<const float4*>(rp);
+        for (int t0 = 0; t0 < D; t0 += 32) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                v[u] = (t0 + 4 * u < D) ? r4[t0 / 4 + u] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int t = t0 + 4 * u;
+                if (t < D) {
+                    float d = __fsub_rn(qs[t], v[u].x);
+                    s = (t == 0) ? __fmul_rn(d, d) : __fadd_rn(s, __fmul_rn(d, d));
+                    d = __fsub_rn(qs[t + 1], v[u].y);
+                    s = __fadd_rn(s, __fmul_rn(d, d));
+                    d = __fsub_rn(qs[t + 2], v[u].z);
+                    s = __fadd_rn(s, __fmul_rn(d, d));
+                    d = __fsub_rn(qs[t + 3], v[u].w);
+                    s = __fadd_rn(s, __fmul_rn(d, d));
+                }
+            }
+        }
+        return s;
+    }
+    return sqd_seq(qs, rp, D);
+}
+
 template <int KCAP>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
 fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t B, int64_t M,
                    int64_t N, int D, int k, const int* __restrict__ bad,
                    const unsigned* __restrict__ counts, const uint2* __restrict__ cand,
                    float* __restrict__ dist, int64_t* __restrict__ idx64,
                    float* __restrict__ sqdist) {
-    const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (row >= B * M) return;
+    static_assert(kCap == 64, "two candidates per lane");
+    extern __shared__ float s_q[];  // [8 warps][D]
+    const int lane = threadIdx.x & 31;
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (row >= B * M) return;  // warp-uniform
     const int64_t b = row / M;
-    const float* qp = q + row * D;
     const float* rb = r + b * N * D;
+    float* qp = s_q + (threadIdx.x >> 5) * D;
+    for (int t = lane; t < D; t += 32) qp[t] = q[row * D + t];
+    __syncwarp();
+    const unsigned cnt = bad[b] ? 0xffffffffu : counts[row];
+    const int64_t o = row * k;
+    if (cnt <= (unsigned)kCap) {
+        float sd[2];
+        uint32_t jj[2];
+        bool ok[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const unsigned c = (unsigned)(lane + 32 * h);
+            ok[h] = c < cnt;
+            jj[h] = ok[h] ? cand[row * kCap + c].x : 0u;
+            sd[h] = ok[h] ? sqd_staged(qp, rb + (int64_t)jj[h] * D, D) : INFINITY;
+            ok[h] = ok[h] && isfinite(sd[h]);
+        }
+        int rank[2] = {0, 0};
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+            const unsigned live = __ballot_sync(FULL_MASK, ok[h2]);
+            for (unsigned m = live; m; m &= m - 1) {
+                const int src = __ffs(m) - 1;
+                const float e = __shfl_sync(FULL_MASK, sd[h2], src);
+                const uint32_t ej = __shfl_sync(FULL_MASK, jj[h2], src);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    rank[h] += (ok[h] && before<kDropNonFinite>(e, ej, sd[h], jj[h])) ? 1 : 0;
+            }
+        }
+        const int total = __popc(__ballot_sync(FULL_MASK, ok[0])) +
+                          __popc(__ballot_sync(FULL_MASK, ok[1]));
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (ok[h] && rank[h] < k) {
+                dist[o + rank[h]] = sqrtf(sd[h]);
+                if (sqdist) sqdist[o + rank[h]] = sd[h];
+                idx64[o + rank[h]] = (int64_t)jj[h];
+            }
+        }
+        for (int t = total + lane; t < k; t += 32) {
+            dist[o + t] = INFINITY;
+            if (sqdist) sqdist[o + t] = INFINITY;
+            idx64[o + t] = -1;
+        }
+        return;
+    }
     TopK<KCAP, kDropNonFinite> top;
     top.init(k);
-    const unsigned cnt = bad[b] ? 0xffffffffu : counts[row];
-    if (cnt > (unsigned)kCap) {
-        for (int64_t j = 0; j < N; ++j) top.offer(sqd_seq(qp, rb + j * D, D), (uint32_t)j);
-    } else {
-        for (unsigned c = 0; c < cnt; ++c) {
-            const uint32_t j = cand[row * kCap + c].x;
-            top.offer(sqd_seq(qp, rb + (int64_t)j * D, D), j);
-        }
-    }
-    const int64_t o = row * k;
+    for (int64_t j = lane; j < N; j += 32) top.offer(sqd_staged(qp, rb + j * D, D), (uint32_t)j);
+    int used = 0;  // entries of this lane's list already emitted
+    for (int t = 0; t < k; ++t) {
+        float hd = INFINITY;
+        uint32_t hj = kNoIndex;
 #pragma unroll
-    for (int s = 0; s < KCAP; ++s) {
-        const int l = s - top.base;
-        if (l >= 0) {
-            const bool filled = l < top.cnt;
-            const float d = filled ? top.d[s] : INFINITY;
-            dist[o + l] = sqrtf(d);
-            if (sqdist) sqdist[o + l] = d;
-            idx64[o + l] = filled ? (int64_t)top.i[s] : -1;
+        for (int s2 = 0; s2 < KCAP; ++s2) {
+            if (s2 == top.base + used && used < top.cnt) {
+                hd = top.d[s2];
+                hj = top.i[s2];
+            }
+        }
+        float bd = hd;
+        uint32_t bj = hj;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            const float od = __shfl_xor_sync(FULL_MASK, bd, off);
+            const uint32_t oj = __shfl_xor_sync(FULL_MASK, bj, off);
+            if (oj != kNoIndex && (bj == kNoIndex || before<kDropNonFinite>(od, oj, bd, bj))) {
+                bd = od;
+                bj = oj;
+            }
+        }
+        if (hj != kNoIndex && hj == bj) ++used;
+        if (lane == 0) {
+            const bool filled = bj != kNoIndex;
+            dist[o + t] = filled ? sqrtf(bd) : INFINITY;
+            if (sqdist) sqdist[o + t] = filled ? bd : INFINITY;
+            idx64[o + t] = filled ? (int64_t)bj : -1;
         }
     }
 }
 
 struct Scratch {
+    unsigned char* qpack;
+    unsigned char* rpack;
     float* nq;
     float* nr;
     float* ubound;
@@ -469,7 +655,7 @@ struct Scratch {
 
 inline size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
-inline Scratch carve(void* base, int64_t B, int64_t M, int64_t N) {
+inline Scratch carve(void* base, int64_t B, int64_t M, int64_t N, int64_t D) {
     Scratch s{};
     size_t off = 0;
     auto take = [&](size_t n) {
@@ -477,8 +663,12 @@ inline Scratch carve(void* base, int64_t B, int64_t M, int64_t N) {
         off += align256(n);
         return base ? static_cast<unsigned char*>(base) + at : nullptr;
     };
+    const int64_t mt = ceil_div(M, kTM), nt = ceil_div(N, kTN);
+    const size_t tile = 2 * (size_t)part_bytes(kpad_of((int)D));
+    s.qpack = take(tile * B * mt);
+    s.rpack = take(tile * B * nt);
     s.nq = reinterpret_cast<float*>(take(sizeof(float) * B * M));
-    s.nr = reinterpret_cast<float*>(take(sizeof(float) * B * N));
+    s.nr = reinterpret_cast<float*>(take(sizeof(float) * B * nt * kTN));
     s.ubound = reinterpret_cast<float*>(take(sizeof(float) * B * M));
     s.counts = reinterpret_cast<unsigned*>(take(sizeof(unsigned) * B * M));
     s.cand = reinterpret_cast<uint2*>(take(sizeof(uint2) * B * M * kCap));
@@ -497,49 +687,61 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
     if (cudaMemsetAsync(w.nmax, 0, sizeof(unsigned) * B + sizeof(int) * B + sizeof(int), s) !=
         cudaSuccess)
         return fail(kCudaError, "knn: scratch reset failed");
-    const int64_t warps = B * (M + N);
-    fknn_norms_kernel<<<(unsigned)ceil_div(warps * 32, 256), 256, 0, s>>>(
-        query, ref, B, M, N, D, w.nq, w.nr, w.nmax, w.bad);
-    int st = check_launch("fknn_norms_kernel");
+    const int Kpad = kpad_of(D);
+    const int64_t mt = ceil_div(M, kTM), nt = ceil_div(N, kTN);
+    const int64_t qchunks = B * mt * 128 * (Kpad / 8), rchunks = B * nt * 128 * (Kpad / 8);
+    fknn_pack_kernel<<<(unsigned)ceil_div(qchunks, 256), 256, 0, s>>>(query, B, M, D, Kpad, mt,
+                                                                      w.qpack);
+    int st = check_launch("fknn_pack_kernel");
     if (st) return st;
+    fknn_pack_kernel<<<(unsigned)ceil_div(rchunks, 256), 256, 0, s>>>(ref, B, N, D, Kpad, nt,
+                                                                      w.rpack);
+    st = check_launch("fknn_pack_kernel");
+    if (st) return st;
+    fknn_norms_kernel<<<(unsigned)ceil_div(B * (M + nt * kTN), 256), 256, 0, s>>>(
+        query, ref, B, M, N, nt, D, w.nq, w.nr, w.nmax, w.bad);
+    st = check_launch("fknn_norms_kernel");
+    if (st) return st;
+    const TcSmem L(Kpad);
     auto k1 = fknn_tc_kernel<1, KCAP>;
     auto k2 = fknn_tc_kernel<2, KCAP>;
-    if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTC) !=
+    if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
             cudaSuccess ||
-        cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTC) !=
+        cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
             cudaSuccess)
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");
-    dim3 grid((unsigned)ceil_div(M, kTM), (unsigned)B);
-    k1<<<grid, kThreadsTC, kSmemTC, s>>>(query, ref, M, N, D, k, w.nq, w.nr, w.nmax, w.bad,
-                                         w.ubound, w.counts, w.cand, w.status);
+    dim3 grid((unsigned)mt, (unsigned)B);
+    k1<<<grid, kThreadsTC, L.total, s>>>(w.qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
+                                         w.bad, w.ubound, w.counts, w.cand, w.status);
     st = check_launch("fknn_tc_kernel<1>");
     if (st) return st;
-    k2<<<grid, kThreadsTC, kSmemTC, s>>>(query, ref, M, N, D, k, w.nq, w.nr, w.nmax, w.bad,
-                                         w.ubound, w.counts, w.cand, w.status);
+    k2<<<grid, kThreadsTC, L.total, s>>>(w.qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
+                                         w.bad, w.ubound, w.counts, w.cand, w.status);
     st = check_launch("fknn_tc_kernel<2>");
     if (st) return st;
-    fknn_rerank_kernel<KCAP><<<(unsigned)ceil_div(B * M, 128), 128, 0, s>>>(
+    const size_t rsmem = (size_t)8 * D * sizeof(float);
+    fknn_rerank_kernel<KCAP><<<(unsigned)ceil_div(B * M * 32, 256), 256, rsmem, s>>>(
         query, ref, B, M, N, D, k, w.bad, w.counts, w.cand, dist, idx, sqdist);
     return check_launch("fknn_rerank_kernel");
 }
 
 }  // namespace
 
-// The tensor path serves D != 3 with 16 <= D <= 1024, k <= 32 and reference
+// The tensor path serves D != 3 with 16 <= D <= 128, k <= 32 and reference
 // clouds of at least 2048 points (smaller problems are cheap exactly).
 bool fknn_tc_eligible(int64_t M, int64_t N, int64_t D, int64_t k) {
-    return D != 3 && D >= 16 && D <= 1024 && k >= 1 && k <= kMaxK && N >= 2048 && M >= 1 &&
+    return D != 3 && D >= 16 && D <= kMaxD && k >= 1 && k <= kMaxK && N >= 2048 && M >= 1 &&
            N <= 0x7fffffffLL;
 }
 
-size_t fknn_tc_workspace_bytes(int64_t B, int64_t M, int64_t N) {
-    return carve(nullptr, B, M, N).bytes;
+size_t fknn_tc_workspace_bytes(int64_t B, int64_t M, int64_t N, int64_t D) {
+    return carve(nullptr, B, M, N, D).bytes;
 }
 
 int fknn_tc_run(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int64_t D,
                 int64_t k, float* dist, int64_t* idx, float* sqdist, void* workspace,
                 size_t workspace_bytes, cudaStream_t s) {
-    const Scratch w = carve(workspace, B, M, N);
+    const Scratch w = carve(workspace, B, M, N, D);
     if (workspace == nullptr || workspace_bytes < w.bytes)
         return fail(kWorkspaceTooSmall,
                     "knn: workspace must hold " + std::to_string(w.bytes) + " bytes");

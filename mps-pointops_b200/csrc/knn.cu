@@ -543,7 +543,7 @@ extern "C" {
 
 size_t mpo_knn_workspace_bytes(int64_t B, int64_t M, int64_t N, int64_t D, int64_t k) {
     if (B <= 0 || M <= 0 || !mpo::fknn_tc_eligible(M, N, D, k)) return 0;
-    return mpo::fknn_tc_workspace_bytes(B, M, N);
+    return mpo::fknn_tc_workspace_bytes(B, M, N, D);
 }
 
 int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int64_t D,

@@ -37,7 +37,7 @@ int sm_count(int device = -1);
 
 // Tensor-core feature kNN (feature_knn_tc.cu).
 bool fknn_tc_eligible(int64_t M, int64_t N, int64_t D, int64_t k);
-size_t fknn_tc_workspace_bytes(int64_t B, int64_t M, int64_t N);
+size_t fknn_tc_workspace_bytes(int64_t B, int64_t M, int64_t N, int64_t D);
 int fknn_tc_run(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int64_t D,
                 int64_t k, float* dist, int64_t* idx, float* sqdist, void* workspace,
                 size_t workspace_bytes, cudaStream_t s);
