@@ -460,22 +460,31 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                         lst[0] = fminf(lst[0], g);
                     }
                 } else {
+                    // Candidate bit mask of the 32 columns (no divergence),
+                    // then one store per set bit.
+                    float sv[32];
+                    unsigned hits = 0u;
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float4 y = ny4[i];
-                        const float sv[4] = {fmaf(-2.f, v[4 * i + 0], y.x),
-                                             fmaf(-2.f, v[4 * i + 1], y.y),
-                                             fmaf(-2.f, v[4 * i + 2], y.z),
-                                             fmaf(-2.f, v[4 * i + 3], y.w)};
+                        sv[4 * i + 0] = fmaf(-2.f, v[4 * i + 0], y.x);
+                        sv[4 * i + 1] = fmaf(-2.f, v[4 * i + 1], y.y);
+                        sv[4 * i + 2] = fmaf(-2.f, v[4 * i + 2], y.z);
+                        sv[4 * i + 3] = fmaf(-2.f, v[4 * i + 3], y.w);
+                    }
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            if (sv[u] <= thr) {
-                                if (found < (unsigned)kCap)
-                                    cand[((int64_t)b * M + gq) * kCap + found] = make_uint2(
-                                        (unsigned)(t * kTN + c * 32 + 4 * i + u), __float_as_uint(sv[u]));
-                                ++found;
-                            }
+                    for (int i = 0; i < 32; ++i) hits |= (sv[i] <= thr ? 1u : 0u) << i;
+                    while (hits) {
+                        const int i = __ffs(hits) - 1;
+                        hits &= hits - 1;
+                        if (found < (unsigned)kCap) {
+                            float si = sv[0];
+#pragma unroll
+                            for (int u = 1; u < 32; ++u) si = (u == i) ? sv[u] : si;
+                            cand[((int64_t)b * M + gq) * kCap + found] =
+                                make_uint2((unsigned)(t * kTN + c * 32 + i), __float_as_uint(si));
                         }
+                        ++found;
                     }
                 }
             }
@@ -511,99 +520,156 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
 // (j = lane mod 32) into per-lane sorted lists, merged by k rounds of warp
 // minimum.
 // Exact sequential SD of query row qs (shared memory) and reference row rp,
-// reading the reference 32 features at a time (float4 when aligned) so that
-// each lane keeps eight loads in flight.
+// reading the reference 32 features at a time (8 float4 loads in flight per
+// lane when rows are 16-byte aligned).
 __device__ __forceinline__ float sqd_staged(const float* __restrict__ qs,
                                             const float* __restrict__ rp, int D) {
+    if ((D & 3) != 0) return sqd_seq(qs, rp, D);
+    const float4* r4 = reinterpret_cast<const float4*>(rp);
     float s = 0.f;
-    if ((D & 3) == 0) {
-        const float4* r4 = reinterpret_cast<const float4*>(rp);
-        for (int t0 = 0; t0 < D; t0 += 32) {
-            float4 v[8];
+    for (int t0 = 0; t0 < D; t0 += 32) {
+        float4 v[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                v[u] = (t0 + 4 * u < D) ? r4[t0 / 4 + u] : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int u = 0; u < 8; ++u)
+            v[u] = (t0 + 4 * u < D) ? __ldg(r4 + t0 / 4 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int t = t0 + 4 * u;
-                if (t < D) {
-                    float d = __fsub_rn(qs[t], v[u].x);
-                    s = (t == 0) ? __fmul_rn(d, d) : __fadd_rn(s, __fmul_rn(d, d));
-                    d = __fsub_rn(qs[t + 1], v[u].y);
-                    s = __fadd_rn(s, __fmul_rn(d, d));
-                    d = __fsub_rn(qs[t + 2], v[u].z);
-                    s = __fadd_rn(s, __fmul_rn(d, d));
-                    d = __fsub_rn(qs[t + 3], v[u].w);
-                    s = __fadd_rn(s, __fmul_rn(d, d));
-                }
+        for (int u = 0; u < 8; ++u) {
+            const int t = t0 + 4 * u;
+            if (t < D) {
+                float d = __fsub_rn(qs[t], v[u].x);
+                s = (t == 0) ? __fmul_rn(d, d) : __fadd_rn(s, __fmul_rn(d, d));
+                d = __fsub_rn(qs[t + 1], v[u].y);
+                s = __fadd_rn(s, __fmul_rn(d, d));
+                d = __fsub_rn(qs[t + 2], v[u].z);
+                s = __fadd_rn(s, __fmul_rn(d, d));
+                d = __fsub_rn(qs[t + 3], v[u].w);
+                s = __fadd_rn(s, __fmul_rn(d, d));
             }
         }
-        return s;
     }
-    return sqd_seq(qs, rp, D);
+    return s;
 }
 
-template <int KCAP>
 __global__ void __launch_bounds__(256)
 fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t B, int64_t M,
                    int64_t N, int D, int k, const int* __restrict__ bad,
                    const unsigned* __restrict__ counts, const uint2* __restrict__ cand,
                    float* __restrict__ dist, int64_t* __restrict__ idx64,
-                   float* __restrict__ sqdist) {
+                   float* __restrict__ sqdist, unsigned* __restrict__ nover,
+                   int64_t* __restrict__ over_rows) {
     static_assert(kCap == 64, "two candidates per lane");
-    extern __shared__ float s_q[];  // [8 warps][D]
+    extern __shared__ float s_q[];  // [warps][D]
     const int lane = threadIdx.x & 31;
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (row >= B * M) return;  // warp-uniform
     const int64_t b = row / M;
     const float* rb = r + b * N * D;
     float* qp = s_q + (threadIdx.x >> 5) * D;
-    for (int t = lane; t < D; t += 32) qp[t] = q[row * D + t];
-    __syncwarp();
     const unsigned cnt = bad[b] ? 0xffffffffu : counts[row];
     const int64_t o = row * k;
-    if (cnt <= (unsigned)kCap) {
-        float sd[2];
-        uint32_t jj[2];
-        bool ok[2];
+    if (cnt > (unsigned)kCap) {  // exact scan by fknn_exact_rows_kernel
+        if (lane == 0) over_rows[atomicAdd(nover, 1u)] = row;
+        return;
+    }
+    for (int t = lane; t < D; t += 32) qp[t] = q[row * D + t];
+    __syncwarp();
+    // Lane l: candidates l and l + 32 (exact SD; non-finite -> (inf, none)).
+    float sd[2];
+    uint32_t jj[2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const unsigned c = (unsigned)(lane + 32 * h);
-            ok[h] = c < cnt;
-            jj[h] = ok[h] ? cand[row * kCap + c].x : 0u;
-            sd[h] = ok[h] ? sqd_staged(qp, rb + (int64_t)jj[h] * D, D) : INFINITY;
-            ok[h] = ok[h] && isfinite(sd[h]);
-        }
-        int rank[2] = {0, 0};
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-            const unsigned live = __ballot_sync(FULL_MASK, ok[h2]);
-            for (unsigned m = live; m; m &= m - 1) {
-                const int src = __ffs(m) - 1;
-                const float e = __shfl_sync(FULL_MASK, sd[h2], src);
-                const uint32_t ej = __shfl_sync(FULL_MASK, jj[h2], src);
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-                    rank[h] += (ok[h] && before<kDropNonFinite>(e, ej, sd[h], jj[h])) ? 1 : 0;
+    for (int h = 0; h < 2; ++h) {
+        const unsigned c = (unsigned)(lane + 32 * h);
+        sd[h] = INFINITY;
+        jj[h] = kNoIndex;
+        if (c < cnt) {
+            const uint32_t j = cand[row * kCap + c].x;
+            const float v = sqd_staged(qp, rb + (int64_t)j * D, D);
+            if (isfinite(v)) {
+                sd[h] = v;
+                jj[h] = j;
             }
         }
-        const int total = __popc(__ballot_sync(FULL_MASK, ok[0])) +
-                          __popc(__ballot_sync(FULL_MASK, ok[1]));
+    }
+    if (cnt <= 32u) {
+        // Bitonic sort of the 32 (SD, index) pairs across the warp.
+        float d = sd[0];
+        uint32_t j = jj[0];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            if (ok[h] && rank[h] < k) {
-                dist[o + rank[h]] = sqrtf(sd[h]);
-                if (sqdist) sqdist[o + rank[h]] = sd[h];
-                idx64[o + rank[h]] = (int64_t)jj[h];
+        for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                const float od = __shfl_xor_sync(FULL_MASK, d, stride);
+                const uint32_t oj = __shfl_xor_sync(FULL_MASK, j, stride);
+                const bool ascending = (lane & size) == 0 || size == 32;
+                const bool lower = (lane & stride) == 0;
+                const bool other_first = od < d || (od == d && oj < j);
+                const bool take = (lower == ascending) ? other_first : !other_first;
+                d = take ? od : d;
+                j = take ? oj : j;
             }
         }
-        for (int t = total + lane; t < k; t += 32) {
-            dist[o + t] = INFINITY;
-            if (sqdist) sqdist[o + t] = INFINITY;
-            idx64[o + t] = -1;
+        if (lane < k) {
+            const bool filled = j != kNoIndex;
+            dist[o + lane] = filled ? sqrtf(d) : INFINITY;
+            if (sqdist) sqdist[o + lane] = filled ? d : INFINITY;
+            idx64[o + lane] = filled ? (int64_t)j : -1;
         }
         return;
     }
+    // 33..64 candidates: rank of each pair in (SD, index) order.
+    bool ok[2] = {jj[0] != kNoIndex, jj[1] != kNoIndex};
+    int rank[2] = {0, 0};
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+        const unsigned live = __ballot_sync(FULL_MASK, ok[h2]);
+        for (unsigned m = live; m; m &= m - 1) {
+            const int src = __ffs(m) - 1;
+            const float e = __shfl_sync(FULL_MASK, sd[h2], src);
+            const uint32_t ej = __shfl_sync(FULL_MASK, jj[h2], src);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                rank[h] += (ok[h] && before<kDropNonFinite>(e, ej, sd[h], jj[h])) ? 1 : 0;
+        }
+    }
+    const int total = __popc(__ballot_sync(FULL_MASK, ok[0])) +
+                      __popc(__ballot_sync(FULL_MASK, ok[1]));
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        if (ok[h] && rank[h] < k) {
+            dist[o + rank[h]] = sqrtf(sd[h]);
+            if (sqdist) sqdist[o + rank[h]] = sd[h];
+            idx64[o + rank[h]] = (int64_t)jj[h];
+        }
+    }
+    for (int t = total + lane; t < k; t += 32) {
+        dist[o + t] = INFINITY;
+        if (sqdist) sqdist[o + t] = INFINITY;
+        idx64[o + t] = -1;
+    }
+}
+
+// Rows whose candidate list overflowed, or whose cloud was flagged (listed
+// by fknn_rerank_kernel): warp per row, lanes scan references j = lane mod 32
+// into per-lane sorted lists, merged by k rounds of warp minimum.
+template <int KCAP>
+__global__ void __launch_bounds__(256)
+fknn_exact_rows_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t B,
+                       int64_t M, int64_t N, int D, int k, const unsigned* __restrict__ nover,
+                       const int64_t* __restrict__ over_rows, float* __restrict__ dist,
+                       int64_t* __restrict__ idx64, float* __restrict__ sqdist) {
+    extern __shared__ float s_q[];  // [8 warps][D]
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const unsigned nrows = *nover;
+    for (int64_t li = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; li < nrows;
+         li += warps) {
+    const int64_t row = over_rows[li];
+    const int64_t b = row / M;
+    const float* rb = r + b * N * D;
+    float* qp = s_q + (threadIdx.x >> 5) * D;
+    for (int t = lane; t < D; t += 32) qp[t] = q[row * D + t];
+    __syncwarp();
+    const int64_t o = row * k;
     TopK<KCAP, kDropNonFinite> top;
     top.init(k);
     for (int64_t j = lane; j < N; j += 32) top.offer(sqd_staged(qp, rb + j * D, D), (uint32_t)j);
@@ -637,6 +703,8 @@ fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int
             idx64[o + t] = filled ? (int64_t)bj : -1;
         }
     }
+    __syncwarp();
+    }
 }
 
 struct Scratch {
@@ -650,10 +718,13 @@ struct Scratch {
     unsigned* nmax;
     int* bad;
     int* status;
+    unsigned* nover;      // rows for the exact scan
+    int64_t* over_rows;   // [B * M]
     size_t bytes;
 };
 
 inline size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+inline size_t flag_bytes(int64_t B) { return (sizeof(unsigned) + sizeof(int)) * B + 8; }
 
 inline Scratch carve(void* base, int64_t B, int64_t M, int64_t N, int64_t D) {
     Scratch s{};
@@ -672,11 +743,14 @@ inline Scratch carve(void* base, int64_t B, int64_t M, int64_t N, int64_t D) {
     s.ubound = reinterpret_cast<float*>(take(sizeof(float) * B * M));
     s.counts = reinterpret_cast<unsigned*>(take(sizeof(unsigned) * B * M));
     s.cand = reinterpret_cast<uint2*>(take(sizeof(uint2) * B * M * kCap));
-    // nmax, bad and status are contiguous so one memset clears them.
-    unsigned char* flags = take(sizeof(unsigned) * B + sizeof(int) * B + sizeof(int));
+    s.over_rows = reinterpret_cast<int64_t*>(take(sizeof(int64_t) * B * M));
+    // nmax, bad, status and nover are contiguous so one memset clears them.
+    unsigned char* flags = take(flag_bytes(B));
     s.nmax = reinterpret_cast<unsigned*>(flags);
     s.bad = flags ? reinterpret_cast<int*>(flags + sizeof(unsigned) * B) : nullptr;
     s.status = flags ? reinterpret_cast<int*>(flags + (sizeof(unsigned) + sizeof(int)) * B) : nullptr;
+    s.nover = flags ? reinterpret_cast<unsigned*>(flags + (sizeof(unsigned) + sizeof(int)) * B + 4)
+                    : nullptr;
     s.bytes = off;
     return s;
 }
@@ -684,8 +758,7 @@ inline Scratch carve(void* base, int64_t B, int64_t M, int64_t N, int64_t D) {
 template <int KCAP>
 int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int D, int k,
            float* dist, int64_t* idx, float* sqdist, const Scratch& w, cudaStream_t s) {
-    if (cudaMemsetAsync(w.nmax, 0, sizeof(unsigned) * B + sizeof(int) * B + sizeof(int), s) !=
-        cudaSuccess)
+    if (cudaMemsetAsync(w.nmax, 0, flag_bytes(B), s) != cudaSuccess)
         return fail(kCudaError, "knn: scratch reset failed");
     const int Kpad = kpad_of(D);
     const int64_t mt = ceil_div(M, kTM), nt = ceil_div(N, kTN);
@@ -720,9 +793,15 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
     st = check_launch("fknn_tc_kernel<2>");
     if (st) return st;
     const size_t rsmem = (size_t)8 * D * sizeof(float);
-    fknn_rerank_kernel<KCAP><<<(unsigned)ceil_div(B * M * 32, 256), 256, rsmem, s>>>(
-        query, ref, B, M, N, D, k, w.bad, w.counts, w.cand, dist, idx, sqdist);
-    return check_launch("fknn_rerank_kernel");
+    const unsigned rgrid = (unsigned)ceil_div(B * M * 32, 256);
+    fknn_rerank_kernel<<<rgrid, 256, rsmem, s>>>(
+        query, ref, B, M, N, D, k, w.bad, w.counts, w.cand, dist, idx, sqdist, w.nover,
+        w.over_rows);
+    st = check_launch("fknn_rerank_kernel");
+    if (st) return st;
+    fknn_exact_rows_kernel<KCAP><<<(unsigned)(2 * sm_count()), 256, rsmem, s>>>(
+        query, ref, B, M, N, D, k, w.nover, w.over_rows, dist, idx, sqdist);
+    return check_launch("fknn_exact_rows_kernel");
 }
 
 }  // namespace
