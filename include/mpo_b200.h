@@ -113,7 +113,7 @@ MPO_API int mpo_fps_noalloc(const float* xyz, int64_t B, int64_t N, int64_t npoi
  *   (inf, -1).
  *   workspace: mpo_knn_workspace_bytes(B, M, N, D, k) bytes of device memory
  *   (0 when the call needs none: D == 3, small or narrow problems).  Feature
- *   kNN with 16 <= D <= 1024, k <= 32 and N >= 2048 proposes candidates with
+ *   kNN with 16 <= D <= 96, k <= 32 and N >= 2048 proposes candidates with
  *   tensor-core (tcgen05) scores and ranks them by the exact fp32 SD. */
 MPO_API size_t mpo_knn_workspace_bytes(int64_t B, int64_t M, int64_t N, int64_t D, int64_t k);
 MPO_API int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int64_t D,

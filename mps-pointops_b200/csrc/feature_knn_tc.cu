@@ -26,9 +26,10 @@
 //     per TMEM lane quarter, one thread per query) read the other accumulator
 //     with tcgen05.ld and form s_j = n(r_j) - 2 dot'_j, so SD'_j = n(q) + s_j
 //     approximates SD_j with |SD'_j - SD_j| <= eps(q) = C_K (n(q) + max n(r)).
-//       pass 1: the minimum of s over each group of 32 consecutive columns;
-//               the k-th smallest group minimum U bounds the k-th smallest s
-//               from above (k groups -> k distinct columns).
+//       pass 1: the minimum of s in each of 64 column buckets (column j of
+//               a tile -> bucket j mod 64); the k-th smallest bucket minimum
+//               U bounds the k-th smallest s from above (k buckets -> k
+//               distinct columns).
 //       pass 2: every column with s_j <= U + 2 eps(q) is appended to the
 //               query's candidate list (capacity kCap).
 //     The k nearest by exact SD are all candidates: F_k <= n(q) + U + eps
@@ -60,10 +61,12 @@ namespace {
 
 constexpr int kTM = 128;         // queries per CTA (TMEM lanes)
 constexpr int kTN = 128;         // references per tile (accumulator columns)
-constexpr int kMaxD = 128;       // widest feature vector of the tensor path
+constexpr int kMaxD = 96;        // widest feature vector of the tensor path (shared memory)
 constexpr int kCap = 64;         // candidates kept per query
 constexpr int kMaxK = 32;        // largest k served by this path
-constexpr int kThreadsTC = 192;  // warp 0 producer, warp 1 MMA, warps 2-5 epilogue
+constexpr int kQT = 2;           // 128-query tiles per CTA (share every reference tile)
+constexpr int kRows = kQT * kTM;  // queries per CTA
+constexpr int kThreadsTC = 576;   // warp 0 producer, warp 1 MMA, warps 2-17 epilogue
 constexpr unsigned long long kWaitNs = 2000000000ull;
 constexpr float kHuge = 1.15292150e18f;  // 2^60: larger norms go to the exact path
 
@@ -74,17 +77,22 @@ constexpr float kHuge = 1.15292150e18f;  // 2^60: larger norms go to the exact p
 __host__ __device__ constexpr int kpad_of(int D) { return (D + 15) / 16 * 16; }
 __host__ __device__ constexpr int part_bytes(int Kpad) { return 128 * Kpad * 2; }
 
-// Shared memory: A (2 parts) | 2 stages x (B 2 parts + 128 norms) | barriers.
+// Shared memory: A (kQT tiles x 2 parts) | 2 stages x B (2 parts) | 4-slot ring of the
+// tiles' reference norms | barriers.  The norms have their own ring so that a
+// B stage is refilled as soon as the MMAs have read it, while the epilogue of
+// that tile still reads its norms.
+constexpr int kNySlots = 4;
 struct TcSmem {
     int part, a_off, b_off, stage_bytes, ny_off, bar_off, total;
     __host__ __device__ TcSmem(int Kpad) {
         part = part_bytes(Kpad);
         a_off = 0;
-        b_off = 2 * part;
-        stage_bytes = 2 * part + kTN * 4;
-        ny_off = 2 * part;  // within a stage
-        bar_off = b_off + 2 * stage_bytes;
-        total = bar_off + 128;
+        b_off = kQT * 2 * part;
+        stage_bytes = 2 * part;
+        ny_off = b_off + 2 * stage_bytes;
+        if (ny_off - b_off < 66 * kRows * 4) ny_off = b_off + 66 * kRows * 4;  // epilogue handoff
+        bar_off = ny_off + kNySlots * kTN * 4;
+        total = bar_off + 192;
     }
 };
 
@@ -117,6 +125,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         if (globaltimer_ns() - t0 > kWaitNs) return false;
     }
     return true;
+}
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -307,9 +318,9 @@ __device__ __forceinline__ float eps_coef(int D) {
 
 // ---- 2. approximate scores on the tensor cores ------------------------------
 // Barriers: full[s] (producer expect_tx + bulk-copy bytes), empty[s] (MMA
-// commit: operands of stage s read, plus the 4 epilogue warps: norms of stage
-// s read), accf[a] (MMA commit: accumulator a written), acce[a] (4 epilogue
-// warps: accumulator a read).  Phase parity of round n = n & 1;
+// commit: operands of stage s read), accf[a] (MMA commit: accumulator a
+// written), acce[a] (4 epilogue warps: accumulator a read), nfull[i] / nempty[i]
+// for the norm ring (bulk copy / the 4 warps of the epilogue group).  Phase parity of round n = n & 1;
 // "free" barriers are waited with the opposite parity first.
 template <int PASS, int KCAP>
 __global__ void __launch_bounds__(kThreadsTC, 1)
@@ -328,20 +339,25 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
     const TcSmem L(Kpad);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar = sbase + L.bar_off;
-    // barrier addresses: full 0,1 | empty 2,3 | accf 4,5 | acce 6,7 | afull 8
+    // barrier addresses: full 0,1 | empty 2,3 | accf 4,5 | acce 6,7 | afull 8 |
+    // norms full 9-12 | norms empty 13-16
     auto B_ = [&](int i) { return bar + 8u * (uint32_t)i; };
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.bar_off + 80);
-    int* s_abort = reinterpret_cast<int*>(smem + L.bar_off + 84);
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.bar_off + 160);
+    int* s_abort = reinterpret_cast<int*>(smem + L.bar_off + 164);
 
-    if (warp == 0) tmem_alloc(smem_u32(s_tmem), 2 * kTN);
+    if (warp == 0) tmem_alloc(smem_u32(s_tmem), 2 * kQT * kTN);
     if (tid == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(B_(0 + i), 1);
-            mbar_init(B_(2 + i), 5);
+            mbar_init(B_(2 + i), 1);
             mbar_init(B_(4 + i), 1);
-            mbar_init(B_(6 + i), 4);
+            mbar_init(B_(6 + i), 4 * kQT);
         }
         mbar_init(B_(8), 1);
+        for (int i = 0; i < kNySlots; ++i) {
+            mbar_init(B_(9 + i), 1);
+            mbar_init(B_(13 + i), 4 * kQT);
+        }
         *s_abort = 0;
         mbar_fence_init();
     }
@@ -354,9 +370,10 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
     if (warp == 0) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            const unsigned char* asrc = qpack + (size_t)(b * mtiles + mt) * a_bytes;
-            bulk_expect(B_(8), a_bytes);
-            bulk_copy(sbase + L.a_off, asrc, a_bytes, B_(8));
+            // kQT consecutive query tiles (the pack has mtiles rounded up).
+            const unsigned char* asrc = qpack + (size_t)(b * mtiles + mt * kQT) * a_bytes;
+            bulk_expect(B_(8), kQT * a_bytes);
+            bulk_copy(sbase + L.a_off, asrc, kQT * a_bytes, B_(8));
             int64_t issued = 0;
             for (int64_t t = 0; t < ntiles; ++t) {
                 const int st = (int)(t & 1);
@@ -367,15 +384,27 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                     break;
                 }
                 const uint32_t dst = sbase + L.b_off + (uint32_t)(st * L.stage_bytes);
-                bulk_expect(B_(0 + st), a_bytes + kTN * 4);
+                bulk_expect(B_(0 + st), a_bytes);
                 bulk_copy(dst, rpack + (size_t)(b * ntiles + t) * a_bytes, a_bytes, B_(0 + st));
-                bulk_copy(dst + L.ny_off, nr + (size_t)(b * ntiles + t) * kTN, kTN * 4, B_(0 + st));
+                const int ns = (int)(t & 3);
+                const uint32_t nn = (uint32_t)(t >> 2);
+                if (!mbar_wait(B_(13 + ns), (nn & 1) ^ 1)) {
+                    atomicExch(status, 1);
+                    *(volatile int*)s_abort = 1;
+                    ++issued;
+                    break;
+                }
+                bulk_expect(B_(9 + ns), kTN * 4);
+                bulk_copy(sbase + L.ny_off + (uint32_t)(ns * kTN * 4),
+                          nr + (size_t)(b * ntiles + t) * kTN, kTN * 4, B_(9 + ns));
                 ++issued;
             }
             // Copies still in flight (only after an abort) land before exit.
             mbar_wait(B_(8), 0);
             for (int64_t t = max64(issued - 2, 0); t < issued; ++t)
                 mbar_wait(B_(0 + (int)(t & 1)), (uint32_t)((t >> 1) & 1));
+            for (int64_t t = max64(issued - kNySlots, 0); t < issued; ++t)
+                mbar_wait(B_(9 + (int)(t & 3)), (uint32_t)((t >> 2) & 1));
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -388,19 +417,22 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                      !*(volatile int*)s_abort;
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)(ac * kTN);
-                const uint32_t a0 = sbase + L.a_off;
                 const uint32_t b0 = sbase + L.b_off + (uint32_t)(st * L.stage_bytes);
                 const uint32_t part = (uint32_t)L.part;
-                for (int s = 0; s < Kpad / 16; ++s) {
-                    const uint32_t ko = (uint32_t)s * 256u;
-                    const uint64_t ahi = smem_desc(a0 + ko, 128, sbo);
-                    const uint64_t alo = smem_desc(a0 + part + ko, 128, sbo);
-                    const uint64_t bhi = smem_desc(b0 + ko, 128, sbo);
-                    const uint64_t blo = smem_desc(b0 + part + ko, 128, sbo);
-                    mma_bf16(d, ahi, bhi, s == 0 ? 0u : 1u);
-                    mma_bf16(d, ahi, blo, 1u);
-                    mma_bf16(d, alo, bhi, 1u);
+                for (int qt = 0; qt < kQT; ++qt) {
+                    // Accumulator ac of query tile qt: columns (ac * kQT + qt) * kTN.
+                    const uint32_t d = tmem + (uint32_t)((ac * kQT + qt) * kTN);
+                    const uint32_t a0 = sbase + L.a_off + (uint32_t)qt * a_bytes;
+                    for (int s = 0; s < Kpad / 16; ++s) {
+                        const uint32_t ko = (uint32_t)s * 256u;
+                        const uint64_t ahi = smem_desc(a0 + ko, 128, sbo);
+                        const uint64_t alo = smem_desc(a0 + part + ko, 128, sbo);
+                        const uint64_t bhi = smem_desc(b0 + ko, 128, sbo);
+                        const uint64_t blo = smem_desc(b0 + part + ko, 128, sbo);
+                        mma_bf16(d, ahi, bhi, s == 0 ? 0u : 1u);
+                        mma_bf16(d, ahi, blo, 1u);
+                        mma_bf16(d, alo, bhi, 1u);
+                    }
                 }
                 mma_commit(B_(2 + st));  // stage st may be refilled
                 mma_commit(B_(4 + ac));  // accumulator ac is ready
@@ -411,78 +443,75 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
             }
         }
     } else {
-        // ---------------- epilogue: one thread per query ----------------
+        // ---------------- epilogue ----------------
+        // Warps 2-17 in sets of 4 (one per TMEM lane quarter): set = 2 g + qt
+        // takes query tile qt of the reference tiles t = g (mod 2), i.e.
+        // accumulator g; one thread per query.
+        const int set = (warp - 2) >> 2;
+        const int group = set >> 1, qt = set & 1;
         const int quarter = warp & 3;
-        const int row = quarter * 32 + lane;
-        const int64_t gq = mt * kTM + row;
+        const int row = qt * kTM + quarter * 32 + lane;
+        const int64_t gq = mt * kRows + row;
         const bool qvalid = gq < M;
         const float nqi = qvalid ? nq[(int64_t)b * M + gq] : 0.f;
         const float eps = eps_coef(D) * (nqi + __uint_as_float(nmax[b]));
         float thr = -INFINITY;  // pass 2: s_j <= thr makes j a candidate
         if (PASS == 2 && qvalid) thr = ubound[(int64_t)b * M + gq] + 2.f * eps;
-        float lst[KCAP];  // pass 1: k smallest group minima, right-aligned
+        // Pass 1: bucket i of group g holds the minimum of s over column i of
+        // every 32-column chunk of the group's tiles; with the other group's
+        // buckets, the k-th smallest of the 64 bucket minima bounds the k-th
+        // smallest s from above (k buckets -> k distinct columns).
+        float bmin[32];
 #pragma unroll
-        for (int i = 0; i < KCAP; ++i) lst[i] = i < KCAP - k ? -INFINITY : INFINITY;
+        for (int i = 0; i < 32; ++i) bmin[i] = INFINITY;
         unsigned found = 0;
         bool ok = true;
-        for (int64_t t = 0; t < ntiles; ++t) {
-            const int st = (int)(t & 1), ac = (int)(t & 1);
+        for (int64_t t = group; t < ntiles; t += 2) {
+            const int ac = group;
             const uint32_t n = (uint32_t)(t >> 1);
-            const bool got = mbar_wait(B_(4 + ac), n & 1);
+            const int ns = (int)(t & 3);
+            const bool got = mbar_wait(B_(4 + ac), n & 1) && mbar_wait(B_(9 + ns), (uint32_t)((t >> 2) & 1));
             ok = __all_sync(FULL_MASK, got) && !*(volatile int*)s_abort;
             if (!ok) break;
             tc_fence_after();
-            const float* s_ny = reinterpret_cast<const float*>(smem + L.b_off + st * L.stage_bytes +
-                                                               L.ny_off);
-            // The norms of stage st stay until this warp arrives on empty[st].
+            const float* s_ny = reinterpret_cast<const float*>(smem + L.ny_off + ns * kTN * 4);
+            // The norms of slot ns stay until this group arrives on its empty barrier.
 #pragma unroll 1
             for (int c = 0; c < kTN / 32; ++c) {
                 float v[32];
-                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(ac * kTN + c * 32),
+                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) +
+                              (uint32_t)((ac * kQT + qt) * kTN + c * 32),
                           v);
                 const float4* ny4 = reinterpret_cast<const float4*>(s_ny + c * 32);
                 if (PASS == 1) {
-                    float g = INFINITY;
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float4 y = ny4[i];
-                        g = fminf(g, fmaf(-2.f, v[4 * i + 0], y.x));
-                        g = fminf(g, fmaf(-2.f, v[4 * i + 1], y.y));
-                        g = fminf(g, fmaf(-2.f, v[4 * i + 2], y.z));
-                        g = fminf(g, fmaf(-2.f, v[4 * i + 3], y.w));
-                    }
-                    if (g < lst[KCAP - 1]) {
-#pragma unroll
-                        for (int i = KCAP - 1; i >= 1; --i) {
-                            const float lo = lst[i - 1];
-                            lst[i] = (g < lo) ? lo : ((g < lst[i]) ? g : lst[i]);
-                        }
-                        lst[0] = fminf(lst[0], g);
+                        bmin[4 * i + 0] = fminf(bmin[4 * i + 0], fmaf(-2.f, v[4 * i + 0], y.x));
+                        bmin[4 * i + 1] = fminf(bmin[4 * i + 1], fmaf(-2.f, v[4 * i + 1], y.y));
+                        bmin[4 * i + 2] = fminf(bmin[4 * i + 2], fmaf(-2.f, v[4 * i + 2], y.z));
+                        bmin[4 * i + 3] = fminf(bmin[4 * i + 3], fmaf(-2.f, v[4 * i + 3], y.w));
                     }
                 } else {
                     // Candidate bit mask of the 32 columns (no divergence),
-                    // then one store per set bit.
-                    float sv[32];
+                    // then one store per set bit.  Group 0 fills the list
+                    // from slot 0 up, group 1 from slot kCap - 1 down.
                     unsigned hits = 0u;
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float4 y = ny4[i];
-                        sv[4 * i + 0] = fmaf(-2.f, v[4 * i + 0], y.x);
-                        sv[4 * i + 1] = fmaf(-2.f, v[4 * i + 1], y.y);
-                        sv[4 * i + 2] = fmaf(-2.f, v[4 * i + 2], y.z);
-                        sv[4 * i + 3] = fmaf(-2.f, v[4 * i + 3], y.w);
+                        hits |= (fmaf(-2.f, v[4 * i + 0], y.x) <= thr ? 1u : 0u) << (4 * i + 0);
+                        hits |= (fmaf(-2.f, v[4 * i + 1], y.y) <= thr ? 1u : 0u) << (4 * i + 1);
+                        hits |= (fmaf(-2.f, v[4 * i + 2], y.z) <= thr ? 1u : 0u) << (4 * i + 2);
+                        hits |= (fmaf(-2.f, v[4 * i + 3], y.w) <= thr ? 1u : 0u) << (4 * i + 3);
                     }
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) hits |= (sv[i] <= thr ? 1u : 0u) << i;
                     while (hits) {
                         const int i = __ffs(hits) - 1;
                         hits &= hits - 1;
                         if (found < (unsigned)kCap) {
-                            float si = sv[0];
-#pragma unroll
-                            for (int u = 1; u < 32; ++u) si = (u == i) ? sv[u] : si;
-                            cand[((int64_t)b * M + gq) * kCap + found] =
-                                make_uint2((unsigned)(t * kTN + c * 32 + i), __float_as_uint(si));
+                            const unsigned slot = group ? (unsigned)kCap - 1u - found : found;
+                            cand[((int64_t)b * M + gq) * kCap + slot] =
+                                make_uint2((unsigned)(t * kTN + c * 32 + i), 0u);
                         }
                         ++found;
                     }
@@ -491,24 +520,63 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(B_(6 + ac));  // accumulator read
-                mbar_arrive(B_(2 + st));  // norms of the stage read
+                mbar_arrive(B_(6 + ac));   // accumulator read
+                mbar_arrive(B_(13 + ns));  // norms read
             }
         }
         if (!ok) {
             if (lane == 0) atomicExch(status, 1);
             *(volatile int*)s_abort = 1;
         }
-        if (qvalid) {
-            if (PASS == 1) ubound[(int64_t)b * M + gq] = ok ? lst[KCAP - 1] : INFINITY;
-            else counts[(int64_t)b * M + gq] = ok ? found : 0xffffffffu;
+        // Hand group 1's state to group 0 through the (idle) B stages:
+        // s_x[u * kTM + row] = bucket u (0-31 group 0, 32-63 group 1), then
+        // group 1's count and status.
+        float* s_x = reinterpret_cast<float*>(smem + L.b_off);
+        named_barrier_sync(1, 16 * 32);  // both epilogue groups finished their tiles
+        if (PASS == 1) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) s_x[(32 * group + i) * kRows + row] = bmin[i];
+        }
+        if (group == 1) {
+            s_x[64 * kRows + row] = __uint_as_float(found);
+            s_x[65 * kRows + row] = ok ? 1.f : 0.f;
+        }
+        named_barrier_sync(1, 16 * 32);
+        if (group == 0) {
+            ok = ok && s_x[65 * kRows + row] != 0.f;
+            if (PASS == 1) {
+                // k-th smallest of the 64 bucket minima (sorted right-aligned list).
+                float lst[KCAP];
+#pragma unroll
+                for (int i = 0; i < KCAP; ++i) lst[i] = i < KCAP - k ? -INFINITY : INFINITY;
+#pragma unroll 1
+                for (int u = 0; u < 64; ++u) {
+                    // Own buckets were parked next to group 1's, so both halves
+                    // are read from shared memory (no dynamic register index).
+                    const float g = s_x[u * kRows + row];
+                    if (g < lst[KCAP - 1]) {
+#pragma unroll
+                        for (int i = KCAP - 1; i >= 1; --i) {
+                            const float lo = lst[i - 1];
+                            lst[i] = (g < lo) ? lo : ((g < lst[i]) ? g : lst[i]);
+                        }
+                        lst[0] = fminf(lst[0], g);
+                    }
+                }
+                if (qvalid) ubound[(int64_t)b * M + gq] = ok ? lst[KCAP - 1] : INFINITY;
+            } else if (qvalid) {
+                const unsigned f1 = __float_as_uint(s_x[64 * kRows + row]);
+                // Packed (group 0 count, group 1 count); overflow -> exact path.
+                counts[(int64_t)b * M + gq] =
+                    (ok && found + f1 <= (unsigned)kCap) ? (found | (f1 << 16)) : 0xffffffffu;
+            }
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * kTN);
+        tmem_dealloc(tmem, 2 * kQT * kTN);
     }
 }
 
@@ -565,12 +633,15 @@ fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int
     const int64_t b = row / M;
     const float* rb = r + b * N * D;
     float* qp = s_q + (threadIdx.x >> 5) * D;
-    const unsigned cnt = bad[b] ? 0xffffffffu : counts[row];
+    const unsigned packed = bad[b] ? 0xffffffffu : counts[row];
     const int64_t o = row * k;
-    if (cnt > (unsigned)kCap) {  // exact scan by fknn_exact_rows_kernel
+    if (packed == 0xffffffffu) {  // exact scan by fknn_exact_rows_kernel
         if (lane == 0) over_rows[atomicAdd(nover, 1u)] = row;
         return;
     }
+    // Candidates: slots [0, f0) from the even tiles, [kCap - f1, kCap) from
+    // the odd tiles.
+    const unsigned f0 = packed & 0xffffu, f1 = packed >> 16, cnt = f0 + f1;
     for (int t = lane; t < D; t += 32) qp[t] = q[row * D + t];
     __syncwarp();
     // Lane l: candidates l and l + 32 (exact SD; non-finite -> (inf, none)).
@@ -582,7 +653,8 @@ fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int
         sd[h] = INFINITY;
         jj[h] = kNoIndex;
         if (c < cnt) {
-            const uint32_t j = cand[row * kCap + c].x;
+            const unsigned slot = c < f0 ? c : (unsigned)kCap - 1u - (c - f0);
+            const uint32_t j = cand[row * kCap + slot].x;
             const float v = sqd_staged(qp, rb + (int64_t)j * D, D);
             if (isfinite(v)) {
                 sd[h] = v;
@@ -734,7 +806,8 @@ inline Scratch carve(void* base, int64_t B, int64_t M, int64_t N, int64_t D) {
         off += align256(n);
         return base ? static_cast<unsigned char*>(base) + at : nullptr;
     };
-    const int64_t mt = ceil_div(M, kTM), nt = ceil_div(N, kTN);
+    // Query tiles rounded up to whole CTAs (kQT tiles each).
+    const int64_t mt = ceil_div(M, kRows) * kQT, nt = ceil_div(N, kTN);
     const size_t tile = 2 * (size_t)part_bytes(kpad_of((int)D));
     s.qpack = take(tile * B * mt);
     s.rpack = take(tile * B * nt);
@@ -761,7 +834,7 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
     if (cudaMemsetAsync(w.nmax, 0, flag_bytes(B), s) != cudaSuccess)
         return fail(kCudaError, "knn: scratch reset failed");
     const int Kpad = kpad_of(D);
-    const int64_t mt = ceil_div(M, kTM), nt = ceil_div(N, kTN);
+    const int64_t mt = ceil_div(M, kRows) * kQT, nt = ceil_div(N, kTN);
     const int64_t qchunks = B * mt * 128 * (Kpad / 8), rchunks = B * nt * 128 * (Kpad / 8);
     fknn_pack_kernel<<<(unsigned)ceil_div(qchunks, 256), 256, 0, s>>>(query, B, M, D, Kpad, mt,
                                                                       w.qpack);
@@ -783,7 +856,7 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
         cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
             cudaSuccess)
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");
-    dim3 grid((unsigned)mt, (unsigned)B);
+    dim3 grid((unsigned)(mt / kQT), (unsigned)B);
     k1<<<grid, kThreadsTC, L.total, s>>>(w.qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
                                          w.bad, w.ubound, w.counts, w.cand, w.status);
     st = check_launch("fknn_tc_kernel<1>");
@@ -806,7 +879,7 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
 
 }  // namespace
 
-// The tensor path serves D != 3 with 16 <= D <= 128, k <= 32 and reference
+// The tensor path serves D != 3 with 16 <= D <= 96, k <= 32 and reference
 // clouds of at least 2048 points (smaller problems are cheap exactly).
 bool fknn_tc_eligible(int64_t M, int64_t N, int64_t D, int64_t k) {
     return D != 3 && D >= 16 && D <= kMaxD && k >= 1 && k <= kMaxK && N >= 2048 && M >= 1 &&

@@ -1,7 +1,7 @@
 """Feature-space kNN through the tensor-core candidate path (tcgen05 bf16x3
 scores, exact fp32 re-rank) vs the exact (SD, index) oracle of
 tests/test_feature_knn.py:16-35 of gamzerA/mps-pointops.  The path serves
-16 <= D <= 1024, k <= 32, N >= 2048; results must be bit-exact like the
+16 <= D <= 96, k <= 32, N >= 2048; results must be bit-exact like the
 exact kernels': indices, squared distances and IEEE sqrt distances."""
 
 from __future__ import annotations
@@ -40,12 +40,12 @@ def test_dgcnn_config4_slice(cuda_device):
     assert torch.equal(i[..., 0].cpu(), torch.arange(4096).expand(2, -1))
 
 
-@pytest.mark.parametrize("d", [16, 20, 33, 64, 100, 128])
+@pytest.mark.parametrize("d", [16, 20, 33, 64, 72, 96])
 @pytest.mark.parametrize("k", [1, 8, 20, 32])
 def test_dims_and_k(cuda_device, d, k):
-    # M not a multiple of 128, N not a multiple of 256; D not a multiple of 16
-    # and D > 64 (several K chunks).
-    q = feats(2, 130, d, seed=d)
+    # M not a multiple of the 256-query CTA tile, N not a multiple of the
+    # 128-reference tile; D not a multiple of 16.
+    q = feats(2, 300, d, seed=d)
     r = feats(2, 2500, d, seed=d + 1)
     check(q, r, k, cuda_device)
 
@@ -55,6 +55,15 @@ def test_scaled_and_offset_features(cuda_device):
     q = feats(1, 300, 32, seed=7, scale=1000.0) + 5000.0
     r = feats(1, 3000, 32, seed=8, scale=1000.0) + 5000.0
     check(q, r, 16, cuda_device)
+
+
+def test_wide_features_use_exact_path(cuda_device):
+    q, r = feats(1, 64, 128, seed=16), feats(1, 2100, 128, seed=17)
+    assert N.lib().mpo_knn_workspace_bytes(1, 64, 2100, 128, 8) == 0
+    want_d, want_i = O.knn(q.numpy(), r.numpy(), 8)
+    d, i = mps_pointops.knn(q.to(cuda_device), r.to(cuda_device), 8)
+    np.testing.assert_array_equal(i.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(d.cpu().numpy(), want_d)
 
 
 def test_ties_and_duplicates(cuda_device):
