@@ -202,6 +202,30 @@ def ssg_secondary(steps: int, warmup: int, world: int, rank: int) -> dict:
             "config": {"workload": "ssg_config1", "global_batch": 8 * world, "points": 4096}}
 
 
+def feature_knn_secondary(steps: int, warmup: int, world: int, rank: int,
+                          flush: torch.Tensor) -> dict:
+    """knn(f, f, 20) on 16 clouds of 4096 unit-norm D=64
+    features per GPU (tensor-core candidates + exact fp32 re-rank); queries/s.
+    L2 flushed between timed steps (the inputs are 16 MB)."""
+    from mps_pointops import knn
+    g = torch.Generator().manual_seed(5 + 1000 * rank)
+    f = torch.nn.functional.normalize(torch.randn(16, 4096, 64, generator=g), dim=-1).cuda()
+
+    def step():
+        knn(f, f, 20)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(statistics.mean(timed_steps(step, steps, flush)), world)
+    return {"metric": "feature kNN queries/sec (B=16,N=4096,D=64,k=20)",
+            "value": 16 * 4096 * world / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms,
+            "config": {"workload": "feature_knn_config4", "global_batch": 16 * world,
+                       "points": 4096, "dims": 64, "k": 20,
+                       "l2": "flushed between timed steps"}}
+
+
 def cpu_baseline_sample(max_seconds: float = 15.0) -> dict:
     """The oracle (C restatement of the reference's CPU Chamfer search,
     mps_pointops/chamfer.py:161-251) on the bench inputs, forward + backward,
@@ -276,6 +300,8 @@ def run_b200(args, world, rank, local):
     e2e_ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
 
     secondary = None if args.no_secondary else ssg_secondary(args.steps, args.warmup, world, rank)
+    fknn = None if args.no_secondary else feature_knn_secondary(args.steps, max(args.warmup, 3),
+                                                                world, rank, flush)
 
     # Roofline of the dominant kernel: the nearest search (8 separately rounded
     # flops per unique pair) against the FP32 pipe: 128 rounded fp32 ops per
@@ -321,6 +347,8 @@ def run_b200(args, world, rank, local):
     }
     if secondary:
         out["secondary"] = secondary
+    if fknn:
+        out["secondary_feature_knn"] = fknn
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline_sample()
     return out
