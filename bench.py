@@ -58,6 +58,14 @@ def parse_args():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="chamfer_config2",
+                    choices=["chamfer_config2", "ssg_config1_ops", "fps_config3",
+                             "feature_knn_config4", "knn_config5", "ball_query_config5"],
+                    help="single-GPU measurement of one BASELINE config (the default is the "
+                         "headline line; the others print their own JSON line and are used "
+                         "for the per-kernel profiles)")
+    ap.add_argument("--queries", type=int, default=131072,
+                    help="config 5: queries per GPU (1M queries / 8 GPUs)")
     return ap.parse_args()
 
 
@@ -224,6 +232,90 @@ def feature_knn_secondary(steps: int, warmup: int, world: int, rank: int,
             "config": {"workload": "feature_knn_config4", "global_batch": 16 * world,
                        "points": 4096, "dims": 64, "k": 20,
                        "l2": "flushed between timed steps"}}
+
+
+def _event_ms(fn, steps: int, warmup: int, flush: torch.Tensor | None) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    return statistics.median(timed_steps(fn, steps, flush))
+
+
+def ssg_config1_ops(steps: int, warmup: int) -> dict:
+    """BASELINE config 1, op by op (B=8 uniform clouds of 4096 points): compat
+    FPS 1024, compat ball query (0.2, 32), kNN k=16 centres -> points, three_nn
+    points -> centres, three_interpolate of 64 N(0,1) features (forward and
+    backward); per-op median ms with the L2 flushed between steps."""
+    from mps_pointops import compat, knn, three_interpolate, three_nn
+    g = torch.Generator().manual_seed(0)
+    xyz = torch.rand(8, 4096, 3, generator=g).cuda()
+    feats = torch.randn(8, 64, 1024, generator=torch.Generator().manual_seed(1)).cuda()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    idx = compat.furthest_point_sample(xyz, 1024)
+    centres = compat.gather_operation(xyz.transpose(1, 2).contiguous(), idx)
+    centres = centres.transpose(1, 2).contiguous()
+    dist, nidx = three_nn(xyz, centres)
+    w = 1.0 / (dist + 1e-8)
+    w = w / w.sum(dim=2, keepdim=True)
+    fg = feats.clone().requires_grad_()
+    out = three_interpolate(fg, nidx, w)
+    gout = torch.randn_like(out)
+    ops = {
+        "fps": lambda: compat.furthest_point_sample(xyz, 1024),
+        "ball_query": lambda: compat.ball_query(0.2, 32, xyz, centres),
+        "knn": lambda: knn(centres, xyz, 16),
+        "three_nn": lambda: three_nn(xyz, centres),
+        "three_interpolate_fwd": lambda: three_interpolate(feats, nidx, w),
+        "three_interpolate_fwd_bwd": lambda: torch.autograd.grad(
+            three_interpolate(fg, nidx, w), fg, gout),
+    }
+    res = {name: _event_ms(fn, steps, warmup, flush) for name, fn in ops.items()}
+    return {"workload": "ssg_config1_ops", "unit": "ms (median, public API, L2 flushed)",
+            "per_op_ms": res, "clouds": 8, "points": 4096, "centres": 1024}
+
+
+def fps_config3(steps: int, warmup: int) -> dict:
+    """FPS of 65,536 centres from one cloud of 2^20 points
+    on the unit sphere with N(0, 0.01) radial jitter, start 0."""
+    from mps_pointops import furthest_point_sample
+    g = torch.Generator().manual_seed(4)
+    p = torch.randn(1, 1 << 20, 3, generator=g)
+    p = p / p.norm(dim=-1, keepdim=True)
+    p = p * (1 + 0.01 * torch.randn(1, 1 << 20, 1, generator=g))
+    p = p.cuda()
+    ms = _event_ms(lambda: furthest_point_sample(p, 65536), max(steps, 1), max(warmup, 1), None)
+    stream_bytes = 65536 * (1 << 20) * 20
+    return {"workload": "fps_config3", "ms": ms, "ns_per_step": ms * 1e6 / 65536,
+            "samples_per_s": 65536 / (ms / 1e3),
+            "streaming_model_GBps": stream_bytes / (ms / 1e3) / 1e9,
+            "note": "streaming model: 20 B per point-step (12 B xyz + 4 B read + 4 B write of "
+                    "min_d2); the kernel keeps the cloud in registers, so this is the rate an "
+                    "HBM-streaming design would need, not DRAM traffic"}
+
+
+def _config5_cloud(seed: int, n: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    centres = torch.rand(64, 3, generator=torch.Generator().manual_seed(6)) * 20 - 10
+    labels = torch.randint(64, (n,), generator=g)
+    return (centres[labels] + 0.5 * torch.randn(n, 3, generator=g)).unsqueeze(0)
+
+
+def config5(kind: str, queries: int, steps: int, warmup: int) -> dict:
+    """BASELINE config 5 on one GPU: reference cloud of 2^20 points from 64
+    Gaussian clusters (centres U[-10,10]^3, sigma 0.5), `queries` query points
+    from the same distribution (the per-GPU shard of the 2^20 queries):
+    knn k=16 or ball_query r=0.3, K=32."""
+    from mps_pointops import ball_query, knn
+    ref = _config5_cloud(6, 1 << 20).cuda()
+    q = _config5_cloud(7, 1 << 20)[:, :queries].contiguous().cuda()
+    if kind == "knn":
+        fn = lambda: knn(q, ref, 16)  # noqa: E731
+    else:
+        fn = lambda: ball_query(q, ref, 0.3, 32)  # noqa: E731
+    ms = _event_ms(fn, max(steps, 1), max(warmup, 1), None)
+    return {"workload": f"{kind}_config5", "queries": queries, "refs": 1 << 20, "ms": ms,
+            "queries_per_s": queries / (ms / 1e3),
+            "pairs_per_s_brute_force": queries * (1 << 20) / (ms / 1e3)}
 
 
 def cpu_baseline_sample(max_seconds: float = 15.0) -> dict:
@@ -394,6 +486,20 @@ def main():
         if int(os.environ.get("RANK", "0")) != 0:
             return
         print(json.dumps(run_reference(args)), flush=True)
+        return
+    if args.workload != "chamfer_config2":
+        torch.cuda.set_device(0)
+        steps, warmup = min(args.steps, 20), max(args.warmup, 1)
+        if args.workload == "ssg_config1_ops":
+            out = ssg_config1_ops(steps, max(warmup, 3))
+        elif args.workload == "fps_config3":
+            out = fps_config3(min(steps, 3), 1)
+        elif args.workload == "feature_knn_config4":
+            flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+            out = feature_knn_secondary(steps, max(warmup, 3), 1, 0, flush)
+        else:
+            out = config5(args.workload.split("_config")[0], args.queries, min(steps, 5), 1)
+        print(json.dumps(out), flush=True)
         return
     world, rank, local = init_dist()
     try:

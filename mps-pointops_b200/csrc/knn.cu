@@ -186,6 +186,162 @@ knn3_kernel(const float* __restrict__ query, const float* __restrict__ ref, int6
 }
 
 // --------------------------------------------------------------------------
+// D == 3, large reference clouds (N > 2^18): thread per (query, split) as in
+// knn3_kernel, but packed over references -- the query sits duplicated in
+// f32x2 registers, (qx, qx), and one packed pass evaluates two reference
+// points, so the distance costs half the issue slots of the scalar loop (the
+// FP32 pipe then bounds the kernel).  The tile stores reference points in
+// structure-of-arrays pairs: (x_2p, x_2p+1, y_2p, y_2p+1) per point pair and
+// (z_4i .. z_4i+3) per four points.
+template <int K, int POLICY>
+__global__ void __launch_bounds__(kThreads, 2)
+knn3p_kernel(const float* __restrict__ query, const float* __restrict__ ref, int64_t M,
+             int64_t N, int k, int S, float* __restrict__ dist, int64_t* __restrict__ idx64,
+             int32_t* __restrict__ idx32, float* __restrict__ sqdist) {
+    extern __shared__ float4 smem4[];
+    float4* txy = smem4;                    // [2][kTile / 2]
+    float4* tz = smem4 + kTile;             // [2][kTile / 4]
+    const int b = blockIdx.y;
+    const int qpc = kThreads / S;
+    const int tid = threadIdx.x;
+    const int split = tid / qpc;
+    const int ql = tid % qpc;
+    const int64_t q = (int64_t)blockIdx.x * qpc + ql;
+    const bool active = q < M;
+    const float* __restrict__ r = ref + (size_t)b * (size_t)N * 3;
+
+    float qx = 0.f, qy = 0.f, qz = 0.f;
+    if (active) {
+        const float* qp = query + ((size_t)b * (size_t)M + (size_t)q) * 3;
+        qx = qp[0];
+        qy = qp[1];
+        qz = qp[2];
+    }
+    const f32x2 X = pack2(qx, qx), Y = pack2(qy, qy), Z = pack2(qz, qz);
+    TopK<K, POLICY> top;
+    top.init(k);
+
+    const int64_t ntiles = ceil_div(N, kTile);
+    const int slice = kTile / S;  // multiple of 4
+    constexpr int kLoads = 3 * kTile / kThreads;
+    float pre[kLoads];
+    uint32_t* qi = reinterpret_cast<uint32_t*>(smem4 + kTile + kTile / 2);
+    float* qd = reinterpret_cast<float*>(qi + kQueue * kThreads);
+    int qn = 0;
+    auto flush = [&]() {
+        for (int e = 0; e < qn; ++e) top.offer(qd[e * kThreads + tid], qi[e * kThreads + tid]);
+        qn = 0;
+    };
+    auto load_tile = [&](int64_t t) {
+        const int64_t base = t * kTile * 3;
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) {
+            const int64_t e = base + tid + (int64_t)u * kThreads;
+            pre[u] = e < N * 3 ? r[e] : 0.f;
+        }
+    };
+    auto store_tile = [&](int buf) {
+        float* xy = reinterpret_cast<float*>(txy + buf * (kTile / 2));
+        float* zz = reinterpret_cast<float*>(tz + buf * (kTile / 4));
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) {
+            const int e = tid + u * kThreads;
+            const int pnt = e / 3, crd = e % 3;
+            if (crd < 2) xy[(pnt >> 1) * 4 + 2 * crd + (pnt & 1)] = pre[u];
+            else zz[pnt] = pre[u];
+        }
+    };
+    if (ntiles > 0) {
+        load_tile(0);
+        store_tile(0);
+    }
+    __syncthreads();
+    float thr = top.kth();
+    for (int64_t t = 0; t < ntiles; ++t) {
+        const int buf = (int)(t & 1);
+        if (t + 1 < ntiles) load_tile(t + 1);
+        if (active) {
+            const float4* xy = txy + buf * (kTile / 2) + split * (slice / 2);
+            const float4* zz = tz + buf * (kTile / 4) + split * (slice / 4);
+            const int64_t j0 = t * kTile + split * slice;
+            const int cnt = (int)max64(0, min64(slice, N - j0));
+            // Eight points per iteration; the common case (no candidate below
+            // the threshold) costs one min per pair and a compare per four.
+            for (int e = 0; e < cnt; e += 8) {
+#pragma unroll
+                for (int g = 0; g < 8; g += 4) {
+                    const ulonglong2 a0 = *reinterpret_cast<const ulonglong2*>(xy + (e + g) / 2);
+                    const ulonglong2 a1 = *reinterpret_cast<const ulonglong2*>(xy + (e + g) / 2 + 1);
+                    const ulonglong2 zp = *reinterpret_cast<const ulonglong2*>(zz + (e + g) / 4);
+                    float d[4];
+                    unpack2(sqd3x2(X, Y, Z, a0.x, a0.y, zp.x), d[0], d[1]);
+                    unpack2(sqd3x2(X, Y, Z, a1.x, a1.y, zp.y), d[2], d[3]);
+                    // fminf skips NaN, which this policy drops anyway.
+                    const float m = fminf(fminf(d[0], d[1]), fminf(d[2], d[3]));
+                    if (!(m > thr) || e + g + 4 > cnt) {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            if (!(d[u] > thr) && e + g + u < cnt) {
+                                qd[qn * kThreads + tid] = d[u];
+                                qi[qn * kThreads + tid] = (uint32_t)(j0 + e + g + u);
+                                ++qn;
+                            }
+                        }
+                    }
+                }
+                if (__any_sync(__activemask(), qn > kQueue - 8)) {
+                    flush();
+                    thr = top.kth();
+                }
+            }
+        }
+        if (t + 1 < ntiles) store_tile(buf ^ 1);
+        __syncthreads();
+    }
+    if (active) flush();
+    __syncthreads();  // the merge reuses the tile and queue memory
+
+    if (S > 1) {
+        float* md = reinterpret_cast<float*>(smem4);
+        uint32_t* mi = reinterpret_cast<uint32_t*>(md + (size_t)kThreads * K);
+        if (split > 0) {
+#pragma unroll
+            for (int s2 = 0; s2 < K; ++s2) {
+                md[(size_t)tid * K + s2] = top.d[s2];
+                mi[(size_t)tid * K + s2] = top.i[s2];
+            }
+        }
+        __syncthreads();
+        if (split == 0 && active) {
+            for (int o = 1; o < S; ++o) {
+                const int src = o * qpc + ql;
+                for (int s2 = K - k; s2 < K; ++s2) {
+                    const uint32_t j = mi[(size_t)src * K + s2];
+                    if (j == kNoIndex) break;
+                    const float dd = md[(size_t)src * K + s2];
+                    if (top.full() && !before<POLICY>(dd, j, top.d[K - 1], top.i[K - 1])) break;
+                    top.offer(dd, j);
+                }
+            }
+        }
+    }
+    if (split != 0 || !active) return;
+    const size_t row = ((size_t)b * (size_t)M + (size_t)q) * (size_t)k;
+#pragma unroll
+    for (int s2 = 0; s2 < K; ++s2) {
+        const int l = s2 - top.base;
+        if (l >= 0) {
+            const bool filled = l < top.cnt;
+            const float dd = filled ? top.d[s2] : INFINITY;
+            dist[row + l] = sqrtf(dd);
+            if (sqdist) sqdist[row + l] = dd;
+            if (idx64) idx64[row + l] = filled ? (int64_t)top.i[s2] : -1;
+            if (idx32) idx32[row + l] = filled ? (int32_t)top.i[s2] : -1;
+        }
+    }
+}
+
+// --------------------------------------------------------------------------
 // Generic D kernel (feature space): the query row and the reference tile
 // both sit in shared memory; SD accumulates in increasing dimension order.
 constexpr int kFeatThreads = 128;
@@ -512,6 +668,23 @@ int launch_knn3(const float* query, const float* ref, int64_t B, int64_t M, int6
     return check_launch("knn3_kernel");
 }
 
+template <int K, int POLICY>
+int launch_knn3p(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int k,
+                 float* dist, int64_t* idx64, int32_t* idx32, float* sqdist, cudaStream_t s) {
+    const int S = choose_splits(B, M, N);
+    const int qpc = kThreads / S;
+    size_t smem = (size_t)(kTile + kTile / 2) * sizeof(float4) + (size_t)kQueue * kThreads * 8;
+    const size_t merge = (size_t)kThreads * K * 8;
+    if (merge > smem) smem = merge;
+    auto kern = knn3p_kernel<K, POLICY>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+        return fail(kCudaError, "knn: cannot raise the shared-memory limit");
+    dim3 grid((unsigned)ceil_div(M, qpc), (unsigned)B);
+    kern<<<grid, kThreads, smem, s>>>(query, ref, M, N, k, S, dist, idx64, idx32, sqdist);
+    return check_launch("knn3p_kernel");
+}
+
 template <int K>
 int launch_knnd(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int D,
                 int k, float* dist, int64_t* idx64, float* sqdist, cudaStream_t s) {
@@ -563,6 +736,12 @@ int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t 
                            workspace_bytes, s);
     if (D == 3 && k <= 32 && use_wq3(N)) {
         return launch_wq3<kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
+    }
+    if (D == 3 && k <= 32) {
+        if (k <= 4) return launch_knn3p<4, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
+        if (k <= 8) return launch_knn3p<8, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
+        if (k <= 16) return launch_knn3p<16, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
+        return launch_knn3p<32, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
     }
     if (D == 3) {
         if (k <= 4) return launch_knn3<4, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
