@@ -83,21 +83,36 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
         GROUP ? slots + (size_t)wave_cloud * 2 * G * kSlotStride : nullptr;
     unsigned* my_error = GROUP ? errors + wave_cloud : nullptr;
 
-    float px[P], py[P], pz[P], md[P];
+    // Points in packed pairs (slot s = 2 h + l is lane l of pair h), so one
+    // f32x2 pass computes two squared distances with the same per-lane
+    // rounding as sqd3.  P = 1 uses one pair with an empty second slot.
+    constexpr int PP = (P + 1) / 2;
+    constexpr int PS = 2 * PP;
+    f32x2 PX[PP], PY[PP], PZ[PP];
+    float md[PS];
 #pragma unroll
-    for (int s = 0; s < P; ++s) {
-        const int64_t j = lo + tid + (int64_t)s * nthr;
-        if (j < hi) {
-            px[s] = p[3 * j + 0];
-            py[s] = p[3 * j + 1];
-            pz[s] = p[3 * j + 2];
-            float init = INFINITY;
-            if (skip && sqd3(px[s], py[s], pz[s], 0.f, 0.f, 0.f) < 1e-3f) init = -INFINITY;
-            md[s] = init;
-        } else {
-            px[s] = py[s] = pz[s] = 0.f;
-            md[s] = -INFINITY;
+    for (int h = 0; h < PP; ++h) {
+        float c[6];
+#pragma unroll
+        for (int l = 0; l < 2; ++l) {
+            const int s = 2 * h + l;
+            const int64_t j = lo + tid + (int64_t)s * nthr;
+            if (s < P && j < hi) {
+                c[3 * l + 0] = p[3 * j + 0];
+                c[3 * l + 1] = p[3 * j + 1];
+                c[3 * l + 2] = p[3 * j + 2];
+                float init = INFINITY;
+                if (skip && sqd3(c[3 * l], c[3 * l + 1], c[3 * l + 2], 0.f, 0.f, 0.f) < 1e-3f)
+                    init = -INFINITY;
+                md[s] = init;
+            } else {
+                c[3 * l + 0] = c[3 * l + 1] = c[3 * l + 2] = 0.f;
+                md[s] = -INFINITY;
+            }
         }
+        PX[h] = pack2(c[0], c[3]);
+        PY[h] = pack2(c[1], c[4]);
+        PZ[h] = pack2(c[2], c[5]);
     }
     if (!GROUP) {
         for (int64_t e = tid; e < 3 * N; e += nthr) s_xyz[e] = p[e];
@@ -105,8 +120,14 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
     if (tid == 0) s_abort = 0;
     bool mine_nonfinite = false;
 #pragma unroll
-    for (int s = 0; s < P; ++s)
-        mine_nonfinite |= !(isfinite(px[s]) && isfinite(py[s]) && isfinite(pz[s]));
+    for (int h = 0; h < PP; ++h) {
+        float a0, a1, b0, b1, c0, c1;
+        unpack2(PX[h], a0, a1);
+        unpack2(PY[h], b0, b1);
+        unpack2(PZ[h], c0, c1);
+        mine_nonfinite |= !(isfinite(a0) && isfinite(b0) && isfinite(c0) && isfinite(a1) &&
+                            isfinite(b1) && isfinite(c1));
+    }
     bool nan_mode = __syncthreads_or(mine_nonfinite) != 0;
 
     uint32_t far = (uint32_t)start_idx;
@@ -141,13 +162,20 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
             // thread's first maximum and the ordered key is formed once.
             float bv = -INFINITY;
             uint32_t bj = 0xffffffffu;
+            const f32x2 CX = pack2(cx, cx), CY = pack2(cy, cy), CZ = pack2(cz, cz);
 #pragma unroll
-            for (int s = 0; s < P; ++s) {
-                const float d = sqd3(px[s], py[s], pz[s], cx, cy, cz);
-                md[s] = fminf(md[s], d);
-                if (md[s] > bv) {
-                    bv = md[s];
-                    bj = (uint32_t)(lo + tid + (int64_t)s * nthr);
+            for (int h = 0; h < PP; ++h) {
+                float d[2];
+                unpack2(sqd3x2(PX[h], PY[h], PZ[h], CX, CY, CZ), d[0], d[1]);
+#pragma unroll
+                for (int l = 0; l < 2; ++l) {
+                    const int s = 2 * h + l;
+                    if (s >= P) break;
+                    md[s] = fminf(md[s], d[l]);
+                    if (md[s] > bv) {
+                        bv = md[s];
+                        bj = (uint32_t)(lo + tid + (int64_t)s * nthr);
+                    }
                 }
             }
             // A lane whose points are all -inf offers its first valid point
@@ -160,7 +188,11 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
             for (int s = 0; s < P; ++s) {
                 const int64_t j = lo + tid + (int64_t)s * nthr;
                 const bool valid = j < hi;
-                const float d = sqd3(px[s], py[s], pz[s], cx, cy, cz);
+                float x0, x1, y0, y1, z0, z1;
+                unpack2(PX[s / 2], x0, x1);
+                unpack2(PY[s / 2], y0, y1);
+                unpack2(PZ[s / 2], z0, z1);
+                const float d = (s & 1) ? sqd3(x1, y1, z1, cx, cy, cz) : sqd3(x0, y0, z0, cx, cy, cz);
                 const float m = fmin_nan(md[s], d);
                 md[s] = valid ? m : md[s];
                 const uint32_t k = !valid ? 0u : (isnan(m) ? 0xffffffffu : ordered_key(m));
