@@ -172,6 +172,15 @@ MPO_API int mpo_three_interpolate_backward(const float* grad_out, const int32_t*
                                    const float* weights, int64_t B, int64_t C, int64_t M,
                                    int64_t N, float* grad_features, void* stream);
 
+/* Replaces the host bounds check of mps_pointops/pointnet2.py:130-131
+ * (torch.any((indices < 0) | (indices >= M)).item()): *flag (int32, device)
+ * becomes 1 if any of the n indices (int32, or int64 when idx_is_int64) lies
+ * outside [0, upper), else 0.  Asynchronous: the caller reads the flag after
+ * queueing the interpolation (whose kernels skip out-of-range indices) and
+ * raises then. */
+MPO_API int mpo_index_check(const void* idx, int idx_is_int64, int64_t n, int64_t upper,
+                            int32_t* flag, void* stream);
+
 /* ------------------------------------------------------------------ Chamfer
  * Replaces `chamfer_nearest_f32` / `chamfer_nearest_nd_f32`
  * (kernels/chamfer_nn.metal:13-82, 159-226) behind

@@ -11,6 +11,10 @@
 //     three indices and weights once and walks the channels, so the (B,C,N)
 //     output is written coalesced along n and each feature row (M floats,
 //     4 KB at M = 1024) stays hot in L1.
+//   * Indices outside [0, M) contribute nothing (the forward sums the valid
+//     terms, the backward skips them): callers check bounds with
+//     mpo_index_check and raise afterwards, without a host round trip before
+//     the launch, so the kernels must stay memory-safe on such input.
 //   * Backward: a CTA owns one (b, c) feature row; it scatters into a
 //     shared-memory copy of that row with shared atomics, then writes the row
 //     once -- no global atomics and no separate zero fill when the row fits
@@ -37,12 +41,13 @@ interp_fwd_kernel(const float* __restrict__ features, const int32_t* __restrict_
     const float* W = weights + (b * N + n) * 3;
     const int32_t i0 = I[0], i1 = I[1], i2 = I[2];
     const float w0 = W[0], w1 = W[1], w2 = W[2];
+    const bool v0 = i0 >= 0 && i0 < M, v1 = i1 >= 0 && i1 < M, v2 = i2 >= 0 && i2 < M;
     const int64_t c1 = min64(C, c0 + kChanPerThread);
     for (int64_t c = c0; c < c1; ++c) {
         const float* F = features + (b * C + c) * M;
-        const float p0 = __fmul_rn(__ldg(F + i0), w0);
-        const float p1 = __fmul_rn(__ldg(F + i1), w1);
-        const float p2 = __fmul_rn(__ldg(F + i2), w2);
+        const float p0 = v0 ? __fmul_rn(__ldg(F + i0), w0) : 0.f;
+        const float p1 = v1 ? __fmul_rn(__ldg(F + i1), w1) : 0.f;
+        const float p2 = v2 ? __fmul_rn(__ldg(F + i2), w2) : 0.f;
         out[(b * C + c) * N + n] = __fadd_rn(__fadd_rn(p0, p1), p2);
     }
 }
@@ -62,7 +67,10 @@ interp_bwd_smem_kernel(const float* __restrict__ grad_out, const int32_t* __rest
     for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
         const float gv = g[n];
 #pragma unroll
-        for (int t = 0; t < 3; ++t) atomicAdd(&row[I[3 * n + t]], __fmul_rn(gv, W[3 * n + t]));
+        for (int t = 0; t < 3; ++t) {
+            const int32_t m = I[3 * n + t];
+            if (m >= 0 && m < M) atomicAdd(&row[m], __fmul_rn(gv, W[3 * n + t]));
+        }
     }
     __syncthreads();
     float* dst = grad_features + (b * C + c) * M;
@@ -84,14 +92,48 @@ interp_bwd_global_kernel(const float* __restrict__ grad_out, const int32_t* __re
         const float gv = grad_out[(b * C + c) * N + n];
         float* dst = grad_features + (b * C + c) * M;
 #pragma unroll
-        for (int t = 0; t < 3; ++t) atomicAdd(dst + I[t], __fmul_rn(gv, W[t]));
+        for (int t = 0; t < 3; ++t)
+            if (I[t] >= 0 && I[t] < M) atomicAdd(dst + I[t], __fmul_rn(gv, W[t]));
     }
+}
+
+// flag = 1 if any of the n indices lies outside [0, upper).
+template <typename T>
+__global__ void index_check_kernel(const T* __restrict__ idx, int64_t n, int64_t upper,
+                                   int32_t* __restrict__ flag) {
+    bool bad = false;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t v = (int64_t)idx[e];
+        bad |= v < 0 || v >= upper;
+    }
+    if (__any_sync(FULL_MASK, bad) && (threadIdx.x & 31) == 0) *flag = 1;
 }
 
 }  // namespace
 }  // namespace mpo
 
 extern "C" {
+
+int mpo_index_check(const void* idx, int idx_is_int64, int64_t n, int64_t upper, int32_t* flag,
+                    void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(n >= 0, "negative size");
+    MPO_REQUIRE(flag, "null flag pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(flag, 0, sizeof(int32_t), s) != cudaSuccess)
+        return fail(kCudaError, "mpo_index_check: memset failed");
+    if (n == 0) return kOk;
+    MPO_REQUIRE(idx, "null pointer");
+    const unsigned grid = (unsigned)min64(ceil_div(n, 256), (int64_t)sm_count() * 8);
+    if (idx_is_int64)
+        index_check_kernel<int64_t><<<grid, 256, 0, s>>>(static_cast<const int64_t*>(idx), n,
+                                                         upper, flag);
+    else
+        index_check_kernel<int32_t><<<grid, 256, 0, s>>>(static_cast<const int32_t*>(idx), n,
+                                                         upper, flag);
+    return check_launch("index_check_kernel");
+}
 
 int mpo_three_interpolate(const float* features, const int32_t* idx, const float* weights,
                           int64_t B, int64_t C, int64_t M, int64_t N, float* out, void* stream) {

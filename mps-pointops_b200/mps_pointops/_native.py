@@ -41,6 +41,7 @@ SIGNATURES = {
     "mpo_fps": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _sz, _vp]),
     "mpo_fps_noalloc": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp]),
     "mpo_knn_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "mpo_index_check": (_int, [_vp, _int, _i64, _i64, _vp, _vp]),
     "mpo_knn": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mpo_ball_query": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp]),
     "mpo_ball_query_pointnet2": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _f32, _vp, _vp]),

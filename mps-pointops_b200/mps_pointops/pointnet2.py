@@ -64,8 +64,8 @@ def three_nn(unknown: Tensor, known: Tensor) -> tuple[Tensor, Tensor]:
 
 
 def _validate_interpolate(features: Tensor, indices: Tensor, weights: Tensor):
-    """mps_pointops/pointnet2.py:103-132 (including the bounds check on
-    caller-supplied indices, which synchronises once with the host)."""
+    """mps_pointops/pointnet2.py:103-132, except the bounds check on the
+    caller-supplied indices, which _queue_index_check runs on the device."""
     if not all(isinstance(t, Tensor) for t in (features, indices, weights)):
         raise TypeError("features, indices, and weights must be tensors")
     if features.ndim != 3:
@@ -90,9 +90,37 @@ def _validate_interpolate(features: Tensor, indices: Tensor, weights: Tensor):
         raise ValueError("three_interpolate supports at most 2**31-1 source points")
     if batch * channels * queries > (1 << 32) - 1:
         raise ValueError("three_interpolate output exceeds the native index range")
-    if indices.numel() and torch.any((indices < 0) | (indices >= points)).item():
-        raise IndexError(f"indices must lie in [0, {points})")
     return batch, channels, points, queries
+
+
+class _PendingIndexCheck:
+    """Device-side version of the reference's bounds check
+    (mps_pointops/pointnet2.py:130-131): the flag is copied to pinned memory
+    behind the check kernel, and read (waiting for that copy only) once the
+    interpolation has been queued; its kernels skip out-of-range indices."""
+
+    def __init__(self, indices: Tensor, points: int):
+        self.points = points
+        self.host = None
+        if not indices.numel():
+            return
+        flag = torch.empty(1, dtype=torch.int32, device=indices.device)
+        idx = indices.contiguous()
+        with N.on_device(indices.device):
+            N.check(N.lib().mpo_index_check(N.ptr(idx), 1 if idx.dtype == torch.int64 else 0,
+                                            idx.numel(), points, N.ptr(flag),
+                                            N.stream(indices.device)), "index check")
+            self.host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+            self.host.copy_(flag, non_blocking=True)
+            self.event = torch.cuda.Event()
+            self.event.record(torch.cuda.current_stream(indices.device))
+
+    def raise_if_bad(self) -> None:
+        if self.host is None:
+            return
+        self.event.synchronize()
+        if int(self.host[0]):
+            raise IndexError(f"indices must lie in [0, {self.points})")
 
 
 class _ThreeInterpolate(torch.autograd.Function):
@@ -142,12 +170,20 @@ def three_interpolate(features: Tensor, indices: Tensor, weights: Tensor) -> Ten
     out[b,c,n] = ((F[b,c,I0]*W0 + F[b,c,I1]*W1) + F[b,c,I2]*W2).  Backward
     accumulates grad_out*W at the selected sources (repeats summed, float
     atomics, so low bits may vary run to run); the weight gradient is an
-    explicit zero tensor.  Index validation synchronises once with the host.
+    explicit zero tensor.  The index bounds check runs on the device and is
+    read once the interpolation is queued (IndexError as in the reference).
     """
-    _validate_interpolate(features, indices, weights)
+    _, _, points, _ = _validate_interpolate(features, indices, weights)
+    if features.device.type != "cuda" and indices.numel():
+        # Same order as the reference: the bounds error before the device error.
+        if torch.any((indices < 0) | (indices >= points)).item():
+            raise IndexError(f"indices must lie in [0, {points})")
     N.require_cuda(features, "three_interpolate")
+    pending = _PendingIndexCheck(indices, points)
     index32 = indices.contiguous() if indices.dtype == torch.int32 else indices.to(torch.int32)
-    return _ThreeInterpolate.apply(features, index32, weights.contiguous())
+    out = _ThreeInterpolate.apply(features, index32, weights.contiguous())
+    pending.raise_if_bad()
+    return out
 
 
 __all__ = ["three_nn", "three_interpolate"]

@@ -114,6 +114,15 @@ def test_empty_and_bad_indices(cuda_device):  # tests/test_pointnet2.py:129-148
     with pytest.raises(IndexError):
         three_interpolate(features, torch.tensor([[[0, 4, 1]]], device=cuda_device),
                           torch.ones((1, 1, 3), device=cuda_device))
+    # The check runs on the caller's indices (device-side, read after the
+    # launch): negative int32, and int64 values that would wrap into range.
+    for bad in (torch.tensor([[[0, -1, 1]]], dtype=torch.int32),
+                torch.tensor([[[0, 2**32 + 1, 1]]], dtype=torch.int64)):
+        with pytest.raises(IndexError, match=r"\[0, 4\)"):
+            three_interpolate(features, bad.to(cuda_device), torch.ones((1, 1, 3), device=cuda_device))
+    ok = three_interpolate(features, torch.tensor([[[0, 3, 1]]], device=cuda_device),
+                           torch.ones((1, 1, 3), device=cuda_device))
+    assert ok.shape == (1, 2, 1)
     for shape in [(0, 7, 0), (2, 0, 0), (2, 0, 5)]:
         b, q, p = shape
         d, i = three_nn(torch.empty((b, q, 3), device=cuda_device),
