@@ -211,6 +211,34 @@ MPO_API int mpo_chamfer_backward(const float* x, const float* y, int64_t B, int6
                          const int64_t* idx_y, const float* grad_dist_y, float* grad_x,
                          float* grad_y, void* stream);
 
+/* Fused loss for chamfer_distance with the common reductions and no weights
+ * or normals (mps_pointops/chamfer.py:436-488, PyTorch3D conventions):
+ * the search of mpo_chamfer_nearest (same dist/idx outputs), then
+ *   per cloud  r_b = red(dist_x[b, :x_len]) (+ red(dist_y[b, :y_len]) when
+ *              bidirectional), red = sum (point_mode 0) or mean over the
+ *              valid points, empty -> divide by 1 (point_mode 1);
+ *   loss       r (batch_mode 0, (B,) floats), sum_b r_b (1) or its mean (2).
+ * Sums run in a fixed order (bit-reproducible).  Workspace:
+ * mpo_chamfer_loss_workspace_bytes.  No reference counterpart as a single
+ * call: it replaces the search plus the torch reductions of chamfer.py. */
+MPO_API size_t mpo_chamfer_loss_workspace_bytes(int64_t B, int64_t P, int64_t Q, int64_t D,
+                                                int bidirectional);
+MPO_API int mpo_chamfer_loss(const float* x, const float* y, const int64_t* x_lengths,
+                             const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q,
+                             int64_t D, int bidirectional, int point_mode, int batch_mode,
+                             float* dist_x, int64_t* idx_x, float* dist_y, int64_t* idx_y,
+                             float* loss, void* workspace, size_t workspace_bytes, void* stream);
+/* Gradient of mpo_chamfer_loss: grad_loss is the loss gradient ((B,) for
+ * batch_mode 0, one float otherwise); grad_x and grad_y are overwritten with
+ * the sums of 2 c (q - r[idx]) over the matched pairs, c = the chain-rule
+ * coefficient of each valid point's distance. */
+MPO_API int mpo_chamfer_loss_backward(const float* x, const float* y, const int64_t* x_lengths,
+                                      const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q,
+                                      int64_t D, int bidirectional, int point_mode, int batch_mode,
+                                      const int64_t* idx_x, const int64_t* idx_y,
+                                      const float* grad_loss, float* grad_x, float* grad_y,
+                                      void* stream);
+
 /* Input checks of mps_pointops/chamfer.py:79-110 in one launch: flags
  * (device int32[4]) receive {x has a non-finite valid coordinate, the same
  * for y, x_lengths outside [0,P], y_lengths outside [0,Q]}, each 0 or 1. */

@@ -183,8 +183,9 @@ nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
 // packed or not; packing halves the issue slots the distance needs, so the
 // min/ballot bookkeeping (about 3 issue slots per pair-row) is what separates
 // the kernel from the FP32 bound of 8 ops per pair.
+constexpr unsigned long long kMaxKeyAll = ~0ull;
 namespace sym {
-constexpr unsigned long long kMaxKey = ~0ull;
+constexpr unsigned long long kMaxKey = kMaxKeyAll;
 
 // Tile shape: kWarps warps, kR x-rows per lane (even: packed in pairs), kC
 // columns per row-minimum block (even), kBN y-columns per item, kMinBlocks
@@ -527,6 +528,132 @@ __global__ void check_inputs_kernel(const float* __restrict__ pts,
     if (i < len && !isfinite(pts[e])) *bad_value = 1;
 }
 
+
+// --------------------------------------------------------------------------
+// Fused loss for the common reductions (no weights, no normals).
+// finalize_reduce_kernel: one CTA per (cloud, direction) segment; it turns
+// the segment's 64-bit keys into the public (dist, idx) arrays (FROM_KEYS) or
+// reads the dist array written by a per-direction search, and sums the
+// segment's distances in a fixed order (strided per thread, then a fixed
+// tree) -> partial[b * 2 + dir].  loss_kernel then combines the partials in
+// a fixed order, so the loss is bit-reproducible from run to run.
+constexpr int kRedThreads = 256;
+
+template <bool FROM_KEYS>
+__global__ void __launch_bounds__(kRedThreads)
+finalize_reduce_kernel(const unsigned long long* __restrict__ keys_x,
+                       const unsigned long long* __restrict__ keys_y,
+                       const int64_t* __restrict__ xl, const int64_t* __restrict__ yl, int64_t B,
+                       int64_t P, int64_t Q, float* __restrict__ dist_x,
+                       int64_t* __restrict__ idx_x, float* __restrict__ dist_y,
+                       int64_t* __restrict__ idx_y, float* __restrict__ partial) {
+    __shared__ float s_red[kRedThreads];
+    const int64_t b = blockIdx.x;
+    const int dir = blockIdx.y;
+    const int64_t M = dir ? Q : P, Nn = dir ? P : Q;
+    const int64_t* self_l = dir ? yl : xl;
+    const int64_t* other_l = dir ? xl : yl;
+    const unsigned long long* keys = dir ? keys_y : keys_x;
+    float* dist = dir ? dist_y : dist_x;
+    int64_t* idx = dir ? idx_y : idx_x;
+    const int64_t len = self_l ? min64(max64(self_l[b], 0), M) : M;
+    const int64_t olen = other_l ? min64(max64(other_l[b], 0), Nn) : Nn;
+    float acc = 0.f;
+    for (int64_t i = threadIdx.x; i < M; i += kRedThreads) {
+        const int64_t e = b * M + i;
+        float d;
+        if (FROM_KEYS) {
+            const unsigned long long key = keys[e];
+            const bool valid = i < len && olen > 0 && key != kMaxKeyAll;
+            d = valid ? __uint_as_float((unsigned)(key >> 32)) : 0.f;
+            dist[e] = d;
+            idx[e] = valid ? (int64_t)(key & 0xffffffffull) : -1;
+        } else {
+            d = i < len ? dist[e] : 0.f;
+        }
+        acc = __fadd_rn(acc, d);
+    }
+    s_red[threadIdx.x] = acc;
+    __syncthreads();
+    for (int w = kRedThreads / 2; w >= 1; w >>= 1) {
+        if (threadIdx.x < w) s_red[threadIdx.x] = __fadd_rn(s_red[threadIdx.x], s_red[threadIdx.x + w]);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) partial[b * 2 + dir] = s_red[0];
+}
+
+// point_mode: 0 sum, 1 mean over valid points; batch_mode: 0 none (loss[b]),
+// 1 sum, 2 mean.  One thread per cloud, then thread 0 sums in order.
+__global__ void loss_kernel(const float* __restrict__ partial, const int64_t* __restrict__ xl,
+                            const int64_t* __restrict__ yl, int64_t B, int64_t P, int64_t Q,
+                            int bidirectional, int point_mode, int batch_mode,
+                            float* __restrict__ per_cloud, float* __restrict__ loss) {
+    for (int64_t b = threadIdx.x; b < B; b += blockDim.x) {
+        float v = partial[b * 2 + 0];
+        if (point_mode == 1) {
+            const int64_t n = xl ? min64(max64(xl[b], 0), P) : P;
+            v = __fdiv_rn(v, (float)max64(n, 1));
+        }
+        if (bidirectional) {
+            float w = partial[b * 2 + 1];
+            if (point_mode == 1) {
+                const int64_t n = yl ? min64(max64(yl[b], 0), Q) : Q;
+                w = __fdiv_rn(w, (float)max64(n, 1));
+            }
+            v = __fadd_rn(v, w);
+        }
+        per_cloud[b] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    if (batch_mode == 0) {
+        for (int64_t b = 0; b < B; ++b) loss[b] = per_cloud[b];
+        return;
+    }
+    float t = 0.f;
+    for (int64_t b = 0; b < B; ++b) t = __fadd_rn(t, per_cloud[b]);
+    if (batch_mode == 2) t = __fdiv_rn(t, (float)max64(B, 1));
+    loss[0] = t;
+}
+
+// Backward of the fused loss: element e of the x rows (then of the y rows)
+// gets coefficient c = g_b * (1/len for the mean) and adds 2c(q - r[idx]) to
+// its own gradient and -2c(q - r[idx]) to its match's.
+__global__ void loss_bwd_kernel(const float* __restrict__ x, const float* __restrict__ y,
+                                const int64_t* __restrict__ xl, const int64_t* __restrict__ yl,
+                                int64_t B, int64_t P, int64_t Q, int64_t D, int bidirectional,
+                                int point_mode, int batch_mode, const int64_t* __restrict__ idx_x,
+                                const int64_t* __restrict__ idx_y,
+                                const float* __restrict__ grad_loss, float* __restrict__ grad_x,
+                                float* __restrict__ grad_y) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nx = B * P;
+    const int64_t total = nx + (bidirectional ? B * Q : 0);
+    if (e >= total) return;
+    const bool dir = e >= nx;
+    const int64_t M = dir ? Q : P, Nn = dir ? P : Q;
+    const int64_t row = dir ? e - nx : e;
+    const int64_t b = row / M, i = row % M;
+    const int64_t* self_l = dir ? yl : xl;
+    const int64_t len = self_l ? min64(max64(self_l[b], 0), M) : M;
+    if (i >= len) return;
+    const int64_t j = (dir ? idx_y : idx_x)[row];
+    if (j < 0) return;
+    float c = batch_mode == 0 ? grad_loss[b] : grad_loss[0];
+    if (batch_mode == 2) c = __fdiv_rn(c, (float)max64(B, 1));
+    if (point_mode == 1) c = __fdiv_rn(c, (float)max64(len, 1));
+    c = 2.0f * c;
+    const float* qp = (dir ? y : x) + row * D;
+    const float* rp = (dir ? x : y) + (b * Nn + j) * D;
+    float* gq = (dir ? grad_y : grad_x) + row * D;
+    float* gr = (dir ? grad_x : grad_y) + (b * Nn + j) * D;
+    for (int64_t t = 0; t < D; ++t) {
+        const float g = __fmul_rn(__fsub_rn(qp[t], rp[t]), c);
+        atomicAdd(gq + t, g);
+        atomicAdd(gr + t, -g);
+    }
+}
+
 }  // namespace
 }  // namespace mpo
 
@@ -571,16 +698,21 @@ static int nearest_dir(const float* q, const float* r, const int64_t* ql, const 
     return check_launch("nearestd_kernel");
 }
 
-int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths,
-                        const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q, int64_t D,
-                        int bidirectional, float* dist_x, int64_t* idx_x, float* dist_y,
-                        int64_t* idx_y, void* workspace, size_t workspace_bytes, void* stream) {
-    using namespace mpo;
-    MPO_REQUIRE(B >= 0 && P >= 0 && Q >= 0 && D >= 1, "bad sizes");
-    MPO_REQUIRE(B <= 65535, "batch must be at most 65535");
-    MPO_REQUIRE(P < (int64_t)0x7fffffff && Q < (int64_t)0x7fffffff, "clouds must be below 2**31");
-    cudaStream_t s = (cudaStream_t)stream;
-    if (B == 0) return kOk;
+}  // extern "C"
+
+namespace mpo {
+namespace {
+// The search shared by mpo_chamfer_nearest and mpo_chamfer_loss.  On the
+// symmetric path it leaves 64-bit keys in the workspace (*keys_x/*keys_y set,
+// dist/idx not yet written); otherwise the per-direction kernels write
+// dist/idx directly (*keys_x = nullptr).
+int chamfer_search(const float* x, const float* y, const int64_t* x_lengths,
+                   const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q, int64_t D,
+                   int bidirectional, float* dist_x, int64_t* idx_x, float* dist_y,
+                   int64_t* idx_y, void* workspace, size_t workspace_bytes, cudaStream_t s,
+                   unsigned long long** keys_x_out, unsigned long long** keys_y_out,
+                   const char* who) {
+    *keys_x_out = *keys_y_out = nullptr;
     if (!sym::use_sym(P, Q, D)) {
         int st = nearest_dir(x, y, x_lengths, y_lengths, B, P, Q, D, dist_x, idx_x, s);
         if (st || !bidirectional) return st;
@@ -588,27 +720,62 @@ int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths
     }
     const size_t need = sym::scratch_bytes(B, P, Q);
     if (workspace == nullptr || workspace_bytes < need)
-        return fail(kWorkspaceTooSmall, "mpo_chamfer_nearest: workspace must hold " +
+        return fail(kWorkspaceTooSmall, std::string(who) + ": workspace must hold " +
                                             std::to_string(need) + " bytes");
     unsigned long long* keys_x = reinterpret_cast<unsigned long long*>(workspace);
     unsigned long long* keys_y = keys_x + (size_t)B * P;
     unsigned* counter = reinterpret_cast<unsigned*>(keys_y + (size_t)B * Q);
     if (cudaMemsetAsync(keys_x, 0xff, (size_t)B * (P + Q) * 8, s) != cudaSuccess ||
         cudaMemsetAsync(counter, 0, sizeof(unsigned), s) != cudaSuccess)
-        return fail(kCudaError, "mpo_chamfer_nearest: scratch reset failed");
+        return fail(kCudaError, std::string(who) + ": scratch reset failed");
     auto kern = sym::chamfer_sym3_kernel<MPO_SYM_DEFAULT>;
     using Sh = sym::Default;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)Sh::kSmem) != cudaSuccess)
-        return fail(kCudaError, "mpo_chamfer_nearest: shared-memory limit");
+        return fail(kCudaError, std::string(who) + ": shared-memory limit");
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Sh::kThreads, Sh::kSmem);
     const int64_t items = B * ceil_div(P, Sh::kBM) * ceil_div(Q, Sh::kCols);
     const int64_t grid = min64(items, (int64_t)sm_count() * max64(per_sm, 1));
     kern<<<(unsigned)grid, Sh::kThreads, Sh::kSmem, s>>>(x, y, x_lengths, y_lengths, B, P, Q,
                                                          keys_x, keys_y, counter);
-    int st = check_launch("chamfer_sym3_kernel");
+    *keys_x_out = keys_x;
+    *keys_y_out = keys_y;
+    return check_launch("chamfer_sym3_kernel");
+}
+
+int check_sizes(int64_t B, int64_t P, int64_t Q, int64_t D, const char* who) {
+    if (!(B >= 0 && P >= 0 && Q >= 0 && D >= 1))
+        return fail(kInvalidArgument, std::string(who) + ": bad sizes");
+    if (B > 65535) return fail(kInvalidArgument, std::string(who) + ": batch must be at most 65535");
+    if (P >= (int64_t)0x7fffffff || Q >= (int64_t)0x7fffffff)
+        return fail(kInvalidArgument, std::string(who) + ": clouds must be below 2**31");
+    return kOk;
+}
+
+// Loss workspace: the search scratch, then partial[B][2] and per_cloud[B].
+size_t loss_extra_offset(int64_t B, int64_t P, int64_t Q, int64_t D) {
+    return sym::use_sym(P, Q, D) ? (sym::scratch_bytes(B, P, Q) + 255) / 256 * 256 : 0;
+}
+}  // namespace
+}  // namespace mpo
+
+extern "C" {
+
+int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths,
+                        const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q, int64_t D,
+                        int bidirectional, float* dist_x, int64_t* idx_x, float* dist_y,
+                        int64_t* idx_y, void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace mpo;
+    int st = check_sizes(B, P, Q, D, "mpo_chamfer_nearest");
     if (st) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (B == 0) return kOk;
+    unsigned long long *keys_x, *keys_y;
+    st = chamfer_search(x, y, x_lengths, y_lengths, B, P, Q, D, bidirectional, dist_x, idx_x,
+                        dist_y, idx_y, workspace, workspace_bytes, s, &keys_x, &keys_y,
+                        "mpo_chamfer_nearest");
+    if (st || keys_x == nullptr) return st;
     sym::finalize_kernel<<<(unsigned)ceil_div(B * P, 256), 256, 0, s>>>(
         keys_x, x_lengths, y_lengths, B, P, Q, dist_x, idx_x);
     st = check_launch("chamfer finalize_kernel");
@@ -616,6 +783,82 @@ int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths
     sym::finalize_kernel<<<(unsigned)ceil_div(B * Q, 256), 256, 0, s>>>(
         keys_y, y_lengths, x_lengths, B, Q, P, dist_y, idx_y);
     return check_launch("chamfer finalize_kernel");
+}
+
+size_t mpo_chamfer_loss_workspace_bytes(int64_t B, int64_t P, int64_t Q, int64_t D,
+                                        int bidirectional) {
+    (void)bidirectional;
+    if (B <= 0) return 0;
+    return mpo::loss_extra_offset(B, P, Q, D) + (size_t)B * 3 * sizeof(float);
+}
+
+int mpo_chamfer_loss(const float* x, const float* y, const int64_t* x_lengths,
+                     const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q, int64_t D,
+                     int bidirectional, int point_mode, int batch_mode, float* dist_x,
+                     int64_t* idx_x, float* dist_y, int64_t* idx_y, float* loss,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace mpo;
+    int st = check_sizes(B, P, Q, D, "mpo_chamfer_loss");
+    if (st) return st;
+    MPO_REQUIRE(point_mode == 0 || point_mode == 1, "point_mode must be 0 (sum) or 1 (mean)");
+    MPO_REQUIRE(batch_mode >= 0 && batch_mode <= 2, "batch_mode must be 0, 1 or 2");
+    MPO_REQUIRE(loss, "null loss pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (B == 0) {
+        if (batch_mode != 0 && cudaMemsetAsync(loss, 0, sizeof(float), s) != cudaSuccess)
+            return fail(kCudaError, "mpo_chamfer_loss: memset failed");
+        return kOk;
+    }
+    const size_t need = mpo_chamfer_loss_workspace_bytes(B, P, Q, D, bidirectional);
+    if (workspace == nullptr || workspace_bytes < need)
+        return fail(kWorkspaceTooSmall,
+                    "mpo_chamfer_loss: workspace must hold " + std::to_string(need) + " bytes");
+    unsigned long long *keys_x, *keys_y;
+    st = chamfer_search(x, y, x_lengths, y_lengths, B, P, Q, D, bidirectional, dist_x, idx_x,
+                        dist_y, idx_y, workspace, workspace_bytes, s, &keys_x, &keys_y,
+                        "mpo_chamfer_loss");
+    if (st) return st;
+    float* partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) +
+                                              loss_extra_offset(B, P, Q, D));
+    float* per_cloud = partial + 2 * B;
+    dim3 grid((unsigned)B, bidirectional ? 2u : 1u);
+    if (keys_x)
+        finalize_reduce_kernel<true><<<grid, kRedThreads, 0, s>>>(
+            keys_x, keys_y, x_lengths, y_lengths, B, P, Q, dist_x, idx_x, dist_y, idx_y, partial);
+    else
+        finalize_reduce_kernel<false><<<grid, kRedThreads, 0, s>>>(
+            nullptr, nullptr, x_lengths, y_lengths, B, P, Q, dist_x, idx_x, dist_y, idx_y,
+            partial);
+    st = check_launch("chamfer finalize_reduce_kernel");
+    if (st) return st;
+    loss_kernel<<<1, 256, 0, s>>>(partial, x_lengths, y_lengths, B, P, Q, bidirectional,
+                                  point_mode, batch_mode, per_cloud, loss);
+    return check_launch("chamfer loss_kernel");
+}
+
+int mpo_chamfer_loss_backward(const float* x, const float* y, const int64_t* x_lengths,
+                              const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q,
+                              int64_t D, int bidirectional, int point_mode, int batch_mode,
+                              const int64_t* idx_x, const int64_t* idx_y,
+                              const float* grad_loss, float* grad_x, float* grad_y,
+                              void* stream) {
+    using namespace mpo;
+    int st = check_sizes(B, P, Q, D, "mpo_chamfer_loss_backward");
+    if (st) return st;
+    MPO_REQUIRE((grad_x || B * P * D == 0) && (grad_y || B * Q * D == 0), "null gradient pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (B * P * D > 0 && cudaMemsetAsync(grad_x, 0, sizeof(float) * B * P * D, s) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_loss_backward: memset failed");
+    if (B * Q * D > 0 && cudaMemsetAsync(grad_y, 0, sizeof(float) * B * Q * D, s) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_loss_backward: memset failed");
+    const int64_t total = B * P + (bidirectional ? B * Q : 0);
+    if (total == 0) return kOk;
+    MPO_REQUIRE(grad_loss && (idx_x || B * P == 0) && (idx_y || !bidirectional || B * Q == 0),
+                "null pointer");
+    loss_bwd_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(
+        x, y, x_lengths, y_lengths, B, P, Q, D, bidirectional, point_mode, batch_mode, idx_x,
+        idx_y, grad_loss, grad_x, grad_y);
+    return check_launch("chamfer loss_bwd_kernel");
 }
 
 int mpo_chamfer_backward(const float* x, const float* y, int64_t B, int64_t P, int64_t Q,

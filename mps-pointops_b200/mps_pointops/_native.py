@@ -51,6 +51,11 @@ SIGNATURES = {
     "mpo_three_interpolate": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "mpo_three_interpolate_backward": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "mpo_chamfer_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _int]),
+    "mpo_chamfer_loss_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _int]),
+    "mpo_chamfer_loss": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _int,
+                                _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "mpo_chamfer_loss_backward": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int,
+                                         _int, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mpo_chamfer_nearest": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp,
                                    _vp, _vp, _vp, _sz, _vp]),
     "mpo_chamfer_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp,

@@ -160,6 +160,56 @@ class _NearestSquared(torch.autograd.Function):
         return grad_x, grad_y, None, None, None
 
 
+class _ChamferLoss(torch.autograd.Function):
+    """Fused search + reduction for the common case (no weights, no normals,
+    point_reduction mean/sum): one native call forward, one backward, instead
+    of the search plus a chain of torch reductions (mps_pointops/chamfer.py:
+    436-488).  The loss sums run in a fixed order (reproducible)."""
+
+    @staticmethod
+    def forward(ctx, x, y, lx, ly, bidirectional: bool, point_mode: int, batch_mode: int):
+        B, P, D = x.shape
+        Q = y.shape[1]
+        dev = x.device
+        dist_x = torch.empty((B, P), dtype=torch.float32, device=dev)
+        idx_x = torch.empty((B, P), dtype=torch.long, device=dev)
+        dist_y = torch.empty((B, Q if bidirectional else 0), dtype=torch.float32, device=dev)
+        idx_y = torch.empty((B, Q if bidirectional else 0), dtype=torch.long, device=dev)
+        loss = torch.empty((B,) if batch_mode == 0 else (), dtype=torch.float32, device=dev)
+        xc, yc = x.contiguous(), y.contiguous()
+        lib = N.lib()
+        with N.on_device(dev):
+            ws = N.workspace(lib.mpo_chamfer_loss_workspace_bytes(B, P, Q, D, int(bidirectional)),
+                             dev)
+            N.check(N.timed("chamfer_nearest", dev, lib.mpo_chamfer_loss,
+                            N.ptr(xc), N.ptr(yc), N.ptr(lx), N.ptr(ly), B, P, Q, D,
+                            int(bidirectional), point_mode, batch_mode, N.ptr(dist_x),
+                            N.ptr(idx_x), N.ptr(dist_y), N.ptr(idx_y), N.ptr(loss), N.ptr(ws),
+                            0 if ws is None else ws.numel(), N.stream(dev)), "chamfer loss")
+        ctx.save_for_backward(xc, yc, idx_x, idx_y)
+        ctx.lengths = (lx, ly)
+        ctx.modes = (bidirectional, point_mode, batch_mode)
+        return loss
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g):
+        x, y, idx_x, idx_y = ctx.saved_tensors
+        lx, ly = ctx.lengths
+        bidirectional, point_mode, batch_mode = ctx.modes
+        B, P, D = x.shape
+        Q = y.shape[1]
+        grad_x = torch.empty_like(x)
+        grad_y = torch.empty_like(y)
+        gl = g.float().contiguous()
+        with N.on_device(x.device):
+            N.check(N.lib().mpo_chamfer_loss_backward(
+                N.ptr(x), N.ptr(y), N.ptr(lx), N.ptr(ly), B, P, Q, D, int(bidirectional),
+                point_mode, batch_mode, N.ptr(idx_x), N.ptr(idx_y), N.ptr(gl), N.ptr(grad_x),
+                N.ptr(grad_y), N.stream(x.device)), "chamfer loss backward")
+        return grad_x, grad_y, None, None, None, None, None
+
+
 def _full_lengths(points: Tensor, lengths: Tensor | None) -> Tensor:
     if lengths is not None:
         return lengths
@@ -259,6 +309,14 @@ def chamfer_distance(
                                      single_directional)
     if norm == 1:
         raise NotImplementedError("norm=1 (L1) Chamfer is not implemented in the B200 build")
+
+    if weights is None and not return_normals and point_reduction in ("mean", "sum"):
+        loss = _ChamferLoss.apply(x, y, lx, ly, not single_directional,
+                                  1 if point_reduction == "mean" else 0,
+                                  {None: 0, "sum": 1, "mean": 2}[batch_reduction])
+        if pending is not None:
+            pending.raise_if_bad()
+        return loss, None
 
     dx, dy, ix, iy = _NearestSquared.apply(x, y, lx, ly, not single_directional)
     if pending is not None:
