@@ -511,21 +511,33 @@ __global__ void chamfer_bwd_kernel(const float* __restrict__ qpts, const float* 
     }
 }
 
-__global__ void check_inputs_kernel(const float* __restrict__ pts,
-                                    const int64_t* __restrict__ lengths, int64_t B, int64_t M,
-                                    int64_t D, int32_t* __restrict__ bad_value,
-                                    int32_t* __restrict__ bad_length) {
-    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (lengths && e < B) {
-        const int64_t len = lengths[e];
-        if (len < 0 || len > M) *bad_length = 1;
+// Both clouds in one grid-stride launch: flags {x value, y value, x length,
+// y length}; a warp sets a flag once.
+__global__ void check_inputs_kernel(const float* __restrict__ x, const float* __restrict__ y,
+                                    const int64_t* __restrict__ xl,
+                                    const int64_t* __restrict__ yl, int64_t B, int64_t P,
+                                    int64_t Q, int64_t D, int32_t* __restrict__ flags) {
+    const int64_t nx = B * P * D, total = nx + B * Q * D;
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t0 < B) {
+        if (xl && (xl[t0] < 0 || xl[t0] > P)) flags[2] = 1;
+        if (yl && (yl[t0] < 0 || yl[t0] > Q)) flags[3] = 1;
     }
-    if (e >= B * M * D) return;
-    const int64_t row = e / D;
-    const int64_t b = row / M;
-    const int64_t i = row % M;
-    const int64_t len = lengths ? lengths[b] : M;
-    if (i < len && !isfinite(pts[e])) *bad_value = 1;
+    bool bad_x = false, bad_y = false;
+    for (int64_t e = t0; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const bool is_y = e >= nx;
+        const int64_t f = is_y ? e - nx : e;
+        const int64_t M = is_y ? Q : P;
+        const int64_t row = f / D, b = row / M, i = row % M;
+        const int64_t* l = is_y ? yl : xl;
+        const int64_t len = l ? l[b] : M;
+        if (i < len && !isfinite((is_y ? y : x)[f])) {
+            bad_x |= !is_y;
+            bad_y |= is_y;
+        }
+    }
+    if (__any_sync(FULL_MASK, bad_x) && (threadIdx.x & 31) == 0) flags[0] = 1;
+    if (__any_sync(FULL_MASK, bad_y) && (threadIdx.x & 31) == 0) flags[1] = 1;
 }
 
 
@@ -896,19 +908,11 @@ int mpo_chamfer_check_inputs(const float* x, const float* y, const int64_t* x_le
     cudaStream_t s = (cudaStream_t)stream;
     if (cudaMemsetAsync(flags, 0, 4 * sizeof(int32_t), s) != cudaSuccess)
         return fail(kCudaError, "mpo_chamfer_check_inputs: memset failed");
-    const int64_t nx = max64(B * P * D, B), ny = max64(B * Q * D, B);
-    if (nx > 0) {
-        check_inputs_kernel<<<(unsigned)ceil_div(nx, 256), 256, 0, s>>>(x, x_lengths, B, P, D,
-                                                                          flags + 0, flags + 2);
-        int st = check_launch("check_inputs_kernel");
-        if (st) return st;
-    }
-    if (ny > 0) {
-        check_inputs_kernel<<<(unsigned)ceil_div(ny, 256), 256, 0, s>>>(y, y_lengths, B, Q, D,
-                                                                          flags + 1, flags + 3);
-        return check_launch("check_inputs_kernel");
-    }
-    return kOk;
+    const int64_t total = max64(B * (P + Q) * D, B);
+    if (total == 0) return kOk;
+    const unsigned grid = (unsigned)min64(ceil_div(total, 256), (int64_t)sm_count() * 8);
+    check_inputs_kernel<<<grid, 256, 0, s>>>(x, y, x_lengths, y_lengths, B, P, Q, D, flags);
+    return check_launch("check_inputs_kernel");
 }
 
 }  // extern "C"
