@@ -21,34 +21,44 @@
 
 #include "../../include/mpo_b200.h"
 #include "mpo_common.cuh"
+#include "segments.cuh"
 
 namespace mpo {
 namespace {
 
 constexpr int kWarpsPerCta = 8;
 
-template <bool POINTNET2>
+template <bool POINTNET2, bool FLAT>
 __global__ void __launch_bounds__(32 * kWarpsPerCta)
 ball_query_kernel(const float* __restrict__ query, const float* __restrict__ ref,
                   const int64_t* __restrict__ query_lengths,
-                  const int64_t* __restrict__ ref_lengths, int64_t M, int64_t N, int64_t K,
-                  float r2, float* __restrict__ dist2, int64_t* __restrict__ idx64,
+                  const int64_t* __restrict__ ref_lengths, Layout L, int64_t K, float r2,
+                  int ignore_same, float* __restrict__ dist2, int64_t* __restrict__ idx64,
                   int32_t* __restrict__ idx32) {
     const int lane = threadIdx.x & 31;
-    const int64_t q = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
-    const int b = blockIdx.y;
-    if (q >= M) return;
-    const size_t row = ((size_t)b * (size_t)M + (size_t)q) * (size_t)K;
-    const int64_t ql = query_lengths ? query_lengths[b] : M;
-    const int64_t nl = ref_lengths ? min64(ref_lengths[b], N) : N;
+    Span sp;
+    if (!locate<FLAT>(L, kWarpsPerCta, sp)) return;
+    const int64_t q = sp.q0 + (threadIdx.x >> 5);  // global query row
+    if (q >= sp.q1) return;
+    const size_t row = (size_t)q * (size_t)K;
+    int64_t nl = sp.n;
+    bool live = true;
+    if (!FLAT) {
+        const int64_t b = blockIdx.y;
+        if (query_lengths) live = q - b * L.M < query_lengths[b];
+        if (ref_lengths) nl = min64(ref_lengths[b], L.N);
+    }
     const unsigned below = (1u << lane) - 1u;
 
     int64_t found = 0;
     int64_t first = -1;
-    if (q < ql) {
-        const float* qp = query + ((size_t)b * (size_t)M + (size_t)q) * 3;
+    if (live) {
+        const float* qp = query + (size_t)q * 3;
         const float qx = qp[0], qy = qp[1], qz = qp[2];
-        const float* __restrict__ r = ref + (size_t)b * (size_t)N * 3;
+        const float* __restrict__ r = ref + (size_t)sp.r0 * 3;
+        // A flat search with ignore_same skips the reference whose global row
+        // equals the query's (local row `self`), before the cap.
+        const int64_t self = (FLAT && ignore_same) ? q - sp.obase : -1;
         // Four 32-point chunks per iteration: their loads are independent,
         // so a lane has 12 loads in flight; hits are still ranked in input
         // order chunk by chunk.
@@ -64,7 +74,7 @@ ball_query_kernel(const float* __restrict__ query, const float* __restrict__ ref
 #pragma unroll
             for (int u = 0; u < kU; ++u) {
                 const int64_t j = j0 + u * 32 + lane;
-                const bool hit = j < nl && d[u] < r2;
+                const bool hit = j < nl && d[u] < r2 && j != self;
                 const unsigned mask = __ballot_sync(FULL_MASK, hit);
                 if (mask == 0u) continue;
                 if (first < 0) first = j0 + u * 32 + (__ffs(mask) - 1);
@@ -73,8 +83,8 @@ ball_query_kernel(const float* __restrict__ query, const float* __restrict__ ref
                     if (POINTNET2) {
                         idx32[row + slot] = (int32_t)j;
                     } else {
-                        idx64[row + slot] = j;
-                        dist2[row + slot] = d[u];
+                        idx64[row + slot] = sp.obase + j;
+                        if (dist2) dist2[row + slot] = d[u];
                     }
                 }
                 found += __popc(mask);
@@ -88,7 +98,7 @@ ball_query_kernel(const float* __restrict__ query, const float* __restrict__ ref
             idx32[row + s] = first < 0 ? 0 : (int32_t)first;
         } else {
             idx64[row + s] = -1;
-            dist2[row + s] = 0.f;
+            if (dist2) dist2[row + s] = 0.f;
         }
     }
 }
@@ -153,9 +163,33 @@ int mpo_ball_query(const float* query, const float* ref, const int64_t* query_le
     MPO_REQUIRE(query && dist2 && idx && (ref || N == 0), "null pointer");
     MPO_REQUIRE(B <= 65535, "batch must be at most 65535");
     dim3 grid((unsigned)ceil_div(M, kWarpsPerCta), (unsigned)B);
-    ball_query_kernel<false><<<grid, 32 * kWarpsPerCta, 0, (cudaStream_t)stream>>>(
-        query, ref, query_lengths, ref_lengths, M, N, K, radius_sq, dist2, idx, nullptr);
+    ball_query_kernel<false, false><<<grid, 32 * kWarpsPerCta, 0, (cudaStream_t)stream>>>(
+        query, ref, query_lengths, ref_lengths, dense_layout(M, N), K, radius_sq, 0, dist2, idx,
+        nullptr);
     return check_launch("ball_query_kernel");
+}
+
+int mpo_flat_radius(const float* x, const float* y, const int64_t* ptr_x, const int64_t* ptr_y,
+                    int64_t segments, int64_t nx, int64_t ny, float radius_sq,
+                    int64_t max_neighbors, int ignore_same_index, int64_t* out, int32_t* status,
+                    void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(segments >= 0 && nx >= 0 && ny >= 0 && max_neighbors >= 0, "negative size");
+    MPO_REQUIRE(status != nullptr, "status must not be null");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(status, 0, sizeof(int32_t), s) != cudaSuccess)
+        return fail(kCudaError, "mpo_flat_radius: status reset failed");
+    if (ny == 0 || max_neighbors == 0) return kOk;
+    MPO_REQUIRE(segments >= 1, "a nonempty query set needs at least one segment");
+    MPO_REQUIRE(y && ptr_x && ptr_y && out && (x || nx == 0), "null pointer");
+    int st = flat_offsets_check(ptr_y, ptr_x, segments, ny, nx, status, s);
+    if (st) return st;
+    Layout L{ny, nx, ptr_y, ptr_x, segments, status};
+    const dim3 grid((unsigned)flat_tiles(ny, segments, kWarpsPerCta));
+    ball_query_kernel<false, true><<<grid, 32 * kWarpsPerCta, 0, s>>>(
+        y, x, nullptr, nullptr, L, max_neighbors, radius_sq, ignore_same_index ? 1 : 0, nullptr,
+        out, nullptr);
+    return check_launch("ball_query_kernel<flat>");
 }
 
 int mpo_ball_query_pointnet2(const float* xyz, const float* new_xyz, int64_t B, int64_t N,
@@ -167,8 +201,9 @@ int mpo_ball_query_pointnet2(const float* xyz, const float* new_xyz, int64_t B, 
     MPO_REQUIRE(new_xyz && idx && (xyz || N == 0), "null pointer");
     MPO_REQUIRE(B <= 65535, "batch must be at most 65535");
     dim3 grid((unsigned)ceil_div(npoint, kWarpsPerCta), (unsigned)B);
-    ball_query_kernel<true><<<grid, 32 * kWarpsPerCta, 0, (cudaStream_t)stream>>>(
-        new_xyz, xyz, nullptr, nullptr, npoint, N, nsample, radius_sq, nullptr, nullptr, idx);
+    ball_query_kernel<true, false><<<grid, 32 * kWarpsPerCta, 0, (cudaStream_t)stream>>>(
+        new_xyz, xyz, nullptr, nullptr, dense_layout(npoint, N), nsample, radius_sq, 0, nullptr,
+        nullptr, idx);
     return check_launch("ball_query_kernel<pointnet2>");
 }
 

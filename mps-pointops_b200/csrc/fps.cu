@@ -56,12 +56,22 @@ inline size_t group_bytes(int64_t clouds, int64_t G) {
     return (size_t)clouds * 2 * (size_t)G * 8 * kSlotStride + (size_t)clouds * 8;
 }
 
-template <int P, bool GROUP>
+// Flat (ragged) batches of the torch_cluster API: cloud b is the rows
+// [ptr[b], ptr[b+1]) of xyz, its samples go to out[out_ptr[b] .. out_ptr[b+1])
+// as global row numbers, starting from the local index starts[b].
+struct FlatFps {
+    const int64_t* ptr;
+    const int64_t* out_ptr;
+    const int64_t* starts;
+    int64_t total_n, total_out, max_len;
+};
+
+template <int P, bool GROUP, bool FLAT>
 __global__ void __launch_bounds__(kMaxThreads, 1)
 fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t start_idx,
            int skip, int out_int32, void* __restrict__ out, int G, int64_t per_cta,
            int cloud_offset, unsigned long long* __restrict__ slots,
-           unsigned* __restrict__ errors, int32_t* __restrict__ status) {
+           unsigned* __restrict__ errors, int32_t* __restrict__ status, FlatFps flat) {
     extern __shared__ float s_xyz[];  // G == 1 only: the cloud, 3 floats per point
     __shared__ uint32_t s_key[2][32];
     __shared__ uint32_t s_idx[2][32];
@@ -76,9 +86,27 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
     const int warp = tid >> 5;
     const int nwarps = blockDim.x >> 5;
     const int nthr = blockDim.x;
-    const float* __restrict__ p = xyz + (size_t)b * (size_t)N * 3;
+    // Rows of this cloud, its sample count and first sample, where its
+    // samples go, and the value added to a local index on output.
+    int64_t base = (int64_t)b * N, n = N, np = npoint, start = start_idx;
+    int64_t obase = (int64_t)b * npoint, vbase = 0;
+    if (FLAT) {
+        base = flat.ptr[b];
+        n = flat.ptr[b + 1] - base;
+        obase = flat.out_ptr[b];
+        np = flat.out_ptr[b + 1] - obase;
+        start = flat.starts[b];
+        vbase = base;
+        if (np == 0) return;  // the same decision in every CTA of the cloud
+        if (!(base >= 0 && n >= 1 && n <= flat.max_len && base + n <= flat.total_n &&
+              obase >= 0 && np > 0 && obase + np <= flat.total_out && start >= 0 && start < n)) {
+            if (tid == 0 && g == 0 && status) atomicExch(status, 2);
+            return;
+        }
+    }
+    const float* __restrict__ p = xyz + (size_t)base * 3;
     const int64_t lo = (int64_t)g * per_cta;
-    const int64_t hi = min64(N, lo + per_cta);
+    const int64_t hi = min64(n, lo + per_cta);
     unsigned long long* my_slots =
         GROUP ? slots + (size_t)wave_cloud * 2 * G * kSlotStride : nullptr;
     unsigned* my_error = GROUP ? errors + wave_cloud : nullptr;
@@ -115,7 +143,7 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
         PZ[h] = pack2(c[2], c[5]);
     }
     if (!GROUP) {
-        for (int64_t e = tid; e < 3 * N; e += nthr) s_xyz[e] = p[e];
+        for (int64_t e = tid; e < 3 * n; e += nthr) s_xyz[e] = p[e];
     }
     if (tid == 0) s_abort = 0;
     bool mine_nonfinite = false;
@@ -130,7 +158,7 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
     }
     bool nan_mode = __syncthreads_or(mine_nonfinite) != 0;
 
-    uint32_t far = (uint32_t)start_idx;
+    uint32_t far = (uint32_t)start;
     float cx, cy, cz;
     if (!GROUP) {
         cx = s_xyz[3 * far + 0];
@@ -141,15 +169,15 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
         cy = p[3 * (size_t)far + 1];
         cz = p[3 * (size_t)far + 2];
     }
-    int64_t* out64 = reinterpret_cast<int64_t*>(out) + (size_t)b * npoint;
-    int32_t* out32 = reinterpret_cast<int32_t*>(out) + (size_t)b * npoint;
+    int64_t* out64 = reinterpret_cast<int64_t*>(out) + (size_t)obase;
+    int32_t* out32 = reinterpret_cast<int32_t*>(out) + (size_t)obase;
 
-    for (int64_t i = 0; i < npoint; ++i) {
+    for (int64_t i = 0; i < np; ++i) {
         if (tid == 0 && g == 0) {
             if (out_int32) out32[i] = (int32_t)far;
-            else out64[i] = (int64_t)far;
+            else out64[i] = vbase + (int64_t)far;
         }
-        if (i + 1 == npoint) break;
+        if (i + 1 == np) break;
 
         // NaN can only enter min_d2 through a non-finite coordinate of this
         // CTA's points or of a centroid; from then on (sticky) the keys must
@@ -299,30 +327,34 @@ int threads_for(int64_t per_cta, int P) {
     return (int)min64(kMaxThreads, ((ceil_div(per_cta, P) + 31) / 32) * 32);
 }
 
-template <int P>
+// N is the cloud size (dense) or the longest segment (flat); it sets P, the
+// CTA size and the shared-memory stage.
+template <int P, bool FLAT>
 int launch_single(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
-                  int skip, int out_int32, void* out, int32_t* status, cudaStream_t stream) {
-    auto kern = fps_kernel<P, false>;
+                  int skip, int out_int32, void* out, int32_t* status, const FlatFps& flat,
+                  cudaStream_t stream) {
+    auto kern = fps_kernel<P, false, FLAT>;
     const size_t smem = (size_t)N * 3 * sizeof(float);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return fail(kCudaError, "mpo_fps: cannot set the shared-memory limit");
     kern<<<(unsigned)B, threads_for(N, P), smem, stream>>>(xyz, N, npoint, start_idx, skip,
                                                            out_int32, out, 1, N, 0, nullptr,
-                                                           nullptr, status);
+                                                           nullptr, status, flat);
     return check_launch("mpo_fps");
 }
 
+template <bool FLAT>
 int launch_single_any(const float* xyz, int64_t B, int64_t N, int64_t npoint,
                       int64_t start_idx, int skip, int o32, void* out, int32_t* status,
-                      cudaStream_t s) {
+                      const FlatFps& f, cudaStream_t s) {
     switch (pick_p(N)) {
-        case 1: return launch_single<1>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
-        case 2: return launch_single<2>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
-        case 4: return launch_single<4>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
-        case 8: return launch_single<8>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
-        case 16: return launch_single<16>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
-        default: return launch_single<32>(xyz, B, N, npoint, start_idx, skip, o32, out, status, s);
+        case 1: return launch_single<1, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
+        case 2: return launch_single<2, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
+        case 4: return launch_single<4, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
+        case 8: return launch_single<8, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
+        case 16: return launch_single<16, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
+        default: return launch_single<32, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
     }
 }
 
@@ -350,10 +382,12 @@ int plan_group(int64_t B, int64_t N, int strategy, GroupPlan* plan, const char* 
 
 // Runs the group path in cooperative waves; `scratch` holds group_bytes()
 // for one wave and is zeroed on the stream before each wave.
+template <bool FLAT>
 int launch_group(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
                  int skip, int out_int32, void* out, const GroupPlan& plan, void* scratch,
-                 int32_t* status, cudaStream_t stream, const char* who) {
-    auto kern = fps_kernel<kMaxP, true>;
+                 int32_t* status, const FlatFps& flat_in, cudaStream_t stream, const char* who) {
+    auto kern = fps_kernel<kMaxP, true, FLAT>;
+    FlatFps flat = flat_in;
     int G = (int)plan.G;
     int64_t per_cta = plan.per_cta;
     const int threads = threads_for(per_cta, kMaxP);
@@ -369,7 +403,7 @@ int launch_group(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t
         void* args[] = {(void*)&xyz,      (void*)&N,         (void*)&npoint, (void*)&start_idx,
                         (void*)&skip,     (void*)&out_int32, (void*)&out,    (void*)&G,
                         (void*)&per_cta,  (void*)&cloud_offset, (void*)&slots, (void*)&errors,
-                        (void*)&status};
+                        (void*)&status,   (void*)&flat};
         cudaError_t e = cudaLaunchCooperativeKernel((const void*)kern, dim3(nc * G),
                                                     dim3(threads), args, 0, stream);
         if (e != cudaSuccess) {
@@ -434,7 +468,8 @@ int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t star
     const int skip = skip_near_origin ? 1 : 0;
     const int o32 = out_int32 ? 1 : 0;
     if (strategy != MPO_FPS_GROUP && N <= kPointsPerCta)
-        return launch_single_any(xyz, B, N, npoint, start_idx, skip, o32, out, status_out, s);
+        return launch_single_any<false>(xyz, B, N, npoint, start_idx, skip, o32, out, status_out,
+                                        FlatFps{}, s);
     GroupPlan plan;
     st = plan_group(B, N, strategy, &plan, "mpo_fps");
     if (st) return st;
@@ -443,8 +478,47 @@ int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t star
         return fail(kWorkspaceTooSmall, "mpo_fps: workspace must hold " + std::to_string(need) +
                                             " bytes");
     }
-    return launch_group(xyz, B, N, npoint, start_idx, skip, o32, out, plan, workspace,
-                        status_out, s, "mpo_fps");
+    return launch_group<false>(xyz, B, N, npoint, start_idx, skip, o32, out, plan, workspace,
+                               status_out, FlatFps{}, s, "mpo_fps");
+}
+
+size_t mpo_flat_fps_workspace_bytes(int64_t segments, int64_t max_len) {
+    if (segments <= 0 || max_len <= mpo::kPointsPerCta) return 0;
+    mpo::GroupPlan plan;
+    if (mpo::plan_group(segments, max_len, MPO_FPS_AUTO, &plan, "mpo_flat_fps_workspace_bytes") !=
+        mpo::kOk)
+        return 0;
+    return mpo::group_bytes(plan.clouds_per_wave, plan.G);
+}
+
+int mpo_flat_fps(const float* x, const int64_t* ptr, const int64_t* out_ptr,
+                 const int64_t* starts, int64_t segments, int64_t total_n, int64_t total_out,
+                 int64_t max_len, int64_t* out, int32_t* status, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(segments >= 0 && total_n >= 0 && total_out >= 0 && max_len >= 0,
+                "negative size");
+    MPO_REQUIRE(status != nullptr, "status must not be null");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(status, 0, sizeof(int32_t), s) != cudaSuccess)
+        return fail(kCudaError, "mpo_flat_fps: status reset failed");
+    if (segments == 0 || total_out == 0) return kOk;
+    MPO_REQUIRE(max_len >= 1 && max_len <= total_n, "max_len must be in [1, total_n]");
+    MPO_REQUIRE(max_len < (int64_t)0x7fffffff, "segments must be below 2**31 points");
+    MPO_REQUIRE(x && ptr && out_ptr && starts && out, "null pointer");
+    const FlatFps flat{ptr, out_ptr, starts, total_n, total_out, max_len};
+    if (max_len <= kPointsPerCta)
+        return launch_single_any<true>(x, segments, max_len, 0, 0, 0, 0, out, status, flat, s);
+    GroupPlan plan;
+    int st = plan_group(segments, max_len, MPO_FPS_AUTO, &plan, "mpo_flat_fps");
+    if (st) return st;
+    const size_t need = group_bytes(plan.clouds_per_wave, plan.G);
+    if (workspace == nullptr || workspace_bytes < need) {
+        return fail(kWorkspaceTooSmall, "mpo_flat_fps: workspace must hold " +
+                                            std::to_string(need) + " bytes");
+    }
+    return launch_group<true>(x, segments, max_len, 0, 0, 0, 0, out, plan, workspace, status,
+                              flat, s, "mpo_flat_fps");
 }
 
 }  // extern "C"
@@ -511,7 +585,8 @@ int mpo_fps_noalloc(const float* xyz, int64_t B, int64_t N, int64_t npoint, int6
     const int skip = skip_near_origin ? 1 : 0;
     const int o32 = out_int32 ? 1 : 0;
     if (strategy != MPO_FPS_GROUP && N <= kPointsPerCta)
-        return launch_single_any(xyz, B, N, npoint, start_idx, skip, o32, out, status_out, s);
+        return launch_single_any<false>(xyz, B, N, npoint, start_idx, skip, o32, out, status_out,
+                                        FlatFps{}, s);
     GroupPlan plan;
     st = plan_group(B, N, strategy, &plan, "mpo_fps_noalloc");
     if (st) return st;
@@ -526,8 +601,8 @@ int mpo_fps_noalloc(const float* xyz, int64_t B, int64_t N, int64_t npoint, int6
     void* scratch = nullptr;
     st = noalloc_scratch(&scratch);
     if (st) return st;
-    return launch_group(xyz, B, N, npoint, start_idx, skip, o32, out, plan, scratch, status_out,
-                        s, "mpo_fps_noalloc");
+    return launch_group<false>(xyz, B, N, npoint, start_idx, skip, o32, out, plan, scratch,
+                               status_out, FlatFps{}, s, "mpo_fps_noalloc");
 }
 
 }  // extern "C"

@@ -35,6 +35,7 @@
 #include "../../include/mpo_b200.h"
 #include "mpo_common.cuh"
 #include "knn_select.cuh"
+#include "segments.cuh"
 
 namespace mpo {
 namespace {
@@ -193,26 +194,28 @@ knn3_kernel(const float* __restrict__ query, const float* __restrict__ ref, int6
 // FP32 pipe then bounds the kernel).  The tile stores reference points in
 // structure-of-arrays pairs: (x_2p, x_2p+1, y_2p, y_2p+1) per point pair and
 // (z_4i .. z_4i+3) per four points.
-template <int K, int POLICY>
+template <int K, int POLICY, bool FLAT>
 __global__ void __launch_bounds__(kThreads, 2)
-knn3p_kernel(const float* __restrict__ query, const float* __restrict__ ref, int64_t M,
-             int64_t N, int k, int S, float* __restrict__ dist, int64_t* __restrict__ idx64,
+knn3p_kernel(const float* __restrict__ query, const float* __restrict__ ref, Layout L, int k,
+             int S, float* __restrict__ dist, int64_t* __restrict__ idx64,
              int32_t* __restrict__ idx32, float* __restrict__ sqdist) {
     extern __shared__ float4 smem4[];
     float4* txy = smem4;                    // [2][kTile / 2]
     float4* tz = smem4 + kTile;             // [2][kTile / 4]
-    const int b = blockIdx.y;
     const int qpc = kThreads / S;
+    Span sp;
+    if (!locate<FLAT>(L, qpc, sp)) return;  // CTA-uniform
     const int tid = threadIdx.x;
     const int split = tid / qpc;
     const int ql = tid % qpc;
-    const int64_t q = (int64_t)blockIdx.x * qpc + ql;
-    const bool active = q < M;
-    const float* __restrict__ r = ref + (size_t)b * (size_t)N * 3;
+    const int64_t q = sp.q0 + ql;
+    const bool active = q < sp.q1;
+    const int64_t N = sp.n;
+    const float* __restrict__ r = ref + (size_t)sp.r0 * 3;
 
     float qx = 0.f, qy = 0.f, qz = 0.f;
     if (active) {
-        const float* qp = query + ((size_t)b * (size_t)M + (size_t)q) * 3;
+        const float* qp = query + (size_t)q * 3;
         qx = qp[0];
         qy = qp[1];
         qz = qp[2];
@@ -326,16 +329,16 @@ knn3p_kernel(const float* __restrict__ query, const float* __restrict__ ref, int
         }
     }
     if (split != 0 || !active) return;
-    const size_t row = ((size_t)b * (size_t)M + (size_t)q) * (size_t)k;
+    const size_t row = (size_t)q * (size_t)k;
 #pragma unroll
     for (int s2 = 0; s2 < K; ++s2) {
         const int l = s2 - top.base;
         if (l >= 0) {
             const bool filled = l < top.cnt;
             const float dd = filled ? top.d[s2] : INFINITY;
-            dist[row + l] = sqrtf(dd);
+            if (dist) dist[row + l] = sqrtf(dd);
             if (sqdist) sqdist[row + l] = dd;
-            if (idx64) idx64[row + l] = filled ? (int64_t)top.i[s2] : -1;
+            if (idx64) idx64[row + l] = filled ? sp.obase + (int64_t)top.i[s2] : -1;
             if (idx32) idx32[row + l] = filled ? (int32_t)top.i[s2] : -1;
         }
     }
@@ -346,30 +349,32 @@ knn3p_kernel(const float* __restrict__ query, const float* __restrict__ ref, int
 // both sit in shared memory; SD accumulates in increasing dimension order.
 constexpr int kFeatThreads = 128;
 
-template <int K, int POLICY>
+template <int K, int POLICY, bool FLAT>
 __global__ void __launch_bounds__(kFeatThreads)
-knnd_kernel(const float* __restrict__ query, const float* __restrict__ ref, int64_t M, int64_t N,
-            int D, int k, int S, int tileN, float* __restrict__ dist, int64_t* __restrict__ idx64,
+knnd_kernel(const float* __restrict__ query, const float* __restrict__ ref, Layout L, int D,
+            int k, int S, int tileN, float* __restrict__ dist, int64_t* __restrict__ idx64,
             float* __restrict__ sqdist) {
     extern __shared__ float smemf[];
     const int qpc = kFeatThreads / S;
+    Span sp;
+    if (!locate<FLAT>(L, qpc, sp)) return;  // CTA-uniform
     const int tid = threadIdx.x;
     const int split = tid / qpc;
     const int ql = tid % qpc;
-    const int b = blockIdx.y;
-    const int64_t q = (int64_t)blockIdx.x * qpc + ql;
-    const bool active = q < M;
+    const int64_t q = sp.q0 + ql;
+    const bool active = q < sp.q1;
+    const int64_t N = sp.n;
     const int qstride = D + 1;  // odd stride: conflict-free per-thread rows
     float* sq = smemf;                          // [qpc][D+1]
     float* st = smemf + (size_t)qpc * qstride;  // [tileN][D]
     for (int e = tid; e < qpc * D; e += kFeatThreads) {
         const int qq = e / D, t = e % D;
-        const int64_t gq = (int64_t)blockIdx.x * qpc + qq;
-        sq[qq * qstride + t] = gq < M ? query[((size_t)b * M + gq) * D + t] : 0.f;
+        const int64_t gq = sp.q0 + qq;
+        sq[qq * qstride + t] = gq < sp.q1 ? query[(size_t)gq * D + t] : 0.f;
     }
     TopK<K, POLICY> top;
     top.init(k);
-    const float* __restrict__ r = ref + (size_t)b * (size_t)N * D;
+    const float* __restrict__ r = ref + (size_t)sp.r0 * D;
     const float* myq = sq + ql * qstride;
     const int slice = tileN / S;
     for (int64_t t0 = 0; t0 < N; t0 += tileN) {
@@ -422,16 +427,16 @@ knnd_kernel(const float* __restrict__ query, const float* __restrict__ ref, int6
         }
     }
     if (split != 0 || !active) return;
-    const size_t row = ((size_t)b * (size_t)M + (size_t)q) * (size_t)k;
+    const size_t row = (size_t)q * (size_t)k;
 #pragma unroll
     for (int s = 0; s < K; ++s) {
         const int l = s - top.base;
         if (l >= 0) {
             const bool filled = l < top.cnt;
             const float d = filled ? top.d[s] : INFINITY;
-            dist[row + l] = sqrtf(d);
+            if (dist) dist[row + l] = sqrtf(d);
             if (sqdist) sqdist[row + l] = d;
-            idx64[row + l] = filled ? (int64_t)top.i[s] : -1;
+            idx64[row + l] = filled ? sp.obase + (int64_t)top.i[s] : -1;
         }
     }
 }
@@ -441,17 +446,21 @@ knnd_kernel(const float* __restrict__ query, const float* __restrict__ ref, int6
 // lanes, slot s held by lane s % 32 in register s / 32.
 constexpr int kWarpSlots = 8;  // 8 * 32 = 256
 
-template <int POLICY>
-__global__ void __launch_bounds__(256)
-knn_warp_kernel(const float* __restrict__ query, const float* __restrict__ ref, int64_t M,
-                int64_t N, int D, int k, float* __restrict__ dist, int64_t* __restrict__ idx64,
+constexpr int kWarpQueries = 8;  // warps (queries) per CTA
+
+template <int POLICY, bool FLAT>
+__global__ void __launch_bounds__(32 * kWarpQueries)
+knn_warp_kernel(const float* __restrict__ query, const float* __restrict__ ref, Layout L, int D,
+                int k, float* __restrict__ dist, int64_t* __restrict__ idx64,
                 float* __restrict__ sqdist) {
     const int lane = threadIdx.x & 31;
-    const int64_t q = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int b = blockIdx.y;
-    if (q >= M) return;
-    const float* __restrict__ qp = query + ((size_t)b * M + q) * D;
-    const float* __restrict__ r = ref + (size_t)b * N * D;
+    Span sp;
+    if (!locate<FLAT>(L, kWarpQueries, sp)) return;
+    const int64_t q = sp.q0 + (threadIdx.x >> 5);
+    if (q >= sp.q1) return;
+    const int64_t N = sp.n;
+    const float* __restrict__ qp = query + (size_t)q * D;
+    const float* __restrict__ r = ref + (size_t)sp.r0 * D;
     float ld[kWarpSlots];
     uint32_t li[kWarpSlots];
 #pragma unroll
@@ -533,16 +542,16 @@ knn_warp_kernel(const float* __restrict__ query, const float* __restrict__ ref, 
             cnt = min(cnt + 1, k);
         }
     }
-    const size_t row = ((size_t)b * M + q) * (size_t)k;
+    const size_t row = (size_t)q * (size_t)k;
 #pragma unroll
     for (int t = 0; t < kWarpSlots; ++t) {
         const int s = t * 32 + lane;
         if (s < k) {
             const bool filled = s < cnt;
             const float d = filled ? ld[t] : INFINITY;
-            dist[row + s] = sqrtf(d);
+            if (dist) dist[row + s] = sqrtf(d);
             if (sqdist) sqdist[row + s] = d;
-            idx64[row + s] = filled ? (int64_t)li[t] : -1;
+            idx64[row + s] = filled ? sp.obase + (int64_t)li[t] : -1;
         }
     }
 }
@@ -558,20 +567,22 @@ knn_warp_kernel(const float* __restrict__ query, const float* __restrict__ ref, 
 constexpr int kWqWarps = 8;
 constexpr int kWqTile = 2048;
 
-template <int POLICY>
+template <int POLICY, bool FLAT>
 __global__ void __launch_bounds__(kWqWarps * 32)
-knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, int64_t M,
-               int64_t N, int k, float* __restrict__ dist, int64_t* __restrict__ idx64,
+knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, Layout L, int k,
+               float* __restrict__ dist, int64_t* __restrict__ idx64,
                int32_t* __restrict__ idx32, float* __restrict__ sqdist) {
     __shared__ float4 tile[kWqTile];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int b = blockIdx.y;
-    const int64_t q = (int64_t)blockIdx.x * kWqWarps + warp;
-    const bool active = q < M;
-    const float* __restrict__ r = ref + (size_t)b * (size_t)N * 3;
+    Span sp;
+    if (!locate<FLAT>(L, kWqWarps, sp)) return;  // CTA-uniform
+    const int64_t q = sp.q0 + warp;
+    const bool active = q < sp.q1;
+    const int64_t N = sp.n;
+    const float* __restrict__ r = ref + (size_t)sp.r0 * 3;
     float qx = 0.f, qy = 0.f, qz = 0.f;
     if (active) {
-        const float* qp = query + ((size_t)b * (size_t)M + (size_t)q) * 3;
+        const float* qp = query + (size_t)q * 3;
         qx = qp[0];
         qy = qp[1];
         qz = qp[2];
@@ -622,21 +633,26 @@ knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, i
         }
     }
     if (!active || lane >= k) return;
-    const size_t row = ((size_t)b * (size_t)M + (size_t)q) * (size_t)k;
+    const size_t row = (size_t)q * (size_t)k;
     const bool filled = lane < cnt;
     const float d = filled ? ld : INFINITY;
-    dist[row + lane] = sqrtf(d);
+    if (dist) dist[row + lane] = sqrtf(d);
     if (sqdist) sqdist[row + lane] = d;
-    if (idx64) idx64[row + lane] = filled ? (int64_t)li : -1;
+    if (idx64) idx64[row + lane] = filled ? sp.obase + (int64_t)li : -1;
     if (idx32) idx32[row + lane] = filled ? (int32_t)li : -1;
 }
 
-template <int POLICY>
-int launch_wq3(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int k,
+// Grid of a search launch: (ceil(M / qpc), B) dense, virtual tiles flat.
+inline dim3 search_grid(const Layout& L, int64_t B, int qpc, bool flat) {
+    if (flat) return dim3((unsigned)flat_tiles(L.M, L.segs, qpc), 1u);
+    return dim3((unsigned)ceil_div(L.M, qpc), (unsigned)B);
+}
+
+template <int POLICY, bool FLAT = false>
+int launch_wq3(const float* query, const float* ref, const Layout& L, int64_t B, int k,
                float* dist, int64_t* idx64, int32_t* idx32, float* sqdist, cudaStream_t s) {
-    dim3 grid((unsigned)ceil_div(M, kWqWarps), (unsigned)B);
-    knn_wq3_kernel<POLICY><<<grid, kWqWarps * 32, 0, s>>>(query, ref, M, N, k, dist, idx64,
-                                                          idx32, sqdist);
+    knn_wq3_kernel<POLICY, FLAT><<<search_grid(L, B, kWqWarps, FLAT), kWqWarps * 32, 0, s>>>(
+        query, ref, L, k, dist, idx64, idx32, sqdist);
     return check_launch("knn_wq3_kernel");
 }
 
@@ -668,28 +684,30 @@ int launch_knn3(const float* query, const float* ref, int64_t B, int64_t M, int6
     return check_launch("knn3_kernel");
 }
 
-template <int K, int POLICY>
-int launch_knn3p(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int k,
-                 float* dist, int64_t* idx64, int32_t* idx32, float* sqdist, cudaStream_t s) {
-    const int S = choose_splits(B, M, N);
+// max_n: the longest reference cloud (segment) of the launch.
+template <int K, int POLICY, bool FLAT = false>
+int launch_knn3p(const float* query, const float* ref, const Layout& L, int64_t B,
+                 int64_t max_n, int k, float* dist, int64_t* idx64, int32_t* idx32,
+                 float* sqdist, cudaStream_t s) {
+    const int S = choose_splits(B, L.M, max_n);
     const int qpc = kThreads / S;
     size_t smem = (size_t)(kTile + kTile / 2) * sizeof(float4) + (size_t)kQueue * kThreads * 8;
     const size_t merge = (size_t)kThreads * K * 8;
     if (merge > smem) smem = merge;
-    auto kern = knn3p_kernel<K, POLICY>;
+    auto kern = knn3p_kernel<K, POLICY, FLAT>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");
-    dim3 grid((unsigned)ceil_div(M, qpc), (unsigned)B);
-    kern<<<grid, kThreads, smem, s>>>(query, ref, M, N, k, S, dist, idx64, idx32, sqdist);
+    kern<<<search_grid(L, B, qpc, FLAT), kThreads, smem, s>>>(query, ref, L, k, S, dist, idx64,
+                                                              idx32, sqdist);
     return check_launch("knn3p_kernel");
 }
 
-template <int K>
-int launch_knnd(const float* query, const float* ref, int64_t B, int64_t M, int64_t N, int D,
-                int k, float* dist, int64_t* idx64, float* sqdist, cudaStream_t s) {
+template <int K, bool FLAT = false>
+int launch_knnd(const float* query, const float* ref, const Layout& L, int64_t B, int D, int k,
+                float* dist, int64_t* idx64, float* sqdist, cudaStream_t s) {
     int S = 1;
-    while (S < 4 && B * M * S < (int64_t)sm_count() * 512) S *= 2;
+    while (S < 4 && B * L.M * S < (int64_t)sm_count() * 512) S *= 2;
     const int qpc = kFeatThreads / S;
     int tileN = 64 * S;
     size_t smem = ((size_t)qpc * (D + 1) + (size_t)tileN * D) * sizeof(float);
@@ -700,13 +718,44 @@ int launch_knnd(const float* query, const float* ref, int64_t B, int64_t M, int6
     if (smem > 200 * 1024) return fail(kUnsupported, "knn: feature dimension too large");
     const size_t merge = (size_t)kFeatThreads * K * 8;
     if (merge > smem) smem = merge;
-    auto kern = knnd_kernel<K, kDropNonFinite>;
+    auto kern = knnd_kernel<K, kDropNonFinite, FLAT>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");
-    dim3 grid((unsigned)ceil_div(M, qpc), (unsigned)B);
-    kern<<<grid, kFeatThreads, smem, s>>>(query, ref, M, N, D, k, S, tileN, dist, idx64, sqdist);
+    kern<<<search_grid(L, B, qpc, FLAT), kFeatThreads, smem, s>>>(query, ref, L, D, k, S, tileN,
+                                                                  dist, idx64, sqdist);
     return check_launch("knnd_kernel");
+}
+
+// Exact kNN over a dense or flat layout.  POLICY3 is the candidate policy for
+// D == 3 (every D != 3 search drops non-finite distances); max_n is the
+// longest reference cloud or segment, which picks the D == 3 kernel.
+template <int POLICY3, bool FLAT>
+int run_knn(const float* query, const float* ref, const Layout& L, int64_t B, int64_t max_n,
+            int64_t D, int k, float* dist, int64_t* idx, float* sqdist, cudaStream_t s) {
+    if (D == 3 && k <= 32 && use_wq3(max_n))
+        return launch_wq3<POLICY3, FLAT>(query, ref, L, B, k, dist, idx, nullptr, sqdist, s);
+    if (D == 3 && k <= 32) {
+        if (k <= 4) return launch_knn3p<4, POLICY3, FLAT>(query, ref, L, B, max_n, k, dist, idx, nullptr, sqdist, s);
+        if (k <= 8) return launch_knn3p<8, POLICY3, FLAT>(query, ref, L, B, max_n, k, dist, idx, nullptr, sqdist, s);
+        if (k <= 16) return launch_knn3p<16, POLICY3, FLAT>(query, ref, L, B, max_n, k, dist, idx, nullptr, sqdist, s);
+        return launch_knn3p<32, POLICY3, FLAT>(query, ref, L, B, max_n, k, dist, idx, nullptr, sqdist, s);
+    }
+    if (D != 3 && D <= 4096 && k <= 32) {
+        if (k <= 4) return launch_knnd<4, FLAT>(query, ref, L, B, (int)D, k, dist, idx, sqdist, s);
+        if (k <= 8) return launch_knnd<8, FLAT>(query, ref, L, B, (int)D, k, dist, idx, sqdist, s);
+        if (k <= 16) return launch_knnd<16, FLAT>(query, ref, L, B, (int)D, k, dist, idx, sqdist, s);
+        return launch_knnd<32, FLAT>(query, ref, L, B, (int)D, k, dist, idx, sqdist, s);
+    }
+    // Large k (or very wide features): warp per query.
+    const dim3 grid = search_grid(L, B, kWarpQueries, FLAT);
+    if (D == 3)
+        knn_warp_kernel<POLICY3, FLAT><<<grid, 32 * kWarpQueries, 0, s>>>(query, ref, L, (int)D, k,
+                                                                         dist, idx, sqdist);
+    else
+        knn_warp_kernel<kDropNonFinite, FLAT><<<grid, 32 * kWarpQueries, 0, s>>>(
+            query, ref, L, (int)D, k, dist, idx, sqdist);
+    return check_launch("knn_warp_kernel");
 }
 
 }  // namespace
@@ -730,37 +779,34 @@ int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t 
     if (B == 0 || M == 0 || k == 0) return kOk;
     MPO_REQUIRE(query && ref && dist && idx, "null pointer");
     cudaStream_t s = (cudaStream_t)stream;
-    const int kk = (int)k;
     if (fknn_tc_eligible(M, N, D, k))
         return fknn_tc_run(query, ref, B, M, N, D, k, dist, idx, sqdist, workspace,
                            workspace_bytes, s);
-    if (D == 3 && k <= 32 && use_wq3(N)) {
-        return launch_wq3<kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
-    }
-    if (D == 3 && k <= 32) {
-        if (k <= 4) return launch_knn3p<4, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
-        if (k <= 8) return launch_knn3p<8, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
-        if (k <= 16) return launch_knn3p<16, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
-        return launch_knn3p<32, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
-    }
-    if (D == 3) {
-        if (k <= 4) return launch_knn3<4, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
-        if (k <= 8) return launch_knn3<8, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
-        if (k <= 16) return launch_knn3<16, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
-        if (k <= 32) return launch_knn3<32, kDropNaN>(query, ref, B, M, N, kk, dist, idx, nullptr, sqdist, s);
-    } else if (D <= 4096) {
-        if (k <= 4) return launch_knnd<4>(query, ref, B, M, N, (int)D, kk, dist, idx, sqdist, s);
-        if (k <= 8) return launch_knnd<8>(query, ref, B, M, N, (int)D, kk, dist, idx, sqdist, s);
-        if (k <= 16) return launch_knnd<16>(query, ref, B, M, N, (int)D, kk, dist, idx, sqdist, s);
-        if (k <= 32) return launch_knnd<32>(query, ref, B, M, N, (int)D, kk, dist, idx, sqdist, s);
-    }
-    // Large k (or very wide features): warp per query.
-    dim3 grid((unsigned)ceil_div(M, 8), (unsigned)B);
-    if (D == 3)
-        knn_warp_kernel<kDropNaN><<<grid, 256, 0, s>>>(query, ref, M, N, (int)D, kk, dist, idx, sqdist);
-    else
-        knn_warp_kernel<kDropNonFinite><<<grid, 256, 0, s>>>(query, ref, M, N, (int)D, kk, dist, idx, sqdist);
-    return check_launch("knn_warp_kernel");
+    return run_knn<kDropNaN, false>(query, ref, dense_layout(M, N), B, N, D, (int)k, dist, idx,
+                                    sqdist, s);
+}
+
+int mpo_flat_knn(const float* x, const float* y, const int64_t* ptr_x, const int64_t* ptr_y,
+                 int64_t segments, int64_t nx, int64_t ny, int64_t D, int64_t k,
+                 int64_t max_segment_x, int64_t* out, int32_t* status, void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(segments >= 0 && nx >= 0 && ny >= 0 && D >= 1, "bad sizes");
+    MPO_REQUIRE(k >= 0 && k <= 256, "k must be in [0, 256]");
+    MPO_REQUIRE(nx < (int64_t)0x7fffffff && ny < (int64_t)0x7fffffff,
+                "the flat row counts must be below 2**31");
+    MPO_REQUIRE(status != nullptr, "status must not be null");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cudaMemsetAsync(status, 0, sizeof(int32_t), s) != cudaSuccess)
+        return fail(kCudaError, "mpo_flat_knn: status reset failed");
+    if (ny == 0 || k == 0) return kOk;
+    MPO_REQUIRE(segments >= 1, "a nonempty query set needs at least one segment");
+    MPO_REQUIRE(y && ptr_x && ptr_y && out && (x || nx == 0), "null pointer");
+    int st = flat_offsets_check(ptr_y, ptr_x, segments, ny, nx, status, s);
+    if (st) return st;
+    Layout L{ny, nx, ptr_y, ptr_x, segments, status};
+    const int64_t max_n = max64(0, min64(max_segment_x, nx));
+    return run_knn<kDropNonFinite, true>(y, x, L, 1, max_n, D, (int)k, nullptr, out, nullptr,
+                                         s);
 }
 
 int mpo_three_nn(const float* unknown, const float* known, int64_t B, int64_t N, int64_t M,
@@ -772,8 +818,8 @@ int mpo_three_nn(const float* unknown, const float* known, int64_t B, int64_t N,
     MPO_REQUIRE(M < (int64_t)0x7fffffff, "M must be below 2**31");
     MPO_REQUIRE(unknown && known && dist && idx, "null pointer");
     if (use_wq3(M))
-        return launch_wq3<kNaNLast>(unknown, known, B, N, M, 3, dist, nullptr, idx, nullptr,
-                                    (cudaStream_t)stream);
+        return launch_wq3<kNaNLast>(unknown, known, dense_layout(N, M), B, 3, dist, nullptr, idx,
+                                    nullptr, (cudaStream_t)stream);
     return launch_knn3<4, kNaNLast>(unknown, known, B, N, M, 3, dist, nullptr, idx, nullptr,
                                     (cudaStream_t)stream);
 }

@@ -43,6 +43,12 @@ int fknn_tc_run(const float* query, const float* ref, int64_t B, int64_t M, int6
                 size_t workspace_bytes, cudaStream_t s);
 int current_device();
 
+// Flat (ragged) batches (flat.cu): one launch checks that ptr_q[0..segs] runs
+// from 0 to M and ptr_r[0..segs] from 0 to N without decreasing, and sets
+// *flag = 1 otherwise (the caller zeroes the flag first, on the same stream).
+int flat_offsets_check(const int64_t* ptr_q, const int64_t* ptr_r, int64_t segs, int64_t M,
+                       int64_t N, int32_t* flag, cudaStream_t s);
+
 #define MPO_REQUIRE(cond, msg)                                   \
     do {                                                         \
         if (!(cond)) return ::mpo::fail(::mpo::kInvalidArgument, \

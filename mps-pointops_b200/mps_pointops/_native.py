@@ -20,7 +20,7 @@ from pathlib import Path
 import torch
 
 LIB_NAME = "libmpo_b200.so"
-ABI_VERSION = 2
+ABI_VERSION = 3
 _lib = None
 _lock = threading.Lock()
 _checked_devices: set[int] = set()
@@ -61,6 +61,13 @@ SIGNATURES = {
     "mpo_chamfer_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp]),
     "mpo_chamfer_check_inputs": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "mpo_flat_knn": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp,
+                            _vp]),
+    "mpo_flat_radius": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i64, _int, _vp, _vp,
+                               _vp]),
+    "mpo_flat_fps_workspace_bytes": (_sz, [_i64, _i64]),
+    "mpo_flat_fps": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _sz,
+                            _vp]),
 }
 
 

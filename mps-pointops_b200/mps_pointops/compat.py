@@ -9,12 +9,14 @@ gamzerA/mps-pointops v1.0.0 (mps_pointops/compat.py:53-172)::
     from pointnet2_ops import pointnet2_utils   # served by mps_pointops
     from knn_cuda import KNN
 
-``install()`` registers ``pointnet2_ops``, ``pointnet2_ops.pointnet2_utils``
-and ``knn_cuda`` in ``sys.modules``; a name that is already importable (the
-real package) is left alone unless ``force=True``.  The reference's
-``torch_cluster`` and Pointcept ``pointops`` shims use its ragged (flat) and
-graph kernels, which this build does not provide; ``pointcept=True`` raises
-``NotImplementedError``.
+``install()`` registers ``pointnet2_ops``, ``pointnet2_ops.pointnet2_utils``,
+``knn_cuda`` and ``torch_cluster`` in ``sys.modules``; a name that is already
+importable (the real package) is left alone unless ``force=True``.  The
+``torch_cluster`` stand-in serves ``fps``, ``knn``, ``radius``, ``knn_graph``
+and ``radius_graph`` from :mod:`mps_pointops.flat`; the reference's clustering
+and random-walk entries (``grid_cluster``, ``graclus_cluster``,
+``random_walk``, ``nearest``) and its Pointcept ``pointops`` shim are not part
+of this build, and ``pointcept=True`` raises ``NotImplementedError``.
 
 The pointnet2_ops FPS and ball query run as fused kernels here: FPS writes its
 int32 indices directly, and the ball query applies pointnet2's first-hit
@@ -32,7 +34,7 @@ import torch
 from torch import Tensor
 
 from . import _native as N
-from . import ops
+from . import flat, ops
 from ._ball_query_cuda import _checked_radius_and_k
 
 
@@ -144,6 +146,16 @@ def install(force: bool = False, *, pointcept: bool = False) -> list[str]:
             "pointnet2_ops.pointnet2_utils": pointnet2_utils,
         },
         "knn_cuda": {"knn_cuda": _module("knn_cuda", KNN=KNN)},
+        "torch_cluster": {
+            "torch_cluster": _module(
+                "torch_cluster",
+                fps=flat.fps,
+                knn=flat.knn,
+                radius=flat.radius,
+                knn_graph=flat.knn_graph,
+                radius_graph=flat.radius_graph,
+            )
+        },
     }
     installed = []
     for top, modules in packages.items():

@@ -63,6 +63,9 @@ def _load():
             _f32p, _f32p, _i64p, _i64p, _i64, _i64, _i64, _i64, _i64p, _i64p, _f32p, _f32p,
             _f32p, _f32p]
         lib.oracle_chamfer_mean_loss_and_grad.restype = ctypes.c_double
+        lib.oracle_flat_search.argtypes = [_f32p, _f32p, _i64p, _i64p, _i64, _i64, _i64,
+                                           ctypes.c_int, ctypes.c_float, ctypes.c_int, _i64, _i64,
+                                           _i64p]
         _lib = lib
     return _lib
 
@@ -299,3 +302,85 @@ def chamfer_mean_loss_and_grad(x, y, x_lengths=None, y_lengths=None):
         _ptr(ix, _i64p), _ptr(iy, _i64p), _ptr(dx, _f32p), _ptr(dy, _f32p),
         _ptr(gx, _f32p), _ptr(gy, _f32p))
     return loss, gx, gy, (dx, ix), (dy, iy)
+
+
+# ---------------------------------------------------------------- flat batches
+def flat_sample_counts(lengths, ratio: float, ratio_dtype=np.float32) -> list[int]:
+    """torch_cluster's GPU count rule (mps_pointops/flat.py:149-158): the batch
+    sizes are converted to the ratio's dtype, multiplied, ceiled."""
+    sizes = np.asarray(lengths, dtype=ratio_dtype)
+    return [int(v) for v in np.ceil(sizes * ratio_dtype(ratio))]
+
+
+def torch_cluster_radius_sq(r: float) -> float:
+    """fl32(r * r) with r * r in double (mps_pointops/_flat_search_mps.py:65-76)."""
+    with np.errstate(over="ignore"):
+        return float(np.float32(r * r))
+
+
+def _flat_search(x, y, ptr_x, ptr_y, width, radius_mode, r2=0.0, ignore_same=False):
+    lib = _load()
+    x, y = _f32(x), _f32(y)
+    px, py = _i64a(ptr_x), _i64a(ptr_y)
+    if y.ndim == 1:
+        y = y.reshape(-1, 1)
+    D = y.shape[1]
+    ny = y.shape[0]
+    out = np.full((ny, width), -1, dtype=np.int64)
+    if ny == 0 or width == 0:
+        return out
+    xx = x if x.size else np.zeros((1, D), np.float32)
+    jobs = []
+    for lo, hi in _ranges(ny, threads() * 4):
+        def job(lo=lo, hi=hi):
+            lib.oracle_flat_search(_ptr(xx, _f32p), _ptr(y, _f32p), _ptr(px, _i64p),
+                                   _ptr(py, _i64p), len(px) - 1, D, width, int(radius_mode),
+                                   ctypes.c_float(r2), int(bool(ignore_same)), lo, hi,
+                                   _ptr(out, _i64p))
+        jobs.append(job)
+    _parallel(jobs)
+    return out
+
+
+def flat_knn_indices(x, y, ptr_x, ptr_y, width: int) -> np.ndarray:
+    """mps_pointops/flat.py:248-272, kNN branch: (ny, width) global x rows in
+    ascending (SD, index) order over the query's cloud, non-finite SD dropped,
+    -1 padded."""
+    return _flat_search(x, y, ptr_x, ptr_y, width, False)
+
+
+def flat_radius_indices(x, y, ptr_x, ptr_y, r: float, width: int,
+                        ignore_same_index: bool = False) -> np.ndarray:
+    """mps_pointops/flat.py:248-272, radius branch: the first `width` global x
+    rows of the query's cloud in input order with SD < fl32(r * r)."""
+    return _flat_search(x, y, ptr_x, ptr_y, width, True, torch_cluster_radius_sq(r),
+                        ignore_same_index)
+
+
+def flat_fps(x, ptr, counts, starts) -> np.ndarray:
+    """mps_pointops/flat.py:213-225: per cloud, reference.furthest_point_sample
+    from the local index starts[b] (reference.py:27-58), shifted to global rows."""
+    lib = _load()
+    x = _f32(x)
+    ptr = [int(v) for v in ptr]
+    counts = [int(c) for c in counts]
+    outs = [np.empty(c, dtype=np.int64) for c in counts]
+
+    def job(b):
+        def run():
+            lo, hi = ptr[b], ptr[b + 1]
+            if counts[b] == 0:
+                return
+            seg = np.ascontiguousarray(x[lo:hi])
+            lib.oracle_fps(_ptr(seg, _f32p), 1, hi - lo, counts[b], int(starts[b]), 0,
+                           _ptr(outs[b], _i64p))
+            outs[b] += lo
+        return run
+    _parallel(job(b) for b in range(len(counts)))
+    return np.concatenate(outs) if outs else np.empty(0, dtype=np.int64)
+
+
+def flat_edges(indices: np.ndarray) -> np.ndarray:
+    """mps_pointops/flat.py:257-263: padded rows -> [query, reference] edges."""
+    q, s = np.nonzero(indices >= 0)
+    return np.stack([q.astype(np.int64), indices[q, s]])

@@ -364,3 +364,64 @@ EXPORT double oracle_chamfer_mean_loss_and_grad(
     free(gy);
     return loss / denom_b;
 }
+
+/* ------------------------------------------------------------------ flat batches
+ * mps_pointops/flat.py:236-272 (_sqdist, _reference_search): the CPU path of
+ * the torch_cluster-style flat API.  x (nx, D) reference rows and y (ny, D)
+ * query rows are split into `segs` clouds by the offset arrays ptr_x and
+ * ptr_y (segs + 1 entries, flat.py:68-98).  For every query row q of cloud b
+ * the row out[q, :width] receives GLOBAL x rows, -1 padded:
+ *   kNN    (radius_mode 0): torch.argsort(d2, stable=True) over the cloud,
+ *          keep the finite d2 (torch.isfinite), first min(width, cloud size)
+ *          -- the ascending (d2, index) order without non-finite entries.
+ *   radius (radius_mode 1): torch.nonzero(d2 < r2)[:take] -- the first rows
+ *          in input order with d2 < r2, r2 = fl32(r * r), r * r in double
+ *          (flat.py:260; mps_pointops/_flat_search_mps.py:65-76).  With
+ *          ignore_same != 0 the x row whose global number equals q's is
+ *          skipped before the cap (pyg-lib's radius, flat_search.metal:196).
+ * d2 = _sqdist(y[q], x[j]) = sequential sum of (x - y)^2, each op rounded.
+ * Only the query rows in [q_lo, q_hi) are written, so host threads can split
+ * the queries without changing any result. */
+EXPORT void oracle_flat_search(const float* x, const float* y, const int64_t* ptr_x,
+                               const int64_t* ptr_y, int64_t segs, int64_t D, int64_t width,
+                               int radius_mode, float r2, int ignore_same, int64_t q_lo,
+                               int64_t q_hi, int64_t* out) {
+    float* ld = (float*)malloc(sizeof(float) * (size_t)(width > 0 ? width : 1));
+    int64_t* li = (int64_t*)malloc(sizeof(int64_t) * (size_t)(width > 0 ? width : 1));
+    for (int64_t b = 0; b < segs; ++b) {
+        const int64_t xa = ptr_x[b], xb = ptr_x[b + 1];
+        const int64_t ya = ptr_y[b] > q_lo ? ptr_y[b] : q_lo;
+        const int64_t yb = ptr_y[b + 1] < q_hi ? ptr_y[b + 1] : q_hi;
+        const int64_t take = width < xb - xa ? width : xb - xa;
+        for (int64_t q = ya; q < yb; ++q) {
+            int64_t* row = out + q * width;
+            int64_t filled = 0;
+            for (int64_t s = 0; s < width; ++s) row[s] = -1;
+            if (take <= 0) continue;
+            for (int64_t j = 0; j < xb - xa; ++j) {
+                const float d = sqdist(y + q * D, x + (xa + j) * D, D);
+                if (radius_mode) {
+                    if (filled == take) break;
+                    if (ignore_same && xa + j == q) continue;
+                    if (d < r2) row[filled++] = xa + j;
+                    continue;
+                }
+                if (!isfinite(d)) continue;
+                if (filled == take && !knn_before(d, j, ld[take - 1], li[take - 1])) continue;
+                int64_t pos = filled < take ? filled : take - 1;
+                while (pos > 0 && knn_before(d, j, ld[pos - 1], li[pos - 1])) {
+                    ld[pos] = ld[pos - 1];
+                    li[pos] = li[pos - 1];
+                    --pos;
+                }
+                ld[pos] = d;
+                li[pos] = j;
+                if (filled < take) ++filled;
+            }
+            if (!radius_mode)
+                for (int64_t s = 0; s < filled; ++s) row[s] = xa + li[s];
+        }
+    }
+    free(ld);
+    free(li);
+}

@@ -315,6 +315,100 @@ def chamfer_cases():
     save("chamfer", **out)
 
 
+# ------------------------------------------------------------------ flat (torch_cluster) API
+def flat_cases():
+    """The CPU path of mps_pointops/flat.py: _reference_search (:248-272) for
+    padded kNN / radius indices, fps (:161-225) and the edge builders."""
+    from mps_pointops import flat as ref_flat
+    out = {}
+
+    def ptr_of(lengths):
+        p = [0]
+        for n in lengths:
+            p.append(p[-1] + n)
+        return torch.tensor(p, dtype=torch.long)
+
+    def search(name, x, y, lx, ly, width, radius=None):
+        px, py = ptr_of(lx), ptr_of(ly)
+        idx = ref_flat._reference_search(x, y, px, py, width, radius)
+        out[f"{name}/x"], out[f"{name}/y"] = x, y
+        out[f"{name}/ptr_x"], out[f"{name}/ptr_y"] = px, py
+        out[f"{name}/meta"] = np.array([width, -1.0 if radius is None else radius])
+        out[f"{name}/idx"] = idx
+
+    g = torch.Generator().manual_seed(31)
+    lx = [0, 1, 7, 33, 100, 257, 0, 64]
+    ly = [5, 3, 0, 40, 17, 90, 2, 64]
+    x = torch.randn(sum(lx), 3, generator=g)
+    y = torch.randn(sum(ly), 3, generator=g)
+    for k in (1, 5, 16, 40):
+        search(f"knn3_k{k}", x, y, lx, ly, k)
+    for r, m in ((0.5, 8), (1.0, 32), (0.21, 4), (3.0, 300)):
+        search(f"radius_r{r}_m{m}", x, y, lx, ly, m, radius=r)
+    xn, yn = x.clone(), y.clone()
+    xn[10, 0] = float("nan")
+    xn[11, 1] = float("inf")
+    xn[50, 2] = -float("inf")
+    yn[4, 0] = float("nan")
+    yn[60, 1] = float("inf")
+    search("knn3_nonfinite", xn, yn, lx, ly, 8)
+    search("radius_nonfinite", xn, yn, lx, ly, 16, radius=1.5)
+    xt = torch.randint(0, 3, (sum(lx), 3), generator=g).float()   # many exact ties
+    yt = torch.randint(0, 3, (sum(ly), 3), generator=g).float()
+    search("knn3_ties", xt, yt, lx, ly, 12)
+    search("radius_ties", xt, yt, lx, ly, 20, radius=1.0)
+    for d in (1, 5, 16, 64):
+        xf = torch.randn(sum(lx), d, generator=g)
+        yf = torch.randn(sum(ly), d, generator=g)
+        search(f"knn_d{d}", xf, yf, lx, ly, 10)
+
+    # FPS: per-cloud samples from given local starts (flat.py:213-225) and the
+    # public call with random_start=False.
+    lf = [1, 2, 30, 0, 257, 1000, 4]
+    xf = torch.randn(sum(lf), 3, generator=g)
+    starts = [0, 1, 17, 0, 200, 999, 3]
+    counts = ref_flat._sample_counts(lf, ref_flat._ratio(0.37, torch.float32), mps=True)
+    pf = ptr_of(lf).tolist()
+    samples = []
+    for b, (lo, hi) in enumerate(zip(pf, pf[1:])):
+        if counts[b]:
+            samples.append(reference.furthest_point_sample(
+                xf[lo:hi].unsqueeze(0), counts[b], start_idx=starts[b])[0] + lo)
+    out["fps_starts/x"], out["fps_starts/ptr"] = xf, torch.tensor(pf)
+    out["fps_starts/starts"] = torch.tensor(starts)
+    out["fps_starts/counts"] = torch.tensor(counts)
+    out["fps_starts/idx"] = torch.cat(samples)
+    out["fps_over/x"] = xf[:10]
+    out["fps_over/idx"] = ref_flat.fps(xf[:10], ptr=[0, 4, 10], ratio=1.7, random_start=False)
+    xd = torch.tensor([[0.0, 0, 0], [1, 0, 0], [1, 0, 0], [-1, 0, 0], [0, 1, 0], [0, 1, 0]])
+    out["fps_dup/x"] = xd
+    out["fps_dup/idx"] = ref_flat.fps(xd, ratio=1.0, random_start=False)
+
+    # Sample counts, CPU rule (float32 sizes) and GPU rule (ratio dtype).
+    lengths = list(range(0, 300))
+    for ratio in (0.05, 0.3, 1 / 3, 0.6, 0.95):
+        r = ref_flat._ratio(ratio, torch.float32)
+        out[f"counts_{ratio:.4f}/cpu"] = torch.tensor(ref_flat._sample_counts(lengths, r, mps=False))
+        out[f"counts_{ratio:.4f}/gpu"] = torch.tensor(ref_flat._sample_counts(lengths, r, mps=True))
+
+    # Public edge builders on one small ragged batch.
+    xe = torch.randn(60, 3, generator=g)
+    be = torch.tensor([0] * 20 + [1] * 15 + [3] * 25)
+    ye = torch.randn(30, 3, generator=g)
+    bye = torch.tensor([0] * 10 + [2] * 5 + [3] * 15)
+    out["edges/x"], out["edges/batch_x"] = xe, be
+    out["edges/y"], out["edges/batch_y"] = ye, bye
+    out["edges/knn"] = ref_flat.knn(xe, ye, 4, be, bye)
+    out["edges/radius"] = ref_flat.radius(xe, ye, 0.8, be, bye, max_num_neighbors=6)
+    out["edges/knn_graph"] = ref_flat.knn_graph(xe, 3, be)
+    out["edges/knn_graph_loop_t2s"] = ref_flat.knn_graph(xe, 3, be, loop=True,
+                                                          flow="target_to_source")
+    out["edges/radius_graph"] = ref_flat.radius_graph(xe, 0.9, be, max_num_neighbors=5)
+    out["edges/radius_graph_loop"] = ref_flat.radius_graph(xe, 0.9, be, loop=True,
+                                                           max_num_neighbors=5)
+    save("flat", **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     fps_cases()
@@ -323,5 +417,6 @@ if __name__ == "__main__":
     ball_query_cases()
     pointnet2_cases()
     chamfer_cases()
+    flat_cases()
     for f in sorted(OUT.glob("*.npz")):
         print(f"{f.name}: {f.stat().st_size / 1024:.0f} KiB")

@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_error_channel():
     lib = N.lib()
-    assert lib.mpo_abi_version() == N.ABI_VERSION == 2
+    assert lib.mpo_abi_version() == N.ABI_VERSION == 3
     # Argument validation happens before any CUDA call, so it runs without a GPU.
     st = lib.mpo_knn(None, None, 1, 1, 1000, 3, 300, None, None, None, None, 0, None)
     assert st == 1
@@ -48,6 +48,20 @@ def test_workspace_queries():
     assert lib.mpo_fps_workspace_bytes(8, 4096, 1024, 0) == 0
     assert lib.mpo_fps_workspace_bytes(1, 1 << 20, 65536, 0) > 0
     assert lib.mpo_fps_workspace_bytes(3, 100, 10, 2) >= 3 * 32
+    assert lib.mpo_flat_fps_workspace_bytes(5, 8192) == 0
+    assert lib.mpo_flat_fps_workspace_bytes(5, 20000) > 0
+
+
+def test_flat_entry_points_validate_before_device_work():
+    lib = N.lib()
+    st = lib.mpo_flat_knn(None, None, None, None, 1, 10, 10, 3, 300, 10, None, None, None)
+    assert st == 1 and "k must be in [0, 256]" in N.last_error()
+    st = lib.mpo_flat_knn(None, None, None, None, 1, 10, 10, 3, 4, 10, None, None, None)
+    assert st == 1 and "status" in N.last_error()
+    st = lib.mpo_flat_radius(None, None, None, None, 1, 10, -1, 0.25, 4, 0, None, None, None)
+    assert st == 1 and "negative size" in N.last_error()
+    st = lib.mpo_flat_fps(None, None, None, None, 2, 10, 4, 5, None, None, None, 0, None)
+    assert st == 1 and "status" in N.last_error()
 
 
 def test_no_oracle_in_product_package():

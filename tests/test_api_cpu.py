@@ -109,7 +109,7 @@ def test_chamfer_validation():  # tests/test_chamfer.py:285-304, test_chamfer_nd
         chamfer_distance(x.int(), y.int())
 
 
-NAMES = ["pointnet2_ops", "pointnet2_ops.pointnet2_utils", "knn_cuda"]
+NAMES = ["pointnet2_ops", "pointnet2_ops.pointnet2_utils", "knn_cuda", "torch_cluster"]
 
 
 @pytest.fixture
@@ -127,10 +127,16 @@ def test_install_serves_imports(installed):  # tests/test_compat.py:28-41
     from pointnet2_ops import pointnet2_utils
     import pointnet2_ops.pointnet2_utils as direct
 
+    from torch_cluster import fps, knn as flat_knn, knn_graph, radius, radius_graph
+
     assert direct is pointnet2_utils
     assert pointnet2_utils.furthest_point_sample is compat.furthest_point_sample
     assert pointnet2_utils.ball_query is compat.ball_query
     assert KNN is compat.KNN
+    assert fps is compat.flat.fps and flat_knn is compat.flat.knn
+    assert radius is compat.flat.radius
+    assert knn_graph is compat.flat.knn_graph and radius_graph is compat.flat.radius_graph
+    assert compat.importlib.util.find_spec("torch_cluster") is not None
 
 
 def test_install_leaves_existing_modules_alone(installed):  # tests/test_compat.py:44-52
@@ -138,6 +144,10 @@ def test_install_leaves_existing_modules_alone(installed):  # tests/test_compat.
     sys.modules["knn_cuda"] = marker
     assert "knn_cuda" not in compat.install()
     assert sys.modules["knn_cuda"] is marker
+
+    sys.modules["torch_cluster"] = marker
+    assert "torch_cluster" not in compat.install()
+    assert sys.modules["torch_cluster"] is marker
 
 
 def test_gather_and_grouping_operations():  # tests/test_compat.py:121-137
