@@ -60,7 +60,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="chamfer_config2",
                     choices=["chamfer_config2", "ssg_config1_ops", "fps_config3",
-                             "feature_knn_config4", "knn_config5", "ball_query_config5"],
+                             "feature_knn_config4", "knn_config5", "ball_query_config5",
+                             "flat_ops"],
                     help="single-GPU measurement of one BASELINE config (the default is the "
                          "headline line; the others print their own JSON line and are used "
                          "for the per-kernel profiles)")
@@ -318,6 +319,131 @@ def config5(kind: str, queries: int, steps: int, warmup: int) -> dict:
             "pairs_per_s_brute_force": queries * (1 << 20) / (ms / 1e3)}
 
 
+def _flat_public_fixture(n: int):
+    """The fixture of the reference's public flat benchmark
+    (bench/bench_flat_public.py:44-64): two randomly ordered clouds with batch
+    ids 0 and 2 (batch_size 3) of 3n/4 and n/4 points whose coordinates are
+    integers in [-128, 128] / 16, and n/32 queries taken from the clouds at a
+    regular stride."""
+    g = torch.Generator().manual_seed(7102 + n)
+    xs, ys, bx, by = [], [], [], []
+    for bid, length, nq in ((0, 3 * n // 4, 3 * n // 128), (2, n // 4, n // 128)):
+        cloud = torch.randint(-128, 129, (length, 3), generator=g).float() / 16
+        xs.append(cloud)
+        ys.append(cloud[torch.arange(nq) * length // nq])
+        bx.append(torch.full((length,), bid, dtype=torch.long))
+        by.append(torch.full((nq,), bid, dtype=torch.long))
+    return tuple(torch.cat(t) for t in (xs, ys, bx, by))
+
+
+def _flat_scale_fixture(clouds: int, seed: int):
+    """A PyG-scale ragged batch: `clouds` clouds of U[4096, 28672) points in
+    the unit cube (about 2^20 points for 64 clouds), queries = every 16th
+    point of each cloud."""
+    g = torch.Generator().manual_seed(seed)
+    lengths = torch.randint(4096, 28672, (clouds,), generator=g).tolist()
+    x = torch.rand(sum(lengths), 3, generator=g)
+    bx = torch.repeat_interleave(torch.arange(clouds), torch.tensor(lengths))
+    ptr = [0]
+    for n in lengths:
+        ptr.append(ptr[-1] + n)
+    rows = torch.cat([torch.arange(ptr[b], ptr[b + 1], 16) for b in range(clouds)])
+    return x, x[rows].contiguous(), bx, bx[rows].contiguous(), lengths
+
+
+def flat_ops(steps: int, warmup: int) -> dict:
+    """The flat torch_cluster API (mps_pointops/flat.py) on two workloads.
+    (1) The reference's public flat benchmark (bench/bench_flat_public.py):
+    N = 1024 and 4096, fps(ratio 1/64), knn(k 16), radius(2.0, 16), timed as
+    there -- public call, inputs resident, synchronized host wall time, median.
+    (2) A PyG-scale ragged batch (64 clouds, ~2^20 points, ~65k queries):
+    fps(ratio 1/16), knn(k 16), radius(0.05, 32) through the public calls
+    (host wall) and the search kernels alone (CUDA events), with the FP32
+    roofline of the kNN pair work; the oracle times the same searches on a
+    bounded query sample for the CPU baseline."""
+    from mps_pointops import flat
+    from mps_pointops import _native as N
+    res = {"workload": "flat_ops"}
+
+    def wall_ms(fn, reps):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        t = []
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter_ns()
+            fn()
+            torch.cuda.synchronize()
+            t.append((time.perf_counter_ns() - t0) / 1e6)
+        return statistics.median(t)
+
+    public = {}
+    for n in (1024, 4096):
+        x, y, bx, by = (t.cuda() for t in _flat_public_fixture(n))
+        public[str(n)] = {
+            "fps": wall_ms(lambda: flat.fps(x, bx, ratio=1 / 64, random_start=False,
+                                            batch_size=3), steps),
+            "knn": wall_ms(lambda: flat.knn(x, y, 16, bx, by, batch_size=3), steps),
+            "radius": wall_ms(lambda: flat.radius(x, y, 2.0, bx, by, max_num_neighbors=16,
+                                                  batch_size=3), steps),
+        }
+    res["public_median_ms"] = public
+
+    x, y, bx, by, lengths = _flat_scale_fixture(64, 11)
+    xc, yc, bxc, byc = x.cuda(), y.cuda(), bx.cuda(), by.cuda()
+    ptr_x, ptr_y = flat._pair_ptrs(xc, yc, bxc, byc, None)
+    pairs = sum(n * len(range(0, n, 16)) for n in lengths)
+    scale = {"clouds": 64, "points": len(x), "queries": len(y),
+             "pairs_per_search": pairs}
+    scale["public_ms"] = {
+        "fps": wall_ms(lambda: flat.fps(xc, bxc, ratio=1 / 16, random_start=False), 3),
+        "knn": wall_ms(lambda: flat.knn(xc, yc, 16, bxc, byc), steps),
+        "radius": wall_ms(lambda: flat.radius(xc, yc, 0.05, bxc, byc, max_num_neighbors=32),
+                          steps),
+    }
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    knn_ms = _event_ms(lambda: flat.knn_indices(xc, yc, ptr_x, ptr_y, 16), steps, warmup, flush)
+    rad_ms = _event_ms(lambda: flat.radius_indices(xc, yc, ptr_x, ptr_y, 0.05, 32), steps,
+                       warmup, flush)
+    mhz = _sm_max_mhz()
+    peak = 128 * torch.cuda.get_device_properties(0).multi_processor_count * mhz * 1e6 / 1e12
+    achieved = pairs * FLOPS_PER_PAIR / (knn_ms / 1e3) / 1e12
+    scale["search_ms"] = {"knn": knn_ms, "radius": rad_ms}
+    scale["knn_roofline"] = {"bound": "fp32", "achieved": achieved, "peak": peak,
+                             "unit": "TFLOP/s", "frac": achieved / peak,
+                             "note": "8 rounded FP32 ops per pair; peak = 128 lane-ops/SM/clk "
+                                     "at the max SM clock"}
+    res["scale"] = scale
+
+    # CPU baseline: the oracle's flat search on the first 2048 queries.
+    from oracle import oracle as O
+    xn, yn = x.numpy(), y.numpy()
+    pxn, pyn = ptr_x.cpu().numpy(), ptr_y.cpu().numpy()
+    sub = 2048
+    pys = np.minimum(pyn, sub)
+    t0 = time.perf_counter()
+    O.flat_knn_indices(xn, yn[:sub], pxn, pys, 16)
+    sec = time.perf_counter() - t0
+    sub_pairs = sum(int(pxn[b + 1] - pxn[b]) * int(pys[b + 1] - pys[b])
+                    for b in range(len(pxn) - 1))
+    res["cpu_baseline"] = {"value": sub / sec, "unit": "kNN queries/s", "cores": O.threads(),
+                           "kind": "port", "pairs_per_s": sub_pairs / sec,
+                           "sample": f"{sub} of {len(y)} queries of the scale batch, k=16"}
+    res["gpu_knn_queries_per_s"] = len(y) / (knn_ms / 1e3)
+    res["launches"] = N.launch_count()
+    return res
+
+
+def _sm_max_mhz() -> float:
+    try:
+        outp = subprocess.run(["nvidia-smi", "--query-gpu=clocks.max.sm", "--format=csv,noheader,nounits",
+                               "-i", "0"], capture_output=True, text=True, timeout=20).stdout
+        return float(outp.strip().splitlines()[0])
+    except Exception:  # noqa: BLE001
+        return 1965.0
+
+
 def cpu_baseline_sample(max_seconds: float = 15.0) -> dict:
     """The oracle (C restatement of the reference's CPU Chamfer search,
     mps_pointops/chamfer.py:161-251) on the bench inputs, forward + backward,
@@ -494,6 +620,8 @@ def main():
             out = ssg_config1_ops(steps, max(warmup, 3))
         elif args.workload == "fps_config3":
             out = fps_config3(min(steps, 3), 1)
+        elif args.workload == "flat_ops":
+            out = flat_ops(steps, max(warmup, 3))
         elif args.workload == "feature_knn_config4":
             flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
             out = feature_knn_secondary(steps, max(warmup, 3), 1, 0, flush)
