@@ -321,7 +321,7 @@ def config5(kind: str, queries: int, steps: int, warmup: int) -> dict:
 
 def _flat_public_fixture(n: int):
     """The fixture of the reference's public flat benchmark
-    (bench/bench_flat_public.py:44-64): two randomly ordered clouds with batch
+    (bench/bench_flat_public.py:43-61): two randomly ordered clouds with batch
     ids 0 and 2 (batch_size 3) of 3n/4 and n/4 points whose coordinates are
     integers in [-128, 128] / 16, and n/32 queries taken from the clouds at a
     regular stride."""

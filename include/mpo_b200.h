@@ -247,18 +247,18 @@ MPO_API int mpo_chamfer_check_inputs(const float* x, const float* y, const int64
                                      int64_t D, int32_t* flags, void* stream);
 
 /* ------------------------------------------------------------------ flat batches
- * The torch_cluster-style API of mps_pointops/flat.py:161-373 works on flat
+ * The torch_cluster-style API of mps_pointops/flat.py:161-425 works on flat
  * (ragged) batches: x (nx, D) reference rows and y (ny, D) query rows, sorted
  * by cloud, with int64 offset arrays ptr_x and ptr_y of `segments + 1`
  * entries (ptr[b] = first row of cloud b, ptr[segments] = the row count;
- * flat.py:68-98).  Results are GLOBAL row numbers of x.  `status` (device
+ * flat.py:67-97).  Results are GLOBAL row numbers of x.  `status` (device
  * int32, required) is zeroed by the call and then set to 1 when the offset
  * arrays do not run from 0 to the row counts without decreasing (the checks
- * of mps_pointops/_flat_search_mps.py:41-62); the search then writes nothing.
+ * of mps_pointops/_flat_search_mps.py:41-63); the search then writes nothing.
  *
- * kNN: replaces knn_indices (mps_pointops/_flat_search_mps.py:79-111,
+ * kNN: replaces knn_indices (mps_pointops/_flat_search_mps.py:79-108,
  * kernels flat_search.metal:45-150 and feature_knn.metal:166-199); contract
- * of the CPU path flat.py:248-272 (_reference_search): out (ny, k) holds the
+ * of the CPU path flat.py:264-288 (_reference_search): out (ny, k) holds the
  * k nearest rows of each query's cloud in ascending (squared distance, index)
  * order, non-finite distances dropped, -1 padding.  k <= 256.
  * max_segment_x: the longest reference cloud (an upper bound is allowed; it
@@ -268,20 +268,20 @@ MPO_API int mpo_flat_knn(const float* x, const float* y, const int64_t* ptr_x,
                          int64_t D, int64_t k, int64_t max_segment_x, int64_t* out,
                          int32_t* status, void* stream);
 
-/* Radius: replaces radius_indices (mps_pointops/_flat_search_mps.py:114-147,
- * kernel flat_search.metal:160-226); contract of flat.py:248-272: out
+/* Radius: replaces radius_indices (mps_pointops/_flat_search_mps.py:111-147,
+ * kernel flat_search.metal:172-276); contract of flat.py:264-288: out
  * (ny, max_neighbors) holds the first max_neighbors rows of the query's cloud
  * IN INPUT ORDER whose squared distance is < radius_sq, -1 padding.  D = 3.
- * radius_sq = fl32(r * r) with r * r in double (_flat_search_mps.py:65-76).
+ * radius_sq = fl32(r * r) with r * r in double (_flat_search_mps.py:66-76).
  * ignore_same_index != 0 skips the x row whose global number equals the
- * query's, before the cap (pyg-lib's radius; mps_pointops/pyg.py:92-124). */
+ * query's, before the cap (pyg-lib's radius; mps_pointops/pyg.py:100-126). */
 MPO_API int mpo_flat_radius(const float* x, const float* y, const int64_t* ptr_x,
                             const int64_t* ptr_y, int64_t segments, int64_t nx, int64_t ny,
                             float radius_sq, int64_t max_neighbors, int ignore_same_index,
                             int64_t* out, int32_t* status, void* stream);
 
 /* FPS: replaces fps_flat (mps_pointops/_flat_fps_mps.py:35-96, kernel
- * fps_flat.metal); contract of flat.py:161-225 with the per-cloud sampling of
+ * fps_flat.metal); contract of flat.py:161-217 with the per-cloud sampling of
  * mps_pointops/reference.py:27-58.  Cloud b (rows ptr[b] .. ptr[b+1] of x,
  * D = 3) yields out_ptr[b+1] - out_ptr[b] samples into out[out_ptr[b] ..],
  * as global rows, starting from the LOCAL index starts[b] (device int64).
@@ -290,7 +290,7 @@ MPO_API int mpo_flat_radius(const float* x, const float* y, const int64_t* ptr_x
  * and need mpo_flat_fps_workspace_bytes(segments, max_len) of workspace).
  * status: 0, 1 (a group exchange timed out), or 2 (a cloud with samples is
  * empty, longer than max_len, or its start is out of range: the checks of
- * _flat_fps_mps.py:72-86; that cloud's samples are not written). */
+ * _flat_fps_mps.py:67-80; that cloud's samples are not written). */
 MPO_API size_t mpo_flat_fps_workspace_bytes(int64_t segments, int64_t max_len);
 MPO_API int mpo_flat_fps(const float* x, const int64_t* ptr, const int64_t* out_ptr,
                          const int64_t* starts, int64_t segments, int64_t total_n,

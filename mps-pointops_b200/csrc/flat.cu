@@ -1,6 +1,6 @@
 // Offset checks of the flat (ragged) batch layout, run on the device ahead of
 // the flat searches.  The reference validates its ptr arrays on the host
-// (gamzerA/mps-pointops mps_pointops/_flat_search_mps.py:41-62, raising
+// (gamzerA/mps-pointops mps_pointops/_flat_search_mps.py:41-63, raising
 // "ptr_x must start at 0 and end at ..." or "... must be nondecreasing ...");
 // here the check runs on the stream, the searches that follow skip their work
 // when it failed (segments.cuh), and the caller reads the flag.

@@ -1,7 +1,7 @@
 // Batch layouts shared by the search kernels: dense batches of equal-size
 // clouds and the flat (ragged) batches of the torch_cluster API, whose
 // sorted segments are given by offset arrays (gamzerA/mps-pointops
-// mps_pointops/flat.py:68-98: ptr[b] = first row of segment b, ptr[B] = the
+// mps_pointops/flat.py:67-97: ptr[b] = first row of segment b, ptr[B] = the
 // row count).
 //
 // A search kernel processes a tile of `qpc` consecutive query rows per CTA,

@@ -15,11 +15,11 @@ every other request on a non-CUDA tensor raises ``RuntimeError``.
 Device rules (the reference's GPU rules, with CUDA in place of MPS):
   * FPS and kNN take float32 points; radius takes float16 or float32, and
     float16 points are widened to float32 before the search (the widening of
-    flat_search.metal:163-170, exact).
+    flat_search.metal:164-167, exact).
   * FPS sample counts use the GPU rule of torch_cluster: the batch sizes are
-    converted to the ratio's dtype before the product (flat.py:149-158).
+    converted to the ratio's dtype before the product (flat.py:150-158).
   * kNN serves an effective k = min(k, len(x)) of at most 256.
-Arithmetic follows the reference's CPU path (flat.py:236-272): squared
+Arithmetic follows the reference's CPU path (flat.py:256-288): squared
 distances ((d0*d0 + d1*d1) + d2*d2) with each operation rounded on its own,
 kNN in ascending (squared distance, index) order with every non-finite
 distance dropped, radius ``d2 < fl32(r * r)`` with ``r * r`` in double.
@@ -93,7 +93,7 @@ def _check_batch(batch: Tensor | None, count: int, device: torch.device, name: s
 
 
 def _ptr_from_batch(batch: Tensor | None, count: int, device: torch.device, size: int) -> Tensor:
-    """Segment offsets of a sorted batch vector (flat.py:68-77)."""
+    """Segment offsets of a sorted batch vector (flat.py:67-76)."""
     if batch is None:
         # A missing batch vector means one point cloud, even if it is empty.
         return torch.tensor([0, count], dtype=torch.long, device=device)
@@ -105,7 +105,7 @@ def _ptr_from_batch(batch: Tensor | None, count: int, device: torch.device, size
 
 def _pair_ptrs(x: Tensor, y: Tensor, batch_x: Tensor | None, batch_y: Tensor | None,
                batch_size: int | None) -> tuple[Tensor, Tensor]:
-    """flat.py:80-98: both offset arrays over the same number of batch slots."""
+    """flat.py:79-97: both offset arrays over the same number of batch slots."""
     explicit_size = _batch_size(batch_size)
     size_x = _check_batch(batch_x, len(x), x.device, "batch_x")
     size_y = _check_batch(batch_y, len(y), y.device, "batch_y")
@@ -122,7 +122,7 @@ def _pair_ptrs(x: Tensor, y: Tensor, batch_x: Tensor | None, batch_y: Tensor | N
 
 def _fps_ptr(x: Tensor, batch: Tensor | None, batch_size: int | None,
              ptr: Tensor | Sequence[int] | None) -> Tensor:
-    """flat.py:101-123: ``ptr`` wins over ``batch``."""
+    """flat.py:100-122: ``ptr`` wins over ``batch``."""
     if ptr is not None:
         if isinstance(ptr, Tensor):
             if ptr.device != x.device or ptr.dtype not in (torch.int32, torch.int64):
@@ -151,7 +151,7 @@ def _fps_ptr(x: Tensor, batch: Tensor | None, batch_size: int | None,
 
 
 def _ratio(value: float | Tensor | None, dtype: torch.dtype) -> Tensor:
-    """The CPU scalar tensor torch_cluster would use as the ratio (flat.py:126-146).
+    """The CPU scalar tensor torch_cluster would use as the ratio (flat.py:125-147).
 
     A Python ratio becomes a tensor of the points' dtype; a tensor ratio keeps
     its dtype and shape, which decide the precision of the sample counts.
@@ -172,7 +172,7 @@ def _ratio(value: float | Tensor | None, dtype: torch.dtype) -> Tensor:
 
 
 def _sample_counts(lengths: list[int], ratio: Tensor, *, gpu: bool) -> list[int]:
-    """torch_cluster's degree conversion and ceiling (flat.py:149-158).
+    """torch_cluster's degree conversion and ceiling (flat.py:150-158).
 
     Its CPU path converts the batch sizes to float32; its GPU path to the
     ratio's dtype.  Torch scalar promotion then depends on whether a tensor
@@ -202,7 +202,7 @@ def fps(
     batch_size: int | None = None,
     ptr: Tensor | Sequence[int] | None = None,
 ) -> Tensor:
-    """Sample global point indices with the torch_cluster count rule (flat.py:161-225).
+    """Sample global point indices with the torch_cluster count rule (flat.py:161-217).
 
     Each cloud yields ``ceil(len * ratio)`` samples (``ratio=None`` means 0.5)
     by farthest point sampling from a random point (``random_start``) or its
@@ -270,13 +270,13 @@ def _nonnegative_int(value: int, name: str) -> int:
 
 
 def _check_cuda_knn_width(width: int) -> None:
-    """Reject requests the flat kNN kernels cannot serve (flat.py:247-254)."""
+    """Reject requests the flat kNN kernels cannot serve (flat.py:238-244)."""
     if width > _CUDA_KNN_MAX_K:
         raise ValueError(f"effective k must be at most {_CUDA_KNN_MAX_K} on CUDA, got {width}")
 
 
 def _edges(indices: Tensor) -> Tensor:
-    """(ny, width) padded global indices -> [query, reference] edges (flat.py:257-263)."""
+    """(ny, width) padded global indices -> [query, reference] edges (flat.py:247-253)."""
     if indices.numel() == 0:
         return torch.empty((2, 0), dtype=torch.long, device=indices.device)
     valid = indices >= 0
@@ -287,7 +287,7 @@ def _edges(indices: Tensor) -> Tensor:
 
 def _radius_sq(r: float) -> float:
     """fl32(r * r) with r * r in double: the threshold torch_cluster compares
-    against (mps_pointops/_flat_search_mps.py:65-76)."""
+    against (mps_pointops/_flat_search_mps.py:66-76)."""
     try:
         return struct.unpack("f", struct.pack("f", r * r))[0]
     except OverflowError:
@@ -302,7 +302,7 @@ def _longest(ptr: Tensor) -> int:
 
 def knn_indices(x: Tensor, y: Tensor, ptr_x: Tensor, ptr_y: Tensor, k: int) -> Tensor:
     """(len(y), k) global x indices per query in (squared distance, index)
-    order, -1 padded: the flat kNN kernel call (_flat_search_mps.py:79-111)."""
+    order, -1 padded: the flat kNN kernel call (_flat_search_mps.py:79-108)."""
     out = torch.empty((y.shape[0], k), dtype=torch.int64, device=x.device)
     if y.shape[0] == 0 or k == 0:
         return out
@@ -320,7 +320,7 @@ def knn_indices(x: Tensor, y: Tensor, ptr_x: Tensor, ptr_y: Tensor, k: int) -> T
 def radius_indices(x: Tensor, y: Tensor, ptr_x: Tensor, ptr_y: Tensor, r: float,
                    max_num_neighbors: int, ignore_same_index: bool = False) -> Tensor:
     """(len(y), max_num_neighbors) first global x indices in input order with
-    squared distance < fl32(r * r), -1 padded (_flat_search_mps.py:114-147).
+    squared distance < fl32(r * r), -1 padded (_flat_search_mps.py:111-147).
     ``ignore_same_index`` drops the x row whose global index equals the
     query's before the cap (pyg-lib's radius)."""
     # The reference's GPU path validates r like its ball query: it must round
@@ -354,7 +354,7 @@ def knn(
     num_workers: int = 1,
     batch_size: int | None = None,
 ) -> Tensor:
-    """Global ``[query, reference]`` edges to the nearest points (flat.py:275-314).
+    """Global ``[query, reference]`` edges to the nearest points (flat.py:291-329).
 
     ``batch_size`` sets the number of batch slots, including empty ones.  x and
     y are coordinate or feature vectors with D >= 1; the effective neighbour
@@ -389,7 +389,7 @@ def radius(
     ignore_same_index: bool = False,
 ) -> Tensor:
     """Global ``[query, reference]`` edges with squared distance ``< r²``
-    (flat.py:317-363): neighbours in reference input order, at most
+    (flat.py:332-373): neighbours in reference input order, at most
     ``max_num_neighbors`` per query.  ``ignore_same_index=True`` is not
     implemented here (the PyG operator surface in :mod:`mps_pointops.pyg`
     offers it); ``num_workers`` is accepted for call-site compatibility.
@@ -434,7 +434,7 @@ def knn_graph(
     num_workers: int = 1,
     batch_size: int | None = None,
 ) -> Tensor:
-    """kNN graph with ``torch_cluster`` 1.6.3 edge orientation (flat.py:376-393)."""
+    """kNN graph with ``torch_cluster`` 1.6.3 edge orientation (flat.py:386-404)."""
     k = _nonnegative_int(k, "k")
     if flow not in ("source_to_target", "target_to_source"):
         raise ValueError("flow must be 'source_to_target' or 'target_to_source'")
@@ -455,7 +455,7 @@ def radius_graph(
     num_workers: int = 1,
     batch_size: int | None = None,
 ) -> Tensor:
-    """Radius graph with ``torch_cluster`` 1.6.3 edge orientation (flat.py:396-413)."""
+    """Radius graph with ``torch_cluster`` 1.6.3 edge orientation (flat.py:407-425)."""
     limit = _nonnegative_int(max_num_neighbors, "max_num_neighbors")
     if flow not in ("source_to_target", "target_to_source"):
         raise ValueError("flow must be 'source_to_target' or 'target_to_source'")

@@ -22,7 +22,7 @@ _CUDA_LIBRARY: torch.library.Library | None = None
 
 def _ptrs(x: Tensor, y: Tensor, ptr_x: Tensor | None, ptr_y: Tensor | None,
           *, feature_space: bool = False) -> tuple[Tensor, Tensor]:
-    """pyg.py:56-69: an unbatched x is the full reference set, even when y has
+    """pyg.py:57-69: an unbatched x is the full reference set, even when y has
     a batch pointer (pyg-lib then ignores ptr_y)."""
     flat._search_inputs(x, y, feature_space=feature_space)
     if ptr_x is None:
@@ -35,7 +35,7 @@ def _ptrs(x: Tensor, y: Tensor, ptr_x: Tensor | None, ptr_y: Tensor | None,
 
 def _check_inputs(x: Tensor, y: Tensor, ptr_x: Tensor, ptr_y: Tensor, *,
                   feature_space: bool = False) -> tuple[int, int]:
-    """The offset checks of mps_pointops/_flat_search_mps.py:41-62, with CUDA in
+    """The offset checks of mps_pointops/_flat_search_mps.py:41-63, with CUDA in
     place of MPS.  The search kernels check the offsets again on the device."""
     if (x.ndim != 2 or y.ndim != 2 or x.shape[1] < 1
             or x.shape[1] != y.shape[1] or (not feature_space and x.shape[1] != 3)):
@@ -61,7 +61,7 @@ def _check_inputs(x: Tensor, y: Tensor, ptr_x: Tensor, ptr_y: Tensor, *,
 
 def _knn_cuda(x: Tensor, y: Tensor, ptr_x: Tensor | None = None, ptr_y: Tensor | None = None,
               k: int = 1, cosine: bool = False, num_workers: int = 1) -> Tensor:
-    """pyg-lib's query-major ``[query, reference]`` kNN edges (pyg.py:72-95)."""
+    """pyg-lib's query-major ``[query, reference]`` kNN edges (pyg.py:72-97)."""
     ptr_x, ptr_y = _ptrs(x, y, ptr_x, ptr_y, feature_space=True)
     _check_inputs(x, y, ptr_x, ptr_y, feature_space=True)
     k = flat._nonnegative_int(k, "k")
@@ -82,7 +82,7 @@ def _radius_cuda(x: Tensor, y: Tensor, ptr_x: Tensor | None = None,
                  ptr_y: Tensor | None = None, r: float = 1.0, max_num_neighbors: int = 32,
                  num_workers: int = 1, ignore_same_index: bool = False) -> Tensor:
     """The first neighbours in x order, optionally omitting the x row with
-    the query's own global index (pyg.py:98-124)."""
+    the query's own global index (pyg.py:100-126)."""
     ptr_x, ptr_y = _ptrs(x, y, ptr_x, ptr_y)
     _check_inputs(x, y, ptr_x, ptr_y)
     limit = flat._nonnegative_int(max_num_neighbors, "max_num_neighbors")
@@ -98,13 +98,13 @@ def _radius_cuda(x: Tensor, y: Tensor, ptr_x: Tensor | None = None,
 
 
 def _fps_cuda(src: Tensor, ptr: Tensor, ratio: float = 0.5, random_start: bool = True) -> Tensor:
-    """pyg-lib's pointer-shaped FPS call surface (pyg.py:127-129)."""
+    """pyg-lib's pointer-shaped FPS call surface (pyg.py:129-131)."""
     return flat.fps(src, ratio=ratio, random_start=random_start, ptr=ptr)
 
 
 def register_cuda(*, override: bool = False) -> list[str]:
     """Register these kernels as CUDA implementations of ``pyg::fps``,
-    ``pyg::knn`` and ``pyg::radius`` (the role of register_mps, pyg.py:140-181).
+    ``pyg::knn`` and ``pyg::radius`` (the role of register_mps, pyg.py:144-181).
 
     Requires pyg-lib 0.6 or newer, whose operator schemas these functions
     implement.  An operator that already has a CUDA kernel (pyg-lib's own) is

@@ -306,14 +306,14 @@ def chamfer_mean_loss_and_grad(x, y, x_lengths=None, y_lengths=None):
 
 # ---------------------------------------------------------------- flat batches
 def flat_sample_counts(lengths, ratio: float, ratio_dtype=np.float32) -> list[int]:
-    """torch_cluster's GPU count rule (mps_pointops/flat.py:149-158): the batch
+    """torch_cluster's GPU count rule (mps_pointops/flat.py:150-158): the batch
     sizes are converted to the ratio's dtype, multiplied, ceiled."""
     sizes = np.asarray(lengths, dtype=ratio_dtype)
     return [int(v) for v in np.ceil(sizes * ratio_dtype(ratio))]
 
 
 def torch_cluster_radius_sq(r: float) -> float:
-    """fl32(r * r) with r * r in double (mps_pointops/_flat_search_mps.py:65-76)."""
+    """fl32(r * r) with r * r in double (mps_pointops/_flat_search_mps.py:66-76)."""
     with np.errstate(over="ignore"):
         return float(np.float32(r * r))
 
@@ -343,7 +343,7 @@ def _flat_search(x, y, ptr_x, ptr_y, width, radius_mode, r2=0.0, ignore_same=Fal
 
 
 def flat_knn_indices(x, y, ptr_x, ptr_y, width: int) -> np.ndarray:
-    """mps_pointops/flat.py:248-272, kNN branch: (ny, width) global x rows in
+    """mps_pointops/flat.py:264-288, kNN branch: (ny, width) global x rows in
     ascending (SD, index) order over the query's cloud, non-finite SD dropped,
     -1 padded."""
     return _flat_search(x, y, ptr_x, ptr_y, width, False)
@@ -351,14 +351,14 @@ def flat_knn_indices(x, y, ptr_x, ptr_y, width: int) -> np.ndarray:
 
 def flat_radius_indices(x, y, ptr_x, ptr_y, r: float, width: int,
                         ignore_same_index: bool = False) -> np.ndarray:
-    """mps_pointops/flat.py:248-272, radius branch: the first `width` global x
+    """mps_pointops/flat.py:264-288, radius branch: the first `width` global x
     rows of the query's cloud in input order with SD < fl32(r * r)."""
     return _flat_search(x, y, ptr_x, ptr_y, width, True, torch_cluster_radius_sq(r),
                         ignore_same_index)
 
 
 def flat_fps(x, ptr, counts, starts) -> np.ndarray:
-    """mps_pointops/flat.py:213-225: per cloud, reference.furthest_point_sample
+    """mps_pointops/flat.py:208-217: per cloud, reference.furthest_point_sample
     from the local index starts[b] (reference.py:27-58), shifted to global rows."""
     lib = _load()
     x = _f32(x)
@@ -381,6 +381,6 @@ def flat_fps(x, ptr, counts, starts) -> np.ndarray:
 
 
 def flat_edges(indices: np.ndarray) -> np.ndarray:
-    """mps_pointops/flat.py:257-263: padded rows -> [query, reference] edges."""
+    """mps_pointops/flat.py:247-253: padded rows -> [query, reference] edges."""
     q, s = np.nonzero(indices >= 0)
     return np.stack([q.astype(np.int64), indices[q, s]])

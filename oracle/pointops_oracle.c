@@ -366,19 +366,19 @@ EXPORT double oracle_chamfer_mean_loss_and_grad(
 }
 
 /* ------------------------------------------------------------------ flat batches
- * mps_pointops/flat.py:236-272 (_sqdist, _reference_search): the CPU path of
+ * mps_pointops/flat.py:256-288 (_sqdist, _reference_search): the CPU path of
  * the torch_cluster-style flat API.  x (nx, D) reference rows and y (ny, D)
  * query rows are split into `segs` clouds by the offset arrays ptr_x and
- * ptr_y (segs + 1 entries, flat.py:68-98).  For every query row q of cloud b
+ * ptr_y (segs + 1 entries, flat.py:67-97).  For every query row q of cloud b
  * the row out[q, :width] receives GLOBAL x rows, -1 padded:
  *   kNN    (radius_mode 0): torch.argsort(d2, stable=True) over the cloud,
  *          keep the finite d2 (torch.isfinite), first min(width, cloud size)
  *          -- the ascending (d2, index) order without non-finite entries.
  *   radius (radius_mode 1): torch.nonzero(d2 < r2)[:take] -- the first rows
  *          in input order with d2 < r2, r2 = fl32(r * r), r * r in double
- *          (flat.py:260; mps_pointops/_flat_search_mps.py:65-76).  With
+ *          (flat.py:272, 286; mps_pointops/_flat_search_mps.py:66-76).  With
  *          ignore_same != 0 the x row whose global number equals q's is
- *          skipped before the cap (pyg-lib's radius, flat_search.metal:196).
+ *          skipped before the cap (pyg-lib's radius, flat_search.metal:199).
  * d2 = _sqdist(y[q], x[j]) = sequential sum of (x - y)^2, each op rounded.
  * Only the query rows in [q_lo, q_hi) are written, so host threads can split
  * the queries without changing any result. */

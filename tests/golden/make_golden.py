@@ -317,8 +317,8 @@ def chamfer_cases():
 
 # ------------------------------------------------------------------ flat (torch_cluster) API
 def flat_cases():
-    """The CPU path of mps_pointops/flat.py: _reference_search (:248-272) for
-    padded kNN / radius indices, fps (:161-225) and the edge builders."""
+    """The CPU path of mps_pointops/flat.py: _reference_search (:264-288) for
+    padded kNN / radius indices, fps (:161-217) and the edge builders."""
     from mps_pointops import flat as ref_flat
     out = {}
 
@@ -362,7 +362,7 @@ def flat_cases():
         yf = torch.randn(sum(ly), d, generator=g)
         search(f"knn_d{d}", xf, yf, lx, ly, 10)
 
-    # FPS: per-cloud samples from given local starts (flat.py:213-225) and the
+    # FPS: per-cloud samples from given local starts (flat.py:208-217) and the
     # public call with random_start=False.
     lf = [1, 2, 30, 0, 257, 1000, 4]
     xf = torch.randn(sum(lf), 3, generator=g)

@@ -22,7 +22,7 @@ from oracle import oracle as O
 
 # ------------------------------------------------------------------ oracle pins
 def test_oracle_matches_reference_flat_search():
-    """tests/golden/flat.npz: mps_pointops/flat.py:248-272 on ragged batches
+    """tests/golden/flat.npz: mps_pointops/flat.py:264-288 on ragged batches
     with empty clouds, non-finite coordinates, exact ties and D in {1..64}."""
     cases = golden("flat")
     n = 0
@@ -81,7 +81,7 @@ def bipartite():
 
 def test_oracle_known_answers_from_reference_tests():
     x, y, px, py = bipartite()
-    # tests/test_flat.py:49-55, 69-78, 20-24
+    # tests/test_flat.py:49-54, 69-77, 20-24
     assert O.flat_edges(O.flat_knn_indices(x, y, px, py, 2)).tolist() == [
         [0, 0, 2, 2, 3, 3], [0, 1, 3, 4, 4, 3]]
     assert O.flat_edges(O.flat_knn_indices(x, y, px, py, 5)).shape == (2, 7)
@@ -96,7 +96,7 @@ def test_oracle_known_answers_from_reference_tests():
     xn = np.array([[0., 0, 0], [np.nan, 0, 0], [np.inf, 0, 0]], np.float32)
     yn = np.array([[0., 0, 0], [np.nan, 0, 0]], np.float32)
     assert O.flat_edges(O.flat_knn_indices(xn, yn, [0, 3], [0, 2], 3)).tolist() == [[0], [0]]
-    # tests/test_pyg28.py:52-57: ignore_same_index drops x row 0 before the cap.
+    # tests/test_pyg28.py:53-58: ignore_same_index drops x row 0 before the cap.
     xs = np.array([[0., 0, 0], [0.1, 0, 0], [0.2, 0, 0]], np.float32)
     assert O.flat_edges(O.flat_radius_indices(xs, xs[:1], [0, 3], [0, 1], 1.0, 1,
                                               ignore_same_index=True)).tolist() == [[0], [1]]
@@ -171,7 +171,7 @@ def test_fps_validation():  # tests/test_flat.py:36-46
         flat.fps(torch.zeros(4, 3, dtype=torch.long))
 
 
-def test_search_validation():  # tests/test_flat.py:95-105
+def test_search_validation():  # tests/test_flat.py:95-104
     x, y, bx, by = tbipartite()
     with pytest.raises(NotImplementedError, match="cosine"):
         flat.knn(x, y, 2, cosine=True)
@@ -200,7 +200,7 @@ def test_search_validation():  # tests/test_flat.py:95-105
 
 
 def test_sample_count_rules():
-    # tests/test_flat.py:160-199: torch_cluster's float32 product rounds up.
+    # tests/test_flat.py:172-199: torch_cluster's float32 product rounds up.
     for n, ratio, want in ((25, 0.6, 16), (45, 0.6, 28), (50, 0.3, 16), (90, 0.3, 28),
                            (10, 0.5, 5), (7, 0.5, 4), (9, 1.0, 9)):
         r = flat._ratio(ratio, torch.float32)

@@ -106,12 +106,12 @@ def test_reference_known_answers(cuda_device):
     assert flat.fps(x, ptr=[0, 3, 3, 5], ratio=0.5, random_start=False).tolist() == [0, 2, 3]
     assert flat.fps(x, bx, ratio=0, random_start=False).shape == (0,)
     assert flat.fps(x, ratio=1.1, random_start=False).shape == (6,)
-    # :49-55
+    # :49-54
     edge = flat.knn(x, y, 2, bx, by)
     assert edge.dtype == torch.long and edge.device == x.device
     assert edge.tolist() == [[0, 0, 2, 2, 3, 3], [0, 1, 3, 4, 4, 3]]
     assert flat.knn(x, y, 5, bx, by).shape == (2, 7)
-    # :69-78
+    # :69-77
     assert flat.radius(x, y, 1.1, bx, by, max_num_neighbors=2).tolist() == [
         [0, 0, 2, 2], [0, 1, 3, 4]]
     assert flat.radius(x[:2], x[:1], 1.0).tolist() == [[0], [0]]
@@ -133,7 +133,7 @@ def test_knn_excludes_nonfinite_coordinates(cuda_device):  # tests/test_flat.py:
 
 
 @pytest.mark.parametrize("dimensions", [3, 64])
-def test_large_effective_k_is_explicit_error(cuda_device, dimensions):  # :127-142
+def test_large_effective_k_is_explicit_error(cuda_device, dimensions):  # :128-142
     x = torch.arange(300, dtype=torch.float32)[:, None].expand(-1, dimensions).contiguous()
     x = x.to(cuda_device)
     y = x[:1]
@@ -150,7 +150,7 @@ def test_large_effective_k_is_explicit_error(cuda_device, dimensions):  # :127-1
 @pytest.mark.parametrize("n, ratio, expected", [
     (25, 0.6, 16), (45, 0.6, 28), (50, 0.3, 16), (90, 0.3, 28), (10, 0.5, 5), (7, 0.5, 4),
     (9, 1.0, 9)])
-def test_fps_sample_counts(cuda_device, n, ratio, expected):  # :160-174
+def test_fps_sample_counts(cuda_device, n, ratio, expected):  # :172-174
     x = torch.rand(n, 3, device=cuda_device)
     assert len(flat.fps(x, ratio=ratio, random_start=False)) == expected
 
@@ -186,7 +186,7 @@ def test_cuda_dtype_rules(cuda_device):
 
 
 # ------------------------------------------------------------------ pyg surface
-def test_pyg_surface_known_answers(cuda_device):  # tests/test_pyg28.py:27-127
+def test_pyg_surface_known_answers(cuda_device):  # tests/test_pyg28.py:27-106
     x = torch.tensor([[0.0, 0, 0], [1.0, 0, 0], [10.0, 0, 0], [11.0, 0, 0]], device=cuda_device)
     y = torch.tensor([[0.1, 0, 0], [10.1, 0, 0]], device=cuda_device)
     ptr_x = torch.tensor([0, 2, 4], device=cuda_device)
