@@ -75,7 +75,7 @@ def _knn_cuda(x: Tensor, y: Tensor, ptr_x: Tensor | None = None, ptr_y: Tensor |
     width = min(k, len(x))
     flat._check_cuda_knn_width(width)
     N.require_cuda(x, "pyg knn")
-    return flat._edges(flat.knn_indices(x, y, ptr_x, ptr_y, width))
+    return flat._edges(flat.knn_indices(x, y, ptr_x, ptr_y, width, check=False))
 
 
 def _radius_cuda(x: Tensor, y: Tensor, ptr_x: Tensor | None = None,
@@ -94,7 +94,7 @@ def _radius_cuda(x: Tensor, y: Tensor, ptr_x: Tensor | None = None,
     width = min(limit, len(x))
     N.require_cuda(x, "pyg radius")
     return flat._edges(flat.radius_indices(x, y, ptr_x, ptr_y, r, width,
-                                           ignore_same_index=ignore_same_index))
+                                           ignore_same_index=ignore_same_index, check=False))
 
 
 def _fps_cuda(src: Tensor, ptr: Tensor, ratio: float = 0.5, random_start: bool = True) -> Tensor:
