@@ -10,13 +10,19 @@
 // (mps_pointops/compat.py:76-85) repeats the first hit in empty slots (all
 // zeros without a hit) and writes int32.
 //
-// Design (B200): one warp per query scans the reference cloud in input order,
-// 128 points per step (four independent 32-point chunks, so the loads of a
-// step overlap).  Each lane evaluates one point; __ballot_sync gives
-// the hit mask and __popc(mask & lanes_below) the rank of each hit, so the
-// hits land in their output slots in order with no serial scan.  The warp
-// stops as soon as K hits are found (on uniform clouds that is a small
-// prefix of the cloud), then writes the padding.  Eight queries per CTA.
+// Design (B200): one warp per query scans the reference cloud in input order;
+// the eight queries of a CTA (one cloud or segment) share reference tiles of
+// kTile points in shared memory.  A warp step covers 128 references, four
+// per lane (lane l takes points 4l .. 4l+3), evaluated as two packed f32x2
+// pairs with the query duplicated in both halves, from a tile stored as
+// float4s A[g] = (x0, x1, y0, y1), B[g] = (x2, x3, y2, y3), Z[g] = (z0 .. z3)
+// per group of four points (a lane's three loads are consecutive across the
+// warp).  One min over the lane's four distances and a ballot skip steps
+// without hits.  Otherwise each lane's hit count (0..4) is spread over three
+// ballots, whose popcounts below the lane give its exclusive prefix, so the
+// hits land in their output slots in input order with no serial scan.  A
+// warp stops as soon as K hits are found; the CTA stops loading tiles once
+// all its warps have stopped.
 #include <string>
 
 #include "../../include/mpo_b200.h"
@@ -27,6 +33,7 @@ namespace mpo {
 namespace {
 
 constexpr int kWarpsPerCta = 8;
+constexpr int kTile = 2048;  // reference points per shared-memory tile (multiple of 128)
 
 template <bool POINTNET2, bool FLAT>
 __global__ void __launch_bounds__(32 * kWarpsPerCta)
@@ -35,62 +42,104 @@ ball_query_kernel(const float* __restrict__ query, const float* __restrict__ ref
                   const int64_t* __restrict__ ref_lengths, Layout L, int64_t K, float r2,
                   int ignore_same, float* __restrict__ dist2, int64_t* __restrict__ idx64,
                   int32_t* __restrict__ idx32) {
+    __shared__ float4 tA[kTile / 4], tB[kTile / 4], tZ[kTile / 4];
     const int lane = threadIdx.x & 31;
     Span sp;
-    if (!locate<FLAT>(L, kWarpsPerCta, sp)) return;
+    if (!locate<FLAT>(L, kWarpsPerCta, sp)) return;  // CTA-uniform
     const int64_t q = sp.q0 + (threadIdx.x >> 5);  // global query row
-    if (q >= sp.q1) return;
+    const bool in_range = q < sp.q1;
     const size_t row = (size_t)q * (size_t)K;
     int64_t nl = sp.n;
-    bool live = true;
+    bool live = in_range;
     if (!FLAT) {
         const int64_t b = blockIdx.y;
-        if (query_lengths) live = q - b * L.M < query_lengths[b];
-        if (ref_lengths) nl = min64(ref_lengths[b], L.N);
+        if (query_lengths && in_range) live = q - b * L.M < query_lengths[b];
+        if (ref_lengths) nl = max64(0, min64(ref_lengths[b], L.N));
     }
     const unsigned below = (1u << lane) - 1u;
+    float qx = 0.f, qy = 0.f, qz = 0.f;
+    if (live) {
+        const float* qp = query + (size_t)q * 3;
+        qx = qp[0];
+        qy = qp[1];
+        qz = qp[2];
+    }
+    const f32x2 X = pack2(qx, qx), Y = pack2(qy, qy), Z = pack2(qz, qz);
+    // A flat search with ignore_same skips the reference whose global row
+    // equals the query's (local row `self`), before the cap.
+    const int64_t self = (FLAT && ignore_same) ? q - sp.obase : -1;
+    const float* __restrict__ r = ref + (size_t)sp.r0 * 3;
+    const int u = threadIdx.x & 3;  // tile fill: fixed place in its group
+    float* const fxy = reinterpret_cast<float*>(u < 2 ? tA : tB);
+    float* const fz = reinterpret_cast<float*>(tZ);
 
     int64_t found = 0;
     int64_t first = -1;
-    if (live) {
-        const float* qp = query + (size_t)q * 3;
-        const float qx = qp[0], qy = qp[1], qz = qp[2];
-        const float* __restrict__ r = ref + (size_t)sp.r0 * 3;
-        // A flat search with ignore_same skips the reference whose global row
-        // equals the query's (local row `self`), before the cap.
-        const int64_t self = (FLAT && ignore_same) ? q - sp.obase : -1;
-        // Four 32-point chunks per iteration: their loads are independent,
-        // so a lane has 12 loads in flight; hits are still ranked in input
-        // order chunk by chunk.
-        constexpr int kU = 4;
-        for (int64_t j0 = 0; j0 < nl && found < K; j0 += 32 * kU) {
-            float d[kU];
+    bool scanning = live && K > 0;
+    for (int64_t t0 = 0; t0 < nl; t0 += kTile) {
+        if (!__syncthreads_or(scanning)) break;  // also guards the tile reuse
+        const int tn = (int)min64(kTile, nl - t0);
+        for (int p = threadIdx.x; p < tn; p += 32 * kWarpsPerCta) {
+            const float* rp = r + (size_t)(t0 + p) * 3;
+            const int g = p >> 2;
+            fxy[4 * g + (u & 1)] = rp[0];
+            fxy[4 * g + 2 + (u & 1)] = rp[1];
+            fz[4 * g + u] = rp[2];
+        }
+        __syncthreads();
+        if (!scanning) continue;
+        for (int c0 = 0; c0 < tn; c0 += 128) {
+            const int g = (c0 >> 2) + lane;
+            const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(tA + g);
+            const ulonglong2 bb = *reinterpret_cast<const ulonglong2*>(tB + g);
+            const ulonglong2 z = *reinterpret_cast<const ulonglong2*>(tZ + g);
+            float d[4];
+            unpack2(sqd3x2(X, Y, Z, a.x, a.y, z.x), d[0], d[1]);
+            unpack2(sqd3x2(X, Y, Z, bb.x, bb.y, z.y), d[2], d[3]);
+            // fminf ignores NaN, which never matches anyway.
+            const float m = fminf(fminf(d[0], d[1]), fminf(d[2], d[3]));
+            if (__ballot_sync(FULL_MASK, 4 * g < tn && m < r2) == 0u) continue;
+            // Hits of this lane, in index order (points past the tile end and
+            // the excluded self row never hit).
+            unsigned h = 0u;
+            const int64_t j0 = t0 + c0 + 4 * lane;
 #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int64_t j = j0 + u * 32 + lane;
-                d[u] = INFINITY;
-                if (j < nl) d[u] = sqd3(qx, qy, qz, r[3 * j], r[3 * j + 1], r[3 * j + 2]);
+            for (int v = 0; v < 4; ++v)
+                h |= (c0 + 4 * lane + v < tn && d[v] < r2 && j0 + v != self) ? (1u << v) : 0u;
+            const int c = __popc(h);
+            const unsigned b0 = __ballot_sync(FULL_MASK, c & 1);
+            const unsigned b1 = __ballot_sync(FULL_MASK, c & 2);
+            const unsigned b2 = __ballot_sync(FULL_MASK, c & 4);
+            const int total = __popc(b0) + 2 * __popc(b1) + 4 * __popc(b2);
+            if (total == 0) continue;
+            if (POINTNET2 && first < 0) {
+                const int src = __ffs(__ballot_sync(FULL_MASK, h != 0u)) - 1;
+                first = t0 + c0 + 4 * src + (__ffs(__shfl_sync(FULL_MASK, h, src)) - 1);
             }
+            int64_t slot = found + __popc(b0 & below) + 2 * __popc(b1 & below) +
+                           4 * __popc(b2 & below);
 #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int64_t j = j0 + u * 32 + lane;
-                const bool hit = j < nl && d[u] < r2 && j != self;
-                const unsigned mask = __ballot_sync(FULL_MASK, hit);
-                if (mask == 0u) continue;
-                if (first < 0) first = j0 + u * 32 + (__ffs(mask) - 1);
-                const int64_t slot = found + __popc(mask & below);
-                if (hit && slot < K) {
-                    if (POINTNET2) {
-                        idx32[row + slot] = (int32_t)j;
-                    } else {
-                        idx64[row + slot] = sp.obase + j;
-                        if (dist2) dist2[row + slot] = d[u];
+            for (int v = 0; v < 4; ++v) {
+                if ((h >> v) & 1u) {
+                    if (slot < K) {
+                        if (POINTNET2) {
+                            idx32[row + slot] = (int32_t)(j0 + v);
+                        } else {
+                            idx64[row + slot] = sp.obase + j0 + v;
+                            if (dist2) dist2[row + slot] = d[v];
+                        }
                     }
+                    ++slot;
                 }
-                found += __popc(mask);
+            }
+            found += total;
+            if (found >= K) {
+                scanning = false;
+                break;
             }
         }
     }
+    if (!in_range) return;
     // Padding.
     const int64_t filled = min64(found, K);
     for (int64_t s = filled + lane; s < K; s += 32) {

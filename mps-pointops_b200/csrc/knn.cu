@@ -557,22 +557,44 @@ knn_warp_kernel(const float* __restrict__ query, const float* __restrict__ ref, 
 }
 
 // --------------------------------------------------------------------------
-// Warp per query, k <= 32 (D == 3): lane s holds list slot s, so the k-th
-// entry -- the threshold every lane compares against -- is one shuffle away
-// and an insertion is a warp-wide shift (ballot + popc for the position,
-// shfl_up for the move): ~12 warp instructions however many lanes see
-// candidates, instead of a per-thread register insertion that diverges.
-// Eight queries of one cloud per CTA share a reference tile of kWqTile points
-// in shared memory; lane l evaluates reference j0 + l of each 32-point chunk.
+// Warp per query, k <= 32 (D == 3).  Eight queries of one cloud per CTA share
+// a reference tile of kWqTile points in shared memory.
+//
+// Each warp step covers 128 references as four 32-point chunks; lane l takes
+// point l of every chunk, and the four distances are evaluated as two packed
+// f32x2 pairs with the query duplicated in both halves -- half the issue
+// slots of scalar distances.  The tile is stored for that access: for step s
+// and lane l, A = (x, x', y, y') of chunk points 0 and 1, B the same for
+// chunks 2 and 3, Z = (z0, z1, z2, z3), so a lane's three loads are
+// consecutive across the warp (conflict-free).  Candidates are offered chunk
+// by chunk, in index order, with the bar updated between chunks.
+//
+// The k best so far are kept UNSORTED, one per lane s < k, as (key, index):
+// key = the ordered bits of the squared distance (monotone in the float,
+// every NaN mapped above +inf, which is the order of every policy here), so
+// (key, index) in lexicographic order is the (SD, index) order.  Empty slots
+// hold (0xffffffff, kNoIndex - lane): worse than any candidate and distinct.
+// A candidate enters iff it precedes the worst entry; it replaces that entry
+// and two redux.sync find the new worst -- about a dozen warp instructions
+// per insertion.  The list is sorted once at the end (bitonic across lanes).
+// One min over a lane's four distances and one ballot against the worst
+// entry's distance skip a step without candidates (fminf ignores NaN, which
+// can only enter a list that has room or already holds a NaN; the threshold
+// then lets every lane through).
 constexpr int kWqWarps = 8;
-constexpr int kWqTile = 2048;
+constexpr int kWqTile = 2048;  // multiple of 128
+constexpr uint32_t kEmptyKey = 0xffffffffu;
+
+__device__ __forceinline__ uint32_t sd_key(float d) {
+    return isnan(d) ? kEmptyKey : ordered_key(d);
+}
 
 template <int POLICY, bool FLAT>
 __global__ void __launch_bounds__(kWqWarps * 32)
 knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, Layout L, int k,
                float* __restrict__ dist, int64_t* __restrict__ idx64,
                int32_t* __restrict__ idx32, float* __restrict__ sqdist) {
-    __shared__ float4 tile[kWqTile];
+    __shared__ float4 tA[kWqTile / 4], tB[kWqTile / 4], tZ[kWqTile / 4];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     Span sp;
     if (!locate<FLAT>(L, kWqWarps, sp)) return;  // CTA-uniform
@@ -587,59 +609,98 @@ knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, L
         qy = qp[1];
         qz = qp[2];
     }
-    float ld = INFINITY;    // slot `lane`
-    uint32_t li = kNoIndex;
-    int cnt = 0;            // warp-uniform
-    float kd = INFINITY;    // k-th entry once the list is full
-    uint32_t ki = kNoIndex;
+    const f32x2 X = pack2(qx, qx), Y = pack2(qy, qy), Z = pack2(qz, qz);
+    // This lane's slot (lanes >= k hold (0, 0): never the worst).
+    uint32_t lk = lane < k ? kEmptyKey : 0u;
+    uint32_t lx = lane < k ? kNoIndex - (uint32_t)lane : 0u;
+    float ld = INFINITY;
+    uint32_t wk = kEmptyKey, wi = kNoIndex;  // the worst entry (lane 0's empty slot)
+    float thr = INFINITY;                    // its distance; +inf while a slot is empty
+    // Tile fill: tile point p is point l = p % 32 of chunk v = (p / 32) % 4 of
+    // step p / 128.  Thread t stores points t, t + 256, ...; l and v are fixed
+    // per thread, so each thread always writes the same fields.
+    const int fl = threadIdx.x & 31, fv = (threadIdx.x >> 5) & 3;
+    float* const fxy = reinterpret_cast<float*>(fv < 2 ? tA : tB) + (fv & 1);
+    float* const fz = reinterpret_cast<float*>(tZ) + fv;
     for (int64_t t0 = 0; t0 < N; t0 += kWqTile) {
         const int tn = (int)min64(kWqTile, N - t0);
         __syncthreads();
-        for (int e = threadIdx.x; e < 3 * tn; e += kWqWarps * 32)
-            reinterpret_cast<float*>(tile)[(e / 3) * 4 + (e % 3)] = r[t0 * 3 + e];
+        for (int p = threadIdx.x; p < tn; p += kWqWarps * 32) {
+            const float* rp = r + (size_t)(t0 + p) * 3;
+            const int e = 4 * ((p >> 7) * 32 + fl);  // float offset of (step, lane)
+            fxy[e] = rp[0];
+            fxy[e + 2] = rp[1];
+            fz[e] = rp[2];
+        }
         __syncthreads();
         if (!active) continue;
-        for (int c0 = 0; c0 < tn; c0 += 32) {
-            const int e = c0 + lane;
-            float d = INFINITY;
-            if (e < tn) {
-                const float4 p = tile[e];
-                d = sqd3(qx, qy, qz, p.x, p.y, p.z);
-            }
-            const float thr = cnt < k ? INFINITY : kd;
-            unsigned pending = __ballot_sync(FULL_MASK, e < tn && !(d > thr));
-            while (pending) {
-                const int src = __ffs(pending) - 1;
-                pending &= pending - 1;
-                const float cd = __shfl_sync(FULL_MASK, d, src);
-                const uint32_t ci = (uint32_t)(t0 + c0 + src);
-                if (!admissible<POLICY>(cd)) continue;
-                if (cnt >= k && !before<POLICY>(cd, ci, kd, ki)) continue;
-                const int pos = __popc(__ballot_sync(
-                    FULL_MASK, lane < cnt && before<POLICY>(ld, li, cd, ci)));
-                const float ud = __shfl_up_sync(FULL_MASK, ld, 1);
-                const uint32_t ui = __shfl_up_sync(FULL_MASK, li, 1);
-                if (lane > pos) {
-                    ld = ud;
-                    li = ui;
-                } else if (lane == pos) {
-                    ld = cd;
-                    li = ci;
+        for (int c0 = 0; c0 < tn; c0 += 128) {
+            const int g = (c0 >> 2) + lane;
+            const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(tA + g);
+            const ulonglong2 b = *reinterpret_cast<const ulonglong2*>(tB + g);
+            const ulonglong2 z = *reinterpret_cast<const ulonglong2*>(tZ + g);
+            float d[4];
+            unpack2(sqd3x2(X, Y, Z, a.x, a.y, z.x), d[0], d[1]);
+            unpack2(sqd3x2(X, Y, Z, b.x, b.y, z.y), d[2], d[3]);
+            const float m = fminf(fminf(d[0], d[1]), fminf(d[2], d[3]));
+            if (__ballot_sync(FULL_MASK, !(m > thr)) == 0u) continue;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const int e = c0 + 32 * v + lane;
+                unsigned pending = __ballot_sync(FULL_MASK, e < tn && !(d[v] > thr));
+                while (pending) {
+                    const int src = __ffs(pending) - 1;
+                    pending &= pending - 1;
+                    const float cd = __shfl_sync(FULL_MASK, d[v], src);
+                    const uint32_t ci = (uint32_t)(t0 + c0 + 32 * v + src);
+                    if (!admissible<POLICY>(cd)) continue;
+                    const uint32_t ck = sd_key(cd);
+                    if (!(ck < wk || (ck == wk && ci < wi))) continue;
+                    if (lk == wk && lx == wi) {
+                        lk = ck;
+                        lx = ci;
+                        ld = cd;
+                    }
+                    wk = __reduce_max_sync(FULL_MASK, lk);
+                    wi = __reduce_max_sync(FULL_MASK, lk == wk ? lx : 0u);
+                    thr = wk != kEmptyKey ? ordered_key_inv(wk)
+                                          : (wi >= 0x80000000u ? INFINITY : __int_as_float(0x7fffffff));
                 }
-                cnt = min(cnt + 1, k);
-                kd = __shfl_sync(FULL_MASK, ld, k - 1);
-                ki = __shfl_sync(FULL_MASK, li, k - 1);
             }
         }
     }
-    if (!active || lane >= k) return;
+    if (!active) return;
+    // Sort the k entries ascending by (key, index): bitonic across the warp,
+    // lanes >= k carrying (max, max) so they end up last.
+    if (lane >= k) {
+        lk = kEmptyKey;
+        lx = 0xffffffffu;
+    }
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const uint32_t ok = __shfl_xor_sync(FULL_MASK, lk, stride);
+            const uint32_t ox = __shfl_xor_sync(FULL_MASK, lx, stride);
+            const float od = __shfl_xor_sync(FULL_MASK, ld, stride);
+            const bool ascending = (lane & size) == 0;
+            const bool lower = (lane & stride) == 0;
+            const bool other_first = ok < lk || (ok == lk && ox < lx);
+            if ((lower == ascending) ? other_first : !other_first) {
+                lk = ok;
+                lx = ox;
+                ld = od;
+            }
+        }
+    }
+    if (lane >= k) return;
     const size_t row = (size_t)q * (size_t)k;
-    const bool filled = lane < cnt;
-    const float d = filled ? ld : INFINITY;
-    if (dist) dist[row + lane] = sqrtf(d);
-    if (sqdist) sqdist[row + lane] = d;
-    if (idx64) idx64[row + lane] = filled ? sp.obase + (int64_t)li : -1;
-    if (idx32) idx32[row + lane] = filled ? (int32_t)li : -1;
+    const bool filled = lx < 0x80000000u;  // real rows are below 2**31
+    const float dd = filled ? ld : INFINITY;
+    if (dist) dist[row + lane] = sqrtf(dd);
+    if (sqdist) sqdist[row + lane] = dd;
+    if (idx64) idx64[row + lane] = filled ? sp.obase + (int64_t)lx : -1;
+    if (idx32) idx32[row + lane] = filled ? (int32_t)lx : -1;
 }
 
 // Grid of a search launch: (ceil(M / qpc), B) dense, virtual tiles flat.
