@@ -38,7 +38,7 @@ extern "C" {
 #define MPO_API
 #endif
 
-#define MPO_ABI_VERSION 3
+#define MPO_ABI_VERSION 4
 
 #define MPO_OK 0
 #define MPO_ERR_INVALID_ARGUMENT 1
@@ -245,6 +245,44 @@ MPO_API int mpo_chamfer_loss_backward(const float* x, const float* y, const int6
 MPO_API int mpo_chamfer_check_inputs(const float* x, const float* y, const int64_t* x_lengths,
                                      const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q,
                                      int64_t D, int32_t* flags, void* stream);
+
+/* ------------------------------------------------------------------ SA grouping
+ * gather_operation / grouping_operation of pointnet2_ops, which the reference
+ * serves with torch gather (mps_pointops/compat.py:62-73):
+ *   out[b, c, p, s] = features[b, c, idx[b, p, s]]      features (B, C, N),
+ *   idx (B, P, S) int32 (idx_is_int64 = 0) or int64, out (B, C, P, S); gather
+ *   is S = 1.  Indices outside [0, N) give 0 (check them with
+ *   mpo_index_check, as the reference's gather raises on them).
+ * The backward overwrites grad_features (B, C, N) with the scatter-add of
+ * grad_out over idx (float atomics: the order of additions into one element
+ * is not fixed). */
+MPO_API int mpo_group_points(const float* features, const void* idx, int idx_is_int64,
+                             int64_t B, int64_t C, int64_t N, int64_t P, int64_t S, float* out,
+                             void* stream);
+MPO_API int mpo_group_points_backward(const float* grad_out, const void* idx, int idx_is_int64,
+                                      int64_t B, int64_t C, int64_t N, int64_t P, int64_t S,
+                                      float* grad_features, void* stream);
+
+/* Fused set-abstraction grouping: the composition of
+ * tests/test_pointnet2_e2e.py:40-44 (compat.ball_query, grouping of xyz minus
+ * the centre, grouping of the features, concatenation along channels) in two
+ * launches and without temporaries.  xyz (B,N,3), new_xyz (B,P,3), features
+ * (B,C,N) (C may be 0), radius_sq = fl32(fl32(r)^2).  Writes idx (B,P,S)
+ * int32 -- the pointnet2_ops ball query of mpo_ball_query_pointnet2 -- and
+ * out (B, 3*use_xyz + C, P, S): channels 0..2 = xyz[b, idx, :] - new_xyz[b, p, :]
+ * when use_xyz != 0, then the grouped features. */
+MPO_API int mpo_query_and_group(const float* xyz, const float* new_xyz, const float* features,
+                                int64_t B, int64_t N, int64_t P, int64_t S, int64_t C,
+                                float radius_sq, int use_xyz, int32_t* idx, float* out,
+                                void* stream);
+/* Its backward: grad_xyz (B,N,3) and grad_features (B,C,N) receive the
+ * scatter-add of grad_out over idx (float atomics), grad_new_xyz (B,P,3) minus
+ * the slot sum of the coordinate channels (slot order); each output is
+ * nullable and, when given, overwritten. */
+MPO_API int mpo_query_and_group_backward(const float* grad_out, const int32_t* idx, int64_t B,
+                                         int64_t N, int64_t P, int64_t S, int64_t C,
+                                         int use_xyz, float* grad_xyz, float* grad_new_xyz,
+                                         float* grad_features, void* stream);
 
 /* ------------------------------------------------------------------ flat batches
  * The torch_cluster-style API of mps_pointops/flat.py:161-425 works on flat

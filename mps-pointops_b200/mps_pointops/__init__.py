@@ -8,13 +8,13 @@ libmpo_b200.so (C ABI: include/mpo_b200.h).  CUDA tensors only; there is no
 CPU or library fallback.
 """
 
-from . import compat, dist, flat, pyg
+from . import compat, dist, flat, grouping, pyg
 from .chamfer import chamfer_distance
 from .ops import ball_query, furthest_point_sample, knn
 from .pointnet2 import three_interpolate, three_nn
 
 __all__ = [
-    "ball_query", "chamfer_distance", "compat", "dist", "flat", "furthest_point_sample", "knn",
-    "pyg", "three_interpolate", "three_nn",
+    "ball_query", "chamfer_distance", "compat", "dist", "flat", "furthest_point_sample",
+    "grouping", "knn", "pyg", "three_interpolate", "three_nn",
 ]
 __version__ = "1.0.0+b200"

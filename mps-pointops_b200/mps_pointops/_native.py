@@ -20,7 +20,7 @@ from pathlib import Path
 import torch
 
 LIB_NAME = "libmpo_b200.so"
-ABI_VERSION = 3
+ABI_VERSION = 4
 _lib = None
 _lock = threading.Lock()
 _checked_devices: set[int] = set()
@@ -65,6 +65,13 @@ SIGNATURES = {
                             _vp]),
     "mpo_flat_radius": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i64, _int, _vp, _vp,
                                _vp]),
+    "mpo_group_points": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "mpo_group_points_backward": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _vp,
+                                         _vp]),
+    "mpo_query_and_group": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _int,
+                                   _vp, _vp, _vp]),
+    "mpo_query_and_group_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _int, _vp,
+                                            _vp, _vp, _vp]),
     "mpo_flat_fps_workspace_bytes": (_sz, [_i64, _i64]),
     "mpo_flat_fps": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _sz,
                             _vp]),

@@ -34,7 +34,7 @@ import torch
 from torch import Tensor
 
 from . import _native as N
-from . import flat, ops
+from . import flat, grouping, ops
 from ._ball_query_cuda import _checked_radius_and_k
 
 
@@ -48,19 +48,13 @@ def furthest_point_sample(xyz: Tensor, npoint: int) -> Tensor:
     return ops._fps(xyz, npoint, 0, True, "auto", out_dtype=torch.int32)
 
 
-def gather_operation(features: Tensor, idx: Tensor) -> Tensor:
-    """(B, C, N), (B, npoint) -> (B, C, npoint) (mps_pointops/compat.py:62-65)."""
-    B, C, _ = features.shape
-    return features.gather(2, idx.long().unsqueeze(1).expand(B, C, -1))
-
-
-def grouping_operation(features: Tensor, idx: Tensor) -> Tensor:
-    """(B, C, N), (B, npoint, nsample) -> (B, C, npoint, nsample)
-    (mps_pointops/compat.py:68-73)."""
-    B, C, _ = features.shape
-    _, npoint, nsample = idx.shape
-    flat = idx.long().reshape(B, 1, npoint * nsample).expand(B, C, -1)
-    return features.gather(2, flat).reshape(B, C, npoint, nsample)
+# gather_operation / grouping_operation (mps_pointops/compat.py:62-73) run on
+# the grouping kernels for float32 CUDA tensors; QueryAndGroup / GroupAll are
+# the pointnet2_ops modules on the fused grouping kernel.
+gather_operation = grouping.gather_operation
+grouping_operation = grouping.grouping_operation
+QueryAndGroup = grouping.QueryAndGroup
+GroupAll = grouping.GroupAll
 
 
 def ball_query(radius: float, nsample: int, xyz: Tensor, new_xyz: Tensor) -> Tensor:
@@ -139,6 +133,8 @@ def install(force: bool = False, *, pointcept: bool = False) -> list[str]:
         gather_operation=gather_operation,
         grouping_operation=grouping_operation,
         ball_query=ball_query,
+        QueryAndGroup=QueryAndGroup,
+        GroupAll=GroupAll,
     )
     packages = {
         "pointnet2_ops": {

@@ -384,3 +384,51 @@ def flat_edges(indices: np.ndarray) -> np.ndarray:
     """mps_pointops/flat.py:247-253: padded rows -> [query, reference] edges."""
     q, s = np.nonzero(indices >= 0)
     return np.stack([q.astype(np.int64), indices[q, s]])
+
+
+# ---------------------------------------------------------------- SA grouping
+def group_points(features, idx) -> np.ndarray:
+    """mps_pointops/compat.py:68-73 (torch gather): out[b, c, p, s] =
+    features[b, c, idx[b, p, s]] -- exact copies.  gather_operation
+    (compat.py:62-65) is the nsample = 1 case."""
+    features = _f32(features)
+    idx = np.asarray(idx).astype(np.int64)
+    return np.stack([features[b][:, idx[b]] for b in range(features.shape[0])])
+
+
+def group_points_backward(grad_out, idx, n: int) -> np.ndarray:
+    """Gradient of group_points: scatter-add of grad_out over idx, accumulated
+    in float64 (the tests compare within a relative tolerance, as the order of
+    float32 additions into one element is not fixed on either side)."""
+    grad_out = np.asarray(grad_out, dtype=np.float64)
+    idx = np.asarray(idx).astype(np.int64)
+    B, C = grad_out.shape[:2]
+    out = np.zeros((B, C, n), dtype=np.float64)
+    for b in range(B):
+        np.add.at(out[b], (slice(None), idx[b].reshape(-1)), grad_out[b].reshape(C, -1))
+    return out
+
+
+def query_and_group(xyz, new_xyz, features, radius: float, nsample: int, use_xyz=True):
+    """tests/test_pointnet2_e2e.py:40-44: pointnet2 ball query, grouped xyz
+    minus the centre (one float32 subtraction), grouped features, concatenated
+    along channels.  Returns (out, idx int32)."""
+    xyz, new_xyz = _f32(xyz), _f32(new_xyz)
+    idx = ball_query_pointnet2(radius, nsample, xyz, new_xyz)
+    parts = []
+    if use_xyz:
+        gx = group_points(np.ascontiguousarray(xyz.transpose(0, 2, 1)), idx)
+        parts.append((gx - new_xyz.transpose(0, 2, 1)[..., None]).astype(np.float32))
+    if features is not None:
+        parts.append(group_points(features, idx))
+    return np.concatenate(parts, axis=1), idx
+
+
+def query_and_group_backward(grad_out, idx, n: int, use_xyz=True):
+    """Gradients of query_and_group for (xyz, new_xyz, features), float64."""
+    g = np.asarray(grad_out, dtype=np.float64)
+    X = 3 if use_xyz else 0
+    gxyz = group_points_backward(g[:, :X], idx, n).transpose(0, 2, 1) if X else None
+    gnew = -g[:, :X].sum(axis=3).transpose(0, 2, 1) if X else None
+    gfeat = group_points_backward(g[:, X:], idx, n) if g.shape[1] > X else None
+    return gxyz, gnew, gfeat

@@ -409,6 +409,40 @@ def flat_cases():
     save("flat", **out)
 
 
+# ------------------------------------------------------------------ SA grouping
+def grouping_cases():
+    """compat.gather_operation / grouping_operation (compat.py:62-73, torch gather
+    on CPU) and the set-abstraction grouping of tests/test_pointnet2_e2e.py:40-44,
+    forward and backward with a fixed output gradient."""
+    out = {}
+    g = torch.Generator().manual_seed(404)
+    B, Np, P, S, C = 2, 300, 40, 12, 5
+    xyz = torch.rand(B, Np, 3, generator=g)
+    feats = torch.randn(B, C, Np, generator=g)
+    sampled = compat.furthest_point_sample(xyz, P)
+    new_xyz = compat.gather_operation(xyz.transpose(1, 2).contiguous(), sampled)
+    new_xyz = new_xyz.transpose(1, 2).contiguous()
+    out["gather/features"], out["gather/idx"] = xyz.transpose(1, 2).contiguous(), sampled
+    out["gather/out"] = compat.gather_operation(xyz.transpose(1, 2).contiguous(), sampled)
+    for radius in (0.15, 0.4):
+        xr = xyz.clone().requires_grad_()
+        qr = new_xyz.clone().requires_grad_()
+        fr = feats.clone().requires_grad_()
+        neighbors = compat.ball_query(radius, S, xr, qr)
+        grouped_xyz = compat.grouping_operation(xr.transpose(1, 2).contiguous(), neighbors)
+        grouped_xyz = grouped_xyz - qr.transpose(1, 2).unsqueeze(-1)
+        grouped = torch.cat((grouped_xyz, compat.grouping_operation(fr, neighbors)), dim=1)
+        gout = torch.randn(grouped.shape, generator=g)
+        grouped.backward(gout)
+        name = f"qg_r{radius}"
+        out[f"{name}/xyz"], out[f"{name}/new_xyz"], out[f"{name}/features"] = xyz, new_xyz, feats
+        out[f"{name}/meta"] = np.array([radius, S])
+        out[f"{name}/idx"], out[f"{name}/out"], out[f"{name}/grad_out"] = neighbors, grouped, gout
+        out[f"{name}/grad_xyz"], out[f"{name}/grad_new_xyz"] = xr.grad, qr.grad
+        out[f"{name}/grad_features"] = fr.grad
+    save("grouping", **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     fps_cases()
@@ -418,5 +452,6 @@ if __name__ == "__main__":
     pointnet2_cases()
     chamfer_cases()
     flat_cases()
+    grouping_cases()
     for f in sorted(OUT.glob("*.npz")):
         print(f"{f.name}: {f.stat().st_size / 1024:.0f} KiB")
