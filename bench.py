@@ -61,7 +61,7 @@ def parse_args():
     ap.add_argument("--workload", default="chamfer_config2",
                     choices=["chamfer_config2", "ssg_config1_ops", "fps_config3",
                              "feature_knn_config4", "knn_config5", "ball_query_config5",
-                             "flat_ops"],
+                             "flat_ops", "sa_grouping_config1"],
                     help="single-GPU measurement of one BASELINE config (the default is the "
                          "headline line; the others print their own JSON line and are used "
                          "for the per-kernel profiles)")
@@ -435,6 +435,100 @@ def flat_ops(steps: int, warmup: int) -> dict:
     return res
 
 
+def sa_grouping_config1(steps: int, warmup: int) -> dict:
+    """SA grouping at BASELINE config 1 sizes (8 clouds of 4096 points, 1024
+    centres, r 0.2, 32 samples, 64 feature channels), forward + backward:
+    (1) the reference's composition (tests/test_pointnet2_e2e.py:40-44) with
+    its torch gather grouping (compat.py:68-73), (2) the same composition on
+    the native grouping kernel, (3) the fused query_and_group.  CUDA events,
+    L2 flushed between steps; HBM roofline of the fused forward kernel."""
+    from mps_pointops import compat, grouping
+    from mps_pointops import _native as N
+    from mps_pointops._ball_query_cuda import _checked_radius_and_k
+    g = torch.Generator().manual_seed(0)
+    xyz = torch.rand(8, 4096, 3, generator=g).cuda()
+    feats = torch.randn(8, 64, 4096, generator=g).cuda()
+    idx0 = compat.furthest_point_sample(xyz, 1024)
+    centres = compat.gather_operation(xyz.transpose(1, 2).contiguous(), idx0)
+    centres = centres.transpose(1, 2).contiguous()
+    B, P, S, C = 8, 1024, 32, 64
+    gout = torch.randn(B, 3 + C, P, S, generator=g).cuda()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    def torch_group(f, i):
+        flat_i = i.long().reshape(B, 1, P * S).expand(B, f.shape[1], -1)
+        return f.gather(2, flat_i).reshape(B, f.shape[1], P, S)
+
+    def composed(group):
+        def run(backward):
+            x = xyz.clone().requires_grad_(backward)
+            q = centres.clone().requires_grad_(backward)
+            f = feats.clone().requires_grad_(backward)
+            nb = compat.ball_query(0.2, S, x, q)
+            gx = group(x.transpose(1, 2).contiguous(), nb) - q.transpose(1, 2).unsqueeze(-1)
+            out = torch.cat((gx, group(f, nb)), dim=1)
+            if backward:
+                out.backward(gout)
+            return out
+        return run
+
+    def fused(backward):
+        x = xyz.clone().requires_grad_(backward)
+        q = centres.clone().requires_grad_(backward)
+        f = feats.clone().requires_grad_(backward)
+        out, _ = grouping.query_and_group(x, q, f, 0.2, S)
+        if backward:
+            out.backward(gout)
+        return out
+
+    arms = {"reference_torch_gather": composed(torch_group),
+            "native_unfused": composed(compat.grouping_operation), "fused": fused}
+    res = {"workload": "sa_grouping_config1", "unit": "ms (median, CUDA events, L2 flushed)",
+           "shape": {"clouds": B, "points": 4096, "centres": P, "nsample": S, "channels": C}}
+    for name, fn in arms.items():
+        res[name] = {"fwd": _event_ms(lambda: fn(False), steps, warmup, flush),
+                     "fwd_bwd": _event_ms(lambda: fn(True), steps, warmup, flush)}
+    # The sampling step: compat FPS then gather_operation, vs the fused FPS.
+    res["sampling"] = {
+        "fps_then_gather": _event_ms(lambda: compat.gather_operation(
+            xyz.transpose(1, 2).contiguous(), compat.furthest_point_sample(xyz, P)),
+            steps, warmup, flush),
+        "fused_sample_and_gather": _event_ms(lambda: grouping.sample_and_gather(xyz, P), steps,
+                                             warmup, flush)}
+    # The fused forward kernel alone (events on the launching stream).
+    idx = torch.empty((B, P, S), dtype=torch.int32, device="cuda")
+    out = torch.empty((B, 3 + C, P, S), device="cuda")
+    lib = N.lib()
+    _, r2 = _checked_radius_and_k(0.2, S)
+
+    ws_bytes = int(lib.mpo_query_and_group_workspace_bytes(B, 4096, P, S, C))
+    ws = N.workspace(ws_bytes, xyz.device)
+
+    def kernel_call():
+        N.check(lib.mpo_query_and_group(N.ptr(xyz), N.ptr(centres), N.ptr(feats), B, 4096, P, S, C,
+                                        r2, 1, N.ptr(idx), N.ptr(out), N.ptr(ws), ws_bytes,
+                                        N.stream(xyz.device)), "query_and_group")
+    q_ms = _event_ms(kernel_call, steps, warmup, flush)
+    algo = out.numel() * 4 + idx.numel() * 4 + feats.numel() * 4 + xyz.numel() * 4 \
+        + centres.numel() * 4
+    peak = _measured_hbm_gbs()
+    res["fused_forward_call"] = {"ms": q_ms, "algorithmic_bytes": algo,
+                                 "achieved_GBps": algo / (q_ms / 1e3) / 1e9, "peak_GBps": peak,
+                                 "frac": algo / (q_ms / 1e3) / 1e9 / peak,
+                                 "note": "ball query + grouping launches; bytes = output + "
+                                         "indices written, features + xyz + centres read once "
+                                         "(the transposed copy of the features adds 2 x 8.4 MB "
+                                         "not counted)"}
+    return res
+
+
+def _measured_hbm_gbs() -> float:
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"])
+    except Exception:  # noqa: BLE001
+        return 6650.0
+
+
 def _sm_max_mhz() -> float:
     try:
         outp = subprocess.run(["nvidia-smi", "--query-gpu=clocks.max.sm", "--format=csv,noheader,nounits",
@@ -620,6 +714,8 @@ def main():
             out = ssg_config1_ops(steps, max(warmup, 3))
         elif args.workload == "fps_config3":
             out = fps_config3(min(steps, 3), 1)
+        elif args.workload == "sa_grouping_config1":
+            out = sa_grouping_config1(steps, max(warmup, 3))
         elif args.workload == "flat_ops":
             out = flat_ops(steps, max(warmup, 3))
         elif args.workload == "feature_knn_config4":

@@ -38,7 +38,7 @@ extern "C" {
 #define MPO_API
 #endif
 
-#define MPO_ABI_VERSION 4
+#define MPO_ABI_VERSION 5
 
 #define MPO_OK 0
 #define MPO_ERR_INVALID_ARGUMENT 1
@@ -86,6 +86,16 @@ MPO_API size_t mpo_fps_workspace_bytes(int64_t B, int64_t N, int64_t npoint, int
 MPO_API int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
                     int skip_near_origin, int out_int32, int strategy, void* out,
                     int32_t* status_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* mpo_fps plus the fused gather of the sampled points: out_xyz (B, npoint, 3)
+ * receives xyz[b, out[b, i], :] -- the FPS -> gather_operation step of a
+ * PointNet++ set abstraction (mps_pointops/compat.py:53-65;
+ * tests/test_pointnet2_e2e.py:37-39) without a separate launch.  Same
+ * arguments, workspace and status as mpo_fps; out_xyz may be NULL. */
+MPO_API int mpo_fps_gather(const float* xyz, int64_t B, int64_t N, int64_t npoint,
+                           int64_t start_idx, int skip_near_origin, int out_int32, int strategy,
+                           void* out, float* out_xyz, int32_t* status_out, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* Allocation-free FPS.  No counterpart in the reference: it exists for
  * callers that cannot allocate device memory (for example a plugin given only
@@ -255,13 +265,28 @@ MPO_API int mpo_chamfer_check_inputs(const float* x, const float* y, const int64
  *   mpo_index_check, as the reference's gather raises on them).
  * The backward overwrites grad_features (B, C, N) with the scatter-add of
  * grad_out over idx (float atomics: the order of additions into one element
- * is not fixed). */
+ * is not fixed).
+ * Workspace (optional, 16-byte aligned): when every point is gathered several
+ * times (P * S >= N, C >= 4), mpo_group_points_workspace_bytes() > 0 and a
+ * workspace of that size lets both calls work on a (B, N, C) copy of the
+ * features or gradient, so that a point's channels are contiguous and every
+ * global access is coalesced; with NULL or too small a workspace they work on
+ * (B, C, N) directly (same forward bits; the backward's float additions may
+ * come in another order). */
+MPO_API size_t mpo_group_points_workspace_bytes(int64_t B, int64_t C, int64_t N, int64_t P,
+                                                int64_t S);
 MPO_API int mpo_group_points(const float* features, const void* idx, int idx_is_int64,
                              int64_t B, int64_t C, int64_t N, int64_t P, int64_t S, float* out,
-                             void* stream);
+                             void* workspace, size_t workspace_bytes, void* stream);
+/* Gradient of the points gathered by mpo_fps_gather: grad_xyz (B,N,3) is
+ * overwritten with the scatter-add of grad (B,P,3) over idx (B,P) int32
+ * (float atomics) -- the backward of gather_operation on the coordinates. */
+MPO_API int mpo_gather_points_backward(const float* grad, const int32_t* idx, int64_t B,
+                                       int64_t N, int64_t P, float* grad_xyz, void* stream);
 MPO_API int mpo_group_points_backward(const float* grad_out, const void* idx, int idx_is_int64,
                                       int64_t B, int64_t C, int64_t N, int64_t P, int64_t S,
-                                      float* grad_features, void* stream);
+                                      float* grad_features, void* workspace,
+                                      size_t workspace_bytes, void* stream);
 
 /* Fused set-abstraction grouping: the composition of
  * tests/test_pointnet2_e2e.py:40-44 (compat.ball_query, grouping of xyz minus
@@ -270,19 +295,24 @@ MPO_API int mpo_group_points_backward(const float* grad_out, const void* idx, in
  * (B,C,N) (C may be 0), radius_sq = fl32(fl32(r)^2).  Writes idx (B,P,S)
  * int32 -- the pointnet2_ops ball query of mpo_ball_query_pointnet2 -- and
  * out (B, 3*use_xyz + C, P, S): channels 0..2 = xyz[b, idx, :] - new_xyz[b, p, :]
- * when use_xyz != 0, then the grouped features. */
+ * when use_xyz != 0, then the grouped features.  The optional workspace
+ * (mpo_query_and_group_workspace_bytes) plays the same role as in
+ * mpo_group_points. */
+MPO_API size_t mpo_query_and_group_workspace_bytes(int64_t B, int64_t N, int64_t P, int64_t S,
+                                                   int64_t C);
 MPO_API int mpo_query_and_group(const float* xyz, const float* new_xyz, const float* features,
                                 int64_t B, int64_t N, int64_t P, int64_t S, int64_t C,
                                 float radius_sq, int use_xyz, int32_t* idx, float* out,
-                                void* stream);
+                                void* workspace, size_t workspace_bytes, void* stream);
 /* Its backward: grad_xyz (B,N,3) and grad_features (B,C,N) receive the
  * scatter-add of grad_out over idx (float atomics), grad_new_xyz (B,P,3) minus
  * the slot sum of the coordinate channels (slot order); each output is
- * nullable and, when given, overwritten. */
+ * nullable and, when given, overwritten.  Workspace as for the forward. */
 MPO_API int mpo_query_and_group_backward(const float* grad_out, const int32_t* idx, int64_t B,
                                          int64_t N, int64_t P, int64_t S, int64_t C,
                                          int use_xyz, float* grad_xyz, float* grad_new_xyz,
-                                         float* grad_features, void* stream);
+                                         float* grad_features, void* workspace,
+                                         size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------ flat batches
  * The torch_cluster-style API of mps_pointops/flat.py:161-425 works on flat

@@ -71,7 +71,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
 fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t start_idx,
            int skip, int out_int32, void* __restrict__ out, int G, int64_t per_cta,
            int cloud_offset, unsigned long long* __restrict__ slots,
-           unsigned* __restrict__ errors, int32_t* __restrict__ status, FlatFps flat) {
+           unsigned* __restrict__ errors, int32_t* __restrict__ status, FlatFps flat,
+           float* __restrict__ out_xyz) {
     extern __shared__ float s_xyz[];  // G == 1 only: the cloud, 3 floats per point
     __shared__ uint32_t s_key[2][32];
     __shared__ uint32_t s_idx[2][32];
@@ -176,6 +177,13 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
         if (tid == 0 && g == 0) {
             if (out_int32) out32[i] = (int32_t)far;
             else out64[i] = vbase + (int64_t)far;
+            // Fused gather of the sample's coordinates (dense layout only).
+            if (out_xyz) {
+                float* o = out_xyz + ((size_t)obase + (size_t)i) * 3;
+                o[0] = cx;
+                o[1] = cy;
+                o[2] = cz;
+            }
         }
         if (i + 1 == np) break;
 
@@ -332,7 +340,7 @@ int threads_for(int64_t per_cta, int P) {
 template <int P, bool FLAT>
 int launch_single(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
                   int skip, int out_int32, void* out, int32_t* status, const FlatFps& flat,
-                  cudaStream_t stream) {
+                  float* out_xyz, cudaStream_t stream) {
     auto kern = fps_kernel<P, false, FLAT>;
     const size_t smem = (size_t)N * 3 * sizeof(float);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
@@ -340,21 +348,21 @@ int launch_single(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_
         return fail(kCudaError, "mpo_fps: cannot set the shared-memory limit");
     kern<<<(unsigned)B, threads_for(N, P), smem, stream>>>(xyz, N, npoint, start_idx, skip,
                                                            out_int32, out, 1, N, 0, nullptr,
-                                                           nullptr, status, flat);
+                                                           nullptr, status, flat, out_xyz);
     return check_launch("mpo_fps");
 }
 
 template <bool FLAT>
 int launch_single_any(const float* xyz, int64_t B, int64_t N, int64_t npoint,
                       int64_t start_idx, int skip, int o32, void* out, int32_t* status,
-                      const FlatFps& f, cudaStream_t s) {
+                      const FlatFps& f, cudaStream_t s, float* oxyz = nullptr) {
     switch (pick_p(N)) {
-        case 1: return launch_single<1, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
-        case 2: return launch_single<2, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
-        case 4: return launch_single<4, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
-        case 8: return launch_single<8, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
-        case 16: return launch_single<16, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
-        default: return launch_single<32, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, s);
+        case 1: return launch_single<1, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+        case 2: return launch_single<2, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+        case 4: return launch_single<4, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+        case 8: return launch_single<8, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+        case 16: return launch_single<16, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+        default: return launch_single<32, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
     }
 }
 
@@ -385,7 +393,8 @@ int plan_group(int64_t B, int64_t N, int strategy, GroupPlan* plan, const char* 
 template <bool FLAT>
 int launch_group(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
                  int skip, int out_int32, void* out, const GroupPlan& plan, void* scratch,
-                 int32_t* status, const FlatFps& flat_in, cudaStream_t stream, const char* who) {
+                 int32_t* status, const FlatFps& flat_in, cudaStream_t stream, const char* who,
+                 float* out_xyz = nullptr) {
     auto kern = fps_kernel<kMaxP, true, FLAT>;
     FlatFps flat = flat_in;
     int G = (int)plan.G;
@@ -403,7 +412,7 @@ int launch_group(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t
         void* args[] = {(void*)&xyz,      (void*)&N,         (void*)&npoint, (void*)&start_idx,
                         (void*)&skip,     (void*)&out_int32, (void*)&out,    (void*)&G,
                         (void*)&per_cta,  (void*)&cloud_offset, (void*)&slots, (void*)&errors,
-                        (void*)&status,   (void*)&flat};
+                        (void*)&status,   (void*)&flat,      (void*)&out_xyz};
         cudaError_t e = cudaLaunchCooperativeKernel((const void*)kern, dim3(nc * G),
                                                     dim3(threads), args, 0, stream);
         if (e != cudaSuccess) {
@@ -459,6 +468,13 @@ size_t mpo_fps_workspace_bytes(int64_t B, int64_t N, int64_t npoint, int strateg
 int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
             int skip_near_origin, int out_int32, int strategy, void* out, int32_t* status_out,
             void* workspace, size_t workspace_bytes, void* stream) {
+    return mpo_fps_gather(xyz, B, N, npoint, start_idx, skip_near_origin, out_int32, strategy,
+                          out, nullptr, status_out, workspace, workspace_bytes, stream);
+}
+
+int mpo_fps_gather(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
+                   int skip_near_origin, int out_int32, int strategy, void* out, float* out_xyz,
+                   int32_t* status_out, void* workspace, size_t workspace_bytes, void* stream) {
     using namespace mpo;
     cudaStream_t s = (cudaStream_t)stream;
     bool done = false;
@@ -469,7 +485,7 @@ int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t star
     const int o32 = out_int32 ? 1 : 0;
     if (strategy != MPO_FPS_GROUP && N <= kPointsPerCta)
         return launch_single_any<false>(xyz, B, N, npoint, start_idx, skip, o32, out, status_out,
-                                        FlatFps{}, s);
+                                        FlatFps{}, s, out_xyz);
     GroupPlan plan;
     st = plan_group(B, N, strategy, &plan, "mpo_fps");
     if (st) return st;
@@ -479,7 +495,7 @@ int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t star
                                             " bytes");
     }
     return launch_group<false>(xyz, B, N, npoint, start_idx, skip, o32, out, plan, workspace,
-                               status_out, FlatFps{}, s, "mpo_fps");
+                               status_out, FlatFps{}, s, "mpo_fps", out_xyz);
 }
 
 size_t mpo_flat_fps_workspace_bytes(int64_t segments, int64_t max_len) {

@@ -20,7 +20,7 @@ from pathlib import Path
 import torch
 
 LIB_NAME = "libmpo_b200.so"
-ABI_VERSION = 4
+ABI_VERSION = 5
 _lib = None
 _lock = threading.Lock()
 _checked_devices: set[int] = set()
@@ -39,6 +39,9 @@ SIGNATURES = {
     "mpo_launch_count": (ctypes.c_uint64, []),
     "mpo_fps_workspace_bytes": (_sz, [_i64, _i64, _i64, _int]),
     "mpo_fps": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _sz, _vp]),
+    "mpo_fps_gather": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp,
+                              _sz, _vp]),
+    "mpo_gather_points_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "mpo_fps_noalloc": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp]),
     "mpo_knn_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "mpo_index_check": (_int, [_vp, _int, _i64, _i64, _vp, _vp]),
@@ -65,13 +68,16 @@ SIGNATURES = {
                             _vp]),
     "mpo_flat_radius": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i64, _int, _vp, _vp,
                                _vp]),
-    "mpo_group_points": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "mpo_group_points_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "mpo_group_points": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _sz,
+                                _vp]),
+    "mpo_query_and_group_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "mpo_group_points_backward": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _vp,
-                                         _vp]),
+                                         _vp, _sz, _vp]),
     "mpo_query_and_group": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _int,
-                                   _vp, _vp, _vp]),
+                                   _vp, _vp, _vp, _sz, _vp]),
     "mpo_query_and_group_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _int, _vp,
-                                            _vp, _vp, _vp]),
+                                            _vp, _vp, _vp, _sz, _vp]),
     "mpo_flat_fps_workspace_bytes": (_sz, [_i64, _i64]),
     "mpo_flat_fps": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _sz,
                             _vp]),

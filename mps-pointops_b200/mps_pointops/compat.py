@@ -45,7 +45,9 @@ def furthest_point_sample(xyz: Tensor, npoint: int) -> Tensor:
     """Like ``pointnet2_ops.pointnet2_utils.furthest_point_sample``
     (mps_pointops/compat.py:53-59): (B, N, 3) float32 -> (B, npoint) int32,
     starting at index 0 and never picking points with x^2 + y^2 + z^2 <= 1e-3."""
-    return ops._fps(xyz, npoint, 0, True, "auto", out_dtype=torch.int32)
+    out = ops._fps(xyz, npoint, 0, True, "auto", out_dtype=torch.int32)
+    out._mpo_index_bound = xyz.shape[1]  # valid indices: gather_operation skips its check
+    return out
 
 
 # gather_operation / grouping_operation (mps_pointops/compat.py:62-73) run on
@@ -84,6 +86,9 @@ def ball_query(radius: float, nsample: int, xyz: Tensor, new_xyz: Tensor) -> Ten
             N.check(N.lib().mpo_ball_query_pointnet2(N.ptr(a), N.ptr(q), B, Np, npoint, nsample,
                                                      radius_sq, N.ptr(out),
                                                      N.stream(xyz.device)), "ball_query")
+    # Every index lies in [0, N) (or is 0): grouping_operation can skip its
+    # bounds check on this tensor.
+    out._mpo_index_bound = Np
     return out
 
 

@@ -47,12 +47,20 @@ def test_gather_operation_matches_reference_golden(cuda_device):
 
 
 def test_out_of_range_index_raises(cuda_device):
+    # Reported without a host wait: by the call itself once the device is
+    # done, else by the next grouping call or check_indices().
     f = torch.randn(1, 4, 10, device=cuda_device)
     bad = torch.tensor([[[0, 3, 10]]], device=cuda_device)
     with pytest.raises(RuntimeError, match="out of bounds"):
         compat.grouping_operation(f, bad)
+        grouping.check_indices()
     with pytest.raises(RuntimeError, match="out of bounds"):
         compat.gather_operation(f, torch.tensor([[-1, 2]], device=cuda_device))
+        grouping.check_indices()
+    grouping.check_indices()  # nothing left pending
+    out = compat.gather_operation(f, torch.tensor([[9, 2]], device=cuda_device))
+    grouping.check_indices()
+    assert torch.equal(out, f[:, :, [9, 2]])
 
 
 @pytest.mark.parametrize("case", ["qg_r0.15", "qg_r0.4"])
@@ -121,3 +129,57 @@ def test_query_and_group_variants(cuda_device):
     _, want_idx = O.query_and_group(xyz.numpy(), q.numpy(), None, 0.3, 16)
     _, _, gf = O.query_and_group_backward(gout.numpy(), want_idx, 700)
     np.testing.assert_allclose(fr.grad.cpu().numpy(), gf, **TOL)
+
+
+def test_sample_and_gather_matches_fps_then_gather(cuda_device):
+    """tests/test_pointnet2_e2e.py:37-39 (compat FPS, then gather_operation) in
+    one launch: identical indices and coordinates, and the gradient of the
+    gathered points scatters back to xyz."""
+    g = torch.Generator().manual_seed(4)
+    for B, Np, P in ((8, 4096, 1024), (2, 9000, 300), (3, 50, 64)):
+        xyz = torch.rand(B, Np, 3, generator=g).to(cuda_device)
+        idx, new_xyz = grouping.sample_and_gather(xyz, P)
+        want_idx = compat.furthest_point_sample(xyz, P)
+        want = compat.gather_operation(xyz.transpose(1, 2).contiguous(), want_idx)
+        assert torch.equal(idx, want_idx)
+        assert torch.equal(new_xyz, want.transpose(1, 2))
+    xr = xyz.clone().requires_grad_()
+    idx, new_xyz = grouping.sample_and_gather(xr, 64)
+    gout = torch.randn(new_xyz.shape, generator=g).to(cuda_device)
+    new_xyz.backward(gout)
+    want = O.group_points_backward(gout.cpu().numpy().transpose(0, 2, 1)[..., None],
+                                   idx.cpu().numpy()[..., None], 50).transpose(0, 2, 1)
+    np.testing.assert_allclose(xr.grad.cpu().numpy(), want, **TOL)
+
+
+@pytest.mark.parametrize("B,Np,P,S,C,use_xyz", [
+    (2, 700, 10, 16, 8, True),      # P*S < N: gathers straight from (B, C, N)
+    (2, 700, 60, 16, 8, False),     # transposed features, 16-byte loads, no coordinates
+    (3, 257, 33, 9, 12, True),      # transposed, 12 channels (partial second chunk)
+    (1, 300, 40, 8, 3, True)])      # C < 4: direct path
+def test_query_and_group_paths(cuda_device, B, Np, P, S, C, use_xyz):
+    g = torch.Generator().manual_seed(5 + C)
+    xyz = torch.rand(B, Np, 3, generator=g)
+    q = xyz[:, :P].clone()
+    f = torch.randn(B, C, Np, generator=g)
+    xr = xyz.to(cuda_device).requires_grad_()
+    qr = q.to(cuda_device).requires_grad_()
+    fr = f.to(cuda_device).requires_grad_()
+    out, idx = grouping.query_and_group(xr, qr, fr, 0.25, S, use_xyz=use_xyz)
+    want, want_idx = O.query_and_group(xyz.numpy(), q.numpy(), f.numpy(), 0.25, S, use_xyz=use_xyz)
+    np.testing.assert_array_equal(idx.cpu().numpy(), want_idx)
+    np.testing.assert_array_equal(out.detach().cpu().numpy(), want)
+    gout = torch.randn(out.shape, generator=g)
+    out.backward(gout.to(cuda_device))
+    gx, gq, gf = O.query_and_group_backward(gout.numpy(), want_idx, Np, use_xyz=use_xyz)
+    np.testing.assert_allclose(fr.grad.cpu().numpy(), gf, **TOL)
+    if use_xyz:
+        np.testing.assert_allclose(xr.grad.cpu().numpy(), gx, **TOL)
+        np.testing.assert_allclose(qr.grad.cpu().numpy(), gq, **TOL)
+    fg = f.to(cuda_device).requires_grad_()
+    got = compat.grouping_operation(fg, idx)
+    np.testing.assert_array_equal(got.detach().cpu().numpy(), O.group_points(f.numpy(), want_idx))
+    gg = torch.randn(got.shape, generator=g)
+    got.backward(gg.to(cuda_device))
+    np.testing.assert_allclose(fg.grad.cpu().numpy(),
+                               O.group_points_backward(gg.numpy(), want_idx, Np), **TOL)
