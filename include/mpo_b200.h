@@ -38,7 +38,7 @@ extern "C" {
 #define MPO_API
 #endif
 
-#define MPO_ABI_VERSION 5
+#define MPO_ABI_VERSION 6
 
 #define MPO_OK 0
 #define MPO_ERR_INVALID_ARGUMENT 1
@@ -220,6 +220,26 @@ MPO_API int mpo_chamfer_backward(const float* x, const float* y, int64_t B, int6
                          int64_t D, const int64_t* idx_x, const float* grad_dist_x,
                          const int64_t* idx_y, const float* grad_dist_y, float* grad_x,
                          float* grad_y, void* stream);
+
+/* L1 Chamfer (norm=1): replaces chamfer_nearest_l1_f32 (kernels/chamfer_nn.metal:86-152)
+ * and the CPU path of mps_pointops/chamfer.py:161-212 with norm == 1.  Same
+ * arguments and conventions as mpo_chamfer_nearest without a workspace: the
+ * distance is |d0| + |d1| + ... in dimension order (d = query - ref, each
+ * operation rounded on its own), first minimum with the lowest index on
+ * ties; invalid rows get (0, -1). */
+MPO_API int mpo_chamfer_nearest_l1(const float* x, const float* y, const int64_t* x_lengths,
+                                   const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q,
+                                   int64_t D, int bidirectional, float* dist_x, int64_t* idx_x,
+                                   float* dist_y, int64_t* idx_y, void* stream);
+/* Its backward (mps_pointops/chamfer.py:269-293, PyTorch3D's subgradient): for
+ * every x row with idx_x >= 0, g = s * grad_dist_x with s = +1 where
+ * x > y[idx_x] and -1 otherwise (equality included); grad_x += g;
+ * grad_y[idx_x] -= g; symmetrically for y.  Outputs overwritten. */
+MPO_API int mpo_chamfer_l1_backward(const float* x, const float* y, int64_t B, int64_t P,
+                                    int64_t Q, int64_t D, const int64_t* idx_x,
+                                    const float* grad_dist_x, const int64_t* idx_y,
+                                    const float* grad_dist_y, float* grad_x, float* grad_y,
+                                    void* stream);
 
 /* Fused loss for chamfer_distance with the common reductions and no weights
  * or normals (mps_pointops/chamfer.py:436-488, PyTorch3D conventions):

@@ -428,6 +428,15 @@ inline size_t scratch_bytes(int64_t B, int64_t P, int64_t Q) {
 // memory, SD accumulated in increasing dimension order.
 constexpr int kDThreads = 128;
 
+// L1 distance in dimension order: |d0| + |d1| + ... (mps_pointops/chamfer.py:194-197).
+__device__ __forceinline__ float l1_seq(const float* a, const float* b, int D) {
+    float s = fabsf(__fsub_rn(a[0], b[0]));
+    for (int t = 1; t < D; ++t) s = __fadd_rn(s, fabsf(__fsub_rn(a[t], b[t])));
+    return s;
+}
+
+// NORM 2: squared L2 (sequential sum of squares); NORM 1: L1.
+template <int NORM>
 __global__ void __launch_bounds__(kDThreads)
 nearestd_kernel(const float* __restrict__ query, const float* __restrict__ ref,
                 const int64_t* __restrict__ query_lengths, const int64_t* __restrict__ ref_lengths,
@@ -461,11 +470,16 @@ nearestd_kernel(const float* __restrict__ query, const float* __restrict__ ref,
         const int cnt = (int)min64(tileN, nl - t0);
         for (int e = 0; e < cnt; ++e) {
             const float* rp = st + (size_t)e * D;
-            float dd = __fsub_rn(myq[0], rp[0]);
-            float s = __fmul_rn(dd, dd);
-            for (int u = 1; u < D; ++u) {
-                dd = __fsub_rn(myq[u], rp[u]);
-                s = __fadd_rn(s, __fmul_rn(dd, dd));
+            float s;
+            if (NORM == 1) {
+                s = l1_seq(myq, rp, D);
+            } else {
+                float dd = __fsub_rn(myq[0], rp[0]);
+                s = __fmul_rn(dd, dd);
+                for (int u = 1; u < D; ++u) {
+                    dd = __fsub_rn(myq[u], rp[u]);
+                    s = __fadd_rn(s, __fmul_rn(dd, dd));
+                }
             }
             if (s < bd) {
                 bd = s;
@@ -482,7 +496,7 @@ nearestd_kernel(const float* __restrict__ query, const float* __restrict__ ref,
     }
     if (bj == kNone) {
         bj = 0;
-        bd = sqd_seq(query + o * D, r, D);
+        bd = NORM == 1 ? l1_seq(query + o * D, r, D) : sqd_seq(query + o * D, r, D);
     }
     out_dist[o] = bd;
     out_idx[o] = (int64_t)bj;
@@ -506,6 +520,31 @@ __global__ void chamfer_bwd_kernel(const float* __restrict__ qpts, const float* 
     float* gr = grad_r + (b * N + j) * D;
     for (int64_t t = 0; t < D; ++t) {
         const float g = __fmul_rn(__fsub_rn(qp[t], rp[t]), c);
+        atomicAdd(gq + t, g);
+        atomicAdd(gr + t, -g);
+    }
+}
+
+// L1 backward for one direction (mps_pointops/chamfer.py:269-293, PyTorch3D's
+// subgradient): rows with idx >= 0 add g = s * gd, s = +1 where q > r[idx]
+// and -1 otherwise (at equality too), to grad_q and -g to grad_r[idx].
+__global__ void chamfer_l1_bwd_kernel(const float* __restrict__ qpts,
+                                      const float* __restrict__ rpts, int64_t B, int64_t M,
+                                      int64_t N, int64_t D, const int64_t* __restrict__ idx,
+                                      const float* __restrict__ gd, float* __restrict__ grad_q,
+                                      float* __restrict__ grad_r) {
+    const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= B * M) return;
+    const int64_t j = idx[row];
+    if (j < 0) return;
+    const int64_t b = row / M;
+    const float c = gd[row];
+    const float* qp = qpts + row * D;
+    const float* rp = rpts + (b * N + j) * D;
+    float* gq = grad_q + row * D;
+    float* gr = grad_r + (b * N + j) * D;
+    for (int64_t t = 0; t < D; ++t) {
+        const float g = qp[t] > rp[t] ? c : -c;
         atomicAdd(gq + t, g);
         atomicAdd(gr + t, -g);
     }
@@ -702,12 +741,50 @@ static int nearest_dir(const float* q, const float* r, const int64_t* ql, const 
         smem = ((size_t)kDThreads * (D + 1) + (size_t)tileN * D) * sizeof(float);
     }
     if (smem > 200 * 1024) return fail(kUnsupported, "chamfer: coordinate dimension too large");
-    if (cudaFuncSetAttribute(nearestd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(nearestd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
         return fail(kCudaError, "chamfer: cannot raise the shared-memory limit");
     dim3 grid((unsigned)ceil_div(M, kDThreads), (unsigned)B);
-    nearestd_kernel<<<grid, kDThreads, smem, s>>>(q, r, ql, rl, M, N, (int)D, tileN, dist, idx);
+    nearestd_kernel<2><<<grid, kDThreads, smem, s>>>(q, r, ql, rl, M, N, (int)D, tileN, dist, idx);
     return check_launch("nearestd_kernel");
+}
+
+static int nearest_l1_dir(const float* q, const float* r, const int64_t* ql, const int64_t* rl,
+                          int64_t B, int64_t M, int64_t N, int64_t D, float* dist, int64_t* idx,
+                          cudaStream_t s) {
+    using namespace mpo;
+    if (B == 0 || M == 0) return kOk;
+    int tileN = 256;
+    size_t smem = ((size_t)kDThreads * (D + 1) + (size_t)tileN * D) * sizeof(float);
+    while (smem > 200 * 1024 && tileN > 1) {
+        tileN /= 2;
+        smem = ((size_t)kDThreads * (D + 1) + (size_t)tileN * D) * sizeof(float);
+    }
+    if (smem > 200 * 1024) return fail(kUnsupported, "chamfer: coordinate dimension too large");
+    if (cudaFuncSetAttribute(nearestd_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return fail(kCudaError, "chamfer: cannot raise the shared-memory limit");
+    dim3 grid((unsigned)ceil_div(M, kDThreads), (unsigned)B);
+    nearestd_kernel<1><<<grid, kDThreads, smem, s>>>(q, r, ql, rl, M, N, (int)D, tileN, dist, idx);
+    return check_launch("nearestd_kernel<L1>");
+}
+
+int mpo_chamfer_nearest_l1(const float* x, const float* y, const int64_t* x_lengths,
+                           const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q, int64_t D,
+                           int bidirectional, float* dist_x, int64_t* idx_x, float* dist_y,
+                           int64_t* idx_y, void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(B >= 0 && P >= 0 && Q >= 0 && D >= 1, "bad sizes");
+    MPO_REQUIRE(B <= 65535, "batch must be at most 65535");
+    MPO_REQUIRE(P < (int64_t)0x7fffffff && Q < (int64_t)0x7fffffff, "P and Q must be below 2**31");
+    if (B == 0) return kOk;
+    MPO_REQUIRE((x || P == 0) && (y || Q == 0), "null pointer");
+    MPO_REQUIRE((dist_x && idx_x) || P == 0, "null output pointer");
+    MPO_REQUIRE(!bidirectional || (dist_y && idx_y) || Q == 0, "null output pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    int st = nearest_l1_dir(x, y, x_lengths, y_lengths, B, P, Q, D, dist_x, idx_x, s);
+    if (st || !bidirectional) return st;
+    return nearest_l1_dir(y, x, y_lengths, x_lengths, B, Q, P, D, dist_y, idx_y, s);
 }
 
 }  // extern "C"
@@ -895,6 +972,32 @@ int mpo_chamfer_backward(const float* x, const float* y, int64_t B, int64_t P, i
         chamfer_bwd_kernel<<<(unsigned)ceil_div(B * Q, 256), 256, 0, s>>>(
             y, x, B, Q, P, D, idx_y, grad_dist_y, grad_y, grad_x);
         return check_launch("chamfer_bwd_kernel");
+    }
+    return kOk;
+}
+
+int mpo_chamfer_l1_backward(const float* x, const float* y, int64_t B, int64_t P, int64_t Q,
+                            int64_t D, const int64_t* idx_x, const float* grad_dist_x,
+                            const int64_t* idx_y, const float* grad_dist_y, float* grad_x,
+                            float* grad_y, void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(B >= 0 && P >= 0 && Q >= 0 && D >= 1, "bad sizes");
+    MPO_REQUIRE((grad_x || B * P * D == 0) && (grad_y || B * Q * D == 0), "null gradient pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (B * P * D > 0 && cudaMemsetAsync(grad_x, 0, sizeof(float) * B * P * D, s) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_l1_backward: memset failed");
+    if (B * Q * D > 0 && cudaMemsetAsync(grad_y, 0, sizeof(float) * B * Q * D, s) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_l1_backward: memset failed");
+    if (grad_dist_x && B * P > 0) {
+        chamfer_l1_bwd_kernel<<<(unsigned)ceil_div(B * P, 256), 256, 0, s>>>(
+            x, y, B, P, Q, D, idx_x, grad_dist_x, grad_x, grad_y);
+        int st = check_launch("chamfer_l1_bwd_kernel");
+        if (st) return st;
+    }
+    if (grad_dist_y && B * Q > 0) {
+        chamfer_l1_bwd_kernel<<<(unsigned)ceil_div(B * Q, 256), 256, 0, s>>>(
+            y, x, B, Q, P, D, idx_y, grad_dist_y, grad_y, grad_x);
+        return check_launch("chamfer_l1_bwd_kernel");
     }
     return kOk;
 }

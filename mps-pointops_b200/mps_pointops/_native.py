@@ -20,7 +20,7 @@ from pathlib import Path
 import torch
 
 LIB_NAME = "libmpo_b200.so"
-ABI_VERSION = 5
+ABI_VERSION = 6
 _lib = None
 _lock = threading.Lock()
 _checked_devices: set[int] = set()
@@ -63,6 +63,10 @@ SIGNATURES = {
                                    _vp, _vp, _vp, _sz, _vp]),
     "mpo_chamfer_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp]),
+    "mpo_chamfer_nearest_l1": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp,
+                                      _vp, _vp, _vp, _vp]),
+    "mpo_chamfer_l1_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp,
+                                       _vp, _vp, _vp]),
     "mpo_chamfer_check_inputs": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "mpo_flat_knn": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp,
                             _vp]),

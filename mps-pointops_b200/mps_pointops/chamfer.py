@@ -1,4 +1,4 @@
-"""Bidirectional squared-L2 Chamfer loss on B200.
+"""Bidirectional Chamfer loss (squared L2 and L1) on B200.
 
 Drop-in for ``mps_pointops.chamfer.chamfer_distance`` of gamzerA/mps-pointops
 v1.0.0 (mps_pointops/chamfer.py:342-488): PyTorch3D argument conventions --
@@ -8,8 +8,8 @@ validation and error messages.  The nearest-neighbour search and its backward
 run in the sm_100a kernels of libmpo_b200.so; the reductions over the
 per-point distances are tensor ops on the device.
 
-Scope of this build: float32 CUDA tensors and ``norm=2``.  ``norm=1`` raises
-``NotImplementedError``; float64 raises ``TypeError``.
+Scope of this build: float32 CUDA tensors, ``norm=2`` and ``norm=1`` (L1, on
+``mpo_chamfer_nearest_l1``); float64 raises ``TypeError``.
 """
 
 from __future__ import annotations
@@ -160,6 +160,48 @@ class _NearestSquared(torch.autograd.Function):
         return grad_x, grad_y, None, None, None
 
 
+class _NearestL1(torch.autograd.Function):
+    """L1 nearest search in both directions and PyTorch3D's selected-pair
+    subgradient (mps_pointops/chamfer.py:254-293)."""
+
+    @staticmethod
+    def forward(ctx, x, y, lx, ly, bidirectional: bool):
+        B, P, D = x.shape
+        Q = y.shape[1]
+        dev = x.device
+        dist_x = torch.empty((B, P), dtype=torch.float32, device=dev)
+        idx_x = torch.empty((B, P), dtype=torch.long, device=dev)
+        dist_y = torch.empty((B, Q if bidirectional else 0), dtype=torch.float32, device=dev)
+        idx_y = torch.empty((B, Q if bidirectional else 0), dtype=torch.long, device=dev)
+        xc, yc = x.contiguous(), y.contiguous()
+        with N.on_device(dev):
+            N.check(N.lib().mpo_chamfer_nearest_l1(
+                N.ptr(xc), N.ptr(yc), N.ptr(lx), N.ptr(ly), B, P, Q, D, int(bidirectional),
+                N.ptr(dist_x), N.ptr(idx_x), N.ptr(dist_y), N.ptr(idx_y), N.stream(dev)),
+                "chamfer nearest (L1)")
+        ctx.save_for_backward(xc, yc, idx_x, idx_y)
+        ctx.bidirectional = bidirectional
+        ctx.mark_non_differentiable(idx_x, idx_y)
+        ctx.set_materialize_grads(False)
+        return dist_x, dist_y, idx_x, idx_y
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g_dx, g_dy, _gix, _giy):
+        x, y, idx_x, idx_y = ctx.saved_tensors
+        B, P, D = x.shape
+        Q = y.shape[1]
+        grad_x = torch.empty_like(x)
+        grad_y = torch.empty_like(y)
+        gx = None if g_dx is None else g_dx.float().contiguous()
+        gy = None if (g_dy is None or not ctx.bidirectional) else g_dy.float().contiguous()
+        with N.on_device(x.device):
+            N.check(N.lib().mpo_chamfer_l1_backward(
+                N.ptr(x), N.ptr(y), B, P, Q, D, N.ptr(idx_x), N.ptr(gx), N.ptr(idx_y), N.ptr(gy),
+                N.ptr(grad_x), N.ptr(grad_y), N.stream(x.device)), "chamfer backward (L1)")
+        return grad_x, grad_y, None, None, None
+
+
 class _ChamferLoss(torch.autograd.Function):
     """Fused search + reduction for the common case (no weights, no normals,
     point_reduction mean/sum): one native call forward, one backward, instead
@@ -265,8 +307,8 @@ def chamfer_distance(
     single_directional: bool = False,
     abs_cosine: bool = True,
 ):
-    """Squared-L2 Chamfer loss with PyTorch3D reduction conventions
-    (mps_pointops/chamfer.py:342-488).
+    """Chamfer loss (squared L2, or L1 with ``norm=1``) with PyTorch3D
+    reduction conventions (mps_pointops/chamfer.py:342-488).
 
     ``x`` (B,P,D) and ``y`` (B,Q,D) float32 CUDA tensors, D >= 1.  Each valid
     point is matched to the FIRST nearest valid point of the other cloud
@@ -307,10 +349,7 @@ def chamfer_distance(
         if bool((weights == 0).all().item()):
             return _all_zero_weights(x, y, lx, ly, weights, point_reduction, batch_reduction,
                                      single_directional)
-    if norm == 1:
-        raise NotImplementedError("norm=1 (L1) Chamfer is not implemented in the B200 build")
-
-    if weights is None and not return_normals and point_reduction in ("mean", "sum"):
+    if norm == 2 and weights is None and not return_normals and point_reduction in ("mean", "sum"):
         loss = _ChamferLoss.apply(x, y, lx, ly, not single_directional,
                                   1 if point_reduction == "mean" else 0,
                                   {None: 0, "sum": 1, "mean": 2}[batch_reduction])
@@ -318,7 +357,8 @@ def chamfer_distance(
             pending.raise_if_bad()
         return loss, None
 
-    dx, dy, ix, iy = _NearestSquared.apply(x, y, lx, ly, not single_directional)
+    search = _NearestL1 if norm == 1 else _NearestSquared
+    dx, dy, ix, iy = search.apply(x, y, lx, ly, not single_directional)
     if pending is not None:
         pending.raise_if_bad()
     nx = ny = None

@@ -267,12 +267,13 @@ def fps(
     out_ptr = torch.tensor(output_offsets, dtype=torch.long, device=device)
     status = torch.empty(1, dtype=torch.int32, device=device)
     points = x.contiguous()
+    starts = starts.contiguous()  # held until the launch is queued
     with N.on_device(device):
         lib = N.lib()
         ws_bytes = int(lib.mpo_flat_fps_workspace_bytes(len(lengths), max_len))
         ws = N.workspace(ws_bytes, device)
         N.check(lib.mpo_flat_fps(N.ptr(points), N.ptr(offsets), N.ptr(out_ptr),
-                                 N.ptr(starts.contiguous()), len(lengths), len(x), total, max_len,
+                                 N.ptr(starts), len(lengths), len(x), total, max_len,
                                  N.ptr(out), N.ptr(status), N.ptr(ws), ws_bytes,
                                  N.stream(device)), "flat fps")
     if max_len > 8192:

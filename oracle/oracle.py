@@ -63,6 +63,8 @@ def _load():
             _f32p, _f32p, _i64p, _i64p, _i64, _i64, _i64, _i64, _i64p, _i64p, _f32p, _f32p,
             _f32p, _f32p]
         lib.oracle_chamfer_mean_loss_and_grad.restype = ctypes.c_double
+        lib.oracle_chamfer_nearest_l1.argtypes = [_f32p, _f32p, _i64p, _i64p, _i64, _i64, _i64,
+                                                  _i64, _f32p, _i64p]
         lib.oracle_flat_search.argtypes = [_f32p, _f32p, _i64p, _i64p, _i64, _i64, _i64,
                                            ctypes.c_int, ctypes.c_float, ctypes.c_int, _i64, _i64,
                                            _i64p]
@@ -256,9 +258,11 @@ def three_interpolate_backward(grad_out, indices, weights, M: int) -> np.ndarray
 
 
 # ---------------------------------------------------------------- Chamfer
-def chamfer_nearest(query, ref, query_lengths=None, ref_lengths=None):
-    """mps_pointops/chamfer.py:161-212 + 297-308: first-minimum index and its SD."""
+def chamfer_nearest(query, ref, query_lengths=None, ref_lengths=None, norm: int = 2):
+    """mps_pointops/chamfer.py:161-212 + 297-320: first-minimum index and its
+    distance (SD for norm 2, L1 for norm 1)."""
     lib = _load()
+    fn = lib.oracle_chamfer_nearest_l1 if norm == 1 else lib.oracle_chamfer_nearest
     query, ref = _f32(query), _f32(ref)
     ql, rl = _i64a(query_lengths), _i64a(ref_lengths)
     B, P, D = query.shape
@@ -274,9 +278,9 @@ def chamfer_nearest(query, ref, query_lengths=None, ref_lengths=None):
             def job(b=b, lo=lo, hi=hi):
                 qlb = None if ql is None else np.array([max(0, min(hi, ql[b]) - lo)], np.int64)
                 rlb = None if rl is None else rl[b:b + 1].copy()
-                lib.oracle_chamfer_nearest(_ptr(query[b, lo:hi], _f32p), _ptr(ref[b], _f32p),
-                                           _ptr(qlb, _i64p), _ptr(rlb, _i64p), 1, hi - lo, Q, D,
-                                           _ptr(dist[b, lo:hi], _f32p), _ptr(idx[b, lo:hi], _i64p))
+                fn(_ptr(query[b, lo:hi], _f32p), _ptr(ref[b], _f32p), _ptr(qlb, _i64p),
+                   _ptr(rlb, _i64p), 1, hi - lo, Q, D, _ptr(dist[b, lo:hi], _f32p),
+                   _ptr(idx[b, lo:hi], _i64p))
             jobs.append(job)
     _parallel(jobs)
     return dist, idx
@@ -302,6 +306,26 @@ def chamfer_mean_loss_and_grad(x, y, x_lengths=None, y_lengths=None):
         _ptr(ix, _i64p), _ptr(iy, _i64p), _ptr(dx, _f32p), _ptr(dy, _f32p),
         _ptr(gx, _f32p), _ptr(gy, _f32p))
     return loss, gx, gy, (dx, ix), (dy, iy)
+
+
+def chamfer_l1_grads(x, y, ix, iy, gdx, gdy):
+    """Gradient of the selected L1 distances (mps_pointops/chamfer.py:269-293):
+    g = s * gd with s = +1 where q > r and -1 otherwise, added to the query and
+    subtracted from the selected reference (float64 sums)."""
+    x, y = np.asarray(x, np.float64), np.asarray(y, np.float64)
+    gx, gy = np.zeros_like(x), np.zeros_like(y)
+    for q, r, idx, gd, gq, gr in ((x, y, ix, gdx, gx, gy), (y, x, iy, gdy, gy, gx)):
+        if gd is None:
+            continue
+        for b in range(q.shape[0]):
+            for i in range(q.shape[1]):
+                j = idx[b, i]
+                if j < 0:
+                    continue
+                g = np.where(q[b, i] > r[b, j], 1.0, -1.0) * float(gd[b, i])
+                gq[b, i] += g
+                gr[b, j] -= g
+    return gx, gy
 
 
 # ---------------------------------------------------------------- flat batches

@@ -316,6 +316,45 @@ EXPORT void oracle_chamfer_nearest(const float* query, const float* ref,
     }
 }
 
+/* L1 variant (mps_pointops/chamfer.py:161-212 with norm == 1; distance of the
+ * selected pair: _selected_l1_distance, chamfer.py:310-320): |d0| + |d1| + ...
+ * in dimension order, d = query - ref, each operation rounded on its own;
+ * the same first-minimum and padding rules as oracle_chamfer_nearest. */
+static inline float l1dist(const float* a, const float* b, int64_t D) {
+    float s = fabsf(a[0] - b[0]);
+    for (int64_t t = 1; t < D; ++t) {
+        float d = fabsf(a[t] - b[t]);
+        s = s + d;
+    }
+    return s;
+}
+
+EXPORT void oracle_chamfer_nearest_l1(const float* query, const float* ref,
+                                      const int64_t* query_lengths, const int64_t* ref_lengths,
+                                      int64_t B, int64_t P, int64_t Q, int64_t D,
+                                      float* dist, int64_t* idx) {
+    for (int64_t b = 0; b < B; ++b) {
+        for (int64_t i = 0; i < P; ++i) {
+            int64_t ql = query_lengths ? query_lengths[b] : P;
+            int64_t rl = ref_lengths ? ref_lengths[b] : Q;
+            int64_t best = -1;
+            float bd = INFINITY;
+            if (i < ql) {
+                const float* qp = query + (b * P + i) * D;
+                for (int64_t j = 0; j < rl; ++j) {
+                    float d = l1dist(qp, ref + (b * Q + j) * D, D);
+                    if (best < 0 || d < bd) {
+                        bd = d;
+                        best = j;
+                    }
+                }
+            }
+            idx[b * P + i] = best;
+            dist[b * P + i] = best < 0 ? 0.f : bd;
+        }
+    }
+}
+
 /* Chamfer squared-L2 loss with point_reduction="mean", batch_reduction="mean"
  * and its gradients, accumulated in binary64 (chamfer.py:342-488 forward,
  * chamfer.py:215-251 backward).  loss = (1/B) sum_b (sum_i dx_i / Px_b +

@@ -315,6 +315,45 @@ def chamfer_cases():
     save("chamfer", **out)
 
 
+def chamfer_l1_cases():
+    """chamfer_distance(norm=1) on the reference's CPU path (chamfer.py:161-212,
+    254-293, 342-488): losses and gradients for lengths, weights, normals,
+    reductions and single-directional calls."""
+    out = {}
+    g = torch.Generator().manual_seed(55)
+    x, y = torch.randn(3, 40, 3, generator=g), torch.randn(3, 31, 3, generator=g)
+    lx, ly = torch.tensor([40, 17, 5]), torch.tensor([31, 9, 30])
+    xn = torch.nn.functional.normalize(torch.randn(3, 40, 3, generator=g), dim=-1)
+    yn = torch.nn.functional.normalize(torch.randn(3, 31, 3, generator=g), dim=-1)
+    w = torch.tensor([0.5, 2.0, 1.0])
+    cases = {
+        "plain": dict(),
+        "lengths": dict(x_lengths=lx, y_lengths=ly),
+        "weights_sum": dict(x_lengths=lx, y_lengths=ly, weights=w, batch_reduction="sum"),
+        "normals": dict(x_lengths=lx, y_lengths=ly, x_normals=xn, y_normals=yn),
+        "single_max": dict(single_directional=True, point_reduction="max", batch_reduction=None),
+        "d5": dict(),
+    }
+    for name, kw in cases.items():
+        xs, ys = (torch.randn(2, 23, 5, generator=g), torch.randn(2, 19, 5, generator=g)) \
+            if name == "d5" else (x, y)
+        xr, yr = xs.clone().requires_grad_(), ys.clone().requires_grad_()
+        loss, nl = ref_chamfer.chamfer_distance(xr, yr, norm=1, **kw)
+        loss.sum().backward()
+        out[f"{name}/x"], out[f"{name}/y"] = xs, ys
+        out[f"{name}/loss"] = loss.detach()
+        out[f"{name}/grad_x"], out[f"{name}/grad_y"] = xr.grad, yr.grad
+        if nl is not None:
+            out[f"{name}/normal_loss"] = nl.detach()
+        if name != "d5":
+            lxx = kw.get("x_lengths", torch.full((3,), 40))
+            lyy = kw.get("y_lengths", torch.full((3,), 31))
+            out[f"{name}/idx_x"] = ref_chamfer._nearest_indices(xs, ys, lxx, lyy, norm=1)
+    out["inputs/x_lengths"], out["inputs/y_lengths"] = lx, ly
+    out["inputs/x_normals"], out["inputs/y_normals"], out["inputs/weights"] = xn, yn, w
+    save("chamfer_l1", **out)
+
+
 # ------------------------------------------------------------------ flat (torch_cluster) API
 def flat_cases():
     """The CPU path of mps_pointops/flat.py: _reference_search (:264-288) for
@@ -453,5 +492,6 @@ if __name__ == "__main__":
     chamfer_cases()
     flat_cases()
     grouping_cases()
+    chamfer_l1_cases()
     for f in sorted(OUT.glob("*.npz")):
         print(f"{f.name}: {f.stat().st_size / 1024:.0f} KiB")
