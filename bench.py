@@ -61,7 +61,7 @@ def parse_args():
     ap.add_argument("--workload", default="chamfer_config2",
                     choices=["chamfer_config2", "ssg_config1_ops", "fps_config3",
                              "feature_knn_config4", "knn_config5", "ball_query_config5",
-                             "flat_ops", "sa_grouping_config1"],
+                             "flat_ops", "sa_grouping_config1", "chamfer_variants_config2"],
                     help="single-GPU measurement of one BASELINE config (the default is the "
                          "headline line; the others print their own JSON line and are used "
                          "for the per-kernel profiles)")
@@ -522,6 +522,35 @@ def sa_grouping_config1(steps: int, warmup: int) -> dict:
     return res
 
 
+def chamfer_variants_config2(steps: int, warmup: int) -> dict:
+    """Chamfer forward + backward at BASELINE config 2 (32 x 8192^2, D = 3) for
+    the calls outside the headline's fused path: L1 (norm=1), per-cloud
+    weights (squared L2, the general path), and normals; pairs/s, CUDA
+    events, L2 flushed between steps."""
+    from mps_pointops.chamfer import chamfer_distance
+    x, y = (t.cuda() for t in chamfer_inputs(B_PER_GPU, seed=2))
+    g = torch.Generator().manual_seed(3)
+    xn = torch.nn.functional.normalize(torch.randn(x.shape, generator=g), dim=-1).cuda()
+    yn = torch.nn.functional.normalize(torch.randn(y.shape, generator=g), dim=-1).cuda()
+    w = torch.rand(B_PER_GPU, generator=g).cuda() + 0.5
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    def step(**kw):
+        xr, yr = x.clone().requires_grad_(), y.clone().requires_grad_()
+        loss, nl = chamfer_distance(xr, yr, **kw)
+        (loss + (nl if nl is not None else 0)).backward()
+
+    arms = {"l2_fused": {}, "l1": {"norm": 1}, "l2_weights": {"weights": w},
+            "l2_normals": {"x_normals": xn, "y_normals": yn}}
+    pairs = B_PER_GPU * NPTS * NPTS
+    res = {"workload": "chamfer_variants_config2", "unit": "ms (median fwd+bwd)",
+           "pairs_per_step": pairs}
+    for name, kw in arms.items():
+        ms = _event_ms(lambda: step(**kw), steps, warmup, flush)
+        res[name] = {"ms": ms, "pairs_per_s": pairs / (ms / 1e3)}
+    return res
+
+
 def _measured_hbm_gbs() -> float:
     try:
         return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"])
@@ -714,6 +743,8 @@ def main():
             out = ssg_config1_ops(steps, max(warmup, 3))
         elif args.workload == "fps_config3":
             out = fps_config3(min(steps, 3), 1)
+        elif args.workload == "chamfer_variants_config2":
+            out = chamfer_variants_config2(min(steps, 10), max(warmup, 3))
         elif args.workload == "sa_grouping_config1":
             out = sa_grouping_config1(steps, max(warmup, 3))
         elif args.workload == "flat_ops":

@@ -29,6 +29,21 @@ constexpr int kThreads = 256;
 constexpr int kTile = 1024;
 constexpr uint32_t kNone = 0xffffffffu;
 
+// L1 distance for D == 3: (|dx| + |dy|) + |dz|, each operation rounded.
+__device__ __forceinline__ float l1d3(float ax, float ay, float az, float bx, float by,
+                                      float bz) {
+    return __fadd_rn(__fadd_rn(fabsf(__fsub_rn(ax, bx)), fabsf(__fsub_rn(ay, by))),
+                     fabsf(__fsub_rn(az, bz)));
+}
+
+// NORM 2: squared L2; NORM 1: L1.
+template <int NORM>
+__device__ __forceinline__ float dist3(float ax, float ay, float az, float bx, float by,
+                                       float bz) {
+    return NORM == 1 ? l1d3(ax, ay, az, bx, by, bz) : sqd3(ax, ay, az, bx, by, bz);
+}
+
+template <int NORM>
 __global__ void __launch_bounds__(kThreads)
 nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
                 const int64_t* __restrict__ query_lengths, const int64_t* __restrict__ ref_lengths,
@@ -96,7 +111,7 @@ nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const float4 p = tp[e + u];
-                    dd[u] = sqd3(qx, qy, qz, p.x, p.y, p.z);
+                    dd[u] = dist3<NORM>(qx, qy, qz, p.x, p.y, p.z);
                 }
                 const float m = fminf(fminf(dd[0], dd[1]), fminf(dd[2], dd[3]));
                 if (m < bd) {
@@ -107,7 +122,7 @@ nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
             }
             for (; e < cnt; ++e) {
                 const float4 p = tp[e];
-                const float d = sqd3(qx, qy, qz, p.x, p.y, p.z);
+                const float d = dist3<NORM>(qx, qy, qz, p.x, p.y, p.z);
                 if (d < bd) {
                     bd = d;
                     bj = (uint32_t)(j0 + e);
@@ -143,7 +158,7 @@ nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
     }
     if (bj == kNone) {  // every SD overflowed: the first valid reference
         bj = 0;
-        bd = sqd3(qx, qy, qz, r[0], r[1], r[2]);
+        bd = dist3<NORM>(qx, qy, qz, r[0], r[1], r[2]);
     }
     out_dist[o] = bd;
     out_idx[o] = (int64_t)bj;
@@ -727,11 +742,11 @@ static int nearest_dir(const float* q, const float* r, const int64_t* ql, const 
         while (S < 8 && B * M * S < (int64_t)sm_count() * 1024) S *= 2;
         const int qpc = kThreads / S;
         const size_t smem = 2 * kTile * sizeof(float4);
-        if (cudaFuncSetAttribute(nearest3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(nearest3_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem) != cudaSuccess)
             return fail(kCudaError, "chamfer: cannot raise the shared-memory limit");
         dim3 grid((unsigned)ceil_div(M, qpc), (unsigned)B);
-        nearest3_kernel<<<grid, kThreads, smem, s>>>(q, r, ql, rl, M, N, S, dist, idx);
+        nearest3_kernel<2><<<grid, kThreads, smem, s>>>(q, r, ql, rl, M, N, S, dist, idx);
         return check_launch("nearest3_kernel");
     }
     int tileN = 256;
@@ -754,6 +769,18 @@ static int nearest_l1_dir(const float* q, const float* r, const int64_t* ql, con
                           cudaStream_t s) {
     using namespace mpo;
     if (B == 0 || M == 0) return kOk;
+    if (D == 3) {
+        int S = 1;
+        while (S < 8 && B * M * S < (int64_t)sm_count() * 1024) S *= 2;
+        const int qpc = kThreads / S;
+        const size_t smem3 = 2 * kTile * sizeof(float4);
+        if (cudaFuncSetAttribute(nearest3_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem3) != cudaSuccess)
+            return fail(kCudaError, "chamfer: cannot raise the shared-memory limit");
+        dim3 grid((unsigned)ceil_div(M, qpc), (unsigned)B);
+        nearest3_kernel<1><<<grid, kThreads, smem3, s>>>(q, r, ql, rl, M, N, S, dist, idx);
+        return check_launch("nearest3_kernel<L1>");
+    }
     int tileN = 256;
     size_t smem = ((size_t)kDThreads * (D + 1) + (size_t)tileN * D) * sizeof(float);
     while (smem > 200 * 1024 && tileN > 1) {
