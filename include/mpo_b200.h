@@ -38,7 +38,7 @@ extern "C" {
 #define MPO_API
 #endif
 
-#define MPO_ABI_VERSION 6
+#define MPO_ABI_VERSION 7
 
 #define MPO_OK 0
 #define MPO_ERR_INVALID_ARGUMENT 1
@@ -333,6 +333,38 @@ MPO_API int mpo_query_and_group_backward(const float* grad_out, const int32_t* i
                                          int use_xyz, float* grad_xyz, float* grad_new_xyz,
                                          float* grad_features, void* workspace,
                                          size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ spatial grid
+ * Grid-accelerated exact search over one cloud: replaces the reference's
+ * opt-in spatial index (mps_pointops/spatial.py:76-264, SpatialIndex with
+ * its Morton BVH, kernels spatial_bvh.metal / spatial_keys.metal).  Results
+ * equal the brute-force searches' (mpo_knn D == 3 policy; mpo_ball_query).
+ * A uniform grid of dims[0] x dims[1] x dims[2] cubic cells of side
+ * cell_size from origin (both HOST arrays of 3) is built by counting sort:
+ * cell_start (device int32, cells + 1 entries), sorted_points (device, N
+ * float4 = x, y, z, original index bits), extra_points (device, room for N
+ * float4: the points with a non-finite coordinate) and *n_extra_out (device
+ * int32: their count).  Points outside the box are clamped into the edge
+ * cells.  Workspace: mpo_grid_workspace_bytes(N, cells). */
+MPO_API size_t mpo_grid_workspace_bytes(int64_t N, int64_t cells);
+MPO_API int mpo_grid_build(const float* points, int64_t N, const float* origin, float cell_size,
+                           const int* dims, int* cell_start, float* sorted_points,
+                           float* extra_points, int32_t* n_extra_out, void* workspace,
+                           size_t workspace_bytes, void* stream);
+/* k nearest (k <= 32) of Q queries (Q, 3): dist (Q, k) Euclidean, idx (Q, k)
+ * int64 original indices, ascending (squared distance, index), NaN dropped,
+ * (inf, -1) padding.  n_extra: the host copy of the build's count. */
+MPO_API int mpo_grid_knn(const float* query, int64_t Q, const float* origin, float cell_size,
+                         const int* dims, const int* cell_start, const float* sorted_points,
+                         const float* extra_points, int32_t n_extra, int64_t k, float* dist,
+                         int64_t* idx, void* stream);
+/* First K (<= 32) points in input order with squared distance < radius_sq:
+ * dist2 (Q, K), idx (Q, K) int64, (0, -1) padding.  radius is the float32
+ * radius (it sets how many cells around the query are searched). */
+MPO_API int mpo_grid_ball_query(const float* query, int64_t Q, const float* origin,
+                                float cell_size, const int* dims, const int* cell_start,
+                                const float* sorted_points, float radius, float radius_sq,
+                                int64_t K, float* dist2, int64_t* idx, void* stream);
 
 /* ------------------------------------------------------------------ flat batches
  * The torch_cluster-style API of mps_pointops/flat.py:161-425 works on flat

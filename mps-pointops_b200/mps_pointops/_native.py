@@ -20,7 +20,7 @@ from pathlib import Path
 import torch
 
 LIB_NAME = "libmpo_b200.so"
-ABI_VERSION = 6
+ABI_VERSION = 7
 _lib = None
 _lock = threading.Lock()
 _checked_devices: set[int] = set()
@@ -29,6 +29,7 @@ _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
 _f32 = ctypes.c_float
+_i32 = ctypes.c_int32
 _sz = ctypes.c_size_t
 
 # name -> (restype, argtypes); mirrors include/mpo_b200.h one to one.
@@ -82,6 +83,11 @@ SIGNATURES = {
                                    _vp, _vp, _vp, _sz, _vp]),
     "mpo_query_and_group_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _int, _vp,
                                             _vp, _vp, _vp, _sz, _vp]),
+    "mpo_grid_workspace_bytes": (_sz, [_i64, _i64]),
+    "mpo_grid_build": (_int, [_vp, _i64, _vp, _f32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "mpo_grid_knn": (_int, [_vp, _i64, _vp, _f32, _vp, _vp, _vp, _vp, _i32, _i64, _vp, _vp, _vp]),
+    "mpo_grid_ball_query": (_int, [_vp, _i64, _vp, _f32, _vp, _vp, _vp, _f32, _f32, _i64, _vp,
+                                   _vp, _vp]),
     "mpo_flat_fps_workspace_bytes": (_sz, [_i64, _i64]),
     "mpo_flat_fps": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _sz,
                             _vp]),
