@@ -61,7 +61,8 @@ def parse_args():
     ap.add_argument("--workload", default="chamfer_config2",
                     choices=["chamfer_config2", "ssg_config1_ops", "fps_config3",
                              "feature_knn_config4", "knn_config5", "ball_query_config5",
-                             "flat_ops", "sa_grouping_config1", "chamfer_variants_config2"],
+                             "flat_ops", "sa_grouping_config1", "chamfer_variants_config2",
+                             "config5_grid"],
                     help="single-GPU measurement of one BASELINE config (the default is the "
                          "headline line; the others print their own JSON line and are used "
                          "for the per-kernel profiles)")
@@ -567,6 +568,34 @@ def _sm_max_mhz() -> float:
         return 1965.0
 
 
+def config5_grid(queries: int, steps: int, warmup: int) -> dict:
+    """BASELINE config 5 through the grid-accelerated SpatialIndex (exact,
+    same results as the scan; a different amount of work, reported on its
+    own): build time, kNN k=16 and ball query r=0.3 K=32 for `queries`
+    queries against the 2^20-point clustered cloud."""
+    from mps_pointops.spatial import SpatialIndex
+    ref = _config5_cloud(6, 1 << 20)[0].contiguous().cuda()
+    q = _config5_cloud(7, 1 << 20)[0, :queries].contiguous().cuda()
+    build = []
+    for _ in range(max(steps, 1) + 1):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        index = SpatialIndex(ref, backend="grid")
+        index._get_grid()
+        torch.cuda.synchronize()
+        build.append((time.perf_counter() - t0) * 1e3)
+    grid = index._get_grid()
+    knn_ms = _event_ms(lambda: index.knn(q, 16), max(steps, 1), max(warmup, 1), None)
+    bq_ms = _event_ms(lambda: index.ball_query(q, 0.3, 32), max(steps, 1), max(warmup, 1), None)
+    return {"workload": "config5_grid", "queries": queries, "refs": 1 << 20,
+            "grid": {"dims": list(grid.dims), "cell_size": grid.h, "n_extra": grid.n_extra},
+            "build_ms_host_wall": statistics.median(build[1:]),
+            "knn_k16_ms": knn_ms, "knn_queries_per_s": queries / (knn_ms / 1e3),
+            "ball_query_r0.3_K32_ms": bq_ms, "ball_query_queries_per_s": queries / (bq_ms / 1e3),
+            "note": "exact: equal to the brute-force results; build includes the sampled "
+                    "8-NN cell-size estimate and one host read of the box"}
+
+
 def cpu_baseline_sample(max_seconds: float = 15.0) -> dict:
     """The oracle (C restatement of the reference's CPU Chamfer search,
     mps_pointops/chamfer.py:161-251) on the bench inputs, forward + backward,
@@ -743,6 +772,8 @@ def main():
             out = ssg_config1_ops(steps, max(warmup, 3))
         elif args.workload == "fps_config3":
             out = fps_config3(min(steps, 3), 1)
+        elif args.workload == "config5_grid":
+            out = config5_grid(args.queries, min(steps, 5), 1)
         elif args.workload == "chamfer_variants_config2":
             out = chamfer_variants_config2(min(steps, 10), max(warmup, 3))
         elif args.workload == "sa_grouping_config1":

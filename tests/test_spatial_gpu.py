@@ -124,3 +124,20 @@ def test_mutation_and_argument_checks(cuda_device):
         index.knn(pts[:3], 4)
     with pytest.raises(ValueError, match="k <= 32"):
         SpatialIndex(pts, backend="grid").knn(pts[:3], 33)
+
+
+def test_config5_scale_grid_equals_scan(cuda_device):
+    """BASELINE config 5 cloud (2^20 points, 64 Gaussian clusters): 16K
+    queries, kNN k=16 and ball query r=0.3 K=32, grid == scan."""
+    g = torch.Generator().manual_seed(6)
+    centres = torch.rand(64, 3, generator=torch.Generator().manual_seed(6)) * 20 - 10
+    labels = torch.randint(64, (1 << 20,), generator=g)
+    pts = (centres[labels] + 0.5 * torch.randn(1 << 20, 3, generator=g)).to(cuda_device)
+    q = clustered(16384, 9).to(cuda_device)
+    index = SpatialIndex(pts, backend="grid")
+    d, i = index.knn(q, 16)
+    wd, wi = scan_knn(pts, q, 16)
+    assert torch.equal(i, wi) and torch.equal(d, wd)
+    d, i = index.ball_query(q, 0.3, 32)
+    wd, wi = scan_bq(pts, q, 0.3, 32)
+    assert torch.equal(i, wi) and torch.equal(d, wd)
