@@ -10,6 +10,10 @@
  *     only enqueues work and returns; results are ready when the stream is.
  *   - Outputs and workspaces are owned by the caller.  Every output slot is
  *     written, padding included.  Nothing is allocated inside the library.
+ *     Workspaces must be 256-byte aligned (as cudaMalloc returns them;
+ *     MPO_ERR_INVALID_ARGUMENT otherwise).  Float arrays need only 4-byte
+ *     alignment: kernels use 16-byte vector loads on a caller's array only
+ *     when its base address allows them.
  *   - The return value is 0 (MPO_OK) or an MPO_ERR_* code; mpo_last_error()
  *     then holds a message (per calling thread).
  *   - Squared distances are ((d0*d0 + d1*d1) + d2*d2) for D == 3 and the
@@ -345,7 +349,8 @@ MPO_API int mpo_query_and_group_backward(const float* grad_out, const int32_t* i
  * float4 = x, y, z, original index bits), extra_points (device, room for N
  * float4: the points with a non-finite coordinate) and *n_extra_out (device
  * int32: their count).  Points outside the box are clamped into the edge
- * cells.  Workspace: mpo_grid_workspace_bytes(N, cells). */
+ * cells.  sorted_points and extra_points must be 16-byte aligned.
+ * Workspace: mpo_grid_workspace_bytes(N, cells). */
 MPO_API size_t mpo_grid_workspace_bytes(int64_t N, int64_t cells);
 MPO_API int mpo_grid_build(const float* points, int64_t N, const float* origin, float cell_size,
                            const int* dims, int* cell_start, float* sorted_points,

@@ -885,6 +885,7 @@ int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths
     using namespace mpo;
     int st = check_sizes(B, P, Q, D, "mpo_chamfer_nearest");
     if (st) return st;
+    MPO_REQUIRE_WORKSPACE(workspace);
     cudaStream_t s = (cudaStream_t)stream;
     if (B == 0) return kOk;
     unsigned long long *keys_x, *keys_y;
@@ -916,6 +917,7 @@ int mpo_chamfer_loss(const float* x, const float* y, const int64_t* x_lengths,
     using namespace mpo;
     int st = check_sizes(B, P, Q, D, "mpo_chamfer_loss");
     if (st) return st;
+    MPO_REQUIRE_WORKSPACE(workspace);
     MPO_REQUIRE(point_mode == 0 || point_mode == 1, "point_mode must be 0 (sum) or 1 (mean)");
     MPO_REQUIRE(batch_mode >= 0 && batch_mode <= 2, "batch_mode must be 0, 1 or 2");
     MPO_REQUIRE(loss, "null loss pointer");

@@ -222,9 +222,10 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
 
 // ---- 1. pack and norms --------------------------------------------------------
 // Thread per (row, 8-feature chunk) of the padded tiles; rows past n and
-// features past D are zero.
+// features past D are zero.  vec: rows are read as float4 (D % 4 == 0 and
+// 16-byte aligned bases).
 __global__ void fknn_pack_kernel(const float* __restrict__ p, int64_t B, int64_t n, int D, int Kpad,
-                                 int64_t tiles, unsigned char* __restrict__ out) {
+                                 int64_t tiles, int vec, unsigned char* __restrict__ out) {
     const int chunks = Kpad / 8;
     const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t rows = B * tiles * 128;
@@ -238,7 +239,7 @@ __global__ void fknn_pack_kernel(const float* __restrict__ p, int64_t B, int64_t
     float x[8];
     const bool live = i < n;
     const float* src = p + (b * n + i) * D + c * 8;
-    if (live && (D & 3) == 0 && c * 8 + 8 <= D) {
+    if (live && vec && c * 8 + 8 <= D) {
         const float4 u = reinterpret_cast<const float4*>(src)[0];
         const float4 v = reinterpret_cast<const float4*>(src)[1];
         x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
@@ -260,7 +261,7 @@ __global__ void fknn_pack_kernel(const float* __restrict__ p, int64_t B, int64_t
 // (+inf past N); nmax = largest finite reference norm per cloud (one atomic
 // per warp), bad = a norm that is not finite or above kHuge.
 __global__ void fknn_norms_kernel(const float* __restrict__ q, const float* __restrict__ r,
-                                  int64_t B, int64_t M, int64_t N, int64_t ntiles, int D,
+                                  int64_t B, int64_t M, int64_t N, int64_t ntiles, int D, int vec,
                                   float* __restrict__ nq, float* __restrict__ nr,
                                   unsigned* __restrict__ nmax, int* __restrict__ bad) {
     const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -278,7 +279,7 @@ __global__ void fknn_norms_kernel(const float* __restrict__ q, const float* __re
             nr[row] = INFINITY;
         } else {
             const float* p = is_q ? q + row * D : r + (b * N + i) * D;
-            if ((D & 3) == 0) {
+            if (vec) {
                 const float4* p4 = reinterpret_cast<const float4*>(p);
                 for (int t = 0; t < D / 4; ++t) {
                     const float4 v = p4[t];
@@ -581,18 +582,21 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
 }
 
 // ---- 3. exact re-rank --------------------------------------------------------
-// Warp per query.  Normal case: lane l takes candidates l and l + 32, computes
-// their exact sequential-fp32 SD (non-finite SD are dropped), and the rank of
-// each candidate in (SD, index) order over the whole list decides its output
-// slot.  Overflowed lists and flagged clouds: the lanes scan every reference
-// (j = lane mod 32) into per-lane sorted lists, merged by k rounds of warp
-// minimum.
-// Exact sequential SD of query row qs (shared memory) and reference row rp,
-// reading the reference 32 features at a time (8 float4 loads in flight per
-// lane when rows are 16-byte aligned).
+// Warp per query.  Normal case: the warp copies its candidates' reference rows
+// into shared memory (coalesced row copies with cp.async; a lane per row would
+// touch one cache line per lane and load), lane l computes the exact
+// sequential-fp32 SD of candidates l and l + 32 from there (non-finite SD are
+// dropped), and a warp bitonic sort of the (SD, index) keys gives the first k.
+// Overflowed lists and flagged clouds: the
+// lanes scan every reference (j = lane mod 32) into per-lane sorted lists,
+// merged by k rounds of warp minimum.
+
+// Exact sequential SD of query row qs (shared memory) and reference row rp
+// (global memory), reading the reference 32 features at a time (8 float4
+// loads in flight per lane when rows are 16-byte aligned, vec != 0).
 __device__ __forceinline__ float sqd_staged(const float* __restrict__ qs,
-                                            const float* __restrict__ rp, int D) {
-    if ((D & 3) != 0) return sqd_seq(qs, rp, D);
+                                            const float* __restrict__ rp, int D, int vec) {
+    if (!vec) return sqd_seq(qs, rp, D);
     const float4* r4 = reinterpret_cast<const float4*>(rp);
     float s = 0.f;
     for (int t0 = 0; t0 < D; t0 += 32) {
@@ -618,21 +622,96 @@ __device__ __forceinline__ float sqd_staged(const float* __restrict__ qs,
     return s;
 }
 
-__global__ void __launch_bounds__(256)
-fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t B, int64_t M,
-                   int64_t N, int D, int k, const int* __restrict__ bad,
+// Exact sequential SD of two shared-memory rows, both 16-byte aligned with
+// D % 4 == 0 (fully unrolled when D is a compile-time DC).
+template <int DC>
+__device__ __forceinline__ float sqd_smem4(const float* __restrict__ a,
+                                           const float* __restrict__ b, int D) {
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+    float4 x = a4[0], y = b4[0];
+    float d = __fsub_rn(x.x, y.x);
+    float s = __fmul_rn(d, d);
+    d = __fsub_rn(x.y, y.y);
+    s = __fadd_rn(s, __fmul_rn(d, d));
+    d = __fsub_rn(x.z, y.z);
+    s = __fadd_rn(s, __fmul_rn(d, d));
+    d = __fsub_rn(x.w, y.w);
+    s = __fadd_rn(s, __fmul_rn(d, d));
+#pragma unroll(DC ? DC / 4 : 4)
+    for (int u = 1; u < D / 4; ++u) {
+        x = a4[u];
+        y = b4[u];
+        d = __fsub_rn(x.x, y.x);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+        d = __fsub_rn(x.y, y.y);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+        d = __fsub_rn(x.z, y.z);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+        d = __fsub_rn(x.w, y.w);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+    }
+    return s;
+}
+
+// Row stride (floats) of the re-rank's staged rows: with 16-byte rows the
+// stride is an odd number of float4s, otherwise an odd number of floats, so
+// that 32 lanes reading the same column of 32 rows hit distinct banks.
+__host__ __device__ constexpr int rerank_stride(int D, int vec) {
+    return vec ? 4 * (((D / 4) & 1) ? D / 4 : D / 4 + 1) : ((D & 1) ? D : D + 1);
+}
+constexpr int kRerankWarps = 8;
+// Shared memory of one re-rank CTA: per warp the query row and 32 staged rows.
+inline size_t rerank_smem_bytes(int D, int vec) {
+    return (size_t)kRerankWarps * 33 * rerank_stride(D, vec) * sizeof(float);
+}
+
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// One compare-exchange stage of a warp bitonic sort over 64-bit keys: the
+// element with position e (its lane, or 32 + lane for a second half) keeps
+// the smaller key of its pair when its block of `size` sorts ascending and it
+// is the lower element of the pair, or neither.
+__device__ __forceinline__ uint64_t bitonic_step(uint64_t key, int e, int size, int stride) {
+    const uint64_t other = __shfl_xor_sync(FULL_MASK, key, stride);
+    const bool keep_min = ((e & size) == 0) == ((e & stride) == 0);
+    const uint64_t lo = other < key ? other : key, hi = other < key ? key : other;
+    return keep_min ? lo : hi;
+}
+
+// VEC: 16-byte rows; DC: the feature width when fixed at compile time (0:
+// D at run time).  Grid (ceil(M / warps), B).
+template <int VEC, int DC>
+__global__ void __launch_bounds__(kRerankWarps * 32)
+fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t M,
+                   int64_t N, int D_rt, int k, const int* __restrict__ bad,
                    const unsigned* __restrict__ counts, const uint2* __restrict__ cand,
                    float* __restrict__ dist, int64_t* __restrict__ idx64,
                    float* __restrict__ sqdist, unsigned* __restrict__ nover,
                    int64_t* __restrict__ over_rows) {
     static_assert(kCap == 64, "two candidates per lane");
-    extern __shared__ float s_q[];  // [warps][D]
+    static_assert(DC == 0 || (VEC && DC % 4 == 0), "fixed widths use 16-byte rows");
+    extern __shared__ __align__(16) float s_stage[];  // [warps][33][stride]
+    const int D = DC ? DC : D_rt;
     const int lane = threadIdx.x & 31;
-    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (row >= B * M) return;  // warp-uniform
-    const int64_t b = row / M;
+    const int64_t m = (int64_t)blockIdx.x * kRerankWarps + (threadIdx.x >> 5);
+    if (m >= M) return;  // warp-uniform
+    const int64_t b = blockIdx.y;
+    const int64_t row = b * M + m;
     const float* rb = r + b * N * D;
-    float* qp = s_q + (threadIdx.x >> 5) * D;
+    const int stride = rerank_stride(D, VEC);
+    float* qp = s_stage + (threadIdx.x >> 5) * 33 * stride;
+    float* rows = qp + stride;
     const unsigned packed = bad[b] ? 0xffffffffu : counts[row];
     const int64_t o = row * k;
     if (packed == 0xffffffffu) {  // exact scan by fknn_exact_rows_kernel
@@ -643,80 +722,90 @@ fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int
     // the odd tiles.
     const unsigned f0 = packed & 0xffffu, f1 = packed >> 16, cnt = f0 + f1;
     for (int t = lane; t < D; t += 32) qp[t] = q[row * D + t];
-    __syncwarp();
-    // Lane l: candidates l and l + 32 (exact SD; non-finite -> (inf, none)).
+    // Copy units (float4 or float) per row; a copy instruction covers R rows
+    // when a row has at most 32 units, lane l taking unit l % U of row l / U.
+    const int U = VEC ? D / 4 : D;
+    const int R = U <= 32 ? 32 / U : 1;
+    const int roff = U <= 32 ? lane / U : 0;
+    const int u0 = U <= 32 ? lane % U : lane;
+    const bool copier = U > 32 || lane < R * U;
     float sd[2];
     uint32_t jj[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-        const unsigned c = (unsigned)(lane + 32 * h);
         sd[h] = INFINITY;
         jj[h] = kNoIndex;
+        const unsigned c0 = 32u * (unsigned)h;
+        if (c0 >= cnt) continue;  // warp-uniform
+        const unsigned n = min(32u, cnt - c0);
+        const unsigned c = c0 + (unsigned)lane;
+        uint32_t j = kNoIndex;
         if (c < cnt) {
             const unsigned slot = c < f0 ? c : (unsigned)kCap - 1u - (c - f0);
-            const uint32_t j = cand[row * kCap + slot].x;
-            const float v = sqd_staged(qp, rb + (int64_t)j * D, D);
+            j = cand[row * kCap + slot].x;
+        }
+        for (unsigned base = 0; base < n; base += (unsigned)R) {
+            const unsigned rl = base + (unsigned)roff;
+            const uint32_t jr = __shfl_sync(FULL_MASK, j, (int)(rl & 31u));
+            if (copier && rl < n && jr < (uint32_t)N) {
+                const float* src = rb + (int64_t)jr * D;
+                float* dst = rows + rl * stride;
+                for (int u = u0; u < U; u += 32) {
+                    if (VEC)
+                        cp_async16(dst + 4 * u, src + 4 * u);
+                    else
+                        cp_async4(dst + u, src + u);
+                }
+            }
+        }
+        cp_async_wait_all();
+        __syncwarp();
+        if (c < cnt && j < (uint32_t)N) {
+            const float* rp = rows + lane * stride;
+            const float v = VEC ? sqd_smem4<DC>(qp, rp, D) : sqd_seq(qp, rp, D);
             if (isfinite(v)) {
                 sd[h] = v;
                 jj[h] = j;
             }
         }
+        __syncwarp();  // the rows are refilled for the second half
     }
-    if (cnt <= 32u) {
-        // Bitonic sort of the 32 (SD, index) pairs across the warp.
-        float d = sd[0];
-        uint32_t j = jj[0];
+    // Sort the (SD, index) pairs as 64-bit keys (finite SD >= 0: the bits
+    // order like the values; an empty slot is (inf, kNoIndex), after all):
+    // a warp bitonic sort of 32 keys, or of 64 keys (two per lane, element
+    // 32 h + lane) when the list has more than 32 candidates.
+    uint64_t a0 = ((uint64_t)__float_as_uint(sd[0]) << 32) | jj[0];
+    if (cnt > 32u) {
+        uint64_t a1 = ((uint64_t)__float_as_uint(sd[1]) << 32) | jj[1];
+#pragma unroll
+        for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                if (stride == 32) {
+                    const uint64_t lo = a1 < a0 ? a1 : a0, hi = a1 < a0 ? a0 : a1;
+                    a0 = lo;
+                    a1 = hi;
+                } else {
+                    a0 = bitonic_step(a0, lane, size, stride);
+                    a1 = bitonic_step(a1, 32 + lane, size, stride);
+                }
+            }
+        }
+    } else {
 #pragma unroll
         for (int size = 2; size <= 32; size <<= 1) {
 #pragma unroll
-            for (int stride = size >> 1; stride > 0; stride >>= 1) {
-                const float od = __shfl_xor_sync(FULL_MASK, d, stride);
-                const uint32_t oj = __shfl_xor_sync(FULL_MASK, j, stride);
-                const bool ascending = (lane & size) == 0 || size == 32;
-                const bool lower = (lane & stride) == 0;
-                const bool other_first = od < d || (od == d && oj < j);
-                const bool take = (lower == ascending) ? other_first : !other_first;
-                d = take ? od : d;
-                j = take ? oj : j;
-            }
-        }
-        if (lane < k) {
-            const bool filled = j != kNoIndex;
-            dist[o + lane] = filled ? sqrtf(d) : INFINITY;
-            if (sqdist) sqdist[o + lane] = filled ? d : INFINITY;
-            idx64[o + lane] = filled ? (int64_t)j : -1;
-        }
-        return;
-    }
-    // 33..64 candidates: rank of each pair in (SD, index) order.
-    bool ok[2] = {jj[0] != kNoIndex, jj[1] != kNoIndex};
-    int rank[2] = {0, 0};
-#pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-        const unsigned live = __ballot_sync(FULL_MASK, ok[h2]);
-        for (unsigned m = live; m; m &= m - 1) {
-            const int src = __ffs(m) - 1;
-            const float e = __shfl_sync(FULL_MASK, sd[h2], src);
-            const uint32_t ej = __shfl_sync(FULL_MASK, jj[h2], src);
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-                rank[h] += (ok[h] && before<kDropNonFinite>(e, ej, sd[h], jj[h])) ? 1 : 0;
+            for (int stride = size >> 1; stride > 0; stride >>= 1)
+                a0 = bitonic_step(a0, lane, size, stride);
         }
     }
-    const int total = __popc(__ballot_sync(FULL_MASK, ok[0])) +
-                      __popc(__ballot_sync(FULL_MASK, ok[1]));
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        if (ok[h] && rank[h] < k) {
-            dist[o + rank[h]] = sqrtf(sd[h]);
-            if (sqdist) sqdist[o + rank[h]] = sd[h];
-            idx64[o + rank[h]] = (int64_t)jj[h];
-        }
-    }
-    for (int t = total + lane; t < k; t += 32) {
-        dist[o + t] = INFINITY;
-        if (sqdist) sqdist[o + t] = INFINITY;
-        idx64[o + t] = -1;
+    if (lane < k) {
+        const uint32_t j = (uint32_t)a0;
+        const float d = __uint_as_float((uint32_t)(a0 >> 32));
+        const bool filled = j != kNoIndex;
+        dist[o + lane] = filled ? sqrtf(d) : INFINITY;
+        if (sqdist) sqdist[o + lane] = filled ? d : INFINITY;
+        idx64[o + lane] = filled ? (int64_t)j : -1;
     }
 }
 
@@ -726,7 +815,8 @@ fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int
 template <int KCAP>
 __global__ void __launch_bounds__(256)
 fknn_exact_rows_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t B,
-                       int64_t M, int64_t N, int D, int k, const unsigned* __restrict__ nover,
+                       int64_t M, int64_t N, int D, int vec, int k,
+                       const unsigned* __restrict__ nover,
                        const int64_t* __restrict__ over_rows, float* __restrict__ dist,
                        int64_t* __restrict__ idx64, float* __restrict__ sqdist) {
     extern __shared__ float s_q[];  // [8 warps][D]
@@ -744,7 +834,8 @@ fknn_exact_rows_kernel(const float* __restrict__ q, const float* __restrict__ r,
     const int64_t o = row * k;
     TopK<KCAP, kDropNonFinite> top;
     top.init(k);
-    for (int64_t j = lane; j < N; j += 32) top.offer(sqd_staged(qp, rb + j * D, D), (uint32_t)j);
+    for (int64_t j = lane; j < N; j += 32)
+        top.offer(sqd_staged(qp, rb + j * D, D, vec), (uint32_t)j);
     int used = 0;  // entries of this lane's list already emitted
     for (int t = 0; t < k; ++t) {
         float hd = INFINITY;
@@ -836,16 +927,18 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
     const int Kpad = kpad_of(D);
     const int64_t mt = ceil_div(M, kRows) * kQT, nt = ceil_div(N, kTN);
     const int64_t qchunks = B * mt * 128 * (Kpad / 8), rchunks = B * nt * 128 * (Kpad / 8);
+    // 16-byte row loads only when every row starts on a 16-byte boundary.
+    const int vec = (D % 4 == 0 && aligned_to(query, 16) && aligned_to(ref, 16)) ? 1 : 0;
     fknn_pack_kernel<<<(unsigned)ceil_div(qchunks, 256), 256, 0, s>>>(query, B, M, D, Kpad, mt,
-                                                                      w.qpack);
+                                                                      vec, w.qpack);
     int st = check_launch("fknn_pack_kernel");
     if (st) return st;
     fknn_pack_kernel<<<(unsigned)ceil_div(rchunks, 256), 256, 0, s>>>(ref, B, N, D, Kpad, nt,
-                                                                      w.rpack);
+                                                                      vec, w.rpack);
     st = check_launch("fknn_pack_kernel");
     if (st) return st;
     fknn_norms_kernel<<<(unsigned)ceil_div(B * (M + nt * kTN), 256), 256, 0, s>>>(
-        query, ref, B, M, N, nt, D, w.nq, w.nr, w.nmax, w.bad);
+        query, ref, B, M, N, nt, D, vec, w.nq, w.nr, w.nmax, w.bad);
     st = check_launch("fknn_norms_kernel");
     if (st) return st;
     const TcSmem L(Kpad);
@@ -865,15 +958,20 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
                                          w.bad, w.ubound, w.counts, w.cand, w.status);
     st = check_launch("fknn_tc_kernel<2>");
     if (st) return st;
-    const size_t rsmem = (size_t)8 * D * sizeof(float);
-    const unsigned rgrid = (unsigned)ceil_div(B * M * 32, 256);
-    fknn_rerank_kernel<<<rgrid, 256, rsmem, s>>>(
-        query, ref, B, M, N, D, k, w.bad, w.counts, w.cand, dist, idx, sqdist, w.nover,
-        w.over_rows);
+    auto rk = !vec ? fknn_rerank_kernel<0, 0>
+                   : (D == 64 ? fknn_rerank_kernel<1, 64> : fknn_rerank_kernel<1, 0>);
+    const size_t stage = rerank_smem_bytes(D, vec);
+    if (cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stage) !=
+        cudaSuccess)
+        return fail(kCudaError, "knn: cannot raise the shared-memory limit");
+    const dim3 rgrid((unsigned)ceil_div(M, kRerankWarps), (unsigned)B);
+    rk<<<rgrid, kRerankWarps * 32, stage, s>>>(query, ref, M, N, D, k, w.bad, w.counts, w.cand,
+                                               dist, idx, sqdist, w.nover, w.over_rows);
     st = check_launch("fknn_rerank_kernel");
     if (st) return st;
+    const size_t rsmem = (size_t)8 * D * sizeof(float);
     fknn_exact_rows_kernel<KCAP><<<(unsigned)(2 * sm_count()), 256, rsmem, s>>>(
-        query, ref, B, M, N, D, k, w.nover, w.over_rows, dist, idx, sqdist);
+        query, ref, B, M, N, D, vec, k, w.nover, w.over_rows, dist, idx, sqdist);
     return check_launch("fknn_exact_rows_kernel");
 }
 

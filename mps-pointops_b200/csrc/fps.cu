@@ -476,6 +476,7 @@ int mpo_fps_gather(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64
                    int skip_near_origin, int out_int32, int strategy, void* out, float* out_xyz,
                    int32_t* status_out, void* workspace, size_t workspace_bytes, void* stream) {
     using namespace mpo;
+    MPO_REQUIRE_WORKSPACE(workspace);
     cudaStream_t s = (cudaStream_t)stream;
     bool done = false;
     int st = check_fps_args(xyz, B, N, npoint, start_idx, strategy, out, status_out, s, "mpo_fps",
@@ -515,6 +516,7 @@ int mpo_flat_fps(const float* x, const int64_t* ptr, const int64_t* out_ptr,
     MPO_REQUIRE(segments >= 0 && total_n >= 0 && total_out >= 0 && max_len >= 0,
                 "negative size");
     MPO_REQUIRE(status != nullptr, "status must not be null");
+    MPO_REQUIRE_WORKSPACE(workspace);
     cudaStream_t s = (cudaStream_t)stream;
     if (cudaMemsetAsync(status, 0, sizeof(int32_t), s) != cudaSuccess)
         return fail(kCudaError, "mpo_flat_fps: status reset failed");

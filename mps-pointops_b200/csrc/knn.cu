@@ -839,6 +839,7 @@ int mpo_knn(const float* query, const float* ref, int64_t B, int64_t M, int64_t 
     MPO_REQUIRE(N < (int64_t)0x7fffffff && M < (int64_t)0x7fffffff, "M and N must be below 2**31");
     if (B == 0 || M == 0 || k == 0) return kOk;
     MPO_REQUIRE(query && ref && dist && idx, "null pointer");
+    MPO_REQUIRE_WORKSPACE(workspace);
     cudaStream_t s = (cudaStream_t)stream;
     if (fknn_tc_eligible(M, N, D, k))
         return fknn_tc_run(query, ref, B, M, N, D, k, dist, idx, sqdist, workspace,

@@ -55,6 +55,17 @@ int flat_offsets_check(const int64_t* ptr_q, const int64_t* ptr_r, int64_t segs,
                                         std::string(__func__) + ": " + (msg)); \
     } while (0)
 
+// Address alignment of a caller's buffer.  Kernels read a float array with
+// 16-byte vector loads only when its base is 16-byte aligned (a contiguous
+// tensor view can start at any 4-byte offset); workspaces must be 256-byte
+// aligned, as cudaMalloc and the torch allocator return them, because the
+// kernels place 64-bit atomics and bulk-copy sources at fixed offsets in them.
+inline bool aligned_to(const void* p, uintptr_t bytes) {
+    return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0;
+}
+#define MPO_REQUIRE_WORKSPACE(ws) \
+    MPO_REQUIRE((ws) == nullptr || ::mpo::aligned_to((ws), 256), "workspace must be 256-byte aligned")
+
 // ------------------------------------------------------------------ math
 __device__ __forceinline__ float sqd3(float ax, float ay, float az, float bx, float by,
                                       float bz) {

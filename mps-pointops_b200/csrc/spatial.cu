@@ -486,6 +486,9 @@ int mpo_grid_build(const float* points, int64_t N, const float* origin, float ce
         return fail(kWorkspaceTooSmall, "mpo_grid_build: workspace must hold " +
                                             std::to_string(need) + " bytes");
     MPO_REQUIRE((points && sorted_points && extra_points) || N == 0, "null pointer");
+    MPO_REQUIRE_WORKSPACE(workspace);
+    MPO_REQUIRE(aligned_to(sorted_points, 16) && aligned_to(extra_points, 16),
+                "sorted_points and extra_points must be 16-byte aligned");
     cudaStream_t s = (cudaStream_t)stream;
     int* cell_of = static_cast<int*>(workspace);
     int* counts = cell_of + N;
@@ -534,6 +537,8 @@ int mpo_grid_knn(const float* query, int64_t Q, const float* origin, float cell_
     MPO_REQUIRE(n_extra >= 0, "negative extra count");
     if (Q == 0 || k == 0) return kOk;
     MPO_REQUIRE(query && origin && dims && cell_start && dist && idx, "null pointer");
+    MPO_REQUIRE(aligned_to(sorted_points, 16) && aligned_to(extra_points, 16),
+                "sorted_points and extra_points must be 16-byte aligned");
     const Grid g = make_grid(origin, cell_size, dims, cell_start,
                              reinterpret_cast<const float4*>(sorted_points),
                              reinterpret_cast<const float4*>(extra_points), n_extra);
@@ -550,6 +555,7 @@ int mpo_grid_ball_query(const float* query, int64_t Q, const float* origin, floa
     MPO_REQUIRE(Q >= 0 && K >= 0 && K <= 32, "K must be in [0, 32]");
     if (Q == 0 || K == 0) return kOk;
     MPO_REQUIRE(query && origin && dims && cell_start && dist2 && idx, "null pointer");
+    MPO_REQUIRE(aligned_to(sorted_points, 16), "sorted_points must be 16-byte aligned");
     MPO_REQUIRE(radius >= 0.f, "radius must be non-negative");
     const Grid g = make_grid(origin, cell_size, dims, cell_start,
                              reinterpret_cast<const float4*>(sorted_points), nullptr, 0);

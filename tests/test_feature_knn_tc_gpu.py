@@ -6,6 +6,8 @@ exact kernels': indices, squared distances and IEEE sqrt distances."""
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -115,3 +117,38 @@ def test_sqdist_output(cuda_device):
     st = lib.mpo_knn(N.ptr(qc), N.ptr(rc), B, M, Nn, D, k, N.ptr(dist), N.ptr(idx), None,
                      N.ptr(ws), ws_bytes - 1, N.stream(cuda_device))
     assert st == 4 and "workspace" in N.last_error()
+
+
+@pytest.mark.parametrize("d", [32, 64])
+def test_unaligned_rows(cuda_device, d):
+    # Contiguous views whose base sits 4 bytes past a 16-byte boundary: the
+    # kernels must use scalar row loads (vector loads would be misaligned).
+    q = feats(2, 300, d, seed=20)
+    r = feats(2, 2500, d, seed=21)
+    qb = torch.zeros(q.numel() + 1, device=cuda_device)
+    rb = torch.zeros(r.numel() + 3, device=cuda_device)
+    qv = qb[1:].view(q.shape)
+    rv = rb[3:].view(r.shape)
+    qv.copy_(q.to(cuda_device))
+    rv.copy_(r.to(cuda_device))
+    assert qv.is_contiguous() and qv.data_ptr() % 16 == 4 and rv.data_ptr() % 16 == 12
+    want_d, want_i = O.knn(q.numpy(), r.numpy(), 20)
+    dd, ii = mps_pointops.knn(qv, rv, 20)
+    np.testing.assert_array_equal(ii.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(dd.cpu().numpy(), want_d)
+
+
+def test_unaligned_workspace_is_rejected(cuda_device):
+    q, r = feats(1, 64, 64, seed=22), feats(1, 2048, 64, seed=23)
+    k = 8
+    B, M, D = q.shape
+    Nn = r.shape[1]
+    dist = torch.empty(B, M, k, device=cuda_device)
+    idx = torch.empty(B, M, k, dtype=torch.long, device=cuda_device)
+    qc, rc = q.to(cuda_device), r.to(cuda_device)
+    lib = N.lib()
+    ws_bytes = int(lib.mpo_knn_workspace_bytes(B, M, Nn, D, k))
+    ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=cuda_device)
+    st = lib.mpo_knn(N.ptr(qc), N.ptr(rc), B, M, Nn, D, k, N.ptr(dist), N.ptr(idx), None,
+                     ctypes.c_void_p(ws.data_ptr() + 16), ws_bytes, N.stream(cuda_device))
+    assert st == 1 and "256-byte aligned" in N.last_error()
