@@ -15,8 +15,9 @@ importable (the real package) is left alone unless ``force=True``.  The
 ``torch_cluster`` stand-in serves ``fps``, ``knn``, ``radius``, ``knn_graph``
 and ``radius_graph`` from :mod:`mps_pointops.flat`; the reference's clustering
 and random-walk entries (``grid_cluster``, ``graclus_cluster``,
-``random_walk``, ``nearest``) and its Pointcept ``pointops`` shim are not part
-of this build, and ``pointcept=True`` raises ``NotImplementedError``.
+``random_walk``, ``nearest``) are not part of this build.  ``pointcept=True``
+also registers the Pointcept v1.2.1 ``pointops`` subset of
+:mod:`mps_pointops.pointcept` (compat.py:161-171).
 
 The pointnet2_ops FPS and ball query run as fused kernels here: FPS writes its
 int32 indices directly, and the ball query applies pointnet2's first-hit
@@ -35,6 +36,7 @@ from torch import Tensor
 
 from . import _native as N
 from . import flat, grouping, ops
+from . import pointcept as pointcept_ops
 from ._ball_query_cuda import _checked_radius_and_k
 
 
@@ -130,8 +132,6 @@ def _module(name: str, **attrs) -> types.ModuleType:
 
 def install(force: bool = False, *, pointcept: bool = False) -> list[str]:
     """Register the stand-ins in ``sys.modules``; returns the names added."""
-    if pointcept:
-        raise NotImplementedError("the Pointcept pointops shim is not part of the B200 build")
     pointnet2_utils = _module(
         "pointnet2_ops.pointnet2_utils",
         furthest_point_sample=furthest_point_sample,
@@ -158,6 +158,17 @@ def install(force: bool = False, *, pointcept: bool = False) -> list[str]:
             )
         },
     }
+    if pointcept:
+        packages["pointops"] = {
+            "pointops": _module(
+                "pointops",
+                farthest_point_sampling=pointcept_ops.farthest_point_sampling,
+                knn_query=pointcept_ops.knn_query,
+                grouping=pointcept_ops.grouping,
+                knn_query_and_group=pointcept_ops.knn_query_and_group,
+                interpolation=pointcept_ops.interpolation,
+            ),
+        }
     installed = []
     for top, modules in packages.items():
         if not force and (top in sys.modules or importlib.util.find_spec(top) is not None):

@@ -404,6 +404,41 @@ def flat_fps(x, ptr, counts, starts) -> np.ndarray:
     return np.concatenate(outs) if outs else np.empty(0, dtype=np.int64)
 
 
+def pointcept_fps(xyz, offset, new_offset) -> np.ndarray:
+    """mps_pointops/pointcept.py:77-98: per batch (cumulative ends `offset`,
+    sample ends `new_offset`), FPS from the batch's first point
+    (reference.py:27-58), as global int32 rows."""
+    ptr = [0, *[int(v) for v in offset]]
+    tgt = [0, *[int(v) for v in new_offset]]
+    counts = [b - a for a, b in zip(tgt, tgt[1:])]
+    return flat_fps(xyz, ptr, counts, [0] * len(counts)).astype(np.int32)
+
+
+def pointcept_knn(nsample: int, xyz, offset, new_xyz=None, new_offset=None):
+    """mps_pointops/pointcept.py:101-165: per query, the nsample nearest rows
+    of its batch in ascending (SD, index) order; a slot is kept only when the
+    SD recomputed from the selected rows, ((dx*dx + dy*dy) + dz*dz), is
+    finite and below 1e10, otherwise it holds (-1, 1e5).  Returns (int32
+    global indices, float32 Euclidean distances)."""
+    xyz = _f32(xyz)
+    if new_xyz is None:
+        new_xyz, new_offset = xyz, offset
+    new_xyz = _f32(new_xyz)
+    ptr_x = np.array([0, *[int(v) for v in offset]], dtype=np.int64)
+    ptr_y = np.array([0, *[int(v) for v in new_offset]], dtype=np.int64)
+    idx = flat_knn_indices(xyz, new_xyz, ptr_x, ptr_y, nsample)
+    sel = idx >= 0
+    rows = xyz[np.where(sel, idx, 0)] if len(xyz) else np.zeros(idx.shape + (3,), np.float32)
+    delta = new_xyz[:, None, :] - rows
+    with np.errstate(invalid="ignore", over="ignore"):
+        sq = delta[..., 0] * delta[..., 0]
+        sq = sq + delta[..., 1] * delta[..., 1]
+        sq = sq + delta[..., 2] * delta[..., 2]
+        valid = sel & (sq < np.float32(1e10))
+        dist = np.where(valid, np.sqrt(sq), np.float32(1e5)).astype(np.float32)
+    return np.where(valid, idx, -1).astype(np.int32), dist
+
+
 def flat_edges(indices: np.ndarray) -> np.ndarray:
     """mps_pointops/flat.py:247-253: padded rows -> [query, reference] edges."""
     q, s = np.nonzero(indices >= 0)

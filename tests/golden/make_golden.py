@@ -482,16 +482,70 @@ def grouping_cases():
     save("grouping", **out)
 
 
+# ------------------------------------------------------------------ Pointcept
+def pointcept_cases():
+    """mps_pointops/pointcept.py on CPU (the reference's own path): FPS with
+    cumulative offsets (:77-98), padded kNN with the 1e10 ceiling (:101-165),
+    grouping with relative xyz and its gradients (:168-203), and
+    interpolation with its feature gradient (:219-243)."""
+    from mps_pointops import pointcept as ref_pc
+    out = {}
+    g = torch.Generator().manual_seed(77)
+    lx = [0, 5, 40, 300, 1, 128, 64]
+    ly = [3, 2, 17, 90, 0, 128, 5]
+    ends = lambda ls: torch.tensor(np.cumsum(ls), dtype=torch.int64)  # noqa: E731
+    x = torch.randn(sum(lx), 3, generator=g)
+    y = torch.randn(sum(ly), 3, generator=g)
+    x[50, 1] = float("nan")               # cloud 2: a NaN reference
+    x[60, 0] = float("inf")               # cloud 3: an inf reference
+    x[100] = torch.tensor([1.0e5, 0.0, 0.0])  # cloud 3: beyond the 1e10 ceiling
+    y[25] = torch.tensor([-1.0e5, 0.0, 0.0])  # cloud 3: a query far from all
+    out["x"], out["y"] = x, y
+    out["offset"], out["new_offset"] = ends(lx), ends(ly)
+    for k in (1, 3, 16, 50):
+        idx, dist = ref_pc.knn_query(k, x, ends(lx), y, ends(ly))
+        out[f"knn_k{k}/idx"], out[f"knn_k{k}/dist"] = idx, dist
+    # Self query (new_xyz omitted) and exact ties on a lattice.
+    xt = torch.randint(0, 4, (sum(lx), 3), generator=g).float()
+    out["ties/x"] = xt
+    out["ties/idx"], out["ties/dist"] = ref_pc.knn_query(12, xt, ends(lx))
+    # FPS: counts per batch at most the batch size, some zero.
+    xf = torch.randn(sum(lx), 3, generator=g)
+    counts = [0, 5, 13, 200, 1, 64, 0]
+    out["fps/x"], out["fps/new_offset"] = xf, ends(counts)
+    out["fps/idx"] = ref_pc.farthest_point_sampling(xf, ends(lx), ends(counts))
+    # Interpolation and grouping, forward and backward.
+    feat = torch.randn(sum(lx), 6, generator=g)
+    f1 = feat.clone().requires_grad_()
+    interp = ref_pc.interpolation(xf, y, f1, ends(lx), ends(ly), k=3)
+    gi = torch.randn(interp.shape, generator=g)
+    interp.backward(gi)
+    out["interp/feat"], out["interp/out"] = feat, interp
+    out["interp/grad_out"], out["interp/grad_feat"] = gi, f1.grad
+    idx, _ = ref_pc.knn_query(8, xf, ends(lx), y, ends(ly))
+    xr = xf.clone().requires_grad_()
+    qr = y.clone().requires_grad_()
+    f2 = feat.clone().requires_grad_()
+    grouped = ref_pc.grouping(idx, f2, xr, qr, with_xyz=True)
+    gg = torch.randn(grouped.shape, generator=g)
+    grouped.backward(gg)
+    out["group/idx"], out["group/out"], out["group/grad_out"] = idx, grouped, gg
+    out["group/grad_xyz"], out["group/grad_new_xyz"] = xr.grad, qr.grad
+    out["group/grad_feat"] = f2.grad
+    save("pointcept", **out)
+
+
+CASES = {
+    "fps": fps_cases, "knn": knn_cases, "feature_knn": feature_knn_cases,
+    "ball_query": ball_query_cases, "pointnet2": pointnet2_cases, "chamfer": chamfer_cases,
+    "flat": flat_cases, "grouping": grouping_cases, "chamfer_l1": chamfer_l1_cases,
+    "pointcept": pointcept_cases,
+}
+
 if __name__ == "__main__":
+    # python make_golden.py [case ...]   (default: every case)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    fps_cases()
-    knn_cases()
-    feature_knn_cases()
-    ball_query_cases()
-    pointnet2_cases()
-    chamfer_cases()
-    flat_cases()
-    grouping_cases()
-    chamfer_l1_cases()
+    for name in sys.argv[1:] or list(CASES):
+        CASES[name]()
     for f in sorted(OUT.glob("*.npz")):
         print(f"{f.name}: {f.stat().st_size / 1024:.0f} KiB")
