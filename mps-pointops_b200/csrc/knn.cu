@@ -264,31 +264,44 @@ knn3p_kernel(const float* __restrict__ query, const float* __restrict__ ref, Lay
         const int buf = (int)(t & 1);
         if (t + 1 < ntiles) load_tile(t + 1);
         if (active) {
-            const float4* xy = txy + buf * (kTile / 2) + split * (slice / 2);
-            const float4* zz = tz + buf * (kTile / 4) + split * (slice / 4);
+            const ulonglong2* xy =
+                reinterpret_cast<const ulonglong2*>(txy + buf * (kTile / 2) + split * (slice / 2));
+            const ulonglong2* zz =
+                reinterpret_cast<const ulonglong2*>(tz + buf * (kTile / 4) + split * (slice / 4));
             const int64_t j0 = t * kTile + split * slice;
             const int cnt = (int)max64(0, min64(slice, N - j0));
-            // Eight points per iteration; the common case (no candidate below
-            // the threshold) costs one min per pair and a compare per four.
-            for (int e = 0; e < cnt; e += 8) {
+            // Eight points per step: the common case (no candidate below the
+            // threshold) costs six loads, the packed distances, one min per
+            // point and one compare-and-branch.  Full steps run without
+            // bounds checks and with running shared-memory pointers: once the
+            // distances are packed, the integer and branch work per point is
+            // what bounds this loop.  The queue gains at most 8 entries per
+            // step and is drained above kQueue - 8.
+            // a, z: shared-window byte addresses of the step's four point
+            // pairs and its eight z values.
+            auto step = [&](uint32_t a, uint32_t z, int e, int valid) {
+                f32x2 ax0, ay0, ax1, ay1, ax2, ay2, ax3, ay3, z01, z23, z45, z67;
+                lds_pairs<0>(a, ax0, ay0);
+                lds_pairs<16>(a, ax1, ay1);
+                lds_pairs<32>(a, ax2, ay2);
+                lds_pairs<48>(a, ax3, ay3);
+                lds_pairs<0>(z, z01, z23);
+                lds_pairs<16>(z, z45, z67);
+                float d[8];
+                unpack2(sqd3x2(X, Y, Z, ax0, ay0, z01), d[0], d[1]);
+                unpack2(sqd3x2(X, Y, Z, ax1, ay1, z23), d[2], d[3]);
+                unpack2(sqd3x2(X, Y, Z, ax2, ay2, z45), d[4], d[5]);
+                unpack2(sqd3x2(X, Y, Z, ax3, ay3, z67), d[6], d[7]);
+                // fminf skips NaN, which this policy drops anyway.
+                const float m = fminf(fminf(fminf(d[0], d[1]), fminf(d[2], d[3])),
+                                      fminf(fminf(d[4], d[5]), fminf(d[6], d[7])));
+                if (!(m > thr)) {
 #pragma unroll
-                for (int g = 0; g < 8; g += 4) {
-                    const ulonglong2 a0 = *reinterpret_cast<const ulonglong2*>(xy + (e + g) / 2);
-                    const ulonglong2 a1 = *reinterpret_cast<const ulonglong2*>(xy + (e + g) / 2 + 1);
-                    const ulonglong2 zp = *reinterpret_cast<const ulonglong2*>(zz + (e + g) / 4);
-                    float d[4];
-                    unpack2(sqd3x2(X, Y, Z, a0.x, a0.y, zp.x), d[0], d[1]);
-                    unpack2(sqd3x2(X, Y, Z, a1.x, a1.y, zp.y), d[2], d[3]);
-                    // fminf skips NaN, which this policy drops anyway.
-                    const float m = fminf(fminf(d[0], d[1]), fminf(d[2], d[3]));
-                    if (!(m > thr) || e + g + 4 > cnt) {
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            if (!(d[u] > thr) && e + g + u < cnt) {
-                                qd[qn * kThreads + tid] = d[u];
-                                qi[qn * kThreads + tid] = (uint32_t)(j0 + e + g + u);
-                                ++qn;
-                            }
+                    for (int u = 0; u < 8; ++u) {
+                        if (!(d[u] > thr) && u < valid) {
+                            qd[qn * kThreads + tid] = d[u];
+                            qi[qn * kThreads + tid] = (uint32_t)(j0 + e + u);
+                            ++qn;
                         }
                     }
                 }
@@ -296,7 +309,15 @@ knn3p_kernel(const float* __restrict__ query, const float* __restrict__ ref, Lay
                     flush();
                     thr = top.kth();
                 }
-            }
+            };
+            const int full = cnt & ~7;
+            uint32_t a = (uint32_t)__cvta_generic_to_shared(xy);
+            uint32_t z = (uint32_t)__cvta_generic_to_shared(zz);
+            for (int e = 0; e < full; e += 8, a += 64, z += 32) step(a, z, e, 8);
+            // Ragged end of the slice (the last tile only): one step whose
+            // points past cnt (zero-filled tile slots inside the slice) are
+            // not offered.
+            if (full < cnt) step(a, z, full, cnt - full);
         }
         if (t + 1 < ntiles) store_tile(buf ^ 1);
         __syncthreads();

@@ -138,6 +138,14 @@ __device__ __forceinline__ f32x2 sqd3x2(f32x2 ax, f32x2 ay, f32x2 az, f32x2 bx, 
     return add2(add2(sq2(dx), sq2(dy)), sq2(dz));
 }
 
+// 16-byte shared-memory load of two packed pairs from a 32-bit shared-window
+// address plus a compile-time byte offset (one base register per loop
+// instead of 64-bit generic pointer arithmetic per load).
+template <int OFF>
+__device__ __forceinline__ void lds_pairs(uint32_t addr, f32x2& lo, f32x2& hi) {
+    asm volatile("ld.shared.v2.b64 {%0, %1}, [%2+%3];" : "=l"(lo), "=l"(hi) : "r"(addr), "n"(OFF));
+}
+
 // NaN-propagating minimum (torch.minimum semantics): PTX min.NaN.f32.
 __device__ __forceinline__ float fmin_nan(float a, float b) {
     float r;
