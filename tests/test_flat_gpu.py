@@ -288,7 +288,8 @@ def test_radius_nonfinite_and_zero(cuda_device):
     radius_case(x, y, LX, LY, 0.0, 16, cuda_device)
 
 
-@pytest.mark.parametrize("lengths", [[1, 2, 30, 0, 257, 1000, 4], [9000, 0, 100, 20000, 8192]])
+@pytest.mark.parametrize("lengths", [[1, 2, 30, 0, 257, 1000, 4], [9000, 0, 100, 20000, 8192],
+                                     [1500, 0, 300, 8192, 4097, 2]])
 def test_fps_ragged_against_oracle(cuda_device, lengths):
     x = ragged(lengths, 3, 15)
     ptr = ptr_of(lengths)
