@@ -322,51 +322,27 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
 }
 
 // ---------------------------------------------------------------------------
-// One CTA per cloud with exact spatial pruning (clouds of 1025-8192 points).
-//
-// The cloud is staged in shared memory and its indices sorted by a 30-bit
-// Morton code of the coordinates (bitonic sort), so thread t owns P points
-// that are close in space: slots [t P, t P + P) of the sorted order, held in
-// ascending index order.  Each thread keeps the bounding box of its points.
-// A step needs the thread's points only if the new centroid can lower one of
-// their min_d2 values: with lb the squared distance from the centroid to the
-// box, formed with the same rounded operations as the point distances,
-// every point's float squared distance is >= lb (each rounded operation is
-// monotone), so lb >= (the thread's largest min_d2) means that no min_d2
-// changes and the thread's (max, first index) from the last update still
-// holds.  The result is bit-identical to the unpruned kernel; in late steps
-// most warps skip the distance pass.  Clouds with a non-finite coordinate
-// keep the identity order and take the NaN path every step (no pruning).
-__device__ __forceinline__ uint32_t morton_part(uint32_t v) {
-    v &= 0x3ffu;
-    v = (v | (v << 16)) & 0x030000ffu;
-    v = (v | (v << 8)) & 0x0300f00fu;
-    v = (v | (v << 4)) & 0x030c30c3u;
-    v = (v | (v << 2)) & 0x09249249u;
-    return v;
-}
-
-// Squared distance from c to the box [lo, hi] with the rounding sequence of
-// sqd3: a lower bound of sqd3(p, c) for every p in the box.
-__device__ __forceinline__ float box_lb(float cx, float cy, float cz, float lx, float ly, float lz,
-                                        float hx, float hy, float hz) {
-    const float gx = cx < lx ? __fsub_rn(lx, cx) : (cx > hx ? __fsub_rn(cx, hx) : 0.f);
-    const float gy = cy < ly ? __fsub_rn(ly, cy) : (cy > hy ? __fsub_rn(cy, hy) : 0.f);
-    const float gz = cz < lz ? __fsub_rn(lz, cz) : (cz > hz ? __fsub_rn(cz, hz) : 0.f);
-    return __fadd_rn(__fadd_rn(__fmul_rn(gx, gx), __fmul_rn(gy, gy)), __fmul_rn(gz, gz));
-}
-
-template <int P, bool FLAT, int MAXT>
-__global__ void __launch_bounds__(MAXT, 1)
-fps_sorted_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t start_idx,
-                  int skip, int out_int32, void* __restrict__ out, int32_t* __restrict__ status,
-                  FlatFps flat, float* __restrict__ out_xyz, int n_pad) {
-    extern __shared__ __align__(16) unsigned char fps_smem[];
-    unsigned long long* s_sort = reinterpret_cast<unsigned long long*>(fps_smem);  // [n_pad]
-    float* s_xyz = reinterpret_cast<float*>(s_sort + n_pad);                      // [3 n]
+// One CTA per cloud (clouds of up to 8192 points), the path of mpo_fps,
+// mpo_fps_gather and mpo_flat_fps.  The cloud is staged in shared memory (the
+// centroid load); thread t owns the contiguous points [t P, t P + P), so its
+// slots are in index order and a strict > keeps its first maximum.  Per step:
+// the packed distance update and the thread's argmax, two redux.sync per
+// warp, one barrier, and a redundant cross-warp reduce in every warp.
+// Contiguous ownership measured faster than the strided one of fps_kernel
+// (8 clouds x 8192 -> 2048 samples: 1.48 -> 1.26 ms; 32 x 2048 -> 512:
+// 0.178 -> 0.163 ms; 8 x 4096 -> 1024: 0.421 -> 0.416 ms).  Sorting the points by Morton code so that a thread could skip
+// steps whose centroid is provably too far from its points' bounding box
+// (bit-exact) was slower at every size: a step's time is dominated by the
+// reduce-and-barrier chain (about 0.3 us of the 0.4 us step at 4096 points),
+// which skipping does not shorten.
+template <int P, bool FLAT>
+__global__ void __launch_bounds__(kMaxThreads, 1)
+fps_cta_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t start_idx,
+               int skip, int out_int32, void* __restrict__ out, int32_t* __restrict__ status,
+               FlatFps flat, float* __restrict__ out_xyz) {
+    extern __shared__ float s_xyz[];  // [3 n]
     __shared__ uint32_t s_key[2][32];
     __shared__ uint32_t s_idx[2][32];
-    __shared__ float s_box[6][32];
 
     const int b = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -389,111 +365,21 @@ fps_sorted_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int6
     }
     const float* __restrict__ p = xyz + (size_t)base * 3;
     const int nn = (int)n;
+    for (int e = tid; e < 3 * nn; e += nthr) s_xyz[e] = p[e];
+    __syncthreads();
 
-    // Stage the cloud; bounding box of the finite cloud.
-    float lo[3] = {INFINITY, INFINITY, INFINITY}, hi[3] = {-INFINITY, -INFINITY, -INFINITY};
-    bool bad = false;
-    for (int e = tid; e < 3 * nn; e += nthr) {
-        const float v = p[e];
-        s_xyz[e] = v;
-        bad |= !isfinite(v);
-    }
-    __syncthreads();
-    for (int i = tid; i < nn; i += nthr) {
-#pragma unroll
-        for (int a = 0; a < 3; ++a) {
-            lo[a] = fminf(lo[a], s_xyz[3 * i + a]);
-            hi[a] = fmaxf(hi[a], s_xyz[3 * i + a]);
-        }
-    }
-    const bool nan_mode = __syncthreads_or(bad) != 0;
-#pragma unroll
-    for (int a = 0; a < 3; ++a) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            lo[a] = fminf(lo[a], __shfl_xor_sync(FULL_MASK, lo[a], o));
-            hi[a] = fmaxf(hi[a], __shfl_xor_sync(FULL_MASK, hi[a], o));
-        }
-        if (lane == 0) {
-            s_box[a][warp] = lo[a];
-            s_box[3 + a][warp] = hi[a];
-        }
-    }
-    __syncthreads();
-    float scale[3], org[3];
-#pragma unroll
-    for (int a = 0; a < 3; ++a) {
-        float l = INFINITY, h = -INFINITY;
-        for (int w = 0; w < nwarps; ++w) {
-            l = fminf(l, s_box[a][w]);
-            h = fmaxf(h, s_box[3 + a][w]);
-        }
-        org[a] = l;
-        const float ext = h - l;
-        scale[a] = ext > 0.f && isfinite(ext) ? 1023.f / ext : 0.f;
-    }
-    // Sort keys: Morton code << 32 | index (identity order for a cloud with
-    // a non-finite coordinate); padding sorts last.
-    for (int i = tid; i < n_pad; i += nthr) {
-        unsigned long long key = ~0ull;
-        if (i < nn) {
-            uint32_t code = 0;
-            if (!nan_mode) {
-                uint32_t qv[3];
-#pragma unroll
-                for (int a = 0; a < 3; ++a) {
-                    const float t = (s_xyz[3 * i + a] - org[a]) * scale[a];
-                    qv[a] = (uint32_t)fminf(fmaxf(t, 0.f), 1023.f);
-                }
-                code = morton_part(qv[0]) | (morton_part(qv[1]) << 1) | (morton_part(qv[2]) << 2);
-            }
-            key = ((unsigned long long)code << 32) | (uint32_t)i;
-        }
-        s_sort[i] = key;
-    }
-    __syncthreads();
-    if (!nan_mode) {
-        for (int k = 2; k <= n_pad; k <<= 1) {
-            for (int lj = __ffs(k) - 2; lj >= 0; --lj) {
-                const int j = 1 << lj;
-                for (int q = tid; q < n_pad / 2; q += nthr) {
-                    // Pair q: lower element i (bit lj clear) and i + j.
-                    const int i = ((q >> lj) << (lj + 1)) | (q & (j - 1));
-                    const int l = i + j;
-                    const unsigned long long a = s_sort[i], c = s_sort[l];
-                    const bool asc = (i & k) == 0;
-                    if ((a > c) == asc) {
-                        s_sort[i] = c;
-                        s_sort[l] = a;
-                    }
-                }
-                __syncthreads();
-            }
-        }
-    }
-
-    // This thread's points: slots [tid P, tid P + P) in ascending index order.
+    // This thread's points: slot u -> index tid P + u (none past n).
     constexpr int PP = (P + 1) / 2;
     constexpr int PS = 2 * PP;
     uint32_t jdx[PS];
 #pragma unroll
     for (int u = 0; u < PS; ++u) {
-        const int sl = tid * P + u;
-        jdx[u] = (u < P && sl < nn) ? (uint32_t)s_sort[sl] : 0xffffffffu;
-    }
-    // Odd-even transposition sort of the P indices (invalid slots last).
-#pragma unroll
-    for (int r = 0; r < PS; ++r) {
-#pragma unroll
-        for (int u = r & 1; u + 1 < PS; u += 2) {
-            const uint32_t a = jdx[u], c = jdx[u + 1];
-            jdx[u] = min(a, c);
-            jdx[u + 1] = max(a, c);
-        }
+        const int j = tid * P + u;
+        jdx[u] = (u < P && j < nn) ? (uint32_t)j : 0xffffffffu;
     }
     f32x2 PX[PP], PY[PP], PZ[PP];
     float md[PS];
-    float bl[3] = {INFINITY, INFINITY, INFINITY}, bh[3] = {-INFINITY, -INFINITY, -INFINITY};
+    bool bad = false;
 #pragma unroll
     for (int h = 0; h < PP; ++h) {
         float c[6];
@@ -505,15 +391,11 @@ fps_sorted_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int6
                 c[3 * l + 0] = s_xyz[3 * j + 0];
                 c[3 * l + 1] = s_xyz[3 * j + 1];
                 c[3 * l + 2] = s_xyz[3 * j + 2];
+                bad |= !(isfinite(c[3 * l]) && isfinite(c[3 * l + 1]) && isfinite(c[3 * l + 2]));
                 float init = INFINITY;
                 if (skip && sqd3(c[3 * l], c[3 * l + 1], c[3 * l + 2], 0.f, 0.f, 0.f) < 1e-3f)
                     init = -INFINITY;
                 md[u] = init;
-#pragma unroll
-                for (int a = 0; a < 3; ++a) {
-                    bl[a] = fminf(bl[a], c[3 * l + a]);
-                    bh[a] = fmaxf(bh[a], c[3 * l + a]);
-                }
             } else {
                 c[3 * l + 0] = c[3 * l + 1] = c[3 * l + 2] = 0.f;
                 md[u] = -INFINITY;
@@ -523,18 +405,9 @@ fps_sorted_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int6
         PY[h] = pack2(c[1], c[4]);
         PZ[h] = pack2(c[2], c[5]);
     }
-    // The thread's (largest min_d2, first index holding it); with every
-    // min_d2 at -inf, its first point (the lowest index among equal keys).
-    float bv = -INFINITY;
-    uint32_t bj = 0xffffffffu;
-#pragma unroll
-    for (int u = 0; u < PS; ++u) {
-        if (jdx[u] != 0xffffffffu && md[u] > bv) {
-            bv = md[u];
-            bj = jdx[u];
-        }
-    }
-    if (bj == 0xffffffffu) bj = jdx[0];
+    // NaN can only enter min_d2 through a non-finite coordinate; then (for
+    // the whole run) the keys rank NaN above every number, like torch.argmax.
+    const bool nan_mode = __syncthreads_or(bad) != 0;
 
     uint32_t far = (uint32_t)start;
     float cx = s_xyz[3 * far + 0], cy = s_xyz[3 * far + 1], cz = s_xyz[3 * far + 2];
@@ -555,28 +428,30 @@ fps_sorted_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int6
         if (i + 1 == np) break;
         uint32_t bkey = 0u, bidx = 0xffffffffu;
         if (!nan_mode) {
-            const float lb = box_lb(cx, cy, cz, bl[0], bl[1], bl[2], bh[0], bh[1], bh[2]);
-            if (!(lb >= bv)) {
-                const f32x2 CX = pack2(cx, cx), CY = pack2(cy, cy), CZ = pack2(cz, cz);
-                bv = -INFINITY;
-                bj = 0xffffffffu;
+            // Finite fast path: min_d2 is -inf (skipped or unused slot, kept
+            // there by min) or in [0, +inf]; a float compare finds the
+            // thread's first maximum and the ordered key is formed once.
+            const f32x2 CX = pack2(cx, cx), CY = pack2(cy, cy), CZ = pack2(cz, cz);
+            float bv = -INFINITY;
+            uint32_t bj = 0xffffffffu;
 #pragma unroll
-                for (int h = 0; h < PP; ++h) {
-                    float d[2];
-                    unpack2(sqd3x2(PX[h], PY[h], PZ[h], CX, CY, CZ), d[0], d[1]);
+            for (int h = 0; h < PP; ++h) {
+                float d[2];
+                unpack2(sqd3x2(PX[h], PY[h], PZ[h], CX, CY, CZ), d[0], d[1]);
 #pragma unroll
-                    for (int l = 0; l < 2; ++l) {
-                        const int u = 2 * h + l;
-                        if (u >= P) break;
-                        md[u] = fminf(md[u], d[l]);
-                        if (md[u] > bv) {
-                            bv = md[u];
-                            bj = jdx[u];
-                        }
+                for (int l = 0; l < 2; ++l) {
+                    const int u = 2 * h + l;
+                    if (u >= P) break;
+                    md[u] = fminf(md[u], d[l]);
+                    if (md[u] > bv) {
+                        bv = md[u];
+                        bj = jdx[u];
                     }
                 }
-                if (bj == 0xffffffffu) bj = jdx[0];
             }
+            // A thread whose points are all -inf offers its first point (the
+            // lowest index among equal keys).
+            if (bj == 0xffffffffu) bj = jdx[0];
             bidx = bj;
             bkey = bj == 0xffffffffu ? 0u : ordered_key(bv);
         } else {
@@ -630,31 +505,19 @@ int threads_for(int64_t per_cta, int P) {
     return (int)min64(kMaxThreads, ((ceil_div(per_cta, P) + 31) / 32) * 32);
 }
 
-// Clouds for which the pruned kernel is faster: 4097-8192 points (32 per
-// thread) and, for dense batches, at least 64 samples.  Measured on B200
-// (8 clouds, a quarter of the points sampled): 8192 points 1.47 -> 1.26 ms;
-// at 2048 and 4096 points the unpruned kernel is faster (0.18 vs 0.23 ms,
-// 0.42 vs 0.49-0.62 ms with 8-32 points per thread): a step's time is the
-// latency of the warps that update plus the cross-warp argmax, and skipping
-// the other warps does not shorten it.
-bool use_sorted(int64_t N, int64_t npoint, bool flat) {
-    return N > 4096 && N <= kPointsPerCta && (flat || npoint >= 64);
-}
-
-template <int P, bool FLAT, int MAXT>
-int launch_sorted(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
-                  int skip, int out_int32, void* out, int32_t* status, const FlatFps& flat,
-                  float* out_xyz, cudaStream_t stream) {
-    auto kern = fps_sorted_kernel<P, FLAT, MAXT>;
-    int n_pad = 1;
-    while (n_pad < N) n_pad <<= 1;
-    const size_t smem = (size_t)n_pad * 8 + (size_t)N * 3 * sizeof(float);
+// fps_cta_kernel launch: N is the cloud size (dense) or the longest segment
+// (flat); it sets P, the CTA size and the shared-memory stage.
+template <int P, bool FLAT>
+int launch_cta(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
+               int skip, int out_int32, void* out, int32_t* status, const FlatFps& flat,
+               float* out_xyz, cudaStream_t stream) {
+    auto kern = fps_cta_kernel<P, FLAT>;
+    const size_t smem = (size_t)N * 3 * sizeof(float);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return fail(kCudaError, "mpo_fps: cannot set the shared-memory limit");
-    const int threads = (int)min64(MAXT, ((ceil_div(N, P) + 31) / 32) * 32);
-    kern<<<(unsigned)B, threads, smem, stream>>>(xyz, N, npoint, start_idx, skip, out_int32, out,
-                                                 status, flat, out_xyz, n_pad);
+    kern<<<(unsigned)B, threads_for(N, P), smem, stream>>>(xyz, N, npoint, start_idx, skip,
+                                                           out_int32, out, status, flat, out_xyz);
     return check_launch("mpo_fps");
 }
 
@@ -675,15 +538,22 @@ int launch_single(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_
     return check_launch("mpo_fps");
 }
 
-// prune: take the spatially pruned kernel where use_sorted() says it pays.
+// cta: take fps_cta_kernel (mpo_fps, mpo_fps_gather, mpo_flat_fps) instead of
+// the one-CTA form of fps_kernel (kept for mpo_fps_noalloc).
 template <bool FLAT>
 int launch_single_any(const float* xyz, int64_t B, int64_t N, int64_t npoint,
                       int64_t start_idx, int skip, int o32, void* out, int32_t* status,
                       const FlatFps& f, cudaStream_t s, float* oxyz = nullptr,
-                      bool prune = false) {
-    if (prune && use_sorted(N, npoint, FLAT)) {
-        return launch_sorted<32, FLAT, kMaxThreads>(xyz, B, N, npoint, start_idx, skip, o32, out,
-                                                    status, f, oxyz, s);
+                      bool cta = false) {
+    if (cta) {
+        switch (pick_p(N)) {
+            case 1: return launch_cta<1, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+            case 2: return launch_cta<2, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+            case 4: return launch_cta<4, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+            case 8: return launch_cta<8, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+            case 16: return launch_cta<16, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+            default: return launch_cta<32, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
+        }
     }
     switch (pick_p(N)) {
         case 1: return launch_single<1, FLAT>(xyz, B, N, npoint, start_idx, skip, o32, out, status, f, oxyz, s);
@@ -815,7 +685,7 @@ int mpo_fps_gather(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64
     const int o32 = out_int32 ? 1 : 0;
     if (strategy != MPO_FPS_GROUP && N <= kPointsPerCta)
         return launch_single_any<false>(xyz, B, N, npoint, start_idx, skip, o32, out, status_out,
-                                        FlatFps{}, s, out_xyz, /*prune=*/true);
+                                        FlatFps{}, s, out_xyz, /*cta=*/true);
     GroupPlan plan;
     st = plan_group(B, N, strategy, &plan, "mpo_fps");
     if (st) return st;
@@ -856,7 +726,7 @@ int mpo_flat_fps(const float* x, const int64_t* ptr, const int64_t* out_ptr,
     const FlatFps flat{ptr, out_ptr, starts, total_n, total_out, max_len};
     if (max_len <= kPointsPerCta)
         return launch_single_any<true>(x, segments, max_len, 0, 0, 0, 0, out, status, flat, s,
-                                       nullptr, /*prune=*/true);
+                                       nullptr, /*cta=*/true);
     GroupPlan plan;
     int st = plan_group(segments, max_len, MPO_FPS_AUTO, &plan, "mpo_flat_fps");
     if (st) return st;

@@ -115,8 +115,8 @@ def test_nan_points_follow_torch_argmax(cuda_device):
     np.testing.assert_array_equal(got.cpu().numpy(), want)
 
 
-# ---- spatially pruned one-CTA path (4096 < N <= 8192 points, >= 64 samples); the
-# smaller sizes run the unpruned kernel on the same cases --------------------------------
+# ---- one-CTA path (fps_cta_kernel: contiguous points per thread) on long runs,
+# ties, duplicates, skip-near-origin, non-finite and overflowing clouds ------------------
 def _check(xyz, npoint, start=0, skip=False, device=None):
     want = O.furthest_point_sample(xyz.numpy(), npoint, start, skip)
     got = mps_pointops.furthest_point_sample(xyz.to(device), npoint, start, skip)
@@ -124,7 +124,7 @@ def _check(xyz, npoint, start=0, skip=False, device=None):
 
 
 @pytest.mark.parametrize("n", [2048, 4097, 6000, 8192])
-def test_pruned_uniform_cube_all_samples(cuda_device, n):
+def test_cta_uniform_cube_all_samples(cuda_device, n):
     """Config 1's distribution, sampled to a quarter and to every point."""
     g = torch.Generator().manual_seed(n)
     xyz = torch.rand(2, n, 3, generator=g)
@@ -132,7 +132,7 @@ def test_pruned_uniform_cube_all_samples(cuda_device, n):
     _check(xyz[:1], n, n - 1, False, cuda_device)
 
 
-def test_pruned_lattice_ties(cuda_device):
+def test_cta_lattice_ties(cuda_device):
     """Integer lattice: min_d2 ties everywhere; the first index must win."""
     g = torch.Generator().manual_seed(8)
     xyz = torch.randint(0, 6, (2, 6144, 3), generator=g).float()
@@ -140,7 +140,7 @@ def test_pruned_lattice_ties(cuda_device):
     _check(xyz, 6144, 0, False, cuda_device)
 
 
-def test_pruned_duplicates_and_degenerate_extent(cuda_device):
+def test_cta_duplicates_and_degenerate_extent(cuda_device):
     xyz = torch.zeros(1, 5000, 3)
     _check(xyz, 100, 7, False, cuda_device)
     line = torch.zeros(1, 4500, 3)
@@ -148,7 +148,7 @@ def test_pruned_duplicates_and_degenerate_extent(cuda_device):
     _check(line, 300, 0, False, cuda_device)
 
 
-def test_pruned_skip_near_origin_and_clusters(cuda_device):
+def test_cta_skip_near_origin_and_clusters(cuda_device):
     g = torch.Generator().manual_seed(21)
     centres = torch.rand(12, 3, generator=g) * 20 - 10
     labels = torch.randint(0, 12, (1, 5000), generator=g)
@@ -158,7 +158,7 @@ def test_pruned_skip_near_origin_and_clusters(cuda_device):
     _check(xyz, 1500, 250, False, cuda_device)
 
 
-def test_pruned_nonfinite_and_overflowing_clouds(cuda_device):
+def test_cta_nonfinite_and_overflowing_clouds(cuda_device):
     g = torch.Generator().manual_seed(22)
     xyz = torch.randn(1, 5000, 3, generator=g)
     xyz[0, 1234, 2] = float("nan")
@@ -170,7 +170,7 @@ def test_pruned_nonfinite_and_overflowing_clouds(cuda_device):
     _check(big, 150, 3, False, cuda_device)
 
 
-def test_pruned_fps_gather_and_int32(cuda_device):
+def test_cta_fps_gather_and_int32(cuda_device):
     g = torch.Generator().manual_seed(23)
     xyz = torch.rand(3, 6000, 3, generator=g)
     want = O.furthest_point_sample(xyz.numpy(), 1024, 0, True).astype(np.int32)
