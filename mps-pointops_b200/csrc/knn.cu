@@ -27,9 +27,10 @@
 //   * k in (32, 256] uses a warp-per-query kernel whose sorted list is spread
 //     over the 32 lanes (8 slots each) and updated with ballot/shuffle.
 //   * k <= 32 on clouds up to 2^18 points (and three_nn) uses a warp-per-query
-//     kernel with one list slot per lane (knn_wq3_kernel): a thread-owned list
-//     makes the whole warp replay the insertion whenever any lane inserts,
-//     which on moderate clouds happens on almost every step.
+//     kernel (knn_wq3_kernel) with the 32 best kept sorted across the lanes
+//     and candidates merged 32 at a time: a thread-owned list makes the whole
+//     warp replay the insertion whenever any lane inserts, which on moderate
+//     clouds happens on almost every step.
 #include <string>
 
 #include "../../include/mpo_b200.h"
@@ -590,18 +591,21 @@ knn_warp_kernel(const float* __restrict__ query, const float* __restrict__ ref, 
 // consecutive across the warp (conflict-free).  Candidates are offered chunk
 // by chunk, in index order, with the bar updated between chunks.
 //
-// The k best so far are kept UNSORTED, one per lane s < k, as (key, index):
-// key = the ordered bits of the squared distance (monotone in the float,
-// every NaN mapped above +inf, which is the order of every policy here), so
-// (key, index) in lexicographic order is the (SD, index) order.  Empty slots
-// hold (0xffffffff, kNoIndex - lane): worse than any candidate and distinct.
-// A candidate enters iff it precedes the worst entry; it replaces that entry
-// and two redux.sync find the new worst -- about a dozen warp instructions
-// per insertion.  The list is sorted once at the end (bitonic across lanes).
-// One min over a lane's four distances and one ballot against the worst
-// entry's distance skip a step without candidates (fminf ignores NaN, which
-// can only enter a list that has room or already holds a NaN; the threshold
-// then lets every lane through).
+// Selection (FAISS-style warp select): the 32 best so far live sorted across
+// the warp, one 64-bit key per lane (the ordered bits of the squared distance
+// << 32 | index; every NaN maps above +inf, which is the order of every
+// policy here, so the key order is the (SD, index) order).  A chunk's points
+// that are admissible and not above the bar (the SD of rank k - 1) are
+// appended to a 32-entry per-warp buffer in shared memory through one ballot
+// (prefix popcounts give the slots); a full buffer is merged into the list by
+// one bitonic sort of the buffer across the lanes and one bitonic merge.  The
+// bar is stale between merges, which only admits more candidates, so every
+// point of the final top k passes it.  This replaced a per-candidate insertion
+// (replace the worst entry, two redux.sync to find the next worst) that made
+// the kernel ALU-bound.  One min over a lane's
+// four distances and one ballot against the bar skip a step without
+// candidates (fminf ignores NaN, which can only enter a list whose rank k - 1
+// is empty or NaN; the bar then lets every lane through).
 constexpr int kWqWarps = 8;
 constexpr int kWqTile = 2048;  // multiple of 128
 constexpr uint32_t kEmptyKey = 0xffffffffu;
@@ -616,6 +620,7 @@ knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, L
                float* __restrict__ dist, int64_t* __restrict__ idx64,
                int32_t* __restrict__ idx32, float* __restrict__ sqdist) {
     __shared__ float4 tA[kWqTile / 4], tB[kWqTile / 4], tZ[kWqTile / 4];
+    __shared__ unsigned long long s_buf[kWqWarps * 32];  // per-warp candidate buffers
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     Span sp;
     if (!locate<FLAT>(L, kWqWarps, sp)) return;  // CTA-uniform
@@ -631,18 +636,51 @@ knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, L
         qz = qp[2];
     }
     const f32x2 X = pack2(qx, qx), Y = pack2(qy, qy), Z = pack2(qz, qz);
-    // This lane's slot (lanes >= k hold (0, 0): never the worst).
-    uint32_t lk = lane < k ? kEmptyKey : 0u;
-    uint32_t lx = lane < k ? kNoIndex - (uint32_t)lane : 0u;
-    float ld = INFINITY;
-    uint32_t wk = kEmptyKey, wi = kNoIndex;  // the worst entry (lane 0's empty slot)
-    float thr = INFINITY;                    // its distance; +inf while a slot is empty
+    // The 32 best so far, sorted across the warp: lane s holds rank s as a
+    // 64-bit key (ordered SD bits << 32 | index); empty ranks are all ones.
+    unsigned long long best = ~0ull;
+    float thr = INFINITY;  // SD of rank k - 1; +inf while that rank is empty
+    unsigned long long* const buf = s_buf + warp * 32;
+    int bc = 0;  // candidates waiting in buf (warp-uniform)
+    // Merge the bc buffered candidates into `best`: bitonic sort of the
+    // buffer across the lanes, then the 32 smallest of both sorted lists
+    // (min of rank i and reversed rank 31 - i: a bitonic sequence) and a
+    // bitonic clean; thr follows rank k - 1.
+    auto merge = [&]() {
+        __syncwarp();
+        unsigned long long b = lane < bc ? buf[lane] : ~0ull;
+#pragma unroll
+        for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                const unsigned long long o = __shfl_xor_sync(FULL_MASK, b, stride);
+                const bool keep_min = ((lane & size) == 0) == ((lane & stride) == 0);
+                b = keep_min ? (o < b ? o : b) : (o < b ? b : o);
+            }
+        }
+        const unsigned long long rb = __shfl_sync(FULL_MASK, b, 31 - lane);
+        best = rb < best ? rb : best;
+#pragma unroll
+        for (int stride = 16; stride > 0; stride >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(FULL_MASK, best, stride);
+            const bool lower = (lane & stride) == 0;
+            best = lower ? (o < best ? o : best) : (o < best ? best : o);
+        }
+        const unsigned long long kth = __shfl_sync(FULL_MASK, best, k - 1);
+        const uint32_t kk = (uint32_t)(kth >> 32);
+        // A NaN (three_nn) or empty rank k - 1 lets every candidate through.
+        thr = kk != kEmptyKey ? ordered_key_inv(kk)
+                              : ((uint32_t)kth >= 0x80000000u ? INFINITY : __int_as_float(0x7fffffff));
+        bc = 0;
+        __syncwarp();
+    };
     // Tile fill: tile point p is point l = p % 32 of chunk v = (p / 32) % 4 of
     // step p / 128.  Thread t stores points t, t + 256, ...; l and v are fixed
     // per thread, so each thread always writes the same fields.
     const int fl = threadIdx.x & 31, fv = (threadIdx.x >> 5) & 3;
     float* const fxy = reinterpret_cast<float*>(fv < 2 ? tA : tB) + (fv & 1);
     float* const fz = reinterpret_cast<float*>(tZ) + fv;
+    const unsigned lt = (1u << lane) - 1u;
     for (int64_t t0 = 0; t0 < N; t0 += kWqTile) {
         const int tn = (int)min64(kWqTile, N - t0);
         __syncthreads();
@@ -665,58 +703,35 @@ knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, L
             unpack2(sqd3x2(X, Y, Z, b.x, b.y, z.y), d[2], d[3]);
             const float m = fminf(fminf(d[0], d[1]), fminf(d[2], d[3]));
             if (__ballot_sync(FULL_MASK, !(m > thr)) == 0u) continue;
+            // Buffer every admissible point not above the bar (stale between
+            // merges: it only ever admits more); a full buffer is merged
+            // first and the chunk re-filtered against the new bar.
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
                 const int e = c0 + 32 * v + lane;
-                unsigned pending = __ballot_sync(FULL_MASK, e < tn && !(d[v] > thr));
-                while (pending) {
-                    const int src = __ffs(pending) - 1;
-                    pending &= pending - 1;
-                    const float cd = __shfl_sync(FULL_MASK, d[v], src);
-                    const uint32_t ci = (uint32_t)(t0 + c0 + 32 * v + src);
-                    if (!admissible<POLICY>(cd)) continue;
-                    const uint32_t ck = sd_key(cd);
-                    if (!(ck < wk || (ck == wk && ci < wi))) continue;
-                    if (lk == wk && lx == wi) {
-                        lk = ck;
-                        lx = ci;
-                        ld = cd;
-                    }
-                    wk = __reduce_max_sync(FULL_MASK, lk);
-                    wi = __reduce_max_sync(FULL_MASK, lk == wk ? lx : 0u);
-                    thr = wk != kEmptyKey ? ordered_key_inv(wk)
-                                          : (wi >= 0x80000000u ? INFINITY : __int_as_float(0x7fffffff));
+                bool cand = e < tn && !(d[v] > thr) && admissible<POLICY>(d[v]);
+                unsigned mk = __ballot_sync(FULL_MASK, cand);
+                if (mk == 0u) continue;
+                if (bc + __popc(mk) > 32) {
+                    merge();
+                    cand = cand && !(d[v] > thr);
+                    mk = __ballot_sync(FULL_MASK, cand);
                 }
+                if (cand) {
+                    buf[bc + __popc(mk & lt)] =
+                        ((unsigned long long)sd_key(d[v]) << 32) | (uint32_t)(t0 + e);
+                }
+                bc += __popc(mk);
             }
         }
     }
     if (!active) return;
-    // Sort the k entries ascending by (key, index): bitonic across the warp,
-    // lanes >= k carrying (max, max) so they end up last.
-    if (lane >= k) {
-        lk = kEmptyKey;
-        lx = 0xffffffffu;
-    }
-#pragma unroll
-    for (int size = 2; size <= 32; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            const uint32_t ok = __shfl_xor_sync(FULL_MASK, lk, stride);
-            const uint32_t ox = __shfl_xor_sync(FULL_MASK, lx, stride);
-            const float od = __shfl_xor_sync(FULL_MASK, ld, stride);
-            const bool ascending = (lane & size) == 0;
-            const bool lower = (lane & stride) == 0;
-            const bool other_first = ok < lk || (ok == lk && ox < lx);
-            if ((lower == ascending) ? other_first : !other_first) {
-                lk = ok;
-                lx = ox;
-                ld = od;
-            }
-        }
-    }
+    if (bc > 0) merge();
     if (lane >= k) return;
     const size_t row = (size_t)q * (size_t)k;
+    const uint32_t lx = (uint32_t)best;
     const bool filled = lx < 0x80000000u;  // real rows are below 2**31
+    const float ld = ordered_key_inv((uint32_t)(best >> 32));
     const float dd = filled ? ld : INFINITY;
     if (dist) dist[row + lane] = sqrtf(dd);
     if (sqdist) sqdist[row + lane] = dd;
