@@ -573,21 +573,44 @@ __global__ void check_inputs_kernel(const float* __restrict__ x, const float* __
                                     int64_t Q, int64_t D, int32_t* __restrict__ flags) {
     const int64_t nx = B * P * D, total = nx + B * Q * D;
     const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     if (t0 < B) {
         if (xl && (xl[t0] < 0 || xl[t0] > P)) flags[2] = 1;
         if (yl && (yl[t0] < 0 || yl[t0] > Q)) flags[3] = 1;
     }
     bool bad_x = false, bad_y = false;
-    for (int64_t e = t0; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-        const bool is_y = e >= nx;
-        const int64_t f = is_y ? e - nx : e;
-        const int64_t M = is_y ? Q : P;
-        const int64_t row = f / D, b = row / M, i = row % M;
-        const int64_t* l = is_y ? yl : xl;
-        const int64_t len = l ? l[b] : M;
-        if (i < len && !isfinite((is_y ? y : x)[f])) {
-            bad_x |= !is_y;
-            bad_y |= is_y;
+    if (xl == nullptr && yl == nullptr) {
+        // Every coordinate is valid: a flat scan, 16-byte loads where the
+        // array allows them (no per-element row arithmetic).
+        for (int a = 0; a < 2; ++a) {
+            const float* p = a ? y : x;
+            const int64_t n = a ? total - nx : nx;
+            bool bad = false;
+            int64_t head = 0;
+            if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+                const float4* p4 = reinterpret_cast<const float4*>(p);
+                for (int64_t e = t0; e < n / 4; e += stride) {
+                    const float4 v = p4[e];
+                    bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+                }
+                head = n / 4 * 4;
+            }
+            for (int64_t e = head + t0; e < n; e += stride) bad |= !isfinite(p[e]);
+            if (a) bad_y = bad;
+            else bad_x = bad;
+        }
+    } else {
+        for (int64_t e = t0; e < total; e += stride) {
+            const bool is_y = e >= nx;
+            const int64_t f = is_y ? e - nx : e;
+            const int64_t M = is_y ? Q : P;
+            const int64_t row = f / D, b = row / M, i = row % M;
+            const int64_t* l = is_y ? yl : xl;
+            const int64_t len = l ? l[b] : M;
+            if (i < len && !isfinite((is_y ? y : x)[f])) {
+                bad_x |= !is_y;
+                bad_y |= is_y;
+            }
         }
     }
     if (__any_sync(FULL_MASK, bad_x) && (threadIdx.x & 31) == 0) flags[0] = 1;
@@ -699,7 +722,15 @@ __global__ void loss_bwd_kernel(const float* __restrict__ x, const float* __rest
     const bool dir = e >= nx;
     const int64_t M = dir ? Q : P, Nn = dir ? P : Q;
     const int64_t row = dir ? e - nx : e;
-    const int64_t b = row / M, i = row % M;
+    int64_t b, i;
+    if (total <= 0x7fffffff) {  // 32-bit division (the 64-bit one is a long sequence)
+        const uint32_t r32 = (uint32_t)row, m32 = (uint32_t)M;
+        b = r32 / m32;
+        i = r32 - (uint32_t)b * m32;
+    } else {
+        b = row / M;
+        i = row % M;
+    }
     const int64_t* self_l = dir ? yl : xl;
     const int64_t len = self_l ? min64(max64(self_l[b], 0), M) : M;
     if (i >= len) return;
