@@ -484,14 +484,20 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                               (uint32_t)((ac * kQT + qt) * kTN + c * 32),
                           v);
                 const float4* ny4 = reinterpret_cast<const float4*>(s_ny + c * 32);
+                // Scores s = n(r) - 2 dot as packed f32x2 FMAs (two columns
+                // per instruction; the same single rounding as fmaf).
+                const f32x2 m2 = pack2(-2.f, -2.f);
                 if (PASS == 1) {
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float4 y = ny4[i];
-                        bmin[4 * i + 0] = fminf(bmin[4 * i + 0], fmaf(-2.f, v[4 * i + 0], y.x));
-                        bmin[4 * i + 1] = fminf(bmin[4 * i + 1], fmaf(-2.f, v[4 * i + 1], y.y));
-                        bmin[4 * i + 2] = fminf(bmin[4 * i + 2], fmaf(-2.f, v[4 * i + 2], y.z));
-                        bmin[4 * i + 3] = fminf(bmin[4 * i + 3], fmaf(-2.f, v[4 * i + 3], y.w));
+                        float sc[4];
+                        unpack2(fma2(pack2(v[4 * i + 0], v[4 * i + 1]), m2, pack2(y.x, y.y)),
+                                sc[0], sc[1]);
+                        unpack2(fma2(pack2(v[4 * i + 2], v[4 * i + 3]), m2, pack2(y.z, y.w)),
+                                sc[2], sc[3]);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) bmin[4 * i + c] = fminf(bmin[4 * i + c], sc[c]);
                     }
                 } else {
                     // Candidate bit mask of the 32 columns (no divergence),
@@ -501,10 +507,14 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float4 y = ny4[i];
-                        hits |= (fmaf(-2.f, v[4 * i + 0], y.x) <= thr ? 1u : 0u) << (4 * i + 0);
-                        hits |= (fmaf(-2.f, v[4 * i + 1], y.y) <= thr ? 1u : 0u) << (4 * i + 1);
-                        hits |= (fmaf(-2.f, v[4 * i + 2], y.z) <= thr ? 1u : 0u) << (4 * i + 2);
-                        hits |= (fmaf(-2.f, v[4 * i + 3], y.w) <= thr ? 1u : 0u) << (4 * i + 3);
+                        float sc[4];
+                        unpack2(fma2(pack2(v[4 * i + 0], v[4 * i + 1]), m2, pack2(y.x, y.y)),
+                                sc[0], sc[1]);
+                        unpack2(fma2(pack2(v[4 * i + 2], v[4 * i + 3]), m2, pack2(y.z, y.w)),
+                                sc[2], sc[3]);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            hits |= (sc[c] <= thr ? 1u : 0u) << (4 * i + c);
                     }
                     while (hits) {
                         const int i = __ffs(hits) - 1;

@@ -116,6 +116,12 @@ __device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
+// a*b + c for both lanes, one rounding each (fmaf on two lanes).
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
 // Rounded square of both lanes, d*d.  ptxas contracts mul.rn.f32x2 followed
 // by add.rn.f32x2 into a fused f32x2 FMA even under -fmad=false, which would
 // change the low bit of about one squared distance in five.  The square is
