@@ -76,6 +76,38 @@ def _lengths_or_none(lengths, *, batch: int, count: int, device: torch.device, n
     return lengths.contiguous()
 
 
+# Large searches run their queries in Morton order of their coordinates.
+# The kernel scans the reference points in input order and stops a query at
+# its K-th hit; the 8 queries of a CTA share each reference tile, so the CTA
+# runs as long as its slowest query.  Neighbouring queries have similar local
+# densities and therefore similar scan lengths: at BASELINE config 5 (131,072
+# clustered queries, 2^20 points) the kernel takes 20.7 ms in Morton order
+# against 29.1 ms in input order (22.2 ms with the ordering and the
+# scatter back).  Each query's result does not depend on the others, so the
+# outputs are identical.  Ragged query counts keep the input order (a
+# query's validity is its position).
+_ORDER_MIN_QUERIES = 16384
+_ORDER_MIN_POINTS = 65536
+
+
+def _morton_order(q: torch.Tensor) -> torch.Tensor:
+    """(B, M, 3) -> (B, M) int64: each cloud's queries sorted by a 30-bit
+    Morton code of their coordinates (non-finite coordinates count as 0)."""
+    x = torch.nan_to_num(q.detach(), nan=0.0, posinf=0.0, neginf=0.0)
+    lo = x.amin(dim=1, keepdim=True)
+    hi = x.amax(dim=1, keepdim=True)
+    v = ((x - lo) * (1023.0 / (hi - lo).clamp_min(1e-30))).clamp_(0, 1023).to(torch.int64)
+
+    def spread(t):  # 10 bits -> every third bit
+        t = (t | (t << 16)) & 0x030000FF
+        t = (t | (t << 8)) & 0x0300F00F
+        t = (t | (t << 4)) & 0x030C30C3
+        return (t | (t << 2)) & 0x09249249
+
+    code = spread(v[..., 0]) | (spread(v[..., 1]) << 1) | (spread(v[..., 2]) << 2)
+    return torch.argsort(code, dim=1)
+
+
 class _BallQuery(torch.autograd.Function):
     @staticmethod
     def forward(ctx, queries, points, query_lengths, point_lengths, radius_sq, k):
@@ -83,6 +115,11 @@ class _BallQuery(torch.autograd.Function):
         point_count = points.shape[1]
         q32 = queries if queries.dtype == torch.float32 else queries.float()
         p32 = points if points.dtype == torch.float32 else points.float()
+        order = None
+        if (query_lengths is None and query_count >= _ORDER_MIN_QUERIES
+                and point_count >= _ORDER_MIN_POINTS and k > 0):
+            order = _morton_order(q32)
+            q32 = torch.gather(q32, 1, order.unsqueeze(-1).expand(-1, -1, 3))
         indices = torch.empty((batch, query_count, k), device=queries.device, dtype=torch.int64)
         distances = torch.empty((batch, query_count, k), device=queries.device, dtype=torch.float32)
         if indices.numel():
@@ -91,6 +128,10 @@ class _BallQuery(torch.autograd.Function):
                     N.ptr(q32), N.ptr(p32), N.ptr(query_lengths), N.ptr(point_lengths), batch,
                     query_count, point_count, k, radius_sq, N.ptr(distances), N.ptr(indices),
                     N.stream(queries.device)), "ball_query")
+            if order is not None:  # back to the callers' query order
+                slots = order.unsqueeze(-1).expand(-1, -1, k)
+                distances = torch.empty_like(distances).scatter_(1, slots, distances)
+                indices = torch.empty_like(indices).scatter_(1, slots, indices)
         ctx.save_for_backward(queries, points, indices)
         ctx.mark_non_differentiable(indices)
         return distances, indices

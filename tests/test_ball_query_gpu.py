@@ -159,3 +159,37 @@ def test_float16_inputs(cuda_device):  # tests/test_ball_query_mps.py:565-583
     assert res.indices.cpu().tolist() == [[[0, 1]]]
     res.distances.backward(torch.tensor([[[1.0, 2.0]]], device=cuda_device))
     torch.testing.assert_close(q.grad.cpu(), torch.tensor([[[-2.5, 0.0, 0.0]]], dtype=torch.float16))
+
+
+def test_large_search_in_morton_order_matches_oracle(cuda_device):
+    """Searches of >= 16384 queries over >= 65536 points run their queries in
+    Morton order and scatter the results back: identical to the oracle, to
+    the input-order run (a ragged query count keeps the input order) and
+    with gradients in the callers' order.  Clustered clouds as BASELINE
+    config 5, with far and non-finite queries."""
+    g = torch.Generator().manual_seed(55)
+    centres = torch.rand(16, 3, generator=g) * 10 - 5
+    ref = (centres[torch.randint(16, (70000,), generator=g)] +
+           0.5 * torch.randn(70000, 3, generator=g)).unsqueeze(0)
+    q = (centres[torch.randint(16, (20000,), generator=g)] +
+         0.5 * torch.randn(20000, 3, generator=g)).unsqueeze(0)
+    q[0, 5] = torch.tensor([100.0, 100.0, 100.0])
+    q[0, 77, 1] = float("nan")
+    want_d, want_i = O.ball_query(q.numpy(), ref.numpy(), 0.3, 32)
+    qc, rc = q.to(cuda_device), ref.to(cuda_device)
+    d, i = mps_pointops.ball_query(qc, rc, 0.3, 32)
+    np.testing.assert_array_equal(i.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(d.cpu().numpy(), want_d)
+    lengths = torch.tensor([20000], device=cuda_device)
+    res = core_ball_query(qc, rc, query_lengths=lengths, radius=0.3, k=32)
+    assert torch.equal(res.indices, i) and torch.equal(res.distances, d)
+    qg = qc.clone().requires_grad_()
+    rg = rc.clone().requires_grad_()
+    dd, _ = mps_pointops.ball_query(qg, rg, 0.3, 32)
+    dd.sum().backward()
+    qh = qc.clone().requires_grad_()
+    rh = rc.clone().requires_grad_()
+    res = core_ball_query(qh, rh, query_lengths=lengths, radius=0.3, k=32)
+    res.distances.sum().backward()
+    torch.testing.assert_close(qg.grad, qh.grad, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(rg.grad, rh.grad, rtol=1e-5, atol=1e-6)
