@@ -230,7 +230,10 @@ MPO_API int mpo_chamfer_backward(const float* x, const float* y, int64_t B, int6
  * arguments and conventions as mpo_chamfer_nearest without a workspace: the
  * distance is |d0| + |d1| + ... in dimension order (d = query - ref, each
  * operation rounded on its own), first minimum with the lowest index on
- * ties; invalid rows get (0, -1). */
+ * ties; invalid rows get (0, -1).  Both directions with D == 3 and P, Q >= 512
+ * run the symmetric tile kernel, which needs scratch: it uses idx_x, idx_y
+ * and the first word of dist_x during the call (all of them are overwritten
+ * with the results). */
 MPO_API int mpo_chamfer_nearest_l1(const float* x, const float* y, const int64_t* x_lengths,
                                    const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q,
                                    int64_t D, int bidirectional, float* dist_x, int64_t* idx_x,

@@ -43,6 +43,16 @@ __device__ __forceinline__ float dist3(float ax, float ay, float az, float bx, f
     return NORM == 1 ? l1d3(ax, ay, az, bx, by, bz) : sqd3(ax, ay, az, bx, by, bz);
 }
 
+// Packed forms for two (a, b) pairs: NORM 2 sqd3x2; NORM 1 ((|d0| + |d1|) +
+// |d2|), the absolute values by clearing both sign bits (exact).
+__device__ __forceinline__ f32x2 abs2(f32x2 v) { return v & 0x7fffffff7fffffffull; }
+template <int NORM>
+__device__ __forceinline__ f32x2 dist3x2(f32x2 ax, f32x2 ay, f32x2 az, f32x2 bx, f32x2 by,
+                                         f32x2 bz) {
+    if (NORM == 2) return sqd3x2(ax, ay, az, bx, by, bz);
+    return add2(add2(abs2(sub2(ax, bx)), abs2(sub2(ay, by))), abs2(sub2(az, bz)));
+}
+
 template <int NORM>
 __global__ void __launch_bounds__(kThreads)
 nearest3_kernel(const float* __restrict__ query, const float* __restrict__ ref,
@@ -214,7 +224,7 @@ struct Shape {
     static constexpr size_t kSmem = kColBytes + (size_t)kWarps * kBN * 8;
 };
 
-template <int kWarps, int kR, int kC, int kBN, int kMinBlocks>
+template <int kWarps, int kR, int kC, int kBN, int kMinBlocks, int NORM = 2>
 __global__ void __launch_bounds__(kWarps * 32, kMinBlocks)
 chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
                     const int64_t* __restrict__ x_lengths, const int64_t* __restrict__ y_lengths,
@@ -305,7 +315,7 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
                     float d[kR];
 #pragma unroll
                     for (int q = 0; q < kR / 2; ++q) {
-                        const f32x2 dd = sqd3x2(X[q], Y[q], Z[q], a.x, a.y, bz);
+                        const f32x2 dd = dist3x2<NORM>(X[q], Y[q], Z[q], a.x, a.y, bz);
                         unpack2(dd, d[2 * q], d[2 * q + 1]);
                     }
 #pragma unroll
@@ -360,7 +370,8 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
                 for (int c = 0; c < kC; ++c) {
                     const int j = blk[k] + c;
                     const float4 pa = s_xy[j];
-                    if (__float_as_uint(sqd3(rx, ry, rz, pa.x, pa.z, s_zf[2 * j])) == best[k]) {
+                    if (__float_as_uint(dist3<NORM>(rx, ry, rz, pa.x, pa.z, s_zf[2 * j])) ==
+                        best[k]) {
                         col = j;
                         break;
                     }
@@ -394,7 +405,8 @@ chamfer_sym3_kernel(const float* __restrict__ x, const float* __restrict__ y,
             for (int k = 0; k < kR; ++k) {
                 const int64_t r = r0 + k;
                 if (r >= xlen) break;
-                const float d = sqd3(xb[3 * r], xb[3 * r + 1], xb[3 * r + 2], pa.x, pa.z, pz);
+                const float d =
+                    dist3<NORM>(xb[3 * r], xb[3 * r + 1], xb[3 * r + 2], pa.x, pa.z, pz);
                 if (__float_as_uint(d) == bv) {
                     row = r;
                     break;
@@ -426,6 +438,26 @@ __global__ void finalize_kernel(const unsigned long long* __restrict__ keys,
     }
     dist[e] = __uint_as_float((unsigned)(key >> 32));
     idx[e] = (int64_t)(key & 0xffffffffull);
+}
+
+// The same with the keys held in the idx array itself (the allocation-free
+// L1 entry): each thread reads its key before it writes its (dist, idx).
+__global__ void finalize_inplace_kernel(int64_t* idx_keys, const int64_t* __restrict__ self_lengths,
+                                        const int64_t* __restrict__ other_lengths, int64_t B,
+                                        int64_t M, int64_t N, float* __restrict__ dist) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= B * M) return;
+    const int64_t b = e / M, i = e % M;
+    const int64_t len = self_lengths ? self_lengths[b] : M;
+    const int64_t olen = other_lengths ? other_lengths[b] : N;
+    const unsigned long long key = static_cast<unsigned long long>(idx_keys[e]);
+    if (i >= len || olen <= 0 || key == kMaxKey) {
+        dist[e] = 0.f;
+        idx_keys[e] = -1;
+        return;
+    }
+    dist[e] = __uint_as_float((unsigned)(key >> 32));
+    idx_keys[e] = (int64_t)(key & 0xffffffffull);
 }
 
 inline bool use_sym(int64_t P, int64_t Q, int64_t D) { return D == 3 && P >= 512 && Q >= 512; }
@@ -840,6 +872,40 @@ int mpo_chamfer_nearest_l1(const float* x, const float* y, const int64_t* x_leng
     MPO_REQUIRE((dist_x && idx_x) || P == 0, "null output pointer");
     MPO_REQUIRE(!bidirectional || (dist_y && idx_y) || Q == 0, "null output pointer");
     cudaStream_t s = (cudaStream_t)stream;
+    if (bidirectional && sym::use_sym(P, Q, D)) {
+        // Both directions from one evaluation per pair (the symmetric tile
+        // kernel with the L1 metric).  This entry takes no workspace: the
+        // 64-bit keys live in the idx arrays until the in-place finalize,
+        // and the work-item counter in the first word of dist_x, which the
+        // finalize overwrites.
+        unsigned long long* keys_x = reinterpret_cast<unsigned long long*>(idx_x);
+        unsigned long long* keys_y = reinterpret_cast<unsigned long long*>(idx_y);
+        unsigned* counter = reinterpret_cast<unsigned*>(dist_x);
+        if (cudaMemsetAsync(keys_x, 0xff, (size_t)B * P * 8, s) != cudaSuccess ||
+            cudaMemsetAsync(keys_y, 0xff, (size_t)B * Q * 8, s) != cudaSuccess ||
+            cudaMemsetAsync(counter, 0, sizeof(unsigned), s) != cudaSuccess)
+            return fail(kCudaError, "mpo_chamfer_nearest_l1: reset failed");
+        auto kern = sym::chamfer_sym3_kernel<MPO_SYM_DEFAULT, 1>;
+        using Sh = sym::Default;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)Sh::kSmem) != cudaSuccess)
+            return fail(kCudaError, "mpo_chamfer_nearest_l1: shared-memory limit");
+        int per_sm = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, Sh::kThreads, Sh::kSmem);
+        const int64_t items = B * ceil_div(P, Sh::kBM) * ceil_div(Q, Sh::kCols);
+        const int64_t grid = min64(items, (int64_t)sm_count() * max64(per_sm, 1));
+        kern<<<(unsigned)grid, Sh::kThreads, Sh::kSmem, s>>>(x, y, x_lengths, y_lengths, B, P, Q,
+                                                             keys_x, keys_y, counter);
+        int st = check_launch("chamfer_sym3_kernel<L1>");
+        if (st) return st;
+        sym::finalize_inplace_kernel<<<(unsigned)ceil_div(B * P, 256), 256, 0, s>>>(
+            idx_x, x_lengths, y_lengths, B, P, Q, dist_x);
+        st = check_launch("chamfer finalize_inplace_kernel");
+        if (st) return st;
+        sym::finalize_inplace_kernel<<<(unsigned)ceil_div(B * Q, 256), 256, 0, s>>>(
+            idx_y, y_lengths, x_lengths, B, Q, P, dist_y);
+        return check_launch("chamfer finalize_inplace_kernel");
+    }
     int st = nearest_l1_dir(x, y, x_lengths, y_lengths, B, P, Q, D, dist_x, idx_x, s);
     if (st || !bidirectional) return st;
     return nearest_l1_dir(y, x, y_lengths, x_lengths, B, Q, P, D, dist_y, idx_y, s);

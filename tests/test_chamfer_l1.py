@@ -95,3 +95,33 @@ def test_l1_nearest_against_oracle_at_scale(cuda_device):
                                 gdx.numpy(), gdy.numpy())
     np.testing.assert_allclose(gx.cpu().numpy(), wx, rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(gy.cpu().numpy(), wy, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.gpu
+def test_l1_symmetric_path_ties_and_single_direction(cuda_device):
+    """Both directions at once (P, Q >= 512, D = 3: the symmetric tile kernel
+    with the L1 metric, keys held in the idx outputs) on an integer lattice,
+    where equal L1 distances are everywhere and the lowest index must win;
+    the one-direction call takes the per-direction kernel."""
+    from mps_pointops import _native as N
+    g = torch.Generator().manual_seed(10)
+    x = torch.randint(0, 5, (2, 1500, 3), generator=g).float()
+    y = torch.randint(0, 5, (2, 1300, 3), generator=g).float()
+    B, P, D = x.shape
+    Q = y.shape[1]
+    xc, yc = x.to(cuda_device), y.to(cuda_device)
+    for bidirectional in (1, 0):
+        dx = torch.full((B, P), 7.0, device=cuda_device)
+        ix = torch.full((B, P), 7, dtype=torch.long, device=cuda_device)
+        dy = torch.full((B, Q), 7.0, device=cuda_device)
+        iy = torch.full((B, Q), 7, dtype=torch.long, device=cuda_device)
+        N.check(N.lib().mpo_chamfer_nearest_l1(N.ptr(xc), N.ptr(yc), None, None, B, P, Q, D,
+                                               bidirectional, N.ptr(dx), N.ptr(ix), N.ptr(dy),
+                                               N.ptr(iy), N.stream(cuda_device)), "l1")
+        want_d, want_i = O.chamfer_nearest(x.numpy(), y.numpy(), norm=1)
+        np.testing.assert_array_equal(ix.cpu().numpy(), want_i)
+        np.testing.assert_array_equal(dx.cpu().numpy(), want_d)
+        if bidirectional:
+            want_d, want_i = O.chamfer_nearest(y.numpy(), x.numpy(), norm=1)
+            np.testing.assert_array_equal(iy.cpu().numpy(), want_i)
+            np.testing.assert_array_equal(dy.cpu().numpy(), want_d)
