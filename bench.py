@@ -60,7 +60,7 @@ def parse_args():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="chamfer_config2",
-                    choices=["chamfer_config2", "ssg_config1_ops", "fps_config3",
+                    choices=["chamfer_config2", "ssg_config1_ops", "fps_config3", "fps_large",
                              "feature_knn_config4", "knn_config5", "ball_query_config5",
                              "flat_ops", "sa_grouping_config1", "chamfer_variants_config2",
                              "config5_grid"],
@@ -294,6 +294,23 @@ def fps_config3(steps: int, warmup: int) -> dict:
             "note": "streaming model: 20 B per point-step (12 B xyz + 4 B read + 4 B write of "
                     "min_d2); the kernel keeps the cloud in registers, so this is the rate an "
                     "HBM-streaming design would need, not DRAM traffic"}
+
+
+def fps_large(steps: int, warmup: int) -> dict:
+    """FPS beyond 8192 points per SM: 4096 samples from jittered-sphere clouds
+    of 1.5 M points (registers + shared-memory tier) and 4 M points
+    (registers + shared memory + workspace tier), start 0; ns per step."""
+    from mps_pointops import furthest_point_sample
+    res = {"workload": "fps_large", "unit": "ns per FPS step (median of CUDA-event runs)"}
+    for n, seed in ((1_500_000, 41), (4_000_000, 42)):
+        g = torch.Generator().manual_seed(seed)
+        p = torch.randn(1, n, 3, generator=g)
+        p = p / p.norm(dim=-1, keepdim=True)
+        p = (p * (1 + 0.01 * torch.randn(1, n, 1, generator=g))).cuda()
+        ms = _event_ms(lambda: furthest_point_sample(p, 4096), max(steps, 1), max(warmup, 1),
+                       None)
+        res[f"n{n}"] = {"ms": ms, "ns_per_step": ms * 1e6 / 4096, "samples": 4096}
+    return res
 
 
 def _config5_cloud(seed: int, n: int) -> torch.Tensor:
@@ -841,6 +858,8 @@ def main():
             out = ssg_config1_ops(steps, max(warmup, 3))
         elif args.workload == "fps_config3":
             out = fps_config3(min(steps, 3), 1)
+        elif args.workload == "fps_large":
+            out = fps_large(min(steps, 5), 1)
         elif args.workload == "config5_grid":
             out = config5_grid(args.queries, min(steps, 5), 1)
         elif args.workload == "chamfer_variants_config2":

@@ -42,7 +42,7 @@ extern "C" {
 #define MPO_API
 #endif
 
-#define MPO_ABI_VERSION 7
+#define MPO_ABI_VERSION 8
 
 #define MPO_OK 0
 #define MPO_ERR_INVALID_ARGUMENT 1
@@ -79,10 +79,13 @@ MPO_API int mpo_device_supported(int device);
  *   0 <= start_idx < N.  strategy mirrors the reference's `strategy=`
  *   argument: MPO_FPS_AUTO picks by size, MPO_FPS_SINGLE runs one CTA per
  *   cloud (N <= 8192), MPO_FPS_GROUP spreads each cloud over a cooperative
- *   group of CTAs (the large-cloud path, selectable at any size).  The
- *   workspace (mpo_fps_workspace_bytes) holds the cross-CTA step slots of the
- *   group path; status_out (nullable, device int32) receives 0, or 1 if a
- *   bounded cross-CTA wait gave up. */
+ *   group of CTAs (the large-cloud path, selectable at any size).  Any
+ *   N < 2^31 is accepted: above 8192 points per SM every SM takes part and
+ *   each CTA keeps its extra points in shared memory and then in the
+ *   workspace.  The workspace (mpo_fps_workspace_bytes) holds the cross-CTA
+ *   step slots of the group path and that overflow tier (16 bytes per point
+ *   beyond 22,528 per SM); status_out (nullable, device int32) receives 0,
+ *   or 1 if a bounded cross-CTA wait gave up. */
 #define MPO_FPS_AUTO 0
 #define MPO_FPS_SINGLE 1
 #define MPO_FPS_GROUP 2
@@ -107,10 +110,13 @@ MPO_API int mpo_fps_gather(const float* xyz, int64_t B, int64_t N, int64_t npoin
  * arguments and results as mpo_fps; the CTA-group path keeps its step slots
  * in a fixed 40 KiB array inside the library (per device) -- enough for any
  * batch on a 148-SM B200, since cooperative waves reuse the slots; a launch
- * that would need more is rejected with MPO_ERR_INVALID_ARGUMENT.  The first
- * call on a device looks the array up (cudaGetSymbolAddress) and should come
- * before any stream capture.  All calls share the array: calls whose GPU
- * work overlaps race on it. */
+ * that would need more, or a cloud above 22,528 points per SM (3,334,144 on
+ * a 148-SM B200, whose extra points would need workspace), is rejected with
+ * MPO_ERR_INVALID_ARGUMENT.  The first call on a device (and the first after
+ * the device's context is replaced, e.g. by cudaDeviceReset) looks the array
+ * up with cudaGetSymbolAddress and should come before any stream capture;
+ * any number of devices is served.  All calls share the array: calls whose
+ * GPU work overlaps race on it. */
 MPO_API int mpo_fps_noalloc(const float* xyz, int64_t B, int64_t N, int64_t npoint,
                             int64_t start_idx, int skip_near_origin, int out_int32, int strategy,
                             void* out, int32_t* status_out, void* stream);
@@ -233,7 +239,9 @@ MPO_API int mpo_chamfer_backward(const float* x, const float* y, int64_t B, int6
  * ties; invalid rows get (0, -1).  Both directions with D == 3 and P, Q >= 512
  * run the symmetric tile kernel, which needs scratch: it uses idx_x, idx_y
  * and the first word of dist_x during the call (all of them are overwritten
- * with the results). */
+ * with the results).  On that path the four outputs must not overlap each
+ * other or the inputs, and idx_x / idx_y must be 8-byte aligned (both are
+ * checked: MPO_ERR_INVALID_ARGUMENT). */
 MPO_API int mpo_chamfer_nearest_l1(const float* x, const float* y, const int64_t* x_lengths,
                                    const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q,
                                    int64_t D, int bidirectional, float* dist_x, int64_t* idx_x,
@@ -247,6 +255,27 @@ MPO_API int mpo_chamfer_l1_backward(const float* x, const float* y, int64_t B, i
                                     const float* grad_dist_x, const int64_t* idx_y,
                                     const float* grad_dist_y, float* grad_x, float* grad_y,
                                     void* stream);
+
+/* float64 Chamfer search: the reference accepts float64 on every device but
+ * MPS (mps_pointops/chamfer.py:101-102, docstring :365) and computes it with
+ * its tiled torch search (chamfer.py:161-212); this replaces that search for
+ * float64 CUDA tensors.  Same arguments and conventions as
+ * mpo_chamfer_nearest (norm 2: squared L2; norm 1: L1) with double inputs
+ * and distances, all arithmetic in double with every operation rounded, in
+ * dimension order; first minimum, lowest index on ties; invalid rows get
+ * (0, -1).  No workspace. */
+MPO_API int mpo_chamfer_nearest_f64(const double* x, const double* y, const int64_t* x_lengths,
+                                    const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q,
+                                    int64_t D, int norm, int bidirectional, double* dist_x,
+                                    int64_t* idx_x, double* dist_y, int64_t* idx_y, void* stream);
+/* Its backward (mps_pointops/chamfer.py:227-251 for norm 2, 269-293 for
+ * norm 1), in double: as mpo_chamfer_backward / mpo_chamfer_l1_backward.
+ * Outputs overwritten. */
+MPO_API int mpo_chamfer_backward_f64(const double* x, const double* y, int64_t B, int64_t P,
+                                     int64_t Q, int64_t D, int norm, const int64_t* idx_x,
+                                     const double* grad_dist_x, const int64_t* idx_y,
+                                     const double* grad_dist_y, double* grad_x, double* grad_y,
+                                     void* stream);
 
 /* Fused loss for chamfer_distance with the common reductions and no weights
  * or normals (mps_pointops/chamfer.py:436-488, PyTorch3D conventions):

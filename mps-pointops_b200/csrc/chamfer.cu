@@ -471,25 +471,273 @@ inline size_t scratch_bytes(int64_t B, int64_t P, int64_t Q) {
 }
 }  // namespace sym
 
+// ---------------------------------------------------------------------------
+// Symmetric tile kernel for D != 3 (feature-space Chamfer, both directions
+// from ONE evaluation per pair, like chamfer_sym3_kernel).  A CTA takes one
+// item (cloud, kBM x rows, kBN y columns):
+//   * x rows are staged transposed in shared memory, [D][kBM], so a lane's two
+//     consecutive rows at dimension t are one packed f32x2 load; y columns as
+//     (y_j, y_j, y_j+1, y_j+1) float4s, [kBN / 2][D], read by warp broadcast.
+//   * Per block of kC = 8 columns the dimension loop accumulates the 16
+//     distances of the lane's two rows in packed registers, in the
+//     reference's order (s = d0*d0, then s = s + dt*dt; L1: |d0| + |d1| ...).
+//   * Row minima: the block minimum per row in registers; the first column of
+//     the winning block is recovered by recomputation.  Column minima: one
+//     redux.sync.min and one ballot per (warp, column) into shared memory,
+//     then the first warp, lane and row holding it.  Both directions commit
+//     64-bit keys (distance bits << 32 | index) with atomicMin, exactly as
+//     the D == 3 kernel, so finalize_kernel and the fused loss serve both.
+template <int kWarps, int kBN>
+struct ShapeD {
+    static constexpr int kThreads = kWarps * 32;
+    static constexpr int kBM = kThreads * 2;  // two rows per lane
+    static constexpr int kC = 8;
+    static size_t smem(int64_t D) {
+        return (size_t)kBM * D * 4 + (size_t)(kBN / 2) * D * 16 + (size_t)kWarps * kBN * 8;
+    }
+};
+// D <= 64: 8 warps x 128 columns (204,800 B of shared memory at D = 64);
+// 64 < D <= 144: 4 warps x 64 columns (223,232 B at D = 144).
+constexpr int64_t kSymDMaxSmall = 64;
+constexpr int64_t kSymDMax = 144;
+
+// One (row, column) distance recomputed from the staged tiles, scalar, in
+// the same order and rounding as the packed loop.
+template <int NORM>
+__device__ __forceinline__ float symd_dist(const float* __restrict__ sx, int kBM, int r,
+                                           const float* __restrict__ sy, int col, int D) {
+    const float* yc = sy + (size_t)(col >> 1) * D * 4 + (col & 1) * 2;
+    float d = __fsub_rn(sx[r], yc[0]);
+    float acc = NORM == 1 ? fabsf(d) : __fmul_rn(d, d);
+    for (int t = 1; t < D; ++t) {
+        d = __fsub_rn(sx[(size_t)t * kBM + r], yc[(size_t)t * 4]);
+        acc = __fadd_rn(acc, NORM == 1 ? fabsf(d) : __fmul_rn(d, d));
+    }
+    return acc;
+}
+
+template <int kWarps, int kBN, int NORM>
+__global__ void __launch_bounds__(kWarps * 32)
+chamfer_symd_kernel(const float* __restrict__ x, const float* __restrict__ y,
+                    const int64_t* __restrict__ x_lengths, const int64_t* __restrict__ y_lengths,
+                    int64_t B, int64_t P, int64_t Q, int D,
+                    unsigned long long* __restrict__ keys_x,
+                    unsigned long long* __restrict__ keys_y) {
+    using S = ShapeD<kWarps, kBN>;
+    constexpr int kThreads = S::kThreads, kBM = S::kBM, kC = S::kC;
+    extern __shared__ float4 smem4[];
+    float* s_x = reinterpret_cast<float*>(smem4);                       // [D][kBM]
+    float4* s_y = smem4 + (size_t)kBM * D / 4;                          // [kBN/2][D]
+    unsigned long long* s_part =
+        reinterpret_cast<unsigned long long*>(s_y + (size_t)(kBN / 2) * D);  // [kWarps][kBN]
+    const float* s_yf = reinterpret_cast<const float*>(s_y);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t row_blocks = ceil_div(P, kBM), col_blocks = ceil_div(Q, kBN);
+    const int64_t item = blockIdx.x;
+    const int64_t b = item / (row_blocks * col_blocks);
+    const int64_t rem = item % (row_blocks * col_blocks);
+    const int64_t i0 = (rem / col_blocks) * kBM, j0 = (rem % col_blocks) * kBN;
+    const int64_t xlen = x_lengths ? min64(max64(x_lengths[b], 0), P) : P;
+    const int64_t ylen = y_lengths ? min64(max64(y_lengths[b], 0), Q) : Q;
+    if (i0 >= xlen || j0 >= ylen) return;  // uniform: nothing valid here
+    const float* __restrict__ xb = x + (size_t)b * P * D;
+    const float* __restrict__ yb = y + (size_t)b * Q * D;
+
+    // Stage: a thread per x row (conflict-free transposed stores), a thread
+    // per y column pair; padding is +inf (ties only at +inf, where the lower
+    // valid index wins; padding x padding is NaN, which never wins).
+    for (int r = tid; r < kBM; r += kThreads) {
+        const int64_t gr = i0 + r;
+        const bool ok = gr < xlen;
+        const float* src = xb + (size_t)gr * D;
+        for (int t = 0; t < D; ++t) s_x[(size_t)t * kBM + r] = ok ? src[t] : INFINITY;
+    }
+    for (int cp = tid; cp < kBN / 2; cp += kThreads) {
+        const int64_t j = j0 + 2 * cp;
+        const bool ok0 = j < ylen, ok1 = j + 1 < ylen;
+        const float* s0 = yb + (size_t)j * D;
+        for (int t = 0; t < D; ++t) {
+            const float a = ok0 ? s0[t] : INFINITY;
+            const float c = ok1 ? s0[D + t] : INFINITY;
+            s_y[(size_t)cp * D + t] = make_float4(a, a, c, c);
+        }
+    }
+    __syncthreads();
+
+    const int lrow = (warp * 32 + lane) * 2;
+    const f32x2* xcol = reinterpret_cast<const f32x2*>(s_x + lrow);  // stride kBM / 2 pairs
+    uint32_t best[2] = {0xffffffffu, 0xffffffffu};
+    int blk[2] = {-1, -1};
+    for (int jb = 0; jb < kBN; jb += kC) {
+        const ulonglong2* yv = reinterpret_cast<const ulonglong2*>(s_y + (size_t)(jb >> 1) * D);
+        f32x2 acc[kC];
+        {
+            const f32x2 X = xcol[0];
+#pragma unroll
+            for (int cp = 0; cp < kC / 2; ++cp) {
+                const ulonglong2 yy = yv[(size_t)cp * D];
+                const f32x2 d0 = sub2(X, yy.x), d1 = sub2(X, yy.y);
+                acc[2 * cp] = NORM == 1 ? abs2(d0) : sq2(d0);
+                acc[2 * cp + 1] = NORM == 1 ? abs2(d1) : sq2(d1);
+            }
+        }
+        for (int t = 1; t < D; ++t) {
+            const f32x2 X = xcol[(size_t)t * (kBM / 2)];
+#pragma unroll
+            for (int cp = 0; cp < kC / 2; ++cp) {
+                const ulonglong2 yy = yv[(size_t)cp * D + t];
+                const f32x2 d0 = sub2(X, yy.x), d1 = sub2(X, yy.y);
+                acc[2 * cp] = add2(acc[2 * cp], NORM == 1 ? abs2(d0) : sq2(d0));
+                acc[2 * cp + 1] = add2(acc[2 * cp + 1], NORM == 1 ? abs2(d1) : sq2(d1));
+            }
+        }
+        float m0 = INFINITY, m1 = INFINITY;
+        unsigned pmin[kC], pmask[kC];
+#pragma unroll
+        for (int c = 0; c < kC; ++c) {
+            float d0, d1;
+            unpack2(acc[c], d0, d1);
+            m0 = c == 0 ? d0 : fminf(m0, d0);
+            m1 = c == 0 ? d1 : fminf(m1, d1);
+            const unsigned cb = __float_as_uint(fminf(d0, d1));
+            pmin[c] = __reduce_min_sync(FULL_MASK, cb);
+            pmask[c] = __ballot_sync(FULL_MASK, cb == pmin[c]);
+        }
+        if (lane < kC) {
+            unsigned v = pmin[0], mk = pmask[0];
+#pragma unroll
+            for (int c = 1; c < kC; ++c) {
+                if (lane == c) {
+                    v = pmin[c];
+                    mk = pmask[c];
+                }
+            }
+            s_part[warp * kBN + jb + lane] = ((unsigned long long)v << 32) | mk;
+        }
+        const uint32_t mb0 = __float_as_uint(m0), mb1 = __float_as_uint(m1);
+        if (mb0 < best[0]) {
+            best[0] = mb0;
+            blk[0] = jb;
+        }
+        if (mb1 < best[1]) {
+            best[1] = mb1;
+            blk[1] = jb;
+        }
+    }
+
+    // Rows: the first column of the winning block, then commit.
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int64_t r = i0 + lrow + k;
+        if (r < xlen && blk[k] >= 0) {
+            int col = blk[k];
+            for (int c = 0; c < kC; ++c) {
+                const int j = blk[k] + c;
+                if (__float_as_uint(symd_dist<NORM>(s_x, kBM, lrow + k, s_yf, j, D)) == best[k]) {
+                    col = j;
+                    break;
+                }
+            }
+            atomicMin(&keys_x[(size_t)b * P + r],
+                      ((unsigned long long)best[k] << 32) | (unsigned long long)(j0 + col));
+        }
+    }
+    __syncthreads();
+    // Columns: first warp, first lane, first row holding the minimum.
+    for (int e = tid; e < kBN; e += kThreads) {
+        const int64_t j = j0 + e;
+        if (j >= ylen) continue;
+        unsigned bv = 0xffffffffu, bm = 0u;
+        int bw = 0;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const unsigned long long pv = s_part[w * kBN + e];
+            const unsigned v = (unsigned)(pv >> 32);
+            if (v < bv) {
+                bv = v;
+                bw = w;
+                bm = (unsigned)pv;
+            }
+        }
+        const int l = __ffs(bm) - 1;
+        const int r0 = (bw * 32 + l) * 2;
+        int row = r0;
+        for (int k = 0; k < 2; ++k) {
+            if (i0 + r0 + k >= xlen) break;
+            if (__float_as_uint(symd_dist<NORM>(s_x, kBM, r0 + k, s_yf, e, D)) == bv) {
+                row = r0 + k;
+                break;
+            }
+        }
+        atomicMin(&keys_y[(size_t)b * Q + j],
+                  ((unsigned long long)bv << 32) | (unsigned long long)(i0 + row));
+    }
+}
+
+inline bool use_symd(int64_t P, int64_t Q, int64_t D) {
+    return D != 3 && D <= kSymDMax && P >= 1 && Q >= 1;
+}
+
+// Launch of the D != 3 symmetric kernel over every item; keys pre-set to all
+// ones by the caller.
+template <int NORM>
+int launch_symd(const float* x, const float* y, const int64_t* xl, const int64_t* yl, int64_t B,
+                int64_t P, int64_t Q, int64_t D, unsigned long long* keys_x,
+                unsigned long long* keys_y, cudaStream_t s, const char* who) {
+    auto run = [&](auto kern, int threads, int64_t bm, int64_t bn, size_t smem) -> int {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return fail(kCudaError, std::string(who) + ": shared-memory limit");
+        const int64_t items = B * ceil_div(P, bm) * ceil_div(Q, bn);
+        if (items > 0x7fffffff)
+            return fail(kUnsupported, std::string(who) + ": too many tiles for one launch");
+        kern<<<(unsigned)items, threads, smem, s>>>(x, y, xl, yl, B, P, Q, (int)D, keys_x, keys_y);
+        return check_launch("chamfer_symd_kernel");
+    };
+    if (D <= kSymDMaxSmall) {
+        using Sh = ShapeD<8, 128>;
+        return run(chamfer_symd_kernel<8, 128, NORM>, Sh::kThreads, Sh::kBM, 128, Sh::smem(D));
+    }
+    using Sh = ShapeD<4, 64>;
+    return run(chamfer_symd_kernel<4, 64, NORM>, Sh::kThreads, Sh::kBM, 64, Sh::smem(D));
+}
+
 // Generic D (feature-space Chamfer): query row and reference tile in shared
 // memory, SD accumulated in increasing dimension order.
 constexpr int kDThreads = 128;
 
-// L1 distance in dimension order: |d0| + |d1| + ... (mps_pointops/chamfer.py:194-197).
-__device__ __forceinline__ float l1_seq(const float* a, const float* b, int D) {
-    float s = fabsf(__fsub_rn(a[0], b[0]));
-    for (int t = 1; t < D; ++t) s = __fadd_rn(s, fabsf(__fsub_rn(a[t], b[t])));
+
+// Separately rounded arithmetic for float and double (the float64 Chamfer of
+// mps_pointops/chamfer.py:101-102 runs the same kernels in double).
+__device__ __forceinline__ float rn_sub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ double rn_sub(double a, double b) { return __dsub_rn(a, b); }
+__device__ __forceinline__ float rn_mul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ double rn_mul(double a, double b) { return __dmul_rn(a, b); }
+__device__ __forceinline__ float rn_add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ double rn_add(double a, double b) { return __dadd_rn(a, b); }
+
+template <int NORM, typename T>
+__device__ __forceinline__ T dist_seq(const T* a, const T* b, int D) {
+    T d = rn_sub(a[0], b[0]);
+    T s = NORM == 1 ? fabs(d) : rn_mul(d, d);
+    for (int t = 1; t < D; ++t) {
+        d = rn_sub(a[t], b[t]);
+        s = rn_add(s, NORM == 1 ? fabs(d) : rn_mul(d, d));
+    }
     return s;
 }
 
-// NORM 2: squared L2 (sequential sum of squares); NORM 1: L1.
-template <int NORM>
+// NORM 2: squared L2 (sequential sum of squares); NORM 1: L1.  T = float, or
+// double for the float64 entry points (every D, D == 3 included: the
+// sequential sum is the reference's ((d0^2 + d1^2) + d2^2) order).
+template <int NORM, typename T = float>
 __global__ void __launch_bounds__(kDThreads)
-nearestd_kernel(const float* __restrict__ query, const float* __restrict__ ref,
+nearestd_kernel(const T* __restrict__ query, const T* __restrict__ ref,
                 const int64_t* __restrict__ query_lengths, const int64_t* __restrict__ ref_lengths,
-                int64_t M, int64_t N, int D, int tileN, float* __restrict__ out_dist,
+                int64_t M, int64_t N, int D, int tileN, T* __restrict__ out_dist,
                 int64_t* __restrict__ out_idx) {
-    extern __shared__ float smemf[];
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T* smemf = reinterpret_cast<T*>(smem_raw);
     const int tid = threadIdx.x;
     const int b = blockIdx.y;
     const int64_t q = (int64_t)blockIdx.x * kDThreads + tid;
@@ -497,16 +745,16 @@ nearestd_kernel(const float* __restrict__ query, const float* __restrict__ ref,
     const int64_t nl = ref_lengths ? min64(ref_lengths[b], N) : N;
     const bool active = q < M && q < qlen;
     const int qs = D + 1;
-    float* sq = smemf;
-    float* st = smemf + (size_t)kDThreads * qs;
+    T* sq = smemf;
+    T* st = smemf + (size_t)kDThreads * qs;
     for (int e = tid; e < kDThreads * D; e += kDThreads) {
         const int qq = e / D, t = e % D;
         const int64_t gq = (int64_t)blockIdx.x * kDThreads + qq;
-        sq[qq * qs + t] = gq < M ? query[((size_t)b * M + gq) * D + t] : 0.f;
+        sq[qq * qs + t] = gq < M ? query[((size_t)b * M + gq) * D + t] : T(0);
     }
-    const float* __restrict__ r = ref + (size_t)b * (size_t)N * D;
-    const float* myq = sq + tid * qs;
-    float bd = INFINITY;
+    const T* __restrict__ r = ref + (size_t)b * (size_t)N * D;
+    const T* myq = sq + tid * qs;
+    T bd = T(INFINITY);
     uint32_t bj = kNone;
     for (int64_t t0 = 0; t0 < nl; t0 += tileN) {
         __syncthreads();
@@ -516,18 +764,8 @@ nearestd_kernel(const float* __restrict__ query, const float* __restrict__ ref,
         if (!active) continue;
         const int cnt = (int)min64(tileN, nl - t0);
         for (int e = 0; e < cnt; ++e) {
-            const float* rp = st + (size_t)e * D;
-            float s;
-            if (NORM == 1) {
-                s = l1_seq(myq, rp, D);
-            } else {
-                float dd = __fsub_rn(myq[0], rp[0]);
-                s = __fmul_rn(dd, dd);
-                for (int u = 1; u < D; ++u) {
-                    dd = __fsub_rn(myq[u], rp[u]);
-                    s = __fadd_rn(s, __fmul_rn(dd, dd));
-                }
-            }
+            const T* rp = st + (size_t)e * D;
+            const T s = dist_seq<NORM>(myq, rp, D);
             if (s < bd) {
                 bd = s;
                 bj = (uint32_t)(t0 + e);
@@ -537,13 +775,13 @@ nearestd_kernel(const float* __restrict__ query, const float* __restrict__ ref,
     if (q >= M) return;
     const size_t o = (size_t)b * (size_t)M + (size_t)q;
     if (!active || nl <= 0) {
-        out_dist[o] = 0.f;
+        out_dist[o] = T(0);
         out_idx[o] = -1;
         return;
     }
     if (bj == kNone) {
         bj = 0;
-        bd = NORM == 1 ? l1_seq(query + o * D, r, D) : sqd_seq(query + o * D, r, D);
+        bd = dist_seq<NORM>(query + o * D, r, D);
     }
     out_dist[o] = bd;
     out_idx[o] = (int64_t)bj;
@@ -551,22 +789,23 @@ nearestd_kernel(const float* __restrict__ query, const float* __restrict__ ref,
 
 // Backward for one direction: rows with idx >= 0 add
 // g = 2 * gd * (q - r[idx]) to grad_q and -g to grad_r[idx].
-__global__ void chamfer_bwd_kernel(const float* __restrict__ qpts, const float* __restrict__ rpts,
+template <typename T = float>
+__global__ void chamfer_bwd_kernel(const T* __restrict__ qpts, const T* __restrict__ rpts,
                                    int64_t B, int64_t M, int64_t N, int64_t D,
-                                   const int64_t* __restrict__ idx, const float* __restrict__ gd,
-                                   float* __restrict__ grad_q, float* __restrict__ grad_r) {
+                                   const int64_t* __restrict__ idx, const T* __restrict__ gd,
+                                   T* __restrict__ grad_q, T* __restrict__ grad_r) {
     const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= B * M) return;
     const int64_t j = idx[row];
     if (j < 0) return;
     const int64_t b = row / M;
-    const float c = 2.0f * gd[row];
-    const float* qp = qpts + row * D;
-    const float* rp = rpts + (b * N + j) * D;
-    float* gq = grad_q + row * D;
-    float* gr = grad_r + (b * N + j) * D;
+    const T c = T(2) * gd[row];
+    const T* qp = qpts + row * D;
+    const T* rp = rpts + (b * N + j) * D;
+    T* gq = grad_q + row * D;
+    T* gr = grad_r + (b * N + j) * D;
     for (int64_t t = 0; t < D; ++t) {
-        const float g = __fmul_rn(__fsub_rn(qp[t], rp[t]), c);
+        const T g = rn_mul(rn_sub(qp[t], rp[t]), c);
         atomicAdd(gq + t, g);
         atomicAdd(gr + t, -g);
     }
@@ -575,23 +814,24 @@ __global__ void chamfer_bwd_kernel(const float* __restrict__ qpts, const float* 
 // L1 backward for one direction (mps_pointops/chamfer.py:269-293, PyTorch3D's
 // subgradient): rows with idx >= 0 add g = s * gd, s = +1 where q > r[idx]
 // and -1 otherwise (at equality too), to grad_q and -g to grad_r[idx].
-__global__ void chamfer_l1_bwd_kernel(const float* __restrict__ qpts,
-                                      const float* __restrict__ rpts, int64_t B, int64_t M,
+template <typename T = float>
+__global__ void chamfer_l1_bwd_kernel(const T* __restrict__ qpts,
+                                      const T* __restrict__ rpts, int64_t B, int64_t M,
                                       int64_t N, int64_t D, const int64_t* __restrict__ idx,
-                                      const float* __restrict__ gd, float* __restrict__ grad_q,
-                                      float* __restrict__ grad_r) {
+                                      const T* __restrict__ gd, T* __restrict__ grad_q,
+                                      T* __restrict__ grad_r) {
     const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= B * M) return;
     const int64_t j = idx[row];
     if (j < 0) return;
     const int64_t b = row / M;
-    const float c = gd[row];
-    const float* qp = qpts + row * D;
-    const float* rp = rpts + (b * N + j) * D;
-    float* gq = grad_q + row * D;
-    float* gr = grad_r + (b * N + j) * D;
+    const T c = gd[row];
+    const T* qp = qpts + row * D;
+    const T* rp = rpts + (b * N + j) * D;
+    T* gq = grad_q + row * D;
+    T* gr = grad_r + (b * N + j) * D;
     for (int64_t t = 0; t < D; ++t) {
-        const float g = qp[t] > rp[t] ? c : -c;
+        const T g = qp[t] > rp[t] ? c : -c;
         atomicAdd(gq + t, g);
         atomicAdd(gr + t, -g);
     }
@@ -790,8 +1030,8 @@ extern "C" {
 
 size_t mpo_chamfer_workspace_bytes(int64_t B, int64_t P, int64_t Q, int64_t D,
                                    int bidirectional) {
-    (void)bidirectional;
-    if (B <= 0 || !mpo::sym::use_sym(P, Q, D)) return 0;
+    if (B <= 0 || !(mpo::sym::use_sym(P, Q, D) || (bidirectional && mpo::use_symd(P, Q, D))))
+        return 0;
     return mpo::sym::scratch_bytes(B, P, Q);
 }
 
@@ -872,12 +1112,37 @@ int mpo_chamfer_nearest_l1(const float* x, const float* y, const int64_t* x_leng
     MPO_REQUIRE((dist_x && idx_x) || P == 0, "null output pointer");
     MPO_REQUIRE(!bidirectional || (dist_y && idx_y) || Q == 0, "null output pointer");
     cudaStream_t s = (cudaStream_t)stream;
-    if (bidirectional && sym::use_sym(P, Q, D)) {
+    if (bidirectional && (sym::use_sym(P, Q, D) || use_symd(P, Q, D))) {
         // Both directions from one evaluation per pair (the symmetric tile
         // kernel with the L1 metric).  This entry takes no workspace: the
         // 64-bit keys live in the idx arrays until the in-place finalize,
         // and the work-item counter in the first word of dist_x, which the
         // finalize overwrites.
+        // The scratch lives in the outputs, so they must not overlap each
+        // other or the inputs, and the key arrays need 8-byte alignment.
+        {
+            const size_t nx = (size_t)B * P, ny = (size_t)B * Q;
+            const struct {
+                const void* p;
+                size_t bytes;
+            } in[2] = {{x, nx * D * 4}, {y, ny * D * 4}},
+              out[4] = {{dist_x, nx * 4}, {idx_x, nx * 8}, {dist_y, ny * 4}, {idx_y, ny * 8}};
+            auto overlap = [](const void* a, size_t na, const void* b, size_t nb) {
+                const uintptr_t ua = reinterpret_cast<uintptr_t>(a);
+                const uintptr_t ub = reinterpret_cast<uintptr_t>(b);
+                return na > 0 && nb > 0 && ua < ub + nb && ub < ua + na;
+            };
+            for (int i = 0; i < 4; ++i) {
+                for (int j = i + 1; j < 4; ++j)
+                    MPO_REQUIRE(!overlap(out[i].p, out[i].bytes, out[j].p, out[j].bytes),
+                                "the four outputs must not overlap each other");
+                for (int j = 0; j < 2; ++j)
+                    MPO_REQUIRE(!overlap(out[i].p, out[i].bytes, in[j].p, in[j].bytes),
+                                "the outputs must not overlap the inputs");
+            }
+            MPO_REQUIRE(aligned_to(idx_x, 8) && aligned_to(idx_y, 8),
+                        "idx_x and idx_y must be 8-byte aligned");
+        }
         unsigned long long* keys_x = reinterpret_cast<unsigned long long*>(idx_x);
         unsigned long long* keys_y = reinterpret_cast<unsigned long long*>(idx_y);
         unsigned* counter = reinterpret_cast<unsigned*>(dist_x);
@@ -885,6 +1150,18 @@ int mpo_chamfer_nearest_l1(const float* x, const float* y, const int64_t* x_leng
             cudaMemsetAsync(keys_y, 0xff, (size_t)B * Q * 8, s) != cudaSuccess ||
             cudaMemsetAsync(counter, 0, sizeof(unsigned), s) != cudaSuccess)
             return fail(kCudaError, "mpo_chamfer_nearest_l1: reset failed");
+        if (use_symd(P, Q, D)) {
+            int st = launch_symd<1>(x, y, x_lengths, y_lengths, B, P, Q, D, keys_x, keys_y, s,
+                                    "mpo_chamfer_nearest_l1");
+            if (st) return st;
+            sym::finalize_inplace_kernel<<<(unsigned)ceil_div(B * P, 256), 256, 0, s>>>(
+                idx_x, x_lengths, y_lengths, B, P, Q, dist_x);
+            st = check_launch("chamfer finalize_inplace_kernel");
+            if (st) return st;
+            sym::finalize_inplace_kernel<<<(unsigned)ceil_div(B * Q, 256), 256, 0, s>>>(
+                idx_y, y_lengths, x_lengths, B, Q, P, dist_y);
+            return check_launch("chamfer finalize_inplace_kernel");
+        }
         auto kern = sym::chamfer_sym3_kernel<MPO_SYM_DEFAULT, 1>;
         using Sh = sym::Default;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -926,7 +1203,8 @@ int chamfer_search(const float* x, const float* y, const int64_t* x_lengths,
                    unsigned long long** keys_x_out, unsigned long long** keys_y_out,
                    const char* who) {
     *keys_x_out = *keys_y_out = nullptr;
-    if (!sym::use_sym(P, Q, D)) {
+    const bool symd = bidirectional && use_symd(P, Q, D);
+    if (!sym::use_sym(P, Q, D) && !symd) {
         int st = nearest_dir(x, y, x_lengths, y_lengths, B, P, Q, D, dist_x, idx_x, s);
         if (st || !bidirectional) return st;
         return nearest_dir(y, x, y_lengths, x_lengths, B, Q, P, D, dist_y, idx_y, s);
@@ -941,6 +1219,11 @@ int chamfer_search(const float* x, const float* y, const int64_t* x_lengths,
     if (cudaMemsetAsync(keys_x, 0xff, (size_t)B * (P + Q) * 8, s) != cudaSuccess ||
         cudaMemsetAsync(counter, 0, sizeof(unsigned), s) != cudaSuccess)
         return fail(kCudaError, std::string(who) + ": scratch reset failed");
+    if (symd) {
+        *keys_x_out = keys_x;
+        *keys_y_out = keys_y;
+        return launch_symd<2>(x, y, x_lengths, y_lengths, B, P, Q, D, keys_x, keys_y, s, who);
+    }
     auto kern = sym::chamfer_sym3_kernel<MPO_SYM_DEFAULT>;
     using Sh = sym::Default;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -967,8 +1250,10 @@ int check_sizes(int64_t B, int64_t P, int64_t Q, int64_t D, const char* who) {
 }
 
 // Loss workspace: the search scratch, then partial[B][2] and per_cloud[B].
-size_t loss_extra_offset(int64_t B, int64_t P, int64_t Q, int64_t D) {
-    return sym::use_sym(P, Q, D) ? (sym::scratch_bytes(B, P, Q) + 255) / 256 * 256 : 0;
+size_t loss_extra_offset(int64_t B, int64_t P, int64_t Q, int64_t D, int bidirectional) {
+    return (sym::use_sym(P, Q, D) || (bidirectional && use_symd(P, Q, D)))
+               ? (sym::scratch_bytes(B, P, Q) + 255) / 256 * 256
+               : 0;
 }
 }  // namespace
 }  // namespace mpo
@@ -1001,9 +1286,8 @@ int mpo_chamfer_nearest(const float* x, const float* y, const int64_t* x_lengths
 
 size_t mpo_chamfer_loss_workspace_bytes(int64_t B, int64_t P, int64_t Q, int64_t D,
                                         int bidirectional) {
-    (void)bidirectional;
     if (B <= 0) return 0;
-    return mpo::loss_extra_offset(B, P, Q, D) + (size_t)B * 3 * sizeof(float);
+    return mpo::loss_extra_offset(B, P, Q, D, bidirectional) + (size_t)B * 3 * sizeof(float);
 }
 
 int mpo_chamfer_loss(const float* x, const float* y, const int64_t* x_lengths,
@@ -1034,7 +1318,7 @@ int mpo_chamfer_loss(const float* x, const float* y, const int64_t* x_lengths,
                         "mpo_chamfer_loss");
     if (st) return st;
     float* partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) +
-                                              loss_extra_offset(B, P, Q, D));
+                                              loss_extra_offset(B, P, Q, D, bidirectional));
     float* per_cloud = partial + 2 * B;
     dim3 grid((unsigned)B, bidirectional ? 2u : 1u);
     if (keys_x)
@@ -1124,6 +1408,74 @@ int mpo_chamfer_l1_backward(const float* x, const float* y, int64_t B, int64_t P
         chamfer_l1_bwd_kernel<<<(unsigned)ceil_div(B * Q, 256), 256, 0, s>>>(
             y, x, B, Q, P, D, idx_y, grad_dist_y, grad_y, grad_x);
         return check_launch("chamfer_l1_bwd_kernel");
+    }
+    return kOk;
+}
+
+int mpo_chamfer_nearest_f64(const double* x, const double* y, const int64_t* x_lengths,
+                            const int64_t* y_lengths, int64_t B, int64_t P, int64_t Q, int64_t D,
+                            int norm, int bidirectional, double* dist_x, int64_t* idx_x,
+                            double* dist_y, int64_t* idx_y, void* stream) {
+    using namespace mpo;
+    int st = check_sizes(B, P, Q, D, "mpo_chamfer_nearest_f64");
+    if (st) return st;
+    MPO_REQUIRE(norm == 1 || norm == 2, "norm must be 1 or 2");
+    if (B == 0) return kOk;
+    MPO_REQUIRE((x || P == 0) && (y || Q == 0), "null pointer");
+    MPO_REQUIRE((dist_x && idx_x) || P == 0, "null output pointer");
+    MPO_REQUIRE(!bidirectional || (dist_y && idx_y) || Q == 0, "null output pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    int tileN = 256;
+    auto bytes = [&](int tn) {
+        return ((size_t)kDThreads * (D + 1) + (size_t)tn * D) * sizeof(double);
+    };
+    while (bytes(tileN) > 200 * 1024 && tileN > 1) tileN /= 2;
+    if (bytes(tileN) > 200 * 1024)
+        return fail(kUnsupported, "mpo_chamfer_nearest_f64: coordinate dimension too large");
+    const size_t smem = bytes(tileN);
+    auto run = [&](auto kern, const double* q, const double* r, const int64_t* ql,
+                   const int64_t* rl, int64_t M, int64_t N, double* dist, int64_t* idx) -> int {
+        if (M == 0) return kOk;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return fail(kCudaError, "mpo_chamfer_nearest_f64: shared-memory limit");
+        dim3 grid((unsigned)ceil_div(M, kDThreads), (unsigned)B);
+        kern<<<grid, kDThreads, smem, s>>>(q, r, ql, rl, M, N, (int)D, tileN, dist, idx);
+        return check_launch("nearestd_kernel<f64>");
+    };
+    auto kern = norm == 1 ? nearestd_kernel<1, double> : nearestd_kernel<2, double>;
+    st = run(kern, x, y, x_lengths, y_lengths, P, Q, dist_x, idx_x);
+    if (st || !bidirectional) return st;
+    return run(kern, y, x, y_lengths, x_lengths, Q, P, dist_y, idx_y);
+}
+
+int mpo_chamfer_backward_f64(const double* x, const double* y, int64_t B, int64_t P, int64_t Q,
+                             int64_t D, int norm, const int64_t* idx_x,
+                             const double* grad_dist_x, const int64_t* idx_y,
+                             const double* grad_dist_y, double* grad_x, double* grad_y,
+                             void* stream) {
+    using namespace mpo;
+    MPO_REQUIRE(B >= 0 && P >= 0 && Q >= 0 && D >= 1, "bad sizes");
+    MPO_REQUIRE(norm == 1 || norm == 2, "norm must be 1 or 2");
+    MPO_REQUIRE((grad_x || B * P * D == 0) && (grad_y || B * Q * D == 0), "null gradient pointer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (B * P * D > 0 && cudaMemsetAsync(grad_x, 0, sizeof(double) * B * P * D, s) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_backward_f64: memset failed");
+    if (B * Q * D > 0 && cudaMemsetAsync(grad_y, 0, sizeof(double) * B * Q * D, s) != cudaSuccess)
+        return fail(kCudaError, "mpo_chamfer_backward_f64: memset failed");
+    auto kern = norm == 1 ? chamfer_l1_bwd_kernel<double> : chamfer_bwd_kernel<double>;
+    if (grad_dist_x && B * P > 0) {
+        MPO_REQUIRE(idx_x, "null pointer");
+        kern<<<(unsigned)ceil_div(B * P, 256), 256, 0, s>>>(x, y, B, P, Q, D, idx_x, grad_dist_x,
+                                                            grad_x, grad_y);
+        int st = check_launch("chamfer_bwd_kernel<f64>");
+        if (st) return st;
+    }
+    if (grad_dist_y && B * Q > 0) {
+        MPO_REQUIRE(idx_y, "null pointer");
+        kern<<<(unsigned)ceil_div(B * Q, 256), 256, 0, s>>>(y, x, B, Q, P, D, idx_y, grad_dist_y,
+                                                            grad_y, grad_x);
+        return check_launch("chamfer_bwd_kernel<f64>");
     }
     return kOk;
 }

@@ -21,15 +21,23 @@
 //     shared memory so the next centroid is a shared-memory load.
 //   * G > 1 (large clouds: 2^20 points on 128 SMs): a
 //     cooperative launch makes the group co-resident.  Each CTA publishes its
-//     best as one 64-bit word (ordered distance key << 32 | step sequence
-//     << 21 | index) into its slot of a double-buffered slot array (buffer =
-//     step parity), and one warp of every CTA polls the G slots with
-//     ld.relaxed.gpu until all carry the current step's sequence, then
-//     reduces them itself -- no atomics and one cross-SM round trip per step.
-//     The poll is bounded in time (kSpinLimitNs of %globaltimer); on expiry
-//     the CTA records status 1, raises the group's error word and returns.
+//     best as one 64-bit word (ordered distance key << 32 | 8-bit step
+//     sequence << 24 | index local to the CTA) into its slot of a
+//     double-buffered slot array (buffer = step parity), and one warp of
+//     every CTA polls the G slots with ld.relaxed.gpu until all carry the
+//     current step's sequence, then reduces them itself -- no atomics and one
+//     cross-SM round trip per step.  The poll is bounded in time
+//     (kSpinLimitNs of %globaltimer); on expiry the CTA records status 1,
+//     raises the group's error word and returns.
+//   * Clouds above 8192 points per SM (more than 1,212,416 points on a
+//     148-SM B200) use every SM; a CTA keeps its first 8192 points in
+//     registers and the rest as float4 (x, y, z, min_d2) records, first in
+//     shared memory (up to kSmemTierPoints, 224 KiB) and beyond that in the
+//     caller's workspace (L2-resident for clouds of a few million points),
+//     streamed once per step.  Any N below 2^31 is accepted.
 #include <cooperative_groups.h>
 
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -43,17 +51,64 @@ constexpr int kMaxThreads = 256;
 constexpr int kMaxP = 32;
 constexpr int64_t kPointsPerCta = (int64_t)kMaxThreads * kMaxP;  // 8192
 constexpr unsigned long long kSpinLimitNs = 2000000000ull;  // 2 s per step
-constexpr int kIndexBits = 21;  // group path: N <= 8192 * 148 < 2^21
-constexpr unsigned long long kIndexMask = (1ull << kIndexBits) - 1;
+// Step word of the group path: ordered key (32) | step sequence (8) | index
+// of the point within its CTA's range (24).  The reader adds c * per_cta.
+// Two steps apart differ in the sequence, which is all the double buffer
+// needs; 24 local bits cover per_cta < 2^24 (every N < 2^31 on >= 128 SMs).
+constexpr int kLocalBits = 24;
+constexpr unsigned long long kLocalMask = (1ull << kLocalBits) - 1;
+constexpr unsigned long long kSeqMask = 0xffull;
+// Overflow tier in shared memory: float4 (x, y, z, min_d2) per point.
+constexpr int kSmemTierPoints = 14336;  // 224 KiB
 
 // Cross-CTA exchange state of the clouds of one cooperative wave, in the
 // caller's workspace (zeroed before each wave):
 //   slots[cloud_in_wave][parity][G]  one u64 per 128-byte line, so the G
 //                                    readers of a step spread over G lines
 //   error[cloud_in_wave]             u32
+// followed, 256-byte aligned, by the overflow tier in global memory:
+//   ovf[cloud_in_wave][G][global_pts] float4 (written by the kernel itself)
 constexpr int kSlotStride = 16;  // u64 words per slot (128 bytes)
 inline size_t group_bytes(int64_t clouds, int64_t G) {
     return (size_t)clouds * 2 * (size_t)G * 8 * kSlotStride + (size_t)clouds * 8;
+}
+inline size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+inline size_t group_total_bytes(int64_t clouds, int64_t G, int64_t global_pts) {
+    const size_t slots = group_bytes(clouds, G);
+    if (global_pts <= 0) return slots;
+    return align256(slots) + (size_t)clouds * (size_t)G * (size_t)global_pts * sizeof(float4);
+}
+
+// One overflow tier of a CTA (records t[e0 .. e1) of index jbase + e), the
+// thread taking e = tid, tid + nthr, ... from `e` on; min_d2 is updated in
+// place (stored only when it changes) and the thread's first maximum is
+// tracked as in the register tier: a float compare on the finite path, the
+// NaN-ranking key otherwise.
+template <bool NANM>
+__device__ __forceinline__ void ovf_scan(float4* __restrict__ t, int& e, int e1, int nthr,
+                                         uint32_t jbase, float cx, float cy, float cz,
+                                         float& bv, uint32_t& bj, uint32_t& bkey,
+                                         uint32_t& bidx) {
+    for (; e < e1; e += nthr) {
+        const float4 v = t[e];
+        const float d = sqd3(v.x, v.y, v.z, cx, cy, cz);
+        if (!NANM) {
+            const float m = fminf(v.w, d);
+            if (m < v.w) t[e].w = m;
+            if (m > bv) {
+                bv = m;
+                bj = jbase + (uint32_t)e;
+            }
+        } else {
+            const float m = fmin_nan(v.w, d);
+            if (__float_as_uint(m) != __float_as_uint(v.w)) t[e].w = m;
+            const uint32_t kk = isnan(m) ? 0xffffffffu : ordered_key(m);
+            if (kk > bkey) {
+                bkey = kk;
+                bidx = jbase + (uint32_t)e;
+            }
+        }
+    }
 }
 
 // Flat (ragged) batches of the torch_cluster API: cloud b is the rows
@@ -72,8 +127,11 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
            int skip, int out_int32, void* __restrict__ out, int G, int64_t per_cta,
            int cloud_offset, unsigned long long* __restrict__ slots,
            unsigned* __restrict__ errors, int32_t* __restrict__ status, FlatFps flat,
-           float* __restrict__ out_xyz) {
-    extern __shared__ float s_xyz[];  // G == 1 only: the cloud, 3 floats per point
+           float* __restrict__ out_xyz, int smem_pts, float4* __restrict__ ovf_global,
+           int64_t global_pts) {
+    // G == 1: the cloud, 3 floats per point.  GROUP: the shared-memory
+    // overflow tier, smem_pts float4 records.
+    extern __shared__ __align__(16) float s_xyz[];
     __shared__ uint32_t s_key[2][32];
     __shared__ uint32_t s_idx[2][32];
     __shared__ uint32_t s_far;
@@ -148,6 +206,25 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
     }
     if (tid == 0) s_abort = 0;
     bool mine_nonfinite = false;
+    // Overflow (GROUP, more than P * nthr points per CTA): points
+    // [ob, hi) as float4 records, the first sc in shared memory, the rest in
+    // this CTA's part of the global tier.
+    const int64_t ob = lo + (int64_t)P * nthr;
+    const int oc = GROUP ? (int)max64(0, hi - ob) : 0;
+    const int sc = min(oc, smem_pts);
+    float4* s_ovf = reinterpret_cast<float4*>(s_xyz);
+    float4* g_ovf = (GROUP && oc > sc)
+                        ? ovf_global + ((size_t)wave_cloud * G + g) * (size_t)global_pts - sc
+                        : nullptr;
+    for (int e = tid; e < oc; e += nthr) {
+        const int64_t j = ob + e;
+        const float x = p[3 * j + 0], y = p[3 * j + 1], z = p[3 * j + 2];
+        mine_nonfinite |= !(isfinite(x) && isfinite(y) && isfinite(z));
+        const float init = (skip && sqd3(x, y, z, 0.f, 0.f, 0.f) < 1e-3f) ? -INFINITY : INFINITY;
+        const float4 v = make_float4(x, y, z, init);
+        if (e < sc) s_ovf[e] = v;
+        else g_ovf[e] = v;
+    }
 #pragma unroll
     for (int h = 0; h < PP; ++h) {
         float a0, a1, b0, b1, c0, c1;
@@ -214,6 +291,12 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
                     }
                 }
             }
+            if (GROUP && oc > 0) {
+                int e = tid;
+                uint32_t k0 = 0u, i0 = 0u;
+                ovf_scan<false>(s_ovf, e, sc, nthr, (uint32_t)ob, cx, cy, cz, bv, bj, k0, i0);
+                ovf_scan<false>(g_ovf, e, oc, nthr, (uint32_t)ob, cx, cy, cz, bv, bj, k0, i0);
+            }
             // A lane whose points are all -inf offers its first valid point
             // (the lowest index among equal keys).
             if (bj == 0xffffffffu && lo + tid < hi) bj = (uint32_t)(lo + tid);
@@ -236,6 +319,13 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
                     bkey = k;
                     bidx = (uint32_t)j;
                 }
+            }
+            if (GROUP && oc > 0) {
+                int e = tid;
+                float v0 = 0.f;
+                uint32_t j0 = 0u;
+                ovf_scan<true>(s_ovf, e, sc, nthr, (uint32_t)ob, cx, cy, cz, v0, j0, bkey, bidx);
+                ovf_scan<true>(g_ovf, e, oc, nthr, (uint32_t)ob, cx, cy, cz, v0, j0, bkey, bidx);
             }
         }
         const uint32_t wmax = __reduce_max_sync(FULL_MASK, bkey);
@@ -261,12 +351,12 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
             // for all G slots of this step and reduces them.  A CTA can be at
             // most one step ahead of the slowest reader, so two buffers suffice.
             unsigned long long* cur = my_slots + (size_t)buf * G * kSlotStride;
-            const unsigned long long seq = (unsigned long long)((i + 1) & 0x7ff);
+            const unsigned long long seq = (unsigned long long)(i + 1) & kSeqMask;
             if (warp == 0) {
                 if (lane == 0) {
-                    const unsigned long long word = ((unsigned long long)cmax << 32) |
-                                                    (seq << kIndexBits) |
-                                                    ((unsigned long long)cidx & kIndexMask);
+                    const unsigned long long word =
+                        ((unsigned long long)cmax << 32) | (seq << kLocalBits) |
+                        ((unsigned long long)(uint32_t)(cidx - (uint32_t)lo) & kLocalMask);
                     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(cur + g * kSlotStride),
                                  "l"(word)
                                  : "memory");
@@ -280,11 +370,12 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
                     bi = 0xffffffffu;
                     for (int c = lane; c < G; c += 32) {
                         const unsigned long long v = ld_relaxed_u64(cur + c * kSlotStride);
-                        if (((v >> kIndexBits) & 0x7ffull) != seq) {
+                        if (((v >> kLocalBits) & kSeqMask) != seq) {
                             ok = false;
                         } else {
                             const uint32_t kk = (uint32_t)(v >> 32);
-                            const uint32_t ii = (uint32_t)(v & kIndexMask);
+                            const uint32_t ii =
+                                (uint32_t)c * (uint32_t)per_cta + (uint32_t)(v & kLocalMask);
                             if (kk > bk || (kk == bk && ii < bi)) {
                                 bk = kk;
                                 bi = ii;
@@ -534,7 +625,8 @@ int launch_single(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_
         return fail(kCudaError, "mpo_fps: cannot set the shared-memory limit");
     kern<<<(unsigned)B, threads_for(N, P), smem, stream>>>(xyz, N, npoint, start_idx, skip,
                                                            out_int32, out, 1, N, 0, nullptr,
-                                                           nullptr, status, flat, out_xyz);
+                                                           nullptr, status, flat, out_xyz, 0,
+                                                           nullptr, 0);
     return check_launch("mpo_fps");
 }
 
@@ -565,26 +657,40 @@ int launch_single_any(const float* xyz, int64_t B, int64_t N, int64_t npoint,
     }
 }
 
-// Group plan for one call: CTAs per cloud and clouds per cooperative wave.
+// Group plan for one call: CTAs per cloud, clouds per cooperative wave, and
+// the overflow tiers of a CTA owning more than kPointsPerCta points.
 struct GroupPlan {
     int64_t G = 0, per_cta = 0, clouds_per_wave = 0;
+    int64_t smem_pts = 0, global_pts = 0;  // per CTA
 };
 
 int plan_group(int64_t B, int64_t N, int strategy, GroupPlan* plan, const char* who) {
     const int sms = sm_count();
+    if (sms < 1) return fail(kCudaError, std::string(who) + ": no SM count for this device");
     int64_t G = ceil_div(N, kPointsPerCta);
     // A forced group on a small cloud still uses at least two CTAs (when the
     // cloud has two points) so the cross-CTA exchange is exercised.
     if (strategy == MPO_FPS_GROUP) G = min64(max64(G, 2), N);
-    if (G > sms) {
+    // Above 8192 points per SM every SM takes part and the CTAs' extra points
+    // go to the overflow tiers.
+    G = min64(G, sms);
+    const int64_t per_cta = ceil_div(N, G);
+    if (per_cta > (int64_t)kLocalMask) {
         return fail(kUnsupported, std::string(who) + ": clouds above " +
-                                      std::to_string((long long)kPointsPerCta * sms) +
+                                      std::to_string((long long)kLocalMask * G) +
                                       " points are not supported on this device");
     }
+    const int64_t over = max64(0, per_cta - kPointsPerCta);
     plan->G = G;
-    plan->per_cta = ceil_div(N, G);
+    plan->per_cta = per_cta;
     plan->clouds_per_wave = min64(B, sms / G);
+    plan->smem_pts = min64(over, kSmemTierPoints);
+    plan->global_pts = over - plan->smem_pts;
     return kOk;
+}
+
+inline size_t plan_bytes(const GroupPlan& plan) {
+    return group_total_bytes(plan.clouds_per_wave, plan.G, plan.global_pts);
 }
 
 // Runs the group path in cooperative waves; `scratch` holds group_bytes()
@@ -603,6 +709,16 @@ int launch_group(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t
     unsigned* errors =
         reinterpret_cast<unsigned*>(slots + (size_t)plan.clouds_per_wave * 2 * G * kSlotStride);
     const size_t bytes = group_bytes(plan.clouds_per_wave, G);
+    int smem_pts = (int)plan.smem_pts;
+    int64_t global_pts = plan.global_pts;
+    float4* ovf_global =
+        global_pts > 0
+            ? reinterpret_cast<float4*>(static_cast<unsigned char*>(scratch) + align256(bytes))
+            : nullptr;
+    const size_t smem = (size_t)smem_pts * sizeof(float4);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return fail(kCudaError, std::string(who) + ": cannot set the shared-memory limit");
     for (int64_t c0 = 0; c0 < B; c0 += plan.clouds_per_wave) {
         const int nc = (int)min64(plan.clouds_per_wave, B - c0);
         if (cudaMemsetAsync(scratch, 0, bytes, stream) != cudaSuccess)
@@ -611,9 +727,10 @@ int launch_group(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t
         void* args[] = {(void*)&xyz,      (void*)&N,         (void*)&npoint, (void*)&start_idx,
                         (void*)&skip,     (void*)&out_int32, (void*)&out,    (void*)&G,
                         (void*)&per_cta,  (void*)&cloud_offset, (void*)&slots, (void*)&errors,
-                        (void*)&status,   (void*)&flat,      (void*)&out_xyz};
+                        (void*)&status,   (void*)&flat,      (void*)&out_xyz,
+                        (void*)&smem_pts, (void*)&ovf_global, (void*)&global_pts};
         cudaError_t e = cudaLaunchCooperativeKernel((const void*)kern, dim3(nc * G),
-                                                    dim3(threads), args, 0, stream);
+                                                    dim3(threads), args, smem, stream);
         if (e != cudaSuccess) {
             return fail(kCudaError, std::string(who) + ": cooperative launch: " +
                                         cudaGetErrorString(e));
@@ -661,7 +778,7 @@ size_t mpo_fps_workspace_bytes(int64_t B, int64_t N, int64_t npoint, int strateg
     if (B <= 0 || N <= 0 || (strategy != MPO_FPS_GROUP && N <= mpo::kPointsPerCta)) return 0;
     mpo::GroupPlan plan;
     if (mpo::plan_group(B, N, strategy, &plan, "mpo_fps_workspace_bytes") != mpo::kOk) return 0;
-    return mpo::group_bytes(plan.clouds_per_wave, plan.G);
+    return mpo::plan_bytes(plan);
 }
 
 int mpo_fps(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64_t start_idx,
@@ -689,7 +806,7 @@ int mpo_fps_gather(const float* xyz, int64_t B, int64_t N, int64_t npoint, int64
     GroupPlan plan;
     st = plan_group(B, N, strategy, &plan, "mpo_fps");
     if (st) return st;
-    const size_t need = group_bytes(plan.clouds_per_wave, plan.G);
+    const size_t need = plan_bytes(plan);
     if (workspace == nullptr || workspace_bytes < need) {
         return fail(kWorkspaceTooSmall, "mpo_fps: workspace must hold " + std::to_string(need) +
                                             " bytes");
@@ -704,7 +821,7 @@ size_t mpo_flat_fps_workspace_bytes(int64_t segments, int64_t max_len) {
     if (mpo::plan_group(segments, max_len, MPO_FPS_AUTO, &plan, "mpo_flat_fps_workspace_bytes") !=
         mpo::kOk)
         return 0;
-    return mpo::group_bytes(plan.clouds_per_wave, plan.G);
+    return mpo::plan_bytes(plan);
 }
 
 int mpo_flat_fps(const float* x, const int64_t* ptr, const int64_t* out_ptr,
@@ -730,7 +847,7 @@ int mpo_flat_fps(const float* x, const int64_t* ptr, const int64_t* out_ptr,
     GroupPlan plan;
     int st = plan_group(segments, max_len, MPO_FPS_AUTO, &plan, "mpo_flat_fps");
     if (st) return st;
-    const size_t need = group_bytes(plan.clouds_per_wave, plan.G);
+    const size_t need = plan_bytes(plan);
     if (workspace == nullptr || workspace_bytes < need) {
         return fail(kWorkspaceTooSmall, "mpo_flat_fps: workspace must hold " +
                                             std::to_string(need) + " bytes");
@@ -753,12 +870,16 @@ int mpo_flat_fps(const float* x, const int64_t* ptr, const int64_t* out_ptr,
 //     that loads this library until the process exits).  The group path
 //     needs 256 bytes per CTA of one cooperative wave plus 8 per cloud (under
 //     38 KiB on a 148-SM B200) whatever the batch size, because waves reuse
-//     the slots; a configuration needing more is rejected.  The
-//     one-CTA-per-cloud path needs no scratch.
+//     the slots; a configuration needing more is rejected, and so is a cloud
+//     too large for registers plus shared memory (above 22,528 points per SM,
+//     3,334,144 on a 148-SM B200), whose extra points would need workspace.
+//     The one-CTA-per-cloud path needs no scratch.
 //   * In host code the array's name is only a host-side stand-in; the
-//     device address is looked up once per device with cudaGetSymbolAddress
-//     (device current) on the first call that needs it, so that first call
-//     should happen before any stream capture begins.
+//     device address is looked up with cudaGetSymbolAddress (device current)
+//     on the first call that needs it on a device, so that first call should
+//     happen before any stream capture begins.  The address is cached with
+//     the ID of the CUDA context it belongs to; a call in a newer context of
+//     the device (after cudaDeviceReset) looks it up again.
 //   * Every call shares the array.  It is cleared on the caller's stream
 //     before each wave, so calls whose GPU work overlaps (different streams,
 //     or different host threads) race on it and must be serialised by the
@@ -768,22 +889,55 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = 40960;
 static __device__ __align__(256) unsigned char g_fps_noalloc_scratch[kNoAllocScratchBytes];
 
+// Unique ID of the calling thread's current CUDA context (IDs are never
+// reused within a process), through the driver entry points the runtime
+// exposes; 0 if unavailable.
+unsigned long long current_context_id() {
+    using GetCurrent = int (*)(void**);
+    using GetId = int (*)(void*, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault) == cudaSuccess)
+            get_current = reinterpret_cast<GetCurrent>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault) == cudaSuccess)
+            get_id = reinterpret_cast<GetId>(f);
+    });
+    void* ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != 0 || ctx == nullptr ||
+        get_id(ctx, &id) != 0)
+        return 0;
+    return id;
+}
+
 int noalloc_scratch(void** out) {
+    struct Entry {
+        unsigned long long ctx = 0;
+        void* addr = nullptr;
+    };
     static std::mutex mu;
-    static void* addr[64] = {};
+    static std::map<int, Entry> cache;
     const int dev = current_device();
-    if (dev < 0 || dev >= 64) return fail(kUnsupported, "mpo_fps_noalloc: device index above 63");
+    if (dev < 0) return fail(kCudaError, "mpo_fps_noalloc: no current device");
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(mu);
-    if (addr[dev] == nullptr) {
+    Entry& e = cache[dev];
+    if (e.addr == nullptr || e.ctx != ctx || ctx == 0) {
         void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_fps_noalloc_scratch);
-        if (e != cudaSuccess || p == nullptr) {
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_fps_noalloc_scratch);
+        if (err != cudaSuccess || p == nullptr) {
+            e = Entry{};
             return fail(kCudaError, std::string("mpo_fps_noalloc: cudaGetSymbolAddress: ") +
-                                        cudaGetErrorString(e));
+                                        cudaGetErrorString(err));
         }
-        addr[dev] = p;
+        e.addr = p;
+        e.ctx = ctx;
     }
-    *out = addr[dev];
+    *out = e.addr;
     return kOk;
 }
 }  // namespace
@@ -808,6 +962,12 @@ int mpo_fps_noalloc(const float* xyz, int64_t B, int64_t N, int64_t npoint, int6
     GroupPlan plan;
     st = plan_group(B, N, strategy, &plan, "mpo_fps_noalloc");
     if (st) return st;
+    if (plan.global_pts > 0) {
+        return fail(kInvalidArgument,
+                    "mpo_fps_noalloc: clouds above " +
+                        std::to_string((long long)(kPointsPerCta + kSmemTierPoints) * plan.G) +
+                        " points need workspace (use mpo_fps with a workspace)");
+    }
     const size_t need = group_bytes(plan.clouds_per_wave, plan.G);
     if (need > kNoAllocScratchBytes) {
         return fail(kInvalidArgument,

@@ -20,7 +20,7 @@ from pathlib import Path
 import torch
 
 LIB_NAME = "libmpo_b200.so"
-ABI_VERSION = 7
+ABI_VERSION = 8
 _lib = None
 _lock = threading.Lock()
 _checked_devices: set[int] = set()
@@ -69,6 +69,10 @@ SIGNATURES = {
     "mpo_chamfer_l1_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp,
                                        _vp, _vp, _vp]),
     "mpo_chamfer_check_inputs": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "mpo_chamfer_nearest_f64": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int,
+                                       _vp, _vp, _vp, _vp, _vp]),
+    "mpo_chamfer_backward_f64": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _vp,
+                                        _vp, _vp, _vp, _vp]),
     "mpo_flat_knn": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp,
                             _vp]),
     "mpo_flat_radius": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _i64, _int, _vp, _vp,

@@ -8,8 +8,10 @@ validation and error messages.  The nearest-neighbour search and its backward
 run in the sm_100a kernels of libmpo_b200.so; the reductions over the
 per-point distances are tensor ops on the device.
 
-Scope of this build: float32 CUDA tensors, ``norm=2`` and ``norm=1`` (L1, on
-``mpo_chamfer_nearest_l1``); float64 raises ``TypeError``.
+Scope of this build: float32 and float64 CUDA tensors, ``norm=2`` and
+``norm=1`` (L1, on ``mpo_chamfer_nearest_l1``); float64 runs the same search
+and backward in double (``mpo_chamfer_nearest_f64``,
+``mpo_chamfer_backward_f64``).
 """
 
 from __future__ import annotations
@@ -88,8 +90,6 @@ def _validate_clouds(x, y, x_lengths, y_lengths, defer: bool = False):
     if x.dtype not in (torch.float32, torch.float64):
         raise TypeError("Chamfer inputs must be float32 (or float64 outside MPS)")
     N.require_cuda(x, "chamfer_distance")
-    if x.dtype != torch.float32:
-        raise TypeError("Chamfer inputs must be float32 on CUDA in this build")
     B, P, D = x.shape
     Q = y.shape[1]
     for value, count, name in ((x_lengths, P, "x_lengths"), (y_lengths, Q, "y_lengths")):
@@ -98,12 +98,19 @@ def _validate_clouds(x, y, x_lengths, y_lengths, defer: bool = False):
             raise ValueError(f"{name} must be an int64 tensor of shape ({B},) on {x.device}")
     lx = None if x_lengths is None else x_lengths.contiguous()
     ly = None if y_lengths is None else y_lengths.contiguous()
-    flags = torch.empty(4, dtype=torch.int32, device=x.device)
     xc, yc = x.detach().contiguous(), y.detach().contiguous()
     with N.on_device(x.device):
-        N.check(N.lib().mpo_chamfer_check_inputs(N.ptr(xc), N.ptr(yc), N.ptr(lx), N.ptr(ly), B, P,
-                                                 Q, D, N.ptr(flags), N.stream(x.device)),
-                "chamfer input check")
+        if x.dtype == torch.float32:
+            flags = torch.empty(4, dtype=torch.int32, device=x.device)
+            N.check(N.lib().mpo_chamfer_check_inputs(N.ptr(xc), N.ptr(yc), N.ptr(lx), N.ptr(ly),
+                                                     B, P, Q, D, N.ptr(flags),
+                                                     N.stream(x.device)),
+                    "chamfer input check")
+        else:
+            # float64: the same four flags from device tensor ops (the native
+            # check reads float32).
+            flags = torch.stack([*_bad_side(xc, lx, P), *_bad_side(yc, ly, Q)])
+            flags = flags[[0, 2, 1, 3]].int()
         host = torch.empty(4, dtype=torch.int32, pin_memory=True)
         host.copy_(flags, non_blocking=True)
         event = torch.cuda.Event()
@@ -113,6 +120,63 @@ def _validate_clouds(x, y, x_lengths, y_lengths, defer: bool = False):
         pending.raise_if_bad()
         pending = None
     return lx, ly, pending
+
+
+def _bad_side(points: Tensor, lengths: Tensor | None, count: int):
+    """(non-finite valid coordinate, length outside [0, count]) as 0-d bool
+    tensors on the device (mps_pointops/chamfer.py:79-110)."""
+    if lengths is None:
+        valid = torch.ones(points.shape[:2], dtype=torch.bool, device=points.device)
+        bad_len = torch.zeros((), dtype=torch.bool, device=points.device)
+    else:
+        valid = (torch.arange(count, device=points.device)[None]
+                 < lengths.clamp(0, count)[:, None])
+        bad_len = ((lengths < 0) | (lengths > count)).any()
+    bad_val = (valid & ~torch.isfinite(points).all(dim=-1)).any()
+    return bad_val, bad_len
+
+
+class _Nearest64(torch.autograd.Function):
+    """float64 search (both norms) and backward on the double kernels
+    (mps_pointops/chamfer.py:161-212, 227-251, 269-293)."""
+
+    @staticmethod
+    def forward(ctx, x, y, lx, ly, bidirectional: bool, norm: int):
+        B, P, D = x.shape
+        Q = y.shape[1]
+        dev = x.device
+        dist_x = torch.empty((B, P), dtype=torch.float64, device=dev)
+        idx_x = torch.empty((B, P), dtype=torch.long, device=dev)
+        dist_y = torch.empty((B, Q if bidirectional else 0), dtype=torch.float64, device=dev)
+        idx_y = torch.empty((B, Q if bidirectional else 0), dtype=torch.long, device=dev)
+        xc, yc = x.contiguous(), y.contiguous()
+        with N.on_device(dev):
+            N.check(N.lib().mpo_chamfer_nearest_f64(
+                N.ptr(xc), N.ptr(yc), N.ptr(lx), N.ptr(ly), B, P, Q, D, norm, int(bidirectional),
+                N.ptr(dist_x), N.ptr(idx_x), N.ptr(dist_y), N.ptr(idx_y), N.stream(dev)),
+                "chamfer nearest (float64)")
+        ctx.save_for_backward(xc, yc, idx_x, idx_y)
+        ctx.bidirectional, ctx.norm = bidirectional, norm
+        ctx.mark_non_differentiable(idx_x, idx_y)
+        ctx.set_materialize_grads(False)
+        return dist_x, dist_y, idx_x, idx_y
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g_dx, g_dy, _gix, _giy):
+        x, y, idx_x, idx_y = ctx.saved_tensors
+        B, P, D = x.shape
+        Q = y.shape[1]
+        grad_x = torch.empty_like(x)
+        grad_y = torch.empty_like(y)
+        gx = None if g_dx is None else g_dx.double().contiguous()
+        gy = None if (g_dy is None or not ctx.bidirectional) else g_dy.double().contiguous()
+        with N.on_device(x.device):
+            N.check(N.lib().mpo_chamfer_backward_f64(
+                N.ptr(x), N.ptr(y), B, P, Q, D, ctx.norm, N.ptr(idx_x), N.ptr(gx), N.ptr(idx_y),
+                N.ptr(gy), N.ptr(grad_x), N.ptr(grad_y), N.stream(x.device)),
+                "chamfer backward (float64)")
+        return grad_x, grad_y, None, None, None, None
 
 
 class _NearestSquared(torch.autograd.Function):
@@ -310,9 +374,10 @@ def chamfer_distance(
     """Chamfer loss (squared L2, or L1 with ``norm=1``) with PyTorch3D
     reduction conventions (mps_pointops/chamfer.py:342-488).
 
-    ``x`` (B,P,D) and ``y`` (B,Q,D) float32 CUDA tensors, D >= 1.  Each valid
-    point is matched to the FIRST nearest valid point of the other cloud
-    (float32 squared distance, no FMA, lowest index on ties); the loss is the
+    ``x`` (B,P,D) and ``y`` (B,Q,D) float32 or float64 CUDA tensors, D >= 1.
+    Each valid point is matched to the FIRST nearest valid point of the other
+    cloud (squared distance in the input precision, no FMA, lowest index on
+    ties); the loss is the
     reduced sum of the matched squared distances in both directions (one with
     ``single_directional``).  Returns ``(loss, normal_loss)``.  Input checks
     synchronise once with the host (twice with weights).
@@ -349,7 +414,8 @@ def chamfer_distance(
         if bool((weights == 0).all().item()):
             return _all_zero_weights(x, y, lx, ly, weights, point_reduction, batch_reduction,
                                      single_directional)
-    if norm == 2 and weights is None and not return_normals and point_reduction in ("mean", "sum"):
+    if (norm == 2 and weights is None and not return_normals and point_reduction in ("mean", "sum")
+            and x.dtype == torch.float32):
         loss = _ChamferLoss.apply(x, y, lx, ly, not single_directional,
                                   1 if point_reduction == "mean" else 0,
                                   {None: 0, "sum": 1, "mean": 2}[batch_reduction])
@@ -357,8 +423,11 @@ def chamfer_distance(
             pending.raise_if_bad()
         return loss, None
 
-    search = _NearestL1 if norm == 1 else _NearestSquared
-    dx, dy, ix, iy = search.apply(x, y, lx, ly, not single_directional)
+    if x.dtype == torch.float64:
+        dx, dy, ix, iy = _Nearest64.apply(x, y, lx, ly, not single_directional, norm)
+    else:
+        search = _NearestL1 if norm == 1 else _NearestSquared
+        dx, dy, ix, iy = search.apply(x, y, lx, ly, not single_directional)
     if pending is not None:
         pending.raise_if_bad()
     nx = ny = None

@@ -19,6 +19,8 @@ for p in (str(ROOT), str(PKG_ROOT)):
         sys.path.insert(0, p)
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
+if str(GOLDEN) not in sys.path:
+    sys.path.insert(0, str(GOLDEN))
 
 
 def pytest_configure(config):

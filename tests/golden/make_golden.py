@@ -1,9 +1,10 @@
 """Generate the golden fixtures in tests/golden/ from the reference package.
 
-Run once, in a container that has the reference checkout (default
-``/root/reference``, override with ``MPO_REFERENCE_PATH``)::
+Run once, in a container that has the reference checkout, with
+``MPO_REFERENCE_PATH`` naming its root (the directory holding the
+``mps_pointops`` package)::
 
-    python tests/golden/make_golden.py
+    MPO_REFERENCE_PATH=<checkout> python tests/golden/make_golden.py [case ...]
 
 Every output is produced by the reference's OWN code: its CPU path
 (``mps_pointops.reference``, ``pointnet2._three_nn_reference``,
@@ -26,7 +27,9 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(os.environ.get("MPO_REFERENCE_PATH", "/root/reference"))
+if "MPO_REFERENCE_PATH" not in os.environ:
+    sys.exit("make_golden.py: set MPO_REFERENCE_PATH to the reference checkout's root")
+REF = Path(os.environ["MPO_REFERENCE_PATH"])
 OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(REF / "tests"))
@@ -38,6 +41,9 @@ from mps_pointops import pointnet2 as ref_pointnet2  # noqa: E402
 import test_feature_knn  # noqa: E402  (reference tests: scalar fp32 oracle)
 import test_knn  # noqa: E402  (reference tests: exact lexsort oracle)
 import pointnet2parity  # noqa: E402  (reference tools: parity inputs)
+
+sys.path.insert(0, str(OUT))
+from cases import ND_CASES, nd_cloud_pair, sphere_cloud  # noqa: E402  (shared with the tests)
 
 
 def cloud(b, n, seed=0):
@@ -315,6 +321,52 @@ def chamfer_cases():
     save("chamfer", **out)
 
 
+def chamfer_nd_cases():
+    """Feature-space (D != 3) Chamfer across several tiles of the symmetric
+    kernel, and float64 inputs (chamfer.py:101-102), on the reference's CPU
+    path: nearest indices of both directions and losses for norm 2 and norm 1,
+    gradients where the clouds are small.  Inputs are rebuilt from the seeds
+    in ND_CASES (a digest is stored to detect a different generator)."""
+    import hashlib
+    out = {}
+    for name, (B, P, Q, D, seed, lens) in ND_CASES.items():
+        x, y = nd_cloud_pair(B, P, Q, D, seed, lattice=name.endswith("lattice"))
+        out[f"{name}/sha256"] = np.frombuffer(
+            hashlib.sha256(x.numpy().tobytes() + y.numpy().tobytes()).digest(), dtype=np.uint8)
+        lx = None if lens is None else torch.tensor(lens[0])
+        ly = None if lens is None else torch.tensor(lens[1])
+        flx = torch.full((B,), P) if lx is None else lx
+        fly = torch.full((B,), Q) if ly is None else ly
+        for dtype in (torch.float32, torch.float64):
+            xs, ys = x.to(dtype), y.to(dtype)
+            tag = f"{name}/{'f64' if dtype == torch.float64 else 'f32'}"
+            for norm in (1, 2):
+                xr, yr = xs.clone().requires_grad_(), ys.clone().requires_grad_()
+                loss, _ = ref_chamfer.chamfer_distance(xr, yr, lx, ly, norm=norm)
+                loss.backward()
+                out[f"{tag}_n{norm}_idx_x"] = ref_chamfer._nearest_indices(
+                    xs, ys, flx, fly, norm=norm).int()
+                out[f"{tag}_n{norm}_idx_y"] = ref_chamfer._nearest_indices(
+                    ys, xs, fly, flx, norm=norm).int()
+                out[f"{tag}_n{norm}_loss"] = loss.detach()
+                if dtype == torch.float32 or D <= 8:
+                    out[f"{tag}_n{norm}_grad_x"] = xr.grad
+                    out[f"{tag}_n{norm}_grad_y"] = yr.grad
+    # float64 single-directional with weights and sum reductions
+    g = torch.Generator().manual_seed(907)
+    x64 = torch.randn(3, 50, 3, generator=g, dtype=torch.float64)
+    y64 = torch.randn(3, 41, 3, generator=g, dtype=torch.float64)
+    w = torch.tensor([0.5, 2.0, 1.0], dtype=torch.float64)
+    xr, yr = x64.clone().requires_grad_(), y64.clone().requires_grad_()
+    loss, _ = ref_chamfer.chamfer_distance(xr, yr, weights=w, batch_reduction="sum",
+                                           single_directional=True)
+    loss.backward()
+    out["f64_weighted/x"], out["f64_weighted/y"], out["f64_weighted/weights"] = x64, y64, w
+    out["f64_weighted/loss"] = loss.detach()
+    out["f64_weighted/grad_x"], out["f64_weighted/grad_y"] = xr.grad, yr.grad
+    save("chamfer_nd", **out)
+
+
 def chamfer_l1_cases():
     """chamfer_distance(norm=1) on the reference's CPU path (chamfer.py:161-212,
     254-293, 342-488): losses and gradients for lengths, weights, normals,
@@ -535,10 +587,32 @@ def pointcept_cases():
     save("pointcept", **out)
 
 
+# ------------------------------------------------------------------ large FPS
+def fps_large_cases():
+    """Full-length config 3 (2^20 points -> 65,536 samples, about 4 minutes on
+    8 cores) and 1024-step runs on 1.5 M and 4 M point clouds, all by
+    reference.furthest_point_sample.  Only the indices and a digest of the
+    input are stored; the tests rebuild the input with the same generator."""
+    import hashlib
+    out = {}
+    for name, n, npoint, seed in (("config3", 1 << 20, 65536, 4),
+                                  ("n1p5m", 1_500_000, 1024, 41),
+                                  ("n4m", 4_000_000, 1024, 42)):
+        xyz = sphere_cloud(n, seed)
+        out[f"{name}/meta"] = np.array([n, npoint, seed], dtype=np.int64)
+        out[f"{name}/sha256"] = np.frombuffer(
+            hashlib.sha256(xyz.numpy().tobytes()).digest(), dtype=np.uint8)
+        out[f"{name}/idx"] = reference.furthest_point_sample(xyz, npoint, 0, False).to(torch.int32)
+        print(name, "done", flush=True)
+    save("fps_large", **out)
+
+
 CASES = {
-    "fps": fps_cases, "knn": knn_cases, "feature_knn": feature_knn_cases,
+    "fps": fps_cases, "fps_large": fps_large_cases, "knn": knn_cases,
+    "feature_knn": feature_knn_cases,
     "ball_query": ball_query_cases, "pointnet2": pointnet2_cases, "chamfer": chamfer_cases,
     "flat": flat_cases, "grouping": grouping_cases, "chamfer_l1": chamfer_l1_cases,
+    "chamfer_nd": chamfer_nd_cases,
     "pointcept": pointcept_cases,
 }
 

@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_error_channel():
     lib = N.lib()
-    assert lib.mpo_abi_version() == N.ABI_VERSION == 7
+    assert lib.mpo_abi_version() == N.ABI_VERSION == 8
     # Argument validation happens before any CUDA call, so it runs without a GPU.
     st = lib.mpo_knn(None, None, 1, 1, 1000, 3, 300, None, None, None, None, 0, None)
     assert st == 1

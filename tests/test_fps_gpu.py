@@ -66,15 +66,60 @@ def test_group_path_matches_single(cuda_device, n):
     np.testing.assert_array_equal(group.cpu().numpy(), want)
 
 
-def test_large_cloud_prefix_matches_oracle(cuda_device):
-    """BASELINE config 3 input (2^20 points on a jittered sphere), first 256 steps."""
-    g = torch.Generator().manual_seed(4)
-    p = torch.randn(1, 1 << 20, 3, generator=g)
+def _sphere(n, seed):
+    """BASELINE config 3's distribution: unit sphere, N(0, 0.01) radial jitter."""
+    g = torch.Generator().manual_seed(seed)
+    p = torch.randn(1, n, 3, generator=g)
     p = p / p.norm(dim=-1, keepdim=True)
-    p = p * (1 + 0.01 * torch.randn(1, 1 << 20, 1, generator=g))
-    want = O.furthest_point_sample(p.numpy(), 256, 0, False)
-    got = mps_pointops.furthest_point_sample(p.to(cuda_device), 256)
+    return p * (1 + 0.01 * torch.randn(1, n, 1, generator=g))
+
+
+def _large_case(name):
+    import hashlib
+    c = golden("fps_large")[name]
+    n, npoint, seed = (int(v) for v in c["meta"])
+    xyz = _sphere(n, seed)
+    digest = np.frombuffer(hashlib.sha256(xyz.numpy().tobytes()).digest(), dtype=np.uint8)
+    assert np.array_equal(digest, c["sha256"]), "torch's generator no longer rebuilds this input"
+    return xyz, npoint, c["idx"].astype(np.int64)
+
+
+def test_config3_full_run_matches_reference(cuda_device):
+    """BASELINE config 3 end to end: 65,536 samples from 2^20 points, against
+    reference.furthest_point_sample's own output (tests/golden/fps_large.npz).
+    The 8-bit step sequence of the cross-CTA exchange wraps 256 times."""
+    xyz, npoint, want = _large_case("config3")
+    got = mps_pointops.furthest_point_sample(xyz.to(cuda_device), npoint)
     np.testing.assert_array_equal(got.cpu().numpy(), want)
+    # the first 256 steps also against the C oracle
+    np.testing.assert_array_equal(want[:, :256], O.furthest_point_sample(xyz.numpy(), 256, 0,
+                                                                         False))
+
+
+@pytest.mark.parametrize("name", ["n1p5m", "n4m"])
+def test_beyond_8192_points_per_sm_matches_reference(cuda_device, name):
+    """1.5 M points (registers + shared-memory tier) and 4 M points (registers
+    + shared memory + workspace tier): 1024 samples against the reference's
+    CPU path and the C oracle."""
+    xyz, npoint, want = _large_case(name)
+    got = mps_pointops.furthest_point_sample(xyz.to(cuda_device), npoint)
+    np.testing.assert_array_equal(got.cpu().numpy(), want)
+    np.testing.assert_array_equal(want, O.furthest_point_sample(xyz.numpy(), npoint, 0, False))
+
+
+def test_overflow_tiers_edge_cases(cuda_device):
+    """Tier boundaries, skip_near_origin, a NaN in the workspace tier, ties on
+    a lattice, a non-zero start and several clouds: all against the oracle."""
+    g = torch.Generator().manual_seed(31)
+    n = 3_600_000                       # beyond registers + shared memory on 148 SMs
+    xyz = torch.randint(0, 40, (1, n, 3), generator=g).float()      # many exact ties
+    xyz[0, 5:20000] *= 1e-3 / 40                                   # near the origin
+    _check(xyz, 200, 12345, True, cuda_device)
+    xyz2 = torch.randn(1, n, 3, generator=g)
+    xyz2[0, n - 17, 1] = float("nan")                              # in the last CTA's tail
+    _check(xyz2, 64, 0, False, cuda_device)
+    two = torch.randn(2, 1_300_000, 3, generator=g)                # two clouds, one wave each
+    _check(two, 128, 77, False, cuda_device)
 
 
 def test_group_status_word_reports_success(cuda_device):

@@ -140,3 +140,38 @@ def test_chamfer_matches_reference():
         np.testing.assert_allclose(loss, c["loss"], rtol=1e-5, atol=1e-7, err_msg=name)
         np.testing.assert_allclose(gx, c["grad_x"], rtol=1e-5, atol=1e-7, err_msg=name)
         np.testing.assert_allclose(gy, c["grad_y"], rtol=1e-5, atol=1e-7, err_msg=name)
+
+
+def _nd_inputs(name):
+    import hashlib
+    from cases import ND_CASES, nd_cloud_pair
+    c = golden("chamfer_nd")[name]
+    B, P, Q, D, seed, lens = ND_CASES[name]
+    x, y = nd_cloud_pair(B, P, Q, D, seed, lattice=name.endswith("lattice"))
+    digest = hashlib.sha256(x.numpy().tobytes() + y.numpy().tobytes()).digest()
+    assert np.frombuffer(digest, dtype=np.uint8).tolist() == c["sha256"].tolist()
+    lx = None if lens is None else np.array(lens[0], dtype=np.int64)
+    ly = None if lens is None else np.array(lens[1], dtype=np.int64)
+    return c, x.numpy(), y.numpy(), lx, ly
+
+
+def test_chamfer_nd_oracle_matches_reference():
+    """Feature-space Chamfer (D != 3): the oracle's nearest indices equal the
+    reference's for both norms, in both directions."""
+    for name in ["d1", "d2_ragged", "d5", "d8_lattice"]:
+        c, x, y, lx, ly = _nd_inputs(name)
+        vx, vy = nd_valid(x, lx), nd_valid(y, ly)
+        for norm in (1, 2):
+            _, ix = O.chamfer_nearest(x, y, lx, ly, norm=norm)
+            _, iy = O.chamfer_nearest(y, x, ly, lx, norm=norm)
+            np.testing.assert_array_equal(ix[vx], c[f"f32_n{norm}_idx_x"][vx], err_msg=name)
+            np.testing.assert_array_equal(iy[vy], c[f"f32_n{norm}_idx_y"][vy], err_msg=name)
+            assert (ix[~vx] == -1).all() and (iy[~vy] == -1).all()
+
+
+def nd_valid(points, lengths):
+    """Rows below each cloud's length (the reference leaves the others'
+    indices unspecified: its loss never reads them)."""
+    B, P = points.shape[:2]
+    lens = np.full(B, P) if lengths is None else lengths
+    return np.arange(P)[None, :] < lens[:, None]
