@@ -4,9 +4,12 @@ Chamfer, and BASELINE config 2 at its full size, on B200.
 Fixtures: tests/golden/chamfer_nd.npz, made by the reference's CPU path
 (mps_pointops/chamfer.py:161-212 search, :342-488 loss, autograd gradients)
 for norm 2 and norm 1 in float32 and float64.  Nearest indices are bit-exact
-on valid rows; float32 losses and gradients within rtol 1e-5 (atol 1e-7),
-float64 within rtol 1e-10 (atol 1e-12) -- the kernels' float atomics sum the
-gradients in another order than torch.
+on valid rows; float32 losses within rtol 1e-5, float64 within rtol 1e-10.
+Gradients: the kernels' float atomics sum each point's terms in another order
+than torch, and a point matched by hundreds of others (a cloud of two points)
+sums terms of both signs that cancel, so gradients are compared with
+rtol 1e-5 (1e-10) plus atol 1e-5 (1e-10) times the largest gradient
+magnitude of the array.
 """
 
 from __future__ import annotations
@@ -96,10 +99,11 @@ def test_feature_space_and_float64_match_reference(cuda_device, name, norm, dtyp
     assert loss.dtype == dtype and xr.grad.dtype == dtype
     np.testing.assert_allclose(loss.item(), c[f"{tag}_n{norm}_loss"], **TOL[dtype])
     if f"{tag}_n{norm}_grad_x" in c:
-        np.testing.assert_allclose(xr.grad.cpu().numpy(), c[f"{tag}_n{norm}_grad_x"],
-                                   **TOL[dtype])
-        np.testing.assert_allclose(yr.grad.cpu().numpy(), c[f"{tag}_n{norm}_grad_y"],
-                                   **TOL[dtype])
+        for got, want in ((xr.grad, c[f"{tag}_n{norm}_grad_x"]),
+                          (yr.grad, c[f"{tag}_n{norm}_grad_y"])):
+            rtol = TOL[dtype]["rtol"]
+            np.testing.assert_allclose(got.cpu().numpy(), want, rtol=rtol,
+                                       atol=rtol * float(np.abs(want).max()))
 
 
 def test_symmetric_kernel_matches_one_direction_passes(cuda_device):
