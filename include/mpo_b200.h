@@ -454,6 +454,42 @@ MPO_API int mpo_flat_fps(const float* x, const int64_t* ptr, const int64_t* out_
                          int64_t total_out, int64_t max_len, int64_t* out, int32_t* status,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------ row gathers
+ * Neighbour gathers with -1 padding: replaces the `_gather_neighbors` tensor
+ * code of the PyTorch3D adapter (mps_pointops/pytorch3d.py:26-38, `knn` of
+ * ball_query with return_nn) and the gathers of Pointcept's `grouping`
+ * (mps_pointops/pointcept.py:168-203).
+ *   src (B, N, W) float32 rows, idx (B, R) int64 (idx_int32 == 0) or int32:
+ *   out[(b R + r) * out_stride + out_offset + w] = src[b, idx[b, r], w], or 0
+ *   when the index is outside [0, N).  centers (nullable, (B R / K, W)):
+ *   subtract centers[(b R + r) / K, w] from valid rows (the relative
+ *   coordinates of `grouping(with_xyz=True)`).  No workspace. */
+MPO_API int mpo_gather_rows(const float* src, int64_t B, int64_t N, int64_t W, const void* idx,
+                            int idx_int32, int64_t R, const float* centers, int64_t K,
+                            float* out, int64_t out_stride, int64_t out_offset, void* stream);
+/* Its backward: for every valid slot, grad_src[b, idx, w] += g and (when
+ * grad_centers is non-null) grad_centers[(b R + r) / K, w] -= g, g read from
+ * grad_out with the same stride and offset.  Accumulates: the caller zeroes
+ * grad_src and grad_centers. */
+MPO_API int mpo_gather_rows_backward(const float* grad_out, int64_t out_stride,
+                                     int64_t out_offset, int64_t B, int64_t N, int64_t W,
+                                     const void* idx, int idx_int32, int64_t R, int64_t K,
+                                     float* grad_src, float* grad_centers, void* stream);
+
+/* Pointcept inverse-distance interpolation (mps_pointops/pointcept.py:219-243):
+ * feat (N, C), the k nearest idx (M, k) int32 (-1 = none) and their distances
+ * dist (M, k) from knn_query -> out (M, C):
+ *   r_t = 1 / (dist_t + 1e-8) for valid t, else 0;  w_t = r_t / max(sum_t r_t, 1e-20);
+ *   out[m, c] = sum_t w_t * feat[idx_t, c], each operation rounded, t in order.
+ * Backward: grad_feat (N, C, overwritten) receives w_t * grad_out[m, c] at
+ * idx_t (the weights carry no gradient, as in the reference). */
+MPO_API int mpo_flat_interpolate(const float* feat, int64_t N, int64_t C, const int32_t* idx,
+                                 const float* dist, int64_t M, int64_t k, float* out,
+                                 void* stream);
+MPO_API int mpo_flat_interpolate_backward(const float* grad_out, const int32_t* idx,
+                                          const float* dist, int64_t M, int64_t k, int64_t N,
+                                          int64_t C, float* grad_feat, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

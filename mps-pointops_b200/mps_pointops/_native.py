@@ -69,6 +69,12 @@ SIGNATURES = {
     "mpo_chamfer_l1_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp,
                                        _vp, _vp, _vp]),
     "mpo_chamfer_check_inputs": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "mpo_gather_rows": (_int, [_vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _i64, _vp, _i64,
+                                _i64, _vp]),
+    "mpo_gather_rows_backward": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _int, _i64,
+                                         _i64, _vp, _vp, _vp]),
+    "mpo_flat_interpolate": (_int, [_vp, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _vp]),
+    "mpo_flat_interpolate_backward": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "mpo_chamfer_nearest_f64": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int,
                                        _vp, _vp, _vp, _vp, _vp]),
     "mpo_chamfer_backward_f64": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _vp,

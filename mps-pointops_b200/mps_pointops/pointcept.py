@@ -15,9 +15,12 @@ distances, non-finite distances dropped).  The padding rules of the
 upstream CUDA heap stay as the reference states them (pointcept.py:17-18,
 141-153): a slot is valid only when its squared distance, recomputed from
 the selected coordinates as ((dx*dx + dy*dy) + dz*dz), is below 1e10;
-missing slots hold index -1 and distance 1e5.  Grouping and interpolation
-are row gathers and weighted sums, written with torch tensor operations as
-in the reference (pointcept.py:168-243).
+missing slots hold index -1 and distance 1e5.  Grouping is one native row
+gather per part written into the concatenated output in place
+(``mpo_gather_rows``: relative coordinates, then features, zero rows for -1
+slots), and interpolation one native pass that forms the inverse-distance
+weights and their weighted sum (``mpo_flat_interpolate``), with native
+scatter backwards (pointcept.py:168-243).
 
 Inputs are validated as the reference does (shape, dtype, offsets) on CPU
 or CUDA tensors; the computation itself runs on CUDA only and raises
@@ -31,6 +34,7 @@ from torch import Tensor
 
 from . import _native as N
 from . import flat
+from ._rows import FlatInterpolate, GroupRows
 
 _PAD_SQUARED_DISTANCE = 1e10  # the upstream CUDA heap's strict ceiling
 _PAD_DISTANCE = 100_000.0  # sqrt(1e10): the upstream unfilled distance
@@ -184,21 +188,15 @@ def grouping(idx: Tensor, feat: Tensor, xyz: Tensor, new_xyz: Tensor | None = No
     if bool(((idx < -1) | (idx >= len(xyz))).any()):
         raise ValueError("idx contains an out-of-range point index")
     N.require_cuda(xyz, "pointcept.grouping")
-    valid = idx >= 0
-    safe_idx = torch.where(valid, idx.long(), len(xyz))
-    padded_feat = torch.cat((feat, feat.new_zeros((1, feat.shape[1]))), dim=0)
-    grouped_feat = padded_feat[safe_idx]
-    if not with_xyz:
-        return grouped_feat
-    if new_xyz is None:
-        new_xyz = xyz
-    _points(new_xyz, "new_xyz")
-    if new_xyz.device != xyz.device or len(new_xyz) != len(idx):
-        raise ValueError("new_xyz must have one row per idx row on the xyz device")
-    padded_xyz = torch.cat((xyz, xyz.new_zeros((1, 3))), dim=0)
-    relative = padded_xyz[safe_idx] - new_xyz.unsqueeze(1)
-    relative = torch.where(valid.unsqueeze(-1), relative, 0)
-    return torch.cat((relative, grouped_feat), dim=-1)
+    if with_xyz:
+        if new_xyz is None:
+            new_xyz = xyz
+        _points(new_xyz, "new_xyz")
+        if new_xyz.device != xyz.device or len(new_xyz) != len(idx):
+            raise ValueError("new_xyz must have one row per idx row on the xyz device")
+    # One native gather per part, written into the concatenated output in
+    # place (mpo_gather_rows): relative coordinates, then the features.
+    return GroupRows.apply(feat, xyz, new_xyz if with_xyz else xyz, idx, with_xyz)
 
 
 def knn_query_and_group(feat: Tensor, xyz: Tensor, offset: Tensor | None = None,
@@ -224,13 +222,8 @@ def interpolation(xyz: Tensor, new_xyz: Tensor, feat: Tensor, offset: Tensor,
     if feat.dtype != torch.float32 or feat.device != xyz.device:
         raise ValueError("feat must be float32 on the xyz device")
     idx, dist = knn_query(k, xyz, offset, new_xyz, new_offset)
-    valid = idx >= 0
-    reciprocal = torch.where(valid, 1.0 / (dist + 1e-8), 0.0)
-    normalizer = reciprocal.sum(dim=1, keepdim=True)
-    weight = reciprocal / normalizer.clamp_min(1e-20)
-    padded_feat = torch.cat((feat, feat.new_zeros((1, feat.shape[1]))), dim=0)
-    safe_idx = torch.where(valid, idx.long(), len(feat))
-    return (padded_feat[safe_idx] * weight.unsqueeze(-1)).sum(dim=1)
+    # Weights and the weighted sum in one native pass (mpo_flat_interpolate).
+    return FlatInterpolate.apply(feat, idx, dist)
 
 
 __all__ = [

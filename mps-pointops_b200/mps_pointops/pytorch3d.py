@@ -6,8 +6,8 @@ K, radius, return_nn, skip_points_outside_cube)`` returning
 ``KNN(dists, idx, knn)``, with the same argument checks and messages.  The
 search is the first-K ball query of ``mps_pointops.ball_query`` (the
 ``mpo_ball_query`` kernel, ragged lengths honoured on the device); the
-returned neighbour coordinates are gathered with the reference's own tensor
-expression (zero rows for ``-1`` slots, gradients to ``p2``).  Import it
+returned neighbour coordinates come from the native row gather
+(``mpo_gather_rows``: zero rows for ``-1`` slots, gradients to ``p2``).  Import it
 explicitly: ``from mps_pointops.pytorch3d import ball_query``.
 """
 
@@ -18,6 +18,7 @@ from typing import NamedTuple
 import torch
 
 from . import _native as N
+from ._rows import GatherRows
 from ._ball_query_cuda import _checked_radius_and_k
 from ._ball_query_cuda import ball_query as _cuda_ball_query
 
@@ -28,22 +29,6 @@ class KNN(NamedTuple):
     dists: torch.Tensor
     idx: torch.Tensor
     knn: torch.Tensor | None
-
-
-def _gather_neighbors(points: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
-    """Neighbour coordinates with zero rows for ``-1`` slots
-    (mps_pointops/pytorch3d.py:26-38)."""
-    batch, queries, k = indices.shape
-    if indices.numel() == 0:
-        # Keeps the autograd connection for empty K, Q or B dimensions.
-        return points[:, :0, :].reshape(batch, queries, k, 3)
-    if points.shape[1] == 0:
-        return points.new_zeros((batch, queries, k, 3)) + points.sum() * 0.0
-    valid = indices >= 0
-    safe = indices.clamp_min(0)
-    gathered = points.gather(1, safe.reshape(batch, -1, 1).expand(-1, -1, 3))
-    gathered = gathered.reshape(batch, queries, k, 3)
-    return torch.where(valid.unsqueeze(-1), gathered, torch.zeros_like(gathered))
 
 
 def ball_query(
@@ -83,7 +68,9 @@ def ball_query(
     result = _cuda_ball_query(p1, p2, radius=radius, k=K, query_lengths=lengths1,
                               point_lengths=lengths2)
     dists, idx = result.distances, result.indices
-    knn = _gather_neighbors(p2, idx) if return_nn else None
+    # Neighbour coordinates: one native gather, zero rows for -1 slots,
+    # gradients scattered back to p2 (mpo_gather_rows).
+    knn = GatherRows.apply(p2, idx) if return_nn else None
     return KNN(dists=dists, idx=idx, knn=knn)
 
 
