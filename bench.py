@@ -165,9 +165,12 @@ def chamfer_step(x, y, world, group_batch):
     xr = x.detach().requires_grad_()
     yr = y.detach().requires_grad_()
     if world > 1:
-        loss = chamfer_distance_sharded(xr, yr, group_batch)
-    else:
-        loss, _ = chamfer_distance(xr, yr)
+        # The loss all-reduce runs on NCCL's stream during the backward; the
+        # step ends once its global loss is in (the stream waits on it).
+        local, pending = chamfer_distance_sharded(xr, yr, group_batch, overlap=True)
+        local.backward()
+        return pending.value()
+    loss, _ = chamfer_distance(xr, yr)
     loss.backward()
     return loss
 
@@ -211,6 +214,115 @@ def ssg_secondary(steps: int, warmup: int, world: int, rank: int) -> dict:
     return {"metric": "clouds/sec for FPS+ball_query+kNN (B=8,N=4096)",
             "value": 8 * world / (ms / 1e3), "unit": "clouds/s", "ms_per_step": ms,
             "config": {"workload": "ssg_config1", "global_batch": 8 * world, "points": 4096}}
+
+
+def _split_ms(step_fn, steps: int, warmup: int, world: int) -> tuple[float, float]:
+    """Per-step time and the part after the compute (the collective), both
+    from CUDA events on the current stream, means over `steps`, max over
+    ranks.  step_fn(mark) must call mark() between its compute and its
+    collective."""
+    for _ in range(warmup):
+        step_fn(lambda: None)
+    torch.cuda.synchronize()
+    barrier(world)
+    s = torch.cuda.current_stream()
+    rec = []
+    for _ in range(steps):
+        a, m, b = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record(s)
+        step_fn(lambda: m.record(s))
+        b.record(s)
+        rec.append((a, m, b))
+    torch.cuda.synchronize()
+    total = statistics.mean(a.elapsed_time(b) for a, _, b in rec)
+    coll = statistics.mean(m.elapsed_time(b) for _, m, b in rec)
+    return max_over_ranks(total, world), max_over_ranks(coll, world)
+
+
+def ssg_strong_secondary(steps: int, warmup: int, world: int, rank: int) -> dict:
+    """BASELINE config 1 with its 8 clouds split over the ranks (strong
+    scaling: 8 / world clouds per GPU): compat FPS 1024 -> gather -> ball
+    query (0.2, 32) -> kNN k=16, then (world > 1) the FPS, ball-query and kNN
+    outputs all-gathered so every rank holds the batch's results."""
+    from mps_pointops import compat, knn
+    from mps_pointops.dist import all_gather_shards, shard_range
+    g = torch.Generator().manual_seed(0)
+    xyz_all = torch.rand(8, 4096, 3, generator=g)
+    lo, hi = shard_range(8, rank, world)
+    xyz = xyz_all[lo:hi].contiguous().cuda()
+
+    def step(mark):
+        idx = compat.furthest_point_sample(xyz, 1024)
+        centres = compat.gather_operation(xyz.transpose(1, 2).contiguous(), idx)
+        centres = centres.transpose(1, 2).contiguous()
+        bq = compat.ball_query(0.2, 32, xyz, centres)
+        d, i = knn(centres, xyz, 16)
+        mark()
+        if world > 1:
+            for t in (idx, bq, d, i):
+                all_gather_shards(t, 8)
+
+    ms, coll = _split_ms(step, steps, warmup, world)
+    return {"metric": "clouds/sec for FPS+ball_query+kNN (B=8,N=4096)",
+            "value": 8 / (ms / 1e3), "unit": "clouds/s", "ms_per_step": ms,
+            "all_gather_ms_per_step": coll, "scaling": "strong",
+            "config": {"workload": "ssg_config1_strong", "global_batch": 8,
+                       "clouds_per_gpu": hi - lo, "points": 4096,
+                       "collective": "all_gather_into_tensor of FPS idx, ball-query idx, kNN "
+                                     "dist and idx (NCCL)" if world > 1 else "none"}}
+
+
+def config5_secondary(steps: int, warmup: int, world: int, rank: int) -> dict:
+    """BASELINE config 5 sharded as specified: 2^20 queries split contiguously
+    over the ranks against the replicated 2^20-point reference cloud (built
+    identically on every rank), brute-force kNN k=16 and ball query r=0.3,
+    K=32 through the public API, then (world > 1) the four outputs
+    all-gathered along the query axis.  Queries/s of the whole job."""
+    from mps_pointops import ball_query, knn
+    from mps_pointops.dist import all_gather_shards, shard_range
+    nq = 1 << 20
+    ref = _config5_cloud(6, 1 << 20).cuda()
+    lo, hi = shard_range(nq, rank, world)
+    q = _config5_cloud(7, nq)[:, lo:hi].contiguous().cuda()
+
+    def step(mark):
+        kd, ki = knn(q, ref, 16)
+        bd, bi = ball_query(q, ref, 0.3, 32)
+        mark()
+        if world > 1:
+            for t in (kd, ki, bd, bi):
+                all_gather_shards(t, nq, dim=1)
+
+    ms, coll = _split_ms(step, steps, warmup, world)
+    return {"metric": "config 5 queries/sec (kNN k=16 + ball query r=0.3 K=32, 2^20 x 2^20)",
+            "value": nq / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms,
+            "all_gather_ms_per_step": coll, "scaling": "strong",
+            "config": {"workload": "config5_sharded", "queries": nq, "refs": 1 << 20,
+                       "queries_per_gpu": hi - lo, "search": "brute force (public API)",
+                       "collective": "all_gather_into_tensor of kNN dist/idx and ball-query "
+                                     "dist/idx along the query axis (NCCL)"
+                                     if world > 1 else "none"}}
+
+
+def loss_all_reduce_us(world: int, reps: int = 50) -> float | None:
+    """Latency of the Chamfer step's collective alone: a 4-byte all_reduce
+    (CUDA events on NCCL's completion, mean, max over ranks)."""
+    if world == 1:
+        return None
+    import torch.distributed as dist
+    t = torch.ones(1, device="cuda")
+    for _ in range(5):
+        dist.all_reduce(t)
+    torch.cuda.synchronize()
+    barrier(world)
+    s = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for _ in range(reps):
+        dist.all_reduce(t)
+    b.record(s)
+    torch.cuda.synchronize()
+    return max_over_ranks(a.elapsed_time(b) * 1e3 / reps, world)
 
 
 def feature_knn_secondary(steps: int, warmup: int, world: int, rank: int,
@@ -753,6 +865,10 @@ def run_b200(args, world, rank, local):
     secondary = None if args.no_secondary else ssg_secondary(args.steps, args.warmup, world, rank)
     fknn = None if args.no_secondary else feature_knn_secondary(args.steps, max(args.warmup, 3),
                                                                 world, rank, flush)
+    strong = None if args.no_secondary else ssg_strong_secondary(min(args.steps, 20),
+                                                                 max(args.warmup, 3), world, rank)
+    c5 = None if args.no_secondary else config5_secondary(min(args.steps, 3), 1, world, rank)
+    ar_us = loss_all_reduce_us(world)
 
     # Roofline of the dominant kernel: the nearest search (8 separately rounded
     # flops per unique pair) against the FP32 pipe: 128 rounded fp32 ops per
@@ -791,6 +907,10 @@ def run_b200(args, world, rank, local):
                                "directions in one pass)",
                      "bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
+                     "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                       "launch of this kernel in the ncu capture summarised in "
+                                       "profiles/chamfer_sym3_config2.md (same workload), not "
+                                       "measured in this run",
                      "kernel_ms": kernel_ms,
                      "work": f"{FLOPS_PER_PAIR} flop x {local_pairs} unique pairs per launch",
                      "peak_source": "nominal FP32 pipe rate for separately rounded add/sub/mul: "
@@ -805,6 +925,16 @@ def run_b200(args, world, rank, local):
         out["secondary"] = secondary
     if fknn:
         out["secondary_feature_knn"] = fknn
+    if strong:
+        out["secondary_config1_strong"] = strong
+    if c5:
+        out["secondary_config5"] = c5
+    if ar_us is not None:
+        out["collectives"] = {
+            "chamfer_loss_all_reduce_us": ar_us,
+            "note": "the Chamfer step's only collective (4-byte all_reduce of the loss "
+                    "partials) runs asynchronously during the backward; this is its latency "
+                    "alone (mean of 50, max over ranks)"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline_sample()
     return out

@@ -12,17 +12,17 @@
 // ranking decision comes from the exact fp32 SD.  Design:
 //
 //  1. Pack (fknn_pack_kernel, fknn_norms_kernel): queries and references are
-//     split as p = hi + lo (hi = bf16(p), lo = bf16(p - hi)) and written once
-//     in the operand layout of the MMA (per 128-row tile, K-major core
-//     matrices), so a tile reaches shared memory with one bulk copy; norms
+//     rounded to tf32 (cvt.rna: 11 significant bits) and written once in the
+//     operand layout of the MMA (per 128-row tile, K-major core matrices), so
+//     a tile reaches shared memory with one bulk copy; norms
 //     n(p) = sum of p_t^2 (fp32), padded with +inf per 128-reference tile;
 //     per cloud the largest reference norm and a flag for non-finite or huge
 //     norms (such clouds skip the tensor path).
 //  2. Approximate scores (fknn_tc_kernel): a CTA owns 128 queries; warp 0
 //     streams 128-reference tiles into a 2-stage shared-memory ring with
-//     cp.async.bulk, warp 1 issues tcgen05.mma kind::f16 (bf16 x bf16 -> fp32,
-//     M = 128, N = 128, K = 16): dot ~= hi.hi' + hi.lo' + lo.hi' into one of
-//     two TMEM accumulators (128 lanes x 128 columns each), and warps 2-5 (one
+//     cp.async.bulk, warp 1 issues tcgen05.mma kind::tf32 (tf32 x tf32 -> fp32,
+//     M = 128, N = 128, K = 8): dot ~= tf32(q).tf32(r), one product, into one
+//     of two TMEM accumulators (128 lanes x 128 columns each), and warps 2-5 (one
 //     per TMEM lane quarter, one thread per query) read the other accumulator
 //     with tcgen05.ld and form s_j = n(r_j) - 2 dot'_j, so SD'_j = n(q) + s_j
 //     approximates SD_j with |SD'_j - SD_j| <= eps(q) = C_K (n(q) + max n(r)).
@@ -39,17 +39,20 @@
 //     ranked by (SD, index).  A query whose list overflowed, or whose cloud
 //     was flagged, is scanned exactly over all references instead.
 //
-// Error bound C_K (per unit of n(q) + n(r), K = D padded to 16): the dropped
-// lo.lo' term and the residual of lo are each below 2^-16 |q_t||r_t|; fp32
+// Error bound C_K (per unit of n(q) + n(r), K = D padded to 16): rounding to
+// tf32 moves each coordinate by at most u|p| with u = 2^-11, so a product
+// q_t r_t moves by at most (2u + u^2)|q_t||r_t| (the tf32 products are exact
+// in fp32), and the dot product by (2u + u^2)(n(q) + n(r)) / 2; fp32
 // accumulation inside the tensor core, the norms, the score FMA and the
-// reference's own rounding add the rest.  C_K = 2 * (2^-13 + 3K 2^-21 +
-// (3D + 16) 2^-24) is about twice the sum of those terms.
+// reference's own rounding add the rest.  C_K = 2 * (2^-10 + 2^-22 + K 2^-21 +
+// (3D + 16) 2^-24) is about twice the sum of those terms.  (Three bf16
+// products hi.hi' + hi.lo' + lo.hi' give a bound 8x tighter for 3x the MMA
+// work; on the config-4 shapes the tf32 bound adds about two candidates per
+// query, which the re-rank absorbs.)
 //
 // Every wait on an mbarrier is bounded (kWaitNs of %globaltimer); on expiry
 // the CTA records status 1, the waiting role stops, the rows of the CTA are
 // sent to the exact path, and the TMEM is freed before the CTA exits.
-#include <cuda_bf16.h>
-
 #include <string>
 
 #include "../../include/mpo_b200.h"
@@ -70,31 +73,49 @@ constexpr int kThreadsTC = 576;   // warp 0 producer, warp 1 MMA, warps 2-17 epi
 constexpr unsigned long long kWaitNs = 2000000000ull;
 constexpr float kHuge = 1.15292150e18f;  // 2^60: larger norms go to the exact path
 
-// Operand layout of one 128-row tile and one bf16 part (hi or lo), K-major
-// core matrices without swizzle: element (row, t) sits at
-//   (row / 8) * SBO + (t / 8) * 128 + (row % 8) * 16 + (t % 8) * 2,
-// SBO = Kpad / 8 * 128.  A tile block holds the hi part, then the lo part.
+// Operand layout of one 128-row tile of tf32 values, K-major core matrices
+// (8 rows x 16 bytes) without swizzle: element (row, t) sits at
+//   (row / 8) * SBO + (t / 4) * 128 + (row % 8) * 16 + (t % 4) * 4,
+// SBO = Kpad / 4 * 128.
 __host__ __device__ constexpr int kpad_of(int D) { return (D + 15) / 16 * 16; }
-__host__ __device__ constexpr int part_bytes(int Kpad) { return 128 * Kpad * 2; }
+__host__ __device__ constexpr int part_bytes(int Kpad) { return 128 * Kpad * 4; }
 
-// Shared memory: A (kQT tiles x 2 parts) | 2 stages x B (2 parts) | 4-slot ring of the
+// Shared memory: A (kQT tiles) | nst stages x B | kNySlots-slot ring of the
 // tiles' reference norms | barriers.  The norms have their own ring so that a
 // B stage is refilled as soon as the MMAs have read it, while the epilogue of
-// that tile still reads its norms.
-constexpr int kNySlots = 4;
+// that tile still reads its norms.  With one tf32 product per tile the MMAs
+// take about 1.1 K cycles per reference tile, less than a 32 KiB bulk copy's
+// latency, so the ring is as deep as shared memory allows (nst = 4 up to
+// D = 64, fewer for wider features; chosen at launch).
+constexpr int kMaxStages = 4;
+constexpr int kNySlots = 8;
+// Barrier indices: full[kMaxStages] | empty[kMaxStages] | accf[2] | acce[2] |
+// afull | nfull[kNySlots] | nempty[kNySlots]; then the TMEM address and the
+// abort flag.
+constexpr int kBarFull = 0, kBarEmpty = kMaxStages, kBarAccF = 2 * kMaxStages,
+              kBarAccE = kBarAccF + 2, kBarAFull = kBarAccE + 2, kBarNyFull = kBarAFull + 1,
+              kBarNyEmpty = kBarNyFull + kNySlots, kBarCount = kBarNyEmpty + kNySlots;
+constexpr int kBarBytes = 256;
+static_assert(kBarCount * 8 + 8 <= kBarBytes, "barrier region");
 struct TcSmem {
     int part, a_off, b_off, stage_bytes, ny_off, bar_off, total;
-    __host__ __device__ TcSmem(int Kpad) {
+    __host__ __device__ TcSmem(int Kpad, int nst) {
         part = part_bytes(Kpad);
         a_off = 0;
-        b_off = kQT * 2 * part;
-        stage_bytes = 2 * part;
-        ny_off = b_off + 2 * stage_bytes;
+        b_off = kQT * part;
+        stage_bytes = part;
+        ny_off = b_off + nst * stage_bytes;
         if (ny_off - b_off < 66 * kRows * 4) ny_off = b_off + 66 * kRows * 4;  // epilogue handoff
         bar_off = ny_off + kNySlots * kTN * 4;
-        total = bar_off + 192;
+        total = bar_off + kBarBytes;
     }
 };
+constexpr int kSmemLimit = 232448;  // opt-in shared memory per CTA on sm_100
+inline int stages_for(int Kpad) {
+    for (int nst = kMaxStages; nst > 2; --nst)
+        if (TcSmem(Kpad, nst).total <= kSmemLimit) return nst;
+    return 2;
+}
 
 // ---- PTX wrappers (tcgen05, mbarrier, bulk copies, proxies) -----------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -150,15 +171,15 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
     return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
-// Instruction descriptor: kind::f16, A = B = bf16 (K-major), D = f32, M = 128,
-// N = kTN.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTN >> 3) << 17) |
+// Instruction descriptor: kind::tf32, A = B = tf32 (format 2, K-major), D =
+// f32, M = 128, N = kTN.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kTN >> 3) << 17) |
                             ((uint32_t)(kTM >> 4) << 24);
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
         ::"r"(d_tmem), "l"(a), "l"(b), "r"(kIdesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
         : "memory");
 }
@@ -186,20 +207,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ uint32_t bf16_bits(float x) {
-    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
-}
-// hi/lo split of 8 floats into two 16-byte rows of 8 bf16.
-__device__ __forceinline__ void split8(const float (&x)[8], uint4& hi, uint4& lo) {
-    uint32_t h[8], l[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        h[i] = bf16_bits(x[i]);
-        const float hf = __uint_as_float(h[i] << 16);
-        l[i] = bf16_bits(__fsub_rn(x[i], hf));
-    }
-    hi = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
-    lo = make_uint4(l[0] | (l[1] << 16), l[2] | (l[3] << 16), l[4] | (l[5] << 16), l[6] | (l[7] << 16));
+// Round to tf32 (nearest, ties away from zero): 11 significant bits, the
+// low 13 bits of the result are zero.
+__device__ __forceinline__ uint32_t tf32_bits(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -221,9 +234,9 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
 }
 
 // ---- 1. pack and norms --------------------------------------------------------
-// Thread per (row, 8-feature chunk) of the padded tiles; rows past n and
-// features past D are zero.  vec: rows are read as float4 (D % 4 == 0 and
-// 16-byte aligned bases).
+// Thread per (row, 8-feature chunk) of the padded tiles (two 16-byte core-
+// matrix rows); rows past n and features past D are zero.  vec: rows are read
+// as float4 (D % 4 == 0 and 16-byte aligned bases).
 __global__ void fknn_pack_kernel(const float* __restrict__ p, int64_t B, int64_t n, int D, int Kpad,
                                  int64_t tiles, int vec, unsigned char* __restrict__ out) {
     const int chunks = Kpad / 8;
@@ -248,13 +261,12 @@ __global__ void fknn_pack_kernel(const float* __restrict__ p, int64_t B, int64_t
 #pragma unroll
         for (int t = 0; t < 8; ++t) x[t] = (live && c * 8 + t < D) ? src[t] : 0.f;
     }
-    uint4 hi, lo;
-    split8(x, hi, lo);
-    const int part = part_bytes(Kpad);
-    unsigned char* blk = out + (size_t)(b * tiles + tile) * 2 * part;
-    const int off = (rr >> 3) * (Kpad / 8 * 128) + c * 128 + (rr & 7) * 16;
-    *reinterpret_cast<uint4*>(blk + off) = hi;
-    *reinterpret_cast<uint4*>(blk + part + off) = lo;
+    const uint4 lo4 = make_uint4(tf32_bits(x[0]), tf32_bits(x[1]), tf32_bits(x[2]), tf32_bits(x[3]));
+    const uint4 hi4 = make_uint4(tf32_bits(x[4]), tf32_bits(x[5]), tf32_bits(x[6]), tf32_bits(x[7]));
+    unsigned char* blk = out + (size_t)(b * tiles + tile) * part_bytes(Kpad);
+    const int off = (rr >> 3) * (Kpad / 4 * 128) + (2 * c) * 128 + (rr & 7) * 16;
+    *reinterpret_cast<uint4*>(blk + off) = lo4;
+    *reinterpret_cast<uint4*>(blk + off + 128) = hi4;
 }
 
 // Thread per point: nq[b*M + i]; nr padded per cloud to tiles*128 entries
@@ -313,7 +325,8 @@ __global__ void fknn_norms_kernel(const float* __restrict__ q, const float* __re
 
 __device__ __forceinline__ float eps_coef(int D) {
     const int K = kpad_of(D);
-    return 2.f * (1.220703125e-4f /* 2^-13 */ + 3.f * (float)K * 4.76837158203125e-7f /* 2^-21 */ +
+    return 2.f * (9.765625e-4f /* 2^-10 */ + 2.384185791015625e-7f /* 2^-22 */ +
+                  (float)K * 4.76837158203125e-7f /* 2^-21 */ +
                   (3.f * (float)D + 16.f) * 5.9604644775390625e-8f /* 2^-24 */);
 }
 
@@ -330,34 +343,36 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                const float* __restrict__ nq, const float* __restrict__ nr,
                const unsigned* __restrict__ nmax, const int* __restrict__ bad,
                float* __restrict__ ubound, unsigned* __restrict__ counts, uint2* __restrict__ cand,
-               int* __restrict__ status) {
+               int* __restrict__ status, int nst) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int b = blockIdx.y;
     const int64_t mt = blockIdx.x;
     if (bad[b]) return;  // uniform: the cloud goes to the exact path
     const int Kpad = kpad_of(D);
-    const TcSmem L(Kpad);
+    const TcSmem L(Kpad, nst);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar = sbase + L.bar_off;
     // barrier addresses: full 0,1 | empty 2,3 | accf 4,5 | acce 6,7 | afull 8 |
     // norms full 9-12 | norms empty 13-16
     auto B_ = [&](int i) { return bar + 8u * (uint32_t)i; };
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.bar_off + 160);
-    int* s_abort = reinterpret_cast<int*>(smem + L.bar_off + 164);
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.bar_off + kBarCount * 8);
+    int* s_abort = reinterpret_cast<int*>(smem + L.bar_off + kBarCount * 8 + 4);
 
     if (warp == 0) tmem_alloc(smem_u32(s_tmem), 2 * kQT * kTN);
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(B_(0 + i), 1);
-            mbar_init(B_(2 + i), 1);
-            mbar_init(B_(4 + i), 1);
-            mbar_init(B_(6 + i), 4 * kQT);
+        for (int i = 0; i < kMaxStages; ++i) {
+            mbar_init(B_(kBarFull + i), 1);
+            mbar_init(B_(kBarEmpty + i), 1);
         }
-        mbar_init(B_(8), 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(B_(kBarAccF + i), 1);
+            mbar_init(B_(kBarAccE + i), 4 * kQT);
+        }
+        mbar_init(B_(kBarAFull), 1);
         for (int i = 0; i < kNySlots; ++i) {
-            mbar_init(B_(9 + i), 1);
-            mbar_init(B_(13 + i), 4 * kQT);
+            mbar_init(B_(kBarNyFull + i), 1);
+            mbar_init(B_(kBarNyEmpty + i), 4 * kQT);
         }
         *s_abort = 0;
         mbar_fence_init();
@@ -365,78 +380,74 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-    const uint32_t sbo = (uint32_t)(Kpad / 8 * 128);
-    const uint32_t a_bytes = (uint32_t)(2 * L.part);
+    const uint32_t sbo = (uint32_t)(Kpad / 4 * 128);
+    const uint32_t a_bytes = (uint32_t)L.part;
 
     if (warp == 0) {
         // ---------------- producer ----------------
         if (lane == 0) {
             // kQT consecutive query tiles (the pack has mtiles rounded up).
             const unsigned char* asrc = qpack + (size_t)(b * mtiles + mt * kQT) * a_bytes;
-            bulk_expect(B_(8), kQT * a_bytes);
-            bulk_copy(sbase + L.a_off, asrc, kQT * a_bytes, B_(8));
+            bulk_expect(B_(kBarAFull), kQT * a_bytes);
+            bulk_copy(sbase + L.a_off, asrc, kQT * a_bytes, B_(kBarAFull));
             int64_t issued = 0;
             for (int64_t t = 0; t < ntiles; ++t) {
-                const int st = (int)(t & 1);
-                const uint32_t n = (uint32_t)(t >> 1);
-                if (!mbar_wait(B_(2 + st), (n & 1) ^ 1) || *(volatile int*)s_abort) {
+                const int st = (int)(t % nst);
+                const uint32_t n = (uint32_t)(t / nst);
+                if (!mbar_wait(B_(kBarEmpty + st), (n & 1) ^ 1) || *(volatile int*)s_abort) {
                     atomicExch(status, 1);
                     *(volatile int*)s_abort = 1;
                     break;
                 }
                 const uint32_t dst = sbase + L.b_off + (uint32_t)(st * L.stage_bytes);
-                bulk_expect(B_(0 + st), a_bytes);
-                bulk_copy(dst, rpack + (size_t)(b * ntiles + t) * a_bytes, a_bytes, B_(0 + st));
-                const int ns = (int)(t & 3);
-                const uint32_t nn = (uint32_t)(t >> 2);
-                if (!mbar_wait(B_(13 + ns), (nn & 1) ^ 1)) {
+                bulk_expect(B_(kBarFull + st), a_bytes);
+                bulk_copy(dst, rpack + (size_t)(b * ntiles + t) * a_bytes, a_bytes,
+                          B_(kBarFull + st));
+                const int ns = (int)(t % kNySlots);
+                const uint32_t nn = (uint32_t)(t / kNySlots);
+                if (!mbar_wait(B_(kBarNyEmpty + ns), (nn & 1) ^ 1)) {
                     atomicExch(status, 1);
                     *(volatile int*)s_abort = 1;
                     ++issued;
                     break;
                 }
-                bulk_expect(B_(9 + ns), kTN * 4);
+                bulk_expect(B_(kBarNyFull + ns), kTN * 4);
                 bulk_copy(sbase + L.ny_off + (uint32_t)(ns * kTN * 4),
-                          nr + (size_t)(b * ntiles + t) * kTN, kTN * 4, B_(9 + ns));
+                          nr + (size_t)(b * ntiles + t) * kTN, kTN * 4, B_(kBarNyFull + ns));
                 ++issued;
             }
             // Copies still in flight (only after an abort) land before exit.
-            mbar_wait(B_(8), 0);
-            for (int64_t t = max64(issued - 2, 0); t < issued; ++t)
-                mbar_wait(B_(0 + (int)(t & 1)), (uint32_t)((t >> 1) & 1));
+            mbar_wait(B_(kBarAFull), 0);
+            for (int64_t t = max64(issued - nst, 0); t < issued; ++t)
+                mbar_wait(B_(kBarFull + (int)(t % nst)), (uint32_t)((t / nst) & 1));
             for (int64_t t = max64(issued - kNySlots, 0); t < issued; ++t)
-                mbar_wait(B_(9 + (int)(t & 3)), (uint32_t)((t >> 2) & 1));
+                mbar_wait(B_(kBarNyFull + (int)(t % kNySlots)), (uint32_t)((t / kNySlots) & 1));
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            bool ok = mbar_wait(B_(8), 0);
+            bool ok = mbar_wait(B_(kBarAFull), 0);
             for (int64_t t = 0; t < ntiles && ok; ++t) {
-                const int st = (int)(t & 1), ac = (int)(t & 1);
-                const uint32_t n = (uint32_t)(t >> 1);
-                ok = mbar_wait(B_(0 + st), n & 1) && mbar_wait(B_(6 + ac), (n & 1) ^ 1) &&
-                     !*(volatile int*)s_abort;
+                const int st = (int)(t % nst), ac = (int)(t & 1);
+                const uint32_t n = (uint32_t)(t / nst), na = (uint32_t)(t >> 1);
+                ok = mbar_wait(B_(kBarFull + st), n & 1) &&
+                     mbar_wait(B_(kBarAccE + ac), (na & 1) ^ 1) && !*(volatile int*)s_abort;
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t b0 = sbase + L.b_off + (uint32_t)(st * L.stage_bytes);
-                const uint32_t part = (uint32_t)L.part;
                 for (int qt = 0; qt < kQT; ++qt) {
                     // Accumulator ac of query tile qt: columns (ac * kQT + qt) * kTN.
                     const uint32_t d = tmem + (uint32_t)((ac * kQT + qt) * kTN);
                     const uint32_t a0 = sbase + L.a_off + (uint32_t)qt * a_bytes;
-                    for (int s = 0; s < Kpad / 16; ++s) {
+                    // K = 8 tf32 per MMA: two core matrices (2 x 128 bytes) per step.
+                    for (int s = 0; s < Kpad / 8; ++s) {
                         const uint32_t ko = (uint32_t)s * 256u;
-                        const uint64_t ahi = smem_desc(a0 + ko, 128, sbo);
-                        const uint64_t alo = smem_desc(a0 + part + ko, 128, sbo);
-                        const uint64_t bhi = smem_desc(b0 + ko, 128, sbo);
-                        const uint64_t blo = smem_desc(b0 + part + ko, 128, sbo);
-                        mma_bf16(d, ahi, bhi, s == 0 ? 0u : 1u);
-                        mma_bf16(d, ahi, blo, 1u);
-                        mma_bf16(d, alo, bhi, 1u);
+                        mma_tf32(d, smem_desc(a0 + ko, 128, sbo), smem_desc(b0 + ko, 128, sbo),
+                                 s == 0 ? 0u : 1u);
                     }
                 }
-                mma_commit(B_(2 + st));  // stage st may be refilled
-                mma_commit(B_(4 + ac));  // accumulator ac is ready
+                mma_commit(B_(kBarEmpty + st));  // stage st may be refilled
+                mma_commit(B_(kBarAccF + ac));   // accumulator ac is ready
             }
             if (!ok) {
                 atomicExch(status, 1);
@@ -470,8 +481,9 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
         for (int64_t t = group; t < ntiles; t += 2) {
             const int ac = group;
             const uint32_t n = (uint32_t)(t >> 1);
-            const int ns = (int)(t & 3);
-            const bool got = mbar_wait(B_(4 + ac), n & 1) && mbar_wait(B_(9 + ns), (uint32_t)((t >> 2) & 1));
+            const int ns = (int)(t % kNySlots);
+            const bool got = mbar_wait(B_(kBarAccF + ac), n & 1) &&
+                             mbar_wait(B_(kBarNyFull + ns), (uint32_t)((t / kNySlots) & 1));
             ok = __all_sync(FULL_MASK, got) && !*(volatile int*)s_abort;
             if (!ok) break;
             tc_fence_after();
@@ -531,8 +543,8 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(B_(6 + ac));   // accumulator read
-                mbar_arrive(B_(13 + ns));  // norms read
+                mbar_arrive(B_(kBarAccE + ac));     // accumulator read
+                mbar_arrive(B_(kBarNyEmpty + ns));  // norms read
             }
         }
         if (!ok) {
@@ -909,7 +921,7 @@ inline Scratch carve(void* base, int64_t B, int64_t M, int64_t N, int64_t D) {
     };
     // Query tiles rounded up to whole CTAs (kQT tiles each).
     const int64_t mt = ceil_div(M, kRows) * kQT, nt = ceil_div(N, kTN);
-    const size_t tile = 2 * (size_t)part_bytes(kpad_of((int)D));
+    const size_t tile = (size_t)part_bytes(kpad_of((int)D));
     s.qpack = take(tile * B * mt);
     s.rpack = take(tile * B * nt);
     s.nq = reinterpret_cast<float*>(take(sizeof(float) * B * M));
@@ -951,7 +963,8 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
         query, ref, B, M, N, nt, D, vec, w.nq, w.nr, w.nmax, w.bad);
     st = check_launch("fknn_norms_kernel");
     if (st) return st;
-    const TcSmem L(Kpad);
+    const int nst = stages_for(Kpad);
+    const TcSmem L(Kpad, nst);
     auto k1 = fknn_tc_kernel<1, KCAP>;
     auto k2 = fknn_tc_kernel<2, KCAP>;
     if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
@@ -961,11 +974,11 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");
     dim3 grid((unsigned)(mt / kQT), (unsigned)B);
     k1<<<grid, kThreadsTC, L.total, s>>>(w.qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
-                                         w.bad, w.ubound, w.counts, w.cand, w.status);
+                                         w.bad, w.ubound, w.counts, w.cand, w.status, nst);
     st = check_launch("fknn_tc_kernel<1>");
     if (st) return st;
     k2<<<grid, kThreadsTC, L.total, s>>>(w.qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
-                                         w.bad, w.ubound, w.counts, w.cand, w.status);
+                                         w.bad, w.ubound, w.counts, w.cand, w.status, nst);
     st = check_launch("fknn_tc_kernel<2>");
     if (st) return st;
     auto rk = !vec ? fknn_rerank_kernel<0, 0>

@@ -367,6 +367,179 @@ knn3p_kernel(const float* __restrict__ query, const float* __restrict__ ref, Lay
 }
 
 // --------------------------------------------------------------------------
+// k <= 3 (three_nn, and kNN with k <= 3), D == 3: thread per (query, split)
+// with the three best held in registers and updated without branches.  A
+// warp's 32 queries differ, so on moderate clouds some lane improves its list
+// on almost every step; a divergent insertion would make the whole warp
+// replay it, and a 32-wide warp select (knn_wq3_kernel) spends most of its
+// instructions merging candidates that k = 3 never needs.  Here a point
+// costs its share of the packed distance (four f32x2 instructions), and, in
+// steps where some lane of the warp has a point below its third distance,
+// one sorted-triple update per point: three compares, three min/max and
+// five selects, issued whether or not the point enters.  Within a thread the
+// reference index grows, so strict < keeps the lowest index on ties.  While a
+// list is not full, or holds a NaN (three_nn ranks NaN last), a step takes
+// the general TopK::offer instead.  Splits merge in (SD, index) order as in
+// knn3p_kernel.
+template <int POLICY, bool FLAT>
+__global__ void __launch_bounds__(kThreads, 2)
+knn3t_kernel(const float* __restrict__ query, const float* __restrict__ ref, Layout L, int k,
+             int S, float* __restrict__ dist, int64_t* __restrict__ idx64,
+             int32_t* __restrict__ idx32, float* __restrict__ sqdist) {
+    constexpr int K = 3;
+    extern __shared__ float4 smem4[];
+    float4* txy = smem4;                    // [2][kTile / 2]
+    float4* tz = smem4 + kTile;             // [2][kTile / 4]
+    const int qpc = kThreads / S;
+    Span sp;
+    if (!locate<FLAT>(L, qpc, sp)) return;  // CTA-uniform
+    const int tid = threadIdx.x;
+    const int split = tid / qpc;
+    const int ql = tid % qpc;
+    const int64_t q = sp.q0 + ql;
+    const bool active = q < sp.q1;
+    const int64_t N = sp.n;
+    const float* __restrict__ r = ref + (size_t)sp.r0 * 3;
+
+    float qx = 0.f, qy = 0.f, qz = 0.f;
+    if (active) {
+        const float* qp = query + (size_t)q * 3;
+        qx = qp[0];
+        qy = qp[1];
+        qz = qp[2];
+    }
+    const f32x2 X = pack2(qx, qx), Y = pack2(qy, qy), Z = pack2(qz, qz);
+    TopK<K, POLICY> top;
+    top.init(k);
+
+    const int64_t ntiles = ceil_div(N, kTile);
+    const int slice = kTile / S;  // multiple of 8
+    constexpr int kLoads = 3 * kTile / kThreads;
+    float pre[kLoads];
+    auto load_tile = [&](int64_t t) {
+        const int64_t base = t * kTile * 3;
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) {
+            const int64_t e = base + tid + (int64_t)u * kThreads;
+            pre[u] = e < N * 3 ? r[e] : 0.f;
+        }
+    };
+    auto store_tile = [&](int buf) {
+        float* xy = reinterpret_cast<float*>(txy + buf * (kTile / 2));
+        float* zz = reinterpret_cast<float*>(tz + buf * (kTile / 4));
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) {
+            const int e = tid + u * kThreads;
+            const int pnt = e / 3, crd = e % 3;
+            if (crd < 2) xy[(pnt >> 1) * 4 + 2 * crd + (pnt & 1)] = pre[u];
+            else zz[pnt] = pre[u];
+        }
+    };
+    if (ntiles > 0) {
+        load_tile(0);
+        store_tile(0);
+    }
+    __syncthreads();
+    for (int64_t t = 0; t < ntiles; ++t) {
+        const int buf = (int)(t & 1);
+        if (t + 1 < ntiles) load_tile(t + 1);
+        if (active) {
+            const ulonglong2* xy =
+                reinterpret_cast<const ulonglong2*>(txy + buf * (kTile / 2) + split * (slice / 2));
+            const ulonglong2* zz =
+                reinterpret_cast<const ulonglong2*>(tz + buf * (kTile / 4) + split * (slice / 4));
+            const int64_t j0 = t * kTile + split * slice;
+            const int cnt = (int)max64(0, min64(slice, N - j0));
+            auto step = [&](uint32_t a, uint32_t z, int e, int valid) {
+                f32x2 ax0, ay0, ax1, ay1, ax2, ay2, ax3, ay3, z01, z23, z45, z67;
+                lds_pairs<0>(a, ax0, ay0);
+                lds_pairs<16>(a, ax1, ay1);
+                lds_pairs<32>(a, ax2, ay2);
+                lds_pairs<48>(a, ax3, ay3);
+                lds_pairs<0>(z, z01, z23);
+                lds_pairs<16>(z, z45, z67);
+                float d[8];
+                unpack2(sqd3x2(X, Y, Z, ax0, ay0, z01), d[0], d[1]);
+                unpack2(sqd3x2(X, Y, Z, ax1, ay1, z23), d[2], d[3]);
+                unpack2(sqd3x2(X, Y, Z, ax2, ay2, z45), d[4], d[5]);
+                unpack2(sqd3x2(X, Y, Z, ax3, ay3, z67), d[6], d[7]);
+                const uint32_t jb = (uint32_t)(j0 + e);
+                if (!top.full() || isnan(top.d[K - 1])) {
+                    for (int u = 0; u < valid; ++u) top.offer(d[u], jb + u);
+                    return;
+                }
+                const unsigned mask = __activemask();
+                const float m = fminf(fminf(fminf(d[0], d[1]), fminf(d[2], d[3])),
+                                      fminf(fminf(d[4], d[5]), fminf(d[6], d[7])));
+                if (!__any_sync(mask, m < top.d[K - 1])) return;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    // Sorted-triple update (no branch: a per-point vote would
+                    // serialise the warp on the list's dependency chain); a
+                    // NaN or a point past the slice compares false
+                    // everywhere and leaves the list as it is.
+                    const float v = u < valid ? d[u] : NAN;
+                    const uint32_t j = jb + u;
+                    const bool c0 = v < top.d[0], c1 = v < top.d[1], c2 = v < top.d[2];
+                    top.d[2] = c1 ? top.d[1] : (c2 ? v : top.d[2]);
+                    top.i[2] = c1 ? top.i[1] : (c2 ? j : top.i[2]);
+                    top.d[1] = c0 ? top.d[0] : (c1 ? v : top.d[1]);
+                    top.i[1] = c0 ? top.i[0] : (c1 ? j : top.i[1]);
+                    top.d[0] = c0 ? v : top.d[0];
+                    top.i[0] = c0 ? j : top.i[0];
+                }
+            };
+            const int full = cnt & ~7;
+            uint32_t a = (uint32_t)__cvta_generic_to_shared(xy);
+            uint32_t z = (uint32_t)__cvta_generic_to_shared(zz);
+            for (int e = 0; e < full; e += 8, a += 64, z += 32) step(a, z, e, 8);
+            if (full < cnt) step(a, z, full, cnt - full);
+        }
+        if (t + 1 < ntiles) store_tile(buf ^ 1);
+        __syncthreads();
+    }
+
+    if (S > 1) {
+        float* md = reinterpret_cast<float*>(smem4);
+        uint32_t* mi = reinterpret_cast<uint32_t*>(md + (size_t)kThreads * K);
+        if (split > 0) {
+#pragma unroll
+            for (int s2 = 0; s2 < K; ++s2) {
+                md[(size_t)tid * K + s2] = top.d[s2];
+                mi[(size_t)tid * K + s2] = top.i[s2];
+            }
+        }
+        __syncthreads();
+        if (split == 0 && active) {
+            for (int o = 1; o < S; ++o) {
+                const int src = o * qpc + ql;
+                for (int s2 = K - k; s2 < K; ++s2) {
+                    const uint32_t j = mi[(size_t)src * K + s2];
+                    if (j == kNoIndex) break;
+                    const float dd = md[(size_t)src * K + s2];
+                    if (top.full() && !before<POLICY>(dd, j, top.d[K - 1], top.i[K - 1])) break;
+                    top.offer(dd, j);
+                }
+            }
+        }
+    }
+    if (split != 0 || !active) return;
+    const size_t row = (size_t)q * (size_t)k;
+#pragma unroll
+    for (int s2 = 0; s2 < K; ++s2) {
+        const int l = s2 - top.base;
+        if (l >= 0) {
+            const bool filled = l < top.cnt;
+            const float dd = filled ? top.d[s2] : INFINITY;
+            if (dist) dist[row + l] = sqrtf(dd);
+            if (sqdist) sqdist[row + l] = dd;
+            if (idx64) idx64[row + l] = filled ? sp.obase + (int64_t)top.i[s2] : -1;
+            if (idx32) idx32[row + l] = filled ? (int32_t)top.i[s2] : -1;
+        }
+    }
+}
+
+// --------------------------------------------------------------------------
 // Generic D kernel (feature space): the query row and the reference tile
 // both sit in shared memory; SD accumulates in increasing dimension order.
 constexpr int kFeatThreads = 128;
@@ -800,6 +973,26 @@ int launch_knn3p(const float* query, const float* ref, const Layout& L, int64_t 
     return check_launch("knn3p_kernel");
 }
 
+// Splits for knn3t_kernel: enough threads for about 512 per SM; each split
+// keeps its own list, so fewer splits mean fewer list updates per point.
+template <int POLICY, bool FLAT = false>
+int launch_knn3t(const float* query, const float* ref, const Layout& L, int64_t B,
+                 int64_t max_n, int k, float* dist, int64_t* idx64, int32_t* idx32,
+                 float* sqdist, cudaStream_t s) {
+    const int64_t want = (int64_t)sm_count() * 512;
+    int S = 1;
+    while (S < 8 && B * L.M * S < want && max_n >= (int64_t)kTile / S) S *= 2;
+    const int qpc = kThreads / S;
+    const size_t smem = (size_t)(kTile + kTile / 2) * sizeof(float4);
+    auto kern = knn3t_kernel<POLICY, FLAT>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+        return fail(kCudaError, "knn: cannot raise the shared-memory limit");
+    kern<<<search_grid(L, B, qpc, FLAT), kThreads, smem, s>>>(query, ref, L, k, S, dist, idx64,
+                                                              idx32, sqdist);
+    return check_launch("knn3t_kernel");
+}
+
 template <int K, bool FLAT = false>
 int launch_knnd(const float* query, const float* ref, const Layout& L, int64_t B, int D, int k,
                 float* dist, int64_t* idx64, float* sqdist, cudaStream_t s) {
@@ -830,6 +1023,9 @@ int launch_knnd(const float* query, const float* ref, const Layout& L, int64_t B
 template <int POLICY3, bool FLAT>
 int run_knn(const float* query, const float* ref, const Layout& L, int64_t B, int64_t max_n,
             int64_t D, int k, float* dist, int64_t* idx, float* sqdist, cudaStream_t s) {
+    if (D == 3 && k <= 3)
+        return launch_knn3t<POLICY3, FLAT>(query, ref, L, B, max_n, k, dist, idx, nullptr, sqdist,
+                                           s);
     if (D == 3 && k <= 32 && use_wq3(max_n))
         return launch_wq3<POLICY3, FLAT>(query, ref, L, B, k, dist, idx, nullptr, sqdist, s);
     if (D == 3 && k <= 32) {
@@ -915,11 +1111,8 @@ int mpo_three_nn(const float* unknown, const float* known, int64_t B, int64_t N,
     MPO_REQUIRE(M >= 3, "three_nn needs at least 3 known points");
     MPO_REQUIRE(M < (int64_t)0x7fffffff, "M must be below 2**31");
     MPO_REQUIRE(unknown && known && dist && idx, "null pointer");
-    if (use_wq3(M))
-        return launch_wq3<kNaNLast>(unknown, known, dense_layout(N, M), B, 3, dist, nullptr, idx,
-                                    nullptr, (cudaStream_t)stream);
-    return launch_knn3<4, kNaNLast>(unknown, known, B, N, M, 3, dist, nullptr, idx, nullptr,
-                                    (cudaStream_t)stream);
+    return launch_knn3t<kNaNLast>(unknown, known, dense_layout(N, M), B, M, 3, dist, nullptr,
+                                  idx, nullptr, (cudaStream_t)stream);
 }
 
 }  // extern "C"

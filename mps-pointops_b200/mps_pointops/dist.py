@@ -55,21 +55,49 @@ def all_gather_shards(local: torch.Tensor, total: int, dim: int = 0, group=None)
     return torch.cat(parts).movedim(0, dim)
 
 
+class PendingLoss:
+    """The global Chamfer loss of :func:`chamfer_distance_sharded` with
+    ``overlap=True``: its all-reduce runs on the communication stream while the
+    caller goes on (backward, next step); :meth:`value` waits for it (the
+    current stream waits on the collective, the host does not)."""
+
+    def __init__(self, total: torch.Tensor, work):
+        self._total, self._work = total, work
+
+    def value(self) -> torch.Tensor:
+        if self._work is not None:
+            self._work.wait()
+            self._work = None
+        return self._total
+
+
 def chamfer_distance_sharded(x_local: torch.Tensor, y_local: torch.Tensor, batch_total: int,
-                             group=None, local_fn: Callable | None = None) -> torch.Tensor:
+                             group=None, local_fn: Callable | None = None,
+                             overlap: bool = False):
     """Mean/mean squared-L2 Chamfer loss over a batch split across ranks.
 
     ``x_local`` / ``y_local`` hold this rank's clouds (its :func:`shard_range`
     slice of ``batch_total``).  Returns the global loss (identical on every
     rank); its backward yields exactly this rank's slice of the single-GPU
     gradient, because loss = (1/B) * sum over clouds of the per-cloud loss.
+
+    With ``overlap`` it returns ``(local, pending)`` instead: ``local`` is this
+    rank's term (1/B) * sum of its per-cloud losses, whose backward gives the
+    same gradients, and ``pending`` (:class:`PendingLoss`) the global loss,
+    all-reduced asynchronously -- the collective then never stalls the
+    compute stream between forward and backward.
     """
     if local_fn is None:
         from .chamfer import chamfer_distance as local_fn
     partial, _ = local_fn(x_local, y_local, batch_reduction="sum")
+    scale = 1.0 / max(batch_total, 1)
+    if overlap:
+        local = partial * scale
+        total = local.detach().clone()
+        work = dist.all_reduce(total, op=dist.ReduceOp.SUM, group=group, async_op=True)
+        return local, PendingLoss(total, work)
     total = partial.detach().clone()
     dist.all_reduce(total, op=dist.ReduceOp.SUM, group=group)
-    scale = 1.0 / max(batch_total, 1)
     return partial * scale + (total - partial.detach()) * scale
 
 

@@ -67,6 +67,15 @@ def _worker(rank, world, port, results):
         out["loss"] = loss.item()
         out["gx"] = all_gather_shards(xl.grad, B).numpy()
         out["gy"] = all_gather_shards(yl.grad, B).numpy()
+        # overlapped mode: backward on this rank's term, global value later
+        xo = x[lo:hi].clone().requires_grad_()
+        yo = y[lo:hi].clone().requires_grad_()
+        local, pending = chamfer_distance_sharded(xo, yo, B, local_fn=oracle_chamfer,
+                                                  overlap=True)
+        local.backward()
+        out["loss_overlap"] = pending.value().item()
+        out["gx_overlap"] = all_gather_shards(xo.grad, B).numpy()
+        out["gy_overlap"] = all_gather_shards(yo.grad, B).numpy()
         q, r = torch.randn(1, 37, 3, generator=g), torch.randn(1, 200, 3, generator=g)
         d, i = knn_query_sharded(q, r, 5, local_fn=oracle_knn)
         out["knn"] = (d.numpy(), i.numpy())
@@ -109,9 +118,10 @@ def test_world2_gloo_matches_single_process():
     loss, _ = oracle_chamfer(xr, yr)
     (loss / 5).backward()
     for r in (r0, r1):
-        np.testing.assert_allclose(r["loss"], loss.item() / 5, rtol=1e-6)
-        np.testing.assert_allclose(r["gx"], xr.grad.numpy(), rtol=1e-6, atol=1e-7)
-        np.testing.assert_allclose(r["gy"], yr.grad.numpy(), rtol=1e-6, atol=1e-7)
+        for tag in ("", "_overlap"):
+            np.testing.assert_allclose(r["loss" + tag], loss.item() / 5, rtol=1e-6)
+            np.testing.assert_allclose(r["gx" + tag], xr.grad.numpy(), rtol=1e-6, atol=1e-7)
+            np.testing.assert_allclose(r["gy" + tag], yr.grad.numpy(), rtol=1e-6, atol=1e-7)
     q, ref = torch.randn(1, 37, 3, generator=g), torch.randn(1, 200, 3, generator=g)
     wd, wi = oracle_knn(q, ref, 5)
     bd, bi = oracle_ball(q, ref, 0.8, 6)

@@ -168,3 +168,49 @@ def test_three_nn_large_known_cloud(cuda_device):
     d, i = three_nn(unknown.to(cuda_device), known.to(cuda_device))
     np.testing.assert_array_equal(i.cpu().numpy(), want_i)
     np.testing.assert_array_equal(d.cpu().numpy(), want_d)
+
+
+# ---- k <= 3: knn3t_kernel (thread per query, branchless sorted triple) -----------------
+@pytest.mark.parametrize("k", [1, 2, 3])
+@pytest.mark.parametrize("n", [3, 7, 8, 9, 127, 1023, 1024, 1025, 4097, 70000])
+def test_k_at_most_3_matches_oracle(cuda_device, n, k):
+    """Every split count and tile edge of knn3t_kernel, uniform and lattice
+    (exact ties) clouds, against the exact (SD, index) oracle."""
+    g = torch.Generator().manual_seed(n * 7 + k)
+    for ref in (torch.randn(2, n, 3, generator=g),
+                torch.randint(0, 4, (2, n, 3), generator=g).float()):
+        query = torch.randn(2, 1500 if n < 10000 else 300, 3, generator=g)
+        check(query, ref, k, cuda_device)
+
+
+def test_k_at_most_3_nonfinite(cuda_device):
+    """NaN references are dropped and +inf ones ranked (D = 3 kNN), also when
+    they come first in a split and when fewer finite points than k exist."""
+    g = torch.Generator().manual_seed(5)
+    ref = torch.randn(1, 3000, 3, generator=g)
+    ref[0, :5, 0] = float("nan")
+    ref[0, 5:9, 1] = float("inf")
+    ref[0, 1500:1510, 2] = float("nan")
+    q = torch.randn(1, 400, 3, generator=g)
+    for k in (1, 2, 3):
+        check(q, ref, k, cuda_device)
+    tiny = torch.tensor([[[float("nan"), 0, 0], [float("inf"), 0, 0], [1.0, 2, 3],
+                          [float("inf"), 1, 1]]])
+    for k in (1, 2, 3):
+        check(torch.zeros(1, 3, 3), tiny, k, cuda_device)
+
+
+def test_three_nn_thread_kernel_matches_oracle(cuda_device):
+    """three_nn on every split count (NaN ranked last), config 1 shapes."""
+    from mps_pointops import three_nn
+    g = torch.Generator().manual_seed(11)
+    for b, n, m in ((8, 4096, 1024), (2, 5000, 3), (1, 300, 70000), (3, 1, 2049)):
+        unknown = torch.rand(b, n, 3, generator=g)
+        known = torch.rand(b, m, 3, generator=g)
+        if m > 10:
+            known[0, 7, 1] = float("nan")
+            known[-1, m // 2] = float("inf")
+        wd, wi = O.three_nn(unknown.numpy(), known.numpy())
+        d, i = three_nn(unknown.to(cuda_device), known.to(cuda_device))
+        np.testing.assert_array_equal(i.cpu().numpy(), wi)
+        np.testing.assert_array_equal(d.cpu().numpy(), wd)
