@@ -58,6 +58,8 @@ constexpr unsigned long long kSpinLimitNs = 2000000000ull;  // 2 s per step
 constexpr int kLocalBits = 24;
 constexpr unsigned long long kLocalMask = (1ull << kLocalBits) - 1;
 constexpr unsigned long long kSeqMask = 0xffull;
+// Slots one polling lane reads: G <= 32 * kSlotsPerLane CTAs per cloud.
+constexpr int kSlotsPerLane = 5;
 // Overflow tier in shared memory: float4 (x, y, z, min_d2) per point.
 constexpr int kSmemTierPoints = 14336;  // 224 KiB
 
@@ -135,6 +137,7 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
     __shared__ uint32_t s_key[2][32];
     __shared__ uint32_t s_idx[2][32];
     __shared__ uint32_t s_far;
+    __shared__ float s_cxyz[3];
     __shared__ int s_abort;
 
     const int wave_cloud = blockIdx.x / G;
@@ -361,28 +364,45 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
                                  "l"(word)
                                  : "memory");
                 }
-                uint32_t bk = 0u, bi = 0xffffffffu;
+                // Each lane polls its slots c = lane + 32 m until every one
+                // carries this step's sequence, re-reading only the slots not
+                // yet seen.  When a slot is seen, the lane starts loading its
+                // candidate's coordinates from the (read-only) cloud, so the
+                // winner's centroid is in registers when the reduction ends
+                // instead of costing another round trip after the barrier.
+                uint32_t sk[kSlotsPerLane], si[kSlotsPerLane];
+                float sx[kSlotsPerLane], sy[kSlotsPerLane], sz[kSlotsPerLane];
+                unsigned need = 0u, seen = 0u;
+#pragma unroll
+                for (int m = 0; m < kSlotsPerLane; ++m) {
+                    sk[m] = 0u;
+                    si[m] = 0xffffffffu;
+                    sx[m] = sy[m] = sz[m] = 0.f;
+                    if (lane + 32 * m < G) need |= 1u << m;
+                }
                 const unsigned long long t0 = globaltimer_ns();
                 bool abort = false;
                 for (unsigned round = 1;; ++round) {
-                    bool ok = true;
-                    bk = 0u;
-                    bi = 0xffffffffu;
-                    for (int c = lane; c < G; c += 32) {
-                        const unsigned long long v = ld_relaxed_u64(cur + c * kSlotStride);
-                        if (((v >> kLocalBits) & kSeqMask) != seq) {
-                            ok = false;
-                        } else {
-                            const uint32_t kk = (uint32_t)(v >> 32);
-                            const uint32_t ii =
-                                (uint32_t)c * (uint32_t)per_cta + (uint32_t)(v & kLocalMask);
-                            if (kk > bk || (kk == bk && ii < bi)) {
-                                bk = kk;
-                                bi = ii;
+#pragma unroll
+                    for (int m = 0; m < kSlotsPerLane; ++m) {
+                        if (((need & ~seen) >> m) & 1u) {
+                            const int c = lane + 32 * m;
+                            const unsigned long long v = ld_relaxed_u64(cur + c * kSlotStride);
+                            if (((v >> kLocalBits) & kSeqMask) == seq) {
+                                seen |= 1u << m;
+                                sk[m] = (uint32_t)(v >> 32);
+                                si[m] = (uint32_t)c * (uint32_t)per_cta + (uint32_t)(v & kLocalMask);
+                                // A key of 0 marks a CTA without valid points
+                                // (it never wins): nothing to load.
+                                if (sk[m] != 0u && si[m] < (uint32_t)n) {
+                                    sx[m] = p[3 * (size_t)si[m] + 0];
+                                    sy[m] = p[3 * (size_t)si[m] + 1];
+                                    sz[m] = p[3 * (size_t)si[m] + 2];
+                                }
                             }
                         }
                     }
-                    if (__all_sync(FULL_MASK, ok)) break;
+                    if (__all_sync(FULL_MASK, seen == need)) break;
                     if ((round & 63u) == 0u &&
                         (globaltimer_ns() - t0 > kSpinLimitNs || ld_acquire_u32(my_error) != 0u)) {
                         abort = true;
@@ -397,17 +417,34 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
                         s_abort = 1;
                     }
                 } else {
+                    uint32_t bk = 0u, bi = 0xffffffffu;
+                    float bx = 0.f, by = 0.f, bz = 0.f;
+#pragma unroll
+                    for (int m = 0; m < kSlotsPerLane; ++m) {
+                        if (((need >> m) & 1u) && (sk[m] > bk || (sk[m] == bk && si[m] < bi))) {
+                            bk = sk[m];
+                            bi = si[m];
+                            bx = sx[m];
+                            by = sy[m];
+                            bz = sz[m];
+                        }
+                    }
                     const uint32_t gk = __reduce_max_sync(FULL_MASK, bk);
                     const uint32_t gi = __reduce_min_sync(FULL_MASK, bk == gk ? bi : 0xffffffffu);
-                    if (lane == 0) s_far = gi;
+                    if (bk == gk && bi == gi) {  // the one lane holding the winner
+                        s_far = gi;
+                        s_cxyz[0] = bx;
+                        s_cxyz[1] = by;
+                        s_cxyz[2] = bz;
+                    }
                 }
             }
             __syncthreads();
             if (s_abort) return;
             far = s_far;
-            cx = p[3 * (size_t)far + 0];
-            cy = p[3 * (size_t)far + 1];
-            cz = p[3 * (size_t)far + 2];
+            cx = s_cxyz[0];
+            cy = s_cxyz[1];
+            cz = s_cxyz[2];
         }
     }
 }
@@ -673,7 +710,7 @@ int plan_group(int64_t B, int64_t N, int strategy, GroupPlan* plan, const char* 
     if (strategy == MPO_FPS_GROUP) G = min64(max64(G, 2), N);
     // Above 8192 points per SM every SM takes part and the CTAs' extra points
     // go to the overflow tiers.
-    G = min64(G, sms);
+    G = min64(G, min64(sms, 32 * kSlotsPerLane));
     const int64_t per_cta = ceil_div(N, G);
     if (per_cta > (int64_t)kLocalMask) {
         return fail(kUnsupported, std::string(who) + ": clouds above " +
