@@ -12,15 +12,19 @@ API.  Metric: Chamfer pairs/s = B * N * M per step / step time (whole job).
 
 N > 1 runs one process per GPU under torchrun (NCCL over NVLink): each rank
 owns 32 clouds (weak scaling) and the only collective is the all-reduce of the
-Chamfer loss partials.  `--impl reference` times the reference's CPU algorithm
+Chamfer loss partials, which runs on NCCL's stream during the backward.  `--impl reference` times the reference's CPU algorithm
 (the C restatement in oracle/, all host threads) on the same workload; under
 torchrun only rank 0 runs it.
 
 Also reported: `e2e` (the same step with the inputs copied from pinned host
 memory and the loss read back every step), the live CUDA-event time of the
 dominant kernel against its roofline, the CPU baseline, SM clocks sampled
-during the timed region, the native kernel launch count, and a secondary
-line for BASELINE config 1 (FPS + ball query + kNN, clouds/s).
+during the timed region, the native kernel launch count, and secondary lines:
+BASELINE config 1 (FPS + ball query + kNN, clouds/s; 8 clouds per GPU), config 4
+(feature kNN, queries/s; 16 clouds per GPU), config 1 with its 8 clouds split
+over the GPUs (strong scaling) and config 5 with its 2^20 queries split over
+the GPUs (strong scaling), their all-gathers timed apart, and the latency of
+the loss all-reduce.
 """
 
 from __future__ import annotations
