@@ -973,13 +973,15 @@ int launch_knn3p(const float* query, const float* ref, const Layout& L, int64_t 
     return check_launch("knn3p_kernel");
 }
 
-// Splits for knn3t_kernel: enough threads for about 512 per SM; each split
-// keeps its own list, so fewer splits mean fewer list updates per point.
+// Splits for knn3t_kernel: enough threads for about 256 per SM; each split
+// keeps its own list, so fewer splits mean fewer list updates per point
+// (three_nn at config 1: 0.059 / 0.047 / 0.057 / 0.082 ms with about 128 /
+// 256 / 512 / 1024 threads per SM).
 template <int POLICY, bool FLAT = false>
 int launch_knn3t(const float* query, const float* ref, const Layout& L, int64_t B,
                  int64_t max_n, int k, float* dist, int64_t* idx64, int32_t* idx32,
                  float* sqdist, cudaStream_t s) {
-    const int64_t want = (int64_t)sm_count() * 512;
+    const int64_t want = (int64_t)sm_count() * 256;
     int S = 1;
     while (S < 8 && B * L.M * S < want && max_n >= (int64_t)kTile / S) S *= 2;
     const int qpc = kThreads / S;
