@@ -67,9 +67,13 @@ constexpr int kTN = 128;         // references per tile (accumulator columns)
 constexpr int kMaxD = 96;        // widest feature vector of the tensor path (shared memory)
 constexpr int kCap = 64;         // candidates kept per query
 constexpr int kMaxK = 32;        // largest k served by this path
-constexpr int kQT = 2;           // 128-query tiles per CTA (share every reference tile)
+constexpr int kQT = 1;           // 128-query tiles per CTA (share every reference tile)
 constexpr int kRows = kQT * kTM;  // queries per CTA
-constexpr int kThreadsTC = 576;   // warp 0 producer, warp 1 MMA, warps 2-17 epilogue
+// Warp 0 producer, warp 1 MMA, 8 kQT epilogue warps.  One 128-query tile per
+// CTA and two CTAs per SM: a second CTA fills the gaps of the first one's MMA
+// issue and epilogue (config 4: 0.370 -> 0.345 ms against two query tiles per
+// CTA and one CTA per SM).
+constexpr int kThreadsTC = 64 + 256 * kQT;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 constexpr float kHuge = 1.15292150e18f;  // 2^60: larger norms go to the exact path
 
@@ -111,7 +115,12 @@ struct TcSmem {
     }
 };
 constexpr int kSmemLimit = 232448;  // opt-in shared memory per CTA on sm_100
+constexpr int kSmemPair = 115712;   // per CTA when two CTAs share an SM (228 KiB, 1 KiB each reserved)
+// The deepest ring that still lets two CTAs share an SM, else (wide features)
+// the deepest ring for one CTA per SM.
 inline int stages_for(int Kpad) {
+    for (int nst = kMaxStages; nst >= 2; --nst)
+        if (TcSmem(Kpad, nst).total <= kSmemPair) return nst;
     for (int nst = kMaxStages; nst > 2; --nst)
         if (TcSmem(Kpad, nst).total <= kSmemLimit) return nst;
     return 2;
@@ -337,7 +346,7 @@ __device__ __forceinline__ float eps_coef(int D) {
 // for the norm ring (bulk copy / the 4 warps of the epilogue group).  Phase parity of round n = n & 1;
 // "free" barriers are waited with the opposite parity first.
 template <int PASS, int KCAP>
-__global__ void __launch_bounds__(kThreadsTC, 1)
+__global__ void __launch_bounds__(kThreadsTC, 2)
 fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __restrict__ rpack,
                int64_t M, int64_t N, int64_t mtiles, int64_t ntiles, int D, int k,
                const float* __restrict__ nq, const float* __restrict__ nr,
@@ -460,7 +469,7 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
         // takes query tile qt of the reference tiles t = g (mod 2), i.e.
         // accumulator g; one thread per query.
         const int set = (warp - 2) >> 2;
-        const int group = set >> 1, qt = set & 1;
+        const int group = set / kQT, qt = set % kQT;
         const int quarter = warp & 3;
         const int row = qt * kTM + quarter * 32 + lane;
         const int64_t gq = mt * kRows + row;
@@ -555,7 +564,7 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
         // s_x[u * kTM + row] = bucket u (0-31 group 0, 32-63 group 1), then
         // group 1's count and status.
         float* s_x = reinterpret_cast<float*>(smem + L.b_off);
-        named_barrier_sync(1, 16 * 32);  // both epilogue groups finished their tiles
+        named_barrier_sync(1, 8 * kQT * 32);  // both epilogue groups finished their tiles
         if (PASS == 1) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) s_x[(32 * group + i) * kRows + row] = bmin[i];
@@ -564,7 +573,7 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
             s_x[64 * kRows + row] = __uint_as_float(found);
             s_x[65 * kRows + row] = ok ? 1.f : 0.f;
         }
-        named_barrier_sync(1, 16 * 32);
+        named_barrier_sync(1, 8 * kQT * 32);
         if (group == 0) {
             ok = ok && s_x[65 * kRows + row] != 0.f;
             if (PASS == 1) {
