@@ -27,7 +27,11 @@
 namespace mpo {
 namespace {
 
-constexpr int kChanPerThread = 8;
+// Channels per forward thread: the three indices and weights of a point are
+// loaded once for this many channels (config 1 forward: 3.9 -> 2.8 us with
+// 32 instead of 8).
+constexpr int kChanPerThread = 32;
+
 
 __global__ void __launch_bounds__(256)
 interp_fwd_kernel(const float* __restrict__ features, const int32_t* __restrict__ idx,
