@@ -380,30 +380,48 @@ fps_kernel(const float* __restrict__ xyz, int64_t N, int64_t npoint, int64_t sta
                     sx[m] = sy[m] = sz[m] = 0.f;
                     if (lane + 32 * m < G) need |= 1u << m;
                 }
-                const unsigned long long t0 = globaltimer_ns();
-                bool abort = false;
-                for (unsigned round = 1;; ++round) {
+                // Two sets of poll results alternate: a round's loads are
+                // issued before the previous round's results are examined, so
+                // a slot that lands is seen about one L2 round trip later
+                // instead of one and a half.
+                unsigned long long va[kSlotsPerLane], vb[kSlotsPerLane];
+                auto issue = [&](unsigned long long (&v)[kSlotsPerLane]) {
+#pragma unroll
+                    for (int m = 0; m < kSlotsPerLane; ++m)
+                        v[m] = (((need & ~seen) >> m) & 1u)
+                                   ? ld_relaxed_u64(cur + (lane + 32 * m) * kSlotStride)
+                                   : 0ull;
+                };
+                auto examine = [&](const unsigned long long (&v)[kSlotsPerLane]) {
 #pragma unroll
                     for (int m = 0; m < kSlotsPerLane; ++m) {
-                        if (((need & ~seen) >> m) & 1u) {
+                        if ((((need & ~seen) >> m) & 1u) &&
+                            ((v[m] >> kLocalBits) & kSeqMask) == seq) {
                             const int c = lane + 32 * m;
-                            const unsigned long long v = ld_relaxed_u64(cur + c * kSlotStride);
-                            if (((v >> kLocalBits) & kSeqMask) == seq) {
-                                seen |= 1u << m;
-                                sk[m] = (uint32_t)(v >> 32);
-                                si[m] = (uint32_t)c * (uint32_t)per_cta + (uint32_t)(v & kLocalMask);
-                                // A key of 0 marks a CTA without valid points
-                                // (it never wins): nothing to load.
-                                if (sk[m] != 0u && si[m] < (uint32_t)n) {
-                                    sx[m] = p[3 * (size_t)si[m] + 0];
-                                    sy[m] = p[3 * (size_t)si[m] + 1];
-                                    sz[m] = p[3 * (size_t)si[m] + 2];
-                                }
+                            seen |= 1u << m;
+                            sk[m] = (uint32_t)(v[m] >> 32);
+                            si[m] = (uint32_t)c * (uint32_t)per_cta + (uint32_t)(v[m] & kLocalMask);
+                            // A key of 0 marks a CTA without valid points
+                            // (it never wins): nothing to load.
+                            if (sk[m] != 0u && si[m] < (uint32_t)n) {
+                                sx[m] = p[3 * (size_t)si[m] + 0];
+                                sy[m] = p[3 * (size_t)si[m] + 1];
+                                sz[m] = p[3 * (size_t)si[m] + 2];
                             }
                         }
                     }
+                };
+                const unsigned long long t0 = globaltimer_ns();
+                bool abort = false;
+                issue(va);
+                for (unsigned round = 1;; ++round) {
+                    issue(vb);
+                    examine(va);
                     if (__all_sync(FULL_MASK, seen == need)) break;
-                    if ((round & 63u) == 0u &&
+                    issue(va);
+                    examine(vb);
+                    if (__all_sync(FULL_MASK, seen == need)) break;
+                    if ((round & 31u) == 0u &&
                         (globaltimer_ns() - t0 > kSpinLimitNs || ld_acquire_u32(my_error) != 0u)) {
                         abort = true;
                         break;
