@@ -787,6 +787,33 @@ __device__ __forceinline__ uint32_t sd_key(float d) {
     return isnan(d) ? kEmptyKey : ordered_key(d);
 }
 
+// The k-th smallest (k <= 32) of 64 values held two per lane (va: element
+// lane, vb: element 32 + lane), by a warp bitonic sort; every lane gets it.
+__device__ __forceinline__ float warp_kth_of_64(float va, float vb, int k) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride == 32) {
+                // Partner of element lane is element 32 + lane (same lane).
+                const bool up = (lane & size) == 0;  // size == 64: always ascending
+                const float lo = fminf(va, vb), hi = fmaxf(va, vb);
+                va = up ? lo : hi;
+                vb = up ? hi : lo;
+            } else {
+                const float oa = __shfl_xor_sync(FULL_MASK, va, stride);
+                const float ob = __shfl_xor_sync(FULL_MASK, vb, stride);
+                const bool lower = (lane & stride) == 0;
+                const bool upa = (lane & size) == 0, upb = ((32 + lane) & size) == 0;
+                va = (lower == upa) ? fminf(va, oa) : fmaxf(va, oa);
+                vb = (lower == upb) ? fminf(vb, ob) : fmaxf(vb, ob);
+            }
+        }
+    }
+    return __shfl_sync(FULL_MASK, va, k - 1);
+}
+
 template <int POLICY, bool FLAT>
 __global__ void __launch_bounds__(kWqWarps * 32)
 knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, Layout L, int k,
@@ -813,6 +840,13 @@ knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, L
     // 64-bit key (ordered SD bits << 32 | index); empty ranks are all ones.
     unsigned long long best = ~0ull;
     float thr = INFINITY;  // SD of rank k - 1; +inf while that rank is empty
+    // Exact upper bound of the k-th smallest SD: lane l keeps the minimum SD of
+    // two buckets of points (chunks 0-1 and 2-3 of every step); the k-th
+    // smallest of the 64 bucket minima is the SD of k distinct points, so no
+    // point above it can be among the k nearest.  A pass over the first tile
+    // before its candidate scan computes it, so the scan starts with a bar
+    // near the final one instead of +inf and merges far fewer candidates.
+    float bkt0 = INFINITY, bkt1 = INFINITY, ubound = INFINITY;
     unsigned long long* const buf = s_buf + warp * 32;
     int bc = 0;  // candidates waiting in buf (warp-uniform)
     // Merge the bc buffered candidates into `best`: bitonic sort of the
@@ -844,6 +878,7 @@ knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, L
         // A NaN (three_nn) or empty rank k - 1 lets every candidate through.
         thr = kk != kEmptyKey ? ordered_key_inv(kk)
                               : ((uint32_t)kth >= 0x80000000u ? INFINITY : __int_as_float(0x7fffffff));
+        thr = fminf(thr, ubound);
         bc = 0;
         __syncwarp();
     };
@@ -866,6 +901,26 @@ knn_wq3_kernel(const float* __restrict__ query, const float* __restrict__ ref, L
         }
         __syncthreads();
         if (!active) continue;
+        // Bound pass over the first tile only (points past tn are not in
+        // it): afterwards the list's own rank k - 1 is about as tight, and
+        // re-scanning every tile of a long cloud costs more than it saves.
+        for (int c0 = 0; c0 < (t0 == 0 ? tn : 0); c0 += 128) {
+            const int g = (c0 >> 2) + lane;
+            const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(tA + g);
+            const ulonglong2 b = *reinterpret_cast<const ulonglong2*>(tB + g);
+            const ulonglong2 z = *reinterpret_cast<const ulonglong2*>(tZ + g);
+            float d[4];
+            unpack2(sqd3x2(X, Y, Z, a.x, a.y, z.x), d[0], d[1]);
+            unpack2(sqd3x2(X, Y, Z, b.x, b.y, z.y), d[2], d[3]);
+            const int e = c0 + lane;
+            // fminf ignores NaN; a +inf or dropped point only loosens the bound.
+            bkt0 = fminf(bkt0, fminf(e < tn ? d[0] : INFINITY, e + 32 < tn ? d[1] : INFINITY));
+            bkt1 = fminf(bkt1, fminf(e + 64 < tn ? d[2] : INFINITY, e + 96 < tn ? d[3] : INFINITY));
+        }
+        if (t0 == 0) {
+            ubound = warp_kth_of_64(bkt0, bkt1, k);
+            thr = fminf(thr, ubound);
+        }
         for (int c0 = 0; c0 < tn; c0 += 128) {
             const int g = (c0 >> 2) + lane;
             const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(tA + g);
