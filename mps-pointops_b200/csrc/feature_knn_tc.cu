@@ -11,13 +11,14 @@
 // The tensor cores only PROPOSE candidates; every reported distance and every
 // ranking decision comes from the exact fp32 SD.  Design:
 //
-//  1. Pack (fknn_pack_kernel, fknn_norms_kernel): queries and references are
-//     rounded to tf32 (cvt.rna: 11 significant bits) and written once in the
-//     operand layout of the MMA (per 128-row tile, K-major core matrices), so
-//     a tile reaches shared memory with one bulk copy; norms
+//  1. Pack (fknn_prep_kernel): queries and references are rounded to tf32
+//     (cvt.rna: 11 significant bits) and written once in the operand layout
+//     of the MMA (per 128-row tile, K-major core matrices), so a tile reaches
+//     shared memory with one bulk copy; in the same pass the norms
 //     n(p) = sum of p_t^2 (fp32), padded with +inf per 128-reference tile;
 //     per cloud the largest reference norm and a flag for non-finite or huge
-//     norms (such clouds skip the tensor path).
+//     norms (such clouds skip the tensor path).  When the queries are the
+//     references (the same array), one pack serves both operands.
 //  2. Approximate scores (fknn_tc_kernel): a CTA owns 128 queries; warp 0
 //     streams 128-reference tiles into a 2-stage shared-memory ring with
 //     cp.async.bulk, warp 1 issues tcgen05.mma kind::tf32 (tf32 x tf32 -> fp32,
@@ -26,10 +27,11 @@
 //     per TMEM lane quarter, one thread per query) read the other accumulator
 //     with tcgen05.ld and form s_j = n(r_j) - 2 dot'_j, so SD'_j = n(q) + s_j
 //     approximates SD_j with |SD'_j - SD_j| <= eps(q) = C_K (n(q) + max n(r)).
-//       pass 1: the minimum of s in each of 64 column buckets (column j of
-//               a tile -> bucket j mod 64); the k-th smallest bucket minimum
-//               U bounds the k-th smallest s from above (k buckets -> k
-//               distinct columns).
+//       pass 1: the minimum of s in each of 64 column buckets (32 per
+//               epilogue group: columns 2u and 2u + 1 of the chunks c of the
+//               group's tiles -> bucket (c & 1) * 16 + u); the k-th smallest
+//               bucket minimum U bounds the k-th smallest s from above (k
+//               buckets -> k distinct columns).
 //       pass 2: every column with s_j <= U + 2 eps(q) is appended to the
 //               query's candidate list (capacity kCap).
 //     The k nearest by exact SD are all candidates: F_k <= n(q) + U + eps
@@ -216,6 +218,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Three-input minimum (PTX min.f32 with three sources; the scores it is used
+// on are never NaN).
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+    float d;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // Round to tf32 (nearest, ties away from zero): 11 significant bits, the
 // low 13 bits of the result are zero.
 __device__ __forceinline__ uint32_t tf32_bits(float x) {
@@ -243,92 +253,90 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
 }
 
 // ---- 1. pack and norms --------------------------------------------------------
-// Thread per (row, 8-feature chunk) of the padded tiles (two 16-byte core-
-// matrix rows); rows past n and features past D are zero.  vec: rows are read
-// as float4 (D % 4 == 0 and 16-byte aligned bases).
-__global__ void fknn_pack_kernel(const float* __restrict__ p, int64_t B, int64_t n, int D, int Kpad,
-                                 int64_t tiles, int vec, unsigned char* __restrict__ out) {
+// Thread per (padded row, 8-feature chunk): 2^lg consecutive lanes per row
+// (the chunk count Kpad / 8 rounded up to a power of two), so that a row's
+// lanes form one aligned group of a warp.  Rows [0, B * ntiles * 128) are the
+// references, then (unless `same`: the queries are the references) the
+// B * mtiles * 128 query rows.  Rows past n and features past D pack zeros.
+// Each lane packs its two 16-byte core-matrix rows and sums the squares of its
+// 8 features in order; a butterfly over the row's lanes gives the norm (every
+// lane the same sum, fp32 addition being commutative).  vec: rows are read as
+// float4 (D % 4 == 0 and 16-byte aligned bases).  nr is padded per cloud to
+// ntiles * 128 entries (+inf past N); nmax = largest finite reference norm per
+// cloud (one atomic per warp), bad = a norm that is not finite or above kHuge.
+__global__ void fknn_prep_kernel(const float* __restrict__ q, const float* __restrict__ r,
+                                 int64_t B, int64_t M, int64_t N, int D, int Kpad,
+                                 int64_t mtiles, int64_t ntiles, int vec, int same, int lg,
+                                 unsigned char* __restrict__ qpack,
+                                 unsigned char* __restrict__ rpack, float* __restrict__ nq,
+                                 float* __restrict__ nr, unsigned* __restrict__ nmax,
+                                 int* __restrict__ bad) {
     const int chunks = Kpad / 8;
     const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t rows = B * tiles * 128;
-    if (e >= rows * chunks) return;
-    const int64_t prow = e / chunks;  // padded row: b * tiles * 128 + tile * 128 + rr
-    const int c = (int)(e % chunks);
+    const int64_t prow_all = e >> lg;
+    const int c = (int)(e & ((1 << lg) - 1));
+    const int64_t rrows = B * ntiles * 128, qrows = same ? 0 : B * mtiles * 128;
+    const bool row_live = prow_all < rrows + qrows;
+    const bool is_ref = prow_all < rrows;
+    const int64_t prow = is_ref ? prow_all : prow_all - rrows;
+    const int64_t tiles = is_ref ? ntiles : mtiles, n = is_ref ? N : M;
     const int64_t b = prow / (tiles * 128);
     const int64_t i = prow % (tiles * 128);
-    const int64_t tile = i / 128;
-    const int rr = (int)(i % 128);
+    const bool point = row_live && i < n;
     float x[8];
-    const bool live = i < n;
-    const float* src = p + (b * n + i) * D + c * 8;
-    if (live && vec && c * 8 + 8 <= D) {
-        const float4 u = reinterpret_cast<const float4*>(src)[0];
-        const float4 v = reinterpret_cast<const float4*>(src)[1];
-        x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
-        x[4] = v.x; x[5] = v.y; x[6] = v.z; x[7] = v.w;
-    } else {
 #pragma unroll
-        for (int t = 0; t < 8; ++t) x[t] = (live && c * 8 + t < D) ? src[t] : 0.f;
-    }
-    const uint4 lo4 = make_uint4(tf32_bits(x[0]), tf32_bits(x[1]), tf32_bits(x[2]), tf32_bits(x[3]));
-    const uint4 hi4 = make_uint4(tf32_bits(x[4]), tf32_bits(x[5]), tf32_bits(x[6]), tf32_bits(x[7]));
-    unsigned char* blk = out + (size_t)(b * tiles + tile) * part_bytes(Kpad);
-    const int off = (rr >> 3) * (Kpad / 4 * 128) + (2 * c) * 128 + (rr & 7) * 16;
-    *reinterpret_cast<uint4*>(blk + off) = lo4;
-    *reinterpret_cast<uint4*>(blk + off + 128) = hi4;
-}
-
-// Thread per point: nq[b*M + i]; nr padded per cloud to tiles*128 entries
-// (+inf past N); nmax = largest finite reference norm per cloud (one atomic
-// per warp), bad = a norm that is not finite or above kHuge.
-__global__ void fknn_norms_kernel(const float* __restrict__ q, const float* __restrict__ r,
-                                  int64_t B, int64_t M, int64_t N, int64_t ntiles, int D, int vec,
-                                  float* __restrict__ nq, float* __restrict__ nr,
-                                  unsigned* __restrict__ nmax, int* __restrict__ bad) {
-    const int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t npad = ntiles * 128;
-    const int64_t total = B * (M + npad);
-    const bool live = w < total;
-    const bool is_q = w < B * M;
-    const int64_t row = is_q ? w : w - B * M;
-    const int64_t b = live ? (is_q ? row / M : row / npad) : -1;
-    const int64_t i = is_q ? row % M : row % npad;
-    bool ref_ok = false;
-    float s = 0.f;
-    if (live) {
-        if (!is_q && i >= N) {
-            nr[row] = INFINITY;
+    for (int t = 0; t < 8; ++t) x[t] = 0.f;
+    if (point && c < chunks) {
+        const float* src = (is_ref ? r : q) + (b * n + i) * D + c * 8;
+        if (vec && c * 8 + 8 <= D) {
+            const float4 u = reinterpret_cast<const float4*>(src)[0];
+            const float4 v = reinterpret_cast<const float4*>(src)[1];
+            x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
+            x[4] = v.x; x[5] = v.y; x[6] = v.z; x[7] = v.w;
         } else {
-            const float* p = is_q ? q + row * D : r + (b * N + i) * D;
-            if (vec) {
-                const float4* p4 = reinterpret_cast<const float4*>(p);
-                for (int t = 0; t < D / 4; ++t) {
-                    const float4 v = p4[t];
-                    s = __fadd_rn(s, __fmul_rn(v.x, v.x));
-                    s = __fadd_rn(s, __fmul_rn(v.y, v.y));
-                    s = __fadd_rn(s, __fmul_rn(v.z, v.z));
-                    s = __fadd_rn(s, __fmul_rn(v.w, v.w));
-                }
-            } else {
-                for (int t = 0; t < D; ++t) s = __fadd_rn(s, __fmul_rn(p[t], p[t]));
-            }
-            const bool ok = isfinite(s) && s <= kHuge;
-            if (!ok) bad[b] = 1;
-            if (is_q) {
-                nq[row] = s;
-            } else {
-                nr[row] = s;
-                ref_ok = ok;
-            }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) x[t] = (c * 8 + t < D) ? src[t] : 0.f;
         }
     }
-    const unsigned bits = ref_ok ? __float_as_uint(s) : 0u;
-    const int64_t b0 = __shfl_sync(FULL_MASK, b, 0);
-    if (__all_sync(FULL_MASK, b == b0)) {
+    if (row_live && c < chunks) {
+        const uint4 lo4 = make_uint4(tf32_bits(x[0]), tf32_bits(x[1]), tf32_bits(x[2]),
+                                     tf32_bits(x[3]));
+        const uint4 hi4 = make_uint4(tf32_bits(x[4]), tf32_bits(x[5]), tf32_bits(x[6]),
+                                     tf32_bits(x[7]));
+        const int64_t tile = i / 128;
+        const int rr = (int)(i % 128);
+        unsigned char* blk =
+            (is_ref ? rpack : qpack) + (size_t)(b * tiles + tile) * part_bytes(Kpad);
+        const int off = (rr >> 3) * (Kpad / 4 * 128) + (2 * c) * 128 + (rr & 7) * 16;
+        *reinterpret_cast<uint4*>(blk + off) = lo4;
+        *reinterpret_cast<uint4*>(blk + off + 128) = hi4;
+    }
+    float s = __fmul_rn(x[0], x[0]);
+#pragma unroll
+    for (int t = 1; t < 8; ++t) s = __fadd_rn(s, __fmul_rn(x[t], x[t]));
+    for (int off = (1 << lg) >> 1; off >= 1; off >>= 1)
+        s = __fadd_rn(s, __shfl_xor_sync(FULL_MASK, s, off));
+    unsigned bits = 0u;
+    if (point && c == 0) {
+        const bool ok = isfinite(s) && s <= kHuge;
+        if (!ok) bad[b] = 1;
+        if (is_ref) {
+            nr[prow] = s;
+            if (same) nq[b * M + i] = s;
+            if (ok) bits = __float_as_uint(s);
+        } else {
+            nq[b * M + i] = s;
+        }
+    } else if (row_live && is_ref && c == 0) {
+        nr[prow] = INFINITY;  // padding column of the last tile
+    }
+    const int64_t bb = is_ref ? b : -1;
+    const int64_t b0 = __shfl_sync(FULL_MASK, bb, 0);
+    if (__all_sync(FULL_MASK, bb == b0)) {
         const unsigned mx = __reduce_max_sync(FULL_MASK, bits);
         if ((threadIdx.x & 31) == 0 && mx) atomicMax(&nmax[b0], mx);
     } else if (bits) {
-        atomicMax(&nmax[b], bits);
+        atomicMax(&nmax[bb], bits);
     }
 }
 
@@ -478,10 +486,11 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
         const float eps = eps_coef(D) * (nqi + __uint_as_float(nmax[b]));
         float thr = -INFINITY;  // pass 2: s_j <= thr makes j a candidate
         if (PASS == 2 && qvalid) thr = ubound[(int64_t)b * M + gq] + 2.f * eps;
-        // Pass 1: bucket i of group g holds the minimum of s over column i of
-        // every 32-column chunk of the group's tiles; with the other group's
-        // buckets, the k-th smallest of the 64 bucket minima bounds the k-th
-        // smallest s from above (k buckets -> k distinct columns).
+        // Pass 1: bucket h * 16 + u of group g holds the minimum of s over
+        // columns 2u and 2u + 1 of the 32-column chunks c with c & 1 == h of
+        // the group's tiles; with the other group's buckets, the k-th smallest
+        // of the 64 bucket minima bounds the k-th smallest s from above (k
+        // buckets -> k distinct columns).
         float bmin[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) bmin[i] = INFINITY;
@@ -498,8 +507,13 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
             tc_fence_after();
             const float* s_ny = reinterpret_cast<const float*>(smem + L.ny_off + ns * kTN * 4);
             // The norms of slot ns stay until this group arrives on its empty barrier.
+            // Chunks in pairs: chunk c feeds buckets (c & 1) * 16 + u, and
+            // the pair index h = c & 1 is a compile-time constant.
 #pragma unroll 1
-            for (int c = 0; c < kTN / 32; ++c) {
+            for (int c2 = 0; c2 < kTN / 32; c2 += 2) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int c = c2 + h;
                 float v[32];
                 tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) +
                               (uint32_t)((ac * kQT + qt) * kTN + c * 32),
@@ -509,6 +523,8 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                 // per instruction; the same single rounding as fmaf).
                 const f32x2 m2 = pack2(-2.f, -2.f);
                 if (PASS == 1) {
+                    // Columns 2u and 2u + 1 of the chunk -> bucket h * 16 + u,
+                    // one three-input minimum per two columns.
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float4 y = ny4[i];
@@ -517,8 +533,8 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                                 sc[0], sc[1]);
                         unpack2(fma2(pack2(v[4 * i + 2], v[4 * i + 3]), m2, pack2(y.z, y.w)),
                                 sc[2], sc[3]);
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) bmin[4 * i + c] = fminf(bmin[4 * i + c], sc[c]);
+                        bmin[16 * h + 2 * i] = fmin3(bmin[16 * h + 2 * i], sc[0], sc[1]);
+                        bmin[16 * h + 2 * i + 1] = fmin3(bmin[16 * h + 2 * i + 1], sc[2], sc[3]);
                     }
                 } else {
                     // Candidate bit mask of the 32 columns (no divergence),
@@ -534,8 +550,8 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                         unpack2(fma2(pack2(v[4 * i + 2], v[4 * i + 3]), m2, pack2(y.z, y.w)),
                                 sc[2], sc[3]);
 #pragma unroll
-                        for (int c = 0; c < 4; ++c)
-                            hits |= (sc[c] <= thr ? 1u : 0u) << (4 * i + c);
+                        for (int e = 0; e < 4; ++e)
+                            hits |= (sc[e] <= thr ? 1u : 0u) << (4 * i + e);
                     }
                     while (hits) {
                         const int i = __ffs(hits) - 1;
@@ -548,6 +564,7 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                         ++found;
                     }
                 }
+              }
             }
             tc_fence_before();
             __syncwarp();
@@ -957,21 +974,19 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
         return fail(kCudaError, "knn: scratch reset failed");
     const int Kpad = kpad_of(D);
     const int64_t mt = ceil_div(M, kRows) * kQT, nt = ceil_div(N, kTN);
-    const int64_t qchunks = B * mt * 128 * (Kpad / 8), rchunks = B * nt * 128 * (Kpad / 8);
+    // kNN of a cloud against itself (knn(f, f, k)): one pack serves both operands.
+    const int same = (query == ref && M == N) ? 1 : 0;
+    int lg = 0;
+    while ((1 << lg) < Kpad / 8) ++lg;
+    const int64_t rows = B * nt * 128 + (same ? 0 : B * mt * 128);
     // 16-byte row loads only when every row starts on a 16-byte boundary.
     const int vec = (D % 4 == 0 && aligned_to(query, 16) && aligned_to(ref, 16)) ? 1 : 0;
-    fknn_pack_kernel<<<(unsigned)ceil_div(qchunks, 256), 256, 0, s>>>(query, B, M, D, Kpad, mt,
-                                                                      vec, w.qpack);
-    int st = check_launch("fknn_pack_kernel");
+    fknn_prep_kernel<<<(unsigned)ceil_div(rows << lg, 256), 256, 0, s>>>(
+        query, ref, B, M, N, D, Kpad, mt, nt, vec, same, lg, w.qpack, w.rpack, w.nq, w.nr,
+        w.nmax, w.bad);
+    int st = check_launch("fknn_prep_kernel");
     if (st) return st;
-    fknn_pack_kernel<<<(unsigned)ceil_div(rchunks, 256), 256, 0, s>>>(ref, B, N, D, Kpad, nt,
-                                                                      vec, w.rpack);
-    st = check_launch("fknn_pack_kernel");
-    if (st) return st;
-    fknn_norms_kernel<<<(unsigned)ceil_div(B * (M + nt * kTN), 256), 256, 0, s>>>(
-        query, ref, B, M, N, nt, D, vec, w.nq, w.nr, w.nmax, w.bad);
-    st = check_launch("fknn_norms_kernel");
-    if (st) return st;
+    const unsigned char* qpack = same ? w.rpack : w.qpack;
     const int nst = stages_for(Kpad);
     const TcSmem L(Kpad, nst);
     auto k1 = fknn_tc_kernel<1, KCAP>;
@@ -982,11 +997,11 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
             cudaSuccess)
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");
     dim3 grid((unsigned)(mt / kQT), (unsigned)B);
-    k1<<<grid, kThreadsTC, L.total, s>>>(w.qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
+    k1<<<grid, kThreadsTC, L.total, s>>>(qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
                                          w.bad, w.ubound, w.counts, w.cand, w.status, nst);
     st = check_launch("fknn_tc_kernel<1>");
     if (st) return st;
-    k2<<<grid, kThreadsTC, L.total, s>>>(w.qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
+    k2<<<grid, kThreadsTC, L.total, s>>>(qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
                                          w.bad, w.ubound, w.counts, w.cand, w.status, nst);
     st = check_launch("fknn_tc_kernel<2>");
     if (st) return st;

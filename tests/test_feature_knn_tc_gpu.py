@@ -1,4 +1,4 @@
-"""Feature-space kNN through the tensor-core candidate path (tcgen05 bf16x3
+"""Feature-space kNN through the tensor-core candidate path (tcgen05 tf32
 scores, exact fp32 re-rank) vs the exact (SD, index) oracle of
 tests/test_feature_knn.py:16-35 of gamzerA/mps-pointops.  The path serves
 16 <= D <= 96, k <= 32, N >= 2048; results must be bit-exact like the
@@ -45,11 +45,24 @@ def test_dgcnn_config4_slice(cuda_device):
 @pytest.mark.parametrize("d", [16, 20, 33, 64, 72, 96])
 @pytest.mark.parametrize("k", [1, 8, 20, 32])
 def test_dims_and_k(cuda_device, d, k):
-    # M not a multiple of the 256-query CTA tile, N not a multiple of the
+    # M not a multiple of the 128-query CTA tile, N not a multiple of the
     # 128-reference tile; D not a multiple of 16.
     q = feats(2, 300, d, seed=d)
     r = feats(2, 2500, d, seed=d + 1)
     check(q, r, k, cuda_device)
+
+
+@pytest.mark.parametrize("d", [16, 20, 33, 64, 96])
+def test_self_knn_one_pack(cuda_device, d):
+    """knn(f, f, k) on ONE device tensor: the references' packed tiles and
+    norms also serve as the queries' (one pack pass instead of two); N not a
+    multiple of 128, D = 33 with scalar row loads."""
+    f = feats(2, 2500, d, seed=40 + d)
+    fc = f.to(cuda_device)
+    want_d, want_i = O.knn(f.numpy(), f.numpy(), 20)
+    dd, ii = mps_pointops.knn(fc, fc, 20)
+    np.testing.assert_array_equal(ii.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(dd.cpu().numpy(), want_d)
 
 
 def test_scaled_and_offset_features(cuda_device):
