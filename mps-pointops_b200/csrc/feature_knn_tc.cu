@@ -770,13 +770,15 @@ fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int
     // the odd tiles.
     const unsigned f0 = packed & 0xffffu, f1 = packed >> 16, cnt = f0 + f1;
     for (int t = lane; t < D; t += 32) qp[t] = q[row * D + t];
-    // Copy units (float4 or float) per row; a copy instruction covers R rows
-    // when a row has at most 32 units, lane l taking unit l % U of row l / U.
+    // Copy units (float4 or float) per row: LPR lanes per row (the largest
+    // power of two <= min(U, 8)), so one copy instruction covers R = 32 / LPR
+    // rows and each lane copies units u0, u0 + LPR, ... of its row (D = 64:
+    // 4 rows of 16 float4s per instruction, two per lane).
     const int U = VEC ? D / 4 : D;
-    const int R = U <= 32 ? 32 / U : 1;
-    const int roff = U <= 32 ? lane / U : 0;
-    const int u0 = U <= 32 ? lane % U : lane;
-    const bool copier = U > 32 || lane < R * U;
+    const int LPR = U >= 8 ? 8 : (U >= 4 ? 4 : (U >= 2 ? 2 : 1));
+    const int R = 32 / LPR;
+    const int roff = lane / LPR;
+    const int u0 = lane % LPR;
     float sd[2];
     uint32_t jj[2];
 #pragma unroll
@@ -795,10 +797,10 @@ fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int
         for (unsigned base = 0; base < n; base += (unsigned)R) {
             const unsigned rl = base + (unsigned)roff;
             const uint32_t jr = __shfl_sync(FULL_MASK, j, (int)(rl & 31u));
-            if (copier && rl < n && jr < (uint32_t)N) {
+            if (rl < n && jr < (uint32_t)N) {
                 const float* src = rb + (int64_t)jr * D;
                 float* dst = rows + rl * stride;
-                for (int u = u0; u < U; u += 32) {
+                for (int u = u0; u < U; u += LPR) {
                     if (VEC)
                         cp_async16(dst + 4 * u, src + 4 * u);
                     else
@@ -840,11 +842,36 @@ fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int
             }
         }
     } else {
+        // Up to 32 candidates: sort 32-bit keys (SD bits with the low five
+        // bits replaced by the lane) and fetch each rank's entry from its
+        // lane.  The order equals the (SD, index) order unless two finite SD
+        // among the first k + 1 ranks agree above their low five bits; then
+        // (rarely) the 64-bit keys are sorted instead.
+        uint32_t k32 = (__float_as_uint(sd[0]) & ~31u) | (uint32_t)lane;
 #pragma unroll
         for (int size = 2; size <= 32; size <<= 1) {
 #pragma unroll
-            for (int stride = size >> 1; stride > 0; stride >>= 1)
-                a0 = bitonic_step(a0, lane, size, stride);
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                const uint32_t other = __shfl_xor_sync(FULL_MASK, k32, stride);
+                const bool keep_min = ((lane & size) == 0) == ((lane & stride) == 0);
+                k32 = keep_min ? min(k32, other) : max(k32, other);
+            }
+        }
+        const uint32_t prev = __shfl_up_sync(FULL_MASK, k32, 1);
+        const bool close = lane >= 1 && lane <= k && (k32 >> 5) == (prev >> 5) &&
+                           (k32 >> 5) < (0x7f800000u >> 5);
+        if (__any_sync(FULL_MASK, close)) {
+#pragma unroll
+            for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+                for (int stride = size >> 1; stride > 0; stride >>= 1)
+                    a0 = bitonic_step(a0, lane, size, stride);
+            }
+        } else {
+            const int src = (int)(k32 & 31u);
+            const uint32_t sj = __shfl_sync(FULL_MASK, jj[0], src);
+            const float sdv = __shfl_sync(FULL_MASK, sd[0], src);
+            a0 = ((uint64_t)__float_as_uint(sdv) << 32) | sj;
         }
     }
     if (lane < k) {
