@@ -14,26 +14,30 @@
 //  1. Pack (fknn_prep_kernel): queries and references are rounded to tf32
 //     (cvt.rna: 11 significant bits) and written once in the operand layout
 //     of the MMA (per 128-row tile, K-major core matrices), so a tile reaches
-//     shared memory with one bulk copy; in the same pass the norms
-//     n(p) = sum of p_t^2 (fp32), padded with +inf per 128-reference tile;
-//     per cloud the largest reference norm and a flag for non-finite or huge
-//     norms (such clouds skip the tensor path).  When the queries are the
-//     references (the same array), one pack serves both operands.
+//     shared memory with one bulk copy.  After the Kpad feature columns every
+//     row has an 8-column norm block: a reference row carries tf32(-n(r)/2)
+//     (n(p) = sum of p_t^2 in fp32; -2^100 for padding rows past N).  The
+//     same pass writes the query norms, per cloud the largest reference norm,
+//     and a flag for non-finite or huge norms (such clouds skip the tensor
+//     path).  When the queries are the references (the same array), one pack
+//     serves both operands.
 //  2. Approximate scores (fknn_tc_kernel): a CTA owns 128 queries; warp 0
-//     streams 128-reference tiles into a 2-stage shared-memory ring with
+//     streams 128-reference tiles into a shared-memory ring with
 //     cp.async.bulk, warp 1 issues tcgen05.mma kind::tf32 (tf32 x tf32 -> fp32,
-//     M = 128, N = 128, K = 8): dot ~= tf32(q).tf32(r), one product, into one
-//     of two TMEM accumulators (128 lanes x 128 columns each), and warps 2-5 (one
-//     per TMEM lane quarter, one thread per query) read the other accumulator
-//     with tcgen05.ld and form s_j = n(r_j) - 2 dot'_j, so SD'_j = n(q) + s_j
-//     approximates SD_j with |SD'_j - SD_j| <= eps(q) = C_K (n(q) + max n(r)).
-//       pass 1: the minimum of s in each of 64 column buckets (32 per
-//               epilogue group: columns 2u and 2u + 1 of the chunks c of the
-//               group's tiles -> bucket (c & 1) * 16 + u); the k-th smallest
-//               bucket minimum U bounds the k-th smallest s from above (k
-//               buckets -> k distinct columns).
-//       pass 2: every column with s_j <= U + 2 eps(q) is appended to the
-//               query's candidate list (capacity kCap).
+//     M = 128, N = 128, K = 8) over the feature columns and one more MMA that
+//     pairs the references' norm block with a constant block of ones in
+//     shared memory, into one of two TMEM accumulators (128 lanes x 128
+//     columns each), so the accumulator holds
+//         t_j = tf32(q) . tf32(r_j) + tf32(-n(r_j) / 2),   s_j := -2 t_j,
+//     and SD'_j = n(q) + s_j approximates SD_j with |SD'_j - SD_j| <= eps(q) =
+//     C_K (n(q) + max n(r)).  Eight epilogue warps (two groups of four, one
+//     thread per query) read the accumulators with tcgen05.ld:
+//       pass 1: the maximum of t in each of 64 column buckets; the k-th
+//               smallest bucket minimum U of s = -2 t bounds the k-th
+//               smallest s from above (k buckets -> k distinct columns);
+//       pass 2: every column with s_j <= U + 2 eps(q), i.e. t_j >=
+//               -(U + 2 eps(q)) / 2, is appended to the query's candidate
+//               list (capacity kCap).
 //     The k nearest by exact SD are all candidates: F_k <= n(q) + U + eps
 //     (k columns have SD' <= n(q) + U), and a needed column has
 //     SD' <= F_k + eps.
@@ -41,16 +45,17 @@
 //     ranked by (SD, index).  A query whose list overflowed, or whose cloud
 //     was flagged, is scanned exactly over all references instead.
 //
-// Error bound C_K (per unit of n(q) + n(r), K = D padded to 16): rounding to
-// tf32 moves each coordinate by at most u|p| with u = 2^-11, so a product
+// Error bound C_K (per unit of n(q) + n(r), K = Kpad): rounding to tf32
+// moves each coordinate by at most u|p| with u = 2^-11, so a product
 // q_t r_t moves by at most (2u + u^2)|q_t||r_t| (the tf32 products are exact
-// in fp32), and the dot product by (2u + u^2)(n(q) + n(r)) / 2; fp32
-// accumulation inside the tensor core, the norms, the score FMA and the
-// reference's own rounding add the rest.  C_K = 2 * (2^-10 + 2^-22 + K 2^-21 +
-// (3D + 16) 2^-24) is about twice the sum of those terms.  (Three bf16
-// products hi.hi' + hi.lo' + lo.hi' give a bound 8x tighter for 3x the MMA
-// work; on the config-4 shapes the tf32 bound adds about two candidates per
-// query, which the re-rank absorbs.)
+// in fp32), the dot product by (2u + u^2)(n(q) + n(r)) / 2 and s by twice
+// that; rounding -n(r)/2 to tf32 moves s by at most u n(r); the fp32
+// accumulation of K + 8 terms inside the tensor core, the norms and the
+// reference's own rounding add the rest.  C_K = 2 * (2^-10 + 2^-11 + 2^-22 +
+// (K + 8) 2^-21 + (3D + 16) 2^-24) is about twice the sum of those terms.
+// (Three bf16 products hi.hi' + hi.lo' + lo.hi' give a bound about 10x
+// tighter for 3x the MMA work; on the config-4 shapes the tf32 bound adds a
+// few candidates per query, which the re-rank absorbs.)
 //
 // Every wait on an mbarrier is bounded (kWaitNs of %globaltimer); on expiry
 // the CTA records status 1, the waiting role stops, the rows of the CTA are
@@ -82,37 +87,39 @@ constexpr float kHuge = 1.15292150e18f;  // 2^60: larger norms go to the exact p
 // Operand layout of one 128-row tile of tf32 values, K-major core matrices
 // (8 rows x 16 bytes) without swizzle: element (row, t) sits at
 //   (row / 8) * SBO + (t / 4) * 128 + (row % 8) * 16 + (t % 4) * 4,
-// SBO = Kpad / 4 * 128.
+// SBO = W / 4 * 128, W = the tile's width in tf32 values.  A packed row holds
+// Kpad feature columns (D padded to 16) and one 8-column norm block: column
+// Kpad holds tf32(-n(p) / 2) for a reference (-2^100 for a padding row past
+// N), the rest zeros.  The norm block of a query row is never read: the MMAs
+// pair the references' norm block with a constant block of ones (column 0 =
+// 1.0) held in shared memory, so the accumulator receives
+//   t_j = tf32(q) . tf32(r_j) + tf32(-n(r_j) / 2)  =  -s_j / 2
+// directly, and the epilogue needs no per-column arithmetic.
 __host__ __device__ constexpr int kpad_of(int D) { return (D + 15) / 16 * 16; }
-__host__ __device__ constexpr int part_bytes(int Kpad) { return 128 * Kpad * 4; }
+__host__ __device__ constexpr int width_of(int D) { return kpad_of(D) + 8; }
+__host__ __device__ constexpr int part_bytes(int W) { return 128 * W * 4; }
+constexpr int kOnesBytes = 128 * 8 * 4;  // the constant ones block (128 rows x 8 tf32)
+constexpr float kPadNorm = 1.26765060e30f;  // 2^100: t = -2^100 for padding columns
 
-// Shared memory: A (kQT tiles) | nst stages x B | kNySlots-slot ring of the
-// tiles' reference norms | barriers.  The norms have their own ring so that a
-// B stage is refilled as soon as the MMAs have read it, while the epilogue of
-// that tile still reads its norms.  With one tf32 product per tile the MMAs
-// take about 1.1 K cycles per reference tile, less than a 32 KiB bulk copy's
-// latency, so the ring is as deep as shared memory allows (nst = 4 up to
-// D = 64, fewer for wider features; chosen at launch).
+// Shared memory: A (kQT tiles) | nst stages x B (also the epilogue's handoff
+// area once the tiles are done) | the ones block | barriers.
 constexpr int kMaxStages = 4;
-constexpr int kNySlots = 8;
 // Barrier indices: full[kMaxStages] | empty[kMaxStages] | accf[2] | acce[2] |
-// afull | nfull[kNySlots] | nempty[kNySlots]; then the TMEM address and the
-// abort flag.
+// afull; then the TMEM address and the abort flag.
 constexpr int kBarFull = 0, kBarEmpty = kMaxStages, kBarAccF = 2 * kMaxStages,
-              kBarAccE = kBarAccF + 2, kBarAFull = kBarAccE + 2, kBarNyFull = kBarAFull + 1,
-              kBarNyEmpty = kBarNyFull + kNySlots, kBarCount = kBarNyEmpty + kNySlots;
+              kBarAccE = kBarAccF + 2, kBarAFull = kBarAccE + 2, kBarCount = kBarAFull + 1;
 constexpr int kBarBytes = 256;
 static_assert(kBarCount * 8 + 8 <= kBarBytes, "barrier region");
 struct TcSmem {
-    int part, a_off, b_off, stage_bytes, ny_off, bar_off, total;
-    __host__ __device__ TcSmem(int Kpad, int nst) {
-        part = part_bytes(Kpad);
+    int part, a_off, b_off, stage_bytes, ones_off, bar_off, total;
+    __host__ __device__ TcSmem(int W, int nst) {
+        part = part_bytes(W);
         a_off = 0;
         b_off = kQT * part;
         stage_bytes = part;
-        ny_off = b_off + nst * stage_bytes;
-        if (ny_off - b_off < 66 * kRows * 4) ny_off = b_off + 66 * kRows * 4;  // epilogue handoff
-        bar_off = ny_off + kNySlots * kTN * 4;
+        ones_off = b_off + nst * stage_bytes;
+        if (ones_off - b_off < 66 * kRows * 4) ones_off = b_off + 66 * kRows * 4;  // epilogue handoff
+        bar_off = ones_off + kOnesBytes;
         total = bar_off + kBarBytes;
     }
 };
@@ -120,11 +127,11 @@ constexpr int kSmemLimit = 232448;  // opt-in shared memory per CTA on sm_100
 constexpr int kSmemPair = 115712;   // per CTA when two CTAs share an SM (228 KiB, 1 KiB each reserved)
 // The deepest ring that still lets two CTAs share an SM, else (wide features)
 // the deepest ring for one CTA per SM.
-inline int stages_for(int Kpad) {
+inline int stages_for(int W) {
     for (int nst = kMaxStages; nst >= 2; --nst)
-        if (TcSmem(Kpad, nst).total <= kSmemPair) return nst;
+        if (TcSmem(W, nst).total <= kSmemPair) return nst;
     for (int nst = kMaxStages; nst > 2; --nst)
-        if (TcSmem(Kpad, nst).total <= kSmemLimit) return nst;
+        if (TcSmem(W, nst).total <= kSmemLimit) return nst;
     return 2;
 }
 
@@ -218,11 +225,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Three-input minimum (PTX min.f32 with three sources; the scores it is used
+// Three-input maximum (PTX max.f32 with three sources; the scores it is used
 // on are never NaN).
-__device__ __forceinline__ float fmin3(float a, float b, float c) {
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
-    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
 }
 
@@ -255,23 +262,25 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
 // ---- 1. pack and norms --------------------------------------------------------
 // Thread per (padded row, 8-feature chunk): 2^lg consecutive lanes per row
 // (the chunk count Kpad / 8 rounded up to a power of two), so that a row's
-// lanes form one aligned group of a warp.  Rows [0, B * ntiles * 128) are the
-// references, then (unless `same`: the queries are the references) the
-// B * mtiles * 128 query rows.  Rows past n and features past D pack zeros.
-// Each lane packs its two 16-byte core-matrix rows and sums the squares of its
-// 8 features in order; a butterfly over the row's lanes gives the norm (every
-// lane the same sum, fp32 addition being commutative).  vec: rows are read as
-// float4 (D % 4 == 0 and 16-byte aligned bases).  nr is padded per cloud to
-// ntiles * 128 entries (+inf past N); nmax = largest finite reference norm per
-// cloud (one atomic per warp), bad = a norm that is not finite or above kHuge.
+// lanes form one aligned group of a warp; the packed row is W = Kpad + 8
+// columns wide.  Rows [0, B * ntiles *
+// 128) are the references, then (unless `same`: the queries are the
+// references) the B * mtiles * 128 query rows.  Rows past n and features past
+// D pack zeros.  Each lane sums the squares of its 8 features in order; a
+// butterfly over the row's lanes gives the norm (every lane the same sum,
+// fp32 addition being commutative); each lane packs its two 16-byte
+// core-matrix rows of features, and lane 0 also the norm block: tf32(-n / 2)
+// (references; -2^100 for padding rows) or zeros (queries).  vec: rows
+// are read as float4 (D % 4 == 0 and 16-byte aligned bases).  nq receives the
+// query norms; nmax = largest finite reference norm per cloud (one atomic per
+// warp), bad = a norm that is not finite or above kHuge.
 __global__ void fknn_prep_kernel(const float* __restrict__ q, const float* __restrict__ r,
-                                 int64_t B, int64_t M, int64_t N, int D, int Kpad,
+                                 int64_t B, int64_t M, int64_t N, int D, int W,
                                  int64_t mtiles, int64_t ntiles, int vec, int same, int lg,
                                  unsigned char* __restrict__ qpack,
                                  unsigned char* __restrict__ rpack, float* __restrict__ nq,
-                                 float* __restrict__ nr, unsigned* __restrict__ nmax,
-                                 int* __restrict__ bad) {
-    const int chunks = Kpad / 8;
+                                 unsigned* __restrict__ nmax, int* __restrict__ bad) {
+    const int chunks = W / 8 - 1;  // feature chunks (the norm block follows)
     const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t prow_all = e >> lg;
     const int c = (int)(e & ((1 << lg) - 1));
@@ -286,7 +295,7 @@ __global__ void fknn_prep_kernel(const float* __restrict__ q, const float* __res
     float x[8];
 #pragma unroll
     for (int t = 0; t < 8; ++t) x[t] = 0.f;
-    if (point && c < chunks) {
+    if (point && c * 8 < D) {
         const float* src = (is_ref ? r : q) + (b * n + i) * D + c * 8;
         if (vec && c * 8 + 8 <= D) {
             const float4 u = reinterpret_cast<const float4*>(src)[0];
@@ -298,37 +307,37 @@ __global__ void fknn_prep_kernel(const float* __restrict__ q, const float* __res
             for (int t = 0; t < 8; ++t) x[t] = (c * 8 + t < D) ? src[t] : 0.f;
         }
     }
-    if (row_live && c < chunks) {
-        const uint4 lo4 = make_uint4(tf32_bits(x[0]), tf32_bits(x[1]), tf32_bits(x[2]),
-                                     tf32_bits(x[3]));
-        const uint4 hi4 = make_uint4(tf32_bits(x[4]), tf32_bits(x[5]), tf32_bits(x[6]),
-                                     tf32_bits(x[7]));
-        const int64_t tile = i / 128;
-        const int rr = (int)(i % 128);
-        unsigned char* blk =
-            (is_ref ? rpack : qpack) + (size_t)(b * tiles + tile) * part_bytes(Kpad);
-        const int off = (rr >> 3) * (Kpad / 4 * 128) + (2 * c) * 128 + (rr & 7) * 16;
-        *reinterpret_cast<uint4*>(blk + off) = lo4;
-        *reinterpret_cast<uint4*>(blk + off + 128) = hi4;
-    }
     float s = __fmul_rn(x[0], x[0]);
 #pragma unroll
     for (int t = 1; t < 8; ++t) s = __fadd_rn(s, __fmul_rn(x[t], x[t]));
     for (int off = (1 << lg) >> 1; off >= 1; off >>= 1)
         s = __fadd_rn(s, __shfl_xor_sync(FULL_MASK, s, off));
+    if (row_live && c < chunks) {
+        const int64_t tile = i / 128;
+        const int rr = (int)(i % 128);
+        unsigned char* blk =
+            (is_ref ? rpack : qpack) + (size_t)(b * tiles + tile) * part_bytes(W);
+        const int row_off = (rr >> 3) * (W / 4 * 128) + (rr & 7) * 16;
+        const int off = row_off + (2 * c) * 128;
+        *reinterpret_cast<uint4*>(blk + off) =
+            make_uint4(tf32_bits(x[0]), tf32_bits(x[1]), tf32_bits(x[2]), tf32_bits(x[3]));
+        *reinterpret_cast<uint4*>(blk + off + 128) =
+            make_uint4(tf32_bits(x[4]), tf32_bits(x[5]), tf32_bits(x[6]), tf32_bits(x[7]));
+        if (c == 0) {
+            // Norm block: -n / 2 (exact halving, then tf32) for a reference,
+            // -2^100 for a padding reference row, zeros for a query.
+            const float aug = is_ref ? (point ? -0.5f * s : -kPadNorm) : 0.f;
+            const int noff = row_off + (2 * chunks) * 128;
+            *reinterpret_cast<uint4*>(blk + noff) = make_uint4(tf32_bits(aug), 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(blk + noff + 128) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
     unsigned bits = 0u;
     if (point && c == 0) {
         const bool ok = isfinite(s) && s <= kHuge;
         if (!ok) bad[b] = 1;
-        if (is_ref) {
-            nr[prow] = s;
-            if (same) nq[b * M + i] = s;
-            if (ok) bits = __float_as_uint(s);
-        } else {
-            nq[b * M + i] = s;
-        }
-    } else if (row_live && is_ref && c == 0) {
-        nr[prow] = INFINITY;  // padding column of the last tile
+        if (!is_ref || same) nq[b * M + i] = s;
+        if (is_ref && ok) bits = __float_as_uint(s);
     }
     const int64_t bb = is_ref ? b : -1;
     const int64_t b0 = __shfl_sync(FULL_MASK, bb, 0);
@@ -340,42 +349,69 @@ __global__ void fknn_prep_kernel(const float* __restrict__ q, const float* __res
     }
 }
 
+// Error coefficient C_K of the approximate score (per unit of n(q) + n(r),
+// K = Kpad): 2 (2^-10 + 2^-22) for the tf32 rounding of the features,
+// 2^-11 for the tf32 rounding of -n(r) / 2 (times 2: the score is -2 t),
+// (K + 8) 2^-21 for the fp32 accumulation of K + 8 terms inside the tensor
+// core (2 ulps per term), (3 D + 16) 2^-24 for the fp32 norms and the
+// reference's own rounding; the whole sum is doubled as a margin.
 __device__ __forceinline__ float eps_coef(int D) {
     const int K = kpad_of(D);
-    return 2.f * (9.765625e-4f /* 2^-10 */ + 2.384185791015625e-7f /* 2^-22 */ +
-                  (float)K * 4.76837158203125e-7f /* 2^-21 */ +
+    return 2.f * (9.765625e-4f /* 2^-10 */ + 4.8828125e-4f /* 2^-11 */ +
+                  2.384185791015625e-7f /* 2^-22 */ +
+                  (float)(K + 8) * 4.76837158203125e-7f /* 2^-21 */ +
                   (3.f * (float)D + 16.f) * 5.9604644775390625e-8f /* 2^-24 */);
 }
 
 // ---- 2. approximate scores on the tensor cores ------------------------------
 // Barriers: full[s] (producer expect_tx + bulk-copy bytes), empty[s] (MMA
 // commit: operands of stage s read), accf[a] (MMA commit: accumulator a
-// written), acce[a] (4 epilogue warps: accumulator a read), nfull[i] / nempty[i]
-// for the norm ring (bulk copy / the 4 warps of the epilogue group).  Phase parity of round n = n & 1;
-// "free" barriers are waited with the opposite parity first.
-template <int PASS, int KCAP>
+// written), acce[a] (4 epilogue warps: accumulator a read), afull (query
+// tile).  Phase parity of round n = n & 1; "free" barriers are waited with
+// the opposite parity first.
+//
+// The accumulator holds t_j = -s_j / 2 (exactly: s'_j := -2 t'_j), so
+//   pass 1: bucket maxima of t (= -1/2 x bucket minima of s), written to the
+//           handoff area as s = -2 t; each epilogue group sorts its 32
+//           buckets in registers and group 0 takes the k-th smallest of the
+//           two sorted runs by a k-step merge;
+//   pass 2: a column joins when t_j >= -(U + 2 eps) / 2, i.e. s_j <= U + 2 eps
+//           (halving and -2 t are exact); a chunk of 32 columns whose maximum
+//           is below the threshold (almost all of them) is skipped after one
+//           three-input max tree.
+template <int PASS>
 __global__ void __launch_bounds__(kThreadsTC, 2)
 fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __restrict__ rpack,
                int64_t M, int64_t N, int64_t mtiles, int64_t ntiles, int D, int k,
-               const float* __restrict__ nq, const float* __restrict__ nr,
-               const unsigned* __restrict__ nmax, const int* __restrict__ bad,
-               float* __restrict__ ubound, unsigned* __restrict__ counts, uint2* __restrict__ cand,
+               const float* __restrict__ nq, const unsigned* __restrict__ nmax,
+               const int* __restrict__ bad, float* __restrict__ ubound,
+               unsigned* __restrict__ counts, uint2* __restrict__ cand,
                int* __restrict__ status, int nst) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int b = blockIdx.y;
     const int64_t mt = blockIdx.x;
     if (bad[b]) return;  // uniform: the cloud goes to the exact path
-    const int Kpad = kpad_of(D);
-    const TcSmem L(Kpad, nst);
+    const int Kpad = kpad_of(D), W = width_of(D);
+    const TcSmem L(W, nst);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar = sbase + L.bar_off;
-    // barrier addresses: full 0,1 | empty 2,3 | accf 4,5 | acce 6,7 | afull 8 |
-    // norms full 9-12 | norms empty 13-16
     auto B_ = [&](int i) { return bar + 8u * (uint32_t)i; };
     uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.bar_off + kBarCount * 8);
     int* s_abort = reinterpret_cast<int*>(smem + L.bar_off + kBarCount * 8 + 4);
 
+    // The ones block: column 0 of every row = 1.0 (tf32), else 0.  Written
+    // with generic stores, then made visible to the tensor core's (async
+    // proxy) operand reads before the CTA barrier.
+    {
+        uint32_t* ones = reinterpret_cast<uint32_t*>(smem + L.ones_off);
+        for (int w = tid; w < kOnesBytes / 4; w += kThreadsTC) {
+            // word w: byte 4 w = (row/8)*256 + (t/4)*128 + (row%8)*16 + (t%4)*4
+            const int t = ((w >> 5) & 1) * 4 + (w & 3);
+            ones[w] = t == 0 ? 0x3f800000u : 0u;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
     if (warp == 0) tmem_alloc(smem_u32(s_tmem), 2 * kQT * kTN);
     if (tid == 0) {
         for (int i = 0; i < kMaxStages; ++i) {
@@ -387,17 +423,13 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
             mbar_init(B_(kBarAccE + i), 4 * kQT);
         }
         mbar_init(B_(kBarAFull), 1);
-        for (int i = 0; i < kNySlots; ++i) {
-            mbar_init(B_(kBarNyFull + i), 1);
-            mbar_init(B_(kBarNyEmpty + i), 4 * kQT);
-        }
         *s_abort = 0;
         mbar_fence_init();
     }
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-    const uint32_t sbo = (uint32_t)(Kpad / 4 * 128);
+    const uint32_t sbo = (uint32_t)(W / 4 * 128);
     const uint32_t a_bytes = (uint32_t)L.part;
 
     if (warp == 0) {
@@ -420,29 +452,18 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                 bulk_expect(B_(kBarFull + st), a_bytes);
                 bulk_copy(dst, rpack + (size_t)(b * ntiles + t) * a_bytes, a_bytes,
                           B_(kBarFull + st));
-                const int ns = (int)(t % kNySlots);
-                const uint32_t nn = (uint32_t)(t / kNySlots);
-                if (!mbar_wait(B_(kBarNyEmpty + ns), (nn & 1) ^ 1)) {
-                    atomicExch(status, 1);
-                    *(volatile int*)s_abort = 1;
-                    ++issued;
-                    break;
-                }
-                bulk_expect(B_(kBarNyFull + ns), kTN * 4);
-                bulk_copy(sbase + L.ny_off + (uint32_t)(ns * kTN * 4),
-                          nr + (size_t)(b * ntiles + t) * kTN, kTN * 4, B_(kBarNyFull + ns));
                 ++issued;
             }
             // Copies still in flight (only after an abort) land before exit.
             mbar_wait(B_(kBarAFull), 0);
             for (int64_t t = max64(issued - nst, 0); t < issued; ++t)
                 mbar_wait(B_(kBarFull + (int)(t % nst)), (uint32_t)((t / nst) & 1));
-            for (int64_t t = max64(issued - kNySlots, 0); t < issued; ++t)
-                mbar_wait(B_(kBarNyFull + (int)(t % kNySlots)), (uint32_t)((t / kNySlots) & 1));
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
+            const uint32_t ones = sbase + L.ones_off;
+            const int fsteps = Kpad / 8;  // K = 8 tf32 per MMA: 2 core matrices (256 bytes)
             bool ok = mbar_wait(B_(kBarAFull), 0);
             for (int64_t t = 0; t < ntiles && ok; ++t) {
                 const int st = (int)(t % nst), ac = (int)(t & 1);
@@ -456,12 +477,14 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                     // Accumulator ac of query tile qt: columns (ac * kQT + qt) * kTN.
                     const uint32_t d = tmem + (uint32_t)((ac * kQT + qt) * kTN);
                     const uint32_t a0 = sbase + L.a_off + (uint32_t)qt * a_bytes;
-                    // K = 8 tf32 per MMA: two core matrices (2 x 128 bytes) per step.
-                    for (int s = 0; s < Kpad / 8; ++s) {
+                    for (int s = 0; s < fsteps; ++s) {
                         const uint32_t ko = (uint32_t)s * 256u;
                         mma_tf32(d, smem_desc(a0 + ko, 128, sbo), smem_desc(b0 + ko, 128, sbo),
                                  s == 0 ? 0u : 1u);
                     }
+                    // + ones . (-n(r) / 2): the references' norm block.
+                    mma_tf32(d, smem_desc(ones, 128, 256),
+                             smem_desc(b0 + (uint32_t)fsteps * 256u, 128, sbo), 1u);
                 }
                 mma_commit(B_(kBarEmpty + st));  // stage st may be refilled
                 mma_commit(B_(kBarAccF + ac));   // accumulator ac is ready
@@ -484,29 +507,29 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
         const bool qvalid = gq < M;
         const float nqi = qvalid ? nq[(int64_t)b * M + gq] : 0.f;
         const float eps = eps_coef(D) * (nqi + __uint_as_float(nmax[b]));
-        float thr = -INFINITY;  // pass 2: s_j <= thr makes j a candidate
-        if (PASS == 2 && qvalid) thr = ubound[(int64_t)b * M + gq] + 2.f * eps;
-        // Pass 1: bucket h * 16 + u of group g holds the minimum of s over
+        // Pass 2: t_j >= tthr makes j a candidate (+inf: no candidates).
+        // Group 0 fills the query's list from slot 0 up, group 1 from slot
+        // kCap - 1 down.
+        uint2* const crow = cand + ((int64_t)b * M + (qvalid ? gq : 0)) * kCap;
+        float tthr = INFINITY;
+        if (PASS == 2 && qvalid) tthr = -0.5f * (ubound[(int64_t)b * M + gq] + 2.f * eps);
+        // Pass 1: bucket h * 16 + u of group g holds the maximum of t over
         // columns 2u and 2u + 1 of the 32-column chunks c with c & 1 == h of
         // the group's tiles; with the other group's buckets, the k-th smallest
-        // of the 64 bucket minima bounds the k-th smallest s from above (k
-        // buckets -> k distinct columns).
-        float bmin[32];
+        // of the 64 bucket minima of s = -2 t bounds the k-th smallest s from
+        // above (k buckets -> k distinct columns).
+        float bmax[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) bmin[i] = INFINITY;
+        for (int i = 0; i < 32; ++i) bmax[i] = -INFINITY;
         unsigned found = 0;
         bool ok = true;
         for (int64_t t = group; t < ntiles; t += 2) {
             const int ac = group;
             const uint32_t n = (uint32_t)(t >> 1);
-            const int ns = (int)(t % kNySlots);
-            const bool got = mbar_wait(B_(kBarAccF + ac), n & 1) &&
-                             mbar_wait(B_(kBarNyFull + ns), (uint32_t)((t / kNySlots) & 1));
+            const bool got = mbar_wait(B_(kBarAccF + ac), n & 1);
             ok = __all_sync(FULL_MASK, got) && !*(volatile int*)s_abort;
             if (!ok) break;
             tc_fence_after();
-            const float* s_ny = reinterpret_cast<const float*>(smem + L.ny_off + ns * kTN * 4);
-            // The norms of slot ns stay until this group arrives on its empty barrier.
             // Chunks in pairs: chunk c feeds buckets (c & 1) * 16 + u, and
             // the pair index h = c & 1 is a compile-time constant.
 #pragma unroll 1
@@ -518,73 +541,75 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                 tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) +
                               (uint32_t)((ac * kQT + qt) * kTN + c * 32),
                           v);
-                const float4* ny4 = reinterpret_cast<const float4*>(s_ny + c * 32);
-                // Scores s = n(r) - 2 dot as packed f32x2 FMAs (two columns
-                // per instruction; the same single rounding as fmaf).
-                const f32x2 m2 = pack2(-2.f, -2.f);
                 if (PASS == 1) {
-                    // Columns 2u and 2u + 1 of the chunk -> bucket h * 16 + u,
-                    // one three-input minimum per two columns.
+                    // Columns 2u and 2u + 1 of the chunk -> bucket h * 16 + u.
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const float4 y = ny4[i];
-                        float sc[4];
-                        unpack2(fma2(pack2(v[4 * i + 0], v[4 * i + 1]), m2, pack2(y.x, y.y)),
-                                sc[0], sc[1]);
-                        unpack2(fma2(pack2(v[4 * i + 2], v[4 * i + 3]), m2, pack2(y.z, y.w)),
-                                sc[2], sc[3]);
-                        bmin[16 * h + 2 * i] = fmin3(bmin[16 * h + 2 * i], sc[0], sc[1]);
-                        bmin[16 * h + 2 * i + 1] = fmin3(bmin[16 * h + 2 * i + 1], sc[2], sc[3]);
+                        bmax[16 * h + 2 * i] = fmax3(bmax[16 * h + 2 * i], v[4 * i], v[4 * i + 1]);
+                        bmax[16 * h + 2 * i + 1] =
+                            fmax3(bmax[16 * h + 2 * i + 1], v[4 * i + 2], v[4 * i + 3]);
                     }
                 } else {
-                    // Candidate bit mask of the 32 columns (no divergence),
-                    // then one store per set bit.  Group 0 fills the list
-                    // from slot 0 up, group 1 from slot kCap - 1 down.
-                    unsigned hits = 0u;
+                    // Candidate bit mask of the 32 columns: one set.ge (all
+                    // ones when t_j >= tthr) and one lop3 per column, then
+                    // one store per set bit (about one in 170 columns).
+                    uint32_t hits = 0u;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 y = ny4[i];
-                        float sc[4];
-                        unpack2(fma2(pack2(v[4 * i + 0], v[4 * i + 1]), m2, pack2(y.x, y.y)),
-                                sc[0], sc[1]);
-                        unpack2(fma2(pack2(v[4 * i + 2], v[4 * i + 3]), m2, pack2(y.z, y.w)),
-                                sc[2], sc[3]);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            hits |= (sc[e] <= thr ? 1u : 0u) << (4 * i + e);
+                    for (int e = 0; e < 32; ++e) {
+                        uint32_t m;
+                        asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(m) : "f"(v[e]), "f"(tthr));
+                        hits |= m & (1u << e);
                     }
-                    while (hits) {
-                        const int i = __ffs(hits) - 1;
-                        hits &= hits - 1;
-                        if (found < (unsigned)kCap) {
-                            const unsigned slot = group ? (unsigned)kCap - 1u - found : found;
-                            cand[((int64_t)b * M + gq) * kCap + slot] =
-                                make_uint2((unsigned)(t * kTN + c * 32 + i), 0u);
-                        }
-                        ++found;
+                    if (hits) {
+                        const uint32_t col0 = (uint32_t)(t * kTN + c * 32);
+                        do {
+                            const int i = __ffs(hits) - 1;
+                            hits &= hits - 1;
+                            if (found < (unsigned)kCap)
+                                crow[group ? (int)(kCap - 1 - found) : (int)found] =
+                                    make_uint2(col0 + (uint32_t)i, 0u);
+                            ++found;
+                        } while (hits);
                     }
                 }
               }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(B_(kBarAccE + ac));     // accumulator read
-                mbar_arrive(B_(kBarNyEmpty + ns));  // norms read
-            }
+            if (lane == 0) mbar_arrive(B_(kBarAccE + ac));  // accumulator read
         }
         if (!ok) {
             if (lane == 0) atomicExch(status, 1);
             *(volatile int*)s_abort = 1;
         }
         // Hand group 1's state to group 0 through the (idle) B stages:
-        // s_x[u * kTM + row] = bucket u (0-31 group 0, 32-63 group 1), then
-        // group 1's count and status.
+        // s_x[u * kRows + row] = bucket u of s (0-31 group 0, 32-63 group 1),
+        // each group's run sorted ascending; then group 1's count and status.
         float* s_x = reinterpret_cast<float*>(smem + L.b_off);
         named_barrier_sync(1, 8 * kQT * 32);  // both epilogue groups finished their tiles
         if (PASS == 1) {
+            // s = -2 t (exact); ascending s = descending t.  Bitonic network
+            // over the 32 registers (compile-time indices).
 #pragma unroll
-            for (int i = 0; i < 32; ++i) s_x[(32 * group + i) * kRows + row] = bmin[i];
+            for (int i = 0; i < 32; ++i) bmax[i] = -2.f * bmax[i];
+#pragma unroll
+            for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+                for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int j = i ^ stride;
+                        if (j > i) {
+                            const float lo = fminf(bmax[i], bmax[j]), hi = fmaxf(bmax[i], bmax[j]);
+                            const bool up = (i & size) == 0;
+                            bmax[i] = up ? lo : hi;
+                            bmax[j] = up ? hi : lo;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) s_x[(32 * group + i) * kRows + row] = bmax[i];
         }
         if (group == 1) {
             s_x[64 * kRows + row] = __uint_as_float(found);
@@ -594,25 +619,18 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
         if (group == 0) {
             ok = ok && s_x[65 * kRows + row] != 0.f;
             if (PASS == 1) {
-                // k-th smallest of the 64 bucket minima (sorted right-aligned list).
-                float lst[KCAP];
-#pragma unroll
-                for (int i = 0; i < KCAP; ++i) lst[i] = i < KCAP - k ? -INFINITY : INFINITY;
-#pragma unroll 1
-                for (int u = 0; u < 64; ++u) {
-                    // Own buckets were parked next to group 1's, so both halves
-                    // are read from shared memory (no dynamic register index).
-                    const float g = s_x[u * kRows + row];
-                    if (g < lst[KCAP - 1]) {
-#pragma unroll
-                        for (int i = KCAP - 1; i >= 1; --i) {
-                            const float lo = lst[i - 1];
-                            lst[i] = (g < lo) ? lo : ((g < lst[i]) ? g : lst[i]);
-                        }
-                        lst[0] = fminf(lst[0], g);
-                    }
+                // k-th smallest of the two sorted runs of 32 (k <= 32).
+                int ia = 0, ib = 0;
+                float kth = INFINITY;
+                for (int i = 0; i < k; ++i) {
+                    const float x0 = ia < 32 ? s_x[ia * kRows + row] : INFINITY;
+                    const float x1 = ib < 32 ? s_x[(32 + ib) * kRows + row] : INFINITY;
+                    const bool first = !(x1 < x0);
+                    kth = first ? x0 : x1;
+                    ia += first ? 1 : 0;
+                    ib += first ? 0 : 1;
                 }
-                if (qvalid) ubound[(int64_t)b * M + gq] = ok ? lst[KCAP - 1] : INFINITY;
+                if (qvalid) ubound[(int64_t)b * M + gq] = ok ? kth : INFINITY;
             } else if (qvalid) {
                 const unsigned f1 = __float_as_uint(s_x[64 * kRows + row]);
                 // Packed (group 0 count, group 1 count); overflow -> exact path.
@@ -949,7 +967,6 @@ struct Scratch {
     unsigned char* qpack;
     unsigned char* rpack;
     float* nq;
-    float* nr;
     float* ubound;
     unsigned* counts;
     uint2* cand;
@@ -974,11 +991,10 @@ inline Scratch carve(void* base, int64_t B, int64_t M, int64_t N, int64_t D) {
     };
     // Query tiles rounded up to whole CTAs (kQT tiles each).
     const int64_t mt = ceil_div(M, kRows) * kQT, nt = ceil_div(N, kTN);
-    const size_t tile = (size_t)part_bytes(kpad_of((int)D));
+    const size_t tile = (size_t)part_bytes(width_of((int)D));
     s.qpack = take(tile * B * mt);
     s.rpack = take(tile * B * nt);
     s.nq = reinterpret_cast<float*>(take(sizeof(float) * B * M));
-    s.nr = reinterpret_cast<float*>(take(sizeof(float) * B * nt * kTN));
     s.ubound = reinterpret_cast<float*>(take(sizeof(float) * B * M));
     s.counts = reinterpret_cast<unsigned*>(take(sizeof(unsigned) * B * M));
     s.cand = reinterpret_cast<uint2*>(take(sizeof(uint2) * B * M * kCap));
@@ -999,37 +1015,37 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
            float* dist, int64_t* idx, float* sqdist, const Scratch& w, cudaStream_t s) {
     if (cudaMemsetAsync(w.nmax, 0, flag_bytes(B), s) != cudaSuccess)
         return fail(kCudaError, "knn: scratch reset failed");
-    const int Kpad = kpad_of(D);
+    const int W = width_of(D);
     const int64_t mt = ceil_div(M, kRows) * kQT, nt = ceil_div(N, kTN);
     // kNN of a cloud against itself (knn(f, f, k)): one pack serves both operands.
     const int same = (query == ref && M == N) ? 1 : 0;
     int lg = 0;
-    while ((1 << lg) < Kpad / 8) ++lg;
+    while ((1 << lg) < W / 8 - 1) ++lg;
     const int64_t rows = B * nt * 128 + (same ? 0 : B * mt * 128);
     // 16-byte row loads only when every row starts on a 16-byte boundary.
     const int vec = (D % 4 == 0 && aligned_to(query, 16) && aligned_to(ref, 16)) ? 1 : 0;
     fknn_prep_kernel<<<(unsigned)ceil_div(rows << lg, 256), 256, 0, s>>>(
-        query, ref, B, M, N, D, Kpad, mt, nt, vec, same, lg, w.qpack, w.rpack, w.nq, w.nr,
-        w.nmax, w.bad);
+        query, ref, B, M, N, D, W, mt, nt, vec, same, lg, w.qpack, w.rpack, w.nq, w.nmax,
+        w.bad);
     int st = check_launch("fknn_prep_kernel");
     if (st) return st;
     const unsigned char* qpack = same ? w.rpack : w.qpack;
-    const int nst = stages_for(Kpad);
-    const TcSmem L(Kpad, nst);
-    auto k1 = fknn_tc_kernel<1, KCAP>;
-    auto k2 = fknn_tc_kernel<2, KCAP>;
+    const int nst = stages_for(W);
+    const TcSmem L(W, nst);
+    auto k1 = fknn_tc_kernel<1>;
+    auto k2 = fknn_tc_kernel<2>;
     if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
             cudaSuccess ||
         cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
             cudaSuccess)
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");
     dim3 grid((unsigned)(mt / kQT), (unsigned)B);
-    k1<<<grid, kThreadsTC, L.total, s>>>(qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
-                                         w.bad, w.ubound, w.counts, w.cand, w.status, nst);
+    k1<<<grid, kThreadsTC, L.total, s>>>(qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nmax, w.bad,
+                                         w.ubound, w.counts, w.cand, w.status, nst);
     st = check_launch("fknn_tc_kernel<1>");
     if (st) return st;
-    k2<<<grid, kThreadsTC, L.total, s>>>(qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nr, w.nmax,
-                                         w.bad, w.ubound, w.counts, w.cand, w.status, nst);
+    k2<<<grid, kThreadsTC, L.total, s>>>(qpack, w.rpack, M, N, mt, nt, D, k, w.nq, w.nmax, w.bad,
+                                         w.ubound, w.counts, w.cand, w.status, nst);
     st = check_launch("fknn_tc_kernel<2>");
     if (st) return st;
     auto rk = !vec ? fknn_rerank_kernel<0, 0>
