@@ -376,9 +376,9 @@ __device__ __forceinline__ float eps_coef(int D) {
 //           buckets in registers and group 0 takes the k-th smallest of the
 //           two sorted runs by a k-step merge;
 //   pass 2: a column joins when t_j >= -(U + 2 eps) / 2, i.e. s_j <= U + 2 eps
-//           (halving and -2 t are exact); a chunk of 32 columns whose maximum
-//           is below the threshold (almost all of them) is skipped after one
-//           three-input max tree.
+//           (halving and -2 t are exact); the candidate mask of a 32-column
+//           chunk costs one packed subtraction per two columns and one funnel
+//           shift per column.
 template <int PASS>
 __global__ void __launch_bounds__(kThreadsTC, 2)
 fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __restrict__ rpack,
@@ -550,24 +550,35 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
                             fmax3(bmax[16 * h + 2 * i + 1], v[4 * i + 2], v[4 * i + 3]);
                     }
                 } else {
-                    // Candidate bit mask of the 32 columns: one set.ge (all
-                    // ones when t_j >= tthr) and one lop3 per column, then
-                    // one store per set bit (about one in 170 columns).
-                    uint32_t hits = 0u;
+                    // Candidate mask of the 32 columns: d = t - tthr for two
+                    // columns per packed subtraction; t_j >= tthr exactly when
+                    // d_j's sign bit is clear (an exact difference of finite
+                    // floats is never -0, and the subtraction keeps
+                    // subnormals).  One funnel shift per column moves d_j's
+                    // sign bit into a running word (four independent words
+                    // of 8 columns), so bit 31 - j of `miss` is set when
+                    // column j is not a candidate.
+                    const f32x2 T2 = pack2(tthr, tthr);
+                    uint32_t acc[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        uint32_t m;
-                        asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(m) : "f"(v[e]), "f"(tthr));
-                        hits |= m & (1u << e);
+                    for (int i = 0; i < 16; ++i) {
+                        float d0, d1;
+                        unpack2(sub2(pack2(v[2 * i], v[2 * i + 1]), T2), d0, d1);
+                        uint32_t& a = acc[i >> 2];
+                        a = __funnelshift_l(__float_as_uint(d0), a, 1);
+                        a = __funnelshift_l(__float_as_uint(d1), a, 1);
                     }
+                    uint32_t hits = ~((acc[0] << 24) | (acc[1] << 16) | (acc[2] << 8) | acc[3]);
                     if (hits) {
+                        // Bit 31 - j set: column j is a candidate (about one
+                        // column in 170).
                         const uint32_t col0 = (uint32_t)(t * kTN + c * 32);
                         do {
-                            const int i = __ffs(hits) - 1;
-                            hits &= hits - 1;
+                            const int j = __clz(hits);
+                            hits ^= 0x80000000u >> j;
                             if (found < (unsigned)kCap)
                                 crow[group ? (int)(kCap - 1 - found) : (int)found] =
-                                    make_uint2(col0 + (uint32_t)i, 0u);
+                                    make_uint2(col0 + (uint32_t)j, 0u);
                             ++found;
                         } while (hits);
                     }
