@@ -699,54 +699,28 @@ __device__ __forceinline__ float sqd_staged(const float* __restrict__ qs,
     return s;
 }
 
-// Exact sequential SD of two shared-memory rows, both 16-byte aligned with
-// D % 4 == 0 (fully unrolled when D is a compile-time DC).
-template <int DC>
-__device__ __forceinline__ float sqd_smem4(const float* __restrict__ a,
-                                           const float* __restrict__ b, int D) {
-    const float4* a4 = reinterpret_cast<const float4*>(a);
-    const float4* b4 = reinterpret_cast<const float4*>(b);
-    float4 x = a4[0], y = b4[0];
-    float d = __fsub_rn(x.x, y.x);
-    float s = __fmul_rn(d, d);
-    d = __fsub_rn(x.y, y.y);
-    s = __fadd_rn(s, __fmul_rn(d, d));
-    d = __fsub_rn(x.z, y.z);
-    s = __fadd_rn(s, __fmul_rn(d, d));
-    d = __fsub_rn(x.w, y.w);
-    s = __fadd_rn(s, __fmul_rn(d, d));
-#pragma unroll(DC ? DC / 4 : 4)
-    for (int u = 1; u < D / 4; ++u) {
-        x = a4[u];
-        y = b4[u];
-        d = __fsub_rn(x.x, y.x);
-        s = __fadd_rn(s, __fmul_rn(d, d));
-        d = __fsub_rn(x.y, y.y);
-        s = __fadd_rn(s, __fmul_rn(d, d));
-        d = __fsub_rn(x.z, y.z);
-        s = __fadd_rn(s, __fmul_rn(d, d));
-        d = __fsub_rn(x.w, y.w);
-        s = __fadd_rn(s, __fmul_rn(d, d));
-    }
-    return s;
-}
-
-// Row stride (floats) of the re-rank's staged rows: with 16-byte rows the
-// stride is an odd number of float4s, otherwise an odd number of floats, so
-// that 32 lanes reading the same column of 32 rows hit distinct banks.
-__host__ __device__ constexpr int rerank_stride(int D, int vec) {
-    return vec ? 4 * (((D / 4) & 1) ? D / 4 : D / 4 + 1) : ((D & 1) ? D : D + 1);
-}
+// Row stride (floats) of the scalar re-rank's staged rows: an odd number of
+// floats, so that 32 lanes reading the same column of 32 rows hit distinct
+// banks.
+__host__ __device__ constexpr int rerank_stride(int D) { return (D & 1) ? D : D + 1; }
 constexpr int kRerankWarps = 8;
-// Shared memory of one re-rank CTA: per warp the query row and 32 staged rows.
-inline size_t rerank_smem_bytes(int D, int vec) {
-    return (size_t)kRerankWarps * 33 * rerank_stride(D, vec) * sizeof(float);
+// Shared memory of one scalar re-rank CTA: per warp the query row and 32 staged rows.
+inline size_t rerank_smem_bytes(int D) {
+    return (size_t)kRerankWarps * 33 * rerank_stride(D) * sizeof(float);
 }
 
-__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-                 : "memory");
+// 16-byte rows (D % 4 == 0, both arrays 16-byte aligned): the candidates'
+// rows are staged in two parts, features [0, Dh) and [Dh, D) with Dh the
+// first half rounded to whole float4s; the sequential SD runs on across the
+// parts.  A staged part's stride is an odd number of float4s (conflict-free
+// lane-per-row float4 reads).
+__host__ __device__ constexpr int bulk_half(int D) { return ((D / 4 + 1) / 2) * 4; }
+__host__ __device__ constexpr int bulk_stride(int D) { return 4 * ((bulk_half(D) / 4) | 1); }
+// Per warp: the query row (D floats) and 32 staged parts.
+inline size_t rerank_bulk_smem_bytes(int D) {
+    return (size_t)kRerankWarps * (D + 32 * bulk_stride(D)) * sizeof(float);
 }
+
 __device__ __forceinline__ void cp_async4(float* dst, const float* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
                  : "memory");
@@ -766,89 +740,13 @@ __device__ __forceinline__ uint64_t bitonic_step(uint64_t key, int e, int size, 
     return keep_min ? lo : hi;
 }
 
-// VEC: 16-byte rows; DC: the feature width when fixed at compile time (0:
-// D at run time).  Grid (ceil(M / warps), B).
-template <int VEC, int DC>
-__global__ void __launch_bounds__(kRerankWarps * 32)
-fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t M,
-                   int64_t N, int D_rt, int k, const int* __restrict__ bad,
-                   const unsigned* __restrict__ counts, const uint2* __restrict__ cand,
-                   float* __restrict__ dist, int64_t* __restrict__ idx64,
-                   float* __restrict__ sqdist, unsigned* __restrict__ nover,
-                   int64_t* __restrict__ over_rows) {
-    static_assert(kCap == 64, "two candidates per lane");
-    static_assert(DC == 0 || (VEC && DC % 4 == 0), "fixed widths use 16-byte rows");
-    extern __shared__ __align__(16) float s_stage[];  // [warps][33][stride]
-    const int D = DC ? DC : D_rt;
-    const int lane = threadIdx.x & 31;
-    const int64_t m = (int64_t)blockIdx.x * kRerankWarps + (threadIdx.x >> 5);
-    if (m >= M) return;  // warp-uniform
-    const int64_t b = blockIdx.y;
-    const int64_t row = b * M + m;
-    const float* rb = r + b * N * D;
-    const int stride = rerank_stride(D, VEC);
-    float* qp = s_stage + (threadIdx.x >> 5) * 33 * stride;
-    float* rows = qp + stride;
-    const unsigned packed = bad[b] ? 0xffffffffu : counts[row];
-    const int64_t o = row * k;
-    if (packed == 0xffffffffu) {  // exact scan by fknn_exact_rows_kernel
-        if (lane == 0) over_rows[atomicAdd(nover, 1u)] = row;
-        return;
-    }
-    // Candidates: slots [0, f0) from the even tiles, [kCap - f1, kCap) from
-    // the odd tiles.
-    const unsigned f0 = packed & 0xffffu, f1 = packed >> 16, cnt = f0 + f1;
-    for (int t = lane; t < D; t += 32) qp[t] = q[row * D + t];
-    // Copy units (float4 or float) per row: LPR lanes per row (the largest
-    // power of two <= min(U, 8)), so one copy instruction covers R = 32 / LPR
-    // rows and each lane copies units u0, u0 + LPR, ... of its row (D = 64:
-    // 4 rows of 16 float4s per instruction, two per lane).
-    const int U = VEC ? D / 4 : D;
-    const int LPR = U >= 8 ? 8 : (U >= 4 ? 4 : (U >= 2 ? 2 : 1));
-    const int R = 32 / LPR;
-    const int roff = lane / LPR;
-    const int u0 = lane % LPR;
-    float sd[2];
-    uint32_t jj[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        sd[h] = INFINITY;
-        jj[h] = kNoIndex;
-        const unsigned c0 = 32u * (unsigned)h;
-        if (c0 >= cnt) continue;  // warp-uniform
-        const unsigned n = min(32u, cnt - c0);
-        const unsigned c = c0 + (unsigned)lane;
-        uint32_t j = kNoIndex;
-        if (c < cnt) {
-            const unsigned slot = c < f0 ? c : (unsigned)kCap - 1u - (c - f0);
-            j = cand[row * kCap + slot].x;
-        }
-        for (unsigned base = 0; base < n; base += (unsigned)R) {
-            const unsigned rl = base + (unsigned)roff;
-            const uint32_t jr = __shfl_sync(FULL_MASK, j, (int)(rl & 31u));
-            if (rl < n && jr < (uint32_t)N) {
-                const float* src = rb + (int64_t)jr * D;
-                float* dst = rows + rl * stride;
-                for (int u = u0; u < U; u += LPR) {
-                    if (VEC)
-                        cp_async16(dst + 4 * u, src + 4 * u);
-                    else
-                        cp_async4(dst + u, src + u);
-                }
-            }
-        }
-        cp_async_wait_all();
-        __syncwarp();
-        if (c < cnt && j < (uint32_t)N) {
-            const float* rp = rows + lane * stride;
-            const float v = VEC ? sqd_smem4<DC>(qp, rp, D) : sqd_seq(qp, rp, D);
-            if (isfinite(v)) {
-                sd[h] = v;
-                jj[h] = j;
-            }
-        }
-        __syncwarp();  // the rows are refilled for the second half
-    }
+// Rank the warp's (SD, index) pairs (lane holds candidates lane and 32 +
+// lane; empty slots are (inf, kNoIndex)) and write the first k.
+__device__ __forceinline__ void rerank_emit(const float (&sd)[2], const uint32_t (&jj)[2],
+                                            unsigned cnt, int k, int lane,
+                                            float* __restrict__ dist,
+                                            int64_t* __restrict__ idx64,
+                                            float* __restrict__ sqdist, int64_t o) {
     // Sort the (SD, index) pairs as 64-bit keys (finite SD >= 0: the bits
     // order like the values; an empty slot is (inf, kNoIndex), after all):
     // a warp bitonic sort of 32 keys, or of 64 keys (two per lane, element
@@ -911,6 +809,215 @@ fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int
         if (sqdist) sqdist[o + lane] = filled ? d : INFINITY;
         idx64[o + lane] = filled ? (int64_t)j : -1;
     }
+}
+
+// Scalar rows (any alignment or width).  Grid (ceil(M / warps), B).  The
+// warp copies its candidates' rows into shared memory with coalesced 4-byte
+// cp.async (LPR lanes per row), lane l computes candidate l's exact SD from
+// there, for candidates 0-31 and then 32-63.
+__global__ void __launch_bounds__(kRerankWarps * 32)
+fknn_rerank_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t M,
+                   int64_t N, int D, int k, const int* __restrict__ bad,
+                   const unsigned* __restrict__ counts, const uint2* __restrict__ cand,
+                   float* __restrict__ dist, int64_t* __restrict__ idx64,
+                   float* __restrict__ sqdist, unsigned* __restrict__ nover,
+                   int64_t* __restrict__ over_rows) {
+    static_assert(kCap == 64, "two candidates per lane");
+    extern __shared__ __align__(16) float s_stage[];  // [warps][33][stride]
+    const int lane = threadIdx.x & 31;
+    const int64_t m = (int64_t)blockIdx.x * kRerankWarps + (threadIdx.x >> 5);
+    if (m >= M) return;  // warp-uniform
+    const int64_t b = blockIdx.y;
+    const int64_t row = b * M + m;
+    const float* rb = r + b * N * D;
+    const int stride = rerank_stride(D);
+    float* qp = s_stage + (threadIdx.x >> 5) * 33 * stride;
+    float* rows = qp + stride;
+    const unsigned packed = bad[b] ? 0xffffffffu : counts[row];
+    const int64_t o = row * k;
+    if (packed == 0xffffffffu) {  // exact scan by fknn_exact_rows_kernel
+        if (lane == 0) over_rows[atomicAdd(nover, 1u)] = row;
+        return;
+    }
+    // Candidates: slots [0, f0) from the even tiles, [kCap - f1, kCap) from
+    // the odd tiles.
+    const unsigned f0 = packed & 0xffffu, f1 = packed >> 16, cnt = f0 + f1;
+    for (int t = lane; t < D; t += 32) qp[t] = q[row * D + t];
+    // LPR lanes per row (the largest power of two <= min(D, 8)), so one copy
+    // instruction covers R = 32 / LPR rows.
+    const int LPR = D >= 8 ? 8 : (D >= 4 ? 4 : (D >= 2 ? 2 : 1));
+    const int R = 32 / LPR;
+    const int roff = lane / LPR;
+    const int u0 = lane % LPR;
+    float sd[2];
+    uint32_t jj[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        sd[h] = INFINITY;
+        jj[h] = kNoIndex;
+        const unsigned c0 = 32u * (unsigned)h;
+        if (c0 >= cnt) continue;  // warp-uniform
+        const unsigned n = min(32u, cnt - c0);
+        const unsigned c = c0 + (unsigned)lane;
+        uint32_t j = kNoIndex;
+        if (c < cnt) {
+            const unsigned slot = c < f0 ? c : (unsigned)kCap - 1u - (c - f0);
+            j = cand[row * kCap + slot].x;
+        }
+        for (unsigned base = 0; base < n; base += (unsigned)R) {
+            const unsigned rl = base + (unsigned)roff;
+            const uint32_t jr = __shfl_sync(FULL_MASK, j, (int)(rl & 31u));
+            if (rl < n && jr < (uint32_t)N) {
+                const float* src = rb + (int64_t)jr * D;
+                float* dst = rows + rl * stride;
+                for (int u = u0; u < D; u += LPR) cp_async4(dst + u, src + u);
+            }
+        }
+        cp_async_wait_all();
+        __syncwarp();
+        if (c < cnt && j < (uint32_t)N) {
+            const float v = sqd_seq(qp, rows + lane * stride, D);
+            if (isfinite(v)) {
+                sd[h] = v;
+                jj[h] = j;
+            }
+        }
+        __syncwarp();  // the rows are refilled for the second half
+    }
+    rerank_emit(sd, jj, cnt, k, lane, dist, idx64, sqdist, o);
+}
+
+// Exact sequential SD over features [t0, t1) (multiples of 4) of the query
+// row qa and the staged part rb (rb holds features from t0 on), continuing
+// the running sum s; t0 == 0 starts it.  Both rows 16-byte aligned.
+template <int T0, int T1>
+__device__ __forceinline__ void sqd_part(const float* __restrict__ qa,
+                                         const float* __restrict__ rb, int t0, int t1,
+                                         float& s) {
+    const int a = T1 ? T0 : t0, e = T1 ? T1 : t1;
+#pragma unroll(T1 ? (T1 - T0) / 4 : 4)
+    for (int t = a; t < e; t += 4) {
+        const float4 x = *reinterpret_cast<const float4*>(qa + t);
+        const float4 y = *reinterpret_cast<const float4*>(rb + (t - a));
+        float d = __fsub_rn(x.x, y.x);
+        s = (t == 0) ? __fmul_rn(d, d) : __fadd_rn(s, __fmul_rn(d, d));
+        d = __fsub_rn(x.y, y.y);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+        d = __fsub_rn(x.z, y.z);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+        d = __fsub_rn(x.w, y.w);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+    }
+}
+
+// 16-byte rows.  Lane l copies candidate l's row part with one cp.async.bulk
+// (completion on the warp's mbarrier; lane 0 also copies the query row and
+// posts the expected bytes), so a part of 32 rows costs one copy instruction
+// per lane.  Two parts per 32 candidates; each warp's barrier serves one
+// query, its phase flips per part.  The previous part's shared-memory reads
+// are ordered before the next bulk writes by fence.proxy.async.  Every wait
+// is bounded (kWaitNs); after a timeout the warp waits once more for its
+// copies in flight and computes the rest from global memory.  Grid
+// (ceil(M / warps), B).
+template <int DC>
+__global__ void __launch_bounds__(kRerankWarps * 32)
+fknn_rerank_bulk_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t M,
+                        int64_t N, int D_rt, int k, const int* __restrict__ bad,
+                        const unsigned* __restrict__ counts, const uint2* __restrict__ cand,
+                        float* __restrict__ dist, int64_t* __restrict__ idx64,
+                        float* __restrict__ sqdist, unsigned* __restrict__ nover,
+                        int64_t* __restrict__ over_rows) {
+    static_assert(kCap == 64, "two candidates per lane");
+    static_assert(DC % 4 == 0, "16-byte rows");
+    extern __shared__ __align__(16) float s_stage[];  // [warps][D + 32 * stride]
+    __shared__ __align__(8) unsigned long long s_bar[kRerankWarps];
+    const int D = DC ? DC : D_rt;
+    constexpr int DH = DC ? bulk_half(DC) : 0;
+    const int Dh = DC ? DH : bulk_half(D);
+    const int hs = bulk_stride(D);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t m = (int64_t)blockIdx.x * kRerankWarps + warp;
+    if (m >= M) return;  // warp-uniform
+    const int64_t b = blockIdx.y;
+    const int64_t row = b * M + m;
+    const float* rb = r + b * N * D;
+    const float* qg = q + row * D;
+    float* qp = s_stage + warp * (D + 32 * hs);
+    float* part = qp + D + lane * hs;  // this lane's staged row part
+    const unsigned packed = bad[b] ? 0xffffffffu : counts[row];
+    const int64_t o = row * k;
+    if (packed == 0xffffffffu) {  // exact scan by fknn_exact_rows_kernel
+        if (lane == 0) over_rows[atomicAdd(nover, 1u)] = row;
+        return;
+    }
+    const unsigned f0 = packed & 0xffffu, f1 = packed >> 16, cnt = f0 + f1;
+    const uint32_t bar = smem_u32(&s_bar[warp]);
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+    uint32_t phase = 0;
+    bool ok = true;
+    float sd[2];
+    uint32_t jj[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        sd[h] = INFINITY;
+        jj[h] = kNoIndex;
+        const unsigned c0 = 32u * (unsigned)h;
+        if (c0 >= cnt) continue;  // warp-uniform
+        const unsigned c = c0 + (unsigned)lane;
+        uint32_t j = kNoIndex;
+        if (c < cnt) {
+            const unsigned slot = c < f0 ? c : (unsigned)kCap - 1u - (c - f0);
+            j = cand[row * kCap + slot].x;
+        }
+        const bool live = c < cnt && j < (uint32_t)N;
+        const unsigned nlive = (unsigned)__popc(__ballot_sync(FULL_MASK, live));
+        const float* rg = rb + (int64_t)(live ? j : 0u) * D;
+        float s = 0.f;
+#pragma unroll
+        for (int pt = 0; pt < 2; ++pt) {
+            const int t0 = pt ? Dh : 0, t1 = pt ? D : Dh;
+            if (ok) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                const bool first = h == 0 && pt == 0;
+                if (lane == 0)
+                    bulk_expect(bar, nlive * (uint32_t)(t1 - t0) * 4u + (first ? (uint32_t)D * 4u : 0u));
+                __syncwarp();
+                if (first && lane == 0) bulk_copy(smem_u32(qp), qg, (uint32_t)D * 4u, bar);
+                if (live) bulk_copy(smem_u32(part), rg + t0, (uint32_t)(t1 - t0) * 4u, bar);
+                bool got = mbar_wait(bar, phase);
+                if (!__all_sync(FULL_MASK, got)) {
+                    // Copies still in flight land before the warp goes on.
+                    got = mbar_wait(bar, phase);
+                    ok = false;
+                }
+                phase ^= 1u;
+            }
+            if (ok) {
+                if (DC) {
+                    if (pt == 0) sqd_part<0, DH>(qp, part, 0, 0, s);
+                    else sqd_part<DH, DC>(qp, part, 0, 0, s);
+                } else {
+                    sqd_part<0, 0>(qp, part, t0, t1, s);
+                }
+            } else {
+                // Fallback after a timed-out wait: the same sums from global memory.
+                for (int t = t0; t < t1; ++t) {
+                    const float d = __fsub_rn(qg[t], rg[t]);
+                    s = (t == 0) ? __fmul_rn(d, d) : __fadd_rn(s, __fmul_rn(d, d));
+                }
+            }
+        }
+        if (live && isfinite(s)) {
+            sd[h] = s;
+            jj[h] = j;
+        }
+    }
+    rerank_emit(sd, jj, cnt, k, lane, dist, idx64, sqdist, o);
 }
 
 // Rows whose candidate list overflowed, or whose cloud was flagged (listed
@@ -1059,9 +1166,11 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
                                          w.ubound, w.counts, w.cand, w.status, nst);
     st = check_launch("fknn_tc_kernel<2>");
     if (st) return st;
-    auto rk = !vec ? fknn_rerank_kernel<0, 0>
-                   : (D == 64 ? fknn_rerank_kernel<1, 64> : fknn_rerank_kernel<1, 0>);
-    const size_t stage = rerank_smem_bytes(D, vec);
+    // 16-byte rows: bulk copies of half rows (D = 64 compiled with the width
+    // fixed); otherwise 4-byte cp.async of whole rows.
+    auto rk = !vec ? fknn_rerank_kernel
+                   : (D == 64 ? fknn_rerank_bulk_kernel<64> : fknn_rerank_bulk_kernel<0>);
+    const size_t stage = vec ? rerank_bulk_smem_bytes(D) : rerank_smem_bytes(D);
     if (cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stage) !=
         cudaSuccess)
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");

@@ -94,6 +94,10 @@ def test_grid_ball_query_matches_scan(cuda_device, r, K):
     wd, wi = scan_bq(pts, q, r, K)
     assert torch.equal(i, wi)
     assert torch.equal(d, wd)
+    # and against the oracle on a slice (including the far queries)
+    od, oi = O.ball_query(q[:300].unsqueeze(0).cpu().numpy(), pts.unsqueeze(0).cpu().numpy(), r, K)
+    np.testing.assert_array_equal(i[:300].cpu().numpy(), oi[0])
+    np.testing.assert_array_equal(d[:300].cpu().numpy().view(np.int32), od[0].view(np.int32))
 
 
 def test_grid_ball_query_gradients_and_auto(cuda_device):
