@@ -966,7 +966,8 @@ def run_reference(args) -> dict:
             "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": sec * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic, seeded (same inputs as the b200 arm)", "impl": "reference",
-            "config": {"workload": "chamfer_config2_fwd_bwd", "global_batch": B_PER_GPU,
+            "config": {"workload": "chamfer_config2_fwd_bwd",
+                       "global_batch": B_PER_GPU * max(1, args.gpus),
                        "points_per_cloud": NPTS, "dims": D, "reduction": "mean/mean",
                        "parallelism": "host threads"},
             "cpu_baseline": {"value": value, "unit": "pairs/s", "cores": O.threads(),
