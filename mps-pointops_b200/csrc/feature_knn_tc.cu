@@ -263,34 +263,32 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
 // Thread per (padded row, 8-feature chunk): 2^lg consecutive lanes per row
 // (the chunk count Kpad / 8 rounded up to a power of two), so that a row's
 // lanes form one aligned group of a warp; the packed row is W = Kpad + 8
-// columns wide.  Rows [0, B * ntiles *
-// 128) are the references, then (unless `same`: the queries are the
-// references) the B * mtiles * 128 query rows.  Rows past n and features past
+// columns wide.  Grid (rows of one cloud, B, 2): z = 0 packs the references
+// (ntiles * 128 rows per cloud), z = 1 the queries (mtiles * 128 rows; not
+// launched when `same`: the queries are the references), y = the cloud, so
+// no thread divides by a run-time row count.  Rows past n and features past
 // D pack zeros.  Each lane sums the squares of its 8 features in order; a
 // butterfly over the row's lanes gives the norm (every lane the same sum,
 // fp32 addition being commutative); each lane packs its two 16-byte
 // core-matrix rows of features, and lane 0 also the norm block: tf32(-n / 2)
-// (references; -2^100 for padding rows) or zeros (queries).  vec: rows
-// are read as float4 (D % 4 == 0 and 16-byte aligned bases).  nq receives the
+// (references; -2^100 for padding rows) or zeros (queries).  vec: rows are
+// read as float4 (D % 4 == 0 and 16-byte aligned bases).  nq receives the
 // query norms; nmax = largest finite reference norm per cloud (one atomic per
 // warp), bad = a norm that is not finite or above kHuge.
 __global__ void fknn_prep_kernel(const float* __restrict__ q, const float* __restrict__ r,
-                                 int64_t B, int64_t M, int64_t N, int D, int W,
-                                 int64_t mtiles, int64_t ntiles, int vec, int same, int lg,
+                                 int64_t M, int64_t N, int D, int W, int64_t mtiles,
+                                 int64_t ntiles, int vec, int same, int lg,
                                  unsigned char* __restrict__ qpack,
                                  unsigned char* __restrict__ rpack, float* __restrict__ nq,
                                  unsigned* __restrict__ nmax, int* __restrict__ bad) {
     const int chunks = W / 8 - 1;  // feature chunks (the norm block follows)
-    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t prow_all = e >> lg;
-    const int c = (int)(e & ((1 << lg) - 1));
-    const int64_t rrows = B * ntiles * 128, qrows = same ? 0 : B * mtiles * 128;
-    const bool row_live = prow_all < rrows + qrows;
-    const bool is_ref = prow_all < rrows;
-    const int64_t prow = is_ref ? prow_all : prow_all - rrows;
+    const bool is_ref = blockIdx.z == 0;
+    const int64_t b = blockIdx.y;
     const int64_t tiles = is_ref ? ntiles : mtiles, n = is_ref ? N : M;
-    const int64_t b = prow / (tiles * 128);
-    const int64_t i = prow % (tiles * 128);
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t i = e >> lg;  // row within the cloud
+    const int c = (int)(e & ((1 << lg) - 1));
+    const bool row_live = i < tiles * 128;
     const bool point = row_live && i < n;
     float x[8];
 #pragma unroll
@@ -339,13 +337,17 @@ __global__ void fknn_prep_kernel(const float* __restrict__ q, const float* __res
         if (!is_ref || same) nq[b * M + i] = s;
         if (is_ref && ok) bits = __float_as_uint(s);
     }
-    const int64_t bb = is_ref ? b : -1;
-    const int64_t b0 = __shfl_sync(FULL_MASK, bb, 0);
-    if (__all_sync(FULL_MASK, bb == b0)) {
+    if (is_ref) {  // block-uniform: one cloud's references per block
+        // One atomic per block (same-address atomics serialise at L2).
+        __shared__ unsigned s_mx[8];
         const unsigned mx = __reduce_max_sync(FULL_MASK, bits);
-        if ((threadIdx.x & 31) == 0 && mx) atomicMax(&nmax[b0], mx);
-    } else if (bits) {
-        atomicMax(&nmax[bb], bits);
+        if ((threadIdx.x & 31) == 0) s_mx[threadIdx.x >> 5] = mx;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            const unsigned v = threadIdx.x < (blockDim.x >> 5) ? s_mx[threadIdx.x] : 0u;
+            const unsigned bm = __reduce_max_sync(FULL_MASK, v);
+            if (threadIdx.x == 0 && bm) atomicMax(&nmax[b], bm);
+        }
     }
 }
 
@@ -1139,12 +1141,12 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
     const int same = (query == ref && M == N) ? 1 : 0;
     int lg = 0;
     while ((1 << lg) < W / 8 - 1) ++lg;
-    const int64_t rows = B * nt * 128 + (same ? 0 : B * mt * 128);
+    const int64_t rows = max64(nt, same ? 0 : mt) * 128;  // per cloud, the longer operand
     // 16-byte row loads only when every row starts on a 16-byte boundary.
     const int vec = (D % 4 == 0 && aligned_to(query, 16) && aligned_to(ref, 16)) ? 1 : 0;
-    fknn_prep_kernel<<<(unsigned)ceil_div(rows << lg, 256), 256, 0, s>>>(
-        query, ref, B, M, N, D, W, mt, nt, vec, same, lg, w.qpack, w.rpack, w.nq, w.nmax,
-        w.bad);
+    const dim3 pgrid((unsigned)ceil_div(rows << lg, 256), (unsigned)B, same ? 1u : 2u);
+    fknn_prep_kernel<<<pgrid, 256, 0, s>>>(query, ref, M, N, D, W, mt, nt, vec, same, lg,
+                                           w.qpack, w.rpack, w.nq, w.nmax, w.bad);
     int st = check_launch("fknn_prep_kernel");
     if (st) return st;
     const unsigned char* qpack = same ? w.rpack : w.qpack;
