@@ -52,6 +52,15 @@ def test_dims_and_k(cuda_device, d, k):
     check(q, r, k, cuda_device)
 
 
+@pytest.mark.parametrize("d", [24, 64])
+def test_more_queries_than_references(cuda_device, d):
+    # The pack grid spans the longer operand: here the query tiles (24 of
+    # 128 rows) outnumber the reference tiles (17).
+    q = feats(3, 3000, d, seed=60 + d)
+    r = feats(3, 2100, d, seed=61 + d)
+    check(q, r, 20, cuda_device)
+
+
 @pytest.mark.parametrize("d", [16, 20, 33, 64, 96])
 def test_self_knn_one_pack(cuda_device, d):
     """knn(f, f, k) on ONE device tensor: the references' packed tiles and
