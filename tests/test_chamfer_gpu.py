@@ -205,6 +205,27 @@ def test_normals_and_empty(cuda_device):  # tests/test_chamfer.py:307-420
         chamfer_distance(x, x, weights=torch.tensor([-1.0], device=d))
 
 
+@pytest.mark.parametrize("where", ["x_last", "x_first", "y_mid", "both"])
+def test_nonfinite_check_float4_arrays(cuda_device, where):
+    # Both arrays a multiple of four floats and 16-byte aligned: the check's
+    # combined x/y scan (mps_pointops/chamfer.py:79-110 messages).
+    d = cuda_device
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(2, 40, 3, generator=g)
+    y = torch.randn(2, 28, 3, generator=g)
+    if where in ("x_last", "both"):
+        x[1, 39, 2] = float("nan")
+    if where == "x_first":
+        x[0, 0, 0] = float("inf")
+    if where in ("y_mid", "both"):
+        y[1, 5, 1] = -float("inf")
+    msg = "valid y coordinates" if where == "y_mid" else "valid x coordinates"
+    with pytest.raises(ValueError, match=msg):
+        chamfer_distance(x.to(d), y.to(d))
+    # the clean pair passes
+    chamfer_distance(torch.randn(2, 40, 3, generator=g).to(d), torch.randn(2, 28, 3, generator=g).to(d))
+
+
 @pytest.mark.parametrize("dimension", [1, 2, 4, 64, 128])
 def test_first_index_tie_any_dimension(cuda_device, dimension):  # tests/test_chamfer_nd.py:50-73
     x = torch.zeros((1, 1, dimension), device=cuda_device, requires_grad=True)
