@@ -52,6 +52,16 @@ def test_dims_and_k(cuda_device, d, k):
     check(q, r, k, cuda_device)
 
 
+@pytest.mark.parametrize("m", [1, 129])
+def test_one_query_and_one_tile_plus_one(cuda_device, m):
+    # A single query (one mostly-padding 128-row tile) and one query past a
+    # whole tile, against exactly 2048 references (the smallest tensor-path
+    # cloud, 16 full reference tiles).
+    q = feats(2, m, 32, seed=70 + m)
+    r = feats(2, 2048, 32, seed=71 + m)
+    check(q, r, 7, cuda_device)
+
+
 @pytest.mark.parametrize("d", [24, 64])
 def test_more_queries_than_references(cuda_device, d):
     # The pack grid spans the longer operand: here the query tiles (24 of
