@@ -716,13 +716,17 @@ inline size_t rerank_smem_bytes(int D) {
 // first half rounded to whole float4s; the sequential SD runs on across the
 // parts.  A staged part's stride is an odd number of float4s (conflict-free
 // lane-per-row float4 reads).
-__host__ __device__ constexpr int bulk_half(int D) { return ((D / 4 + 1) / 2) * 4; }
-__host__ __device__ constexpr int bulk_stride(int D) { return 4 * ((bulk_half(D) / 4) | 1); }
+__host__ __device__ constexpr int half_split(int D) { return ((D / 4 + 1) / 2) * 4; }
+__host__ __device__ constexpr int half_stride(int D) { return 4 * ((half_split(D) / 4) | 1); }
 // Per warp: the query row (D floats) and 32 staged parts.
-inline size_t rerank_bulk_smem_bytes(int D) {
-    return (size_t)kRerankWarps * (D + 32 * bulk_stride(D)) * sizeof(float);
+inline size_t rerank_half_smem_bytes(int D) {
+    return (size_t)kRerankWarps * (D + 32 * half_stride(D)) * sizeof(float);
 }
 
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async4(float* dst, const float* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
                  : "memory");
@@ -912,18 +916,14 @@ __device__ __forceinline__ void sqd_part(const float* __restrict__ qa,
     }
 }
 
-// 16-byte rows.  Lane l copies candidate l's row part with one cp.async.bulk
-// (completion on the warp's mbarrier; lane 0 also copies the query row and
-// posts the expected bytes), so a part of 32 rows costs one copy instruction
-// per lane.  Two parts per 32 candidates; each warp's barrier serves one
-// query, its phase flips per part.  The previous part's shared-memory reads
-// are ordered before the next bulk writes by fence.proxy.async.  Every wait
-// is bounded (kWaitNs); after a timeout the warp waits once more for its
-// copies in flight and computes the rest from global memory.  Grid
-// (ceil(M / warps), B).
+// 16-byte rows.  Candidates' rows are staged in two half-row parts (so a
+// warp needs 4.9 KB of shared memory at D = 64, 40 warps per SM), each copied
+// with coalesced 16-byte cp.async: 8 lanes per row, four rows per copy
+// instruction; the warp waits for its own copies with cp.async.wait_all.
+// The sequential SD runs on across the parts.  Grid (ceil(M / warps), B).
 template <int DC>
 __global__ void __launch_bounds__(kRerankWarps * 32)
-fknn_rerank_bulk_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t M,
+fknn_rerank_half_kernel(const float* __restrict__ q, const float* __restrict__ r, int64_t M,
                         int64_t N, int D_rt, int k, const int* __restrict__ bad,
                         const unsigned* __restrict__ counts, const uint2* __restrict__ cand,
                         float* __restrict__ dist, int64_t* __restrict__ idx64,
@@ -932,11 +932,10 @@ fknn_rerank_bulk_kernel(const float* __restrict__ q, const float* __restrict__ r
     static_assert(kCap == 64, "two candidates per lane");
     static_assert(DC % 4 == 0, "16-byte rows");
     extern __shared__ __align__(16) float s_stage[];  // [warps][D + 32 * stride]
-    __shared__ __align__(8) unsigned long long s_bar[kRerankWarps];
     const int D = DC ? DC : D_rt;
-    constexpr int DH = DC ? bulk_half(DC) : 0;
-    const int Dh = DC ? DH : bulk_half(D);
-    const int hs = bulk_stride(D);
+    constexpr int DH = DC ? half_split(DC) : 0;
+    const int Dh = DC ? DH : half_split(D);
+    const int hs = half_stride(D);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t m = (int64_t)blockIdx.x * kRerankWarps + warp;
     if (m >= M) return;  // warp-uniform
@@ -945,7 +944,8 @@ fknn_rerank_bulk_kernel(const float* __restrict__ q, const float* __restrict__ r
     const float* rb = r + b * N * D;
     const float* qg = q + row * D;
     float* qp = s_stage + warp * (D + 32 * hs);
-    float* part = qp + D + lane * hs;  // this lane's staged row part
+    float* rows = qp + D;
+    float* part = rows + lane * hs;  // this lane's staged row part
     const unsigned packed = bad[b] ? 0xffffffffu : counts[row];
     const int64_t o = row * k;
     if (packed == 0xffffffffu) {  // exact scan by fknn_exact_rows_kernel
@@ -953,14 +953,8 @@ fknn_rerank_bulk_kernel(const float* __restrict__ q, const float* __restrict__ r
         return;
     }
     const unsigned f0 = packed & 0xffffu, f1 = packed >> 16, cnt = f0 + f1;
-    const uint32_t bar = smem_u32(&s_bar[warp]);
-    if (lane == 0) {
-        mbar_init(bar, 1);
-        mbar_fence_init();
-    }
-    __syncwarp();
-    uint32_t phase = 0;
-    bool ok = true;
+    for (int t = 4 * lane; t < D; t += 128) cp_async16(qp + t, qg + t);
+    const int roff = lane >> 3, u0 = lane & 7;  // 8 lanes per row, 4 rows per instruction
     float sd[2];
     uint32_t jj[2];
 #pragma unroll
@@ -969,6 +963,7 @@ fknn_rerank_bulk_kernel(const float* __restrict__ q, const float* __restrict__ r
         jj[h] = kNoIndex;
         const unsigned c0 = 32u * (unsigned)h;
         if (c0 >= cnt) continue;  // warp-uniform
+        const unsigned n = min(32u, cnt - c0);
         const unsigned c = c0 + (unsigned)lane;
         uint32_t j = kNoIndex;
         if (c < cnt) {
@@ -976,43 +971,29 @@ fknn_rerank_bulk_kernel(const float* __restrict__ q, const float* __restrict__ r
             j = cand[row * kCap + slot].x;
         }
         const bool live = c < cnt && j < (uint32_t)N;
-        const unsigned nlive = (unsigned)__popc(__ballot_sync(FULL_MASK, live));
-        const float* rg = rb + (int64_t)(live ? j : 0u) * D;
         float s = 0.f;
 #pragma unroll
         for (int pt = 0; pt < 2; ++pt) {
             const int t0 = pt ? Dh : 0, t1 = pt ? D : Dh;
-            if (ok) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                const bool first = h == 0 && pt == 0;
-                if (lane == 0)
-                    bulk_expect(bar, nlive * (uint32_t)(t1 - t0) * 4u + (first ? (uint32_t)D * 4u : 0u));
-                __syncwarp();
-                if (first && lane == 0) bulk_copy(smem_u32(qp), qg, (uint32_t)D * 4u, bar);
-                if (live) bulk_copy(smem_u32(part), rg + t0, (uint32_t)(t1 - t0) * 4u, bar);
-                bool got = mbar_wait(bar, phase);
-                if (!__all_sync(FULL_MASK, got)) {
-                    // Copies still in flight land before the warp goes on.
-                    got = mbar_wait(bar, phase);
-                    ok = false;
+            const int U = (t1 - t0) / 4;  // float4 per part-row
+            for (unsigned base = 0; base < n; base += 4u) {
+                const unsigned rl = base + (unsigned)roff;
+                const uint32_t jr = __shfl_sync(FULL_MASK, j, (int)(rl & 31u));
+                if (rl < n && jr < (uint32_t)N) {
+                    const float* src = rb + (int64_t)jr * D + t0;
+                    float* dst = rows + rl * hs;
+                    for (int u = u0; u < U; u += 8) cp_async16(dst + 4 * u, src + 4 * u);
                 }
-                phase ^= 1u;
             }
-            if (ok) {
-                if (DC) {
-                    if (pt == 0) sqd_part<0, DH>(qp, part, 0, 0, s);
-                    else sqd_part<DH, DC>(qp, part, 0, 0, s);
-                } else {
-                    sqd_part<0, 0>(qp, part, t0, t1, s);
-                }
+            cp_async_wait_all();
+            __syncwarp();
+            if (DC) {
+                if (pt == 0) sqd_part<0, DH>(qp, part, 0, 0, s);
+                else sqd_part<DH, DC>(qp, part, 0, 0, s);
             } else {
-                // Fallback after a timed-out wait: the same sums from global memory.
-                for (int t = t0; t < t1; ++t) {
-                    const float d = __fsub_rn(qg[t], rg[t]);
-                    s = (t == 0) ? __fmul_rn(d, d) : __fadd_rn(s, __fmul_rn(d, d));
-                }
+                sqd_part<0, 0>(qp, part, t0, t1, s);
             }
+            __syncwarp();  // the part is refilled next
         }
         if (live && isfinite(s)) {
             sd[h] = s;
@@ -1168,11 +1149,11 @@ int run_tc(const float* query, const float* ref, int64_t B, int64_t M, int64_t N
                                          w.ubound, w.counts, w.cand, w.status, nst);
     st = check_launch("fknn_tc_kernel<2>");
     if (st) return st;
-    // 16-byte rows: bulk copies of half rows (D = 64 compiled with the width
-    // fixed); otherwise 4-byte cp.async of whole rows.
+    // 16-byte rows: half-row parts by 16-byte cp.async (D = 64 compiled with
+    // the width fixed); otherwise 4-byte cp.async of whole rows.
     auto rk = !vec ? fknn_rerank_kernel
-                   : (D == 64 ? fknn_rerank_bulk_kernel<64> : fknn_rerank_bulk_kernel<0>);
-    const size_t stage = vec ? rerank_bulk_smem_bytes(D) : rerank_smem_bytes(D);
+                   : (D == 64 ? fknn_rerank_half_kernel<64> : fknn_rerank_half_kernel<0>);
+    const size_t stage = vec ? rerank_half_smem_bytes(D) : rerank_smem_bytes(D);
     if (cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stage) !=
         cudaSuccess)
         return fail(kCudaError, "knn: cannot raise the shared-memory limit");
