@@ -41,9 +41,11 @@
 //     The k nearest by exact SD are all candidates: F_k <= n(q) + U + eps
 //     (k columns have SD' <= n(q) + U), and a needed column has
 //     SD' <= F_k + eps.
-//  3. Exact re-rank (fknn_rerank_kernel): exact fp32 SD of every candidate,
+//  3. Exact re-rank (fknn_rerank_half_kernel for 16-byte rows,
+//     fknn_rerank_kernel otherwise): exact fp32 SD of every candidate,
 //     ranked by (SD, index).  A query whose list overflowed, or whose cloud
-//     was flagged, is scanned exactly over all references instead.
+//     was flagged, is scanned exactly over all references instead
+//     (fknn_exact_rows_kernel).
 //
 // Error bound C_K (per unit of n(q) + n(r), K = Kpad): rounding to tf32
 // moves each coordinate by at most u|p| with u = 2^-11, so a product
@@ -662,13 +664,13 @@ fknn_tc_kernel(const unsigned char* __restrict__ qpack, const unsigned char* __r
 
 // ---- 3. exact re-rank --------------------------------------------------------
 // Warp per query.  Normal case: the warp copies its candidates' reference rows
-// into shared memory (coalesced row copies with cp.async; a lane per row would
-// touch one cache line per lane and load), lane l computes the exact
-// sequential-fp32 SD of candidates l and l + 32 from there (non-finite SD are
-// dropped), and a warp bitonic sort of the (SD, index) keys gives the first k.
-// Overflowed lists and flagged clouds: the
-// lanes scan every reference (j = lane mod 32) into per-lane sorted lists,
-// merged by k rounds of warp minimum.
+// (whole, or in two halves for 16-byte rows) into shared memory with
+// coalesced cp.async (a lane per row would touch one cache line per lane and
+// load), lane l computes the exact sequential-fp32 SD of candidates l and
+// l + 32 from there (non-finite SD are dropped), and a warp bitonic sort of
+// the (SD, index) keys gives the first k.  Overflowed lists and flagged
+// clouds: the lanes scan every reference (j = lane mod 32) into per-lane
+// sorted lists, merged by k rounds of warp minimum.
 
 // Exact sequential SD of query row qs (shared memory) and reference row rp
 // (global memory), reading the reference 32 features at a time (8 float4
