@@ -73,6 +73,9 @@ def parse_args():
                          "for the per-kernel profiles)")
     ap.add_argument("--queries", type=int, default=131072,
                     help="config 5: queries per GPU (1M queries / 8 GPUs)")
+    ap.add_argument("--loss-reducer", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: all-reduce of the Chamfer loss partials through the library's "
+                         "peer-memory kernel (default) or NCCL")
     return ap.parse_args()
 
 
@@ -163,15 +166,17 @@ def barrier(world: int):
 
 
 # ------------------------------------------------------------------ B200 arm
-def chamfer_step(x, y, world, group_batch):
+def chamfer_step(x, y, world, group_batch, reducer=None):
     from mps_pointops.chamfer import chamfer_distance
     from mps_pointops.dist import chamfer_distance_sharded
     xr = x.detach().requires_grad_()
     yr = y.detach().requires_grad_()
     if world > 1:
-        # The loss all-reduce runs on NCCL's stream during the backward; the
-        # step ends once its global loss is in (the stream waits on it).
-        local, pending = chamfer_distance_sharded(xr, yr, group_batch, overlap=True)
+        # The loss all-reduce (peer-memory kernel, or NCCL without a reducer)
+        # runs on a side stream during the backward; the step ends once its
+        # global loss is in (the compute stream waits on it).
+        local, pending = chamfer_distance_sharded(xr, yr, group_batch, overlap=True,
+                                                  reducer=reducer)
         local.backward()
         return pending.value()
     loss, _ = chamfer_distance(xr, yr)
@@ -308,22 +313,39 @@ def config5_secondary(steps: int, warmup: int, world: int, rank: int) -> dict:
                                      if world > 1 else "none"}}
 
 
-def loss_all_reduce_us(world: int, reps: int = 50) -> float | None:
-    """Latency of the Chamfer step's collective alone: a 4-byte all_reduce
-    (CUDA events on NCCL's completion, mean, max over ranks)."""
+def loss_all_reduce_us(world: int, reducer=None, reps: int = 50) -> float | None:
+    """Latency of the Chamfer step's collective alone: a 4-byte all-reduce
+    through NCCL, or through ``reducer`` (the peer-memory kernel), ``reps``
+    times back to back.  A ~2.5 ms spin kernel goes first so that the host
+    has enqueued every reduction before the first runs: the time is the
+    device's, not the Python launch rate's.  CUDA events, mean, max over
+    ranks."""
     if world == 1:
         return None
     import torch.distributed as dist
     t = torch.ones(1, device="cuda")
+
+    def one():
+        if reducer is None:
+            dist.all_reduce(t)
+            return None
+        return reducer.reduce(t)
+
     for _ in range(5):
-        dist.all_reduce(t)
+        p = one()
+        if p is not None:
+            p.value()
     torch.cuda.synchronize()
     barrier(world)
     s = torch.cuda.current_stream()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(5_000_000)
     a.record(s)
+    last = None
     for _ in range(reps):
-        dist.all_reduce(t)
+        last = one()
+    if last is not None:
+        last.value()
     b.record(s)
     torch.cuda.synchronize()
     return max_over_ranks(a.elapsed_time(b) * 1e3 / reps, world)
@@ -751,7 +773,7 @@ def cpu_baseline_sample(max_seconds: float = 15.0) -> dict:
                       f"{sec:.1f} s"}
 
 
-def e2e_chamfer(xh, yh, dev, world, group_batch, steps):
+def e2e_chamfer(xh, yh, dev, world, group_batch, steps, reducer=None):
     """End-to-end Chamfer steps through the public API from pinned host inputs.
 
     Pipelined (the first number): step i+1's inputs are copied host->device
@@ -782,7 +804,7 @@ def e2e_chamfer(xh, yh, dev, world, group_batch, steps):
     def run_step(i):
         k = i % 2
         comp.wait_event(copied[k])
-        loss = chamfer_step(bufs[k][0], bufs[k][1], world, group_batch)
+        loss = chamfer_step(bufs[k][0], bufs[k][1], world, group_batch, reducer)
         consumed[k].record(comp)
         host_loss[i].copy_(loss.detach(), non_blocking=True)
         ready[i].record(comp)
@@ -816,7 +838,7 @@ def e2e_chamfer(xh, yh, dev, world, group_batch, steps):
     def sequential_step():
         xd = xh.to(dev, non_blocking=True)
         yd = yh.to(dev, non_blocking=True)
-        return float(chamfer_step(xd, yd, world, group_batch).item())
+        return float(chamfer_step(xd, yd, world, group_batch, reducer).item())
 
     sequential_step()
     barrier(world)
@@ -841,9 +863,22 @@ def run_b200(args, world, rank, local):
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     props = torch.cuda.get_device_properties(dev)
     bus = {str(getattr(props, "pci_bus_id", "")).lower()[-12:]}
+    reducer = None
+    if world > 1 and args.loss_reducer == "peer":
+        from mps_pointops.dist import PeerLossReducer
+        reducer = PeerLossReducer()
+    out = _run_b200_steps(args, world, rank, dev, props, bus, x, y, x_cpu, y_cpu, flush,
+                          group_batch, reducer)
+    if reducer is not None:
+        reducer.close()      # collective: every rank got here without an error
+    return out
 
+
+def _run_b200_steps(args, world, rank, dev, props, bus, x, y, x_cpu, y_cpu, flush, group_batch,
+                    reducer):
+    from mps_pointops import _native as N
     for _ in range(max(args.warmup, 3)):
-        chamfer_step(x, y, world, group_batch)
+        chamfer_step(x, y, world, group_batch, reducer)
     torch.cuda.synchronize()
     barrier(world)
     clocks = ClockSampler()
@@ -852,7 +887,8 @@ def run_b200(args, world, rank, local):
     launches0 = N.launch_count()
     clocks.mark(True)
     with N.KernelTimer("chamfer_nearest") as ktimer:
-        step_ms = timed_steps(lambda: chamfer_step(x, y, world, group_batch), args.steps, flush)
+        step_ms = timed_steps(lambda: chamfer_step(x, y, world, group_batch, reducer), args.steps,
+                              flush)
     clocks.mark(False)
     launches = N.launch_count() - launches0
     barrier(world)
@@ -864,7 +900,7 @@ def run_b200(args, world, rank, local):
 
     # e2e: public API with pinned host inputs, H2D every step, loss read back.
     xh, yh = x_cpu.pin_memory(), y_cpu.pin_memory()
-    e2e_ms, e2e_seq_ms = e2e_chamfer(xh, yh, dev, world, group_batch, args.steps)
+    e2e_ms, e2e_seq_ms = e2e_chamfer(xh, yh, dev, world, group_batch, args.steps, reducer)
 
     secondary = None if args.no_secondary else ssg_secondary(args.steps, args.warmup, world, rank)
     fknn = None if args.no_secondary else feature_knn_secondary(args.steps, max(args.warmup, 3),
@@ -872,7 +908,10 @@ def run_b200(args, world, rank, local):
     strong = None if args.no_secondary else ssg_strong_secondary(min(args.steps, 20),
                                                                  max(args.warmup, 3), world, rank)
     c5 = None if args.no_secondary else config5_secondary(min(args.steps, 3), 1, world, rank)
-    ar_us = loss_all_reduce_us(world)
+    ar_us = loss_all_reduce_us(world, reducer)
+    nccl_us = loss_all_reduce_us(world) if reducer is not None else ar_us
+    if reducer is not None:
+        reducer.check()
 
     # Roofline of the dominant kernel: the nearest search (8 separately rounded
     # flops per unique pair) against the FP32 pipe: 128 rounded fp32 ops per
@@ -936,9 +975,13 @@ def run_b200(args, world, rank, local):
     if ar_us is not None:
         out["collectives"] = {
             "chamfer_loss_all_reduce_us": ar_us,
-            "note": "the Chamfer step's only collective (4-byte all_reduce of the loss "
-                    "partials) runs asynchronously during the backward; this is its latency "
-                    "alone (mean of 50, max over ranks)"}
+            "loss_reducer": "peer-memory kernel (mpo_allreduce_sum_f32_p2p)" if reducer
+                            is not None else "NCCL all_reduce",
+            "nccl_all_reduce_us": nccl_us,
+            "note": "the Chamfer step's only collective (4-byte all-reduce of the loss "
+                    "partials) runs on a side stream during the backward; these are latencies "
+                    "alone (mean of 50 back to back, enqueued behind a spin kernel so that the "
+                    "host launch rate does not bound them; max over ranks)"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline_sample()
     return out

@@ -9,7 +9,9 @@
  *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call
  *     only enqueues work and returns; results are ready when the stream is.
  *   - Outputs and workspaces are owned by the caller.  Every output slot is
- *     written, padding included.  Nothing is allocated inside the library.
+ *     written, padding included.  Nothing is allocated inside the library,
+ *     except the exchange arrays of mpo_p2p_slots_create (device memory
+ *     that other processes map through CUDA IPC).
  *     Workspaces must be 256-byte aligned (as cudaMalloc returns them;
  *     MPO_ERR_INVALID_ARGUMENT otherwise).  Float arrays need only 4-byte
  *     alignment: kernels use 16-byte vector loads on a caller's array only
@@ -42,7 +44,7 @@ extern "C" {
 #define MPO_API
 #endif
 
-#define MPO_ABI_VERSION 8
+#define MPO_ABI_VERSION 9
 
 #define MPO_OK 0
 #define MPO_ERR_INVALID_ARGUMENT 1
@@ -489,6 +491,45 @@ MPO_API int mpo_flat_interpolate(const float* feat, int64_t N, int64_t C, const 
 MPO_API int mpo_flat_interpolate_backward(const float* grad_out, const int32_t* idx,
                                           const float* dist, int64_t M, int64_t k, int64_t N,
                                           int64_t C, float* grad_feat, void* stream);
+
+/* ------------------------------------------------------------------ ranks
+ * All-reduce (sum) of one float per rank over peer memory, for the loss of a
+ * batch of Chamfer clouds split across the GPUs of one node (the reference is
+ * single-device; this replaces the 4-byte NCCL all_reduce that would follow
+ * its chamfer_distance, mps_pointops/chamfer.py:342-488, in a data-parallel
+ * step).  Each rank creates one exchange array (mpo_p2p_slots_bytes() bytes
+ * of device memory, zeroed) with mpo_p2p_slots_create, which also returns
+ * its CUDA IPC handle (MPO_P2P_IPC_HANDLE_BYTES bytes); the ranks exchange the
+ * handles (e.g. torch.distributed.all_gather_object) and map every other
+ * rank's array with mpo_p2p_slots_open.
+ *
+ * mpo_allreduce_sum_f32_p2p: slots[r] = rank r's array as mapped in this
+ * process (slots[rank] = the array this rank created), 1 <= world <=
+ * MPO_P2P_MAX_RANKS.  Every rank makes the same sequence of calls with the
+ * same seq (a counter that starts at 1, advances by one per call and skips
+ * 0 when it wraps); each stores fl(value[0] * scale) into every rank's array
+ * and waits until all W values have arrived in its own; out[0] = the W
+ * values summed in rank order, each addition rounded -- the same bits on
+ * every rank.  The wait is bounded: after timeout_ns without some rank's
+ * value, out[0] = NaN and *status = 1 + the lowest missing rank (the caller
+ * zeroes *status once; it is never cleared by the kernel).  One 32-thread
+ * launch; calls on different ranks wait on one another, so each rank's call
+ * must run on its own GPU.
+ *
+ * Teardown: once no call is in flight on any rank (synchronize, then a
+ * barrier), close the mappings (mpo_p2p_slots_close), barrier again, then
+ * free the own array (mpo_p2p_slots_destroy). */
+#define MPO_P2P_MAX_RANKS 32
+#define MPO_P2P_IPC_HANDLE_BYTES 64
+MPO_API size_t mpo_p2p_slots_bytes(void);
+MPO_API int mpo_p2p_slots_create(void** slots, void* ipc_handle);
+MPO_API int mpo_p2p_slots_open(const void* ipc_handle, void** peer_slots);
+MPO_API int mpo_p2p_slots_close(void* peer_slots);
+MPO_API int mpo_p2p_slots_destroy(void* slots);
+MPO_API int mpo_allreduce_sum_f32_p2p(const float* value, float scale, float* out,
+                                      void* const* slots, int64_t world, int64_t rank,
+                                      uint32_t seq, int64_t timeout_ns, int32_t* status,
+                                      void* stream);
 
 #ifdef __cplusplus
 }

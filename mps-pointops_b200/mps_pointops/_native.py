@@ -20,7 +20,7 @@ from pathlib import Path
 import torch
 
 LIB_NAME = "libmpo_b200.so"
-ABI_VERSION = 8
+ABI_VERSION = 9
 _lib = None
 _lock = threading.Lock()
 _checked_devices: set[int] = set()
@@ -101,6 +101,13 @@ SIGNATURES = {
     "mpo_flat_fps_workspace_bytes": (_sz, [_i64, _i64]),
     "mpo_flat_fps": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _sz,
                             _vp]),
+    "mpo_p2p_slots_bytes": (_sz, []),
+    "mpo_p2p_slots_create": (_int, [_vp, _vp]),
+    "mpo_p2p_slots_open": (_int, [_vp, _vp]),
+    "mpo_p2p_slots_close": (_int, [_vp]),
+    "mpo_p2p_slots_destroy": (_int, [_vp]),
+    "mpo_allreduce_sum_f32_p2p": (_int, [_vp, _f32, _vp, _vp, _i64, _i64, ctypes.c_uint32, _i64,
+                                         _vp, _vp]),
 }
 
 

@@ -13,12 +13,17 @@ rank runs the single-GPU kernels on its shard.  The only cross-rank traffic is
   gradient exchange is needed.
 
 Both go through NCCL over NVLink on GPUs and work with ``gloo`` on the CPU.
+For the 4-byte loss all-reduce of a data-parallel step, ``PeerLossReducer``
+replaces NCCL with the library's own kernel over peer memory (one NVLink
+store per rank pair and a bounded poll), which has a fraction of the
+latency of a collective launch.
 The functions take the local op as a parameter (``local_fn``) so the
 partitioning logic can be exercised without a GPU.
 """
 
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
@@ -71,9 +76,111 @@ class PendingLoss:
         return self._total
 
 
+class _StreamWork:
+    """The wait handle of a reduction enqueued on a side stream: waiting makes
+    the caller's current stream wait for it (the host does not block)."""
+
+    def __init__(self, stream: torch.cuda.Stream):
+        self._stream = stream
+
+    def wait(self):
+        torch.cuda.current_stream(self._stream.device).wait_stream(self._stream)
+
+
+class PeerLossReducer:
+    """All-reduce (sum) of one float per rank through the ranks' peer memory,
+    for the global loss of a data-parallel Chamfer step on the GPUs of one
+    node (``mpo_allreduce_sum_f32_p2p``).
+
+    Construction is collective: every rank of ``group`` creates its exchange
+    array, the CUDA IPC handles are all-gathered, and each rank maps the
+    others' arrays.  :meth:`reduce` enqueues one 32-thread kernel on a side
+    stream that stores this rank's value into every rank's array over NVLink
+    and waits (bounded by ``timeout_s``) for all of theirs; the result is the
+    values summed in rank order, the same bits on every rank.  Every rank must
+    call :meth:`reduce` the same number of times, in the same order.
+    :meth:`check` raises if a wait ran out; :meth:`close` (collective) frees
+    the mappings.
+    """
+
+    def __init__(self, group=None, timeout_s: float = 10.0):
+        from . import _native as N
+        self._N = N
+        self._lib = N.lib()
+        self.rank, self.world = _world(group)
+        self._group = group
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        limit = 32
+        if self.world > limit:
+            raise ValueError(f"PeerLossReducer: at most {limit} ranks, got {self.world}")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        N.check(self._lib.mpo_p2p_slots_create(ctypes.byref(own), handle), "mpo_p2p_slots_create")
+        self._own = own.value
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._mapped: list[int] = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            buf = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+            N.check(self._lib.mpo_p2p_slots_open(buf, ctypes.byref(p)), "mpo_p2p_slots_open")
+            self._mapped.append(p.value)
+            ptrs.append(p.value)
+        self._slots = (ctypes.c_void_p * self.world)(*ptrs)
+        self._seq = 0
+        self._timeout_ns = int(timeout_s * 1e9)
+        self._status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._stream = torch.cuda.Stream(self.device)
+
+    def reduce(self, value: torch.Tensor, scale: float = 1.0) -> "PendingLoss":
+        """Sum of fl(value[0] * scale) over the ranks (float32, one element),
+        as a :class:`PendingLoss`."""
+        if value.dtype != torch.float32 or value.numel() != 1 or value.device != self.device:
+            raise ValueError("PeerLossReducer.reduce: value must be one float32 element on "
+                             f"{self.device}")
+        if self._slots is None:
+            raise RuntimeError("PeerLossReducer: closed")
+        value = value.detach().contiguous()
+        self._seq = self._seq % 0xFFFFFFFF + 1
+        out = torch.empty(1, dtype=torch.float32, device=self.device)
+        self._stream.wait_stream(torch.cuda.current_stream(self.device))
+        self._N.check(self._lib.mpo_allreduce_sum_f32_p2p(
+            self._N.ptr(value), ctypes.c_float(scale), self._N.ptr(out), self._slots, self.world,
+            self.rank, self._seq, self._timeout_ns, self._N.ptr(self._status),
+            ctypes.c_void_p(self._stream.cuda_stream)), "mpo_allreduce_sum_f32_p2p")
+        value.record_stream(self._stream)
+        out.record_stream(self._stream)
+        return PendingLoss(out.view(()), _StreamWork(self._stream))
+
+    def check(self) -> None:
+        """Raise if any reduction so far gave up waiting (synchronises)."""
+        st = int(self._status.item())
+        if st:
+            raise RuntimeError(f"PeerLossReducer: no value from rank {st - 1} within "
+                               f"{self._timeout_ns / 1e9:g} s (loss reported as NaN)")
+
+    def close(self) -> None:
+        """Collective: unmap the other ranks' arrays and free this rank's."""
+        if self._slots is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self._group)
+        for p in self._mapped:
+            self._N.check(self._lib.mpo_p2p_slots_close(ctypes.c_void_p(p)), "mpo_p2p_slots_close")
+        self._mapped = []
+        dist.barrier(group=self._group)
+        self._N.check(self._lib.mpo_p2p_slots_destroy(ctypes.c_void_p(self._own)),
+                      "mpo_p2p_slots_destroy")
+        self._slots = None
+
+
 def chamfer_distance_sharded(x_local: torch.Tensor, y_local: torch.Tensor, batch_total: int,
                              group=None, local_fn: Callable | None = None,
-                             overlap: bool = False):
+                             overlap: bool = False, reducer: PeerLossReducer | None = None):
     """Mean/mean squared-L2 Chamfer loss over a batch split across ranks.
 
     ``x_local`` / ``y_local`` hold this rank's clouds (its :func:`shard_range`
@@ -85,12 +192,16 @@ def chamfer_distance_sharded(x_local: torch.Tensor, y_local: torch.Tensor, batch
     rank's term (1/B) * sum of its per-cloud losses, whose backward gives the
     same gradients, and ``pending`` (:class:`PendingLoss`) the global loss,
     all-reduced asynchronously -- the collective then never stalls the
-    compute stream between forward and backward.
+    compute stream between forward and backward.  ``reducer`` (with
+    ``overlap``) sums the partials with a :class:`PeerLossReducer` instead of
+    NCCL.
     """
     if local_fn is None:
         from .chamfer import chamfer_distance as local_fn
     partial, _ = local_fn(x_local, y_local, batch_reduction="sum")
     scale = 1.0 / max(batch_total, 1)
+    if overlap and reducer is not None:
+        return partial * scale, reducer.reduce(partial, scale)
     if overlap:
         local = partial * scale
         total = local.detach().clone()

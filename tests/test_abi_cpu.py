@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_error_channel():
     lib = N.lib()
-    assert lib.mpo_abi_version() == N.ABI_VERSION == 8
+    assert lib.mpo_abi_version() == N.ABI_VERSION == 9
     # Argument validation happens before any CUDA call, so it runs without a GPU.
     st = lib.mpo_knn(None, None, 1, 1, 1000, 3, 300, None, None, None, None, 0, None)
     assert st == 1
@@ -71,3 +71,22 @@ def test_no_oracle_in_product_package():
         assert "oracle" not in text.replace("# ", ""), path
     for path in (pkg / "csrc").glob("*"):
         assert "oracle" not in path.read_text(), path
+
+
+def test_peer_allreduce_validates_before_device_work():
+    lib = N.lib()
+    fake = ctypes.c_void_p(0x1000)
+    slots = (ctypes.c_void_p * 2)(0x2000, 0x3000)
+    st = lib.mpo_allreduce_sum_f32_p2p(fake, 1.0, fake, slots, 2, 0, 0, 10, fake, None)
+    assert st == 1 and "seq must not be 0" in N.last_error()
+    st = lib.mpo_allreduce_sum_f32_p2p(fake, 1.0, fake, slots, 33, 0, 1, 10, fake, None)
+    assert st == 1 and "world must be in [1, 32]" in N.last_error()
+    st = lib.mpo_allreduce_sum_f32_p2p(fake, 1.0, fake, slots, 2, 2, 1, 10, fake, None)
+    assert st == 1 and "rank must be in [0, world)" in N.last_error()
+    st = lib.mpo_allreduce_sum_f32_p2p(fake, 1.0, fake, slots, 2, 0, 1, 0, fake, None)
+    assert st == 1 and "timeout_ns" in N.last_error()
+    bad = (ctypes.c_void_p * 2)(0x2000, 0x3004)
+    st = lib.mpo_allreduce_sum_f32_p2p(fake, 1.0, fake, bad, 2, 0, 1, 10, fake, None)
+    assert st == 1 and "slots[1]" in N.last_error()
+    st = lib.mpo_allreduce_sum_f32_p2p(fake, 1.0, None, slots, 2, 0, 1, 10, fake, None)
+    assert st == 1 and "must not be NULL" in N.last_error()

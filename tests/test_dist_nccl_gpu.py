@@ -4,6 +4,9 @@ Two ranks, one per GPU: the Chamfer loss of a batch split across the ranks
 (one all-reduce of the loss partials) and its gradients must equal the
 single-GPU result, and the sharded kNN / ball query with a replicated
 reference cloud (all-gather of the outputs) must equal the single-GPU call.
+The same loss through the peer-memory all-reduce kernel (PeerLossReducer,
+CUDA IPC mappings of each rank's exchange array) must carry the same bits on
+both ranks, step after step.
 """
 
 from __future__ import annotations
@@ -39,7 +42,7 @@ def _worker(rank, world, port, results):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(root, "mps-pointops_b200"))
     import torch.distributed as dist
-    from mps_pointops.dist import (all_gather_shards, ball_query_sharded,
+    from mps_pointops.dist import (PeerLossReducer, all_gather_shards, ball_query_sharded,
                                    chamfer_distance_sharded, knn_query_sharded, shard_range)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -58,8 +61,20 @@ def _worker(rank, world, port, results):
         d, i = knn_query_sharded(q.to(dev), r.to(dev), 16)
         bd, bi = ball_query_sharded(q.to(dev), r.to(dev), 0.3, 32)
         torch.cuda.synchronize()
+        red = PeerLossReducer(timeout_s=20.0)
+        peer = []
+        for step in range(4):
+            xo = x[lo:hi].to(dev).requires_grad_()
+            yo = (y[lo:hi] * (1.0 + 0.01 * step)).to(dev).requires_grad_()
+            local, pending = chamfer_distance_sharded(xo, yo, x.shape[0], overlap=True,
+                                                      reducer=red)
+            local.backward()
+            peer.append(pending.value().item())
+        pgx = all_gather_shards(xo.grad, x.shape[0])
+        red.check()
+        red.close()
         results[rank] = {"loss": loss.item(), "gx": gx.cpu(), "gy": gy.cpu(), "knn": (d.cpu(), i.cpu()),
-                         "ball": (bd.cpu(), bi.cpu())}
+                         "ball": (bd.cpu(), bi.cpu()), "peer": peer, "peer_gx": pgx.cpu()}
     finally:
         dist.destroy_process_group()
 
@@ -84,6 +99,15 @@ def test_two_rank_nccl_matches_single_gpu():
     loss.backward()
     d, i = mps_pointops.knn(q.cuda(), r.cuda(), 16)
     bd, bi = mps_pointops.ball_query(q.cuda(), r.cuda(), 0.3, 32)
+    assert results[0]["peer"] == results[1]["peer"]          # same bits on both ranks
+    for step, got in enumerate(results[0]["peer"]):
+        xs = x.cuda().requires_grad_()
+        ys = (y * (1.0 + 0.01 * step)).cuda().requires_grad_()
+        want, _ = mps_pointops.chamfer_distance(xs, ys)
+        want.backward()
+        assert abs(got - want.item()) <= 1e-5 * abs(want.item())
+    for rank in (0, 1):
+        torch.testing.assert_close(results[rank]["peer_gx"], xs.grad.cpu(), rtol=1e-5, atol=1e-8)
     for rank in (0, 1):
         res = results[rank]
         assert abs(res["loss"] - loss.item()) <= 1e-5 * abs(loss.item())
