@@ -132,7 +132,8 @@ class ClockSampler:
             return None
         busy = [s for s in sm if s > 0.5 * max(sm)]
         return {"sm_mhz": statistics.median(busy or sm), "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(sm)}
+                "reasons": reasons, "samples": len(sm),
+                "gpus": len({r[1].strip().lower() for r in mine})}
 
 
 # ------------------------------------------------------------------ distributed
@@ -880,19 +881,28 @@ def _run_b200_steps(args, world, rank, dev, props, bus, x, y, x_cpu, y_cpu, flus
     for _ in range(max(args.warmup, 3)):
         chamfer_step(x, y, world, group_batch, reducer)
     torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        buses: list = [None] * world
+        dist.all_gather_object(buses, sorted(bus))
+        bus = set().union(*(set(b) for b in buses))
     barrier(world)
-    clocks = ClockSampler()
-    clocks.start()
+    # One sampler (rank 0, single node) records the clocks of every rank's GPU.
+    clocks = ClockSampler() if rank == 0 else None
+    if clocks:
+        clocks.start()
     time.sleep(0.3)
     launches0 = N.launch_count()
-    clocks.mark(True)
+    if clocks:
+        clocks.mark(True)
     with N.KernelTimer("chamfer_nearest") as ktimer:
         step_ms = timed_steps(lambda: chamfer_step(x, y, world, group_batch, reducer), args.steps,
                               flush)
-    clocks.mark(False)
+    if clocks:
+        clocks.mark(False)
     launches = N.launch_count() - launches0
     barrier(world)
-    clock_info = clocks.stop(bus)
+    clock_info = clocks.stop(bus) if clocks else None
     ms = max_over_ranks(statistics.mean(step_ms), world)
     kernel_ms = max_over_ranks(ktimer.mean_ms(), world)
     pairs_per_step = group_batch * NPTS * NPTS
