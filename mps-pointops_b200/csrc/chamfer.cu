@@ -846,9 +846,9 @@ __global__ void check_inputs_kernel(const float* __restrict__ x, const float* __
     const int64_t nx = B * P * D, total = nx + B * Q * D;
     const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    if (t0 < B) {
-        if (xl && (xl[t0] < 0 || xl[t0] > P)) flags[2] = 1;
-        if (yl && (yl[t0] < 0 || yl[t0] > Q)) flags[3] = 1;
+    for (int64_t b = t0; b < B; b += stride) {
+        if (xl && (xl[b] < 0 || xl[b] > P)) flags[2] = 1;
+        if (yl && (yl[b] < 0 || yl[b] > Q)) flags[3] = 1;
     }
     bool bad_x = false, bad_y = false;
     if (xl == nullptr && yl == nullptr) {
@@ -861,11 +861,23 @@ __global__ void check_inputs_kernel(const float* __restrict__ x, const float* __
             int64_t head = 0;
             if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
                 const float4* p4 = reinterpret_cast<const float4*>(p);
-                for (int64_t e = t0; e < n / 4; e += stride) {
-                    const float4 v = p4[e];
-                    bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+                const int64_t n4 = n / 4;
+                // Four independent loads in flight per thread: the grid is
+                // small (one CTA per SM) so that, beside a search kernel, the
+                // check holds few SM slots.
+                for (int64_t e = t0; e < n4; e += 4 * stride) {
+                    float4 v[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int64_t f = e + u * stride;
+                        v[u] = f < n4 ? p4[f] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        bad |= !(isfinite(v[u].x) && isfinite(v[u].y) && isfinite(v[u].z) &&
+                                 isfinite(v[u].w));
                 }
-                head = n / 4 * 4;
+                head = n4 * 4;
             }
             for (int64_t e = head + t0; e < n; e += stride) bad |= !isfinite(p[e]);
             if (a) bad_y = bad;
@@ -1540,7 +1552,10 @@ int mpo_chamfer_check_inputs(const float* x, const float* y, const int64_t* x_le
         return fail(kCudaError, "mpo_chamfer_check_inputs: memset failed");
     const int64_t total = max64(B * (P + Q) * D, B);
     if (total == 0) return kOk;
-    const unsigned grid = (unsigned)min64(ceil_div(total, 256), (int64_t)sm_count() * 8);
+    // One CTA per SM at most: callers run this check on a side stream beside
+    // the search, whose CTAs fill the SMs' registers, so every CTA here holds
+    // back one search CTA until it ends.
+    const unsigned grid = (unsigned)min64(ceil_div(total, 1024), (int64_t)sm_count());
     check_inputs_kernel<<<grid, 256, 0, s>>>(x, y, x_lengths, y_lengths, B, P, Q, D, flags);
     return check_launch("check_inputs_kernel");
 }

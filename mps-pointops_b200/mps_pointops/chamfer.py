@@ -75,12 +75,30 @@ class _PendingCheck:
             raise ValueError("valid y coordinates must be finite")
 
 
+_check_streams: dict[int, torch.cuda.Stream] = {}
+
+
+def _check_stream(device: torch.device) -> torch.cuda.Stream:
+    """The side stream (one per device) that runs the input check and copies
+    its flags to the host, so that neither the check nor the device-to-host
+    copy sits in the compute stream ahead of the search."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    st = _check_streams.get(key)
+    if st is None:
+        st = _check_streams[key] = torch.cuda.Stream(torch.device("cuda", key))
+    return st
+
+
 def _validate_clouds(x, y, x_lengths, y_lengths, defer: bool = False):
     """mps_pointops/chamfer.py:79-110: shapes, dtype, lengths in range and
-    finite valid coordinates -- here one native check.  With ``defer`` the
-    result is returned as a _PendingCheck to be raised after the search has
-    been queued (the kernels clamp lengths, so queuing them first is safe);
-    otherwise it is raised here."""
+    finite valid coordinates -- here one native check.  The check and the
+    copy of its flags to pinned host memory run on a side stream that first
+    waits for the caller's stream (the inputs as the caller sees them), so
+    the search queued next starts at once, beside the check.  With ``defer``
+    the result is returned as a _PendingCheck to be raised after the search
+    has been queued (the kernels clamp lengths and are memory-safe on the
+    inputs the check rejects, so queuing them first is safe); otherwise it is
+    raised here."""
     if x.ndim != 3 or y.ndim != 3 or x.shape[-1] < 1 or y.shape[-1] != x.shape[-1]:
         raise ValueError("x and y must have shapes (B, P, D) and (B, Q, D) with D >= 1")
     if x.shape[0] != y.shape[0]:
@@ -100,21 +118,29 @@ def _validate_clouds(x, y, x_lengths, y_lengths, defer: bool = False):
     ly = None if y_lengths is None else y_lengths.contiguous()
     xc, yc = x.detach().contiguous(), y.detach().contiguous()
     with N.on_device(x.device):
-        if x.dtype == torch.float32:
-            flags = torch.empty(4, dtype=torch.int32, device=x.device)
-            N.check(N.lib().mpo_chamfer_check_inputs(N.ptr(xc), N.ptr(yc), N.ptr(lx), N.ptr(ly),
-                                                     B, P, Q, D, N.ptr(flags),
-                                                     N.stream(x.device)),
-                    "chamfer input check")
-        else:
-            # float64: the same four flags from device tensor ops (the native
-            # check reads float32).
-            flags = torch.stack([*_bad_side(xc, lx, P), *_bad_side(yc, ly, Q)])
-            flags = flags[[0, 2, 1, 3]].int()
-        host = torch.empty(4, dtype=torch.int32, pin_memory=True)
-        host.copy_(flags, non_blocking=True)
-        event = torch.cuda.Event()
-        event.record(torch.cuda.current_stream(x.device))
+        side = _check_stream(x.device)
+        side.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(side):
+            if x.dtype == torch.float32:
+                flags = torch.empty(4, dtype=torch.int32, device=x.device)
+                N.check(N.lib().mpo_chamfer_check_inputs(N.ptr(xc), N.ptr(yc), N.ptr(lx),
+                                                         N.ptr(ly), B, P, Q, D, N.ptr(flags),
+                                                         N.stream(x.device)),
+                        "chamfer input check")
+            else:
+                # float64: the same four flags from device tensor ops (the
+                # native check reads float32).
+                flags = torch.stack([*_bad_side(xc, lx, P), *_bad_side(yc, ly, Q)])
+                flags = flags[[0, 2, 1, 3]].int()
+            host = torch.empty(4, dtype=torch.int32, pin_memory=True)
+            host.copy_(flags, non_blocking=True)
+            event = torch.cuda.Event()
+            event.record(side)
+        # The caller's tensors are read on the side stream: keep their memory
+        # from being reused on the caller's stream before the check has run.
+        for t in (xc, yc, lx, ly):
+            if t is not None:
+                t.record_stream(side)
     pending = _PendingCheck(host, event, P, Q)
     if not defer:
         pending.raise_if_bad()

@@ -226,6 +226,39 @@ def test_nonfinite_check_float4_arrays(cuda_device, where):
     chamfer_distance(torch.randn(2, 40, 3, generator=g).to(d), torch.randn(2, 28, 3, generator=g).to(d))
 
 
+@pytest.mark.parametrize("pos", [0, 12345, 4 * 8192 * 3 - 1])
+def test_nonfinite_check_large_arrays(cuda_device, pos):
+    # Config-2-sized clouds: the check's grid (one CTA per SM) takes several
+    # strided rounds of four loads per thread; the first, a middle and the
+    # last element are each found in either cloud.
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(4, 8192, 3, generator=g)
+    y = torch.randn(4, 8192, 3, generator=g)
+    xb = x.clone()
+    xb.view(-1)[pos] = float("nan")
+    with pytest.raises(ValueError, match="valid x coordinates"):
+        chamfer_distance(xb.to(cuda_device), y.to(cuda_device))
+    yb = y.clone()
+    yb.view(-1)[pos] = float("inf")
+    with pytest.raises(ValueError, match="valid y coordinates"):
+        chamfer_distance(x.to(cuda_device), yb.to(cuda_device))
+    chamfer_distance(x.to(cuda_device), y.to(cuda_device))
+
+
+def test_length_check_more_clouds_than_threads(cuda_device):
+    # 50,000 clouds: more lengths than the check's threads (one 256-thread CTA
+    # per SM), so the lengths are checked in a strided loop; the bad one is
+    # the last.
+    B = 50000
+    x = torch.zeros(B, 2, 3, device=cuda_device)
+    ok = torch.full((B,), 2, dtype=torch.long, device=cuda_device)
+    bad = ok.clone()
+    bad[-1] = 3
+    with pytest.raises(ValueError, match=r"y_lengths must lie in \[0, 2\]"):
+        chamfer_distance(x, x, ok, bad)
+    chamfer_distance(x, x, ok, ok)
+
+
 @pytest.mark.parametrize("dimension", [1, 2, 4, 64, 128])
 def test_first_index_tie_any_dimension(cuda_device, dimension):  # tests/test_chamfer_nd.py:50-73
     x = torch.zeros((1, 1, dimension), device=cuda_device, requires_grad=True)
