@@ -920,6 +920,22 @@ __host__ __device__ inline int red_chunks(int64_t M) {
     return (int)min64(kMaxRedChunks, max64(1, ceil_div(M, 2048)));
 }
 
+__device__ void loss_from_partials(const float* partial, const int64_t* __restrict__ xl,
+                                   const int64_t* __restrict__ yl, int64_t B, int64_t P,
+                                   int64_t Q, int bidirectional, int point_mode, int batch_mode,
+                                   float* __restrict__ per_cloud, float* __restrict__ loss);
+
+// LossArgs.done (nullable): a zeroed counter; the CTA that finishes last
+// (of `blocks` CTAs that have rows) computes the loss from every partial, so
+// no separate loss launch follows.
+struct LossArgs {
+    unsigned* done;
+    int blocks;
+    int bidirectional, point_mode, batch_mode;
+    float* per_cloud;
+    float* loss;
+};
+
 template <bool FROM_KEYS>
 __global__ void __launch_bounds__(kRedThreads)
 finalize_reduce_kernel(const unsigned long long* __restrict__ keys_x,
@@ -927,7 +943,7 @@ finalize_reduce_kernel(const unsigned long long* __restrict__ keys_x,
                        const int64_t* __restrict__ xl, const int64_t* __restrict__ yl, int64_t B,
                        int64_t P, int64_t Q, float* __restrict__ dist_x,
                        int64_t* __restrict__ idx_x, float* __restrict__ dist_y,
-                       int64_t* __restrict__ idx_y, float* __restrict__ partial) {
+                       int64_t* __restrict__ idx_y, float* __restrict__ partial, LossArgs la) {
     __shared__ float s_red[kRedThreads];
     const int64_t b = blockIdx.x;
     const int dir = blockIdx.y;
@@ -965,19 +981,33 @@ finalize_reduce_kernel(const unsigned long long* __restrict__ keys_x,
         __syncthreads();
     }
     if (threadIdx.x == 0) partial[(b * 2 + dir) * kMaxRedChunks + blockIdx.z] = s_red[0];
+    if (la.done == nullptr) return;  // grid-uniform
+    // Last CTA: publish this partial (fence), count, and the CTA that sees
+    // the final count reads every partial after a fence of its own.
+    __shared__ bool s_last;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(la.done, 1u) == (unsigned)(la.blocks - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    loss_from_partials(partial, xl, yl, B, P, Q, la.bidirectional, la.point_mode, la.batch_mode,
+                       la.per_cloud, la.loss);
 }
 
 // point_mode: 0 sum, 1 mean over valid points; batch_mode: 0 none (loss[b]),
-// 1 sum, 2 mean.  One thread per cloud, then thread 0 sums in order.
-__global__ void loss_kernel(const float* __restrict__ partial, const int64_t* __restrict__ xl,
-                            const int64_t* __restrict__ yl, int64_t B, int64_t P, int64_t Q,
-                            int bidirectional, int point_mode, int batch_mode,
-                            float* __restrict__ per_cloud, float* __restrict__ loss) {
-    // Segment sum: its chunks in order.
+// 1 sum, 2 mean.  One thread per cloud (segment sums: their chunks in
+// order), then thread 0 sums the clouds in order.  Run by a whole CTA; the
+// partials are read through L2 (other CTAs wrote them).
+__device__ void loss_from_partials(const float* partial, const int64_t* __restrict__ xl,
+                                   const int64_t* __restrict__ yl, int64_t B, int64_t P,
+                                   int64_t Q, int bidirectional, int point_mode, int batch_mode,
+                                   float* __restrict__ per_cloud, float* __restrict__ loss) {
     auto seg = [&](int64_t b, int dir, int64_t M) {
         const float* c = partial + (b * 2 + dir) * kMaxRedChunks;
-        float v = c[0];
-        for (int k = 1; k < red_chunks(M); ++k) v = __fadd_rn(v, c[k]);
+        float v = __ldcg(c);
+        for (int k = 1; k < red_chunks(M); ++k) v = __fadd_rn(v, __ldcg(c + k));
         return v;
     };
     for (int64_t b = threadIdx.x; b < B; b += blockDim.x) {
@@ -1006,6 +1036,35 @@ __global__ void loss_kernel(const float* __restrict__ partial, const int64_t* __
     for (int64_t b = 0; b < B; ++b) t = __fadd_rn(t, per_cloud[b]);
     if (batch_mode == 2) t = __fdiv_rn(t, (float)max64(B, 1));
     loss[0] = t;
+}
+
+// The loss from the partials in a launch of its own (the per-direction
+// search path, whose workspace holds no zeroed counter).
+__global__ void loss_kernel(const float* __restrict__ partial, const int64_t* __restrict__ xl,
+                            const int64_t* __restrict__ yl, int64_t B, int64_t P, int64_t Q,
+                            int bidirectional, int point_mode, int batch_mode,
+                            float* __restrict__ per_cloud, float* __restrict__ loss) {
+    loss_from_partials(partial, xl, yl, B, P, Q, bidirectional, point_mode, batch_mode,
+                       per_cloud, loss);
+}
+
+// Both gradient arrays to zero in one launch (the backward accumulates into
+// them with atomics).
+__global__ void zero2_kernel(float* __restrict__ a, int64_t na, float* __restrict__ b,
+                             int64_t nb) {
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int h = 0; h < 2; ++h) {
+        float* p = h ? b : a;
+        const int64_t n = h ? nb : na;
+        int64_t head = 0;
+        if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+            float4* p4 = reinterpret_cast<float4*>(p);
+            for (int64_t e = t0; e < n / 4; e += stride) p4[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+            head = n / 4 * 4;
+        }
+        for (int64_t e = head + t0; e < n; e += stride) p[e] = 0.f;
+    }
 }
 
 // (a, b, c) added to the three floats of row r of a D = 3 array whose base
@@ -1249,6 +1308,20 @@ int mpo_chamfer_nearest_l1(const float* x, const float* y, const int64_t* x_leng
 
 namespace mpo {
 namespace {
+// Scratch reset of the symmetric searches in one launch: every 64-bit key to
+// all ones (nothing found yet) and the `nz` counter words that follow the
+// keys to zero (the search's work-item counter, then the loss's CTA count).
+// keys is 256-byte aligned (the workspace's start).
+__global__ void scratch_reset_kernel(unsigned long long* __restrict__ keys, int64_t nkeys,
+                                     unsigned* __restrict__ counters, int nz) {
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    ulonglong2* k2 = reinterpret_cast<ulonglong2*>(keys);
+    for (int64_t e = t0; e < nkeys / 2; e += stride) k2[e] = make_ulonglong2(~0ull, ~0ull);
+    if (t0 == 0 && (nkeys & 1)) keys[nkeys - 1] = ~0ull;
+    if (t0 < nz) counters[t0] = 0u;
+}
+
 // The search shared by mpo_chamfer_nearest and mpo_chamfer_loss.  On the
 // symmetric path it leaves 64-bit keys in the workspace (*keys_x/*keys_y set,
 // dist/idx not yet written); otherwise the per-direction kernels write
@@ -1273,9 +1346,13 @@ int chamfer_search(const float* x, const float* y, const int64_t* x_lengths,
     unsigned long long* keys_x = reinterpret_cast<unsigned long long*>(workspace);
     unsigned long long* keys_y = keys_x + (size_t)B * P;
     unsigned* counter = reinterpret_cast<unsigned*>(keys_y + (size_t)B * Q);
-    if (cudaMemsetAsync(keys_x, 0xff, (size_t)B * (P + Q) * 8, s) != cudaSuccess ||
-        cudaMemsetAsync(counter, 0, sizeof(unsigned), s) != cudaSuccess)
-        return fail(kCudaError, std::string(who) + ": scratch reset failed");
+    {
+        const int64_t nkeys = B * (P + Q);
+        const int64_t grid = max64(1, min64(ceil_div(nkeys / 2, 256), (int64_t)sm_count() * 4));
+        scratch_reset_kernel<<<(unsigned)grid, 256, 0, s>>>(keys_x, nkeys, counter, 2);
+        int st = check_launch("chamfer scratch_reset_kernel");
+        if (st) return st;
+    }
     if (symd) {
         *keys_x_out = keys_x;
         *keys_y_out = keys_y;
@@ -1381,13 +1458,20 @@ int mpo_chamfer_loss(const float* x, const float* y, const int64_t* x_lengths,
     float* per_cloud = partial + 2 * B * kMaxRedChunks;
     dim3 grid((unsigned)B, bidirectional ? 2u : 1u,
               (unsigned)red_chunks(bidirectional ? max64(P, Q) : P));
-    if (keys_x)
+    // On the keyed (symmetric) path the scratch reset zeroed a counter after
+    // the search's: the last finalize CTA computes the loss itself.
+    LossArgs la{nullptr, 0, bidirectional, point_mode, batch_mode, per_cloud, loss};
+    if (keys_x) {
+        la.done = reinterpret_cast<unsigned*>(keys_y + (size_t)B * Q) + 1;
+        la.blocks = (int)(B * (red_chunks(P) + (bidirectional ? red_chunks(Q) : 0)));
         finalize_reduce_kernel<true><<<grid, kRedThreads, 0, s>>>(
-            keys_x, keys_y, x_lengths, y_lengths, B, P, Q, dist_x, idx_x, dist_y, idx_y, partial);
-    else
-        finalize_reduce_kernel<false><<<grid, kRedThreads, 0, s>>>(
-            nullptr, nullptr, x_lengths, y_lengths, B, P, Q, dist_x, idx_x, dist_y, idx_y,
-            partial);
+            keys_x, keys_y, x_lengths, y_lengths, B, P, Q, dist_x, idx_x, dist_y, idx_y, partial,
+            la);
+        return check_launch("chamfer finalize_reduce_kernel");
+    }
+    finalize_reduce_kernel<false><<<grid, kRedThreads, 0, s>>>(
+        nullptr, nullptr, x_lengths, y_lengths, B, P, Q, dist_x, idx_x, dist_y, idx_y, partial,
+        la);
     st = check_launch("chamfer finalize_reduce_kernel");
     if (st) return st;
     loss_kernel<<<1, 256, 0, s>>>(partial, x_lengths, y_lengths, B, P, Q, bidirectional,
@@ -1406,10 +1490,15 @@ int mpo_chamfer_loss_backward(const float* x, const float* y, const int64_t* x_l
     if (st) return st;
     MPO_REQUIRE((grad_x || B * P * D == 0) && (grad_y || B * Q * D == 0), "null gradient pointer");
     cudaStream_t s = (cudaStream_t)stream;
-    if (B * P * D > 0 && cudaMemsetAsync(grad_x, 0, sizeof(float) * B * P * D, s) != cudaSuccess)
-        return fail(kCudaError, "mpo_chamfer_loss_backward: memset failed");
-    if (B * Q * D > 0 && cudaMemsetAsync(grad_y, 0, sizeof(float) * B * Q * D, s) != cudaSuccess)
-        return fail(kCudaError, "mpo_chamfer_loss_backward: memset failed");
+    {
+        const int64_t nz = B * (P + Q) * D;
+        if (nz > 0) {
+            const int64_t grid = max64(1, min64(ceil_div(nz / 4, 256), (int64_t)sm_count() * 4));
+            zero2_kernel<<<(unsigned)grid, 256, 0, s>>>(grad_x, B * P * D, grad_y, B * Q * D);
+            st = check_launch("chamfer zero2_kernel");
+            if (st) return st;
+        }
+    }
     const int64_t total = B * P + (bidirectional ? B * Q : 0);
     if (total == 0) return kOk;
     MPO_REQUIRE(grad_loss && (idx_x || B * P == 0) && (idx_y || !bidirectional || B * Q == 0),
