@@ -177,6 +177,20 @@ def stream(device: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+_side_streams: dict[int, torch.cuda.Stream] = {}
+
+
+def side_stream(device: torch.device) -> torch.cuda.Stream:
+    """A second stream per device for the input checks: a check and the copy
+    of its flags to the host run there (after waiting for the caller's
+    stream), so neither sits in the caller's stream ahead of the compute."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    st = _side_streams.get(key)
+    if st is None:
+        st = _side_streams[key] = torch.cuda.Stream(torch.device("cuda", key))
+    return st
+
+
 class on_device:
     """Make ``device`` current for the duration of a native call."""
 

@@ -75,20 +75,6 @@ class _PendingCheck:
             raise ValueError("valid y coordinates must be finite")
 
 
-_check_streams: dict[int, torch.cuda.Stream] = {}
-
-
-def _check_stream(device: torch.device) -> torch.cuda.Stream:
-    """The side stream (one per device) that runs the input check and copies
-    its flags to the host, so that neither the check nor the device-to-host
-    copy sits in the compute stream ahead of the search."""
-    key = device.index if device.index is not None else torch.cuda.current_device()
-    st = _check_streams.get(key)
-    if st is None:
-        st = _check_streams[key] = torch.cuda.Stream(torch.device("cuda", key))
-    return st
-
-
 def _validate_clouds(x, y, x_lengths, y_lengths, defer: bool = False):
     """mps_pointops/chamfer.py:79-110: shapes, dtype, lengths in range and
     finite valid coordinates -- here one native check.  The check and the
@@ -118,7 +104,7 @@ def _validate_clouds(x, y, x_lengths, y_lengths, defer: bool = False):
     ly = None if y_lengths is None else y_lengths.contiguous()
     xc, yc = x.detach().contiguous(), y.detach().contiguous()
     with N.on_device(x.device):
-        side = _check_stream(x.device)
+        side = N.side_stream(x.device)
         side.wait_stream(torch.cuda.current_stream(x.device))
         with torch.cuda.stream(side):
             if x.dtype == torch.float32:
